@@ -1,0 +1,153 @@
+/*
+ * nvcr_sm100: C ABI of the Blackwell (sm_100a) executor for the
+ * nvcr.intconv.v1 exact-convolution profile.
+ *
+ * This is the shim a new execution provider calls (one process, one GPU, one
+ * executor per stream). It replaces the reference's CUDA executor behind the
+ * provider boundary:
+ *   reference src/deterministic/cuda_executor.hpp:26-53   (CudaExecutor)
+ *   reference src/deterministic/normative_stage.hpp:28-65 (normative helpers)
+ *   reference src/provider/tensorrt/session.cpp:1464-1467,1526-1594 (exact stages)
+ * Every output is bit-identical to the reference's CPU executor run_cpu
+ * (src/deterministic/program.cpp:702-820); NaN payloads are unspecified.
+ *
+ * Plain C types only. Every function returns NVCR_SM100_OK (0) or
+ * 1 + the reference's nvcr::ErrorCode value (include/nvcr/common/error.hpp:11-34),
+ * and leaves a message for nvcr_sm100_last_error() on the calling thread. No
+ * exception crosses the ABI.
+ */
+#ifndef NVCR_SM100_H
+#define NVCR_SM100_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NVCR_SM100_ABI_VERSION 1
+
+/* Status codes: 0, or 1 + nvcr::ErrorCode. */
+#define NVCR_SM100_OK 0
+#define NVCR_SM100_INVALID_ARGUMENT 1
+#define NVCR_SM100_INVALID_STATE 2
+#define NVCR_SM100_IO_ERROR 3
+#define NVCR_SM100_RESOURCE_EXHAUSTED 5
+#define NVCR_SM100_BACKEND_ERROR 7
+#define NVCR_SM100_NOT_IMPLEMENTED 8
+#define NVCR_SM100_INTERNAL_ERROR 9
+#define NVCR_SM100_MISSING_ARTIFACT 12
+#define NVCR_SM100_INCOMPATIBLE_TARGET 16
+#define NVCR_SM100_INCOMPATIBLE_PRECISION 17
+#define NVCR_SM100_DIGEST_MISMATCH 19
+
+typedef struct nvcr_sm100_executor nvcr_sm100_executor;
+
+/* A named batch-1 NCHW tensor. `data` is device FP16 for run_half, device
+ * FP32 for run_float and host FP32 for run_host (reference HalfDeviceTensor,
+ * cuda_executor.hpp:19-24, and Tensor, program.hpp:116-127). */
+typedef struct nvcr_sm100_tensor {
+    const char* name;
+    int32_t channels;
+    int32_t height;
+    int32_t width;
+    void* data;
+} nvcr_sm100_tensor;
+
+/* One timed step of a profiled run (see nvcr_sm100_set_profiling). */
+typedef struct nvcr_sm100_step_time {
+    char label[96];
+    char kernel[32];
+    double milliseconds;
+    double algorithmic_ops;   /* 2 * C_in * kh * kw * C_out * P for integer convs */
+    double algorithmic_bytes; /* each input read once and the output written once */
+} nvcr_sm100_step_time;
+
+int nvcr_sm100_abi_version(void);
+
+/* Message of the last failed call on this thread; returns its full length. */
+size_t nvcr_sm100_last_error(char* buffer, size_t size);
+
+/* 1 when `profile` is nvcr.intconv.v1 and the current device is sm_100, else 0
+ * (reference IProviderSession::supports_numerics_profile,
+ * include/nvcr/provider/experimental/session.hpp:147-150, as the TensorRT
+ * provider answers it at src/provider/tensorrt/session.cpp:1464-1467). */
+int nvcr_sm100_supports_profile(const char* profile);
+
+/* Reference is_normative (normative_stage.hpp:28-31): *normative = 0 for an
+ * empty profile (a native stage), 1 for nvcr.intconv.v1; any other profile is
+ * NVCR_SM100_INCOMPATIBLE_PRECISION. */
+int nvcr_sm100_is_normative(const char* profile, int* normative);
+
+/* Reference load_program + CudaExecutor::create (program.cpp:537-626,
+ * cuda_executor.cu:1279-1313): loads <path> (.detprog.json) and the .detw it
+ * names, checks the weight digest, uploads and quantises the weights on the
+ * current device. `stream` is a cudaStream_t, or NULL for an executor-owned
+ * non-blocking stream; with a stream, all work is ordered on it. */
+int nvcr_sm100_executor_create(const char* program_json_path, void* stream, nvcr_sm100_executor** executor);
+
+/* The same from JSON text with the weights given as FP32 values (the in-memory
+ * Program form of the reference's tests, tests/deterministic_executor_tests.cpp:96-179);
+ * `weight_count` must equal the JSON's weights.count. */
+int nvcr_sm100_executor_create_from_memory(const char* program_json, size_t json_size, const float* weights,
+                                           size_t weight_count, void* stream, nvcr_sm100_executor** executor);
+
+/* Reference load_normative_program (normative_stage.cpp:71-91): the program is
+ * <directory>/<component>.detprog.json and its SHA-256 must equal
+ * `expected_sha256_hex` (64 lowercase hex digits); a missing file is
+ * NVCR_SM100_MISSING_ARTIFACT, a different digest NVCR_SM100_DIGEST_MISMATCH. */
+int nvcr_sm100_load_normative(const char* directory, const char* component, const char* expected_sha256_hex,
+                              void* stream, nvcr_sm100_executor** executor);
+
+void nvcr_sm100_executor_destroy(nvcr_sm100_executor* executor);
+
+/* Program metadata: names and channel counts of inputs (is_output = 0) and
+ * outputs (is_output = 1). `name` stays valid for the executor's lifetime. */
+int nvcr_sm100_tensor_count(const nvcr_sm100_executor* executor, int is_output, size_t* count);
+int nvcr_sm100_tensor_info(const nvcr_sm100_executor* executor, int is_output, size_t index, const char** name,
+                           int32_t* channels);
+
+/* Reference infer_output_extents (normative_stage.cpp:42-65): inputs in
+ * program order (names ignored); fills name/channels/height/width of
+ * `outputs[0..output_count)` in program order. */
+int nvcr_sm100_infer_output_extents(const nvcr_sm100_executor* executor, const nvcr_sm100_tensor* inputs,
+                                    size_t input_count, nvcr_sm100_tensor* outputs, size_t output_count);
+
+/* Reference CudaExecutor::run_half (cuda_executor.cu:1315-1373): named device
+ * FP16 tensors; inputs widen exactly, outputs round to nearest even. Returns
+ * once the work is enqueued; outputs are complete in stream order. */
+int nvcr_sm100_run_half(nvcr_sm100_executor* executor, const nvcr_sm100_tensor* inputs, size_t input_count,
+                        const nvcr_sm100_tensor* outputs, size_t output_count);
+
+/* As run_half with device FP32 tensors on both sides (no boundary rounding). */
+int nvcr_sm100_run_float(nvcr_sm100_executor* executor, const nvcr_sm100_tensor* inputs, size_t input_count,
+                         const nvcr_sm100_tensor* outputs, size_t output_count);
+
+/* Reference CudaExecutor::run (cuda_executor.cu:1375-1397): host FP32 tensors,
+ * synchronous; the output buffers are caller-allocated. */
+int nvcr_sm100_run_host(nvcr_sm100_executor* executor, const nvcr_sm100_tensor* inputs, size_t input_count,
+                        const nvcr_sm100_tensor* outputs, size_t output_count);
+
+/* Waits for the executor's stream; NVCR_SM100_BACKEND_ERROR if a CUDA error
+ * occurred or a device-side bounded wait gave up. */
+int nvcr_sm100_synchronize(nvcr_sm100_executor* executor);
+
+/* The stream all work is ordered on (a cudaStream_t). */
+void* nvcr_sm100_stream(const nvcr_sm100_executor* executor);
+
+/* Kernels launched by the last run, and the workspace bytes held. */
+int nvcr_sm100_last_launch_count(const nvcr_sm100_executor* executor);
+size_t nvcr_sm100_workspace_bytes(const nvcr_sm100_executor* executor);
+
+/* Per-step CUDA-event timing of subsequent runs (off by default). */
+int nvcr_sm100_set_profiling(nvcr_sm100_executor* executor, int enabled);
+/* Synchronises and copies up to `capacity` step times of the last profiled
+ * run; *count receives the number of steps. */
+int nvcr_sm100_profile(nvcr_sm100_executor* executor, nvcr_sm100_step_time* steps, size_t capacity, size_t* count);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NVCR_SM100_H */

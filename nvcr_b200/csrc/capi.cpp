@@ -1,0 +1,279 @@
+// The extern "C" entry points of include/nvcr_sm100.h over the executor.
+// Failures become 1 + the reference's ErrorCode value and a thread-local message.
+
+#include "../../include/nvcr_sm100.h"
+
+#include "executor.hpp"
+#include "sha256.hpp"
+
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <new>
+#include <sstream>
+#include <string>
+#include <sys/stat.h>
+
+struct nvcr_sm100_executor {
+    std::unique_ptr<nvcr_sm100::Executor> executor;
+};
+
+namespace {
+
+using nvcr_sm100::Code;
+using nvcr_sm100::Error;
+
+thread_local std::string last_error;
+
+int report(const Error& error) {
+    last_error = error.message;
+    return static_cast<int>(error.code) + 1;
+}
+
+int report(Code code, const std::string& message) { return report(Error{code, message}); }
+
+int succeed() {
+    last_error.clear();
+    return NVCR_SM100_OK;
+}
+
+template <typename F>
+int guarded(F&& body) {
+    try {
+        return body();
+    } catch (const std::bad_alloc&) {
+        return report(Code::resource_exhausted, "host allocation failed");
+    } catch (const std::exception& exception) {
+        return report(Code::internal_error, exception.what());
+    } catch (...) {
+        return report(Code::internal_error, "unknown exception");
+    }
+}
+
+std::vector<nvcr_sm100::TensorView> views(const nvcr_sm100_tensor* tensors, size_t count) {
+    std::vector<nvcr_sm100::TensorView> out;
+    for (size_t i = 0; i < count; ++i) {
+        out.push_back(nvcr_sm100::TensorView{tensors[i].name != nullptr ? tensors[i].name : "",
+                                             {tensors[i].channels, tensors[i].height, tensors[i].width},
+                                             tensors[i].data});
+    }
+    return out;
+}
+
+int finish_create(nvcr_sm100::Result<nvcr_sm100::Program> program, void* stream, nvcr_sm100_executor** executor) {
+    if (!program) return report(program.error());
+    auto created = nvcr_sm100::Executor::create(std::move(program.value()), static_cast<cudaStream_t>(stream));
+    if (!created) return report(created.error());
+    *executor = new nvcr_sm100_executor{std::move(created.value())};
+    return succeed();
+}
+
+template <typename Run>
+int run_with(nvcr_sm100_executor* executor, const nvcr_sm100_tensor* inputs, size_t input_count,
+             const nvcr_sm100_tensor* outputs, size_t output_count, Run run) {
+    if (executor == nullptr || (inputs == nullptr && input_count > 0) || (outputs == nullptr && output_count > 0)) {
+        return report(Code::invalid_argument, "null executor or tensor array");
+    }
+    auto status = run(*executor->executor, views(inputs, input_count), views(outputs, output_count));
+    if (!status) return report(status.error());
+    return succeed();
+}
+
+}  // namespace
+
+extern "C" {
+
+int nvcr_sm100_abi_version(void) { return NVCR_SM100_ABI_VERSION; }
+
+size_t nvcr_sm100_last_error(char* buffer, size_t size) {
+    if (buffer != nullptr && size > 0) std::snprintf(buffer, size, "%s", last_error.c_str());
+    return last_error.size();
+}
+
+int nvcr_sm100_supports_profile(const char* profile) {
+    if (profile == nullptr || std::string_view(profile) != nvcr_sm100::intconv_profile) return 0;
+    int device = 0;
+    int major = 0;
+    int minor = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) return 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess) return 0;
+    if (cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device) != cudaSuccess) return 0;
+    return major == 10 && minor == 0 ? 1 : 0;
+}
+
+int nvcr_sm100_is_normative(const char* profile, int* normative) {
+    if (normative == nullptr) return report(Code::invalid_argument, "null output");
+    const std::string_view text = profile != nullptr ? profile : "";
+    if (text.empty()) {
+        *normative = 0;
+        return succeed();
+    }
+    if (text == nvcr_sm100::intconv_profile) {
+        *normative = 1;
+        return succeed();
+    }
+    return report(Code::incompatible_precision, "unknown numerics profile '" + std::string(text) + "'");
+}
+
+int nvcr_sm100_executor_create(const char* path, void* stream, nvcr_sm100_executor** executor) {
+    return guarded([&] {
+        if (path == nullptr || executor == nullptr) return report(Code::invalid_argument, "null argument");
+        return finish_create(nvcr_sm100::load_program_file(path), stream, executor);
+    });
+}
+
+int nvcr_sm100_executor_create_from_memory(const char* json, size_t json_size, const float* weights,
+                                           size_t weight_count, void* stream, nvcr_sm100_executor** executor) {
+    return guarded([&] {
+        if (json == nullptr || executor == nullptr || (weights == nullptr && weight_count > 0)) {
+            return report(Code::invalid_argument, "null argument");
+        }
+        static const float no_weights = 0.0f;
+        return finish_create(nvcr_sm100::load_program_text(std::string_view(json, json_size), ".",
+                                                           weights != nullptr ? weights : &no_weights, weight_count),
+                             stream, executor);
+    });
+}
+
+int nvcr_sm100_load_normative(const char* directory, const char* component, const char* expected, void* stream,
+                              nvcr_sm100_executor** executor) {
+    return guarded([&] {
+        if (directory == nullptr || component == nullptr || executor == nullptr) {
+            return report(Code::invalid_argument, "null argument");
+        }
+        const std::string name(component);
+        if (expected == nullptr || std::strlen(expected) == 0) {
+            return report(Code::invalid_argument, "normative stage " + name + " has no program digest");
+        }
+        const std::string path = std::string(directory) + "/" + name + ".detprog.json";
+        struct stat info{};
+        if (stat(path.c_str(), &info) != 0 || !S_ISREG(info.st_mode)) {
+            return report(Code::missing_artifact, "normative program is missing: " + path);
+        }
+        std::ifstream stream_in(path, std::ios::binary);
+        std::ostringstream contents;
+        contents << stream_in.rdbuf();
+        const std::string text = contents.str();
+        if (nvcr_sm100::sha256_hex(text.data(), text.size()) != std::string(expected)) {
+            return report(Code::digest_mismatch, "normative program digest mismatch: " + path);
+        }
+        return finish_create(nvcr_sm100::load_program_file(path), stream, executor);
+    });
+}
+
+void nvcr_sm100_executor_destroy(nvcr_sm100_executor* executor) { delete executor; }
+
+int nvcr_sm100_tensor_count(const nvcr_sm100_executor* executor, int is_output, size_t* count) {
+    if (executor == nullptr || count == nullptr) return report(Code::invalid_argument, "null argument");
+    const auto& program = executor->executor->program();
+    *count = is_output ? program.outputs.size() : program.inputs.size();
+    return succeed();
+}
+
+int nvcr_sm100_tensor_info(const nvcr_sm100_executor* executor, int is_output, size_t index, const char** name,
+                           int32_t* channels) {
+    if (executor == nullptr) return report(Code::invalid_argument, "null executor");
+    const auto& program = executor->executor->program();
+    const auto& ids = is_output ? program.outputs : program.inputs;
+    if (index >= ids.size()) return report(Code::invalid_argument, "tensor index out of range");
+    if (name != nullptr) *name = program.tensor_names[ids[index]].c_str();
+    if (channels != nullptr) *channels = program.tensor_channels[ids[index]];
+    return succeed();
+}
+
+int nvcr_sm100_infer_output_extents(const nvcr_sm100_executor* executor, const nvcr_sm100_tensor* inputs,
+                                    size_t input_count, nvcr_sm100_tensor* outputs, size_t output_count) {
+    return guarded([&] {
+        if (executor == nullptr || (inputs == nullptr && input_count > 0)) {
+            return report(Code::invalid_argument, "null argument");
+        }
+        const auto& program = executor->executor->program();
+        std::vector<nvcr_sm100::Extent> extents;
+        for (size_t i = 0; i < input_count; ++i) {
+            extents.push_back({inputs[i].channels, inputs[i].height, inputs[i].width});
+        }
+        auto inferred = nvcr_sm100::infer_output_extents(program, extents);
+        if (!inferred) return report(inferred.error());
+        if (output_count < inferred.value().size() || outputs == nullptr) {
+            return report(Code::invalid_argument, "output array is too small");
+        }
+        for (size_t slot = 0; slot < inferred.value().size(); ++slot) {
+            outputs[slot].name = program.tensor_names[program.outputs[slot]].c_str();
+            outputs[slot].channels = inferred.value()[slot].channels;
+            outputs[slot].height = inferred.value()[slot].height;
+            outputs[slot].width = inferred.value()[slot].width;
+        }
+        return succeed();
+    });
+}
+
+int nvcr_sm100_run_half(nvcr_sm100_executor* executor, const nvcr_sm100_tensor* inputs, size_t input_count,
+                        const nvcr_sm100_tensor* outputs, size_t output_count) {
+    return guarded([&] {
+        return run_with(executor, inputs, input_count, outputs, output_count,
+                        [](nvcr_sm100::Executor& e, const auto& in, const auto& out) { return e.run_half(in, out); });
+    });
+}
+
+int nvcr_sm100_run_float(nvcr_sm100_executor* executor, const nvcr_sm100_tensor* inputs, size_t input_count,
+                         const nvcr_sm100_tensor* outputs, size_t output_count) {
+    return guarded([&] {
+        return run_with(executor, inputs, input_count, outputs, output_count,
+                        [](nvcr_sm100::Executor& e, const auto& in, const auto& out) { return e.run_float(in, out); });
+    });
+}
+
+int nvcr_sm100_run_host(nvcr_sm100_executor* executor, const nvcr_sm100_tensor* inputs, size_t input_count,
+                        const nvcr_sm100_tensor* outputs, size_t output_count) {
+    return guarded([&] {
+        return run_with(executor, inputs, input_count, outputs, output_count,
+                        [](nvcr_sm100::Executor& e, const auto& in, const auto& out) { return e.run_host(in, out); });
+    });
+}
+
+int nvcr_sm100_synchronize(nvcr_sm100_executor* executor) {
+    return guarded([&] {
+        if (executor == nullptr) return report(Code::invalid_argument, "null executor");
+        auto status = executor->executor->synchronize();
+        if (!status) return report(status.error());
+        return succeed();
+    });
+}
+
+void* nvcr_sm100_stream(const nvcr_sm100_executor* executor) {
+    return executor == nullptr ? nullptr : static_cast<void*>(executor->executor->stream());
+}
+
+int nvcr_sm100_last_launch_count(const nvcr_sm100_executor* executor) {
+    return executor == nullptr ? 0 : executor->executor->launches_last_run();
+}
+
+size_t nvcr_sm100_workspace_bytes(const nvcr_sm100_executor* executor) {
+    return executor == nullptr ? 0 : executor->executor->workspace_bytes();
+}
+
+int nvcr_sm100_set_profiling(nvcr_sm100_executor* executor, int enabled) {
+    if (executor == nullptr) return report(Code::invalid_argument, "null executor");
+    executor->executor->set_profiling(enabled != 0);
+    return succeed();
+}
+
+int nvcr_sm100_profile(nvcr_sm100_executor* executor, nvcr_sm100_step_time* steps, size_t capacity, size_t* count) {
+    return guarded([&] {
+        if (executor == nullptr || count == nullptr) return report(Code::invalid_argument, "null argument");
+        auto timings = executor->executor->profile();
+        if (!timings) return report(timings.error());
+        *count = timings.value().size();
+        for (size_t i = 0; i < timings.value().size() && i < capacity && steps != nullptr; ++i) {
+            const auto& t = timings.value()[i];
+            std::snprintf(steps[i].label, sizeof(steps[i].label), "%s", t.label.c_str());
+            std::snprintf(steps[i].kernel, sizeof(steps[i].kernel), "%s", t.kernel.c_str());
+            steps[i].milliseconds = t.milliseconds;
+            steps[i].algorithmic_ops = t.algorithmic_ops;
+            steps[i].algorithmic_bytes = t.algorithmic_bytes;
+        }
+        return succeed();
+    });
+}
+
+}  // extern "C"

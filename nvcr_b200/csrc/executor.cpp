@@ -1,0 +1,897 @@
+#include "executor.hpp"
+
+#include <algorithm>
+#include <climits>
+#include <cstring>
+#include <limits>
+#include <set>
+
+namespace nvcr_sm100 {
+
+// ---------------------------------------------------------------- internals
+
+struct Executor::IntegerConv {
+    int weight_limbs{1}, activation_limbs{1}, activation_bits{8};
+    int k_real{0}, k_padded{0};
+    int n_tile{0}, n_tiles{0};
+    int out_channels{0};  // logical output channels of the step (halved by chunk-add)
+    bool chunk_add{false};
+    std::int8_t* b_high{nullptr};
+    std::int8_t* b_low{nullptr};
+    float* scales{nullptr};
+    float* bias{nullptr};
+    long long* row_terms{nullptr};
+    void* allocation{nullptr};
+    CUtensorMap b_high_map{};
+    CUtensorMap b_low_map{};
+    long long column_high_factor{0}, column_low_factor{0};
+};
+
+enum class StepKind { generic, integer_conv, chunk_add };
+
+struct Executor::Step {
+    StepKind kind{StepKind::generic};
+    std::size_t node{0};
+    std::vector<std::size_t> reads;
+    std::size_t output{0};
+    // integer conv
+    int conv{-1};
+    std::size_t source{0};
+    bool fused_im2col{false};
+    kernels::Window window{1, 1, 1, 1, 0, 0};
+    bool wsilu{false};
+    float wsilu_scale{0.0f};
+    bool chunk_add{false};
+    std::optional<std::size_t> residual;
+};
+
+struct PlannedConv {
+    std::size_t pixel_max{0}, a_high{0}, a_low{0}, exponents{0}, column_terms{0};
+    int positions{0}, positions_padded{0};
+    kernels::GemmMaps maps{};
+};
+
+struct Executor::Plan {
+    std::vector<Extent> extents;
+    std::vector<std::size_t> offsets;  // per tensor id, npos when not materialised
+    std::vector<PlannedConv> convs;    // per step
+    std::size_t arena_bytes{0};
+    std::uint64_t maps_generation{0};
+};
+
+namespace {
+
+constexpr std::size_t npos = std::numeric_limits<std::size_t>::max();
+constexpr std::size_t alignment = 1024;
+
+std::size_t align_up(std::size_t value, std::size_t to) { return (value + to - 1) / to * to; }
+int round_up(int value, int to) { return (value + to - 1) / to * to; }
+
+Error cuda_error(const char* what, cudaError_t status) {
+    return fail(Code::backend_error, std::string(what) + ": " + cudaGetErrorString(status));
+}
+
+// First-fit allocator over one arena: offsets only, no device memory.
+class OffsetAllocator {
+public:
+    std::size_t allocate(std::size_t bytes) {
+        bytes = align_up(std::max<std::size_t>(bytes, 1), alignment);
+        for (auto it = free_.begin(); it != free_.end(); ++it) {
+            if (it->second >= bytes) {
+                const std::size_t offset = it->first;
+                const std::size_t remaining = it->second - bytes;
+                free_.erase(it);
+                if (remaining > 0) free_.insert({offset + bytes, remaining});
+                sizes_[offset] = bytes;
+                return offset;
+            }
+        }
+        const std::size_t offset = top_;
+        top_ += bytes;
+        sizes_[offset] = bytes;
+        return offset;
+    }
+    void release(std::size_t offset) {
+        auto found = sizes_.find(offset);
+        if (found == sizes_.end()) return;
+        std::size_t start = offset;
+        std::size_t size = found->second;
+        sizes_.erase(found);
+        // Coalesce with free neighbours.
+        auto next = free_.lower_bound({start, 0});
+        if (next != free_.end() && next->first == start + size) {
+            size += next->second;
+            next = free_.erase(next);
+        }
+        if (next != free_.begin()) {
+            auto previous = std::prev(next);
+            if (previous->first + previous->second == start) {
+                start = previous->first;
+                size += previous->second;
+                free_.erase(previous);
+            }
+        }
+        if (start + size == top_) {
+            top_ = start;
+        } else {
+            free_.insert({start, size});
+        }
+    }
+    std::size_t peak() const { return peak_ = std::max(peak_, top_), peak_; }
+    void note_peak() { peak_ = std::max(peak_, top_); }
+
+private:
+    std::set<std::pair<std::size_t, std::size_t>> free_;
+    std::map<std::size_t, std::size_t> sizes_;
+    std::size_t top_{0};
+    mutable std::size_t peak_{0};
+};
+
+const TensorView* find_view(const std::vector<TensorView>& views, const std::string& name) {
+    for (const auto& view : views) {
+        if (view.name == name) return &view;
+    }
+    return nullptr;
+}
+
+const char* op_name(Op op) {
+    switch (op) {
+    case Op::conv: return "conv";
+    case Op::mul: return "mul";
+    case Op::add: return "add";
+    case Op::mul_scalar: return "mul_scalar";
+    case Op::sigmoid: return "sigmoid";
+    case Op::slice_channels: return "slice_channels";
+    case Op::depth_to_space: return "depth_to_space";
+    case Op::scale_channels: return "scale_channels";
+    case Op::clamp: return "clamp";
+    case Op::concat: return "concat";
+    case Op::crop: return "crop";
+    case Op::space_to_depth: return "space_to_depth";
+    case Op::im2col: return "im2col";
+    }
+    return "?";
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- creation
+
+Result<std::unique_ptr<Executor>> Executor::create(Program program, cudaStream_t stream) {
+    std::unique_ptr<Executor> executor(new Executor());
+    executor->program_ = std::move(program);
+    int device = 0;
+    cudaError_t status = cudaGetDevice(&device);
+    int major = 0;
+    int minor = 0;
+    if (status == cudaSuccess) status = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+    if (status == cudaSuccess) status = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
+    if (status != cudaSuccess) return cuda_error("cudaDeviceGetAttribute", status);
+    if (major != 10 || minor != 0) {
+        return fail(Code::incompatible_target,
+                    std::string(intconv_profile) + " on this provider needs an sm_100 (B200-class) GPU");
+    }
+    if (stream != nullptr) {
+        executor->stream_ = stream;
+    } else {
+        status = cudaStreamCreateWithFlags(&executor->stream_, cudaStreamNonBlocking);
+        if (status != cudaSuccess) return cuda_error("cudaStreamCreate", status);
+        executor->owns_stream_ = true;
+    }
+    auto prepared = executor->prepare();
+    if (!prepared) return prepared.error();
+    return executor;
+}
+
+Executor::~Executor() {
+    if (stream_ != nullptr) cudaStreamSynchronize(stream_);
+    for (auto& conv : convs_) cudaFree(conv.allocation);
+    for (auto event : events_) cudaEventDestroy(event);
+    cudaFree(arena_);
+    cudaFree(weights_);
+    cudaFree(status_);
+    if (owns_stream_ && stream_ != nullptr) cudaStreamDestroy(stream_);
+}
+
+Status Executor::prepare() {
+    const std::size_t bytes = std::max<std::size_t>(program_.weights.size(), 1) * sizeof(float);
+    cudaError_t status = cudaMalloc(reinterpret_cast<void**>(&weights_), bytes);
+    if (status != cudaSuccess) return cuda_error("cudaMalloc weights", status);
+    status = cudaMemcpy(weights_, program_.weights.data(), program_.weights.size() * sizeof(float),
+                        cudaMemcpyHostToDevice);
+    if (status != cudaSuccess) return cuda_error("cudaMemcpy weights", status);
+    status = cudaMalloc(reinterpret_cast<void**>(&status_), sizeof(unsigned int));
+    if (status != cudaSuccess) return cuda_error("cudaMalloc status", status);
+    status = cudaMemset(status_, 0, sizeof(unsigned int));
+    if (status != cudaSuccess) return cuda_error("cudaMemset status", status);
+    plan_fusions();
+    for (std::size_t index = 0; index < steps_.size(); ++index) {
+        if (steps_[index].kind != StepKind::integer_conv) continue;
+        auto prepared = prepare_integer_conv(index);
+        if (!prepared) return prepared;
+    }
+    return Ok{};
+}
+
+// Folds node patterns into single steps. Only tensors that no other node reads
+// and that are not program outputs are folded away, so every observable tensor
+// keeps its bits; the arithmetic per element is unchanged by folding.
+void Executor::plan_fusions() {
+    const auto& nodes = program_.nodes;
+    const std::size_t tensor_count = program_.tensor_names.size();
+    std::vector<int> readers(tensor_count, 0);
+    std::vector<std::ptrdiff_t> producer(tensor_count, -1);
+    std::vector<bool> is_output(tensor_count, false);
+    for (std::size_t i = 0; i < nodes.size(); ++i) {
+        for (std::size_t slot = 0; slot < nodes[i].input_count; ++slot) ++readers[nodes[i].inputs[slot]];
+        producer[nodes[i].output] = static_cast<std::ptrdiff_t>(i);
+    }
+    for (const auto id : program_.outputs) is_output[id] = true;
+    auto private_tensor = [&](std::size_t id, int expected) { return readers[id] == expected && !is_output[id]; };
+    auto same_pair = [](const Node& node, std::size_t a, std::size_t b) {
+        return (node.inputs[0] == a && node.inputs[1] == b) || (node.inputs[0] == b && node.inputs[1] == a);
+    };
+    // nodes[at..at+2] = slice(source, 0, C/2), slice(source, C/2, C), add of the two.
+    auto chunk_add_at = [&](std::size_t at, std::size_t source) {
+        if (at + 2 >= nodes.size()) return false;
+        const auto& first = nodes[at];
+        const auto& second = nodes[at + 1];
+        const auto& sum = nodes[at + 2];
+        const auto channels = program_.tensor_channels[source];
+        return channels % 2 == 0 && first.op == Op::slice_channels && first.inputs[0] == source &&
+            second.op == Op::slice_channels && second.inputs[0] == source && first.begin == 0 &&
+            first.end == channels / 2 && second.begin == channels / 2 && second.end == channels &&
+            sum.op == Op::add && sum.input_count == 2 && same_pair(sum, first.output, second.output) &&
+            first.output != second.output && private_tensor(first.output, 1) && private_tensor(second.output, 1);
+    };
+
+    std::vector<bool> absorbed(nodes.size(), false);
+    std::vector<std::ptrdiff_t> im2col_of(nodes.size(), -1);
+    for (std::size_t i = 0; i < nodes.size(); ++i) {
+        if (!is_integer_pointwise(nodes[i])) continue;
+        const auto input = nodes[i].inputs[0];
+        const auto j = producer[input];
+        if (j >= 0 && nodes[static_cast<std::size_t>(j)].op == Op::im2col && private_tensor(input, 1)) {
+            im2col_of[i] = j;
+            absorbed[static_cast<std::size_t>(j)] = true;
+        }
+    }
+
+    steps_.clear();
+    for (std::size_t i = 0; i < nodes.size(); ++i) {
+        if (absorbed[i]) continue;
+        const auto& node = nodes[i];
+        Step step;
+        step.node = i;
+        if (is_integer_pointwise(node)) {
+            step.kind = StepKind::integer_conv;
+            step.source = node.inputs[0];
+            if (im2col_of[i] >= 0) {
+                const auto& cols = nodes[static_cast<std::size_t>(im2col_of[i])];
+                step.fused_im2col = true;
+                step.source = cols.inputs[0];
+                step.window = kernels::Window{cols.kernel[0], cols.kernel[1], cols.stride[0], cols.stride[1],
+                                              cols.pads[0], cols.pads[1]};
+            }
+            std::size_t out = node.output;
+            std::size_t last = i;
+            if (i + 3 < nodes.size()) {
+                const auto& scale = nodes[i + 1];
+                const auto& gate = nodes[i + 2];
+                const auto& product = nodes[i + 3];
+                if (scale.op == Op::mul_scalar && scale.inputs[0] == out && gate.op == Op::sigmoid &&
+                    gate.inputs[0] == scale.output && product.op == Op::mul && product.input_count == 2 &&
+                    same_pair(product, gate.output, out) && gate.output != out && private_tensor(out, 2) &&
+                    private_tensor(scale.output, 1) && private_tensor(gate.output, 1)) {
+                    step.wsilu = true;
+                    step.wsilu_scale = scale.scalar;
+                    out = product.output;
+                    last = i + 3;
+                }
+            }
+            if (last + 3 < nodes.size() && private_tensor(out, 2) && chunk_add_at(last + 1, out)) {
+                step.chunk_add = true;
+                out = nodes[last + 3].output;
+                last += 3;
+            }
+            if (last + 1 < nodes.size() && nodes[last + 1].op == Op::add && nodes[last + 1].input_count == 2 &&
+                private_tensor(out, 1)) {
+                const auto& sum = nodes[last + 1];
+                const std::size_t other = sum.inputs[0] == out ? sum.inputs[1]
+                    : (sum.inputs[1] == out ? sum.inputs[0] : out);
+                if (other != out && producer[other] < static_cast<std::ptrdiff_t>(i)) {
+                    step.residual = other;
+                    out = sum.output;
+                    last += 1;
+                }
+            }
+            for (std::size_t folded = i + 1; folded <= last; ++folded) absorbed[folded] = true;
+            step.output = out;
+            step.reads.push_back(step.source);
+            if (step.residual) step.reads.push_back(*step.residual);
+        } else if (node.op == Op::slice_channels && chunk_add_at(i, node.inputs[0])) {
+            step.kind = StepKind::chunk_add;
+            step.source = node.inputs[0];
+            step.output = nodes[i + 2].output;
+            step.reads.push_back(step.source);
+            absorbed[i + 1] = true;
+            absorbed[i + 2] = true;
+        } else {
+            step.kind = StepKind::generic;
+            step.output = node.output;
+            for (std::size_t slot = 0; slot < node.input_count; ++slot) step.reads.push_back(node.inputs[slot]);
+        }
+        steps_.push_back(std::move(step));
+    }
+}
+
+// Quantises one integer conv's weights into int8 limb matrices
+// [n_tiles * n_tile][k_padded] (K contiguous, zero padded) with per-row scale,
+// bias and exact row term, and encodes their TMA maps.
+Status Executor::prepare_integer_conv(std::size_t step_index) {
+    Step& step = steps_[step_index];
+    const Node& node = program_.nodes[step.node];
+    IntegerConv conv;
+    conv.weight_limbs = node.weight_bits == 16 ? 2 : 1;
+    conv.activation_limbs = node.activation_bits == 16 ? 2 : 1;
+    conv.activation_bits = node.activation_bits;
+    conv.k_real = node.in_channels;
+    if (conv.k_real > 65536) {
+        return fail(Code::invalid_argument, "integer conv reduction length above 65536 is not supported");
+    }
+    conv.k_padded = round_up(conv.k_real, 128);
+    conv.chunk_add = step.chunk_add;
+    const int rows = node.out_channels;
+    const int accumulators = 1 + ((conv.weight_limbs == 2 || conv.activation_limbs == 2) ? 1 : 0) +
+        ((conv.weight_limbs == 2 && conv.activation_limbs == 2) ? 1 : 0);
+    const int max_tile = accumulators == 3 ? 128 : 256;
+    if (conv.chunk_add) {
+        const int pairs = rows / 2;
+        conv.n_tiles = (2 * pairs + max_tile - 1) / max_tile;
+        conv.n_tile = round_up((pairs + conv.n_tiles - 1) / conv.n_tiles, 16) * 2;
+        conv.out_channels = pairs;
+    } else {
+        conv.n_tiles = (rows + max_tile - 1) / max_tile;
+        conv.n_tile = round_up((rows + conv.n_tiles - 1) / conv.n_tiles, 16);
+        conv.out_channels = rows;
+    }
+    const int n_padded = conv.n_tiles * conv.n_tile;
+    // Physical weight row -> node row (-1: zero padding). A chunk-add conv puts
+    // pair (c, c + C/2) in columns j and j + n_tile/2 of one tile.
+    auto source_row = [&](int physical) -> int {
+        if (!conv.chunk_add) return physical < rows ? physical : -1;
+        const int tile = physical / conv.n_tile;
+        const int local = physical % conv.n_tile;
+        const int half = conv.n_tile / 2;
+        const int pair = tile * half + (local % half);
+        if (pair >= rows / 2) return -1;
+        return local < half ? pair : rows / 2 + pair;
+    };
+
+    const auto quantized = quantize_weights(program_, node);
+    const std::size_t matrix = static_cast<std::size_t>(n_padded) * conv.k_padded;
+    std::vector<std::int8_t> high(matrix, 0);
+    std::vector<std::int8_t> low(conv.weight_limbs == 2 ? matrix : 0, 0);
+    std::vector<float> scales(n_padded, 0.0f);
+    std::vector<float> bias(n_padded, 0.0f);
+    std::vector<long long> row_terms(n_padded, 0);
+    const long long aw = conv.weight_limbs == 2 ? 256 : 1;
+    const long long cw = conv.weight_limbs == 2 ? 128 : 0;
+    const long long cx = conv.activation_limbs == 2 ? 128 : 0;
+    for (int physical = 0; physical < n_padded; ++physical) {
+        const int row = source_row(physical);
+        if (row < 0) continue;
+        scales[physical] = quantized.scales[static_cast<std::size_t>(row)];
+        bias[physical] = program_.weights[node.bias_offset + static_cast<std::size_t>(row)];
+        long long high_sum = 0;
+        long long low_sum = 0;
+        for (int k = 0; k < conv.k_real; ++k) {
+            const int q = quantized.values[static_cast<std::size_t>(row) * conv.k_real + k];
+            const std::size_t at = static_cast<std::size_t>(physical) * conv.k_padded + k;
+            if (conv.weight_limbs == 2) {
+                const int h = q >> 8;  // arithmetic shift: floor(q / 256)
+                const int l = (q & 255) - 128;
+                high[at] = static_cast<std::int8_t>(h);
+                low[at] = static_cast<std::int8_t>(l);
+                high_sum += h;
+                low_sum += l;
+            } else {
+                high[at] = static_cast<std::int8_t>(q);
+                high_sum += q;
+            }
+        }
+        // cx (aw sum Wh + sum Wl') + K cw cx
+        row_terms[physical] = cx * (aw * high_sum + low_sum) + static_cast<long long>(conv.k_real) * cw * cx;
+    }
+    // column term factors: cw (ax sum Xh + sum Xl')
+    const long long ax = conv.activation_limbs == 2 ? 256 : 1;
+    conv.column_high_factor = cw * ax;
+    conv.column_low_factor = conv.activation_limbs == 2 ? cw : 0;
+
+    // One allocation: [high][low][scales][bias][row_terms], each 1024-aligned.
+    const std::size_t high_at = 0;
+    const std::size_t low_at = align_up(high_at + matrix, alignment);
+    const std::size_t scales_at = align_up(low_at + low.size(), alignment);
+    const std::size_t bias_at = align_up(scales_at + n_padded * sizeof(float), alignment);
+    const std::size_t terms_at = align_up(bias_at + n_padded * sizeof(float), alignment);
+    const std::size_t total = align_up(terms_at + n_padded * sizeof(long long), alignment);
+    cudaError_t status = cudaMalloc(&conv.allocation, total);
+    if (status != cudaSuccess) return cuda_error("cudaMalloc integer weights", status);
+    auto* base = static_cast<std::uint8_t*>(conv.allocation);
+    conv.b_high = reinterpret_cast<std::int8_t*>(base + high_at);
+    conv.b_low = conv.weight_limbs == 2 ? reinterpret_cast<std::int8_t*>(base + low_at) : conv.b_high;
+    conv.scales = reinterpret_cast<float*>(base + scales_at);
+    conv.bias = reinterpret_cast<float*>(base + bias_at);
+    conv.row_terms = reinterpret_cast<long long*>(base + terms_at);
+    struct Upload {
+        void* to;
+        const void* from;
+        std::size_t bytes;
+    };
+    const Upload uploads[] = {{conv.b_high, high.data(), high.size()},
+                              {base + low_at, low.data(), low.size()},
+                              {conv.scales, scales.data(), scales.size() * sizeof(float)},
+                              {conv.bias, bias.data(), bias.size() * sizeof(float)},
+                              {conv.row_terms, row_terms.data(), row_terms.size() * sizeof(long long)}};
+    for (const auto& upload : uploads) {
+        if (upload.bytes == 0) continue;
+        status = cudaMemcpy(upload.to, upload.from, upload.bytes, cudaMemcpyHostToDevice);
+        if (status != cudaSuccess) {
+            cudaFree(conv.allocation);
+            return cuda_error("cudaMemcpy integer weights", status);
+        }
+    }
+    status = kernels::encode_int8_map(&conv.b_high_map, conv.b_high, n_padded, conv.k_padded, conv.n_tile);
+    if (status == cudaSuccess) {
+        status = kernels::encode_int8_map(&conv.b_low_map, conv.b_low, n_padded, conv.k_padded, conv.n_tile);
+    }
+    if (status != cudaSuccess) {
+        cudaFree(conv.allocation);
+        return cuda_error("cuTensorMapEncodeTiled weights", status);
+    }
+    step.conv = static_cast<int>(convs_.size());
+    convs_.push_back(conv);
+    return Ok{};
+}
+
+// ---------------------------------------------------------------- planning
+
+Result<Executor::Plan*> Executor::plan_for(const std::vector<Extent>& input_extents) {
+    std::vector<std::int32_t> key;
+    for (const auto& e : input_extents) {
+        key.push_back(e.channels);
+        key.push_back(e.height);
+        key.push_back(e.width);
+    }
+    if (auto found = plans_.find(key); found != plans_.end()) return found->second.get();
+
+    auto plan = std::make_unique<Plan>();
+    const std::size_t tensor_count = program_.tensor_names.size();
+    plan->extents.assign(tensor_count, Extent{});
+    plan->offsets.assign(tensor_count, npos);
+    plan->convs.assign(steps_.size(), PlannedConv{});
+    // Extents of every tensor, validated exactly as the reference validates them.
+    for (std::size_t slot = 0; slot < program_.inputs.size(); ++slot) {
+        plan->extents[program_.inputs[slot]] = input_extents[slot];
+    }
+    for (const auto& node : program_.nodes) {
+        Extent in[2] = {plan->extents[node.inputs[0]], plan->extents[node.inputs[1]]};
+        auto extent = output_extent(program_, node, in, node.input_count);
+        if (!extent) return extent.error();
+        plan->extents[node.output] = extent.value();
+    }
+    for (const auto& step : steps_) {
+        if (step.kind == StepKind::chunk_add) {
+            const Extent source = plan->extents[step.source];
+            plan->extents[step.output] = Extent{source.channels / 2, source.height, source.width};
+        }
+    }
+
+    // Lifetimes in steps: a tensor is freed after the last step that reads it.
+    const std::size_t step_count = steps_.size();
+    std::vector<std::ptrdiff_t> last_read(tensor_count, -1);
+    for (std::size_t s = 0; s < step_count; ++s) {
+        for (const auto id : steps_[s].reads) last_read[id] = static_cast<std::ptrdiff_t>(s);
+    }
+    std::vector<bool> pinned(tensor_count, false);
+    for (const auto id : program_.outputs) pinned[id] = true;
+    for (const auto id : program_.inputs) pinned[id] = pinned[id] || last_read[id] < 0;
+
+    OffsetAllocator allocator;
+    auto tensor_bytes = [&](std::size_t id) { return plan->extents[id].count() * sizeof(float); };
+    for (const auto id : program_.inputs) {
+        if (plan->offsets[id] == npos) plan->offsets[id] = allocator.allocate(tensor_bytes(id));
+    }
+    allocator.note_peak();
+    for (std::size_t s = 0; s < step_count; ++s) {
+        const Step& step = steps_[s];
+        plan->offsets[step.output] = allocator.allocate(tensor_bytes(step.output));
+        std::vector<std::size_t> scratch;
+        if (step.kind == StepKind::integer_conv) {
+            const IntegerConv& conv = convs_[static_cast<std::size_t>(step.conv)];
+            const Node& node = program_.nodes[step.node];
+            const Extent source = plan->extents[step.source];
+            const Extent out = plan->extents[node.output];
+            PlannedConv& pc = plan->convs[s];
+            pc.positions = out.height * out.width;
+            pc.positions_padded = round_up(std::max(pc.positions, 1), 128);
+            if (pc.positions_padded / 128 > 65535) {
+                return fail(Code::invalid_argument, "integer conv has too many output positions");
+            }
+            const std::size_t matrix = static_cast<std::size_t>(pc.positions_padded) * conv.k_padded;
+            pc.pixel_max = allocator.allocate(static_cast<std::size_t>(source.height) * source.width * sizeof(float));
+            pc.a_high = allocator.allocate(matrix);
+            pc.a_low = conv.activation_limbs == 2 ? allocator.allocate(matrix) : pc.a_high;
+            pc.exponents = allocator.allocate(static_cast<std::size_t>(pc.positions) * sizeof(int));
+            pc.column_terms = conv.weight_limbs == 2
+                ? allocator.allocate(static_cast<std::size_t>(pc.positions) * sizeof(long long)) : npos;
+            scratch = {pc.pixel_max, pc.a_high, pc.exponents};
+            if (conv.activation_limbs == 2) scratch.push_back(pc.a_low);
+            if (pc.column_terms != npos) scratch.push_back(pc.column_terms);
+        }
+        allocator.note_peak();
+        for (const auto offset : scratch) allocator.release(offset);
+        // Release what this step read for the last time, and a dead output.
+        std::set<std::size_t> done(step.reads.begin(), step.reads.end());
+        done.insert(step.output);
+        for (const auto id : done) {
+            if (!pinned[id] && last_read[id] <= static_cast<std::ptrdiff_t>(s) && plan->offsets[id] != npos) {
+                allocator.release(plan->offsets[id]);
+            }
+        }
+    }
+    plan->arena_bytes = std::max<std::size_t>(allocator.peak(), alignment);
+    auto* raw = plan.get();
+    plans_.emplace(std::move(key), std::move(plan));
+    return raw;
+}
+
+Status Executor::ensure_arena(std::size_t bytes) {
+    if (bytes <= arena_bytes_ && arena_ != nullptr) return Ok{};
+    if (arena_ != nullptr) {
+        // In-flight work may still use the old arena.
+        const cudaError_t synced = cudaStreamSynchronize(stream_);
+        if (synced != cudaSuccess) return cuda_error("cudaStreamSynchronize", synced);
+        cudaFree(arena_);
+        arena_ = nullptr;
+        arena_bytes_ = 0;
+    }
+    const cudaError_t status = cudaMalloc(&arena_, bytes);
+    if (status != cudaSuccess) {
+        return fail(Code::resource_exhausted, std::string("cudaMalloc workspace: ") + cudaGetErrorString(status));
+    }
+    arena_bytes_ = bytes;
+    ++arena_generation_;
+    return Ok{};
+}
+
+Status Executor::encode_activation_maps(Plan& plan) {
+    if (plan.maps_generation == arena_generation_) return Ok{};
+    auto* base = static_cast<std::uint8_t*>(arena_);
+    for (std::size_t s = 0; s < steps_.size(); ++s) {
+        if (steps_[s].kind != StepKind::integer_conv) continue;
+        const IntegerConv& conv = convs_[static_cast<std::size_t>(steps_[s].conv)];
+        PlannedConv& pc = plan.convs[s];
+        cudaError_t status = kernels::encode_int8_map(&pc.maps.a_high, base + pc.a_high, pc.positions_padded,
+                                                      conv.k_padded, 128);
+        if (status == cudaSuccess) {
+            status = kernels::encode_int8_map(&pc.maps.a_low, base + pc.a_low, pc.positions_padded, conv.k_padded,
+                                              128);
+        }
+        if (status != cudaSuccess) return cuda_error("cuTensorMapEncodeTiled activations", status);
+        pc.maps.b_high = conv.b_high_map;
+        pc.maps.b_low = conv.b_low_map;
+    }
+    plan.maps_generation = arena_generation_;
+    return Ok{};
+}
+
+// ---------------------------------------------------------------- execution
+
+Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
+    auto* base = static_cast<std::uint8_t*>(arena_);
+    auto tensor = [&](std::size_t id) { return reinterpret_cast<float*>(base + plan.offsets[id]); };
+    const Node& node = program_.nodes[step.node];
+    const Extent out_extent = plan.extents[step.output];
+    const std::size_t count = out_extent.count();
+    cudaError_t status = cudaSuccess;
+    int launched = 1;
+    switch (step.kind) {
+    case StepKind::integer_conv: {
+        const IntegerConv& conv = convs_[static_cast<std::size_t>(step.conv)];
+        const PlannedConv& pc = plan.convs[index];
+        const Extent source = plan.extents[step.source];
+        const Extent conv_out = plan.extents[node.output];
+        kernels::QuantizeArgs q{};
+        q.in = tensor(step.source);
+        q.channels = source.channels;
+        q.in_h = source.height;
+        q.in_w = source.width;
+        q.out_h = conv_out.height;
+        q.out_w = conv_out.width;
+        q.window = step.window;
+        q.k_padded = conv.k_padded;
+        q.positions_padded = pc.positions_padded;
+        q.pixel_max = reinterpret_cast<float*>(base + pc.pixel_max);
+        q.high = reinterpret_cast<std::int8_t*>(base + pc.a_high);
+        q.low = reinterpret_cast<std::int8_t*>(base + pc.a_low);
+        q.exponents = reinterpret_cast<int*>(base + pc.exponents);
+        q.column_terms = pc.column_terms == npos ? nullptr : reinterpret_cast<long long*>(base + pc.column_terms);
+        q.activation_bits = conv.activation_bits;
+        q.high_factor = conv.column_high_factor;
+        q.low_factor = conv.column_low_factor;
+        status = kernels::quantize_activations(q, stream_);
+        if (status != cudaSuccess) return cuda_error("activation quantiser launch", status);
+        kernels::GemmShape shape{conv.weight_limbs, conv.activation_limbs, conv.n_tile, conv.n_tiles, conv.k_padded,
+                                 pc.positions_padded};
+        kernels::GemmEpilogue ep{};
+        ep.scales = conv.scales;
+        ep.bias = conv.bias;
+        ep.row_terms = conv.activation_limbs == 2 ? conv.row_terms : nullptr;
+        ep.exponents = q.exponents;
+        ep.column_terms = q.column_terms;
+        ep.wsilu = step.wsilu ? 1 : 0;
+        ep.wsilu_scale = step.wsilu_scale;
+        ep.chunk_add = step.chunk_add ? 1 : 0;
+        ep.residual = step.residual ? tensor(*step.residual) : nullptr;
+        ep.out = tensor(step.output);
+        ep.out_half = 0;
+        ep.out_channels = conv.out_channels;
+        ep.positions = pc.positions;
+        ep.status = status_;
+        status = kernels::integer_gemm(pc.maps, shape, ep, stream_);
+        if (status != cudaSuccess) return cuda_error("integer conv launch", status);
+        launched = 3;
+        break;
+    }
+    case StepKind::chunk_add:
+        status = kernels::chunk_add(tensor(step.source), tensor(step.output), count, stream_);
+        break;
+    case StepKind::generic: {
+        const float* a = tensor(node.inputs[0]);
+        const Extent in = plan.extents[node.inputs[0]];
+        float* out = tensor(step.output);
+        switch (node.op) {
+        case Op::conv: {
+            kernels::ConvShape shape{node.in_channels, node.out_channels, node.depthwise ? 1 : 0, in.height, in.width,
+                                     out_extent.height, out_extent.width,
+                                     kernels::Window{node.kernel[0], node.kernel[1], node.stride[0], node.stride[1],
+                                                     node.pads[0], node.pads[1]}};
+            status = kernels::conv_fp32(weights_ + node.weight_offset, weights_ + node.bias_offset, a, out, shape,
+                                        stream_);
+            break;
+        }
+        case Op::mul:
+        case Op::add:
+            status = kernels::binary(node.op == Op::mul ? kernels::Binary::mul : kernels::Binary::add, a,
+                                     tensor(node.inputs[1]), out, count, stream_);
+            break;
+        case Op::mul_scalar:
+            status = kernels::mul_scalar(a, node.scalar, out, count, stream_);
+            break;
+        case Op::sigmoid:
+            status = kernels::sigmoid(a, out, count, stream_);
+            break;
+        case Op::slice_channels:
+            status = kernels::copy(a + static_cast<std::size_t>(node.begin) * in.height * in.width, out, count,
+                                   stream_);
+            launched = 0;
+            break;
+        case Op::depth_to_space:
+            status = kernels::depth_to_space(a, out, out_extent.channels, out_extent.height, out_extent.width,
+                                             in.height, in.width, node.block, stream_);
+            break;
+        case Op::space_to_depth:
+            status = kernels::space_to_depth(a, out, out_extent.channels, out_extent.height, out_extent.width,
+                                             in.height, in.width, node.block, stream_);
+            break;
+        case Op::scale_channels:
+            status = kernels::scale_channels(a, tensor(node.inputs[1]), out, count,
+                                             static_cast<std::size_t>(in.height) * in.width, stream_);
+            break;
+        case Op::clamp:
+            status = kernels::clamp(a, node.minimum, node.maximum, out, count, stream_);
+            break;
+        case Op::crop:
+            status = kernels::crop(a, out, out_extent.channels, out_extent.height, out_extent.width, in.height,
+                                   in.width, stream_);
+            break;
+        case Op::concat: {
+            const std::size_t head = in.count();
+            status = kernels::copy(a, out, head, stream_);
+            if (status == cudaSuccess) status = kernels::copy(tensor(node.inputs[1]), out + head, count - head, stream_);
+            launched = 0;
+            break;
+        }
+        case Op::im2col:
+            status = kernels::im2col(a, out, out_extent.channels, out_extent.height, out_extent.width, in.height,
+                                     in.width,
+                                     kernels::Window{node.kernel[0], node.kernel[1], node.stride[0], node.stride[1],
+                                                     node.pads[0], node.pads[1]},
+                                     stream_);
+            break;
+        }
+        break;
+    }
+    }
+    if (status != cudaSuccess) return cuda_error(op_name(node.op), status);
+    launches_ += launched;
+    return Ok{};
+}
+
+Status Executor::execute(const std::vector<TensorView>& inputs, const std::vector<TensorView>& outputs,
+                         Boundary boundary) {
+    std::vector<Extent> extents;
+    std::vector<const TensorView*> input_views;
+    for (const auto id : program_.inputs) {
+        const auto& name = program_.tensor_names[id];
+        const TensorView* view = find_view(inputs, name);
+        if (view == nullptr || view->data == nullptr || view->extent.channels != program_.tensor_channels[id] ||
+            view->extent.height <= 0 || view->extent.width <= 0) {
+            return fail(Code::invalid_argument, program_.name + ": missing or misshapen input " + name);
+        }
+        extents.push_back(view->extent);
+        input_views.push_back(view);
+    }
+    auto planned = plan_for(extents);
+    if (!planned) return planned.error();
+    Plan& plan = *planned.value();
+    std::vector<const TensorView*> output_views;
+    for (const auto id : program_.outputs) {
+        const auto& name = program_.tensor_names[id];
+        const TensorView* view = find_view(outputs, name);
+        if (view == nullptr || view->data == nullptr || !(view->extent == plan.extents[id])) {
+            return fail(Code::invalid_argument, program_.name + ": missing or misshapen output " + name);
+        }
+        output_views.push_back(view);
+    }
+    auto arena = ensure_arena(plan.arena_bytes);
+    if (!arena) return arena;
+    auto maps = encode_activation_maps(plan);
+    if (!maps) return maps;
+
+    launches_ = 0;
+    const bool timing = profiling_;
+    std::vector<std::string> labels;
+    std::vector<std::string> kernel_names;
+    std::vector<double> ops;
+    std::vector<double> bytes;
+    std::size_t event_count = 0;
+    auto mark = [&]() -> Status {
+        if (!timing) return Ok{};
+        if (event_count >= events_.size()) {
+            cudaEvent_t event;
+            const cudaError_t created = cudaEventCreate(&event);
+            if (created != cudaSuccess) return cuda_error("cudaEventCreate", created);
+            events_.push_back(event);
+        }
+        const cudaError_t recorded = cudaEventRecord(events_[event_count++], stream_);
+        if (recorded != cudaSuccess) return cuda_error("cudaEventRecord", recorded);
+        return Ok{};
+    };
+
+    auto* base = static_cast<std::uint8_t*>(arena_);
+    auto first = mark();
+    if (!first) return first;
+    for (std::size_t slot = 0; slot < program_.inputs.size(); ++slot) {
+        const auto id = program_.inputs[slot];
+        float* target = reinterpret_cast<float*>(base + plan.offsets[id]);
+        const std::size_t count = plan.extents[id].count();
+        cudaError_t status;
+        if (boundary == Boundary::half) {
+            status = kernels::half_to_float(static_cast<const std::uint16_t*>(input_views[slot]->data), target, count,
+                                            stream_);
+            ++launches_;
+        } else {
+            status = cudaMemcpyAsync(target, input_views[slot]->data, count * sizeof(float),
+                                     boundary == Boundary::host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice,
+                                     stream_);
+        }
+        if (status != cudaSuccess) return cuda_error("input conversion", status);
+    }
+    if (timing) {
+        labels.push_back("inputs");
+        kernel_names.push_back("half_to_float");
+        ops.push_back(0.0);
+        double b = 0.0;
+        for (const auto id : program_.inputs) b += static_cast<double>(plan.extents[id].count()) * 6.0;
+        bytes.push_back(b);
+        auto m = mark();
+        if (!m) return m;
+    }
+    for (std::size_t s = 0; s < steps_.size(); ++s) {
+        auto launched = launch_step(steps_[s], plan, s);
+        if (!launched) return launched;
+        if (timing) {
+            const Step& step = steps_[s];
+            const Node& node = program_.nodes[step.node];
+            labels.push_back(std::string(op_name(node.op)) + ":" + program_.tensor_names[step.output]);
+            double o = 0.0;
+            double b = static_cast<double>(plan.extents[step.output].count()) * 4.0;
+            for (const auto id : step.reads) b += static_cast<double>(plan.extents[id].count()) * 4.0;
+            if (step.kind == StepKind::integer_conv) {
+                const Extent conv_out = plan.extents[node.output];
+                o = 2.0 * node.in_channels * static_cast<double>(node.out_channels) * conv_out.height * conv_out.width;
+                b += static_cast<double>(node.in_channels) * node.out_channels;  // int8 weights
+                kernel_names.push_back("integer_gemm");
+            } else {
+                kernel_names.push_back(op_name(node.op));
+            }
+            ops.push_back(o);
+            bytes.push_back(b);
+            auto m = mark();
+            if (!m) return m;
+        }
+    }
+    for (std::size_t slot = 0; slot < program_.outputs.size(); ++slot) {
+        const auto id = program_.outputs[slot];
+        const float* source = reinterpret_cast<const float*>(base + plan.offsets[id]);
+        const std::size_t count = plan.extents[id].count();
+        cudaError_t status;
+        if (boundary == Boundary::half) {
+            status = kernels::float_to_half(source, static_cast<std::uint16_t*>(output_views[slot]->data), count,
+                                            stream_);
+            ++launches_;
+        } else {
+            status = cudaMemcpyAsync(output_views[slot]->data, source, count * sizeof(float),
+                                     boundary == Boundary::host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice,
+                                     stream_);
+        }
+        if (status != cudaSuccess) return cuda_error("output conversion", status);
+    }
+    if (timing) {
+        labels.push_back("outputs");
+        kernel_names.push_back("float_to_half");
+        ops.push_back(0.0);
+        double b = 0.0;
+        for (const auto id : program_.outputs) b += static_cast<double>(plan.extents[id].count()) * 6.0;
+        bytes.push_back(b);
+        auto m = mark();
+        if (!m) return m;
+        timings_.clear();
+        for (std::size_t i = 0; i < labels.size(); ++i) {
+            timings_.push_back(StepTiming{labels[i], kernel_names[i], 0.0, ops[i], bytes[i]});
+        }
+    }
+    if (boundary == Boundary::host) return synchronize();
+    return Ok{};
+}
+
+Status Executor::run_half(const std::vector<TensorView>& inputs, const std::vector<TensorView>& outputs) {
+    return execute(inputs, outputs, Boundary::half);
+}
+
+Status Executor::run_float(const std::vector<TensorView>& inputs, const std::vector<TensorView>& outputs) {
+    return execute(inputs, outputs, Boundary::float32);
+}
+
+Status Executor::run_host(const std::vector<TensorView>& inputs, const std::vector<TensorView>& outputs) {
+    return execute(inputs, outputs, Boundary::host);
+}
+
+Status Executor::synchronize() {
+    cudaError_t status = cudaStreamSynchronize(stream_);
+    if (status != cudaSuccess) return cuda_error("cudaStreamSynchronize", status);
+    unsigned int word = 0;
+    status = cudaMemcpy(&word, status_, sizeof(word), cudaMemcpyDeviceToHost);
+    if (status != cudaSuccess) return cuda_error("cudaMemcpy status", status);
+    if (word != 0) {
+        cudaMemset(status_, 0, sizeof(unsigned int));
+        return fail(Code::backend_error, "a device-side wait gave up (status word " + std::to_string(word) + ")");
+    }
+    return Ok{};
+}
+
+Result<std::vector<StepTiming>> Executor::profile() {
+    auto synced = synchronize();
+    if (!synced) return synced.error();
+    for (std::size_t i = 0; i < timings_.size() && i + 1 < events_.size(); ++i) {
+        float ms = 0.0f;
+        const cudaError_t status = cudaEventElapsedTime(&ms, events_[i], events_[i + 1]);
+        if (status != cudaSuccess) return cuda_error("cudaEventElapsedTime", status);
+        timings_[i].milliseconds = ms;
+    }
+    return timings_;
+}
+
+}  // namespace nvcr_sm100

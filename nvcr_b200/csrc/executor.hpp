@@ -1,0 +1,100 @@
+#pragma once
+
+// The sm_100a executor of intconv.v1 programs: the counterpart of the
+// reference's CudaExecutor (src/deterministic/cuda_executor.hpp:26-53).
+//
+//  * create(): uploads FP32 weights, quantises every integer pointwise conv's
+//    weights once into int8 limb matrices with their exact row terms, and plans
+//    fusions (im2col into the quantiser; WSiLU, chunk-add and residual add into
+//    the GEMM epilogue; slice/slice/add into one kernel).
+//  * run_half(): named batch-1 NCHW FP16 device tensors in and out; enqueues
+//    on the executor's stream and returns. The memory plan for a set of input
+//    extents is computed once (liveness-based offsets into one arena, TMA maps
+//    encoded against it) and reused: no allocation on the steady-state path.
+//  * run_host(): FP32 host tensors, synchronous (the conformance path).
+// One executor per stream; not thread-safe (as the reference's).
+
+#include "kernels.hpp"
+#include "program.hpp"
+#include "status.hpp"
+
+#include <cuda_runtime.h>
+
+#include <map>
+#include <memory>
+#include <optional>
+#include <string>
+#include <vector>
+
+namespace nvcr_sm100 {
+
+struct TensorView {
+    std::string name;
+    Extent extent;
+    void* data{nullptr};
+};
+
+struct StepTiming {
+    std::string label;  // "<op>:<output tensor>"
+    std::string kernel; // dominant kernel of the step
+    double milliseconds{0.0};
+    double algorithmic_ops{0.0};    // 2 * C_in * kh * kw * C_out * P for integer convs
+    double algorithmic_bytes{0.0};  // bytes read once + written once at the step's I/O types
+};
+
+class Executor {
+public:
+    static Result<std::unique_ptr<Executor>> create(Program program, cudaStream_t stream);
+    ~Executor();
+    Executor(const Executor&) = delete;
+    Executor& operator=(const Executor&) = delete;
+
+    const Program& program() const { return program_; }
+    cudaStream_t stream() const { return stream_; }
+
+    Status run_half(const std::vector<TensorView>& inputs, const std::vector<TensorView>& outputs);
+    Status run_float(const std::vector<TensorView>& inputs, const std::vector<TensorView>& outputs);
+    Status run_host(const std::vector<TensorView>& inputs, const std::vector<TensorView>& outputs);
+    // Waits for the stream and reports a device-side wait that gave up.
+    Status synchronize();
+
+    int launches_last_run() const { return launches_; }
+    std::size_t workspace_bytes() const { return arena_bytes_; }
+    void set_profiling(bool enabled) { profiling_ = enabled; }
+    // Per-step device times of the last profiled run (synchronises).
+    Result<std::vector<StepTiming>> profile();
+
+    struct IntegerConv;
+    struct Step;
+    struct Plan;
+
+private:
+    Executor() = default;
+    Status prepare();
+    Status prepare_integer_conv(std::size_t step_index);
+    void plan_fusions();
+    Result<Plan*> plan_for(const std::vector<Extent>& input_extents);
+    Status ensure_arena(std::size_t bytes);
+    Status encode_activation_maps(Plan& plan);
+    enum class Boundary { half, float32, host };
+    Status execute(const std::vector<TensorView>& inputs, const std::vector<TensorView>& outputs, Boundary boundary);
+    Status launch_step(const Step& step, Plan& plan, std::size_t index);
+
+    Program program_;
+    cudaStream_t stream_{nullptr};
+    bool owns_stream_{false};
+    float* weights_{nullptr};
+    unsigned int* status_{nullptr};
+    std::vector<Step> steps_;
+    std::vector<IntegerConv> convs_;
+    std::map<std::vector<std::int32_t>, std::unique_ptr<Plan>> plans_;
+    void* arena_{nullptr};
+    std::size_t arena_bytes_{0};
+    std::uint64_t arena_generation_{0};
+    int launches_{0};
+    bool profiling_{false};
+    std::vector<cudaEvent_t> events_;
+    std::vector<StepTiming> timings_;
+};
+
+}  // namespace nvcr_sm100

@@ -1,0 +1,170 @@
+// C entry points over the reference's own CPU executor, for tests and the CPU
+// baseline only. TEST INFRASTRUCTURE: compiled by oracle/Makefile together with
+// the reference sources it names (src/deterministic/program.cpp,
+// normative_stage.cpp, src/common/{json,sha256,error}.cpp) into
+// oracle/_ref/libnvcr_ref.so. Nothing in the product links or loads it.
+//
+// Programs reach the reference through its own loader (load_program,
+// src/deterministic/program.cpp:537-626) from the .detprog.json/.detw files the
+// tests write, so the reference also checks the files' format and digests.
+#include "deterministic/det_math.hpp"
+#include "deterministic/normative_stage.hpp"
+#include "deterministic/program.hpp"
+
+#include <chrono>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+namespace det = nvcr::deterministic;
+
+namespace {
+
+void write_error(char* buffer, std::size_t size, std::string_view message) {
+    if (buffer == nullptr || size == 0) return;
+    std::snprintf(buffer, size, "%.*s", static_cast<int>(message.size()), message.data());
+}
+
+}  // namespace
+
+extern "C" {
+
+// 0 when the reference accepts the program file; otherwise the reference's
+// ErrorCode value plus one, with its message.
+int ref_load_check(const char* program_json, char* error, std::size_t error_size) {
+    auto program = det::load_program(program_json);
+    if (program) return 0;
+    write_error(error, error_size, program.error().message());
+    return static_cast<int>(program.error().code()) + 1;
+}
+
+// Runs run_cpu on FP32 NCHW inputs (program.inputs order). When weights is not
+// null it replaces the program's FP16-widened weights with the given FP32
+// values (the in-memory Program form the reference's tests use). Outputs are
+// malloc'd; extents receive (c, h, w) per output. Returns 0 or ErrorCode + 1.
+int ref_run(const char* program_json, const float* weights, std::int64_t weight_count,
+            int input_count, const std::int32_t* input_extents, const float* const* inputs,
+            int output_capacity, std::int32_t* output_extents, float** outputs, char* error,
+            std::size_t error_size) {
+    auto loaded = det::load_program(program_json);
+    if (!loaded) {
+        write_error(error, error_size, loaded.error().message());
+        return static_cast<int>(loaded.error().code()) + 1;
+    }
+    auto& program = loaded.value();
+    if (weights != nullptr) {
+        if (static_cast<std::size_t>(weight_count) != program.weights.size()) {
+            write_error(error, error_size, "weight override has the wrong count");
+            return 1;
+        }
+        program.weights.assign(weights, weights + weight_count);
+    }
+    std::vector<det::Tensor> tensors;
+    for (int index = 0; index < input_count; ++index) {
+        det::Tensor tensor{input_extents[3 * index], input_extents[3 * index + 1],
+                           input_extents[3 * index + 2], {}};
+        tensor.values.assign(inputs[index], inputs[index] + tensor.size());
+        tensors.push_back(std::move(tensor));
+    }
+    auto results = det::run_cpu(program, tensors);
+    if (!results) {
+        write_error(error, error_size, results.error().message());
+        return static_cast<int>(results.error().code()) + 1;
+    }
+    if (static_cast<int>(results.value().size()) > output_capacity) {
+        write_error(error, error_size, "too many outputs");
+        return 1;
+    }
+    for (std::size_t slot = 0; slot < results.value().size(); ++slot) {
+        const auto& result = results.value()[slot];
+        output_extents[3 * slot] = result.channels;
+        output_extents[3 * slot + 1] = result.height;
+        output_extents[3 * slot + 2] = result.width;
+        outputs[slot] = static_cast<float*>(std::malloc(result.values.size() * sizeof(float) + 4));
+        std::memcpy(outputs[slot], result.values.data(), result.values.size() * sizeof(float));
+    }
+    return 0;
+}
+
+// Times `repeats` calls of run_cpu on the given inputs (weights as loaded) and
+// returns the mean seconds per call, or a negative value on failure.
+double ref_time_run(const char* program_json, int input_count, const std::int32_t* input_extents,
+                    const float* const* inputs, int repeats) {
+    auto loaded = det::load_program(program_json);
+    if (!loaded) return -1.0;
+    std::vector<det::Tensor> tensors;
+    for (int index = 0; index < input_count; ++index) {
+        det::Tensor tensor{input_extents[3 * index], input_extents[3 * index + 1],
+                           input_extents[3 * index + 2], {}};
+        tensor.values.assign(inputs[index], inputs[index] + tensor.size());
+        tensors.push_back(std::move(tensor));
+    }
+    const auto start = std::chrono::steady_clock::now();
+    for (int repeat = 0; repeat < repeats; ++repeat) {
+        auto results = det::run_cpu(loaded.value(), tensors);
+        if (!results) return -2.0;
+    }
+    const std::chrono::duration<double> elapsed = std::chrono::steady_clock::now() - start;
+    return elapsed.count() / repeats;
+}
+
+// Output extents of a program for the given input extents (infer_output_extents,
+// normative_stage.cpp:42-65). Returns 0 or ErrorCode + 1.
+int ref_infer_extents(const char* program_json, int input_count, const std::int32_t* input_extents,
+                      int output_capacity, std::int32_t* output_extents, char* error,
+                      std::size_t error_size) {
+    auto loaded = det::load_program(program_json);
+    if (!loaded) {
+        write_error(error, error_size, loaded.error().message());
+        return static_cast<int>(loaded.error().code()) + 1;
+    }
+    std::vector<det::Extent> extents;
+    for (int index = 0; index < input_count; ++index) {
+        extents.push_back(det::Extent{input_extents[3 * index], input_extents[3 * index + 1],
+                                      input_extents[3 * index + 2]});
+    }
+    auto inferred = det::infer_output_extents(loaded.value(), extents);
+    if (!inferred) {
+        write_error(error, error_size, inferred.error().message());
+        return static_cast<int>(inferred.error().code()) + 1;
+    }
+    if (static_cast<int>(inferred.value().size()) > output_capacity) return 1;
+    for (std::size_t slot = 0; slot < inferred.value().size(); ++slot) {
+        output_extents[3 * slot] = inferred.value()[slot].channels;
+        output_extents[3 * slot + 1] = inferred.value()[slot].height;
+        output_extents[3 * slot + 2] = inferred.value()[slot].width;
+    }
+    return 0;
+}
+
+// quantize_weights (program.cpp:509-535) on one [out][in] matrix.
+void ref_quantize_weights(const float* weights, std::int32_t out_channels, std::int32_t in_channels,
+                          std::int32_t weight_bits, std::int16_t* values, float* scales) {
+    det::Program program;
+    program.weights.assign(weights, weights + static_cast<std::size_t>(out_channels) * in_channels);
+    det::Node node;
+    node.in_channels = in_channels;
+    node.out_channels = out_channels;
+    node.weight_bits = weight_bits;
+    const auto quantized = det::quantize_weights(program, node);
+    std::memcpy(values, quantized.values.data(), quantized.values.size() * sizeof(std::int16_t));
+    std::memcpy(scales, quantized.scales.data(), quantized.scales.size() * sizeof(float));
+}
+
+float ref_det_exp(float x) { return det::det_exp(x); }
+float ref_det_sigmoid(float x) { return det::det_sigmoid(x); }
+float ref_det_ldexp(float x, int e) { return det::det_ldexp(x, e); }
+int ref_det_int_exponent(float maximum, int bits) { return det::det_int_exponent(maximum, bits); }
+int ref_det_int_quantize(float x, int e, int bits) { return det::det_int_quantize(x, e, bits); }
+float ref_det_int_output(long long acc, float scale, int e, float bias) {
+    return det::det_int_output(acc, scale, e, bias);
+}
+float ref_half_to_float(std::uint16_t h) { return det::det_half_bits_to_float(h); }
+std::uint16_t ref_float_to_half(float x) { return det::det_float_to_half_bits(x); }
+
+void ref_free(void* pointer) { std::free(pointer); }
+
+}  // extern "C"

@@ -1,0 +1,115 @@
+"""CPU-side checks of the product library and its host logic (no GPU needed):
+the C ABI loads and exports every function include/nvcr_sm100.h declares, the
+profile negotiation answers as the reference's, and program files are accepted
+or refused exactly as the reference's loader does."""
+from __future__ import annotations
+
+import json
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from nvcr_b200 import executor as ex
+from nvcr_b200.program import OpKind, Program, SeededStream
+from tests.programs import data_movement_program, op_program
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "nvcr_sm100.h"
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"\b(nvcr_sm100_[a-z_0-9]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_function(built_library):
+    lib = ex.library()
+    names = declared_functions()
+    assert len(names) >= 20
+    for name in names:
+        assert hasattr(lib, name), f"{name} is declared but not exported"
+    assert set(names) == set(ex.EXPORTS)
+    assert lib.nvcr_sm100_abi_version() == 1
+
+
+def test_is_normative_matches_reference_rule(built_library):
+    assert ex.is_normative("") is False
+    assert ex.is_normative("nvcr.intconv.v1") is True
+    with pytest.raises(ex.ExecutorError) as error:
+        ex.is_normative("nvcr.fx.v1")
+    assert error.value.code == ex.ErrorCode.incompatible_precision
+
+
+def test_supports_profile_refuses_other_profiles(built_library):
+    assert ex.supports_numerics_profile("nvcr.fx.v1") is False
+    assert ex.supports_numerics_profile("native") is False
+
+
+def _write_variants(tmp_path: Path):
+    """A valid program, then malformed variants of its JSON and weights."""
+    stream = SeededStream(7)
+    program = op_program(stream).with_widths(8, 16)
+    good = program.write(tmp_path / "good", "ops")
+    base = json.loads(good.read_text())
+    variants = {"good": good}
+
+    def variant(name, mutate, weights=None):
+        directory = tmp_path / name
+        directory.mkdir()
+        document = json.loads(json.dumps(base))
+        mutate(document)
+        blob = (tmp_path / "good" / "ops.detw").read_bytes() if weights is None else weights
+        (directory / "ops.detw").write_bytes(blob)
+        path = directory / "ops.detprog.json"
+        path.write_text(json.dumps(document))
+        variants[name] = path
+
+    variant("wrong_format", lambda d: d.update(format="other"))
+    variant("wrong_version", lambda d: d.update(version=2))
+    variant("fx_profile", lambda d: d.update(numerics="nvcr.fx.v1"))
+    variant("digest", lambda d: d["weights"].update(sha256="0" * 64))
+    variant("weights_path", lambda d: d["weights"].update(file="../ops.detw"))
+    variant("unknown_op", lambda d: d["nodes"][1].update(op="gelu"))
+    variant("undefined_tensor", lambda d: d["nodes"][1].update(input="nope"))
+    variant("duplicate_output", lambda d: d["nodes"][2].update(output=d["nodes"][1]["output"]))
+    variant("bad_widths", lambda d: d["nodes"][0].update(integer={"weight_bits": 4, "activation_bits": 8}))
+    variant("widths_on_sigmoid", lambda d: d["nodes"][2].update(integer={"weight_bits": 8, "activation_bits": 8}))
+    variant("inexact_scalar", lambda d: d["nodes"][1].update(value=0.1))
+    variant("weights_overflow", lambda d: d["nodes"][0].update(weight_offset=10 ** 9))
+    variant("bad_block", lambda d: d["nodes"][8].update(block=0))
+    variant("depthwise_mismatch", lambda d: d["nodes"][4].update(out_channels=5))
+    variant("float_channels", lambda d: d["nodes"][0].update(in_channels=70.0))
+    variant("missing_output", lambda d: d["outputs"].append({"name": "ghost"}))
+    variant("short_weights", lambda d: d["weights"].update(count=d["weights"]["count"] + 1))
+    return variants
+
+
+def test_loader_accepts_and_refuses_like_the_reference(built_library, reference, tmp_path):
+    """Without a GPU, creation reaches the device check only after the program
+    loaded; a refused program fails earlier with the loader's code."""
+    loader_codes = {ex.ErrorCode.invalid_argument, ex.ErrorCode.io_error, ex.ErrorCode.digest_mismatch}
+    for name, path in _write_variants(tmp_path).items():
+        ref_code, ref_message = reference.load_check(path)
+        try:
+            executor = ex.CudaExecutor.create(path)
+            ours = None
+            executor.close()
+        except ex.ExecutorError as error:
+            ours = error.code if error.code in loader_codes else None
+        expected = None if ref_code == 0 else ex.ErrorCode(ref_code - 1)
+        assert ours == expected, f"{name}: reference {expected} ({ref_message}), ours {ours}"
+
+
+def test_load_normative_checks_presence_and_digest(built_library, tmp_path):
+    stream = SeededStream(7)
+    path = data_movement_program().write(tmp_path, "stage")
+    with pytest.raises(ex.ExecutorError) as error:
+        ex.CudaExecutor.load_normative(tmp_path, "absent", "0" * 64)
+    assert error.value.code == ex.ErrorCode.missing_artifact
+    with pytest.raises(ex.ExecutorError) as error:
+        ex.CudaExecutor.load_normative(tmp_path, "stage", "0" * 64)
+    assert error.value.code == ex.ErrorCode.digest_mismatch
+    with pytest.raises(ex.ExecutorError) as error:
+        ex.CudaExecutor.load_normative(tmp_path, "stage", "")
+    assert error.value.code == ex.ErrorCode.invalid_argument

@@ -1,0 +1,263 @@
+"""CUDA path == CPU oracle, bit for bit (NaN equals NaN), through the C ABI.
+
+The programs are the reference's own conformance programs
+(tests/deterministic_executor_tests.cpp:95-410) rebuilt here, the BASELINE
+configs, and integer-conv cases aimed at the sm_100a kernels' edges: every
+width pair, K and positions off the 128 tiles, multiple N tiles, chunk-add,
+WSiLU and residual fusion, strided and padded windows, non-finite, tiny and
+huge activations.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from nvcr_b200.executor import CudaExecutor
+from nvcr_b200.program import OpKind, Program, SeededStream
+from nvcr_b200.workloads import config1, layer_input
+from oracle.oracle import count_differing, same_bits
+from tests.programs import data_movement_program, op_program, sigmoid_program, sigmoid_sweep_values
+
+pytestmark = pytest.mark.gpu
+
+WIDTHS = [(16, 16), (8, 16), (16, 8), (8, 8)]
+
+
+def run_gpu(program: Program, inputs, fp16_weights=False):
+    with CudaExecutor.from_program(program, fp16_weights=fp16_weights) as executor:
+        outputs = executor.run(inputs)
+        executor.synchronize()
+    return outputs
+
+
+def assert_parity(program, inputs, oracle, label, fp16_weights=False):
+    weights = program.fp16_weights() if fp16_weights else program.weights
+    expected = oracle.run(program, inputs, weights=weights)
+    got = run_gpu(program, inputs, fp16_weights=fp16_weights)
+    assert len(got) == len(expected)
+    for index, (g, e) in enumerate(zip(got, expected)):
+        assert g.shape == e.shape, f"{label} output {index}: shape {g.shape} != {e.shape}"
+        bad = count_differing(g, e)
+        assert bad == 0, f"{label} output {index}: {bad} of {e.size} elements differ"
+
+
+@pytest.mark.parametrize("height,width", [(11, 18), (2, 64), (33, 47)])
+@pytest.mark.parametrize("bits", WIDTHS, ids=lambda b: f"w{b[0]}a{b[1]}")
+def test_op_program(cuda, oracle, height, width, bits):
+    stream = SeededStream(11)
+    program = op_program(stream).with_widths(*bits)
+    x = stream.tensor(70, height, width, 3.0)
+    assert_parity(program, [x], oracle, f"ops {height}x{width} w{bits[0]}a{bits[1]}")
+
+
+def test_data_movement(cuda, oracle):
+    stream = SeededStream(41)
+    inputs = [stream.tensor(5, 12, 20, 1.5), stream.tensor(20, 1, 1, 2.0), stream.tensor(1, 5, 7, 1.0)]
+    assert_parity(data_movement_program(), inputs, oracle, "data movement")
+
+
+def test_sigmoid_sweep(cuda, oracle):
+    values = sigmoid_sweep_values()
+    x = values.reshape(1, 1, -1)
+    assert_parity(sigmoid_program(), [x], oracle, "sigmoid sweep")
+
+
+def test_half_boundary_exhaustive(cuda, oracle):
+    """Every binary16 pattern widens exactly and rounds back unchanged (mul by 1)."""
+    import torch
+
+    p = Program(name="identity")
+    x = p.add_input("x", 1)
+    y = p.unary(OpKind.mul_scalar, x, "y", scalar=1.0)
+    p.finish([y])
+    bits = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    with CudaExecutor.from_program(p) as executor:
+        xh = torch.from_numpy(bits.view(np.float16).copy()).cuda().reshape(1, 1, -1)
+        yh = torch.empty_like(xh)
+        executor.run_half({"x": xh}, {"y": yh})
+        executor.synchronize()
+        got = yh.cpu().numpy().reshape(-1).view(np.uint16)
+    nan = (bits & 0x7C00) == 0x7C00
+    nan &= (bits & 0x03FF) != 0
+    assert np.array_equal(got[~nan], bits[~nan])
+    assert np.all(((got[nan] & 0x7C00) == 0x7C00) & ((got[nan] & 0x3FF) != 0))
+
+
+def test_float_to_half_rounding(cuda, oracle):
+    """FP32 -> FP16 at the stage boundary rounds to nearest even (subnormals,
+    ties, overflow to inf), like the reference's det_float_to_half_bits: every
+    binary16 input times 2^-11, 3 and 1.5 gives FP32 values that need rounding."""
+    import torch
+
+    p = Program(name="round")
+    x = p.add_input("x", 1)
+    outs = [p.unary(OpKind.mul_scalar, x, f"y{i}", scalar=s) for i, s in enumerate((2.0 ** -11, 3.0, 1.5))]
+    p.finish(outs)
+    halves = np.arange(65536, dtype=np.uint32).astype(np.uint16).view(np.float16)
+    with CudaExecutor.from_program(p) as executor:
+        xh = torch.from_numpy(halves.copy()).cuda().reshape(1, 1, -1)
+        ys = {f"y{i}": torch.empty_like(xh) for i in range(3)}
+        executor.run_half({"x": xh}, ys)
+        executor.synchronize()
+        got = [ys[f"y{i}"].cpu().numpy().reshape(-1).view(np.uint16) for i in range(3)]
+    widened = halves.astype(np.float32)
+    for g, s in zip(got, (2.0 ** -11, 3.0, 1.5)):
+        products = widened * np.float32(s)
+        expected = np.array([oracle.lib.or_float_to_half(float(v)) for v in products], np.uint16)
+        nan = np.isnan(products)
+        assert np.array_equal(g[~nan], expected[~nan]), f"scale {s}"
+        assert np.all((g[nan] & 0x7C00) == 0x7C00)
+
+
+def test_config1_half(cuda, oracle):
+    """BASELINE config 1 through run_half (FP16 stage boundary)."""
+    import torch
+
+    layer = config1()
+    x = layer_input(layer, seed=1)
+    expected = oracle.run(layer.program, [x])[0].astype(np.float16)
+    with CudaExecutor.from_program(layer.program) as executor:
+        xh = torch.from_numpy(x.astype(np.float16)).cuda()
+        yh = torch.empty(expected.shape, dtype=torch.float16, device="cuda")
+        executor.run_half({"x": xh}, {"y": yh})
+        executor.synchronize()
+        got = yh.cpu().numpy()
+    assert count_differing(got.astype(np.float32), expected.astype(np.float32)) == 0
+
+
+def _random_conv_program(stream: SeededStream, cin, cout, kernel, stride, pads, bits, *, wsilu=False,
+                         chunk_add=False, residual=False, name="conv") -> Program:
+    p = Program(name=name)
+    x = p.add_input("x", cin)
+    r = None
+    if residual:
+        # An earlier tensor of the output's shape (produced before the conv, so
+        # the add folds into the conv's epilogue): a 1x1 FP32 depthwise of x, sliced.
+        out_c = cout // 2 if chunk_add else cout
+        if out_c > cin:
+            raise ValueError("residual needs out channels <= in channels")
+        r = p.conv(x, cin, stream.uniform(-1, 1, cin), stream.uniform(-1, 1, cin), "r_dw", depthwise=True)
+        if out_c < cin:
+            r = p.unary(OpKind.slice_channels, r, "r", begin=0, end=out_c)
+    taps = kernel[0] * kernel[1]
+    w = stream.uniform(-0.5, 0.5, cout * cin * taps)
+    b = stream.uniform(-0.2, 0.2, cout)
+    y = p.dense_conv(x, cout, w, b, "c", kernel=kernel, stride=stride, pads=pads, bits=bits)
+    if wsilu:
+        s = p.unary(OpKind.mul_scalar, y, "s", scalar=4.0)
+        g = p.unary(OpKind.sigmoid, s, "g")
+        y = p.binary(OpKind.mul, y, g, "w")
+    if chunk_add:
+        a = p.unary(OpKind.slice_channels, y, "a", begin=0, end=cout // 2)
+        b2 = p.unary(OpKind.slice_channels, y, "b", begin=cout // 2, end=cout)
+        y = p.binary(OpKind.add, a, b2, "ca")
+    if residual:
+        y = p.binary(OpKind.add, y, r, "res")
+    return p.finish([y])
+
+
+CONV_CASES = [
+    # cin, cout, kernel, stride, pads, height, width
+    (64, 64, (3, 3), (1, 1), (1, 1, 1, 1), 36, 44),      # config-1 shape
+    (3, 64, (3, 3), (2, 2), (1, 1, 1, 1), 40, 70),       # config-2 L1 shape (K = 27)
+    (128, 256, (1, 1), (1, 1), (0, 0, 0, 0), 17, 30),    # pointwise, one full N tile
+    (70, 133, (1, 1), (1, 1), (0, 0, 0, 0), 11, 18),     # ragged N, K
+    (96, 300, (1, 1), (1, 1), (0, 0, 0, 0), 9, 15),      # two N tiles
+    (32, 520, (3, 3), (1, 1), (1, 1, 1, 1), 8, 9),       # three N tiles
+    (16, 24, (2, 2), (2, 2), (0, 0, 0, 0), 10, 14),      # 2x2 stride 2
+    (20, 40, (3, 5), (1, 2), (2, 0, 1, 3), 13, 21),      # asymmetric window and pads
+    (200, 48, (3, 3), (1, 1), (1, 1, 1, 1), 5, 7),       # K = 1800, ragged
+]
+
+
+@pytest.mark.parametrize("case", CONV_CASES, ids=lambda c: f"{c[0]}to{c[1]}k{c[2][0]}x{c[2][1]}s{c[3][0]}")
+@pytest.mark.parametrize("bits", WIDTHS, ids=lambda b: f"w{b[0]}a{b[1]}")
+def test_integer_conv(cuda, oracle, case, bits):
+    cin, cout, kernel, stride, pads, h, w = case
+    stream = SeededStream(1000 + cin + cout)
+    program = _random_conv_program(stream, cin, cout, kernel, stride, pads, bits)
+    x = stream.tensor(cin, h, w, 2.0)
+    assert_parity(program, [x], oracle, f"conv {case} w{bits[0]}a{bits[1]}")
+
+
+@pytest.mark.parametrize("bits", WIDTHS, ids=lambda b: f"w{b[0]}a{b[1]}")
+@pytest.mark.parametrize("fusion", ["wsilu", "chunk", "wsilu_chunk_residual", "residual"])
+def test_epilogue_fusions(cuda, oracle, bits, fusion):
+    stream = SeededStream(77)
+    cin, cout = (96, 192) if "chunk" in fusion else (96, 64)
+    program = _random_conv_program(stream, cin, cout, (1, 1), (1, 1), (0, 0, 0, 0), bits,
+                                   wsilu="wsilu" in fusion, chunk_add="chunk" in fusion,
+                                   residual="residual" in fusion)
+    x = stream.tensor(cin, 13, 29, 3.0)
+    assert_parity(program, [x], oracle, f"fusion {fusion}")
+
+
+def test_chunk_add_many_tiles(cuda, oracle):
+    stream = SeededStream(78)
+    program = _random_conv_program(stream, 64, 1040, (1, 1), (1, 1), (0, 0, 0, 0), (8, 8), chunk_add=True)
+    x = stream.tensor(64, 7, 23, 2.0)
+    assert_parity(program, [x], oracle, "chunk-add over several tiles")
+
+
+@pytest.mark.parametrize("bits", WIDTHS, ids=lambda b: f"w{b[0]}a{b[1]}")
+def test_activation_edge_values(cuda, oracle, bits):
+    """All-zero positions (e = 0), NaN/inf positions (NaN out), subnormal and
+    tiny inputs (exponents below -126: the wide ldexp path), huge inputs, and
+    values on rounding ties."""
+    stream = SeededStream(5)
+    cin, h, w = 40, 6, 50
+    x = stream.tensor(cin, h, w, 1.0)
+    x[:, 0, 0] = 0.0                                   # all-zero position
+    x[3, 0, 1] = np.nan                                # NaN position
+    x[7, 0, 2] = np.inf
+    x[8, 0, 3] = -np.inf
+    x[:, 1, :] *= np.float32(2.0 ** -130)              # subnormal-range maxima
+    x[:, 2, :10] = np.float32(2.0 ** -149) * np.arange(1, 41, dtype=np.float32)[:, None]
+    x[:, 3, :] *= np.float32(60000.0)                   # large magnitudes
+    x[:, 4, :] = (np.round(x[:, 4, :] * 64) + 0.5) / 64  # ties after scaling
+    x[0, 5, :] = np.float32(3.4e38)
+    program = _random_conv_program(stream, cin, 72, (3, 3), (1, 1), (1, 1, 1, 1), bits)
+    assert_parity(program, [x], oracle, f"edge values w{bits[0]}a{bits[1]}")
+    program = _random_conv_program(stream, cin, 72, (1, 1), (1, 1), (0, 0, 0, 0), bits)
+    assert_parity(program, [x], oracle, f"edge values pointwise w{bits[0]}a{bits[1]}")
+
+
+def test_weight_edge_values(cuda, oracle):
+    """A zero weight row (scale 1), FP16-subnormal weights, +-65504 weights."""
+    stream = SeededStream(9)
+    p = Program(name="weights")
+    x = p.add_input("x", 48)
+    w = stream.uniform(-1, 1, 32 * 48).reshape(32, 48)
+    w[0] = 0.0
+    w[1] = np.float32(2.0 ** -24) * np.arange(48)
+    w[2, :5] = [65504.0, -65504.0, 1.0, -1.0, 0.5]
+    b = stream.uniform(-1, 1, 32)
+    y = p.conv(x, 32, w, b, "y", bits=(16, 16))
+    p.finish([y])
+    xs = stream.tensor(48, 9, 9, 4.0)
+    for bits in WIDTHS:
+        assert_parity(p.with_widths(*bits), [xs], oracle, f"weight edges w{bits[0]}a{bits[1]}", fp16_weights=True)
+
+
+def test_bit_stable_repeats(cuda, oracle):
+    """Sixty runs of one executor give identical bits (no scheduling-dependent results)."""
+    stream = SeededStream(3)
+    program = op_program(stream).with_widths(16, 16)
+    x = stream.tensor(70, 33, 47, 3.0)
+    with CudaExecutor.from_program(program) as executor:
+        first = executor.run([x])
+        for _ in range(59):
+            again = executor.run([x])
+            assert all(same_bits(a, b) for a, b in zip(first, again))
+
+
+def test_one_executor_many_extents(cuda, oracle):
+    """Plans are cached per input extent; alternating extents reuse them."""
+    stream = SeededStream(4)
+    program = op_program(stream).with_widths(8, 16)
+    xs = [stream.tensor(70, h, w, 2.0) for h, w in [(11, 18), (33, 47), (11, 18), (5, 200)]]
+    with CudaExecutor.from_program(program) as executor:
+        for x in xs:
+            got = executor.run([x])
+            expected = oracle.run(program, [x])
+            assert all(count_differing(g, e) == 0 for g, e in zip(got, expected))
