@@ -1,0 +1,402 @@
+#!/usr/bin/env python3
+"""Benchmark of the nvcr.intconv.v1 exact-convolution path on B200.
+
+Workload: the 1920x1088 layer sweep, w8a8 integer convs
+lowered as the reference's exporter lowers them (im2col + pointwise conv), FP16
+at the stage boundary, every value an int8 in [-127, 127] from a seeded
+std::mt19937 stream:
+  L1 3x3 s2 3->64 at 1088x1920, L2 3x3 64->64 at 544x960, L3 1x1 128->256 at
+  272x480, L4 3x3 256->256 at 136x240, L5 3x3 256->1024 at 68x120 + depth_to_space 2.
+A step runs the five layers once (125.9 G algorithmic int8 ops, one MAC = 2 ops;
+limb expansion and padding are not counted). The step touches about 1 GB, far
+more than the 126 MB L2, so no L2 flush is inserted.
+
+  value  whole-job int8 TOPS with inputs resident in HBM (device FP16 tensors);
+  e2e    the same through the C ABI with pinned host FP16 buffers, the
+         host->device input copy and device->host output copy inside the timing;
+  roofline  the integer GEMM kernel (CUDA events on its stream, timed region).
+
+N > 1 (torchrun): every rank runs the same sweep on its own GPU (independent
+replicas, no collective on the data path); value = all ranks' ops / max time.
+`--impl reference` times the reference's own CPU executor (run_cpu, compiled
+from its sources into oracle/_ref) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+MEASURED_PEAKS = ROOT / "MEASURED_PEAKS.json"
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+CPU_BASELINE_FRACTION = 2   # cpu_baseline leg: the first half of each layer's output rows
+REFERENCE_ARM_FRACTION = 32  # --impl reference: 1/32 per step, so K + W steps end in minutes
+
+
+def parse_args():
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    parser.add_argument("--no-cpu-baseline", action="store_true", help="skip the reference CPU timing")
+    parser.add_argument("--layers", type=str, default="", help="comma-separated layer indices (default: all)")
+    return parser.parse_args()
+
+
+def peaks():
+    if MEASURED_PEAKS.exists():
+        data = json.loads(MEASURED_PEAKS.read_text())
+        return data["hbm_gbs"], data["bf16_tflops"], "measured"
+    return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str | None) -> None:
+        self.uuid = uuid
+        self.process = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.process = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.process = None
+            return self
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+        return self
+
+    def _read(self):
+        for line in self.process.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.process is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.process.terminate()
+        try:
+            self.process.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.process.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+        sm, sm_max, power, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 10:
+                continue
+            if self.uuid and parts[1] != self.uuid:
+                continue
+            try:
+                sm.append(float(parts[2]))
+                sm_max.append(float(parts[3]))
+                power.append(float(parts[4]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[6:10]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(sm_max), "power_w_max": max(power),
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def distributed():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def select_layers(spec: str):
+    from nvcr_b200.workloads import config2
+
+    layers = config2()
+    if spec:
+        layers = [layers[int(i)] for i in spec.split(",")]
+    return layers
+
+
+def reference_sample(layers, directory: Path, fraction: int, repeats: int = 1):
+    """Times the reference's run_cpu on the first 1/`fraction` of each layer's
+    output rows (the input rows that feed them); returns (TOPS, seconds, ops, sample text)."""
+    import numpy as np
+
+    from nvcr_b200.workloads import layer_input
+    from oracle.oracle import Reference
+
+    reference = Reference()
+    total_ops = 0.0
+    total_seconds = 0.0
+    parts = []
+    for index, layer in enumerate(layers):
+        c, h, w = layer.input_shape
+        node = [n for n in layer.program.nodes if n.kind.name == "im2col"]
+        stride = node[0].stride[0] if node else 1
+        kernel = node[0].kernel[0] if node else 1
+        out_h = (h + (2 if node else 0) - kernel) // stride + 1
+        rows_out = max(1, out_h // fraction)
+        rows_in = min(h, rows_out * stride + (kernel - 1))
+        x = layer_input(layer, seed=200 + index, height=rows_in)
+        path = layer.program.write(directory, layer.name)
+        seconds = reference.time_run(path, [x], repeats=repeats)
+        sample_out_h = (rows_in + (2 if node else 0) - kernel) // stride + 1
+        ops = layer.ops * sample_out_h / out_h
+        total_ops += ops
+        total_seconds += seconds
+        parts.append(f"{layer.name}: {rows_in}/{h} input rows")
+    tops = total_ops / total_seconds / 1e12
+    return tops, total_seconds, total_ops, "; ".join(parts)
+
+
+def run_reference_arm(args):
+    world, rank, _ = distributed()
+    if rank != 0:
+        return 0
+    layers = select_layers(args.layers)
+    threads = min(os.cpu_count() or 1, 16)
+    with tempfile.TemporaryDirectory() as directory:
+        for _ in range(args.warmup):
+            reference_sample(layers, Path(directory), REFERENCE_ARM_FRACTION)
+        times = []
+        ops = 0.0
+        sample = ""
+        for _ in range(args.steps):
+            tops, seconds, ops, sample = reference_sample(layers, Path(directory), REFERENCE_ARM_FRACTION)
+            times.append(seconds)
+    total = sum(times)
+    value = ops * args.steps / total / 1e12
+    line = {
+        "impl": "reference", "metric": "int8 conv TOPS (config 2 layer sweep, bit-exact intconv.v1)",
+        "value": value, "unit": "TOPS", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * total / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded mt19937 int8 values)",
+        "config": {"workload": "config2: 1920x1088 layer sweep L1-L5, w8a8, FP16 stage boundary",
+                   "parallelism": "reference CPU run_cpu, rank 0 only"},
+        "cpu_baseline": {"value": value, "unit": "TOPS", "cores": threads, "kind": "reference",
+                         "sample": f"reference run_cpu (oracle/_ref) on {sample}"},
+        "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference_arm(args)
+
+    import numpy as np
+    import torch
+
+    world, rank, local = distributed()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+
+    from nvcr_b200.executor import CudaExecutor
+    from nvcr_b200.workloads import layer_input
+
+    layers = select_layers(args.layers)
+    stream = torch.cuda.Stream(device=device)
+    executors, inputs, outputs, pinned_in, pinned_out = [], [], [], [], []
+    for index, layer in enumerate(layers):
+        executor = CudaExecutor.from_program(layer.program, stream=stream.cuda_stream)
+        x = layer_input(layer, seed=200 + index)
+        (c, h, w), = executor.infer_output_extents([x.shape])
+        xh = torch.from_numpy(x.astype(np.float16)).to(device)
+        yh = torch.empty((c, h, w), dtype=torch.float16, device=device)
+        executors.append(executor)
+        inputs.append(xh)
+        outputs.append(yh)
+        pinned_in.append(torch.from_numpy(x.astype(np.float16)).pin_memory())
+        pinned_out.append(torch.empty((c, h, w), dtype=torch.float16).pin_memory())
+    ops_per_step = sum(layer.ops for layer in layers)
+
+    def step():
+        for executor, xh, yh in zip(executors, inputs, outputs):
+            executor.run_half({"x": xh}, {"y": yh})
+
+    def step_e2e():
+        with torch.cuda.stream(stream):
+            for executor, xh, yh, hi, ho in zip(executors, inputs, outputs, pinned_in, pinned_out):
+                xh.copy_(hi, non_blocking=True)
+                executor.run_half({"x": xh}, {"y": yh})
+                ho.copy_(yh, non_blocking=True)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+
+    def max_over_ranks(value: float) -> float:
+        if world == 1:
+            return value
+        import torch.distributed as dist
+
+        t = torch.tensor([value], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(function, steps, profile=False):
+        for executor in executors:
+            executor.set_profiling(profile)
+        barrier()
+        torch.cuda.synchronize(device)
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(steps):
+            function()
+        end.record(stream)
+        torch.cuda.synchronize(device)
+        barrier()
+        for executor in executors:
+            executor.synchronize()
+        return start.elapsed_time(end)
+
+    # Warm-up (plans, arenas, TMA maps), then the timed region.
+    for _ in range(max(args.warmup, 3)):
+        step()
+    for executor in executors:
+        executor.synchronize()
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+    except Exception:
+        pass
+    sampler = ClockSampler(uuid).start()
+    time.sleep(0.3)
+    elapsed_ms = timed(step, args.steps, profile=True)
+    clocks = sampler.stop()
+    launches = sum(e.launches for e in executors) * args.steps
+    per_layer_segments = [e.profile() for e in executors]
+    elapsed_ms = max_over_ranks(elapsed_ms)
+    value = world * ops_per_step * args.steps / (elapsed_ms / 1000.0) / 1e12
+
+    # End to end through the C ABI with host buffers.
+    for _ in range(2):
+        step_e2e()
+    e2e_ms = max_over_ranks(timed(step_e2e, args.steps))
+    e2e_value = world * ops_per_step * args.steps / (e2e_ms / 1000.0) / 1e12
+    h2d = sum(t.numel() * 2 for t in pinned_in)
+    d2h = sum(t.numel() * 2 for t in pinned_out)
+
+    # Roofline of the integer GEMM kernel and per-layer bounds.
+    hbm, bf16, source = peaks()
+    int8_peak = 2.0 * bf16  # B200's dense int8 rate is twice its dense bf16 rate
+    ridge = int8_peak * 1e12 / (hbm * 1e9)  # ops per byte
+    kernel_ms: dict[str, float] = {}
+    for segments in per_layer_segments:
+        for seg in segments:
+            kernel_ms[seg["kernel"]] = kernel_ms.get(seg["kernel"], 0.0) + seg["ms"]
+    total_ms = sum(kernel_ms.values())
+    shares = {k: round(v / total_ms, 3) for k, v in sorted(kernel_ms.items(), key=lambda kv: -kv[1])} \
+        if total_ms else {}
+    layer_rows = []
+    tensor_ops = tensor_ms = all_ops = all_ms = 0.0
+    for layer, segments in zip(layers, per_layer_segments):
+        gemms = [seg for seg in segments if seg["kernel"] == "integer_gemm"]
+        quants = [seg for seg in segments if seg["kernel"] == "quantize_activations"]
+        if not gemms:
+            continue
+        ms = sum(seg["ms"] for seg in gemms) / len(gemms)
+        q_ms = sum(seg["ms"] for seg in quants) / max(1, len(quants))
+        ops, bytes_ = gemms[0]["ops"], gemms[0]["bytes"]
+        bound = "tensor" if ops / bytes_ > ridge else "hbm"
+        tops = ops / (ms / 1000.0) / 1e12
+        gbs = bytes_ / (ms / 1000.0) / 1e9
+        layer_rows.append({"layer": layer.name, "gemm_ms": round(ms, 4), "quantize_ms": round(q_ms, 4),
+                           "gemm_tops": round(tops, 1), "gemm_gbs": round(gbs, 1), "bound": bound,
+                           "frac": round(tops / int8_peak if bound == "tensor" else gbs / hbm, 3)})
+        all_ops += ops * len(gemms)
+        all_ms += ms * len(gemms)
+        if bound == "tensor":
+            tensor_ops += ops * len(gemms)
+            tensor_ms += ms * len(gemms)
+    if tensor_ms > 0:
+        achieved = tensor_ops / (tensor_ms / 1000.0) / 1e12
+    else:
+        achieved = all_ops / (all_ms / 1000.0) / 1e12 if all_ms else 0.0
+    traffic = None
+    traffic_file = ROOT / "profiles" / "integer_gemm_traffic.json"
+    if traffic_file.exists():
+        traffic = json.loads(traffic_file.read_text()).get("bytes_per_launch")
+    roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(int8_peak, 1), "unit": "TOPS",
+                "frac": round(achieved / int8_peak, 4), "traffic": traffic,
+                "kernel": "integer_gemm (tcgen05 kind::i8) on the tensor-bound layers",
+                "peak_source": f"2 x bf16 dense ({source} MEASURED_PEAKS bf16_tflops={bf16})",
+                "time_share": shares,
+                "layers": layer_rows}
+
+    cpu_baseline = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            with tempfile.TemporaryDirectory() as directory:
+                tops, seconds, _, sample = reference_sample(layers, Path(directory), CPU_BASELINE_FRACTION)
+            cpu_baseline = {"value": tops, "unit": "TOPS", "cores": min(os.cpu_count() or 1, 16),
+                            "kind": "reference", "seconds": round(seconds, 2),
+                            "sample": f"reference run_cpu (oracle/_ref) on {sample}"}
+        except Exception as error:  # the reference build may be absent
+            cpu_baseline = {"value": None, "unit": "TOPS", "cores": 0, "kind": "reference",
+                            "sample": f"unavailable: {error}"}
+
+    if rank == 0:
+        line = {
+            "metric": "int8 conv TOPS (config 2 layer sweep, bit-exact intconv.v1)",
+            "value": round(value, 2), "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(elapsed_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (seeded mt19937 int8 values)",
+            "config": {"workload": "config2: 1920x1088 layer sweep L1-L5, w8a8, FP16 stage boundary",
+                       "layers": [layer.name for layer in layers], "ops_per_step": ops_per_step,
+                       "l2": "inputs larger than L2 (about 1 GB touched per step), no flush",
+                       "parallelism": f"replicas x{world}"},
+            "e2e": {"value": round(e2e_value, 2), "unit": "TOPS", "ms_per_step": round(e2e_ms / args.steps, 4),
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "roofline": roofline,
+            "cpu_baseline": cpu_baseline,
+            "clocks": clocks,
+            "gpu_launches": launches,
+        }
+        print(json.dumps(line), flush=True)
+    for executor in executors:
+        executor.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -142,8 +142,9 @@ size_t nvcr_sm100_workspace_bytes(const nvcr_sm100_executor* executor);
 
 /* Per-step CUDA-event timing of subsequent runs (off by default). */
 int nvcr_sm100_set_profiling(nvcr_sm100_executor* executor, int enabled);
-/* Synchronises and copies up to `capacity` step times of the last profiled
- * run; *count receives the number of steps. */
+/* Synchronises and copies up to `capacity` kernel-segment times recorded by
+ * the profiled runs since the previous call (which are then forgotten);
+ * *count receives the number of segments. */
 int nvcr_sm100_profile(nvcr_sm100_executor* executor, nvcr_sm100_step_time* steps, size_t capacity, size_t* count);
 
 #ifdef __cplusplus

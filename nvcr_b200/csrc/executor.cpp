@@ -622,6 +622,13 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
         q.low_factor = conv.column_low_factor;
         status = kernels::quantize_activations(q, stream_);
         if (status != cudaSuccess) return cuda_error("activation quantiser launch", status);
+        const std::string label = program_.tensor_names[step.output];
+        const double positions = static_cast<double>(pc.positions);
+        const double a_bytes = positions * conv.k_real * conv.activation_limbs;
+        auto marked = mark("quantize:" + label, "quantize_activations", 0.0,
+                           static_cast<double>(source.count()) * 4.0 + a_bytes + positions * 4.0 +
+                               (q.column_terms != nullptr ? positions * 8.0 : 0.0));
+        if (!marked) return marked;
         kernels::GemmShape shape{conv.weight_limbs, conv.activation_limbs, conv.n_tile, conv.n_tiles, conv.k_padded,
                                  pc.positions_padded};
         kernels::GemmEpilogue ep{};
@@ -641,8 +648,11 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
         ep.status = status_;
         status = kernels::integer_gemm(pc.maps, shape, ep, stream_);
         if (status != cudaSuccess) return cuda_error("integer conv launch", status);
-        launched = 3;
-        break;
+        launches_ += 3;
+        const double ops = 2.0 * conv.k_real * static_cast<double>(node.out_channels) * positions;
+        const double out_bytes = static_cast<double>(out_extent.count()) * 4.0 * (step.residual ? 2.0 : 1.0);
+        return mark("integer_gemm:" + label, "integer_gemm", ops,
+                    a_bytes + static_cast<double>(node.out_channels) * conv.k_real * conv.weight_limbs + out_bytes);
     }
     case StepKind::chunk_add:
         status = kernels::chunk_add(tensor(step.source), tensor(step.output), count, stream_);
@@ -716,7 +726,11 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
     }
     if (status != cudaSuccess) return cuda_error(op_name(node.op), status);
     launches_ += launched;
-    return Ok{};
+    double bytes = static_cast<double>(count) * 4.0;
+    for (const auto id : step.reads) bytes += static_cast<double>(plan.extents[id].count()) * 4.0;
+    return mark(std::string(step.kind == StepKind::chunk_add ? "chunk_add" : op_name(node.op)) + ":" +
+                    program_.tensor_names[step.output],
+                step.kind == StepKind::chunk_add ? "chunk_add" : op_name(node.op), 0.0, bytes);
 }
 
 Status Executor::execute(const std::vector<TensorView>& inputs, const std::vector<TensorView>& outputs,
@@ -751,32 +765,16 @@ Status Executor::execute(const std::vector<TensorView>& inputs, const std::vecto
     if (!maps) return maps;
 
     launches_ = 0;
-    const bool timing = profiling_;
-    std::vector<std::string> labels;
-    std::vector<std::string> kernel_names;
-    std::vector<double> ops;
-    std::vector<double> bytes;
-    std::size_t event_count = 0;
-    auto mark = [&]() -> Status {
-        if (!timing) return Ok{};
-        if (event_count >= events_.size()) {
-            cudaEvent_t event;
-            const cudaError_t created = cudaEventCreate(&event);
-            if (created != cudaSuccess) return cuda_error("cudaEventCreate", created);
-            events_.push_back(event);
-        }
-        const cudaError_t recorded = cudaEventRecord(events_[event_count++], stream_);
-        if (recorded != cudaSuccess) return cuda_error("cudaEventRecord", recorded);
-        return Ok{};
-    };
-
+    run_started_ = false;
     auto* base = static_cast<std::uint8_t*>(arena_);
-    auto first = mark();
-    if (!first) return first;
+    auto started = mark("", "", 0.0, 0.0);
+    if (!started) return started;
+    double input_bytes = 0.0;
     for (std::size_t slot = 0; slot < program_.inputs.size(); ++slot) {
         const auto id = program_.inputs[slot];
         float* target = reinterpret_cast<float*>(base + plan.offsets[id]);
         const std::size_t count = plan.extents[id].count();
+        input_bytes += static_cast<double>(count) * 6.0;
         cudaError_t status;
         if (boundary == Boundary::half) {
             status = kernels::half_to_float(static_cast<const std::uint16_t*>(input_views[slot]->data), target, count,
@@ -789,44 +787,18 @@ Status Executor::execute(const std::vector<TensorView>& inputs, const std::vecto
         }
         if (status != cudaSuccess) return cuda_error("input conversion", status);
     }
-    if (timing) {
-        labels.push_back("inputs");
-        kernel_names.push_back("half_to_float");
-        ops.push_back(0.0);
-        double b = 0.0;
-        for (const auto id : program_.inputs) b += static_cast<double>(plan.extents[id].count()) * 6.0;
-        bytes.push_back(b);
-        auto m = mark();
-        if (!m) return m;
-    }
+    auto marked = mark("inputs", boundary == Boundary::half ? "half_to_float" : "copy", 0.0, input_bytes);
+    if (!marked) return marked;
     for (std::size_t s = 0; s < steps_.size(); ++s) {
         auto launched = launch_step(steps_[s], plan, s);
         if (!launched) return launched;
-        if (timing) {
-            const Step& step = steps_[s];
-            const Node& node = program_.nodes[step.node];
-            labels.push_back(std::string(op_name(node.op)) + ":" + program_.tensor_names[step.output]);
-            double o = 0.0;
-            double b = static_cast<double>(plan.extents[step.output].count()) * 4.0;
-            for (const auto id : step.reads) b += static_cast<double>(plan.extents[id].count()) * 4.0;
-            if (step.kind == StepKind::integer_conv) {
-                const Extent conv_out = plan.extents[node.output];
-                o = 2.0 * node.in_channels * static_cast<double>(node.out_channels) * conv_out.height * conv_out.width;
-                b += static_cast<double>(node.in_channels) * node.out_channels;  // int8 weights
-                kernel_names.push_back("integer_gemm");
-            } else {
-                kernel_names.push_back(op_name(node.op));
-            }
-            ops.push_back(o);
-            bytes.push_back(b);
-            auto m = mark();
-            if (!m) return m;
-        }
     }
+    double output_bytes = 0.0;
     for (std::size_t slot = 0; slot < program_.outputs.size(); ++slot) {
         const auto id = program_.outputs[slot];
         const float* source = reinterpret_cast<const float*>(base + plan.offsets[id]);
         const std::size_t count = plan.extents[id].count();
+        output_bytes += static_cast<double>(count) * 6.0;
         cudaError_t status;
         if (boundary == Boundary::half) {
             status = kernels::float_to_half(source, static_cast<std::uint16_t*>(output_views[slot]->data), count,
@@ -839,21 +811,32 @@ Status Executor::execute(const std::vector<TensorView>& inputs, const std::vecto
         }
         if (status != cudaSuccess) return cuda_error("output conversion", status);
     }
-    if (timing) {
-        labels.push_back("outputs");
-        kernel_names.push_back("float_to_half");
-        ops.push_back(0.0);
-        double b = 0.0;
-        for (const auto id : program_.outputs) b += static_cast<double>(plan.extents[id].count()) * 6.0;
-        bytes.push_back(b);
-        auto m = mark();
-        if (!m) return m;
-        timings_.clear();
-        for (std::size_t i = 0; i < labels.size(); ++i) {
-            timings_.push_back(StepTiming{labels[i], kernel_names[i], 0.0, ops[i], bytes[i]});
-        }
-    }
+    marked = mark("outputs", boundary == Boundary::half ? "float_to_half" : "copy", 0.0, output_bytes);
+    if (!marked) return marked;
     if (boundary == Boundary::host) return synchronize();
+    return Ok{};
+}
+
+// Records an event on the stream when profiling; the segment since the
+// previous event is attributed to `label` (the first call only starts).
+// Segments accumulate over runs until profile() collects them, so profiled
+// runs need no synchronisation.
+Status Executor::mark(const std::string& label, const std::string& kernel, double ops, double bytes) {
+    if (!profiling_) return Ok{};
+    if (marks_ >= events_.size()) {
+        cudaEvent_t event;
+        const cudaError_t created = cudaEventCreate(&event);
+        if (created != cudaSuccess) return cuda_error("cudaEventCreate", created);
+        events_.push_back(event);
+    }
+    const cudaError_t recorded = cudaEventRecord(events_[marks_], stream_);
+    if (recorded != cudaSuccess) return cuda_error("cudaEventRecord", recorded);
+    if (run_started_) {
+        timings_.push_back(StepTiming{label, kernel, 0.0, ops, bytes});
+        segment_starts_.push_back(marks_ - 1);
+    }
+    run_started_ = true;
+    ++marks_;
     return Ok{};
 }
 
@@ -885,13 +868,18 @@ Status Executor::synchronize() {
 Result<std::vector<StepTiming>> Executor::profile() {
     auto synced = synchronize();
     if (!synced) return synced.error();
-    for (std::size_t i = 0; i < timings_.size() && i + 1 < events_.size(); ++i) {
+    for (std::size_t i = 0; i < timings_.size(); ++i) {
         float ms = 0.0f;
-        const cudaError_t status = cudaEventElapsedTime(&ms, events_[i], events_[i + 1]);
+        const std::size_t first = segment_starts_[i];
+        const cudaError_t status = cudaEventElapsedTime(&ms, events_[first], events_[first + 1]);
         if (status != cudaSuccess) return cuda_error("cudaEventElapsedTime", status);
         timings_[i].milliseconds = ms;
     }
-    return timings_;
+    std::vector<StepTiming> collected;
+    collected.swap(timings_);
+    segment_starts_.clear();
+    marks_ = 0;
+    return collected;
 }
 
 }  // namespace nvcr_sm100

@@ -61,7 +61,8 @@ public:
     int launches_last_run() const { return launches_; }
     std::size_t workspace_bytes() const { return arena_bytes_; }
     void set_profiling(bool enabled) { profiling_ = enabled; }
-    // Per-step device times of the last profiled run (synchronises).
+    // Per-kernel device times of every profiled run since the last call
+    // (synchronises, then forgets them).
     Result<std::vector<StepTiming>> profile();
 
     struct IntegerConv;
@@ -79,6 +80,7 @@ private:
     enum class Boundary { half, float32, host };
     Status execute(const std::vector<TensorView>& inputs, const std::vector<TensorView>& outputs, Boundary boundary);
     Status launch_step(const Step& step, Plan& plan, std::size_t index);
+    Status mark(const std::string& label, const std::string& kernel, double ops, double bytes);
 
     Program program_;
     cudaStream_t stream_{nullptr};
@@ -94,6 +96,9 @@ private:
     int launches_{0};
     bool profiling_{false};
     std::vector<cudaEvent_t> events_;
+    std::size_t marks_{0};
+    bool run_started_{false};
+    std::vector<std::size_t> segment_starts_;
     std::vector<StepTiming> timings_;
 };
 

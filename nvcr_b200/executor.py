@@ -279,10 +279,11 @@ class CudaExecutor:
     def set_profiling(self, enabled: bool) -> None:
         _check(library().nvcr_sm100_set_profiling(self._handle, int(enabled)))
 
-    def profile(self) -> list[dict]:
+    def profile(self, capacity: int = 65536) -> list[dict]:
+        """Kernel segments of every profiled run since the last call."""
         count = ctypes.c_size_t(0)
-        steps = (StepTime * 256)()
-        _check(library().nvcr_sm100_profile(self._handle, steps, 256, ctypes.byref(count)))
+        steps = (StepTime * capacity)()
+        _check(library().nvcr_sm100_profile(self._handle, steps, capacity, ctypes.byref(count)))
         return [{"label": steps[i].label.decode(), "kernel": steps[i].kernel.decode(),
                  "ms": steps[i].milliseconds, "ops": steps[i].algorithmic_ops,
-                 "bytes": steps[i].algorithmic_bytes} for i in range(min(count.value, 256))]
+                 "bytes": steps[i].algorithmic_bytes} for i in range(min(count.value, capacity))]
