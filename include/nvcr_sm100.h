@@ -43,6 +43,7 @@ extern "C" {
 #define NVCR_SM100_DIGEST_MISMATCH 19
 
 typedef struct nvcr_sm100_executor nvcr_sm100_executor;
+typedef struct nvcr_sm100_program nvcr_sm100_program;
 
 /* A named batch-1 NCHW tensor. `data` is device FP16 for run_half, device
  * FP32 for run_float and host FP32 for run_host (reference HalfDeviceTensor,
@@ -79,6 +80,23 @@ int nvcr_sm100_supports_profile(const char* profile);
  * empty profile (a native stage), 1 for nvcr.intconv.v1; any other profile is
  * NVCR_SM100_INCOMPATIBLE_PRECISION. */
 int nvcr_sm100_is_normative(const char* profile, int* normative);
+
+/* A loaded program without a device (reference Program, program.hpp:105-115,
+ * from load_program, program.cpp:537-626): for output sizing and validation
+ * on hosts that have not created an executor yet. No GPU is needed. */
+int nvcr_sm100_program_load(const char* program_json_path, nvcr_sm100_program** program);
+int nvcr_sm100_program_load_memory(const char* program_json, size_t json_size, const float* weights,
+                                   size_t weight_count, nvcr_sm100_program** program);
+void nvcr_sm100_program_destroy(nvcr_sm100_program* program);
+int nvcr_sm100_program_tensor_count(const nvcr_sm100_program* program, int is_output, size_t* count);
+int nvcr_sm100_program_tensor_info(const nvcr_sm100_program* program, int is_output, size_t index,
+                                   const char** name, int32_t* channels);
+/* Reference infer_output_extents (normative_stage.cpp:42-65) on a program handle. */
+int nvcr_sm100_program_infer_output_extents(const nvcr_sm100_program* program, const nvcr_sm100_tensor* inputs,
+                                            size_t input_count, nvcr_sm100_tensor* outputs, size_t output_count);
+/* An executor over a copy of a loaded program (CudaExecutor::create). */
+int nvcr_sm100_executor_create_from_program(const nvcr_sm100_program* program, void* stream,
+                                            nvcr_sm100_executor** executor);
 
 /* Reference load_program + CudaExecutor::create (program.cpp:537-626,
  * cuda_executor.cu:1279-1313): loads <path> (.detprog.json) and the .detw it

@@ -18,6 +18,10 @@ struct nvcr_sm100_executor {
     std::unique_ptr<nvcr_sm100::Executor> executor;
 };
 
+struct nvcr_sm100_program {
+    nvcr_sm100::Program program;
+};
+
 namespace {
 
 using nvcr_sm100::Code;
@@ -76,6 +80,34 @@ int run_with(nvcr_sm100_executor* executor, const nvcr_sm100_tensor* inputs, siz
     }
     auto status = run(*executor->executor, views(inputs, input_count), views(outputs, output_count));
     if (!status) return report(status.error());
+    return succeed();
+}
+
+int infer_extents(const nvcr_sm100::Program& program, const nvcr_sm100_tensor* inputs, size_t input_count,
+                  nvcr_sm100_tensor* outputs, size_t output_count) {
+    if (inputs == nullptr && input_count > 0) return report(Code::invalid_argument, "null argument");
+    std::vector<nvcr_sm100::Extent> extents;
+    for (size_t i = 0; i < input_count; ++i) extents.push_back({inputs[i].channels, inputs[i].height, inputs[i].width});
+    auto inferred = nvcr_sm100::infer_output_extents(program, extents);
+    if (!inferred) return report(inferred.error());
+    if (output_count < inferred.value().size() || outputs == nullptr) {
+        return report(Code::invalid_argument, "output array is too small");
+    }
+    for (size_t slot = 0; slot < inferred.value().size(); ++slot) {
+        outputs[slot].name = program.tensor_names[program.outputs[slot]].c_str();
+        outputs[slot].channels = inferred.value()[slot].channels;
+        outputs[slot].height = inferred.value()[slot].height;
+        outputs[slot].width = inferred.value()[slot].width;
+    }
+    return succeed();
+}
+
+int tensor_info(const nvcr_sm100::Program& program, int is_output, size_t index, const char** name,
+                int32_t* channels) {
+    const auto& ids = is_output ? program.outputs : program.inputs;
+    if (index >= ids.size()) return report(Code::invalid_argument, "tensor index out of range");
+    if (name != nullptr) *name = program.tensor_names[ids[index]].c_str();
+    if (channels != nullptr) *channels = program.tensor_channels[ids[index]];
     return succeed();
 }
 
@@ -181,29 +213,66 @@ int nvcr_sm100_tensor_info(const nvcr_sm100_executor* executor, int is_output, s
     return succeed();
 }
 
+int nvcr_sm100_program_load(const char* path, nvcr_sm100_program** program) {
+    return guarded([&] {
+        if (path == nullptr || program == nullptr) return report(Code::invalid_argument, "null argument");
+        auto loaded = nvcr_sm100::load_program_file(path);
+        if (!loaded) return report(loaded.error());
+        *program = new nvcr_sm100_program{std::move(loaded.value())};
+        return succeed();
+    });
+}
+
+int nvcr_sm100_program_load_memory(const char* json, size_t json_size, const float* weights, size_t weight_count,
+                                   nvcr_sm100_program** program) {
+    return guarded([&] {
+        if (json == nullptr || program == nullptr || (weights == nullptr && weight_count > 0)) {
+            return report(Code::invalid_argument, "null argument");
+        }
+        static const float no_weights = 0.0f;
+        auto loaded = nvcr_sm100::load_program_text(std::string_view(json, json_size), ".",
+                                                    weights != nullptr ? weights : &no_weights, weight_count);
+        if (!loaded) return report(loaded.error());
+        *program = new nvcr_sm100_program{std::move(loaded.value())};
+        return succeed();
+    });
+}
+
+void nvcr_sm100_program_destroy(nvcr_sm100_program* program) { delete program; }
+
+int nvcr_sm100_program_tensor_count(const nvcr_sm100_program* program, int is_output, size_t* count) {
+    if (program == nullptr || count == nullptr) return report(Code::invalid_argument, "null argument");
+    *count = is_output ? program->program.outputs.size() : program->program.inputs.size();
+    return succeed();
+}
+
+int nvcr_sm100_program_tensor_info(const nvcr_sm100_program* program, int is_output, size_t index,
+                                   const char** name, int32_t* channels) {
+    if (program == nullptr) return report(Code::invalid_argument, "null program");
+    return tensor_info(program->program, is_output, index, name, channels);
+}
+
+int nvcr_sm100_program_infer_output_extents(const nvcr_sm100_program* program, const nvcr_sm100_tensor* inputs,
+                                            size_t input_count, nvcr_sm100_tensor* outputs, size_t output_count) {
+    return guarded([&] {
+        if (program == nullptr) return report(Code::invalid_argument, "null program");
+        return infer_extents(program->program, inputs, input_count, outputs, output_count);
+    });
+}
+
+int nvcr_sm100_executor_create_from_program(const nvcr_sm100_program* program, void* stream,
+                                            nvcr_sm100_executor** executor) {
+    return guarded([&] {
+        if (program == nullptr || executor == nullptr) return report(Code::invalid_argument, "null argument");
+        return finish_create(nvcr_sm100::Result<nvcr_sm100::Program>(program->program), stream, executor);
+    });
+}
+
 int nvcr_sm100_infer_output_extents(const nvcr_sm100_executor* executor, const nvcr_sm100_tensor* inputs,
                                     size_t input_count, nvcr_sm100_tensor* outputs, size_t output_count) {
     return guarded([&] {
-        if (executor == nullptr || (inputs == nullptr && input_count > 0)) {
-            return report(Code::invalid_argument, "null argument");
-        }
-        const auto& program = executor->executor->program();
-        std::vector<nvcr_sm100::Extent> extents;
-        for (size_t i = 0; i < input_count; ++i) {
-            extents.push_back({inputs[i].channels, inputs[i].height, inputs[i].width});
-        }
-        auto inferred = nvcr_sm100::infer_output_extents(program, extents);
-        if (!inferred) return report(inferred.error());
-        if (output_count < inferred.value().size() || outputs == nullptr) {
-            return report(Code::invalid_argument, "output array is too small");
-        }
-        for (size_t slot = 0; slot < inferred.value().size(); ++slot) {
-            outputs[slot].name = program.tensor_names[program.outputs[slot]].c_str();
-            outputs[slot].channels = inferred.value()[slot].channels;
-            outputs[slot].height = inferred.value()[slot].height;
-            outputs[slot].width = inferred.value()[slot].width;
-        }
-        return succeed();
+        if (executor == nullptr) return report(Code::invalid_argument, "null executor");
+        return infer_extents(executor->executor->program(), inputs, input_count, outputs, output_count);
     });
 }
 

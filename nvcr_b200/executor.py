@@ -70,7 +70,9 @@ EXPORTS = [
     "nvcr_sm100_executor_destroy", "nvcr_sm100_tensor_count", "nvcr_sm100_tensor_info",
     "nvcr_sm100_infer_output_extents", "nvcr_sm100_run_half", "nvcr_sm100_run_float", "nvcr_sm100_run_host",
     "nvcr_sm100_synchronize", "nvcr_sm100_stream", "nvcr_sm100_last_launch_count", "nvcr_sm100_workspace_bytes",
-    "nvcr_sm100_set_profiling", "nvcr_sm100_profile",
+    "nvcr_sm100_set_profiling", "nvcr_sm100_profile", "nvcr_sm100_program_load", "nvcr_sm100_program_load_memory",
+    "nvcr_sm100_program_destroy", "nvcr_sm100_program_tensor_count", "nvcr_sm100_program_tensor_info",
+    "nvcr_sm100_program_infer_output_extents", "nvcr_sm100_executor_create_from_program",
 ]
 
 _lib: ctypes.CDLL | None = None
@@ -111,6 +113,15 @@ def library() -> ctypes.CDLL:
         "nvcr_sm100_workspace_bytes": (sz, [vp]),
         "nvcr_sm100_set_profiling": (ctypes.c_int, [vp, ctypes.c_int]),
         "nvcr_sm100_profile": (ctypes.c_int, [vp, ctypes.POINTER(StepTime), sz, ctypes.POINTER(sz)]),
+        "nvcr_sm100_program_load": (ctypes.c_int, [ctypes.c_char_p, handle_out]),
+        "nvcr_sm100_program_load_memory": (ctypes.c_int, [ctypes.c_char_p, sz, ctypes.POINTER(ctypes.c_float), sz,
+                                                          handle_out]),
+        "nvcr_sm100_program_destroy": (None, [vp]),
+        "nvcr_sm100_program_tensor_count": (ctypes.c_int, [vp, ctypes.c_int, ctypes.POINTER(sz)]),
+        "nvcr_sm100_program_tensor_info": (ctypes.c_int, [vp, ctypes.c_int, sz, ctypes.POINTER(ctypes.c_char_p),
+                                                          i32p]),
+        "nvcr_sm100_program_infer_output_extents": (ctypes.c_int, [vp, tp, sz, tp, sz]),
+        "nvcr_sm100_executor_create_from_program": (ctypes.c_int, [vp, vp, handle_out]),
     }
     for name, (restype, argtypes) in signatures.items():
         function = getattr(lib, name)
@@ -146,6 +157,67 @@ def _stream_handle(stream) -> int | None:
     if isinstance(stream, int):
         return stream
     return int(getattr(stream, "cuda_stream"))
+
+
+class LoadedProgram:
+    """A program loaded and validated by the library, without a device
+    (reference load_program + infer_output_extents)."""
+
+    def __init__(self, handle: int) -> None:
+        self._handle = ctypes.c_void_p(handle)
+        lib = library()
+        self.input_names, self.output_names = [], []
+        for is_output, names in ((0, self.input_names), (1, self.output_names)):
+            count = ctypes.c_size_t(0)
+            _check(lib.nvcr_sm100_program_tensor_count(self._handle, is_output, ctypes.byref(count)))
+            for index in range(count.value):
+                name = ctypes.c_char_p()
+                channels = ctypes.c_int32()
+                _check(lib.nvcr_sm100_program_tensor_info(self._handle, is_output, index, ctypes.byref(name),
+                                                          ctypes.byref(channels)))
+                names.append(name.value.decode())
+
+    @classmethod
+    def load(cls, program_json: str | Path) -> "LoadedProgram":
+        handle = ctypes.c_void_p()
+        _check(library().nvcr_sm100_program_load(str(program_json).encode(), ctypes.byref(handle)))
+        return cls(handle.value)
+
+    @classmethod
+    def from_program(cls, program: Program, fp16_weights: bool = True) -> "LoadedProgram":
+        weights = np.ascontiguousarray(program.fp16_weights() if fp16_weights else program.weights, np.float32)
+        text = json.dumps(program.to_json(f"{program.name}.detw", "0" * 64)).encode()
+        handle = ctypes.c_void_p()
+        _check(library().nvcr_sm100_program_load_memory(text, len(text),
+                                                        weights.ctypes.data_as(ctypes.POINTER(ctypes.c_float)),
+                                                        weights.size, ctypes.byref(handle)))
+        return cls(handle.value)
+
+    def infer_output_extents(self, extents: Sequence[tuple[int, int, int]]) -> list[tuple[int, int, int]]:
+        ins = (Tensor * max(1, len(extents)))()
+        for i, (c, h, w) in enumerate(extents):
+            ins[i] = Tensor(None, c, h, w, None)
+        outs = (Tensor * max(1, len(self.output_names)))()
+        _check(library().nvcr_sm100_program_infer_output_extents(self._handle, ins, len(extents), outs,
+                                                                 len(self.output_names)))
+        return [(outs[i].channels, outs[i].height, outs[i].width) for i in range(len(self.output_names))]
+
+    def executor(self, stream=None) -> "CudaExecutor":
+        handle = ctypes.c_void_p()
+        _check(library().nvcr_sm100_executor_create_from_program(self._handle, _stream_handle(stream),
+                                                                 ctypes.byref(handle)))
+        return CudaExecutor(handle.value, None)
+
+    def close(self) -> None:
+        if self._handle:
+            library().nvcr_sm100_program_destroy(self._handle)
+            self._handle = ctypes.c_void_p()
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class CudaExecutor:

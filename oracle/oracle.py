@@ -248,7 +248,7 @@ class Reference:
         status = self.lib.ref_infer_extents(str(program_json).encode(), len(extents_in), flat,
                                             max_outputs, out, error, 512)
         if status != 0:
-            return status - 1, error.value.decode()
+            return status, error.value.decode()  # 1 + ErrorCode
         return 0, [tuple(out[3 * i: 3 * i + 3]) for i in range(max_outputs) if out[3 * i] != 0]
 
     def quantize_weights(self, weights: np.ndarray, weight_bits: int):

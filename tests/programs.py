@@ -67,3 +67,66 @@ def sigmoid_sweep_values(step: int = 1021) -> np.ndarray:
     values = bits.view(np.float32)
     edges = np.array([-88.0, -87.0, -86.99999, 87.0, 87.99999, 88.0], np.float32)
     return np.concatenate([values, edges])
+
+
+def conv_program(stream: SeededStream, cin, cout, kernel, stride, pads, bits, *, wsilu=False,
+                         chunk_add=False, residual=False, name="conv") -> Program:
+    p = Program(name=name)
+    x = p.add_input("x", cin)
+    r = None
+    if residual:
+        # An earlier tensor of the output's shape (produced before the conv, so
+        # the add folds into the conv's epilogue): a 1x1 FP32 depthwise of x, sliced.
+        out_c = cout // 2 if chunk_add else cout
+        if out_c > cin:
+            raise ValueError("residual needs out channels <= in channels")
+        r = p.conv(x, cin, stream.uniform(-1, 1, cin), stream.uniform(-1, 1, cin), "r_dw", depthwise=True)
+        if out_c < cin:
+            r = p.unary(OpKind.slice_channels, r, "r", begin=0, end=out_c)
+    taps = kernel[0] * kernel[1]
+    w = stream.uniform(-0.5, 0.5, cout * cin * taps)
+    b = stream.uniform(-0.2, 0.2, cout)
+    y = p.dense_conv(x, cout, w, b, "c", kernel=kernel, stride=stride, pads=pads, bits=bits)
+    if wsilu:
+        s = p.unary(OpKind.mul_scalar, y, "s", scalar=4.0)
+        g = p.unary(OpKind.sigmoid, s, "g")
+        y = p.binary(OpKind.mul, y, g, "w")
+    if chunk_add:
+        a = p.unary(OpKind.slice_channels, y, "a", begin=0, end=cout // 2)
+        b2 = p.unary(OpKind.slice_channels, y, "b", begin=cout // 2, end=cout)
+        y = p.binary(OpKind.add, a, b2, "ca")
+    if residual:
+        y = p.binary(OpKind.add, y, r, "res")
+    return p.finish([y])
+
+
+CONV_CASES = [
+    # cin, cout, kernel, stride, pads, height, width
+    (64, 64, (3, 3), (1, 1), (1, 1, 1, 1), 36, 44),      # config-1 shape
+    (3, 64, (3, 3), (2, 2), (1, 1, 1, 1), 40, 70),       # config-2 L1 shape (K = 27)
+    (128, 256, (1, 1), (1, 1), (0, 0, 0, 0), 17, 30),    # pointwise, one full N tile
+    (70, 133, (1, 1), (1, 1), (0, 0, 0, 0), 11, 18),     # ragged N, K
+    (96, 300, (1, 1), (1, 1), (0, 0, 0, 0), 9, 15),      # two N tiles
+    (32, 520, (3, 3), (1, 1), (1, 1, 1, 1), 8, 9),       # three N tiles
+    (16, 24, (2, 2), (2, 2), (0, 0, 0, 0), 10, 14),      # 2x2 stride 2
+    (20, 40, (3, 5), (1, 2), (2, 0, 1, 3), 13, 21),      # asymmetric window and pads
+    (200, 48, (3, 3), (1, 1), (1, 1, 1, 1), 5, 7),       # K = 1800, ragged
+]
+
+
+def edge_value_input(stream: SeededStream, cin: int = 40) -> np.ndarray:
+    """All-zero positions (e = 0), NaN/inf positions (NaN out), maxima in the
+    subnormal range (exponents below -126: the wide ldexp path), subnormal
+    steps, large magnitudes, values on rounding ties and a near-FLT_MAX value."""
+    h, w = 6, 50
+    x = stream.tensor(cin, h, w, 1.0)
+    x[:, 0, 0] = 0.0
+    x[3, 0, 1] = np.nan
+    x[7, 0, 2] = np.inf
+    x[8, 0, 3] = -np.inf
+    x[:, 1, :] *= np.float32(2.0 ** -130)
+    x[:, 2, :10] = np.float32(2.0 ** -149) * np.arange(1, cin + 1, dtype=np.float32)[:, None]
+    x[:, 3, :] *= np.float32(60000.0)
+    x[:, 4, :] = (np.round(x[:, 4, :] * 64) + 0.5) / 64
+    x[0, 5, :] = np.float32(3.4e38)
+    return x

@@ -113,3 +113,44 @@ def test_load_normative_checks_presence_and_digest(built_library, tmp_path):
     with pytest.raises(ex.ExecutorError) as error:
         ex.CudaExecutor.load_normative(tmp_path, "stage", "")
     assert error.value.code == ex.ErrorCode.invalid_argument
+
+
+def test_program_handle_infers_extents_like_the_reference(built_library, reference, tmp_path):
+    """Shape inference needs no GPU; it must agree with the reference's
+    infer_output_extents, errors included."""
+    stream = SeededStream(3)
+    program = op_program(stream)
+    path = program.write(tmp_path)
+    loaded = ex.LoadedProgram.load(path)
+    assert loaded.input_names == ["x"] and loaded.output_names == ["sum", "pointwise"]
+    for extent in [(70, 33, 47), (70, 2, 64), (70, 11, 18), (70, 1, 1), (70, 4, 2), (71, 5, 5), (70, 0, 4),
+                   (70, 5, -1)]:
+        ref_code, ref_value = reference.infer_extents(path, [extent])
+        try:
+            ours = loaded.infer_output_extents([extent])
+            assert ref_code == 0, f"{extent}: reference refused ({ref_value}), ours accepted"
+            assert ours == ref_value, extent
+        except ex.ExecutorError as error:
+            assert ref_code == int(error.code) + 1, f"{extent}: reference {ref_code}, ours {error}"
+    data = data_movement_program().write(tmp_path / "dm")
+    loaded = ex.LoadedProgram.load(data)
+    for extents in [[(5, 12, 20), (20, 1, 1), (1, 5, 7)], [(5, 12, 20), (20, 1, 2), (1, 5, 7)],
+                    [(5, 11, 20), (20, 1, 1), (1, 5, 7)], [(5, 12, 20), (20, 1, 1), (1, 7, 7)]]:
+        ref_code, ref_value = reference.infer_extents(data, extents)
+        try:
+            assert loaded.infer_output_extents(extents) == ref_value and ref_code == 0, extents
+        except ex.ExecutorError as error:
+            assert ref_code == int(error.code) + 1, f"{extents}: reference {ref_code}, ours {error}"
+
+
+def test_program_handle_without_gpu_refuses_executor(built_library, tmp_path):
+    """Creating an executor needs an sm_100 device: on a host without one the
+    call fails cleanly with a backend or target error, never a crash."""
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    loaded = ex.LoadedProgram.from_program(data_movement_program())
+    with pytest.raises(ex.ExecutorError) as error:
+        loaded.executor()
+    assert error.value.code in (ex.ErrorCode.backend_error, ex.ErrorCode.incompatible_target)

@@ -16,7 +16,8 @@ from nvcr_b200.executor import CudaExecutor
 from nvcr_b200.program import OpKind, Program, SeededStream
 from nvcr_b200.workloads import config1, layer_input
 from oracle.oracle import count_differing, same_bits
-from tests.programs import data_movement_program, op_program, sigmoid_program, sigmoid_sweep_values
+from tests.programs import (CONV_CASES, conv_program, data_movement_program, edge_value_input, op_program,
+                            sigmoid_program, sigmoid_sweep_values)
 
 pytestmark = pytest.mark.gpu
 
@@ -125,49 +126,6 @@ def test_config1_half(cuda, oracle):
     assert count_differing(got.astype(np.float32), expected.astype(np.float32)) == 0
 
 
-def _random_conv_program(stream: SeededStream, cin, cout, kernel, stride, pads, bits, *, wsilu=False,
-                         chunk_add=False, residual=False, name="conv") -> Program:
-    p = Program(name=name)
-    x = p.add_input("x", cin)
-    r = None
-    if residual:
-        # An earlier tensor of the output's shape (produced before the conv, so
-        # the add folds into the conv's epilogue): a 1x1 FP32 depthwise of x, sliced.
-        out_c = cout // 2 if chunk_add else cout
-        if out_c > cin:
-            raise ValueError("residual needs out channels <= in channels")
-        r = p.conv(x, cin, stream.uniform(-1, 1, cin), stream.uniform(-1, 1, cin), "r_dw", depthwise=True)
-        if out_c < cin:
-            r = p.unary(OpKind.slice_channels, r, "r", begin=0, end=out_c)
-    taps = kernel[0] * kernel[1]
-    w = stream.uniform(-0.5, 0.5, cout * cin * taps)
-    b = stream.uniform(-0.2, 0.2, cout)
-    y = p.dense_conv(x, cout, w, b, "c", kernel=kernel, stride=stride, pads=pads, bits=bits)
-    if wsilu:
-        s = p.unary(OpKind.mul_scalar, y, "s", scalar=4.0)
-        g = p.unary(OpKind.sigmoid, s, "g")
-        y = p.binary(OpKind.mul, y, g, "w")
-    if chunk_add:
-        a = p.unary(OpKind.slice_channels, y, "a", begin=0, end=cout // 2)
-        b2 = p.unary(OpKind.slice_channels, y, "b", begin=cout // 2, end=cout)
-        y = p.binary(OpKind.add, a, b2, "ca")
-    if residual:
-        y = p.binary(OpKind.add, y, r, "res")
-    return p.finish([y])
-
-
-CONV_CASES = [
-    # cin, cout, kernel, stride, pads, height, width
-    (64, 64, (3, 3), (1, 1), (1, 1, 1, 1), 36, 44),      # config-1 shape
-    (3, 64, (3, 3), (2, 2), (1, 1, 1, 1), 40, 70),       # config-2 L1 shape (K = 27)
-    (128, 256, (1, 1), (1, 1), (0, 0, 0, 0), 17, 30),    # pointwise, one full N tile
-    (70, 133, (1, 1), (1, 1), (0, 0, 0, 0), 11, 18),     # ragged N, K
-    (96, 300, (1, 1), (1, 1), (0, 0, 0, 0), 9, 15),      # two N tiles
-    (32, 520, (3, 3), (1, 1), (1, 1, 1, 1), 8, 9),       # three N tiles
-    (16, 24, (2, 2), (2, 2), (0, 0, 0, 0), 10, 14),      # 2x2 stride 2
-    (20, 40, (3, 5), (1, 2), (2, 0, 1, 3), 13, 21),      # asymmetric window and pads
-    (200, 48, (3, 3), (1, 1), (1, 1, 1, 1), 5, 7),       # K = 1800, ragged
-]
 
 
 @pytest.mark.parametrize("case", CONV_CASES, ids=lambda c: f"{c[0]}to{c[1]}k{c[2][0]}x{c[2][1]}s{c[3][0]}")
@@ -175,7 +133,7 @@ CONV_CASES = [
 def test_integer_conv(cuda, oracle, case, bits):
     cin, cout, kernel, stride, pads, h, w = case
     stream = SeededStream(1000 + cin + cout)
-    program = _random_conv_program(stream, cin, cout, kernel, stride, pads, bits)
+    program = conv_program(stream, cin, cout, kernel, stride, pads, bits)
     x = stream.tensor(cin, h, w, 2.0)
     assert_parity(program, [x], oracle, f"conv {case} w{bits[0]}a{bits[1]}")
 
@@ -185,7 +143,7 @@ def test_integer_conv(cuda, oracle, case, bits):
 def test_epilogue_fusions(cuda, oracle, bits, fusion):
     stream = SeededStream(77)
     cin, cout = (96, 192) if "chunk" in fusion else (96, 64)
-    program = _random_conv_program(stream, cin, cout, (1, 1), (1, 1), (0, 0, 0, 0), bits,
+    program = conv_program(stream, cin, cout, (1, 1), (1, 1), (0, 0, 0, 0), bits,
                                    wsilu="wsilu" in fusion, chunk_add="chunk" in fusion,
                                    residual="residual" in fusion)
     x = stream.tensor(cin, 13, 29, 3.0)
@@ -194,7 +152,7 @@ def test_epilogue_fusions(cuda, oracle, bits, fusion):
 
 def test_chunk_add_many_tiles(cuda, oracle):
     stream = SeededStream(78)
-    program = _random_conv_program(stream, 64, 1040, (1, 1), (1, 1), (0, 0, 0, 0), (8, 8), chunk_add=True)
+    program = conv_program(stream, 64, 1040, (1, 1), (1, 1), (0, 0, 0, 0), (8, 8), chunk_add=True)
     x = stream.tensor(64, 7, 23, 2.0)
     assert_parity(program, [x], oracle, "chunk-add over several tiles")
 
@@ -205,20 +163,11 @@ def test_activation_edge_values(cuda, oracle, bits):
     tiny inputs (exponents below -126: the wide ldexp path), huge inputs, and
     values on rounding ties."""
     stream = SeededStream(5)
-    cin, h, w = 40, 6, 50
-    x = stream.tensor(cin, h, w, 1.0)
-    x[:, 0, 0] = 0.0                                   # all-zero position
-    x[3, 0, 1] = np.nan                                # NaN position
-    x[7, 0, 2] = np.inf
-    x[8, 0, 3] = -np.inf
-    x[:, 1, :] *= np.float32(2.0 ** -130)              # subnormal-range maxima
-    x[:, 2, :10] = np.float32(2.0 ** -149) * np.arange(1, 41, dtype=np.float32)[:, None]
-    x[:, 3, :] *= np.float32(60000.0)                   # large magnitudes
-    x[:, 4, :] = (np.round(x[:, 4, :] * 64) + 0.5) / 64  # ties after scaling
-    x[0, 5, :] = np.float32(3.4e38)
-    program = _random_conv_program(stream, cin, 72, (3, 3), (1, 1), (1, 1, 1, 1), bits)
+    cin = 40
+    x = edge_value_input(stream, cin)
+    program = conv_program(stream, cin, 72, (3, 3), (1, 1), (1, 1, 1, 1), bits)
     assert_parity(program, [x], oracle, f"edge values w{bits[0]}a{bits[1]}")
-    program = _random_conv_program(stream, cin, 72, (1, 1), (1, 1), (0, 0, 0, 0), bits)
+    program = conv_program(stream, cin, 72, (1, 1), (1, 1), (0, 0, 0, 0), bits)
     assert_parity(program, [x], oracle, f"edge values pointwise w{bits[0]}a{bits[1]}")
 
 
