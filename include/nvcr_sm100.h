@@ -165,6 +165,21 @@ int nvcr_sm100_set_profiling(nvcr_sm100_executor* executor, int enabled);
  * *count receives the number of segments. */
 int nvcr_sm100_profile(nvcr_sm100_executor* executor, nvcr_sm100_step_time* steps, size_t capacity, size_t* count);
 
+/* run_half without device allocation. No counterpart in the reference: it
+ * exists for hosts that cannot call cudaMalloc while they run (an enqueue
+ * inside a framework that owns all device memory, a real-time decode thread
+ * that must not block on the allocator). Every scratch tensor of the run lives
+ * in one file-scope static device array of NVCR_SM100_STATIC_WORKSPACE_BYTES,
+ * which each GPU that loads the library keeps until exit. The first call on a
+ * device looks the array's address up (cudaGetSymbolAddress): make it before
+ * any stream capture. All calls share the array: calls whose work overlaps on
+ * the GPU race and must be ordered by the caller. A run needing more than the
+ * array holds fails with NVCR_SM100_INVALID_ARGUMENT before enqueuing work.
+ * Inputs, outputs and their meaning are those of nvcr_sm100_run_half. */
+#define NVCR_SM100_STATIC_WORKSPACE_BYTES (64u * 1024u * 1024u)
+int nvcr_sm100_run_half_static(nvcr_sm100_executor* executor, const nvcr_sm100_tensor* inputs, size_t input_count,
+                               const nvcr_sm100_tensor* outputs, size_t output_count);
+
 #ifdef __cplusplus
 }
 #endif

@@ -3,7 +3,7 @@
 
 #include "../../include/nvcr_sm100.h"
 
-#include "executor.hpp"
+#include "capi_internal.hpp"
 #include "sha256.hpp"
 
 #include <cstdio>
@@ -13,10 +13,6 @@
 #include <sstream>
 #include <string>
 #include <sys/stat.h>
-
-struct nvcr_sm100_executor {
-    std::unique_ptr<nvcr_sm100::Executor> executor;
-};
 
 struct nvcr_sm100_program {
     nvcr_sm100::Program program;
@@ -40,6 +36,13 @@ int succeed() {
     last_error.clear();
     return NVCR_SM100_OK;
 }
+
+}  // namespace
+
+int nvcr_sm100::report_error(const Error& error) { return report(error); }
+int nvcr_sm100::report_ok() { return succeed(); }
+
+namespace {
 
 template <typename F>
 int guarded(F&& body) {

@@ -57,6 +57,8 @@ struct Executor::Plan {
     std::vector<PlannedConv> convs;    // per step
     std::size_t arena_bytes{0};
     std::uint64_t maps_generation{0};
+    std::vector<kernels::GemmMaps> workspace_maps;  // per step, against workspace_base
+    std::uint8_t* workspace_base{nullptr};
 };
 
 namespace {
@@ -586,10 +588,32 @@ Status Executor::encode_activation_maps(Plan& plan) {
     return Ok{};
 }
 
+// The activation maps of a plan placed in a caller's workspace at `base`.
+Status Executor::encode_workspace_maps(Plan& plan, std::uint8_t* base) {
+    if (plan.workspace_base == base && plan.workspace_maps.size() == steps_.size()) return Ok{};
+    plan.workspace_maps.assign(steps_.size(), kernels::GemmMaps{});
+    for (std::size_t s = 0; s < steps_.size(); ++s) {
+        if (steps_[s].kind != StepKind::integer_conv) continue;
+        const IntegerConv& conv = convs_[static_cast<std::size_t>(steps_[s].conv)];
+        const PlannedConv& pc = plan.convs[s];
+        kernels::GemmMaps& maps = plan.workspace_maps[s];
+        cudaError_t status = kernels::encode_int8_map(&maps.a_high, base + pc.a_high, pc.positions_padded,
+                                                      conv.k_padded, 128);
+        if (status == cudaSuccess) {
+            status = kernels::encode_int8_map(&maps.a_low, base + pc.a_low, pc.positions_padded, conv.k_padded, 128);
+        }
+        if (status != cudaSuccess) return cuda_error("cuTensorMapEncodeTiled activations", status);
+        maps.b_high = conv.b_high_map;
+        maps.b_low = conv.b_low_map;
+    }
+    plan.workspace_base = base;
+    return Ok{};
+}
+
 // ---------------------------------------------------------------- execution
 
 Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
-    auto* base = static_cast<std::uint8_t*>(arena_);
+    auto* base = run_base_;
     auto tensor = [&](std::size_t id) { return reinterpret_cast<float*>(base + plan.offsets[id]); };
     const Node& node = program_.nodes[step.node];
     const Extent out_extent = plan.extents[step.output];
@@ -646,7 +670,7 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
         ep.out_channels = conv.out_channels;
         ep.positions = pc.positions;
         ep.status = status_;
-        status = kernels::integer_gemm(pc.maps, shape, ep, stream_);
+        status = kernels::integer_gemm(run_in_workspace_ ? plan.workspace_maps[index] : pc.maps, shape, ep, stream_);
         if (status != cudaSuccess) return cuda_error("integer conv launch", status);
         launches_ += 3;
         const double ops = 2.0 * conv.k_real * static_cast<double>(node.out_channels) * positions;
@@ -734,7 +758,7 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
 }
 
 Status Executor::execute(const std::vector<TensorView>& inputs, const std::vector<TensorView>& outputs,
-                         Boundary boundary) {
+                         Boundary boundary, void* workspace, std::size_t workspace_bytes) {
     std::vector<Extent> extents;
     std::vector<const TensorView*> input_views;
     for (const auto id : program_.inputs) {
@@ -759,14 +783,28 @@ Status Executor::execute(const std::vector<TensorView>& inputs, const std::vecto
         }
         output_views.push_back(view);
     }
-    auto arena = ensure_arena(plan.arena_bytes);
-    if (!arena) return arena;
-    auto maps = encode_activation_maps(plan);
-    if (!maps) return maps;
+    if (workspace == nullptr) {
+        auto arena = ensure_arena(plan.arena_bytes);
+        if (!arena) return arena;
+        auto maps = encode_activation_maps(plan);
+        if (!maps) return maps;
+        run_base_ = static_cast<std::uint8_t*>(arena_);
+        run_in_workspace_ = false;
+    } else {
+        if (plan.arena_bytes > workspace_bytes) {
+            return fail(Code::invalid_argument, program_.name + ": this run needs " + std::to_string(plan.arena_bytes) +
+                                                    " bytes of workspace, more than the " +
+                                                    std::to_string(workspace_bytes) + " bytes provided");
+        }
+        auto maps = encode_workspace_maps(plan, static_cast<std::uint8_t*>(workspace));
+        if (!maps) return maps;
+        run_base_ = static_cast<std::uint8_t*>(workspace);
+        run_in_workspace_ = true;
+    }
 
     launches_ = 0;
     run_started_ = false;
-    auto* base = static_cast<std::uint8_t*>(arena_);
+    auto* base = run_base_;
     auto started = mark("", "", 0.0, 0.0);
     if (!started) return started;
     double input_bytes = 0.0;
@@ -842,6 +880,12 @@ Status Executor::mark(const std::string& label, const std::string& kernel, doubl
 
 Status Executor::run_half(const std::vector<TensorView>& inputs, const std::vector<TensorView>& outputs) {
     return execute(inputs, outputs, Boundary::half);
+}
+
+Status Executor::run_half_in_workspace(const std::vector<TensorView>& inputs, const std::vector<TensorView>& outputs,
+                                       void* workspace, std::size_t bytes) {
+    if (workspace == nullptr) return fail(Code::invalid_argument, "null workspace");
+    return execute(inputs, outputs, Boundary::half, workspace, bytes);
 }
 
 Status Executor::run_float(const std::vector<TensorView>& inputs, const std::vector<TensorView>& outputs) {

@@ -55,6 +55,11 @@ public:
     Status run_half(const std::vector<TensorView>& inputs, const std::vector<TensorView>& outputs);
     Status run_float(const std::vector<TensorView>& inputs, const std::vector<TensorView>& outputs);
     Status run_host(const std::vector<TensorView>& inputs, const std::vector<TensorView>& outputs);
+    // run_half with every scratch tensor placed in the caller-provided device
+    // workspace instead of the executor's own arena: nothing is allocated.
+    // Fails with invalid_argument when the plan needs more than `bytes`.
+    Status run_half_in_workspace(const std::vector<TensorView>& inputs, const std::vector<TensorView>& outputs,
+                                 void* workspace, std::size_t bytes);
     // Waits for the stream and reports a device-side wait that gave up.
     Status synchronize();
 
@@ -78,7 +83,9 @@ private:
     Status ensure_arena(std::size_t bytes);
     Status encode_activation_maps(Plan& plan);
     enum class Boundary { half, float32, host };
-    Status execute(const std::vector<TensorView>& inputs, const std::vector<TensorView>& outputs, Boundary boundary);
+    Status execute(const std::vector<TensorView>& inputs, const std::vector<TensorView>& outputs, Boundary boundary,
+                   void* workspace = nullptr, std::size_t workspace_bytes = 0);
+    Status encode_workspace_maps(Plan& plan, std::uint8_t* base);
     Status launch_step(const Step& step, Plan& plan, std::size_t index);
     Status mark(const std::string& label, const std::string& kernel, double ops, double bytes);
 
@@ -91,6 +98,8 @@ private:
     std::vector<IntegerConv> convs_;
     std::map<std::vector<std::int32_t>, std::unique_ptr<Plan>> plans_;
     void* arena_{nullptr};
+    std::uint8_t* run_base_{nullptr};  // arena_ or a caller's workspace, for the run in progress
+    bool run_in_workspace_{false};
     std::size_t arena_bytes_{0};
     std::uint64_t arena_generation_{0};
     int launches_{0};

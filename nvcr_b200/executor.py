@@ -73,6 +73,7 @@ EXPORTS = [
     "nvcr_sm100_set_profiling", "nvcr_sm100_profile", "nvcr_sm100_program_load", "nvcr_sm100_program_load_memory",
     "nvcr_sm100_program_destroy", "nvcr_sm100_program_tensor_count", "nvcr_sm100_program_tensor_info",
     "nvcr_sm100_program_infer_output_extents", "nvcr_sm100_executor_create_from_program",
+    "nvcr_sm100_run_half_static",
 ]
 
 _lib: ctypes.CDLL | None = None
@@ -122,6 +123,7 @@ def library() -> ctypes.CDLL:
                                                           i32p]),
         "nvcr_sm100_program_infer_output_extents": (ctypes.c_int, [vp, tp, sz, tp, sz]),
         "nvcr_sm100_executor_create_from_program": (ctypes.c_int, [vp, vp, handle_out]),
+        "nvcr_sm100_run_half_static": (ctypes.c_int, [vp, tp, sz, tp, sz]),
     }
     for name, (restype, argtypes) in signatures.items():
         function = getattr(lib, name)
@@ -329,6 +331,14 @@ class CudaExecutor:
         ins, k1 = self._tensors(inputs)
         outs, k2 = self._tensors(outputs)
         _check(library().nvcr_sm100_run_half(self._handle, ins, len(inputs), outs, len(outputs)))
+
+    def run_half_static(self, inputs: Mapping[str, object], outputs: Mapping[str, object]) -> None:
+        """run_half with all scratch in the library's fixed static device array
+        (nvcr_sm100_run_half_static): for hosts that cannot allocate device
+        memory while running. Calls overlapping on the GPU race on that array."""
+        ins, k1 = self._tensors(inputs)
+        outs, k2 = self._tensors(outputs)
+        _check(library().nvcr_sm100_run_half_static(self._handle, ins, len(inputs), outs, len(outputs)))
 
     def run_float(self, inputs: Mapping[str, object], outputs: Mapping[str, object]) -> None:
         ins, k1 = self._tensors(inputs)
