@@ -325,8 +325,8 @@ def main():
     layer_rows = []
     tensor_ops = tensor_ms = all_ops = all_ms = 0.0
     for layer, segments in zip(layers, per_layer_segments):
-        gemms = [seg for seg in segments if seg["kernel"] == "integer_gemm"]
-        quants = [seg for seg in segments if seg["kernel"] == "quantize_activations"]
+        gemms = [seg for seg in segments if seg["kernel"] == "integer_conv"]
+        quants = [seg for seg in segments if seg["kernel"] == "pixel_max"]
         if not gemms:
             continue
         ms = sum(seg["ms"] for seg in gemms) / len(gemms)
@@ -335,8 +335,8 @@ def main():
         bound = "tensor" if ops / bytes_ > ridge else "hbm"
         tops = ops / (ms / 1000.0) / 1e12
         gbs = bytes_ / (ms / 1000.0) / 1e9
-        layer_rows.append({"layer": layer.name, "gemm_ms": round(ms, 4), "quantize_ms": round(q_ms, 4),
-                           "gemm_tops": round(tops, 1), "gemm_gbs": round(gbs, 1), "bound": bound,
+        layer_rows.append({"layer": layer.name, "conv_ms": round(ms, 4), "pixel_max_ms": round(q_ms, 4),
+                           "conv_tops": round(tops, 1), "conv_gbs": round(gbs, 1), "bound": bound,
                            "frac": round(tops / int8_peak if bound == "tensor" else gbs / hbm, 3)})
         all_ops += ops * len(gemms)
         all_ms += ms * len(gemms)
@@ -353,7 +353,7 @@ def main():
         traffic = json.loads(traffic_file.read_text()).get("bytes_per_launch")
     roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(int8_peak, 1), "unit": "TOPS",
                 "frac": round(achieved / int8_peak, 4), "traffic": traffic,
-                "kernel": "integer_gemm (tcgen05 kind::i8) on the tensor-bound layers",
+                "kernel": "integer_conv: fused quantise-on-load tcgen05 kind::i8 implicit GEMM, tensor-bound layers",
                 "peak_source": f"2 x bf16 dense ({source} MEASURED_PEAKS bf16_tflops={bf16})",
                 "time_share": shares,
                 "layers": layer_rows}

@@ -25,6 +25,12 @@ struct Executor::IntegerConv {
     CUtensorMap b_high_map{};
     CUtensorMap b_low_map{};
     long long column_high_factor{0}, column_low_factor{0};
+    // Fused kernel geometry fixed at create time: channels per halo load and
+    // shared-memory ring depths, and the bytes one halo buffer may take.
+    int taps{1};
+    int group{1}, groups{1};
+    int a_stages{2}, b_stages{4};
+    int halo_budget{0};
 };
 
 enum class StepKind { generic, integer_conv, chunk_add };
@@ -46,9 +52,14 @@ struct Executor::Step {
 };
 
 struct PlannedConv {
-    std::size_t pixel_max{0}, a_high{0}, a_low{0}, exponents{0}, column_terms{0};
-    int positions{0}, positions_padded{0};
-    kernels::GemmMaps maps{};
+    std::size_t pixel_max{0};      // arena offset of the per-input-pixel maxima
+    std::size_t padded{0};         // arena offset of a row-padded copy of the source, or npos
+    int padded_width{0};
+    int positions{0};
+    int patch_h{0}, patch_w{0}, tiles_y{0}, tiles_x{0};
+    int halo_rows{0}, halo_box_w{0}, halo_bytes{0};
+    CUtensorMap halo_map{};
+    const void* halo_base{nullptr};  // source address halo_map was encoded for
 };
 
 struct Executor::Plan {
@@ -56,9 +67,6 @@ struct Executor::Plan {
     std::vector<std::size_t> offsets;  // per tensor id, npos when not materialised
     std::vector<PlannedConv> convs;    // per step
     std::size_t arena_bytes{0};
-    std::uint64_t maps_generation{0};
-    std::vector<kernels::GemmMaps> workspace_maps;  // per step, against workspace_base
-    std::uint8_t* workspace_base{nullptr};
 };
 
 namespace {
@@ -134,6 +142,19 @@ const TensorView* find_view(const std::vector<TensorView>& views, const std::str
         if (view.name == name) return &view;
     }
     return nullptr;
+}
+
+// Halo of a patch of output pixels: input rows and the TMA box width in
+// elements (a multiple of `align`, wide enough for a start rounded down to it).
+struct HaloShape {
+    int rows;
+    int box_w;
+};
+
+HaloShape halo_shape(int patch_h, int patch_w, const kernels::Window& w, int align) {
+    const int rows = (patch_h - 1) * w.stride_y + w.kernel_h;
+    const int cols = (patch_w - 1) * w.stride_x + w.kernel_w;
+    return {rows, ((cols + align - 1 + align - 1) / align) * align};
 }
 
 const char* op_name(Op op) {
@@ -342,6 +363,8 @@ Status Executor::prepare_integer_conv(std::size_t step_index) {
         return fail(Code::invalid_argument, "integer conv reduction length above 65536 is not supported");
     }
     conv.k_padded = round_up(conv.k_real, 128);
+    const int taps = step.window.kernel_h * step.window.kernel_w;
+    if (taps <= 0 || conv.k_real % taps != 0) return fail(Code::internal_error, "integer conv window mismatch");
     conv.chunk_add = step.chunk_add;
     const int rows = node.out_channels;
     const int accumulators = 1 + ((conv.weight_limbs == 2 || conv.activation_limbs == 2) ? 1 : 0) +
@@ -358,6 +381,34 @@ Status Executor::prepare_integer_conv(std::size_t step_index) {
         conv.out_channels = rows;
     }
     const int n_padded = conv.n_tiles * conv.n_tile;
+    conv.taps = taps;
+    const int source_channels = conv.k_real / taps;
+    // Shared memory: two A stages (filled by the producers), four B stages
+    // (TMA), and two halo buffers sized from what is left.
+    for (conv.b_stages = 4; conv.b_stages >= 2; --conv.b_stages) {
+        const int fixed = kernels::fused_conv_shared_bytes(conv.weight_limbs, conv.activation_limbs, conv.n_tile,
+                                                           conv.a_stages, conv.b_stages, 0);
+        conv.halo_budget = ((kernels::fused_conv_max_shared - fixed) / 2) / 1024 * 1024;
+        if (conv.halo_budget >= 16 * 1024) break;
+    }
+    {
+        const HaloShape reference = halo_shape(4, 32, step.window, 4);
+        const int per_channel = reference.rows * reference.box_w * static_cast<int>(sizeof(float));
+        int group = std::min({source_channels, 256, conv.halo_budget / per_channel});
+        if (group < source_channels && group >= 16) group = group / 16 * 16;
+        if (group < 1) return fail(Code::invalid_argument, "integer conv window is too large for the halo");
+        conv.group = group;
+        conv.groups = (source_channels + group - 1) / group;
+    }
+    // Node order k = c * taps + tap (weights [O][C][kh][kw]); kernel order is
+    // channel-group-major: g * (taps * group) + tap * G_g + (c - g * group).
+    auto kernel_k = [&](int k) {
+        const int c = k / taps;
+        const int tap = k - c * taps;
+        const int g = c / conv.group;
+        const int in_group = std::min(conv.group, source_channels - g * conv.group);
+        return g * taps * conv.group + tap * in_group + (c - g * conv.group);
+    };
     // Physical weight row -> node row (-1: zero padding). A chunk-add conv puts
     // pair (c, c + C/2) in columns j and j + n_tile/2 of one tile.
     auto source_row = [&](int physical) -> int {
@@ -389,7 +440,7 @@ Status Executor::prepare_integer_conv(std::size_t step_index) {
         long long low_sum = 0;
         for (int k = 0; k < conv.k_real; ++k) {
             const int q = quantized.values[static_cast<std::size_t>(row) * conv.k_real + k];
-            const std::size_t at = static_cast<std::size_t>(physical) * conv.k_padded + k;
+            const std::size_t at = static_cast<std::size_t>(physical) * conv.k_padded + kernel_k(k);
             if (conv.weight_limbs == 2) {
                 const int h = q >> 8;  // arithmetic shift: floor(q / 256)
                 const int l = (q & 255) - 128;
@@ -516,20 +567,42 @@ Result<Executor::Plan*> Executor::plan_for(const std::vector<Extent>& input_exte
             const Extent out = plan->extents[node.output];
             PlannedConv& pc = plan->convs[s];
             pc.positions = out.height * out.width;
-            pc.positions_padded = round_up(std::max(pc.positions, 1), 128);
-            if (pc.positions_padded / 128 > 65535) {
-                return fail(Code::invalid_argument, "integer conv has too many output positions");
+            // Patch shape: least padding waste, then the smallest halo that fits.
+            int best_waste = INT_MAX;
+            int best_bytes = INT_MAX;
+            for (const int patch_w : {32, 16, 64, 8, 128}) {
+                const int patch_h = 128 / patch_w;
+                const int tiles_y = (out.height + patch_h - 1) / patch_h;
+                const int tiles_x = (out.width + patch_w - 1) / patch_w;
+                const HaloShape halo = halo_shape(patch_h, patch_w, step.window, 4);
+                const int bytes = round_up(conv.group * halo.rows * halo.box_w * static_cast<int>(sizeof(float)), 1024);
+                if (bytes > conv.halo_budget || halo.box_w > 256 || halo.rows > 256) continue;
+                const long long covered = static_cast<long long>(tiles_y) * tiles_x * 128;
+                const int waste = static_cast<int>((covered - pc.positions) * 1000 / std::max(pc.positions, 1));
+                if (waste < best_waste - 30 || (waste <= best_waste + 30 && bytes < best_bytes)) {
+                    if (waste < best_waste) best_waste = waste;
+                    best_bytes = bytes;
+                    pc.patch_h = patch_h;
+                    pc.patch_w = patch_w;
+                    pc.tiles_y = tiles_y;
+                    pc.tiles_x = tiles_x;
+                    pc.halo_rows = halo.rows;
+                    pc.halo_box_w = halo.box_w;
+                    pc.halo_bytes = bytes;
+                }
             }
-            const std::size_t matrix = static_cast<std::size_t>(pc.positions_padded) * conv.k_padded;
+            if (pc.patch_w == 0) return fail(Code::invalid_argument, "integer conv window is too large for the halo");
+            // The halo TMA needs 16-byte rows: pad the source rows when they are not.
+            pc.padded = npos;
+            pc.padded_width = source.width;
+            if (source.width % 4 != 0) {
+                pc.padded_width = round_up(source.width, 4);
+                pc.padded = allocator.allocate(static_cast<std::size_t>(source.channels) * source.height *
+                                               pc.padded_width * sizeof(float));
+            }
             pc.pixel_max = allocator.allocate(static_cast<std::size_t>(source.height) * source.width * sizeof(float));
-            pc.a_high = allocator.allocate(matrix);
-            pc.a_low = conv.activation_limbs == 2 ? allocator.allocate(matrix) : pc.a_high;
-            pc.exponents = allocator.allocate(static_cast<std::size_t>(pc.positions) * sizeof(int));
-            pc.column_terms = conv.weight_limbs == 2
-                ? allocator.allocate(static_cast<std::size_t>(pc.positions) * sizeof(long long)) : npos;
-            scratch = {pc.pixel_max, pc.a_high, pc.exponents};
-            if (conv.activation_limbs == 2) scratch.push_back(pc.a_low);
-            if (pc.column_terms != npos) scratch.push_back(pc.column_terms);
+            scratch = {pc.pixel_max};
+            if (pc.padded != npos) scratch.push_back(pc.padded);
         }
         allocator.note_peak();
         for (const auto offset : scratch) allocator.release(offset);
@@ -567,49 +640,6 @@ Status Executor::ensure_arena(std::size_t bytes) {
     return Ok{};
 }
 
-Status Executor::encode_activation_maps(Plan& plan) {
-    if (plan.maps_generation == arena_generation_) return Ok{};
-    auto* base = static_cast<std::uint8_t*>(arena_);
-    for (std::size_t s = 0; s < steps_.size(); ++s) {
-        if (steps_[s].kind != StepKind::integer_conv) continue;
-        const IntegerConv& conv = convs_[static_cast<std::size_t>(steps_[s].conv)];
-        PlannedConv& pc = plan.convs[s];
-        cudaError_t status = kernels::encode_int8_map(&pc.maps.a_high, base + pc.a_high, pc.positions_padded,
-                                                      conv.k_padded, 128);
-        if (status == cudaSuccess) {
-            status = kernels::encode_int8_map(&pc.maps.a_low, base + pc.a_low, pc.positions_padded, conv.k_padded,
-                                              128);
-        }
-        if (status != cudaSuccess) return cuda_error("cuTensorMapEncodeTiled activations", status);
-        pc.maps.b_high = conv.b_high_map;
-        pc.maps.b_low = conv.b_low_map;
-    }
-    plan.maps_generation = arena_generation_;
-    return Ok{};
-}
-
-// The activation maps of a plan placed in a caller's workspace at `base`.
-Status Executor::encode_workspace_maps(Plan& plan, std::uint8_t* base) {
-    if (plan.workspace_base == base && plan.workspace_maps.size() == steps_.size()) return Ok{};
-    plan.workspace_maps.assign(steps_.size(), kernels::GemmMaps{});
-    for (std::size_t s = 0; s < steps_.size(); ++s) {
-        if (steps_[s].kind != StepKind::integer_conv) continue;
-        const IntegerConv& conv = convs_[static_cast<std::size_t>(steps_[s].conv)];
-        const PlannedConv& pc = plan.convs[s];
-        kernels::GemmMaps& maps = plan.workspace_maps[s];
-        cudaError_t status = kernels::encode_int8_map(&maps.a_high, base + pc.a_high, pc.positions_padded,
-                                                      conv.k_padded, 128);
-        if (status == cudaSuccess) {
-            status = kernels::encode_int8_map(&maps.a_low, base + pc.a_low, pc.positions_padded, conv.k_padded, 128);
-        }
-        if (status != cudaSuccess) return cuda_error("cuTensorMapEncodeTiled activations", status);
-        maps.b_high = conv.b_high_map;
-        maps.b_low = conv.b_low_map;
-    }
-    plan.workspace_base = base;
-    return Ok{};
-}
-
 // ---------------------------------------------------------------- execution
 
 Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
@@ -626,57 +656,81 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
         const PlannedConv& pc = plan.convs[index];
         const Extent source = plan.extents[step.source];
         const Extent conv_out = plan.extents[node.output];
-        kernels::QuantizeArgs q{};
-        q.in = tensor(step.source);
-        q.channels = source.channels;
-        q.in_h = source.height;
-        q.in_w = source.width;
-        q.out_h = conv_out.height;
-        q.out_w = conv_out.width;
-        q.window = step.window;
-        q.k_padded = conv.k_padded;
-        q.positions_padded = pc.positions_padded;
-        q.pixel_max = reinterpret_cast<float*>(base + pc.pixel_max);
-        q.high = reinterpret_cast<std::int8_t*>(base + pc.a_high);
-        q.low = reinterpret_cast<std::int8_t*>(base + pc.a_low);
-        q.exponents = reinterpret_cast<int*>(base + pc.exponents);
-        q.column_terms = pc.column_terms == npos ? nullptr : reinterpret_cast<long long*>(base + pc.column_terms);
-        q.activation_bits = conv.activation_bits;
-        q.high_factor = conv.column_high_factor;
-        q.low_factor = conv.column_low_factor;
-        status = kernels::quantize_activations(q, stream_);
-        if (status != cudaSuccess) return cuda_error("activation quantiser launch", status);
+        PlannedConv& planned = plan.convs[index];
+        float* pixel_max = reinterpret_cast<float*>(base + pc.pixel_max);
+        const float* halo_source = tensor(step.source);
+        if (pc.padded != npos) {
+            float* padded = reinterpret_cast<float*>(base + pc.padded);
+            status = kernels::pad_rows(halo_source, padded, static_cast<std::size_t>(source.channels) * source.height,
+                                       source.width, pc.padded_width, stream_);
+            if (status != cudaSuccess) return cuda_error("row padding launch", status);
+            halo_source = padded;
+            ++launches_;
+        }
+        if (planned.halo_base != halo_source) {
+            status = kernels::encode_halo_map(&planned.halo_map, halo_source, 0, source.channels, source.height,
+                                              pc.padded_width, pc.halo_box_w, pc.halo_rows, conv.group);
+            if (status != cudaSuccess) return cuda_error("cuTensorMapEncodeTiled halo", status);
+            planned.halo_base = halo_source;
+        }
+        status = kernels::pixel_max(tensor(step.source), 0, source.channels, source.height * source.width, pixel_max,
+                                    stream_);
+        if (status != cudaSuccess) return cuda_error("pixel max launch", status);
         const std::string label = program_.tensor_names[step.output];
         const double positions = static_cast<double>(pc.positions);
-        const double a_bytes = positions * conv.k_real * conv.activation_limbs;
-        auto marked = mark("quantize:" + label, "quantize_activations", 0.0,
-                           static_cast<double>(source.count()) * 4.0 + a_bytes + positions * 4.0 +
-                               (q.column_terms != nullptr ? positions * 8.0 : 0.0));
+        auto marked = mark("pixel_max:" + label, "pixel_max", 0.0,
+                           static_cast<double>(source.count()) * 4.0 + 4.0 * source.height * source.width);
         if (!marked) return marked;
-        kernels::GemmShape shape{conv.weight_limbs, conv.activation_limbs, conv.n_tile, conv.n_tiles, conv.k_padded,
-                                 pc.positions_padded};
-        kernels::GemmEpilogue ep{};
-        ep.scales = conv.scales;
-        ep.bias = conv.bias;
-        ep.row_terms = conv.activation_limbs == 2 ? conv.row_terms : nullptr;
-        ep.exponents = q.exponents;
-        ep.column_terms = q.column_terms;
-        ep.wsilu = step.wsilu ? 1 : 0;
-        ep.wsilu_scale = step.wsilu_scale;
-        ep.chunk_add = step.chunk_add ? 1 : 0;
-        ep.residual = step.residual ? tensor(*step.residual) : nullptr;
-        ep.out = tensor(step.output);
-        ep.out_half = 0;
-        ep.out_channels = conv.out_channels;
-        ep.positions = pc.positions;
-        ep.status = status_;
-        status = kernels::integer_gemm(run_in_workspace_ ? plan.workspace_maps[index] : pc.maps, shape, ep, stream_);
+        kernels::FusedConvArgs f{};
+        f.source = tensor(step.source);
+        f.source_half = 0;
+        f.pixel_max = pixel_max;
+        f.channels = source.channels;
+        f.in_h = source.height;
+        f.in_w = source.width;
+        f.out_h = conv_out.height;
+        f.out_w = conv_out.width;
+        f.window = step.window;
+        f.k_real = conv.k_real;
+        f.k_blocks = conv.k_padded / 128;
+        f.positions = pc.positions;
+        f.patch_h = pc.patch_h;
+        f.patch_w = pc.patch_w;
+        f.tiles_y = pc.tiles_y;
+        f.tiles_x = pc.tiles_x;
+        f.p_tiles = pc.tiles_y * pc.tiles_x;
+        f.group = conv.group;
+        f.groups = conv.groups;
+        f.halo_rows = pc.halo_rows;
+        f.halo_box_w = pc.halo_box_w;
+        f.halo_bytes = pc.halo_bytes;
+        f.a_stages = conv.a_stages;
+        f.b_stages = conv.b_stages;
+        f.n_tile = conv.n_tile;
+        f.n_tiles = conv.n_tiles;
+        f.column_high_factor = conv.weight_limbs == 2 ? conv.column_high_factor : 0;
+        f.column_low_factor = conv.weight_limbs == 2 ? conv.column_low_factor : 0;
+        f.scales = conv.scales;
+        f.bias = conv.bias;
+        f.row_terms = conv.activation_limbs == 2 ? conv.row_terms : nullptr;
+        f.wsilu = step.wsilu ? 1 : 0;
+        f.wsilu_scale = step.wsilu_scale;
+        f.chunk_add = step.chunk_add ? 1 : 0;
+        f.residual = step.residual ? tensor(*step.residual) : nullptr;
+        f.out = tensor(step.output);
+        f.out_half = 0;
+        f.out_channels = conv.out_channels;
+        f.d2s_block = 0;
+        f.status = status_;
+        status = kernels::fused_conv(conv.b_high_map, conv.b_low_map, planned.halo_map, conv.weight_limbs,
+                                     conv.activation_limbs, f, stream_);
         if (status != cudaSuccess) return cuda_error("integer conv launch", status);
-        launches_ += 3;
+        launches_ += 2;
         const double ops = 2.0 * conv.k_real * static_cast<double>(node.out_channels) * positions;
         const double out_bytes = static_cast<double>(out_extent.count()) * 4.0 * (step.residual ? 2.0 : 1.0);
-        return mark("integer_gemm:" + label, "integer_gemm", ops,
-                    a_bytes + static_cast<double>(node.out_channels) * conv.k_real * conv.weight_limbs + out_bytes);
+        return mark("integer_conv:" + label, "integer_conv", ops,
+                    static_cast<double>(source.count()) * 4.0 +
+                        static_cast<double>(node.out_channels) * conv.k_real * conv.weight_limbs + out_bytes);
     }
     case StepKind::chunk_add:
         status = kernels::chunk_add(tensor(step.source), tensor(step.output), count, stream_);
@@ -786,20 +840,14 @@ Status Executor::execute(const std::vector<TensorView>& inputs, const std::vecto
     if (workspace == nullptr) {
         auto arena = ensure_arena(plan.arena_bytes);
         if (!arena) return arena;
-        auto maps = encode_activation_maps(plan);
-        if (!maps) return maps;
         run_base_ = static_cast<std::uint8_t*>(arena_);
-        run_in_workspace_ = false;
     } else {
         if (plan.arena_bytes > workspace_bytes) {
             return fail(Code::invalid_argument, program_.name + ": this run needs " + std::to_string(plan.arena_bytes) +
                                                     " bytes of workspace, more than the " +
                                                     std::to_string(workspace_bytes) + " bytes provided");
         }
-        auto maps = encode_workspace_maps(plan, static_cast<std::uint8_t*>(workspace));
-        if (!maps) return maps;
         run_base_ = static_cast<std::uint8_t*>(workspace);
-        run_in_workspace_ = true;
     }
 
     launches_ = 0;

@@ -81,11 +81,10 @@ private:
     void plan_fusions();
     Result<Plan*> plan_for(const std::vector<Extent>& input_extents);
     Status ensure_arena(std::size_t bytes);
-    Status encode_activation_maps(Plan& plan);
     enum class Boundary { half, float32, host };
     Status execute(const std::vector<TensorView>& inputs, const std::vector<TensorView>& outputs, Boundary boundary,
                    void* workspace = nullptr, std::size_t workspace_bytes = 0);
-    Status encode_workspace_maps(Plan& plan, std::uint8_t* base);
+
     Status launch_step(const Step& step, Plan& plan, std::size_t index);
     Status mark(const std::string& label, const std::string& kernel, double ops, double bytes);
 
@@ -99,7 +98,6 @@ private:
     std::map<std::vector<std::int32_t>, std::unique_ptr<Plan>> plans_;
     void* arena_{nullptr};
     std::uint8_t* run_base_{nullptr};  // arena_ or a caller's workspace, for the run in progress
-    bool run_in_workspace_{false};
     std::size_t arena_bytes_{0};
     std::uint64_t arena_generation_{0};
     int launches_{0};

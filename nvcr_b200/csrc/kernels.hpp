@@ -41,6 +41,9 @@ struct Window {
 cudaError_t im2col(const float* in, float* out, int out_channels, int out_h, int out_w, int in_h, int in_w,
                    Window window, cudaStream_t stream);
 
+// Rows of `width` floats into rows of `padded` floats, zero-filled after each row.
+cudaError_t pad_rows(const float* in, float* out, std::size_t rows, int width, int padded, cudaStream_t stream);
+
 // ---- FP32 conv in the profile's fma order (bias, then channel, row, column) ----
 struct ConvShape {
     int in_channels, out_channels, depthwise;
@@ -50,58 +53,55 @@ struct ConvShape {
 cudaError_t conv_fp32(const float* weights, const float* bias, const float* in, float* out, ConvShape shape,
                       cudaStream_t stream);
 
-// ---- integer conv: activation quantiser ----
-// Positions are the output pixels of the (implicit) im2col window over `in`
-// ([channels][in_h][in_w]); K = channels * kernel_h * kernel_w in im2col order.
-struct QuantizeArgs {
-    const float* in;
+// ---- integer conv: fused quantise-on-load implicit GEMM (persistent, tcgen05) ----
+// K is channel-group-major: k = g * (taps * group) + tap * G_g + c; the weight
+// matrices must use the same order.
+struct FusedConvArgs {
+    const void* source;            // [channels][in_h][in_w], FP16 when source_half else FP32
+    int source_half;
+    const float* pixel_max;        // [in_h][in_w] from pixel_max()
     int channels, in_h, in_w, out_h, out_w;
     Window window;
-    int k_padded;            // row length of the limb matrices (multiple of 128)
-    int positions_padded;    // rows of the limb matrices (multiple of 128)
-    float* pixel_max;        // [in_h * in_w] scratch: max |x| over channels, +inf if non-finite
-    std::int8_t* high;       // [positions_padded][k_padded] first limb (the value for 8 bits)
-    std::int8_t* low;        // second limb l - 128 (16-bit activations), else unused
-    int* exponents;          // [positions] activation exponent, INT_MIN if non-finite
-    long long* column_terms; // [positions] exact correction for 2-limb weights, else unused
-    int activation_bits;     // 8 or 16
-    long long high_factor;   // correction: sum over k of (high_factor * h + low_factor * l')
-    long long low_factor;
-};
-cudaError_t quantize_activations(const QuantizeArgs& args, cudaStream_t stream);
-
-// ---- integer conv: tcgen05 GEMM with the profile's epilogue ----
-struct GemmEpilogue {
-    const float* scales;           // [n_padded] per physical weight row
-    const float* bias;             // [n_padded]
-    const long long* row_terms;    // [n_padded] exact correction for 2-limb activations
-    const int* exponents;          // [positions]
-    const long long* column_terms; // [positions] or null
-    int wsilu;                     // apply v * sigmoid(k v)
+    int k_real, k_blocks;          // K = channels * kernel_h * kernel_w, blocks of 128 bytes
+    int positions, p_tiles;        // out_h * out_w; p_tiles = tiles_y * tiles_x
+    int patch_h, patch_w;          // a tile is a patch_h x patch_w block of output pixels (product 128)
+    int tiles_y, tiles_x;
+    int group, groups;             // channels per halo load, halo loads per tile
+    int halo_rows, halo_box_w;     // halo box: group x halo_rows x halo_box_w elements
+    int halo_bytes;                // bytes per halo buffer (multiple of 1024)
+    int a_stages, b_stages;        // shared-memory ring depths for activations and weights
+    int n_tile, n_tiles;
+    long long column_high_factor, column_low_factor;  // column term (two-limb weights), else 0
+    const float* scales;           // [n_tiles * n_tile] per physical weight row
+    const float* bias;
+    const long long* row_terms;    // two-limb activations, else null
+    int wsilu;
     float wsilu_scale;
-    int chunk_add;                 // physical tile columns j and j + n_tile/2 are one pair
-    const float* residual;         // [out_channels][positions] added last, or null
-    void* out;                     // [out_channels][positions] FP32, or FP16 when out_half
+    int chunk_add;
+    const float* residual;         // [out_channels][positions] FP32, or null
+    void* out;                     // FP32, or FP16 when out_half
     int out_half;
-    int out_channels;              // logical output channels (after chunk-add)
-    int positions;
-    unsigned int* status;          // device word; bit 0: a bounded wait gave up
+    int out_channels;              // logical channels stored (after chunk-add)
+    int d2s_block;                 // 0: NCHW store; b: store through depth_to_space(b)
+    unsigned int* status;
 };
-struct GemmShape {
-    int weight_limbs, activation_limbs;
-    int n_tile;                  // output columns per CTA (multiple of 16, <= 256)
-    int n_tiles;                 // CTAs along N
-    int k_padded;                // multiple of 128
-    int positions_padded;        // multiple of 128
-};
-struct GemmMaps {
-    CUtensorMap a_high, a_low, b_high, b_low;  // unused limbs may be copies of the high maps
-};
-cudaError_t integer_gemm(const GemmMaps& maps, const GemmShape& shape, const GemmEpilogue& epilogue,
-                         cudaStream_t stream);
+// Per input pixel, max |x| over channels (+inf when any channel is non-finite).
+cudaError_t pixel_max(const void* in, int source_half, int channels, int pixels, float* out, cudaStream_t stream);
+cudaError_t fused_conv(const CUtensorMap& b_high, const CUtensorMap& b_low, const CUtensorMap& halo, int weight_limbs,
+                       int activation_limbs, const FusedConvArgs& args, cudaStream_t stream);
+// Dynamic shared memory the fused conv needs for these ring depths and halo buffers.
+int fused_conv_shared_bytes(int weight_limbs, int activation_limbs, int n_tile, int a_stages, int b_stages,
+                            int halo_bytes);
+constexpr int fused_conv_max_shared = 232448;
+// Encodes the 3-D halo map over a [channels][height][width] FP32 or FP16 tensor
+// (row bytes a multiple of 16, base 16-byte aligned) with a box of
+// box_w x box_h x box_c elements, no swizzle, zero fill outside the tensor.
+cudaError_t encode_halo_map(CUtensorMap* map, const void* base, int half, std::uint64_t channels,
+                            std::uint64_t height, std::uint64_t width, std::uint32_t box_w, std::uint32_t box_h,
+                            std::uint32_t box_c);
 
 // Encodes a 2D tensor map over an int8 [rows][row_bytes] matrix with 128x`box_rows`
-// boxes and 128-byte swizzle, the layout the GEMM's shared-memory descriptors expect.
+// boxes and 128-byte swizzle, the layout the MMA's shared-memory descriptors expect.
 cudaError_t encode_int8_map(CUtensorMap* map, const void* base, std::uint64_t rows, std::uint64_t row_bytes,
                             std::uint32_t box_rows);
 
