@@ -151,10 +151,38 @@ struct HaloShape {
     int box_w;
 };
 
+// Among box widths up to 64 elements wider than needed, the one whose rows put
+// a warp's 32 positions (one tap, one channel) on the fewest words per bank.
 HaloShape halo_shape(int patch_h, int patch_w, const kernels::Window& w, int align) {
     const int rows = (patch_h - 1) * w.stride_y + w.kernel_h;
     const int cols = (patch_w - 1) * w.stride_x + w.kernel_w;
-    return {rows, ((cols + align - 1 + align - 1) / align) * align};
+    const int minimum = ((cols + align - 1 + align - 1) / align) * align;
+    int best = minimum;
+    int best_conflicts = 33;
+    for (int box = minimum; box <= minimum + 64; box += align) {
+        int worst = 0;
+        for (int warp_start = 0; warp_start < 128; warp_start += 32) {
+            int count[32] = {};
+            int seen[32][32];
+            int distinct = 0;
+            for (int lane = 0; lane < 32; ++lane) {
+                const int position = warp_start + lane;
+                const int word = (position / patch_w) * w.stride_y * box + (position % patch_w) * w.stride_x;
+                const int bank = word % 32;
+                bool repeat = false;
+                for (int i = 0; i < count[bank]; ++i) repeat = repeat || seen[bank][i] == word;
+                if (!repeat) seen[bank][count[bank]++] = word;
+                distinct = std::max(distinct, count[bank]);
+            }
+            worst = std::max(worst, distinct);
+        }
+        if (worst < best_conflicts) {
+            best_conflicts = worst;
+            best = box;
+        }
+        if (best_conflicts == 1) break;
+    }
+    return {rows, best};
 }
 
 const char* op_name(Op op) {

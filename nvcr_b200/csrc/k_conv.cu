@@ -82,6 +82,53 @@ struct ConvLayout {
 };
 
 template <bool Half>
+__device__ __forceinline__ float load_halo(std::uint32_t address) {
+    if constexpr (Half) {
+        unsigned short bits;
+        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(bits) : "r"(address));
+        return __half2float(__ushort_as_half(bits));
+    } else {
+        float value;
+        asm volatile("ld.shared.f32 %0, [%1];" : "=f"(value) : "r"(address));
+        return value;
+    }
+}
+
+// Bytes 0 of a, b, c, d packed into one word, a lowest.
+__device__ __forceinline__ std::uint32_t pack_low_bytes(std::uint32_t a, std::uint32_t b, std::uint32_t c,
+                                                        std::uint32_t d) {
+    return __byte_perm(__byte_perm(a, b, 0x0040u), __byte_perm(c, d, 0x0040u), 0x5410u);
+}
+__device__ __forceinline__ std::uint32_t pack_low_bytes(int a, int b, int c, int d) {
+    return pack_low_bytes(static_cast<std::uint32_t>(a), static_cast<std::uint32_t>(b), static_cast<std::uint32_t>(c),
+                          static_cast<std::uint32_t>(d));
+}
+
+// Sixteen bytes assembled one at a time in two 64-bit registers.
+struct ByteRow {
+    unsigned long long lo{0}, hi{0};
+    __device__ __forceinline__ void put(int j, int value) {
+        const unsigned long long b = static_cast<unsigned long long>(static_cast<std::uint32_t>(value) & 255u);
+        if (j < 8) {
+            lo |= b << (8 * j);
+        } else {
+            hi |= b << (8 * (j - 8));
+        }
+    }
+    __device__ __forceinline__ void words(std::uint32_t (&w)[4]) const {
+        w[0] = static_cast<std::uint32_t>(lo);
+        w[1] = static_cast<std::uint32_t>(lo >> 32);
+        w[2] = static_cast<std::uint32_t>(hi);
+        w[3] = static_cast<std::uint32_t>(hi >> 32);
+    }
+};
+
+__device__ __forceinline__ void store_shared_v4(std::uint32_t address, const std::uint32_t (&w)[4]) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(address), "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3])
+                 : "memory");
+}
+
+template <bool Half>
 __device__ __forceinline__ float load_source(const void* base, std::size_t index) {
     if constexpr (Half) {
         return __half2float(__ldg(static_cast<const __half*>(base) + index));
@@ -353,19 +400,39 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
             const int base_x = px * a.window.stride_x + (x0 - x_start);
             int sum_high = 0;
             int sum_low = 0;
-            // Walk state: group, channels in it, tap, channel, element offset.
+            // Walk state: group, channels in it, tap, channel, element offset in the halo.
             int group = 0;
             int group_channels = a.group < a.channels ? a.group : a.channels;
             int tap = 0;
             int c = 0;
-            int tap_offset = base_y * a.halo_box_w + base_x;
-            int index = tap_offset;
-            const std::uint8_t* halo = nullptr;
+            int index = base_y * a.halo_box_w + base_x;
+            std::uint32_t halo = 0;  // shared address of the current halo buffer
             auto acquire_halo = [&]() -> bool {
                 const int h = static_cast<int>(job % halo_buffers);
                 if (!barrier_wait(smem_address(&tail->halo_full[h]), (job / halo_buffers) & 1u, a.status)) return false;
-                halo = halo_smem + h * a.halo_bytes;
+                halo = smem_address(halo_smem + h * a.halo_bytes);
                 return true;
+            };
+            // After the last channel of a tap: the next tap, or the next channel group.
+            auto next_tap = [&]() -> bool {
+                c = 0;
+                if (++tap == taps) {
+                    tap = 0;
+                    barrier_arrive(smem_address(&tail->halo_empty[job % halo_buffers]));
+                    ++job;
+                    if (++group < a.groups) {
+                        const int left = a.channels - group * a.group;
+                        group_channels = left < a.group ? left : a.group;
+                        if (!acquire_halo()) return false;
+                    }
+                }
+                const int ky = tap / kernel_w;
+                const int kx = tap - ky * kernel_w;
+                index = (base_y + ky) * a.halo_box_w + base_x + kx;
+                return true;
+            };
+            auto load = [&](int element) -> float {
+                return load_halo<SourceHalf>(halo + static_cast<std::uint32_t>(element) * (SourceHalf ? 2u : 4u));
             };
             if (*abort || !acquire_halo()) {
                 *abort = 1;
@@ -379,85 +446,115 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                     ok = false;
                     break;
                 }
-                std::uint8_t* a_hi = smem + s * L::a_stage_bytes + row * tile_k_bytes;
-                std::uint8_t* a_lo = a_hi + L::a_bytes;
+                const std::uint32_t a_hi = smem_address(smem + s * L::a_stage_bytes + row * tile_k_bytes);
+                const std::uint32_t a_lo = a_hi + L::a_bytes;
                 int k = kb * tile_k_bytes;
 #pragma unroll 1
                 for (int chunk = 0; chunk < tile_k_bytes / 16; ++chunk) {
-                    std::uint32_t high_words[4];
-                    std::uint32_t low_words[4];
+                    std::uint32_t high_words[4] = {0, 0, 0, 0};
+                    std::uint32_t low_words[4] = {0, 0, 0, 0};
+                    if (c + 16 <= group_channels && k + 16 <= a.k_real) {
+                        // Sixteen channels of one tap: independent loads, then the rounding.
+                        if (fast) {
+                            std::uint32_t rounded[16];
 #pragma unroll
-                    for (int word = 0; word < 4; ++word) {
-                        std::uint32_t hw = 0;
-                        std::uint32_t lw = 0;
+                            for (int j = 0; j < 16; ++j) rounded[j] = __float_as_uint(load(index + j * channel_stride));
 #pragma unroll
-                        for (int byte = 0; byte < 4; ++byte) {
-                            int q = 0;
-                            const bool real_tap = k < a.k_real;
-                            if (real_tap) {
-                                if (live) {
-                                    float x;
-                                    if constexpr (SourceHalf) {
-                                        x = __half2float(reinterpret_cast<const __half*>(halo)[index]);
-                                    } else {
-                                        x = reinterpret_cast<const float*>(halo)[index];
-                                    }
-                                    if (fast) {
-                                        float y = __fmaf_rn(x, scale, round_magic);
-                                        y = fminf(fmaxf(y, round_magic - limit), round_magic + limit);
-                                        q = __float_as_int(y) - round_magic_bits;
-                                    } else {
-                                        q = quantize_value<bits>(x, exponent);
-                                    }
-                                }
-                                // Next k: next channel of the tap; then next tap; then next group.
-                                index += channel_stride;
-                                if (++c == group_channels) {
-                                    c = 0;
-                                    if (++tap == taps) {
-                                        tap = 0;
-                                        barrier_arrive(smem_address(&tail->halo_empty[job % halo_buffers]));
-                                        ++job;
-                                        ++group;
-                                        if (group < a.groups) {
-                                            const int left = a.channels - group * a.group;
-                                            group_channels = left < a.group ? left : a.group;
-                                            if (!acquire_halo()) {
-                                                *abort = 1;
-                                                ok = false;
-                                            }
+                            for (int j = 0; j < 16; ++j) {
+                                float y = __fmaf_rn(__uint_as_float(rounded[j]), scale, round_magic);
+                                y = fminf(fmaxf(y, round_magic - limit), round_magic + limit);
+                                rounded[j] = __float_as_uint(y);
+                            }
+#pragma unroll
+                            for (int w = 0; w < 4; ++w) {
+                                const std::uint32_t* b = rounded + 4 * w;
+                                if constexpr (AL == 2) {
+                                    // q = bits - bits(magic); h = q >> 8; l' = (q & 255) - 128.
+                                    int h[4];
+#pragma unroll
+                                    for (int j = 0; j < 4; ++j) {
+                                        const int q = static_cast<int>(b[j]) - round_magic_bits;
+                                        h[j] = q >> 8;
+                                        if constexpr (WL == 2) {
+                                            sum_high += h[j];
+                                            sum_low += (q & 255) - 128;
                                         }
                                     }
-                                    const int ky = tap / kernel_w;
-                                    const int kx = tap - ky * kernel_w;
-                                    tap_offset = (base_y + ky) * a.halo_box_w + base_x + kx;
-                                    index = tap_offset;
+                                    high_words[w] = pack_low_bytes(h[0], h[1], h[2], h[3]);
+                                    low_words[w] = pack_low_bytes(b[0], b[1], b[2], b[3]) ^ 0x80808080u;
+                                } else {
+                                    // The low byte of bits(magic + q) is q in two's complement.
+                                    high_words[w] = pack_low_bytes(b[0], b[1], b[2], b[3]);
+                                    if constexpr (WL == 2) {
+#pragma unroll
+                                        for (int j = 0; j < 4; ++j) sum_high += static_cast<int>(b[j]) - round_magic_bits;
+                                    }
                                 }
                             }
-                            int h = q;
-                            int l = 0;
-                            if constexpr (AL == 2) {
-                                h = q >> 8;
-                                l = real_tap ? (q & 255) - 128 : 0;
-                                lw |= (static_cast<std::uint32_t>(l) & 255u) << (8 * byte);
+                        } else if (live) {
+                            ByteRow hb, lb;
+#pragma unroll 1
+                            for (int j = 0; j < 16; ++j) {
+                                const int q = quantize_value<bits>(load(index + j * channel_stride), exponent);
+                                const int h = AL == 2 ? (q >> 8) : q;
+                                const int l = AL == 2 ? (q & 255) - 128 : 0;
+                                hb.put(j, h);
+                                lb.put(j, l);
+                                if constexpr (WL == 2) {
+                                    sum_high += h;
+                                    sum_low += l;
+                                }
                             }
-                            hw |= (static_cast<std::uint32_t>(h) & 255u) << (8 * byte);
+                            hb.words(high_words);
+                            lb.words(low_words);
+                        } else if constexpr (AL == 2) {
+                            // q = 0 for every real tap of a non-finite position: l' = -128.
+                            low_words[0] = low_words[1] = low_words[2] = low_words[3] = 0x80808080u;
+                        }
+                        index += 16 * channel_stride;
+                        c += 16;
+                        k += 16;
+                        if (c == group_channels && !next_tap()) {
+                            *abort = 1;
+                            ok = false;
+                        }
+                    } else {
+                        // General walk, one k at a time (tap or group changes inside the chunk).
+                        ByteRow hb, lb;
+#pragma unroll 1
+                        for (int j = 0; j < 16; ++j, ++k) {
+                            if (k >= a.k_real) continue;
+                            int q = 0;
+                            if (live) {
+                                const float x = load(index);
+                                if (fast) {
+                                    float y = __fmaf_rn(x, scale, round_magic);
+                                    y = fminf(fmaxf(y, round_magic - limit), round_magic + limit);
+                                    q = __float_as_int(y) - round_magic_bits;
+                                } else {
+                                    q = quantize_value<bits>(x, exponent);
+                                }
+                            }
+                            const int h = AL == 2 ? (q >> 8) : q;
+                            const int l = AL == 2 ? (q & 255) - 128 : 0;
+                            hb.put(j, h);
+                            lb.put(j, l);
                             if constexpr (WL == 2) {
                                 sum_high += h;
                                 sum_low += l;
                             }
-                            ++k;
+                            index += channel_stride;
+                            if (++c == group_channels && !next_tap()) {
+                                *abort = 1;
+                                ok = false;
+                            }
                         }
-                        high_words[word] = hw;
-                        low_words[word] = lw;
+                        hb.words(high_words);
+                        lb.words(low_words);
                     }
-                    const int slot = (chunk ^ (row & 7)) * 16;
-                    *reinterpret_cast<uint4*>(a_hi + slot) =
-                        make_uint4(high_words[0], high_words[1], high_words[2], high_words[3]);
-                    if constexpr (AL == 2) {
-                        *reinterpret_cast<uint4*>(a_lo + slot) =
-                            make_uint4(low_words[0], low_words[1], low_words[2], low_words[3]);
-                    }
+                    const std::uint32_t slot = static_cast<std::uint32_t>((chunk ^ (row & 7)) * 16);
+                    store_shared_v4(a_hi + slot, high_words);
+                    if constexpr (AL == 2) store_shared_v4(a_lo + slot, low_words);
                 }
                 fence_proxy_async_shared();
                 barrier_arrive(smem_address(&tail->full_a[s]));
@@ -514,16 +611,31 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
             const int logical0 = a.chunk_add ? n_index * (n_tile / 2) : physical0;
             const std::uint32_t acc = tmem + static_cast<std::uint32_t>(buffer) * buffer_columns + lane_base;
 
-            auto value_at = [&](int column_index, int hh, int md, int lo) -> float {
-                const int physical = physical0 + column_index;
-                const float scale = __ldg(a.scales + physical);
-                const float bias = __ldg(a.bias + physical);
+            // Per-channel parameters of one 16-column chunk, one coalesced load per
+            // warp: lane l < 16 holds column j0 + l, lane 16 + l its chunk-add
+            // partner j0 + pair_offset + l. Shuffled to every lane when used, and
+            // fetched one chunk ahead.
+            auto fetch = [&](int j0, float& scale, float& bias, long long& terms) {
+                const int column = j0 + (lane < 16 ? lane : pair_offset + lane - 16);
+                const int physical = physical0 + (column < n_tile ? column : 0);
+                scale = __ldg(a.scales + physical);
+                bias = __ldg(a.bias + physical);
+                terms = AL == 2 ? __ldg(a.row_terms + physical) : 0;
+            };
+            float next_scale, next_bias;
+            long long next_terms;
+            fetch(0, next_scale, next_bias, next_terms);
+
+            auto value_at = [&](int source_lane, int hh, int md, int lo, float scales, float biases,
+                                long long terms) -> float {
+                const float scale = __shfl_sync(0xffffffffu, scales, source_lane);
+                const float bias = __shfl_sync(0xffffffffu, biases, source_lane);
+                const long long row_term = AL == 2 ? __shfl_sync(0xffffffffu, terms, source_lane) : 0;
                 float v;
                 if constexpr (WL == 1 && AL == 1) {
                     v = integer_output32(hh, scale, exponent, bias);
                 } else {
-                    long long sum = high_factor * hh + column + mid_factor * md;
-                    if constexpr (AL == 2) sum += __ldg(a.row_terms + physical);
+                    long long sum = high_factor * hh + column + mid_factor * md + row_term;
                     if constexpr (WL == 2 && AL == 2) sum += lo;
                     v = integer_output(sum, scale, exponent, bias);
                 }
@@ -532,6 +644,10 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
             };
 
             for (int j0 = 0; j0 < columns; j0 += 16) {
+                const float scales = next_scale;
+                const float biases = next_bias;
+                const long long terms = next_terms;
+                if (j0 + 16 < columns) fetch(j0 + 16, next_scale, next_bias, next_terms);
                 int hh[16], md[16], lo[16], hh2[16], md2[16], lo2[16];
                 tmem_load16(acc + static_cast<std::uint32_t>(j0), hh);
                 if constexpr (L::accumulators > 1) tmem_load16(acc + static_cast<std::uint32_t>(n_tile + j0), md);
@@ -545,27 +661,41 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                     }
                 }
                 tmem_load_wait();
-                if (real) {
+                // Shuffles need the whole warp, so values are computed for every lane.
+                float v[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    v[j] = value_at(j, hh[j], L::accumulators > 1 ? md[j] : 0, L::accumulators > 2 ? lo[j] : 0,
+                                    scales, biases, terms);
+                }
+                if (a.chunk_add) {
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
-                        const int c = logical0 + j0 + j;
-                        if (c >= a.out_channels) break;
-                        float v;
-                        if (exponent == INT_MIN) {
-                            v = canonical_nan();
-                        } else {
-                            v = value_at(j0 + j, hh[j], L::accumulators > 1 ? md[j] : 0,
-                                         L::accumulators > 2 ? lo[j] : 0);
-                            if (a.chunk_add) {
-                                const float w = value_at(j0 + pair_offset + j, hh2[j],
-                                                         L::accumulators > 1 ? md2[j] : 0,
-                                                         L::accumulators > 2 ? lo2[j] : 0);
-                                v = __fadd_rn(v, w);
-                            }
+                        const float w = value_at(16 + j, hh2[j], L::accumulators > 1 ? md2[j] : 0,
+                                                 L::accumulators > 2 ? lo2[j] : 0, scales, biases, terms);
+                        v[j] = __fadd_rn(v[j], w);
+                    }
+                }
+                const int c0 = logical0 + j0;
+                const int count = a.out_channels - c0 < 16 ? a.out_channels - c0 : 16;
+                if (real) {
+                    if (exponent == INT_MIN) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) v[j] = canonical_nan();
+                    }
+                    if (a.residual != nullptr) {
+                        float r[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            r[j] = j < count ? __ldg(a.residual + static_cast<std::size_t>(c0 + j) * a.positions + p) : 0.0f;
                         }
-                        if (a.residual != nullptr) {
-                            v = __fadd_rn(v, __ldg(a.residual + static_cast<std::size_t>(c) * a.positions + p));
-                        }
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], r[j]);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        if (j >= count) break;
+                        const int c = c0 + j;
                         std::size_t index;
                         if (b > 0) {
                             const int bb = b * b;
@@ -578,9 +708,9 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                             index = static_cast<std::size_t>(c) * a.positions + p;
                         }
                         if (a.out_half) {
-                            reinterpret_cast<__half*>(a.out)[index] = __float2half_rn(v);
+                            reinterpret_cast<__half*>(a.out)[index] = __float2half_rn(v[j]);
                         } else {
-                            reinterpret_cast<float*>(a.out)[index] = v;
+                            reinterpret_cast<float*>(a.out)[index] = v[j];
                         }
                     }
                 }

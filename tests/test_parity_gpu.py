@@ -210,3 +210,21 @@ def test_one_executor_many_extents(cuda, oracle):
             got = executor.run([x])
             expected = oracle.run(program, [x])
             assert all(count_differing(g, e) == 0 for g, e in zip(got, expected))
+
+
+@pytest.mark.parametrize("bits", WIDTHS, ids=lambda b: f"w{b[0]}a{b[1]}")
+def test_many_tiles_per_cta(cuda, oracle, bits):
+    """More tiles than SMs, so each persistent CTA walks several tiles and every
+    ring (halo, A, B, TMEM, per-tile info) wraps around many times."""
+    stream = SeededStream(90)
+    program = conv_program(stream, 64, 64, (3, 3), (1, 1), (1, 1, 1, 1), bits)
+    x = stream.tensor(64, 160, 200, 2.0)
+    assert_parity(program, [x], oracle, f"many tiles w{bits[0]}a{bits[1]}")
+
+
+def test_many_tiles_with_fusions_and_groups(cuda, oracle):
+    """Several channel groups per tile (C = 256), chunk-add and residual, many tiles."""
+    stream = SeededStream(91)
+    program = conv_program(stream, 256, 128, (3, 3), (1, 1), (1, 1, 1, 1), (16, 16), chunk_add=True, residual=True)
+    x = stream.tensor(256, 48, 200, 2.0)
+    assert_parity(program, [x], oracle, "many tiles, groups, fusions")
