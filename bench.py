@@ -326,7 +326,7 @@ def main():
     tensor_ops = tensor_ms = all_ops = all_ms = 0.0
     for layer, segments in zip(layers, per_layer_segments):
         gemms = [seg for seg in segments if seg["kernel"] == "integer_conv"]
-        quants = [seg for seg in segments if seg["kernel"] == "pixel_max"]
+        quants = [seg for seg in segments if seg["kernel"] == "stage_source"]
         if not gemms:
             continue
         ms = sum(seg["ms"] for seg in gemms) / len(gemms)
@@ -335,7 +335,7 @@ def main():
         bound = "tensor" if ops / bytes_ > ridge else "hbm"
         tops = ops / (ms / 1000.0) / 1e12
         gbs = bytes_ / (ms / 1000.0) / 1e9
-        layer_rows.append({"layer": layer.name, "conv_ms": round(ms, 4), "pixel_max_ms": round(q_ms, 4),
+        layer_rows.append({"layer": layer.name, "conv_ms": round(ms, 4), "stage_ms": round(q_ms, 4),
                            "conv_tops": round(tops, 1), "conv_gbs": round(gbs, 1), "bound": bound,
                            "frac": round(tops / int8_peak if bound == "tensor" else gbs / hbm, 3)})
         all_ops += ops * len(gemms)

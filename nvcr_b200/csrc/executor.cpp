@@ -12,23 +12,29 @@ namespace nvcr_sm100 {
 
 struct Executor::IntegerConv {
     int weight_limbs{1}, activation_limbs{1}, activation_bits{8};
-    int k_real{0}, k_padded{0};
+    int channels{0}, c_pad{0};   // source channels, and padded to a multiple of 16
+    int k_real{0}, k_padded{0};  // K = taps * c_pad, and rounded up to 128-byte blocks
     int n_tile{0}, n_tiles{0};
     int out_channels{0};  // logical output channels of the step (halved by chunk-add)
     bool chunk_add{false};
-    std::int8_t* b_high{nullptr};
-    std::int8_t* b_low{nullptr};
     float* scales{nullptr};
     float* bias{nullptr};
     long long* row_terms{nullptr};
     void* allocation{nullptr};
-    CUtensorMap b_high_map{};
-    CUtensorMap b_low_map{};
     long long column_high_factor{0}, column_low_factor{0};
-    // Fused kernel geometry fixed at create time: channels per halo load and
-    // shared-memory ring depths, and the bytes one halo buffer may take.
+    // K order and weight matrices per source type ([0] FP32, [1] FP16): the
+    // channels per halo load make 128-byte records where the padding allows.
+    struct Layout {
+        int group{0}, groups{0};
+        std::int8_t* b_high{nullptr};
+        std::int8_t* b_low{nullptr};
+        CUtensorMap b_high_map{};
+        CUtensorMap b_low_map{};
+    };
+    Layout layouts[2];
+    // Shared-memory ring depths fixed at create time, and the bytes one halo
+    // buffer may take.
     int taps{1};
-    int group{1}, groups{1};
     int a_stages{2}, b_stages{4};
     int halo_budget{0};
 };
@@ -49,20 +55,22 @@ struct Executor::Step {
     float wsilu_scale{0.0f};
     bool chunk_add{false};
     std::optional<std::size_t> residual;
+    int d2s_block{0};  // the output goes through depth_to_space(d2s_block)
 };
 
 struct PlannedConv {
+    bool source_half{false};       // the conv reads an FP16 program input directly
+    std::size_t staged{0};         // arena offset of the channel-innermost copy of the source
     std::size_t pixel_max{0};      // arena offset of the per-input-pixel maxima
-    std::size_t padded{0};         // arena offset of a row-padded copy of the source, or npos
-    int padded_width{0};
     int positions{0};
     int patch_h{0}, patch_w{0}, tiles_y{0}, tiles_x{0};
     int halo_rows{0}, halo_box_w{0}, halo_bytes{0};
     CUtensorMap halo_map{};
-    const void* halo_base{nullptr};  // source address halo_map was encoded for
+    const void* halo_base{nullptr};  // staged address halo_map was encoded for
 };
 
 struct Executor::Plan {
+    Boundary boundary{Boundary::host};
     std::vector<Extent> extents;
     std::vector<std::size_t> offsets;  // per tensor id, npos when not materialised
     std::vector<PlannedConv> convs;    // per step
@@ -146,45 +154,6 @@ const TensorView* find_view(const std::vector<TensorView>& views, const std::str
 
 // Halo of a patch of output pixels: input rows and the TMA box width in
 // elements (a multiple of `align`, wide enough for a start rounded down to it).
-struct HaloShape {
-    int rows;
-    int box_w;
-};
-
-// Among box widths up to 64 elements wider than needed, the one whose rows put
-// a warp's 32 positions (one tap, one channel) on the fewest words per bank.
-HaloShape halo_shape(int patch_h, int patch_w, const kernels::Window& w, int align) {
-    const int rows = (patch_h - 1) * w.stride_y + w.kernel_h;
-    const int cols = (patch_w - 1) * w.stride_x + w.kernel_w;
-    const int minimum = ((cols + align - 1 + align - 1) / align) * align;
-    int best = minimum;
-    int best_conflicts = 33;
-    for (int box = minimum; box <= minimum + 64; box += align) {
-        int worst = 0;
-        for (int warp_start = 0; warp_start < 128; warp_start += 32) {
-            int count[32] = {};
-            int seen[32][32];
-            int distinct = 0;
-            for (int lane = 0; lane < 32; ++lane) {
-                const int position = warp_start + lane;
-                const int word = (position / patch_w) * w.stride_y * box + (position % patch_w) * w.stride_x;
-                const int bank = word % 32;
-                bool repeat = false;
-                for (int i = 0; i < count[bank]; ++i) repeat = repeat || seen[bank][i] == word;
-                if (!repeat) seen[bank][count[bank]++] = word;
-                distinct = std::max(distinct, count[bank]);
-            }
-            worst = std::max(worst, distinct);
-        }
-        if (worst < best_conflicts) {
-            best_conflicts = worst;
-            best = box;
-        }
-        if (best_conflicts == 1) break;
-    }
-    return {rows, best};
-}
-
 const char* op_name(Op op) {
     switch (op) {
     case Op::conv: return "conv";
@@ -260,6 +229,35 @@ Status Executor::prepare() {
         if (steps_[index].kind != StepKind::integer_conv) continue;
         auto prepared = prepare_integer_conv(index);
         if (!prepared) return prepared;
+    }
+    // Which program inputs and outputs device runs may leave in the caller's buffers.
+    const std::size_t tensor_count = program_.tensor_names.size();
+    std::vector<std::vector<std::size_t>> readers(tensor_count);
+    for (std::size_t s = 0; s < steps_.size(); ++s) {
+        for (const auto id : steps_[s].reads) readers[id].push_back(s);
+    }
+    std::vector<int> output_uses(tensor_count, 0);
+    for (const auto id : program_.outputs) ++output_uses[id];
+    input_conv_only_.assign(program_.inputs.size(), false);
+    for (std::size_t slot = 0; slot < program_.inputs.size(); ++slot) {
+        const auto id = program_.inputs[slot];
+        bool only = output_uses[id] == 0;
+        for (const auto s : readers[id]) {
+            const Step& step = steps_[s];
+            only = only && step.kind == StepKind::integer_conv && step.source == id &&
+                !(step.residual && *step.residual == id);
+        }
+        input_conv_only_[slot] = only;
+    }
+    output_step_.assign(program_.outputs.size(), -1);
+    for (std::size_t slot = 0; slot < program_.outputs.size(); ++slot) {
+        const auto id = program_.outputs[slot];
+        if (output_uses[id] != 1 || !readers[id].empty()) continue;
+        for (std::size_t s = 0; s < steps_.size(); ++s) {
+            if (steps_[s].kind == StepKind::integer_conv && steps_[s].output == id) {
+                output_step_[slot] = static_cast<std::ptrdiff_t>(s);
+            }
+        }
     }
     return Ok{};
 }
@@ -356,6 +354,12 @@ void Executor::plan_fusions() {
                     last += 1;
                 }
             }
+            if (last + 1 < nodes.size() && nodes[last + 1].op == Op::depth_to_space &&
+                nodes[last + 1].inputs[0] == out && nodes[last + 1].block >= 1 && private_tensor(out, 1)) {
+                step.d2s_block = nodes[last + 1].block;
+                out = nodes[last + 1].output;
+                last += 1;
+            }
             for (std::size_t folded = i + 1; folded <= last; ++folded) absorbed[folded] = true;
             step.output = out;
             step.reads.push_back(step.source);
@@ -386,13 +390,16 @@ Status Executor::prepare_integer_conv(std::size_t step_index) {
     conv.weight_limbs = node.weight_bits == 16 ? 2 : 1;
     conv.activation_limbs = node.activation_bits == 16 ? 2 : 1;
     conv.activation_bits = node.activation_bits;
-    conv.k_real = node.in_channels;
+    const int taps = step.window.kernel_h * step.window.kernel_w;
+    if (taps <= 0 || node.in_channels % taps != 0) return fail(Code::internal_error, "integer conv window mismatch");
+    conv.taps = taps;
+    conv.channels = node.in_channels / taps;
+    conv.c_pad = round_up(conv.channels, 16);
+    conv.k_real = taps * conv.c_pad;
     if (conv.k_real > 65536) {
         return fail(Code::invalid_argument, "integer conv reduction length above 65536 is not supported");
     }
     conv.k_padded = round_up(conv.k_real, 128);
-    const int taps = step.window.kernel_h * step.window.kernel_w;
-    if (taps <= 0 || conv.k_real % taps != 0) return fail(Code::internal_error, "integer conv window mismatch");
     conv.chunk_add = step.chunk_add;
     const int rows = node.out_channels;
     const int accumulators = 1 + ((conv.weight_limbs == 2 || conv.activation_limbs == 2) ? 1 : 0) +
@@ -409,34 +416,49 @@ Status Executor::prepare_integer_conv(std::size_t step_index) {
         conv.out_channels = rows;
     }
     const int n_padded = conv.n_tiles * conv.n_tile;
-    conv.taps = taps;
-    const int source_channels = conv.k_real / taps;
-    // Shared memory: two A stages (filled by the producers), four B stages
-    // (TMA), and two halo buffers sized from what is left.
-    for (conv.b_stages = 4; conv.b_stages >= 2; --conv.b_stages) {
-        const int fixed = kernels::fused_conv_shared_bytes(conv.weight_limbs, conv.activation_limbs, conv.n_tile,
-                                                           conv.a_stages, conv.b_stages, 0);
-        conv.halo_budget = ((kernels::fused_conv_max_shared - fixed) / 2) / 1024 * 1024;
-        if (conv.halo_budget >= 16 * 1024) break;
+    // Channels per halo load: 128-byte records (64 FP16 or 32 FP32 channels)
+    // when they divide the padded channels, else the largest power of two that does.
+    for (int half = 0; half < 2; ++half) {
+        int group = half ? 64 : 32;
+        while (conv.c_pad % group != 0) group /= 2;
+        conv.layouts[half].group = group;
     }
-    {
-        const HaloShape reference = halo_shape(4, 32, step.window, 4);
-        const int per_channel = reference.rows * reference.box_w * static_cast<int>(sizeof(float));
-        int group = std::min({source_channels, 256, conv.halo_budget / per_channel});
-        if (group < source_channels && group >= 16) group = group / 16 * 16;
-        if (group < 1) return fail(Code::invalid_argument, "integer conv window is too large for the halo");
-        conv.group = group;
-        conv.groups = (source_channels + group - 1) / group;
-    }
-    // Node order k = c * taps + tap (weights [O][C][kh][kw]); kernel order is
-    // channel-group-major: g * (taps * group) + tap * G_g + (c - g * group).
-    auto kernel_k = [&](int k) {
-        const int c = k / taps;
-        const int tap = k - c * taps;
-        const int g = c / conv.group;
-        const int in_group = std::min(conv.group, source_channels - g * conv.group);
-        return g * taps * conv.group + tap * in_group + (c - g * conv.group);
+    // Smallest halo buffer over the patch shapes for a channel group.
+    auto smallest_halo = [&](int group, int element) {
+        int best = INT_MAX;
+        for (const int patch_w : {32, 16, 64, 8, 128}) {
+            const int patch_h = 128 / patch_w;
+            const int halo_rows = (patch_h - 1) * step.window.stride_y + step.window.kernel_h;
+            const int halo_box_w = (patch_w - 1) * step.window.stride_x + step.window.kernel_w;
+            if (halo_box_w > 256 || halo_rows > 256) continue;
+            best = std::min(best, round_up(halo_rows * halo_box_w * group * element, 1024));
+        }
+        return best;
     };
+    // Shared memory: two A stages (filled by the producers), two to four B
+    // stages (TMA), the per-column parameters, and two halo buffers from what
+    // is left; the deepest B ring whose leftover holds a halo of both source
+    // types, with smaller channel groups when none does.
+    for (;;) {
+        const int need = std::max(smallest_halo(conv.layouts[0].group, 4), smallest_halo(conv.layouts[1].group, 2));
+        bool fits = false;
+        for (conv.b_stages = 4; conv.b_stages >= 2; --conv.b_stages) {
+            const int fixed = kernels::fused_conv_shared_bytes(conv.weight_limbs, conv.activation_limbs, conv.n_tile,
+                                                               conv.n_tiles, conv.a_stages, conv.b_stages, 0);
+            conv.halo_budget = ((kernels::fused_conv_max_shared - fixed) / 2) / 1024 * 1024;
+            if (conv.halo_budget >= need) {
+                fits = true;
+                break;
+            }
+        }
+        if (fits) break;
+        auto& wider = conv.layouts[0].group * 4 >= conv.layouts[1].group * 2 ? conv.layouts[0] : conv.layouts[1];
+        if (wider.group <= 16) {
+            return fail(Code::invalid_argument, "integer conv window or output channels too large for shared memory");
+        }
+        wider.group /= 2;
+    }
+    for (auto& layout : conv.layouts) layout.groups = conv.c_pad / layout.group;
     // Physical weight row -> node row (-1: zero padding). A chunk-add conv puts
     // pair (c, c + C/2) in columns j and j + n_tile/2 of one tile.
     auto source_row = [&](int physical) -> int {
@@ -450,14 +472,23 @@ Status Executor::prepare_integer_conv(std::size_t step_index) {
     };
 
     const auto quantized = quantize_weights(program_, node);
-    const std::size_t matrix = static_cast<std::size_t>(n_padded) * conv.k_padded;
-    std::vector<std::int8_t> high(matrix, 0);
-    std::vector<std::int8_t> low(conv.weight_limbs == 2 ? matrix : 0, 0);
+    // q of (row, channel c, tap) in the node's order k = c * taps + tap; the
+    // padded channels hold q = 0.
+    auto weight_q = [&](int row, int c, int tap) -> int {
+        if (c >= conv.channels) return 0;
+        return quantized.values[static_cast<std::size_t>(row) * node.in_channels + static_cast<std::size_t>(c) * taps +
+                                tap];
+    };
+    // Limbs of q: (q >> 8, (q & 255) - 128) for 16-bit weights, q for 8-bit.
+    const bool two = conv.weight_limbs == 2;
+    auto high_limb = [&](int q) { return two ? q >> 8 : q; };  // arithmetic shift: floor(q / 256)
+    auto low_limb = [&](int q) { return two ? (q & 255) - 128 : 0; };
+
     std::vector<float> scales(n_padded, 0.0f);
     std::vector<float> bias(n_padded, 0.0f);
     std::vector<long long> row_terms(n_padded, 0);
-    const long long aw = conv.weight_limbs == 2 ? 256 : 1;
-    const long long cw = conv.weight_limbs == 2 ? 128 : 0;
+    const long long aw = two ? 256 : 1;
+    const long long cw = two ? 128 : 0;
     const long long cx = conv.activation_limbs == 2 ? 128 : 0;
     for (int physical = 0; physical < n_padded; ++physical) {
         const int row = source_row(physical);
@@ -466,22 +497,14 @@ Status Executor::prepare_integer_conv(std::size_t step_index) {
         bias[physical] = program_.weights[node.bias_offset + static_cast<std::size_t>(row)];
         long long high_sum = 0;
         long long low_sum = 0;
-        for (int k = 0; k < conv.k_real; ++k) {
-            const int q = quantized.values[static_cast<std::size_t>(row) * conv.k_real + k];
-            const std::size_t at = static_cast<std::size_t>(physical) * conv.k_padded + kernel_k(k);
-            if (conv.weight_limbs == 2) {
-                const int h = q >> 8;  // arithmetic shift: floor(q / 256)
-                const int l = (q & 255) - 128;
-                high[at] = static_cast<std::int8_t>(h);
-                low[at] = static_cast<std::int8_t>(l);
-                high_sum += h;
-                low_sum += l;
-            } else {
-                high[at] = static_cast<std::int8_t>(q);
-                high_sum += q;
+        for (int c = 0; c < conv.c_pad; ++c) {
+            for (int tap = 0; tap < taps; ++tap) {
+                const int q = weight_q(row, c, tap);
+                high_sum += high_limb(q);
+                low_sum += low_limb(q);
             }
         }
-        // cx (aw sum Wh + sum Wl') + K cw cx
+        // cx (aw sum Wh + sum Wl') + K cw cx, over all K = taps * c_pad entries.
         row_terms[physical] = cx * (aw * high_sum + low_sum) + static_cast<long long>(conv.k_real) * cw * cx;
     }
     // column term factors: cw (ax sum Xh + sum Xl')
@@ -489,18 +512,48 @@ Status Executor::prepare_integer_conv(std::size_t step_index) {
     conv.column_high_factor = cw * ax;
     conv.column_low_factor = conv.activation_limbs == 2 ? cw : 0;
 
-    // One allocation: [high][low][scales][bias][row_terms], each 1024-aligned.
-    const std::size_t high_at = 0;
-    const std::size_t low_at = align_up(high_at + matrix, alignment);
-    const std::size_t scales_at = align_up(low_at + low.size(), alignment);
+    // Weight matrices [n_padded][k_padded] in a layout's K order:
+    // k = g * (taps * group) + tap * group + (c - g * group); zero bytes past K.
+    const std::size_t matrix = static_cast<std::size_t>(n_padded) * conv.k_padded;
+    auto build = [&](int group, std::vector<std::int8_t>& high, std::vector<std::int8_t>& low) {
+        high.assign(matrix, 0);
+        low.assign(two ? matrix : 0, 0);
+        for (int physical = 0; physical < n_padded; ++physical) {
+            const int row = source_row(physical);
+            if (row < 0) continue;
+            for (int c = 0; c < conv.c_pad; ++c) {
+                const int g = c / group;
+                for (int tap = 0; tap < taps; ++tap) {
+                    const int q = weight_q(row, c, tap);
+                    const std::size_t at = static_cast<std::size_t>(physical) * conv.k_padded +
+                        static_cast<std::size_t>(g) * taps * group + static_cast<std::size_t>(tap) * group +
+                        (c - g * group);
+                    high[at] = static_cast<std::int8_t>(high_limb(q));
+                    if (two) low[at] = static_cast<std::int8_t>(low_limb(q));
+                }
+            }
+        }
+    };
+    const bool shared_layout = conv.layouts[0].group == conv.layouts[1].group;
+    std::vector<std::int8_t> high[2], low[2];
+    build(conv.layouts[0].group, high[0], low[0]);
+    if (!shared_layout) build(conv.layouts[1].group, high[1], low[1]);
+
+    // One allocation: [scales][bias][row_terms][high 0][low 0][high 1][low 1], each 1024-aligned.
+    const std::size_t scales_at = 0;
     const std::size_t bias_at = align_up(scales_at + n_padded * sizeof(float), alignment);
     const std::size_t terms_at = align_up(bias_at + n_padded * sizeof(float), alignment);
-    const std::size_t total = align_up(terms_at + n_padded * sizeof(long long), alignment);
+    std::size_t matrices_at[2][2] = {{0, 0}, {0, 0}};
+    std::size_t total = align_up(terms_at + n_padded * sizeof(long long), alignment);
+    for (int layout = 0; layout < (shared_layout ? 1 : 2); ++layout) {
+        for (int limb = 0; limb < conv.weight_limbs; ++limb) {
+            matrices_at[layout][limb] = total;
+            total = align_up(total + matrix, alignment);
+        }
+    }
     cudaError_t status = cudaMalloc(&conv.allocation, total);
     if (status != cudaSuccess) return cuda_error("cudaMalloc integer weights", status);
     auto* base = static_cast<std::uint8_t*>(conv.allocation);
-    conv.b_high = reinterpret_cast<std::int8_t*>(base + high_at);
-    conv.b_low = conv.weight_limbs == 2 ? reinterpret_cast<std::int8_t*>(base + low_at) : conv.b_high;
     conv.scales = reinterpret_cast<float*>(base + scales_at);
     conv.bias = reinterpret_cast<float*>(base + bias_at);
     conv.row_terms = reinterpret_cast<long long*>(base + terms_at);
@@ -509,11 +562,19 @@ Status Executor::prepare_integer_conv(std::size_t step_index) {
         const void* from;
         std::size_t bytes;
     };
-    const Upload uploads[] = {{conv.b_high, high.data(), high.size()},
-                              {base + low_at, low.data(), low.size()},
-                              {conv.scales, scales.data(), scales.size() * sizeof(float)},
-                              {conv.bias, bias.data(), bias.size() * sizeof(float)},
-                              {conv.row_terms, row_terms.data(), row_terms.size() * sizeof(long long)}};
+    std::vector<Upload> uploads = {{conv.scales, scales.data(), scales.size() * sizeof(float)},
+                                   {conv.bias, bias.data(), bias.size() * sizeof(float)},
+                                   {conv.row_terms, row_terms.data(), row_terms.size() * sizeof(long long)}};
+    for (int layout = 0; layout < 2; ++layout) {
+        const int from = shared_layout ? 0 : layout;
+        auto& target = conv.layouts[layout];
+        target.b_high = reinterpret_cast<std::int8_t*>(base + matrices_at[from][0]);
+        target.b_low = two ? reinterpret_cast<std::int8_t*>(base + matrices_at[from][1]) : target.b_high;
+        if (from == layout) {
+            uploads.push_back({target.b_high, high[from].data(), matrix});
+            if (two) uploads.push_back({target.b_low, low[from].data(), matrix});
+        }
+    }
     for (const auto& upload : uploads) {
         if (upload.bytes == 0) continue;
         status = cudaMemcpy(upload.to, upload.from, upload.bytes, cudaMemcpyHostToDevice);
@@ -522,13 +583,15 @@ Status Executor::prepare_integer_conv(std::size_t step_index) {
             return cuda_error("cudaMemcpy integer weights", status);
         }
     }
-    status = kernels::encode_int8_map(&conv.b_high_map, conv.b_high, n_padded, conv.k_padded, conv.n_tile);
-    if (status == cudaSuccess) {
-        status = kernels::encode_int8_map(&conv.b_low_map, conv.b_low, n_padded, conv.k_padded, conv.n_tile);
-    }
-    if (status != cudaSuccess) {
-        cudaFree(conv.allocation);
-        return cuda_error("cuTensorMapEncodeTiled weights", status);
+    for (auto& layout : conv.layouts) {
+        status = kernels::encode_int8_map(&layout.b_high_map, layout.b_high, n_padded, conv.k_padded, conv.n_tile);
+        if (status == cudaSuccess) {
+            status = kernels::encode_int8_map(&layout.b_low_map, layout.b_low, n_padded, conv.k_padded, conv.n_tile);
+        }
+        if (status != cudaSuccess) {
+            cudaFree(conv.allocation);
+            return cuda_error("cuTensorMapEncodeTiled weights", status);
+        }
     }
     step.conv = static_cast<int>(convs_.size());
     convs_.push_back(conv);
@@ -537,8 +600,8 @@ Status Executor::prepare_integer_conv(std::size_t step_index) {
 
 // ---------------------------------------------------------------- planning
 
-Result<Executor::Plan*> Executor::plan_for(const std::vector<Extent>& input_extents) {
-    std::vector<std::int32_t> key;
+Result<Executor::Plan*> Executor::plan_for(const std::vector<Extent>& input_extents, Boundary boundary) {
+    std::vector<std::int32_t> key{static_cast<std::int32_t>(boundary)};
     for (const auto& e : input_extents) {
         key.push_back(e.channels);
         key.push_back(e.height);
@@ -547,6 +610,7 @@ Result<Executor::Plan*> Executor::plan_for(const std::vector<Extent>& input_exte
     if (auto found = plans_.find(key); found != plans_.end()) return found->second.get();
 
     auto plan = std::make_unique<Plan>();
+    plan->boundary = boundary;
     const std::size_t tensor_count = program_.tensor_names.size();
     plan->extents.assign(tensor_count, Extent{});
     plan->offsets.assign(tensor_count, npos);
@@ -595,6 +659,11 @@ Result<Executor::Plan*> Executor::plan_for(const std::vector<Extent>& input_exte
             const Extent out = plan->extents[node.output];
             PlannedConv& pc = plan->convs[s];
             pc.positions = out.height * out.width;
+            const bool program_input = std::find(program_.inputs.begin(), program_.inputs.end(), step.source) !=
+                program_.inputs.end();
+            pc.source_half = boundary == Boundary::half && program_input;
+            const int element = pc.source_half ? 2 : 4;
+            const int record_bytes = conv.layouts[pc.source_half ? 1 : 0].group * element;
             // Patch shape: least padding waste, then the smallest halo that fits.
             int best_waste = INT_MAX;
             int best_bytes = INT_MAX;
@@ -602,9 +671,10 @@ Result<Executor::Plan*> Executor::plan_for(const std::vector<Extent>& input_exte
                 const int patch_h = 128 / patch_w;
                 const int tiles_y = (out.height + patch_h - 1) / patch_h;
                 const int tiles_x = (out.width + patch_w - 1) / patch_w;
-                const HaloShape halo = halo_shape(patch_h, patch_w, step.window, 4);
-                const int bytes = round_up(conv.group * halo.rows * halo.box_w * static_cast<int>(sizeof(float)), 1024);
-                if (bytes > conv.halo_budget || halo.box_w > 256 || halo.rows > 256) continue;
+                const int halo_rows = (patch_h - 1) * step.window.stride_y + step.window.kernel_h;
+                const int halo_box_w = (patch_w - 1) * step.window.stride_x + step.window.kernel_w;
+                const int bytes = round_up(halo_rows * halo_box_w * record_bytes, 1024);
+                if (bytes > conv.halo_budget || halo_box_w > 256 || halo_rows > 256) continue;
                 const long long covered = static_cast<long long>(tiles_y) * tiles_x * 128;
                 const int waste = static_cast<int>((covered - pc.positions) * 1000 / std::max(pc.positions, 1));
                 if (waste < best_waste - 30 || (waste <= best_waste + 30 && bytes < best_bytes)) {
@@ -614,23 +684,16 @@ Result<Executor::Plan*> Executor::plan_for(const std::vector<Extent>& input_exte
                     pc.patch_w = patch_w;
                     pc.tiles_y = tiles_y;
                     pc.tiles_x = tiles_x;
-                    pc.halo_rows = halo.rows;
-                    pc.halo_box_w = halo.box_w;
+                    pc.halo_rows = halo_rows;
+                    pc.halo_box_w = halo_box_w;
                     pc.halo_bytes = bytes;
                 }
             }
             if (pc.patch_w == 0) return fail(Code::invalid_argument, "integer conv window is too large for the halo");
-            // The halo TMA needs 16-byte rows: pad the source rows when they are not.
-            pc.padded = npos;
-            pc.padded_width = source.width;
-            if (source.width % 4 != 0) {
-                pc.padded_width = round_up(source.width, 4);
-                pc.padded = allocator.allocate(static_cast<std::size_t>(source.channels) * source.height *
-                                               pc.padded_width * sizeof(float));
-            }
-            pc.pixel_max = allocator.allocate(static_cast<std::size_t>(source.height) * source.width * sizeof(float));
-            scratch = {pc.pixel_max};
-            if (pc.padded != npos) scratch.push_back(pc.padded);
+            const std::size_t pixels = static_cast<std::size_t>(source.height) * source.width;
+            pc.staged = allocator.allocate(pixels * conv.c_pad * element);
+            pc.pixel_max = allocator.allocate(pixels * sizeof(float));
+            scratch = {pc.staged, pc.pixel_max};
         }
         allocator.note_peak();
         for (const auto offset : scratch) allocator.release(offset);
@@ -681,39 +744,40 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
     switch (step.kind) {
     case StepKind::integer_conv: {
         const IntegerConv& conv = convs_[static_cast<std::size_t>(step.conv)];
-        const PlannedConv& pc = plan.convs[index];
         const Extent source = plan.extents[step.source];
         const Extent conv_out = plan.extents[node.output];
-        PlannedConv& planned = plan.convs[index];
+        PlannedConv& pc = plan.convs[index];
+        const IntegerConv::Layout& layout = conv.layouts[pc.source_half ? 1 : 0];
+        const int element = pc.source_half ? 2 : 4;
         float* pixel_max = reinterpret_cast<float*>(base + pc.pixel_max);
-        const float* halo_source = tensor(step.source);
-        if (pc.padded != npos) {
-            float* padded = reinterpret_cast<float*>(base + pc.padded);
-            status = kernels::pad_rows(halo_source, padded, static_cast<std::size_t>(source.channels) * source.height,
-                                       source.width, pc.padded_width, stream_);
-            if (status != cudaSuccess) return cuda_error("row padding launch", status);
-            halo_source = padded;
-            ++launches_;
+        void* staged = base + pc.staged;
+        const Direct& direct_in = run_inputs_[step.source];
+        const void* from = direct_in.data != nullptr ? direct_in.data : tensor(step.source);
+        if (direct_in.data != nullptr && direct_in.half != pc.source_half) {
+            return fail(Code::internal_error, "integer conv source type does not match its plan");
         }
-        if (planned.halo_base != halo_source) {
-            status = kernels::encode_halo_map(&planned.halo_map, halo_source, 0, source.channels, source.height,
-                                              pc.padded_width, pc.halo_box_w, pc.halo_rows, conv.group);
-            if (status != cudaSuccess) return cuda_error("cuTensorMapEncodeTiled halo", status);
-            planned.halo_base = halo_source;
-        }
-        status = kernels::pixel_max(tensor(step.source), 0, source.channels, source.height * source.width, pixel_max,
-                                    stream_);
-        if (status != cudaSuccess) return cuda_error("pixel max launch", status);
+        const int pixels = source.height * source.width;
+        status = kernels::stage_source(from, pc.source_half ? 1 : 0, source.channels, conv.c_pad, pixels, staged,
+                                       pixel_max, stream_);
+        if (status != cudaSuccess) return cuda_error("source staging launch", status);
         const std::string label = program_.tensor_names[step.output];
         const double positions = static_cast<double>(pc.positions);
-        auto marked = mark("pixel_max:" + label, "pixel_max", 0.0,
-                           static_cast<double>(source.count()) * 4.0 + 4.0 * source.height * source.width);
+        auto marked = mark("stage_source:" + label, "stage_source", 0.0,
+                           static_cast<double>(source.count()) * element +
+                               static_cast<double>(pixels) * (conv.c_pad * element + 4.0));
         if (!marked) return marked;
+        if (pc.halo_base != staged) {
+            status = kernels::encode_halo_map(&pc.halo_map, staged, pc.source_half ? 1 : 0, conv.c_pad, source.height,
+                                              source.width, layout.group, pc.halo_box_w, pc.halo_rows);
+            if (status != cudaSuccess) return cuda_error("cuTensorMapEncodeTiled halo", status);
+            pc.halo_base = staged;
+        }
+        const Direct& direct_out = run_outputs_[index];
         kernels::FusedConvArgs f{};
-        f.source = tensor(step.source);
-        f.source_half = 0;
+        f.source_half = pc.source_half ? 1 : 0;
         f.pixel_max = pixel_max;
         f.channels = source.channels;
+        f.c_pad = conv.c_pad;
         f.in_h = source.height;
         f.in_w = source.width;
         f.out_h = conv_out.height;
@@ -727,8 +791,9 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
         f.tiles_y = pc.tiles_y;
         f.tiles_x = pc.tiles_x;
         f.p_tiles = pc.tiles_y * pc.tiles_x;
-        f.group = conv.group;
-        f.groups = conv.groups;
+        f.group = layout.group;
+        f.groups = layout.groups;
+        f.record_bytes = layout.group * element;
         f.halo_rows = pc.halo_rows;
         f.halo_box_w = pc.halo_box_w;
         f.halo_bytes = pc.halo_bytes;
@@ -745,19 +810,20 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
         f.wsilu_scale = step.wsilu_scale;
         f.chunk_add = step.chunk_add ? 1 : 0;
         f.residual = step.residual ? tensor(*step.residual) : nullptr;
-        f.out = tensor(step.output);
-        f.out_half = 0;
+        f.out = direct_out.data != nullptr ? direct_out.data : tensor(step.output);
+        f.out_half = direct_out.data != nullptr && direct_out.half ? 1 : 0;
         f.out_channels = conv.out_channels;
-        f.d2s_block = 0;
+        f.d2s_block = step.d2s_block;
         f.status = status_;
-        status = kernels::fused_conv(conv.b_high_map, conv.b_low_map, planned.halo_map, conv.weight_limbs,
+        status = kernels::fused_conv(layout.b_high_map, layout.b_low_map, pc.halo_map, conv.weight_limbs,
                                      conv.activation_limbs, f, stream_);
         if (status != cudaSuccess) return cuda_error("integer conv launch", status);
         launches_ += 2;
-        const double ops = 2.0 * conv.k_real * static_cast<double>(node.out_channels) * positions;
-        const double out_bytes = static_cast<double>(out_extent.count()) * 4.0 * (step.residual ? 2.0 : 1.0);
+        const double ops = 2.0 * conv.channels * conv.taps * static_cast<double>(node.out_channels) * positions;
+        const double out_bytes = static_cast<double>(out_extent.count()) * (f.out_half ? 2.0 : 4.0) +
+            (step.residual ? static_cast<double>(out_extent.count()) * 4.0 : 0.0);
         return mark("integer_conv:" + label, "integer_conv", ops,
-                    static_cast<double>(source.count()) * 4.0 +
+                    static_cast<double>(pixels) * (conv.c_pad * element + 4.0) +
                         static_cast<double>(node.out_channels) * conv.k_real * conv.weight_limbs + out_bytes);
     }
     case StepKind::chunk_add:
@@ -853,7 +919,7 @@ Status Executor::execute(const std::vector<TensorView>& inputs, const std::vecto
         extents.push_back(view->extent);
         input_views.push_back(view);
     }
-    auto planned = plan_for(extents);
+    auto planned = plan_for(extents, boundary);
     if (!planned) return planned.error();
     Plan& plan = *planned.value();
     std::vector<const TensorView*> output_views;
@@ -881,11 +947,27 @@ Status Executor::execute(const std::vector<TensorView>& inputs, const std::vecto
     launches_ = 0;
     run_started_ = false;
     auto* base = run_base_;
+    // Device runs: integer convs stage their program inputs straight from the
+    // caller's buffers and store outputs that nothing reads straight into them.
+    const bool device = boundary != Boundary::host;
+    run_inputs_.assign(program_.tensor_names.size(), Direct{});
+    run_outputs_.assign(steps_.size(), Direct{});
+    if (device) {
+        for (std::size_t slot = 0; slot < program_.inputs.size(); ++slot) {
+            run_inputs_[program_.inputs[slot]] = Direct{input_views[slot]->data, boundary == Boundary::half};
+        }
+        for (std::size_t slot = 0; slot < program_.outputs.size(); ++slot) {
+            if (output_step_[slot] < 0) continue;
+            run_outputs_[static_cast<std::size_t>(output_step_[slot])] =
+                Direct{output_views[slot]->data, boundary == Boundary::half};
+        }
+    }
     auto started = mark("", "", 0.0, 0.0);
     if (!started) return started;
     double input_bytes = 0.0;
     for (std::size_t slot = 0; slot < program_.inputs.size(); ++slot) {
         const auto id = program_.inputs[slot];
+        if (device && input_conv_only_[slot]) continue;
         float* target = reinterpret_cast<float*>(base + plan.offsets[id]);
         const std::size_t count = plan.extents[id].count();
         input_bytes += static_cast<double>(count) * 6.0;
@@ -910,6 +992,7 @@ Status Executor::execute(const std::vector<TensorView>& inputs, const std::vecto
     double output_bytes = 0.0;
     for (std::size_t slot = 0; slot < program_.outputs.size(); ++slot) {
         const auto id = program_.outputs[slot];
+        if (device && output_step_[slot] >= 0) continue;
         const float* source = reinterpret_cast<const float*>(base + plan.offsets[id]);
         const std::size_t count = plan.extents[id].count();
         output_bytes += static_cast<double>(count) * 6.0;

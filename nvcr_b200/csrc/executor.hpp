@@ -79,9 +79,9 @@ private:
     Status prepare();
     Status prepare_integer_conv(std::size_t step_index);
     void plan_fusions();
-    Result<Plan*> plan_for(const std::vector<Extent>& input_extents);
-    Status ensure_arena(std::size_t bytes);
     enum class Boundary { half, float32, host };
+    Result<Plan*> plan_for(const std::vector<Extent>& input_extents, Boundary boundary);
+    Status ensure_arena(std::size_t bytes);
     Status execute(const std::vector<TensorView>& inputs, const std::vector<TensorView>& outputs, Boundary boundary,
                    void* workspace = nullptr, std::size_t workspace_bytes = 0);
 
@@ -95,6 +95,20 @@ private:
     unsigned int* status_{nullptr};
     std::vector<Step> steps_;
     std::vector<IntegerConv> convs_;
+    // Per program input: every reader is an integer conv reading it as its
+    // source, so on device runs the conv prepass reads the caller's buffer.
+    std::vector<bool> input_conv_only_;
+    // Per program output: the integer conv step that produces it when no step
+    // reads it (the epilogue stores into the caller's buffer), else -1.
+    std::vector<std::ptrdiff_t> output_step_;
+    // The run in progress: caller buffers for direct inputs (by tensor id) and
+    // direct outputs (by step), with their element type.
+    struct Direct {
+        void* data{nullptr};
+        bool half{false};
+    };
+    std::vector<Direct> run_inputs_;
+    std::vector<Direct> run_outputs_;
     std::map<std::vector<std::int32_t>, std::unique_ptr<Plan>> plans_;
     void* arena_{nullptr};
     std::uint8_t* run_base_{nullptr};  // arena_ or a caller's workspace, for the run in progress

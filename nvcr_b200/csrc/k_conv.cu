@@ -1,32 +1,45 @@
 // Fused integer conv on sm_100a: quantise-on-load implicit GEMM.
 //
-// One persistent CTA per SM walks tiles of 128 output positions (a 2-D patch
-// of patch_h x patch_w output pixels) x n_tile output channels. Warp roles:
+// A prepass (stage_source) rewrites the conv's source channel-innermost,
+// [in_h][in_w][c_pad] in its own type (FP16 stays FP16), and writes the
+// per-pixel max |x|. Then one persistent CTA per SM walks tiles of 128 output
+// positions (a 2-D patch of patch_h x patch_w output pixels) x n_tile output
+// channels. Warp roles:
 //   warps 0-3  epilogue: one TMEM lane (= one position) per thread, the
 //              profile's output arithmetic and the folded ops, then the store;
 //   warp 4     TMA: int8 weight tiles (n_tile x 128 B per K block);
 //   warp 5     allocates TMEM and issues the tcgen05 MMAs (one thread);
 //   warps 6-9  producers: one thread per position quantises its receptive
 //              field from the shared-memory halo into the 128-byte-swizzled A
-//              tile; the im2col tensor and the quantised activation matrix
-//              never exist in memory;
-//   warp 10    TMA: the activation halo of the tile, one channel group at a
+//              tile, 16 channels of one tap per 16-byte A chunk; the im2col
+//              tensor and the quantised activation matrix never exist in memory;
+//   warp 10    TMA: the activation halo of the tile, `group` channels at a
 //              time, into a double-buffered shared-memory ring. Padding taps
 //              and the image border come back as the TMA's zero fill.
 // The accumulators are double-buffered in TMEM when they fit, so the epilogue
-// of one tile overlaps the main loop of the next.
+// of one tile overlaps the main loop of the next. The per-column scale, bias
+// and row term of every output column are copied to shared memory once.
 //
-// K is channel-group-major: k = g * (taps * G) + tap * G_g + c, for groups of
-// G channels (the last group holds G_g <= G); the weights are laid out to
-// match on the host. Integer sums do not depend on the K order.
+// Halo layout: one record of `group` channels (record_bytes = 16..128) per
+// pixel, pixels row-major; the TMA swizzles 16-byte pieces inside each
+// 128-byte line (piece ^= line bits), so the 32 positions of a warp read
+// distinct banks. A producer reads 8 FP16 (or 4 FP32) channels per 16-byte load.
+//
+// K is channel-group-major over the padded channels: k = g * (taps * group) +
+// tap * group + c; the weights are laid out to match on the host. Integer sums
+// do not depend on the K order.
 //
 // Activation quantisation per position p: e_p = frexp(max |x| over the
 // receptive field) - (bits - 1) from the per-pixel maxima; then
-// q = clamp(rint(x * 2^-e_p), +-L). With 2^-e_p a normal float the rounding is
-// one fma: fma(x, 2^-e_p, 1.5 * 2^23) is exact in the product and rounds once
-// to the nearest integer at the 2^23 scale, ties to even, so its low bits hold
-// rint(x * 2^-e_p) for |x * 2^-e_p| < 2^22 (always < 2^15 here). Positions whose
-// 2^-e_p is not a normal float take the exact bit-level path.
+// q = clamp(rint(x * 2^-e_p), +-L). Three exact ways, chosen per position:
+//  * FP16 pairs (FP16 source, 8-bit, 2^-e_p a normal half, max * 2^-e_p <
+//    127.5 so no clamp can act): fma.rn.f16x2(x, 2^-e_p, 1536) is exact in the
+//    product and rounds once; |x * 2^-e_p| < 128 keeps it in [1024, 2048)
+//    where halves are the integers, so the low byte of each half is q.
+//  * FP32 (2^-e_p a normal float): fma(x, 2^-e_p, 1.5 * 2^23) likewise rounds
+//    once to the integer (|x * 2^-e_p| < 2^15 < 2^22), low 16 bits = q, with
+//    the clamp applied only when max * 2^-e_p can round past L.
+//  * otherwise the bit-level ldexp + rint of each element.
 //
 // Every wait is bounded (about 2 s of the global timer); after a timeout the
 // CTA sets bit 0 of the status word, stops issuing, drains its MMAs and TMA
@@ -37,6 +50,7 @@
 #include "tcgen05.cuh"
 
 #include <climits>
+#include <type_traits>
 
 #include <cuda_fp16.h>
 
@@ -51,8 +65,8 @@ constexpr int first_producer_warp = 6;
 constexpr int halo_warp = 10;
 constexpr int halo_buffers = 2;
 constexpr int max_stages = 8;
-constexpr float round_magic = 12582912.0f;           // 1.5 * 2^23
-constexpr int round_magic_bits = 0x4B400000;
+constexpr float round_magic = 12582912.0f;              // 1.5 * 2^23
+constexpr std::uint32_t half_magic_pair = 0x66006600u;  // (1536, 1536) as an FP16 pair
 
 struct ConvTail {
     unsigned long long full_a[max_stages];
@@ -72,6 +86,12 @@ struct ConvTail {
     long long column_terms[2][tile_positions_m];
 };
 
+// Bytes of the per-column parameters after the tail: scales, biases and (two-
+// limb activations) row terms of all n_tiles * n_tile physical columns.
+__host__ __device__ constexpr int parameter_bytes(int columns, int activation_limbs) {
+    return columns * 8 + (activation_limbs == 2 ? columns * 8 : 0);
+}
+
 template <int WL, int AL>
 struct ConvLayout {
     static constexpr int accumulators = 1 + ((WL == 2 || AL == 2) ? 1 : 0) + ((WL == 2 && AL == 2) ? 1 : 0);
@@ -81,85 +101,227 @@ struct ConvLayout {
     static __host__ __device__ int b_stage_bytes(int n_tile) { return WL * b_bytes(n_tile); }
 };
 
-template <bool Half>
-__device__ __forceinline__ float load_halo(std::uint32_t address) {
-    if constexpr (Half) {
-        unsigned short bits;
-        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(bits) : "r"(address));
-        return __half2float(__ushort_as_half(bits));
-    } else {
-        float value;
-        asm volatile("ld.shared.f32 %0, [%1];" : "=f"(value) : "r"(address));
-        return value;
-    }
+__device__ __forceinline__ uint4 load_shared_v4(std::uint32_t address) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(address));
+    return v;
 }
-
-// Bytes 0 of a, b, c, d packed into one word, a lowest.
-__device__ __forceinline__ std::uint32_t pack_low_bytes(std::uint32_t a, std::uint32_t b, std::uint32_t c,
-                                                        std::uint32_t d) {
-    return __byte_perm(__byte_perm(a, b, 0x0040u), __byte_perm(c, d, 0x0040u), 0x5410u);
-}
-__device__ __forceinline__ std::uint32_t pack_low_bytes(int a, int b, int c, int d) {
-    return pack_low_bytes(static_cast<std::uint32_t>(a), static_cast<std::uint32_t>(b), static_cast<std::uint32_t>(c),
-                          static_cast<std::uint32_t>(d));
-}
-
-// Sixteen bytes assembled one at a time in two 64-bit registers.
-struct ByteRow {
-    unsigned long long lo{0}, hi{0};
-    __device__ __forceinline__ void put(int j, int value) {
-        const unsigned long long b = static_cast<unsigned long long>(static_cast<std::uint32_t>(value) & 255u);
-        if (j < 8) {
-            lo |= b << (8 * j);
-        } else {
-            hi |= b << (8 * (j - 8));
-        }
-    }
-    __device__ __forceinline__ void words(std::uint32_t (&w)[4]) const {
-        w[0] = static_cast<std::uint32_t>(lo);
-        w[1] = static_cast<std::uint32_t>(lo >> 32);
-        w[2] = static_cast<std::uint32_t>(hi);
-        w[3] = static_cast<std::uint32_t>(hi >> 32);
-    }
-};
 
 __device__ __forceinline__ void store_shared_v4(std::uint32_t address, const std::uint32_t (&w)[4]) {
     asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(address), "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3])
                  : "memory");
 }
 
+// Byte N of each of a, b, c, d packed into one word, a lowest.
+template <int N>
+__device__ __forceinline__ std::uint32_t pack_byte(std::uint32_t a, std::uint32_t b, std::uint32_t c, std::uint32_t d) {
+    constexpr std::uint32_t pair = static_cast<std::uint32_t>(N) | (static_cast<std::uint32_t>(N + 4) << 4);
+    return __byte_perm(__byte_perm(a, b, pair), __byte_perm(c, d, pair), 0x5410u);
+}
+
+// RN(x * s + 1536) for a pair of FP16 channels: q in the low byte of each half.
+__device__ __forceinline__ std::uint32_t round_half_pair(std::uint32_t x, std::uint32_t s) {
+    std::uint32_t y;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(y) : "r"(x), "r"(s), "r"(half_magic_pair));
+    return y;
+}
+
+__device__ __forceinline__ float half_low(std::uint32_t pair) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(pair & 0xffffu)));
+}
+__device__ __forceinline__ float half_high(std::uint32_t pair) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(pair >> 16)));
+}
+
+// Sum of the four signed bytes of w.
+__device__ __forceinline__ int byte_sum(std::uint32_t w) { return __dp4a(static_cast<int>(w), 0x01010101, 0); }
+
+// ---------------------------------------------------------------- prepass
+
 template <bool Half>
-__device__ __forceinline__ float load_source(const void* base, std::size_t index) {
-    if constexpr (Half) {
-        return __half2float(__ldg(static_cast<const __half*>(base) + index));
-    } else {
-        return __ldg(static_cast<const float*>(base) + index);
+struct StageShape {
+    static constexpr int max_slab = Half ? 256 : 128;     // channels per pass through shared memory
+    static constexpr int tile_elements = Half ? 9216 : 4352;
+    static constexpr int max_pixels = Half ? 512 : 256;   // pixels per block
+    static __host__ __device__ constexpr int pitch(int slab) { return slab + (Half ? 2 : 1); }  // odd words apart
+    // Pixels per block for c_pad channels: a multiple of 32 whose tile fits.
+    static int pixels(int c_pad) {
+        const int slab = c_pad < max_slab ? c_pad : max_slab;
+        int m = tile_elements / (32 * pitch(slab));
+        if (m > max_pixels / 32) m = max_pixels / 32;
+        return 32 * (m < 1 ? 1 : m);
+    }
+};
+
+// `block_pixels` consecutive pixels per block, the channels in slabs through
+// shared memory: coalesced reads of each channel plane, contiguous
+// channel-innermost writes, and the per-pixel maximum.
+template <bool Half>
+__global__ void __launch_bounds__(256) stage_source_kernel(const void* __restrict__ in, int channels, int c_pad,
+                                                           int pixels, int block_pixels, void* __restrict__ out,
+                                                           float* __restrict__ pixel_max) {
+    using T = std::conditional_t<Half, unsigned short, float>;
+    using S = StageShape<Half>;
+    constexpr int per_word = Half ? 2 : 1;
+    __shared__ __align__(16) T tile[S::tile_elements];
+    __shared__ float partial[8][S::max_pixels];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int slab = c_pad < S::max_slab ? c_pad : S::max_slab;
+    const int pitch = S::pitch(slab);
+    const long long first = static_cast<long long>(blockIdx.x) * block_pixels;
+    const int valid = static_cast<int>(pixels - first < block_pixels ? pixels - first : block_pixels);
+    const T* source = static_cast<const T*>(in);
+    std::uint32_t* target = static_cast<std::uint32_t*>(out);
+    float maximum[S::max_pixels / 32];
+#pragma unroll
+    for (int k = 0; k < S::max_pixels / 32; ++k) maximum[k] = 0.0f;
+    for (int base = 0; base < c_pad; base += slab) {
+        const int count = c_pad - base < slab ? c_pad - base : slab;
+        for (int c = warp; c < count; c += 8) {
+            const int channel = base + c;
+#pragma unroll
+            for (int k = 0; k < S::max_pixels / 32; ++k) {
+                const int p = k * 32 + lane;
+                if (k * 32 >= block_pixels) break;
+                T v = 0;
+                if (p < valid && channel < channels) {
+                    v = source[static_cast<std::size_t>(channel) * pixels + first + p];
+                    float x;
+                    if constexpr (Half) {
+                        x = __half2float(__ushort_as_half(v));
+                    } else {
+                        x = v;
+                    }
+                    maximum[k] = is_finite_value(x) ? fmaxf(maximum[k], fabsf(x)) : __uint_as_float(0x7f800000u);
+                }
+                tile[p * pitch + c] = v;
+            }
+        }
+        __syncthreads();
+        // Pixel p's `count` channels go to words ((first + p) * c_pad + base) / per_word onwards.
+        const int words = count / per_word;
+        const std::uint32_t* rows = reinterpret_cast<const std::uint32_t*>(tile);
+        const int row_words = pitch / per_word;
+        if (words <= 32) {
+            const int per_pass = 32 / words;  // pixels one warp writes per pass
+            const int sub = lane / words;
+            const int w = lane - sub * words;
+            if (sub < per_pass) {
+                for (int p = warp * per_pass + sub; p < valid; p += 8 * per_pass) {
+                    const std::size_t origin = ((static_cast<std::size_t>(first) + p) * c_pad + base) / per_word;
+                    target[origin + w] = Half ? rows[p * row_words + w] : rows[p * pitch + w];
+                }
+            }
+        } else {
+            for (int p = warp; p < valid; p += 8) {
+                const std::size_t origin = ((static_cast<std::size_t>(first) + p) * c_pad + base) / per_word;
+                for (int w = lane; w < words; w += 32) {
+                    target[origin + w] = Half ? rows[p * row_words + w] : rows[p * pitch + w];
+                }
+            }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int k = 0; k < S::max_pixels / 32; ++k) {
+        if (k * 32 >= block_pixels) break;
+        partial[warp][k * 32 + lane] = maximum[k];
+    }
+    __syncthreads();
+    for (int p = threadIdx.x; p < valid; p += 256) {
+        float m = partial[0][p];
+        for (int g = 1; g < 8; ++g) m = fmaxf(m, partial[g][p]);
+        pixel_max[first + p] = m;
     }
 }
 
-// Per-pixel max |x| over channels; +inf when any channel is non-finite.
-template <bool Half>
-__global__ void __launch_bounds__(256) pixel_max_kernel(const void* __restrict__ in, int channels, int pixels,
-                                                        float* __restrict__ out) {
-    __shared__ float partial[8][32];
-    const int lane = threadIdx.x & 31;
-    const int group = threadIdx.x >> 5;
-    const int pixel = blockIdx.x * 32 + lane;
-    float maximum = 0.0f;
-    bool finite = true;
-    if (pixel < pixels) {
-        for (int c = group; c < channels; c += 8) {
-            const float x = load_source<Half>(in, static_cast<std::size_t>(c) * pixels + pixel);
-            finite = finite && is_finite_value(x);
-            maximum = fmaxf(maximum, fabsf(x));
+// ---------------------------------------------------------------- fused conv
+
+// How one position's activations are quantised in a tile.
+enum QuantMode : int { quant_skip = 0, quant_half = 1, quant_float = 2, quant_float_clamp = 3, quant_exact = 4 };
+
+// Quantises 16 channels of one tap of this position: the 16-byte pieces
+// first .. first + 16 / (channels per piece) - 1 of the halo record whose
+// swizzled base is `record` (piece b lives at record ^ (b << 4)). `high` gets
+// the 16 high-limb bytes (the whole q for 8-bit), `low` the low limbs.
+template <int WL, int AL, bool SourceHalf>
+__device__ __forceinline__ void quantize_chunk(std::uint32_t record, int first, int mode, std::uint32_t scale_pair,
+                                               float scale, int exponent, std::uint32_t (&high)[4],
+                                               std::uint32_t (&low)[4], int& sum_high, int& sum_low) {
+    constexpr int bits = AL == 2 ? 16 : 8;
+    constexpr float limit = AL == 2 ? 32767.0f : 127.0f;
+    auto piece = [&](int b) { return load_shared_v4(record ^ (static_cast<std::uint32_t>(b) << 4)); };
+    if (mode == quant_skip) {
+        high[0] = high[1] = high[2] = high[3] = 0;
+        low[0] = low[1] = low[2] = low[3] = 0;
+        return;
+    }
+    if constexpr (SourceHalf && AL == 1) {
+        if (mode == quant_half) {
+            const uint4 d0 = piece(first);
+            const uint4 d1 = piece(first + 1);
+            const std::uint32_t x[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+            std::uint32_t y[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) y[i] = round_half_pair(x[i], scale_pair);
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+                high[w] = __byte_perm(y[2 * w], y[2 * w + 1], 0x6420u);
+                if constexpr (WL == 2) sum_high += byte_sum(high[w]);
+            }
+            return;
         }
     }
-    partial[group][lane] = finite ? maximum : __uint_as_float(0x7f800000u);
-    __syncthreads();
-    if (group == 0 && pixel < pixels) {
-        float m = partial[0][lane];
-        for (int g = 1; g < 8; ++g) m = fmaxf(m, partial[g][lane]);
-        out[pixel] = m;
+    float v[16];
+    if constexpr (SourceHalf) {
+        const uint4 d0 = piece(first);
+        const uint4 d1 = piece(first + 1);
+        const std::uint32_t x[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            v[2 * i] = half_low(x[i]);
+            v[2 * i + 1] = half_high(x[i]);
+        }
+    } else {
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const uint4 d = piece(first + b);
+            v[4 * b] = __uint_as_float(d.x);
+            v[4 * b + 1] = __uint_as_float(d.y);
+            v[4 * b + 2] = __uint_as_float(d.z);
+            v[4 * b + 3] = __uint_as_float(d.w);
+        }
+    }
+    std::uint32_t u[16];
+    if (mode == quant_exact) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) u[j] = static_cast<std::uint32_t>(quantize_value<bits>(v[j], exponent));
+    } else {
+        // The bits of magic + q: the low 16 bits are q in two's complement.
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            float y = __fmaf_rn(v[j], scale, round_magic);
+            if (mode == quant_float_clamp) y = fminf(fmaxf(y, round_magic - limit), round_magic + limit);
+            u[j] = __float_as_uint(y);
+        }
+    }
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        if constexpr (AL == 2) {
+            // h = q >> 8 is byte 1 of q; l' = (q & 255) - 128 is byte 0 with its top bit flipped.
+            high[w] = pack_byte<1>(u[4 * w], u[4 * w + 1], u[4 * w + 2], u[4 * w + 3]);
+            low[w] = pack_byte<0>(u[4 * w], u[4 * w + 1], u[4 * w + 2], u[4 * w + 3]) ^ 0x80808080u;
+            if constexpr (WL == 2) {
+                sum_high += byte_sum(high[w]);
+                sum_low += byte_sum(low[w]);
+            }
+        } else {
+            high[w] = pack_byte<0>(u[4 * w], u[4 * w + 1], u[4 * w + 2], u[4 * w + 3]);
+            if constexpr (WL == 2) sum_high += byte_sum(high[w]);
+        }
     }
 }
 
@@ -176,15 +338,26 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
     const int n_tile = a.n_tile;
     const int a_stages = a.a_stages;
     const int b_stages = a.b_stages;
-    // Shared memory: [A stages][B stages][halo buffers][tail], each part 1 KiB aligned.
+    // Shared memory: [A stages][B stages][halo buffers][tail][column parameters],
+    // the first three 1 KiB aligned.
     std::uint8_t* b_smem = smem + a_stages * L::a_stage_bytes;
     std::uint8_t* halo_smem = b_smem + b_stages * L::b_stage_bytes(n_tile);
     ConvTail* tail = reinterpret_cast<ConvTail*>(halo_smem + halo_buffers * a.halo_bytes);
+    const int all_columns = a.n_tiles * n_tile;
+    float* column_scale = reinterpret_cast<float*>(reinterpret_cast<std::uint8_t*>(tail) +
+                                                   ((sizeof(ConvTail) + 15) / 16) * 16);
+    float* column_bias = column_scale + all_columns;
+    long long* column_row_terms = reinterpret_cast<long long*>(column_bias + all_columns);
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int total_tiles = a.p_tiles * a.n_tiles;
     const int k_blocks = a.k_blocks;
 
+    for (int i = threadIdx.x; i < all_columns; i += conv_threads) {
+        column_scale[i] = a.scales[i];
+        column_bias[i] = a.bias[i];
+        if constexpr (AL == 2) column_row_terms[i] = a.row_terms[i];
+    }
     if (warp == mma_warp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_address(&tail->tmem_base)), "r"(tmem_columns)
@@ -322,14 +495,14 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
             std::uint32_t job = 0;
             std::uint32_t issued = 0;
             bool ok = true;
-            const int align = a.source_half ? 8 : 4;  // 16 bytes of elements
+            const std::uint32_t box_bytes =
+                static_cast<std::uint32_t>(a.record_bytes) * static_cast<std::uint32_t>(a.halo_box_w * a.halo_rows);
             for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
                 const int p_tile = t / a.n_tiles;
                 const int ty = p_tile / a.tiles_x;
                 const int tx = p_tile - ty * a.tiles_x;
                 const int y0 = ty * a.patch_h * a.window.stride_y - a.window.pad_top;
                 const int x0 = tx * a.patch_w * a.window.stride_x - a.window.pad_left;
-                const int x_start = x0 >= 0 ? (x0 / align) * align : -(((-x0) + align - 1) / align) * align;
                 for (int g = 0; g < a.groups; ++g, ++job) {
                     const int h = static_cast<int>(job % halo_buffers);
                     const std::uint32_t phase = (job / halo_buffers) & 1u;
@@ -339,10 +512,9 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                         break;
                     }
                     const std::uint32_t full = smem_address(&tail->halo_full[h]);
-                    // The TMA delivers exactly the box: group x halo_rows x halo_box_w elements.
-                    barrier_expect_bytes(full, static_cast<std::uint32_t>(a.group * a.halo_rows * a.halo_box_w *
-                                                                          (SourceHalf ? 2 : 4)));
-                    tma_load_3d(smem_address(halo_smem + h * a.halo_bytes), &halo_map, full, x_start, y0, g * a.group);
+                    barrier_expect_bytes(full, box_bytes);
+                    // Innermost coordinate: the group's first channel, a multiple of 16 bytes.
+                    tma_load_3d(smem_address(halo_smem + h * a.halo_bytes), &halo_map, full, g * a.group, x0, y0);
                     issued = job + 1;
                 }
             }
@@ -360,9 +532,14 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
         const int px = row - py * a.patch_w;
         const int kernel_w = a.window.kernel_w;
         const int taps = a.window.kernel_h * kernel_w;
-        const int align = a.source_half ? 8 : 4;
-        const int channel_stride = a.halo_rows * a.halo_box_w;  // elements per channel plane of the halo
-        constexpr float limit = AL == 2 ? 32767.0f : 127.0f;
+        const int record_bytes = a.record_bytes;
+        // Byte offset r * record_bytes >> 7 picks the 128-byte line; its low bits
+        // (as many as there are 16-byte pieces in a record) swizzle the pieces.
+        const std::uint32_t swizzle_mask = static_cast<std::uint32_t>(record_bytes / 16 - 1);
+        const int chunks_per_tap = a.group / 16;
+        constexpr int pieces_per_chunk = SourceHalf ? 2 : 4;
+        const int base_record = py * a.window.stride_y * a.halo_box_w + px * a.window.stride_x;
+        const std::uint32_t slot_key = static_cast<std::uint32_t>(row & 7);
         std::uint32_t g_stage = 0;  // K blocks issued so far (stage ring)
         std::uint32_t job = 0;      // halo groups consumed so far (halo ring)
         int local = 0;
@@ -377,6 +554,9 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
             const int iy0 = oy * a.window.stride_y - a.window.pad_top;
             const int ix0 = ox * a.window.stride_x - a.window.pad_left;
             int exponent = INT_MIN;
+            int mode = quant_skip;
+            float scale = 0.0f;
+            std::uint32_t scale_pair = 0;
             if (real) {
                 float maximum = 0.0f;
                 for (int ky = 0; ky < a.window.kernel_h; ++ky) {
@@ -388,179 +568,91 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                         maximum = fmaxf(maximum, __ldg(a.pixel_max + static_cast<std::size_t>(iy) * a.in_w + ix));
                     }
                 }
-                exponent = maximum == __uint_as_float(0x7f800000u) ? INT_MIN : activation_exponent(maximum, bits);
-            }
-            const bool live = exponent != INT_MIN;
-            const bool fast = live && exponent >= -127 && exponent <= 126;  // 2^-e is a normal float
-            const float scale = fast ? power_of_two(-exponent) : 0.0f;
-            // Halo coordinates of this position's (0, 0) tap.
-            const int x0 = tx * a.patch_w * a.window.stride_x - a.window.pad_left;
-            const int x_start = x0 >= 0 ? (x0 / align) * align : -(((-x0) + align - 1) / align) * align;
-            const int base_y = py * a.window.stride_y;
-            const int base_x = px * a.window.stride_x + (x0 - x_start);
-            int sum_high = 0;
-            int sum_low = 0;
-            // Walk state: group, channels in it, tap, channel, element offset in the halo.
-            int group = 0;
-            int group_channels = a.group < a.channels ? a.group : a.channels;
-            int tap = 0;
-            int c = 0;
-            int index = base_y * a.halo_box_w + base_x;
-            std::uint32_t halo = 0;  // shared address of the current halo buffer
-            auto acquire_halo = [&]() -> bool {
-                const int h = static_cast<int>(job % halo_buffers);
-                if (!barrier_wait(smem_address(&tail->halo_full[h]), (job / halo_buffers) & 1u, a.status)) return false;
-                halo = smem_address(halo_smem + h * a.halo_bytes);
-                return true;
-            };
-            // After the last channel of a tap: the next tap, or the next channel group.
-            auto next_tap = [&]() -> bool {
-                c = 0;
-                if (++tap == taps) {
-                    tap = 0;
-                    barrier_arrive(smem_address(&tail->halo_empty[job % halo_buffers]));
-                    ++job;
-                    if (++group < a.groups) {
-                        const int left = a.channels - group * a.group;
-                        group_channels = left < a.group ? left : a.group;
-                        if (!acquire_halo()) return false;
+                if (maximum != __uint_as_float(0x7f800000u)) {
+                    exponent = activation_exponent(maximum, bits);
+                    if (exponent >= -127 && exponent <= 126) {
+                        scale = power_of_two(-exponent);
+                        const float scaled = __fmul_rn(maximum, scale);  // exact: a power-of-two scaling
+                        constexpr float bound = AL == 2 ? 32767.5f : 127.5f;
+                        mode = scaled < bound ? quant_float : quant_float_clamp;
+                        if (SourceHalf && AL == 1 && mode == quant_float && exponent >= -15 && exponent <= 14) {
+                            const std::uint32_t h = static_cast<std::uint32_t>(15 - exponent) << 10;
+                            scale_pair = h | (h << 16);
+                            mode = quant_half;
+                        }
+                    } else {
+                        mode = quant_exact;
                     }
                 }
-                const int ky = tap / kernel_w;
-                const int kx = tap - ky * kernel_w;
-                index = (base_y + ky) * a.halo_box_w + base_x + kx;
+            }
+            int sum_high = 0;
+            int sum_low = 0;
+            int chunk = 0;            // 16-byte chunk of the open A stage, 0..7
+            int stage = 0;
+            std::uint32_t a_row = 0;  // this position's row in the open A stage
+            auto open_stage = [&]() -> bool {
+                stage = static_cast<int>(g_stage % a_stages);
+                const std::uint32_t phase = (g_stage / a_stages) & 1u;
+                if (*abort || !barrier_wait(smem_address(&tail->empty_a[stage]), phase ^ 1u, a.status)) return false;
+                a_row = smem_address(smem + stage * L::a_stage_bytes + row * tile_k_bytes);
                 return true;
             };
-            auto load = [&](int element) -> float {
-                return load_halo<SourceHalf>(halo + static_cast<std::uint32_t>(element) * (SourceHalf ? 2u : 4u));
+            auto close_stage = [&]() {
+                fence_proxy_async_shared();
+                barrier_arrive(smem_address(&tail->full_a[stage]));
+                ++g_stage;
             };
-            if (*abort || !acquire_halo()) {
-                *abort = 1;
-                break;
-            }
-            for (int kb = 0; kb < k_blocks; ++kb, ++g_stage) {
-                const int s = static_cast<int>(g_stage % a_stages);
-                const std::uint32_t phase = (g_stage / a_stages) & 1u;
-                if (*abort || !barrier_wait(smem_address(&tail->empty_a[s]), phase ^ 1u, a.status)) {
-                    *abort = 1;
+            for (int g = 0; g < a.groups && ok; ++g, ++job) {
+                const int h = static_cast<int>(job % halo_buffers);
+                if (*abort || !barrier_wait(smem_address(&tail->halo_full[h]), (job / halo_buffers) & 1u, a.status)) {
                     ok = false;
                     break;
                 }
-                const std::uint32_t a_hi = smem_address(smem + s * L::a_stage_bytes + row * tile_k_bytes);
-                const std::uint32_t a_lo = a_hi + L::a_bytes;
-                int k = kb * tile_k_bytes;
-#pragma unroll 1
-                for (int chunk = 0; chunk < tile_k_bytes / 16; ++chunk) {
-                    std::uint32_t high_words[4] = {0, 0, 0, 0};
-                    std::uint32_t low_words[4] = {0, 0, 0, 0};
-                    if (c + 16 <= group_channels && k + 16 <= a.k_real) {
-                        // Sixteen channels of one tap: independent loads, then the rounding.
-                        if (fast) {
-                            std::uint32_t rounded[16];
-#pragma unroll
-                            for (int j = 0; j < 16; ++j) rounded[j] = __float_as_uint(load(index + j * channel_stride));
-#pragma unroll
-                            for (int j = 0; j < 16; ++j) {
-                                float y = __fmaf_rn(__uint_as_float(rounded[j]), scale, round_magic);
-                                y = fminf(fmaxf(y, round_magic - limit), round_magic + limit);
-                                rounded[j] = __float_as_uint(y);
-                            }
-#pragma unroll
-                            for (int w = 0; w < 4; ++w) {
-                                const std::uint32_t* b = rounded + 4 * w;
-                                if constexpr (AL == 2) {
-                                    // q = bits - bits(magic); h = q >> 8; l' = (q & 255) - 128.
-                                    int h[4];
-#pragma unroll
-                                    for (int j = 0; j < 4; ++j) {
-                                        const int q = static_cast<int>(b[j]) - round_magic_bits;
-                                        h[j] = q >> 8;
-                                        if constexpr (WL == 2) {
-                                            sum_high += h[j];
-                                            sum_low += (q & 255) - 128;
-                                        }
-                                    }
-                                    high_words[w] = pack_low_bytes(h[0], h[1], h[2], h[3]);
-                                    low_words[w] = pack_low_bytes(b[0], b[1], b[2], b[3]) ^ 0x80808080u;
-                                } else {
-                                    // The low byte of bits(magic + q) is q in two's complement.
-                                    high_words[w] = pack_low_bytes(b[0], b[1], b[2], b[3]);
-                                    if constexpr (WL == 2) {
-#pragma unroll
-                                        for (int j = 0; j < 4; ++j) sum_high += static_cast<int>(b[j]) - round_magic_bits;
-                                    }
-                                }
-                            }
-                        } else if (live) {
-                            ByteRow hb, lb;
-#pragma unroll 1
-                            for (int j = 0; j < 16; ++j) {
-                                const int q = quantize_value<bits>(load(index + j * channel_stride), exponent);
-                                const int h = AL == 2 ? (q >> 8) : q;
-                                const int l = AL == 2 ? (q & 255) - 128 : 0;
-                                hb.put(j, h);
-                                lb.put(j, l);
-                                if constexpr (WL == 2) {
-                                    sum_high += h;
-                                    sum_low += l;
-                                }
-                            }
-                            hb.words(high_words);
-                            lb.words(low_words);
-                        } else if constexpr (AL == 2) {
-                            // q = 0 for every real tap of a non-finite position: l' = -128.
-                            low_words[0] = low_words[1] = low_words[2] = low_words[3] = 0x80808080u;
-                        }
-                        index += 16 * channel_stride;
-                        c += 16;
-                        k += 16;
-                        if (c == group_channels && !next_tap()) {
-                            *abort = 1;
+                const std::uint32_t halo = smem_address(halo_smem + h * a.halo_bytes);
+                int ky = 0;
+                int kx = 0;
+                for (int tap = 0; tap < taps && ok; ++tap) {
+                    const int r = base_record + ky * a.halo_box_w + kx;
+                    const std::uint32_t offset = static_cast<std::uint32_t>(r * record_bytes);
+                    const std::uint32_t record = (halo + offset) ^ (((offset >> 7) & swizzle_mask) << 4);
+                    for (int q = 0; q < chunks_per_tap; ++q) {
+                        if (chunk == 0 && !open_stage()) {
                             ok = false;
+                            break;
                         }
-                    } else {
-                        // General walk, one k at a time (tap or group changes inside the chunk).
-                        ByteRow hb, lb;
-#pragma unroll 1
-                        for (int j = 0; j < 16; ++j, ++k) {
-                            if (k >= a.k_real) continue;
-                            int q = 0;
-                            if (live) {
-                                const float x = load(index);
-                                if (fast) {
-                                    float y = __fmaf_rn(x, scale, round_magic);
-                                    y = fminf(fmaxf(y, round_magic - limit), round_magic + limit);
-                                    q = __float_as_int(y) - round_magic_bits;
-                                } else {
-                                    q = quantize_value<bits>(x, exponent);
-                                }
-                            }
-                            const int h = AL == 2 ? (q >> 8) : q;
-                            const int l = AL == 2 ? (q & 255) - 128 : 0;
-                            hb.put(j, h);
-                            lb.put(j, l);
-                            if constexpr (WL == 2) {
-                                sum_high += h;
-                                sum_low += l;
-                            }
-                            index += channel_stride;
-                            if (++c == group_channels && !next_tap()) {
-                                *abort = 1;
-                                ok = false;
-                            }
+                        std::uint32_t high[4], low[4];
+                        quantize_chunk<WL, AL, SourceHalf>(record, q * pieces_per_chunk, mode, scale_pair, scale,
+                                                           exponent, high, low, sum_high, sum_low);
+                        const std::uint32_t slot = (static_cast<std::uint32_t>(chunk) ^ slot_key) * 16u;
+                        store_shared_v4(a_row + slot, high);
+                        if constexpr (AL == 2) store_shared_v4(a_row + L::a_bytes + slot, low);
+                        if (++chunk == tile_k_bytes / 16) {
+                            close_stage();
+                            chunk = 0;
                         }
-                        hb.words(high_words);
-                        lb.words(low_words);
                     }
-                    const std::uint32_t slot = static_cast<std::uint32_t>((chunk ^ (row & 7)) * 16);
-                    store_shared_v4(a_hi + slot, high_words);
-                    if constexpr (AL == 2) store_shared_v4(a_lo + slot, low_words);
+                    if (++kx == kernel_w) {
+                        kx = 0;
+                        ++ky;
+                    }
                 }
-                fence_proxy_async_shared();
-                barrier_arrive(smem_address(&tail->full_a[s]));
-                if (!ok) break;
+                barrier_arrive(smem_address(&tail->halo_empty[h]));
             }
-            if (!ok) break;
+            if (ok && chunk > 0) {
+                // K past taps * c_pad: zero limbs (the weights are zero there too).
+                const std::uint32_t zero[4] = {0, 0, 0, 0};
+                for (; chunk < tile_k_bytes / 16; ++chunk) {
+                    const std::uint32_t slot = (static_cast<std::uint32_t>(chunk) ^ slot_key) * 16u;
+                    store_shared_v4(a_row + slot, zero);
+                    if constexpr (AL == 2) store_shared_v4(a_row + L::a_bytes + slot, zero);
+                }
+                close_stage();
+                chunk = 0;
+            }
+            if (!ok) {
+                *abort = 1;
+                break;
+            }
             const int info = local & 1;
             if (!barrier_wait(smem_address(&tail->info_empty[info]), ((local >> 1) & 1) ^ 1u, a.status)) {
                 *abort = 1;
@@ -568,7 +660,7 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
             }
             tail->exponents[info][row] = real ? exponent : INT_MIN;
             tail->column_terms[info][row] =
-                live ? a.column_high_factor * sum_high + a.column_low_factor * sum_low : 0;
+                mode != quant_skip ? a.column_high_factor * sum_high + a.column_low_factor * sum_low : 0;
             barrier_arrive(smem_address(&tail->info_full[info]));
         }
     } else {
@@ -610,69 +702,69 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
             const int physical0 = n_index * n_tile;
             const int logical0 = a.chunk_add ? n_index * (n_tile / 2) : physical0;
             const std::uint32_t acc = tmem + static_cast<std::uint32_t>(buffer) * buffer_columns + lane_base;
+            // out = ((float(acc) * scale) * 2^e) + bias. ldexp by e is one multiply
+            // by 2^e when e is in [-126, 127]; rows without an exponent become NaN.
+            const bool normal = exponent >= -126 && exponent <= 127;
+            const bool plain = normal || exponent == INT_MIN;
+            const float power = normal ? power_of_two(exponent) : 1.0f;
 
-            // Per-channel parameters of one 16-column chunk, one coalesced load per
-            // warp: lane l < 16 holds column j0 + l, lane 16 + l its chunk-add
-            // partner j0 + pair_offset + l. Shuffled to every lane when used, and
-            // fetched one chunk ahead.
-            auto fetch = [&](int j0, float& scale, float& bias, long long& terms) {
-                const int column = j0 + (lane < 16 ? lane : pair_offset + lane - 16);
-                const int physical = physical0 + (column < n_tile ? column : 0);
-                scale = __ldg(a.scales + physical);
-                bias = __ldg(a.bias + physical);
-                terms = AL == 2 ? __ldg(a.row_terms + physical) : 0;
-            };
-            float next_scale, next_bias;
-            long long next_terms;
-            fetch(0, next_scale, next_bias, next_terms);
-
-            auto value_at = [&](int source_lane, int hh, int md, int lo, float scales, float biases,
-                                long long terms) -> float {
-                const float scale = __shfl_sync(0xffffffffu, scales, source_lane);
-                const float bias = __shfl_sync(0xffffffffu, biases, source_lane);
-                const long long row_term = AL == 2 ? __shfl_sync(0xffffffffu, terms, source_lane) : 0;
-                float v;
+            auto value_at = [&](int physical, int hh, int md, int lo, float scale, float bias) -> float {
+                float scaled;
                 if constexpr (WL == 1 && AL == 1) {
-                    v = integer_output32(hh, scale, exponent, bias);
+                    scaled = __fmul_rn(__int2float_rn(hh), scale);
                 } else {
-                    long long sum = high_factor * hh + column + mid_factor * md + row_term;
+                    long long sum = high_factor * hh + column + mid_factor * md;
+                    if constexpr (AL == 2) sum += column_row_terms[physical];
                     if constexpr (WL == 2 && AL == 2) sum += lo;
-                    v = integer_output(sum, scale, exponent, bias);
+                    scaled = __fmul_rn(__ll2float_rn(sum), scale);
                 }
+                const float shifted = plain ? __fmul_rn(scaled, power) : exact_ldexp(scaled, exponent);
+                float v = __fadd_rn(shifted, bias);
                 if (a.wsilu) v = profile_wsilu(v, a.wsilu_scale);
                 return v;
             };
+            // 16 consecutive per-column parameters from shared memory (16-byte aligned).
+            auto load16 = [](const float* from, float (&to)[16]) {
+                const float4* v = reinterpret_cast<const float4*>(from);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float4 f = v[i];
+                    to[4 * i] = f.x;
+                    to[4 * i + 1] = f.y;
+                    to[4 * i + 2] = f.z;
+                    to[4 * i + 3] = f.w;
+                }
+            };
 
             for (int j0 = 0; j0 < columns; j0 += 16) {
-                const float scales = next_scale;
-                const float biases = next_bias;
-                const long long terms = next_terms;
-                if (j0 + 16 < columns) fetch(j0 + 16, next_scale, next_bias, next_terms);
-                int hh[16], md[16], lo[16], hh2[16], md2[16], lo2[16];
+                int hh[16], md[16], lo[16];
                 tmem_load16(acc + static_cast<std::uint32_t>(j0), hh);
                 if constexpr (L::accumulators > 1) tmem_load16(acc + static_cast<std::uint32_t>(n_tile + j0), md);
                 if constexpr (L::accumulators > 2) tmem_load16(acc + static_cast<std::uint32_t>(2 * n_tile + j0), lo);
-                if (a.chunk_add) {
-                    const std::uint32_t second = static_cast<std::uint32_t>(j0 + pair_offset);
-                    tmem_load16(acc + second, hh2);
-                    if constexpr (L::accumulators > 1) tmem_load16(acc + static_cast<std::uint32_t>(n_tile) + second, md2);
-                    if constexpr (L::accumulators > 2) {
-                        tmem_load16(acc + static_cast<std::uint32_t>(2 * n_tile) + second, lo2);
-                    }
-                }
+                float scales[16], biases[16];
+                load16(column_scale + physical0 + j0, scales);
+                load16(column_bias + physical0 + j0, biases);
                 tmem_load_wait();
-                // Shuffles need the whole warp, so values are computed for every lane.
                 float v[16];
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
-                    v[j] = value_at(j, hh[j], L::accumulators > 1 ? md[j] : 0, L::accumulators > 2 ? lo[j] : 0,
-                                    scales, biases, terms);
+                    v[j] = value_at(physical0 + j0 + j, hh[j], L::accumulators > 1 ? md[j] : 0,
+                                    L::accumulators > 2 ? lo[j] : 0, scales[j], biases[j]);
                 }
                 if (a.chunk_add) {
+                    const int second = j0 + pair_offset;
+                    tmem_load16(acc + static_cast<std::uint32_t>(second), hh);
+                    if constexpr (L::accumulators > 1) tmem_load16(acc + static_cast<std::uint32_t>(n_tile + second), md);
+                    if constexpr (L::accumulators > 2) {
+                        tmem_load16(acc + static_cast<std::uint32_t>(2 * n_tile + second), lo);
+                    }
+                    load16(column_scale + physical0 + second, scales);
+                    load16(column_bias + physical0 + second, biases);
+                    tmem_load_wait();
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
-                        const float w = value_at(16 + j, hh2[j], L::accumulators > 1 ? md2[j] : 0,
-                                                 L::accumulators > 2 ? lo2[j] : 0, scales, biases, terms);
+                        const float w = value_at(physical0 + second + j, hh[j], L::accumulators > 1 ? md[j] : 0,
+                                                 L::accumulators > 2 ? lo[j] : 0, scales[j], biases[j]);
                         v[j] = __fadd_rn(v[j], w);
                     }
                 }
@@ -698,10 +790,16 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                         const int c = c0 + j;
                         std::size_t index;
                         if (b > 0) {
-                            const int bb = b * b;
-                            const int oc = c / bb;
-                            const int i = (c / b) % b;
-                            const int jj = c % b;
+                            int oc, i, jj;
+                            if (b == 2) {
+                                oc = c >> 2;
+                                i = (c >> 1) & 1;
+                                jj = c & 1;
+                            } else {
+                                oc = c / (b * b);
+                                i = (c / b) % b;
+                                jj = c % b;
+                            }
                             index = (static_cast<std::size_t>(oc) * out_h_full + static_cast<std::size_t>(y) * b + i) *
                                     out_w_full + static_cast<std::size_t>(x) * b + jj;
                         } else {
@@ -748,16 +846,44 @@ EncodeTiled encoder() {
     return function;
 }
 
+int shared_bytes(int weight_limbs, int activation_limbs, int n_tile, int n_tiles, int a_stages, int b_stages,
+                 int halo_bytes) {
+    return 1024 + a_stages * activation_limbs * tile_positions_m * tile_k_bytes +
+        b_stages * weight_limbs * n_tile * tile_k_bytes + halo_buffers * halo_bytes +
+        static_cast<int>((sizeof(ConvTail) + 15) / 16 * 16) + parameter_bytes(n_tile * n_tiles, activation_limbs);
+}
+
+// Host-side checks of everything the kernel's indexing relies on.
+bool valid_geometry(const FusedConvArgs& a, int accumulators) {
+    const int element = a.source_half ? 2 : 4;
+    const int taps = a.window.kernel_h * a.window.kernel_w;
+    const bool record_ok = a.record_bytes == 16 || a.record_bytes == 32 || a.record_bytes == 64 ||
+        a.record_bytes == 128;
+    const bool aligned = (reinterpret_cast<std::uintptr_t>(a.scales) & 15u) == 0 &&
+        (reinterpret_cast<std::uintptr_t>(a.bias) & 15u) == 0;
+    return aligned && a.n_tile >= 16 && a.n_tile <= 256 && a.n_tile % 16 == 0 &&
+        (!a.chunk_add || a.n_tile % 32 == 0) && accumulators * a.n_tile <= 512 && a.k_blocks >= 1 &&
+        a.p_tiles >= 1 && a.n_tiles >= 1 && taps >= 1 && a.patch_h * a.patch_w == tile_positions_m &&
+        a.patch_w >= 1 && record_ok && a.group % 16 == 0 && a.group * element == a.record_bytes &&
+        a.c_pad % a.group == 0 && a.groups * a.group == a.c_pad && a.c_pad >= a.channels &&
+        a.k_real == taps * a.c_pad && a.k_blocks == (a.k_real + tile_k_bytes - 1) / tile_k_bytes &&
+        a.halo_rows == (a.patch_h - 1) * a.window.stride_y + a.window.kernel_h &&
+        a.halo_box_w >= (a.patch_w - 1) * a.window.stride_x + a.window.kernel_w && a.halo_box_w <= 256 &&
+        a.halo_rows <= 256 && a.halo_bytes % 1024 == 0 &&
+        a.halo_bytes >= a.halo_rows * a.halo_box_w * a.record_bytes && a.a_stages >= 1 &&
+        a.a_stages <= max_stages && a.b_stages >= 1 && a.b_stages <= max_stages && a.tiles_y * a.patch_h >= a.out_h &&
+        a.tiles_x * a.patch_w >= a.out_w && a.p_tiles == a.tiles_y * a.tiles_x &&
+        a.positions == a.out_h * a.out_w && a.d2s_block >= 0 &&
+        (a.chunk_add ? a.out_channels <= a.n_tiles * a.n_tile / 2 : a.out_channels <= a.n_tiles * a.n_tile);
+}
+
 template <int WL, int AL, bool SourceHalf>
 cudaError_t launch_fused(const CUtensorMap& b_high, const CUtensorMap& b_low, const CUtensorMap& halo,
                          const FusedConvArgs& args, int sm_count, cudaStream_t stream) {
     using L = ConvLayout<WL, AL>;
     constexpr int max_dynamic = 232448;
     const int n_tile = args.n_tile;
-    if (n_tile < 16 || n_tile > 256 || n_tile % 16 != 0 || (args.chunk_add && n_tile % 32 != 0) ||
-        args.k_blocks < 1 || args.p_tiles < 1 || args.n_tiles < 1) {
-        return cudaErrorInvalidValue;
-    }
+    if (!valid_geometry(args, L::accumulators)) return cudaErrorInvalidValue;
     int buffers = 2;
     std::uint32_t columns = 32;
     while (static_cast<int>(columns) < 2 * L::accumulators * n_tile) columns <<= 1;
@@ -767,12 +893,7 @@ cudaError_t launch_fused(const CUtensorMap& b_high, const CUtensorMap& b_low, co
         while (static_cast<int>(columns) < L::accumulators * n_tile) columns <<= 1;
         if (columns > 512) return cudaErrorInvalidValue;
     }
-    if (args.a_stages < 1 || args.a_stages > max_stages || args.b_stages < 1 || args.b_stages > max_stages ||
-        args.halo_bytes % 1024 != 0 || args.halo_bytes <= 0) {
-        return cudaErrorInvalidValue;
-    }
-    const int smem = 1024 + args.a_stages * L::a_stage_bytes + args.b_stages * L::b_stage_bytes(n_tile) +
-        halo_buffers * args.halo_bytes + static_cast<int>(sizeof(ConvTail));
+    const int smem = shared_bytes(WL, AL, n_tile, args.n_tiles, args.a_stages, args.b_stages, args.halo_bytes);
     if (smem > max_dynamic) return cudaErrorInvalidValue;
     static bool configured = false;
     if (!configured) {
@@ -815,39 +936,49 @@ cudaError_t encode_int8_map(CUtensorMap* map, const void* base, std::uint64_t ro
     return result == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-int fused_conv_shared_bytes(int weight_limbs, int activation_limbs, int n_tile, int a_stages, int b_stages,
-                            int halo_bytes) {
-    return 1024 + a_stages * activation_limbs * tile_positions_m * tile_k_bytes +
-        b_stages * weight_limbs * n_tile * tile_k_bytes + halo_buffers * halo_bytes + static_cast<int>(sizeof(ConvTail));
+int fused_conv_shared_bytes(int weight_limbs, int activation_limbs, int n_tile, int n_tiles, int a_stages,
+                            int b_stages, int halo_bytes) {
+    return shared_bytes(weight_limbs, activation_limbs, n_tile, n_tiles, a_stages, b_stages, halo_bytes);
 }
 
-cudaError_t encode_halo_map(CUtensorMap* map, const void* base, int half, std::uint64_t channels,
-                            std::uint64_t height, std::uint64_t width, std::uint32_t box_w, std::uint32_t box_h,
-                            std::uint32_t box_c) {
+cudaError_t encode_halo_map(CUtensorMap* map, const void* base, int half, std::uint64_t c_pad, std::uint64_t height,
+                            std::uint64_t width, std::uint32_t group, std::uint32_t box_w, std::uint32_t box_h) {
     const EncodeTiled encode = encoder();
     if (encode == nullptr) return cudaErrorNotSupported;
     const std::uint64_t element = half ? 2 : 4;
-    if ((reinterpret_cast<std::uintptr_t>(base) & 15u) != 0 || (width * element) % 16 != 0 || box_w == 0 ||
-        box_w > 256 || box_h == 0 || box_h > 256 || box_c == 0 || box_c > 256 || (box_w * element) % 16 != 0) {
+    const std::uint64_t record = group * element;
+    if ((reinterpret_cast<std::uintptr_t>(base) & 15u) != 0 || (c_pad * element) % 16 != 0 || group == 0 ||
+        c_pad % group != 0 || (record != 16 && record != 32 && record != 64 && record != 128) || box_w == 0 ||
+        box_w > 256 || box_h == 0 || box_h > 256) {
         return cudaErrorInvalidValue;
     }
-    const cuuint64_t dims[3] = {width, height, channels};
-    const cuuint64_t strides[2] = {width * element, width * height * element};
-    const cuuint32_t box[3] = {box_w, box_h, box_c};
+    const CUtensorMapSwizzle swizzle = record == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+        : record == 64                               ? CU_TENSOR_MAP_SWIZZLE_64B
+        : record == 32                               ? CU_TENSOR_MAP_SWIZZLE_32B
+                                                     : CU_TENSOR_MAP_SWIZZLE_NONE;
+    const cuuint64_t dims[3] = {c_pad, width, height};
+    const cuuint64_t strides[2] = {c_pad * element, width * c_pad * element};
+    const cuuint32_t box[3] = {group, box_w, box_h};
     const cuuint32_t element_strides[3] = {1, 1, 1};
     const CUresult result = encode(map, half ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
                                    const_cast<void*>(base), dims, strides, box, element_strides,
-                                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return result == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-cudaError_t pixel_max(const void* in, int source_half, int channels, int pixels, float* out, cudaStream_t stream) {
+cudaError_t stage_source(const void* in, int source_half, int channels, int c_pad, int pixels, void* out,
+                         float* pixel_max, cudaStream_t stream) {
     if (pixels <= 0) return cudaSuccess;
+    if (channels < 1 || c_pad < channels || c_pad % 16 != 0) return cudaErrorInvalidValue;
     if (source_half) {
-        pixel_max_kernel<true><<<(pixels + 31) / 32, 256, 0, stream>>>(in, channels, pixels, out);
+        const int block = StageShape<true>::pixels(c_pad);
+        const unsigned blocks = static_cast<unsigned>((static_cast<long long>(pixels) + block - 1) / block);
+        stage_source_kernel<true><<<blocks, 256, 0, stream>>>(in, channels, c_pad, pixels, block, out, pixel_max);
     } else {
-        pixel_max_kernel<false><<<(pixels + 31) / 32, 256, 0, stream>>>(in, channels, pixels, out);
+        const int block = StageShape<false>::pixels(c_pad);
+        const unsigned blocks = static_cast<unsigned>((static_cast<long long>(pixels) + block - 1) / block);
+        stage_source_kernel<false><<<blocks, 256, 0, stream>>>(in, channels, c_pad, pixels, block, out, pixel_max);
     }
     return cudaGetLastError();
 }

@@ -205,17 +205,6 @@ __global__ void im2col_kernel(const float* __restrict__ in, float* __restrict__ 
     }
 }
 
-// Copies rows of `width` floats into rows of `padded` floats, zeros after each row.
-__global__ void pad_rows_kernel(const float* __restrict__ in, float* __restrict__ out, std::size_t rows, int width,
-                                int padded) {
-    const std::size_t count = rows * static_cast<std::size_t>(padded);
-    for (std::size_t i = global_index(); i < count; i += global_stride()) {
-        const int x = static_cast<int>(i % padded);
-        const std::size_t row = i / padded;
-        out[i] = x < width ? in[row * width + x] : 0.0f;
-    }
-}
-
 // FP32 conv, one thread per output: acc = bias, then for each input channel of
 // the group, each kernel row and column, acc = fma(w, x, acc) with x = 0 on
 // padding taps (the padding fma can still turn -0 into +0, so it is kept).
@@ -351,13 +340,6 @@ cudaError_t im2col(const float* in, float* out, int out_channels, int out_h, int
     const std::size_t count = static_cast<std::size_t>(out_channels) * out_h * out_w;
     if (count == 0) return cudaSuccess;
     im2col_kernel<<<grid_for(count), threads, 0, stream>>>(in, out, out_channels, out_h, out_w, in_h, in_w, window);
-    return cudaGetLastError();
-}
-
-cudaError_t pad_rows(const float* in, float* out, std::size_t rows, int width, int padded, cudaStream_t stream) {
-    const std::size_t count = rows * static_cast<std::size_t>(padded);
-    if (count == 0) return cudaSuccess;
-    pad_rows_kernel<<<grid_for(count), threads, 0, stream>>>(in, out, rows, width, padded);
     return cudaGetLastError();
 }
 

@@ -41,9 +41,6 @@ struct Window {
 cudaError_t im2col(const float* in, float* out, int out_channels, int out_h, int out_w, int in_h, int in_w,
                    Window window, cudaStream_t stream);
 
-// Rows of `width` floats into rows of `padded` floats, zero-filled after each row.
-cudaError_t pad_rows(const float* in, float* out, std::size_t rows, int width, int padded, cudaStream_t stream);
-
 // ---- FP32 conv in the profile's fma order (bias, then channel, row, column) ----
 struct ConvShape {
     int in_channels, out_channels, depthwise;
@@ -54,26 +51,29 @@ cudaError_t conv_fp32(const float* weights, const float* bias, const float* in, 
                       cudaStream_t stream);
 
 // ---- integer conv: fused quantise-on-load implicit GEMM (persistent, tcgen05) ----
-// K is channel-group-major: k = g * (taps * group) + tap * G_g + c; the weight
-// matrices must use the same order.
+// The conv reads its source from a channel-innermost copy [in_h][in_w][c_pad]
+// (FP16 or FP32, channels c_pad > channels zero) made by stage_source(), which
+// also writes the per-pixel maxima. K is channel-group-major over the padded
+// channels: k = g * (taps * group) + tap * group + c, K = taps * c_pad; the
+// weight matrices must use the same order.
 struct FusedConvArgs {
-    const void* source;            // [channels][in_h][in_w], FP16 when source_half else FP32
-    int source_half;
-    const float* pixel_max;        // [in_h][in_w] from pixel_max()
-    int channels, in_h, in_w, out_h, out_w;
+    int source_half;               // staged copy is FP16 (else FP32)
+    const float* pixel_max;        // [in_h][in_w] from stage_source()
+    int channels, c_pad, in_h, in_w, out_h, out_w;
     Window window;
-    int k_real, k_blocks;          // K = channels * kernel_h * kernel_w, blocks of 128 bytes
+    int k_real, k_blocks;          // K = taps * c_pad, blocks of 128 bytes
     int positions, p_tiles;        // out_h * out_w; p_tiles = tiles_y * tiles_x
     int patch_h, patch_w;          // a tile is a patch_h x patch_w block of output pixels (product 128)
     int tiles_y, tiles_x;
-    int group, groups;             // channels per halo load, halo loads per tile
-    int halo_rows, halo_box_w;     // halo box: group x halo_rows x halo_box_w elements
+    int group, groups;             // channels per halo load (divides c_pad), halo loads per tile
+    int record_bytes;              // group * element bytes: 16, 32, 64 or 128 (the halo swizzle span)
+    int halo_rows, halo_box_w;     // halo box: halo_rows x halo_box_w pixels of `group` channels
     int halo_bytes;                // bytes per halo buffer (multiple of 1024)
     int a_stages, b_stages;        // shared-memory ring depths for activations and weights
     int n_tile, n_tiles;
     long long column_high_factor, column_low_factor;  // column term (two-limb weights), else 0
-    const float* scales;           // [n_tiles * n_tile] per physical weight row
-    const float* bias;
+    const float* scales;           // [n_tiles * n_tile] per physical weight row (16-byte aligned)
+    const float* bias;             // (16-byte aligned)
     const long long* row_terms;    // two-limb activations, else null
     int wsilu;
     float wsilu_scale;
@@ -85,20 +85,24 @@ struct FusedConvArgs {
     int d2s_block;                 // 0: NCHW store; b: store through depth_to_space(b)
     unsigned int* status;
 };
-// Per input pixel, max |x| over channels (+inf when any channel is non-finite).
-cudaError_t pixel_max(const void* in, int source_half, int channels, int pixels, float* out, cudaStream_t stream);
+// Channel-innermost copy of a [channels][pixels] FP16 or FP32 tensor with
+// c_pad >= channels channels per pixel (c_pad a multiple of 16, the extra
+// channels zero), and per pixel max |x| over the channels (+inf when any
+// channel is non-finite).
+cudaError_t stage_source(const void* in, int source_half, int channels, int c_pad, int pixels, void* out,
+                         float* pixel_max, cudaStream_t stream);
 cudaError_t fused_conv(const CUtensorMap& b_high, const CUtensorMap& b_low, const CUtensorMap& halo, int weight_limbs,
                        int activation_limbs, const FusedConvArgs& args, cudaStream_t stream);
-// Dynamic shared memory the fused conv needs for these ring depths and halo buffers.
-int fused_conv_shared_bytes(int weight_limbs, int activation_limbs, int n_tile, int a_stages, int b_stages,
-                            int halo_bytes);
+// Dynamic shared memory the fused conv needs for these ring depths and halo
+// buffers, with the per-column parameters of all n_tiles * n_tile columns.
+int fused_conv_shared_bytes(int weight_limbs, int activation_limbs, int n_tile, int n_tiles, int a_stages,
+                            int b_stages, int halo_bytes);
 constexpr int fused_conv_max_shared = 232448;
-// Encodes the 3-D halo map over a [channels][height][width] FP32 or FP16 tensor
-// (row bytes a multiple of 16, base 16-byte aligned) with a box of
-// box_w x box_h x box_c elements, no swizzle, zero fill outside the tensor.
-cudaError_t encode_halo_map(CUtensorMap* map, const void* base, int half, std::uint64_t channels,
-                            std::uint64_t height, std::uint64_t width, std::uint32_t box_w, std::uint32_t box_h,
-                            std::uint32_t box_c);
+// Encodes the 3-D halo map over a staged [height][width][c_pad] tensor with a
+// box of box_h x box_w pixels x `group` channels, zero fill outside the tensor,
+// and the shared-memory swizzle whose span is group * element bytes (none for 16).
+cudaError_t encode_halo_map(CUtensorMap* map, const void* base, int half, std::uint64_t c_pad, std::uint64_t height,
+                            std::uint64_t width, std::uint32_t group, std::uint32_t box_w, std::uint32_t box_h);
 
 // Encodes a 2D tensor map over an int8 [rows][row_bytes] matrix with 128x`box_rows`
 // boxes and 128-byte swizzle, the layout the MMA's shared-memory descriptors expect.

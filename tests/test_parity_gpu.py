@@ -228,3 +228,110 @@ def test_many_tiles_with_fusions_and_groups(cuda, oracle):
     program = conv_program(stream, 256, 128, (3, 3), (1, 1), (1, 1, 1, 1), (16, 16), chunk_add=True, residual=True)
     x = stream.tensor(256, 48, 200, 2.0)
     assert_parity(program, [x], oracle, "many tiles, groups, fusions")
+
+
+def run_half_gpu(program: Program, inputs):
+    """FP16 device tensors in and out (run_half): integer convs stage FP16
+    program inputs directly and store outputs nothing else reads directly."""
+    import torch
+
+    with CudaExecutor.from_program(program) as executor:
+        extents = executor.infer_output_extents([x.shape for x in inputs])
+        ins = {name: torch.from_numpy(x.astype(np.float16)).cuda() for name, x in zip(executor.input_names, inputs)}
+        outs = {name: torch.empty(tuple(e), dtype=torch.float16, device="cuda")
+                for name, e in zip(executor.output_names, extents)}
+        executor.run_half(ins, outs)
+        executor.synchronize()
+        return [outs[name].float().cpu().numpy() for name in executor.output_names]
+
+
+def assert_half_parity(program, inputs, oracle, label):
+    rounded = [x.astype(np.float16).astype(np.float32) for x in inputs]
+    expected = [e.astype(np.float16).astype(np.float32) for e in oracle.run(program, rounded)]
+    got = run_half_gpu(program, inputs)
+    for index, (g, e) in enumerate(zip(got, expected)):
+        assert g.shape == e.shape, f"{label} output {index}: shape {g.shape} != {e.shape}"
+        bad = count_differing(g, e)
+        assert bad == 0, f"{label} output {index}: {bad} of {e.size} elements differ"
+
+
+@pytest.mark.parametrize("case", CONV_CASES, ids=lambda c: f"{c[0]}to{c[1]}k{c[2][0]}x{c[2][1]}s{c[3][0]}")
+@pytest.mark.parametrize("bits", WIDTHS, ids=lambda b: f"w{b[0]}a{b[1]}")
+def test_integer_conv_half(cuda, oracle, case, bits):
+    """The FP16 source path: channel counts 3..200 cover every halo record
+    width (16-128 bytes, each swizzle) for FP16 sources, as the FP32 runs do
+    for FP32 sources."""
+    cin, cout, kernel, stride, pads, h, w = case
+    stream = SeededStream(2000 + cin + cout)
+    program = conv_program(stream, cin, cout, kernel, stride, pads, bits)
+    x = stream.tensor(cin, h, w, 2.0)
+    assert_half_parity(program, [x], oracle, f"half conv {case} w{bits[0]}a{bits[1]}")
+
+
+def clamp_and_tiny_input(stream: SeededStream, cin: int, h: int, w: int) -> np.ndarray:
+    """FP16-exact values: maxima whose scaled value rounds past 127 (the clamp
+    path: 127.5 and 127.75 times a power of two), maxima below 2^-8 (exponents
+    under -15, so no FP16 scale), FP16 subnormals, and ordinary positions."""
+    x = stream.tensor(cin, h, w, 1.0).astype(np.float16).astype(np.float32)
+    x[0, 0, :] = 127.75
+    x[1, 1, :] = -127.5
+    x[2, 2, :] = np.float32(127.75 * 2.0 ** -6)
+    x[:, 3, :] *= np.float32(2.0 ** -12)
+    x[:, 4, :] = np.float32(2.0 ** -24) * (np.arange(cin, dtype=np.float32)[:, None] - cin / 2)
+    x[5 % cin, 5, 3:9] = -np.float32(127.5 * 2.0 ** 3)
+    return x.astype(np.float16).astype(np.float32)
+
+
+@pytest.mark.parametrize("bits", WIDTHS, ids=lambda b: f"w{b[0]}a{b[1]}")
+@pytest.mark.parametrize("half", [False, True], ids=["f32", "f16"])
+def test_quantisation_modes(cuda, oracle, bits, half):
+    """Positions on the clamp path, below the FP16-scale range and on the
+    paired-FP16 path, in one tile (a warp takes several paths at once)."""
+    stream = SeededStream(31)
+    cin = 24
+    x = clamp_and_tiny_input(stream, cin, 8, 40)
+    for kernel, pads in (((3, 3), (1, 1, 1, 1)), ((1, 1), (0, 0, 0, 0))):
+        program = conv_program(stream, cin, 40, kernel, (1, 1), pads, bits)
+        if half:
+            assert_half_parity(program, [x], oracle, f"modes half {kernel} w{bits[0]}a{bits[1]}")
+        else:
+            assert_parity(program, [x], oracle, f"modes {kernel} w{bits[0]}a{bits[1]}")
+
+
+def d2s_program(stream: SeededStream, cin, cout, block, bits) -> Program:
+    p = Program(name="conv_d2s")
+    x = p.add_input("x", cin)
+    w = stream.uniform(-0.5, 0.5, cout * cin * 9)
+    b = stream.uniform(-0.2, 0.2, cout)
+    y = p.dense_conv(x, cout, w, b, "c", kernel=(3, 3), stride=(1, 1), pads=(1, 1, 1, 1), bits=bits)
+    z = p.unary(OpKind.depth_to_space, y, "z", block=block)
+    return p.finish([z])
+
+
+@pytest.mark.parametrize("block", [2, 3])
+@pytest.mark.parametrize("half", [False, True], ids=["f32", "f16"])
+def test_depth_to_space_fold(cuda, oracle, block, half):
+    """conv -> depth_to_space folds into the conv's store (config-2 L5's shape, smaller)."""
+    stream = SeededStream(40 + block)
+    program = d2s_program(stream, 32, 36 * block, block, (8, 8))
+    x = stream.tensor(32, 19, 45, 2.0)
+    if half:
+        assert_half_parity(program, [x], oracle, f"d2s {block} half")
+    else:
+        assert_parity(program, [x], oracle, f"d2s {block}")
+
+
+def test_half_input_shared_with_other_ops(cuda, oracle):
+    """An FP16 program input read by a conv and by a generic op, and a conv
+    output that a later op reads: the conv stages the caller's FP16 buffer, the
+    other readers see the converted FP32 copy, the read output goes through
+    the arena."""
+    stream = SeededStream(44)
+    p = Program(name="shared")
+    x = p.add_input("x", 48)
+    y = p.dense_conv(x, 48, stream.uniform(-0.5, 0.5, 48 * 48 * 9), stream.uniform(-0.2, 0.2, 48), "y",
+                     bits=(8, 8))
+    s = p.binary(OpKind.add, y, x, "s")
+    p.finish([s, y])
+    xs = stream.tensor(48, 21, 37, 2.0)
+    assert_half_parity(p, [xs], oracle, "shared input")
