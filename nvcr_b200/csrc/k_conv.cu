@@ -142,69 +142,82 @@ __device__ __forceinline__ int byte_sum(std::uint32_t w) { return __dp4a(static_
 
 template <bool Half>
 struct StageShape {
-    static constexpr int max_slab = Half ? 256 : 128;     // channels per pass through shared memory
+    static constexpr int max_slab = Half ? 256 : 128;  // channels per pass through shared memory
     static constexpr int tile_elements = Half ? 9216 : 4352;
-    static constexpr int max_pixels = Half ? 512 : 256;   // pixels per block
+    static constexpr int max_pixels = Half ? 512 : 256;  // pixels per block
     static __host__ __device__ constexpr int pitch(int slab) { return slab + (Half ? 2 : 1); }  // odd words apart
-    // Pixels per block for c_pad channels: a multiple of 32 whose tile fits.
+    // Pixels per block for c_pad channels: the largest power-of-two multiple
+    // of 32 whose tile fits.
     static int pixels(int c_pad) {
         const int slab = c_pad < max_slab ? c_pad : max_slab;
-        int m = tile_elements / (32 * pitch(slab));
-        if (m > max_pixels / 32) m = max_pixels / 32;
-        return 32 * (m < 1 ? 1 : m);
+        int p = max_pixels;
+        while (p > 32 && p * pitch(slab) > tile_elements) p /= 2;
+        return p;
     }
 };
 
-// `block_pixels` consecutive pixels per block, the channels in slabs through
-// shared memory: coalesced reads of each channel plane, contiguous
-// channel-innermost writes, and the per-pixel maximum.
-template <bool Half>
+// Pixels consecutive pixels per block, the channels in slabs through shared
+// memory: coalesced reads of each channel plane (up to 16 loads in flight per
+// thread), contiguous channel-innermost writes, and the per-pixel maximum.
+template <bool Half, int Pixels>
 __global__ void __launch_bounds__(256) stage_source_kernel(const void* __restrict__ in, int channels, int c_pad,
-                                                           int pixels, int block_pixels, void* __restrict__ out,
+                                                           int pixels, void* __restrict__ out,
                                                            float* __restrict__ pixel_max) {
     using T = std::conditional_t<Half, unsigned short, float>;
     using S = StageShape<Half>;
     constexpr int per_word = Half ? 2 : 1;
+    constexpr int groups = Pixels / 32;                     // pixel groups of 32 per thread
+    constexpr int batch = groups >= 16 ? 1 : 16 / groups;  // channels per thread per pass
     __shared__ __align__(16) T tile[S::tile_elements];
-    __shared__ float partial[8][S::max_pixels];
+    __shared__ float partial[8][Pixels];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int slab = c_pad < S::max_slab ? c_pad : S::max_slab;
     const int pitch = S::pitch(slab);
-    const long long first = static_cast<long long>(blockIdx.x) * block_pixels;
-    const int valid = static_cast<int>(pixels - first < block_pixels ? pixels - first : block_pixels);
+    const long long first = static_cast<long long>(blockIdx.x) * Pixels;
+    const int valid = static_cast<int>(pixels - first < Pixels ? pixels - first : Pixels);
     const T* source = static_cast<const T*>(in);
     std::uint32_t* target = static_cast<std::uint32_t*>(out);
-    float maximum[S::max_pixels / 32];
+    float maximum[groups];
 #pragma unroll
-    for (int k = 0; k < S::max_pixels / 32; ++k) maximum[k] = 0.0f;
+    for (int k = 0; k < groups; ++k) maximum[k] = 0.0f;
     for (int base = 0; base < c_pad; base += slab) {
         const int count = c_pad - base < slab ? c_pad - base : slab;
-        for (int c = warp; c < count; c += 8) {
-            const int channel = base + c;
+        for (int c0 = warp; c0 < count; c0 += 8 * batch) {
+            T v[batch][groups];
 #pragma unroll
-            for (int k = 0; k < S::max_pixels / 32; ++k) {
-                const int p = k * 32 + lane;
-                if (k * 32 >= block_pixels) break;
-                T v = 0;
-                if (p < valid && channel < channels) {
-                    v = source[static_cast<std::size_t>(channel) * pixels + first + p];
+            for (int u = 0; u < batch; ++u) {
+                const int channel = base + c0 + 8 * u;
+#pragma unroll
+                for (int k = 0; k < groups; ++k) {
+                    const int p = k * 32 + lane;
+                    v[u][k] = (p < valid && channel < channels && c0 + 8 * u < count)
+                        ? source[static_cast<std::size_t>(channel) * pixels + first + p]
+                        : T(0);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < batch; ++u) {
+                const int c = c0 + 8 * u;
+                if (c >= count) break;
+#pragma unroll
+                for (int k = 0; k < groups; ++k) {
                     float x;
                     if constexpr (Half) {
-                        x = __half2float(__ushort_as_half(v));
+                        x = __half2float(__ushort_as_half(v[u][k]));
                     } else {
-                        x = v;
+                        x = v[u][k];
                     }
                     maximum[k] = is_finite_value(x) ? fmaxf(maximum[k], fabsf(x)) : __uint_as_float(0x7f800000u);
+                    tile[(k * 32 + lane) * pitch + c] = v[u][k];
                 }
-                tile[p * pitch + c] = v;
             }
         }
         __syncthreads();
         // Pixel p's `count` channels go to words ((first + p) * c_pad + base) / per_word onwards.
         const int words = count / per_word;
-        const std::uint32_t* rows = reinterpret_cast<const std::uint32_t*>(tile);
         const int row_words = pitch / per_word;
+        const std::uint32_t* rows = reinterpret_cast<const std::uint32_t*>(tile);
         if (words <= 32) {
             const int per_pass = 32 / words;  // pixels one warp writes per pass
             const int sub = lane / words;
@@ -212,30 +225,45 @@ __global__ void __launch_bounds__(256) stage_source_kernel(const void* __restric
             if (sub < per_pass) {
                 for (int p = warp * per_pass + sub; p < valid; p += 8 * per_pass) {
                     const std::size_t origin = ((static_cast<std::size_t>(first) + p) * c_pad + base) / per_word;
-                    target[origin + w] = Half ? rows[p * row_words + w] : rows[p * pitch + w];
+                    target[origin + w] = rows[p * row_words + w];
                 }
             }
         } else {
             for (int p = warp; p < valid; p += 8) {
                 const std::size_t origin = ((static_cast<std::size_t>(first) + p) * c_pad + base) / per_word;
-                for (int w = lane; w < words; w += 32) {
-                    target[origin + w] = Half ? rows[p * row_words + w] : rows[p * pitch + w];
-                }
+                for (int w = lane; w < words; w += 32) target[origin + w] = rows[p * row_words + w];
             }
         }
         __syncthreads();
     }
 #pragma unroll
-    for (int k = 0; k < S::max_pixels / 32; ++k) {
-        if (k * 32 >= block_pixels) break;
-        partial[warp][k * 32 + lane] = maximum[k];
-    }
+    for (int k = 0; k < groups; ++k) partial[warp][k * 32 + lane] = maximum[k];
     __syncthreads();
     for (int p = threadIdx.x; p < valid; p += 256) {
         float m = partial[0][p];
         for (int g = 1; g < 8; ++g) m = fmaxf(m, partial[g][p]);
         pixel_max[first + p] = m;
     }
+}
+
+template <bool Half>
+cudaError_t launch_stage(const void* in, int channels, int c_pad, int pixels, void* out, float* pixel_max,
+                         cudaStream_t stream) {
+    const int block = StageShape<Half>::pixels(c_pad);
+    const unsigned blocks = static_cast<unsigned>((static_cast<long long>(pixels) + block - 1) / block);
+    switch (block) {
+    case 32: stage_source_kernel<Half, 32><<<blocks, 256, 0, stream>>>(in, channels, c_pad, pixels, out, pixel_max); break;
+    case 64: stage_source_kernel<Half, 64><<<blocks, 256, 0, stream>>>(in, channels, c_pad, pixels, out, pixel_max); break;
+    case 128: stage_source_kernel<Half, 128><<<blocks, 256, 0, stream>>>(in, channels, c_pad, pixels, out, pixel_max); break;
+    case 256: stage_source_kernel<Half, 256><<<blocks, 256, 0, stream>>>(in, channels, c_pad, pixels, out, pixel_max); break;
+    default:
+        if constexpr (Half) {
+            stage_source_kernel<Half, 512><<<blocks, 256, 0, stream>>>(in, channels, c_pad, pixels, out, pixel_max);
+        } else {
+            return cudaErrorInvalidValue;
+        }
+    }
+    return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------- fused conv
@@ -971,16 +999,8 @@ cudaError_t stage_source(const void* in, int source_half, int channels, int c_pa
                          float* pixel_max, cudaStream_t stream) {
     if (pixels <= 0) return cudaSuccess;
     if (channels < 1 || c_pad < channels || c_pad % 16 != 0) return cudaErrorInvalidValue;
-    if (source_half) {
-        const int block = StageShape<true>::pixels(c_pad);
-        const unsigned blocks = static_cast<unsigned>((static_cast<long long>(pixels) + block - 1) / block);
-        stage_source_kernel<true><<<blocks, 256, 0, stream>>>(in, channels, c_pad, pixels, block, out, pixel_max);
-    } else {
-        const int block = StageShape<false>::pixels(c_pad);
-        const unsigned blocks = static_cast<unsigned>((static_cast<long long>(pixels) + block - 1) / block);
-        stage_source_kernel<false><<<blocks, 256, 0, stream>>>(in, channels, c_pad, pixels, block, out, pixel_max);
-    }
-    return cudaGetLastError();
+    return source_half ? launch_stage<true>(in, channels, c_pad, pixels, out, pixel_max, stream)
+                       : launch_stage<false>(in, channels, c_pad, pixels, out, pixel_max, stream);
 }
 
 cudaError_t fused_conv(const CUtensorMap& b_high, const CUtensorMap& b_low, const CUtensorMap& halo, int weight_limbs,
