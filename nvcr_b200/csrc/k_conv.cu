@@ -736,65 +736,67 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
             const bool plain = normal || exponent == INT_MIN;
             const float power = normal ? power_of_two(exponent) : 1.0f;
 
-            auto value_at = [&](int physical, int hh, int md, int lo, float scale, float bias) -> float {
-                float scaled;
+            // The exact integer sum of accumulator column j of a chunk, times the column scale.
+            auto scaled_at = [&](int physical, int hh, int md, int lo, float scale) -> float {
                 if constexpr (WL == 1 && AL == 1) {
-                    scaled = __fmul_rn(__int2float_rn(hh), scale);
+                    return __fmul_rn(__int2float_rn(hh), scale);
                 } else {
                     long long sum = high_factor * hh + column + mid_factor * md;
                     if constexpr (AL == 2) sum += column_row_terms[physical];
                     if constexpr (WL == 2 && AL == 2) sum += lo;
-                    scaled = __fmul_rn(__ll2float_rn(sum), scale);
+                    return __fmul_rn(__ll2float_rn(sum), scale);
                 }
-                const float shifted = plain ? __fmul_rn(scaled, power) : exact_ldexp(scaled, exponent);
-                float v = __fadd_rn(shifted, bias);
-                if (a.wsilu) v = profile_wsilu(v, a.wsilu_scale);
-                return v;
             };
-            // 16 consecutive per-column parameters from shared memory (16-byte aligned).
-            auto load16 = [](const float* from, float (&to)[16]) {
-                const float4* v = reinterpret_cast<const float4*>(from);
+            // 16 output values of the chunk at accumulator columns first.. (one
+            // decision per chunk for the rare wide-exponent path and for WSiLU).
+            auto values16 = [&](int first, float (&v)[16]) {
+                int hh[16], md[16], lo[16];
+                tmem_load16(acc + static_cast<std::uint32_t>(first), hh);
+                if constexpr (L::accumulators > 1) tmem_load16(acc + static_cast<std::uint32_t>(n_tile + first), md);
+                if constexpr (L::accumulators > 2) tmem_load16(acc + static_cast<std::uint32_t>(2 * n_tile + first), lo);
+                const float4* scale4 = reinterpret_cast<const float4*>(column_scale + physical0 + first);
+                const float4* bias4 = reinterpret_cast<const float4*>(column_bias + physical0 + first);
+                float scales[16], biases[16];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    const float4 f = v[i];
-                    to[4 * i] = f.x;
-                    to[4 * i + 1] = f.y;
-                    to[4 * i + 2] = f.z;
-                    to[4 * i + 3] = f.w;
+                    const float4 f = scale4[i];
+                    const float4 g = bias4[i];
+                    scales[4 * i] = f.x;
+                    scales[4 * i + 1] = f.y;
+                    scales[4 * i + 2] = f.z;
+                    scales[4 * i + 3] = f.w;
+                    biases[4 * i] = g.x;
+                    biases[4 * i + 1] = g.y;
+                    biases[4 * i + 2] = g.z;
+                    biases[4 * i + 3] = g.w;
+                }
+                tmem_load_wait();
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    v[j] = scaled_at(physical0 + first + j, hh[j], L::accumulators > 1 ? md[j] : 0,
+                                     L::accumulators > 2 ? lo[j] : 0, scales[j]);
+                }
+                if (plain) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(__fmul_rn(v[j], power), biases[j]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(exact_ldexp(v[j], exponent), biases[j]);
+                }
+                if (a.wsilu) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = profile_wsilu(v[j], a.wsilu_scale);
                 }
             };
 
             for (int j0 = 0; j0 < columns; j0 += 16) {
-                int hh[16], md[16], lo[16];
-                tmem_load16(acc + static_cast<std::uint32_t>(j0), hh);
-                if constexpr (L::accumulators > 1) tmem_load16(acc + static_cast<std::uint32_t>(n_tile + j0), md);
-                if constexpr (L::accumulators > 2) tmem_load16(acc + static_cast<std::uint32_t>(2 * n_tile + j0), lo);
-                float scales[16], biases[16];
-                load16(column_scale + physical0 + j0, scales);
-                load16(column_bias + physical0 + j0, biases);
-                tmem_load_wait();
                 float v[16];
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    v[j] = value_at(physical0 + j0 + j, hh[j], L::accumulators > 1 ? md[j] : 0,
-                                    L::accumulators > 2 ? lo[j] : 0, scales[j], biases[j]);
-                }
+                values16(j0, v);
                 if (a.chunk_add) {
-                    const int second = j0 + pair_offset;
-                    tmem_load16(acc + static_cast<std::uint32_t>(second), hh);
-                    if constexpr (L::accumulators > 1) tmem_load16(acc + static_cast<std::uint32_t>(n_tile + second), md);
-                    if constexpr (L::accumulators > 2) {
-                        tmem_load16(acc + static_cast<std::uint32_t>(2 * n_tile + second), lo);
-                    }
-                    load16(column_scale + physical0 + second, scales);
-                    load16(column_bias + physical0 + second, biases);
-                    tmem_load_wait();
+                    float w[16];
+                    values16(j0 + pair_offset, w);
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const float w = value_at(physical0 + second + j, hh[j], L::accumulators > 1 ? md[j] : 0,
-                                                 L::accumulators > 2 ? lo[j] : 0, scales[j], biases[j]);
-                        v[j] = __fadd_rn(v[j], w);
-                    }
+                    for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], w[j]);
                 }
                 const int c0 = logical0 + j0;
                 const int count = a.out_channels - c0 < 16 ? a.out_channels - c0 : 16;
@@ -804,39 +806,46 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                         for (int j = 0; j < 16; ++j) v[j] = canonical_nan();
                     }
                     if (a.residual != nullptr) {
-                        float r[16];
+                        const float* r = a.residual + static_cast<std::size_t>(c0) * a.positions + p;
+                        float add[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) add[j] = j < count ? __ldg(r + static_cast<std::size_t>(j) * a.positions) : 0.0f;
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], add[j]);
+                    }
+                    if (b == 0 && count == 16) {
+                        // Sixteen channel planes of this position.
+                        const std::size_t stride = static_cast<std::size_t>(a.positions);
+                        const std::size_t at = static_cast<std::size_t>(c0) * stride + p;
+                        if (a.out_half) {
+                            __half* o = reinterpret_cast<__half*>(a.out) + at;
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) o[j * stride] = __float2half_rn(v[j]);
+                        } else {
+                            float* o = reinterpret_cast<float*>(a.out) + at;
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) o[j * stride] = v[j];
+                        }
+                    } else {
 #pragma unroll
                         for (int j = 0; j < 16; ++j) {
-                            r[j] = j < count ? __ldg(a.residual + static_cast<std::size_t>(c0 + j) * a.positions + p) : 0.0f;
-                        }
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], r[j]);
-                    }
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        if (j >= count) break;
-                        const int c = c0 + j;
-                        std::size_t index;
-                        if (b > 0) {
-                            int oc, i, jj;
-                            if (b == 2) {
-                                oc = c >> 2;
-                                i = (c >> 1) & 1;
-                                jj = c & 1;
+                            if (j >= count) break;
+                            const int c = c0 + j;
+                            std::size_t index;
+                            if (b > 0) {
+                                const int oc = c / (b * b);
+                                const int i = (c / b) % b;
+                                const int jj = c % b;
+                                index = (static_cast<std::size_t>(oc) * out_h_full + static_cast<std::size_t>(y) * b + i) *
+                                        out_w_full + static_cast<std::size_t>(x) * b + jj;
                             } else {
-                                oc = c / (b * b);
-                                i = (c / b) % b;
-                                jj = c % b;
+                                index = static_cast<std::size_t>(c) * a.positions + p;
                             }
-                            index = (static_cast<std::size_t>(oc) * out_h_full + static_cast<std::size_t>(y) * b + i) *
-                                    out_w_full + static_cast<std::size_t>(x) * b + jj;
-                        } else {
-                            index = static_cast<std::size_t>(c) * a.positions + p;
-                        }
-                        if (a.out_half) {
-                            reinterpret_cast<__half*>(a.out)[index] = __float2half_rn(v[j]);
-                        } else {
-                            reinterpret_cast<float*>(a.out)[index] = v[j];
+                            if (a.out_half) {
+                                reinterpret_cast<__half*>(a.out)[index] = __float2half_rn(v[j]);
+                            } else {
+                                reinterpret_cast<float*>(a.out)[index] = v[j];
+                            }
                         }
                     }
                 }
