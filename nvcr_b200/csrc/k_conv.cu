@@ -572,6 +572,31 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
         std::uint32_t job = 0;      // halo groups consumed so far (halo ring)
         int local = 0;
         bool ok = true;
+        // Pixel maxima of this position's window in the tile t: windows of up to
+        // nine taps load into registers one tile ahead (their latency hides
+        // behind the tile before); larger windows load when needed.
+        constexpr int window_taps = 9;
+        const bool small_window = taps <= window_taps;
+        auto window_loads = [&](int t, float (&m)[window_taps]) {
+            const int p_tile = t / a.n_tiles;
+            const int ty = p_tile / a.tiles_x;
+            const int oy = ty * a.patch_h + py;
+            const int ox = (p_tile - ty * a.tiles_x) * a.patch_w + px;
+            const int iy0 = oy * a.window.stride_y - a.window.pad_top;
+            const int ix0 = ox * a.window.stride_x - a.window.pad_left;
+            const bool real = oy < a.out_h && ox < a.out_w;
+#pragma unroll
+            for (int i = 0; i < window_taps; ++i) {
+                const int ky = i / kernel_w;
+                const int iy = iy0 + ky;
+                const int ix = ix0 + (i - ky * kernel_w);
+                m[i] = (real && i < taps && iy >= 0 && iy < a.in_h && ix >= 0 && ix < a.in_w)
+                    ? __ldg(a.pixel_max + static_cast<std::size_t>(iy) * a.in_w + ix)
+                    : 0.0f;
+            }
+        };
+        float next_window[window_taps];
+        if (small_window && static_cast<int>(blockIdx.x) < total_tiles) window_loads(blockIdx.x, next_window);
         for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++local) {
             const int p_tile = t / a.n_tiles;
             const int ty = p_tile / a.tiles_x;
@@ -581,12 +606,12 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
             const bool real = oy < a.out_h && ox < a.out_w;
             const int iy0 = oy * a.window.stride_y - a.window.pad_top;
             const int ix0 = ox * a.window.stride_x - a.window.pad_left;
-            int exponent = INT_MIN;
-            int mode = quant_skip;
-            float scale = 0.0f;
-            std::uint32_t scale_pair = 0;
-            if (real) {
-                float maximum = 0.0f;
+            float maximum = 0.0f;
+            if (small_window) {
+#pragma unroll
+                for (int i = 0; i < window_taps; ++i) maximum = fmaxf(maximum, next_window[i]);
+                if (t + static_cast<int>(gridDim.x) < total_tiles) window_loads(t + gridDim.x, next_window);
+            } else if (real) {
                 for (int ky = 0; ky < a.window.kernel_h; ++ky) {
                     const int iy = iy0 + ky;
                     if (iy < 0 || iy >= a.in_h) continue;
@@ -596,6 +621,12 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                         maximum = fmaxf(maximum, __ldg(a.pixel_max + static_cast<std::size_t>(iy) * a.in_w + ix));
                     }
                 }
+            }
+            int exponent = INT_MIN;
+            int mode = quant_skip;
+            float scale = 0.0f;
+            std::uint32_t scale_pair = 0;
+            if (real) {
                 if (maximum != __uint_as_float(0x7f800000u)) {
                     exponent = activation_exponent(maximum, bits);
                     if (exponent >= -127 && exponent <= 126) {
@@ -825,6 +856,22 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                             float* o = reinterpret_cast<float*>(a.out) + at;
 #pragma unroll
                             for (int j = 0; j < 16; ++j) o[j * stride] = v[j];
+                        }
+                    } else if (b == 2 && count == 16 && a.out_half) {
+                        // depth_to_space(2): channel c0 + 4q + 2i + jj goes to plane c0 / 4 + q,
+                        // row 2y + i, column 2x + jj; the jj pair is one aligned FP16 pair.
+                        __half2* o = reinterpret_cast<__half2*>(a.out);
+                        const std::size_t plane = static_cast<std::size_t>(out_h_full) * out_w_full;
+                        const std::size_t at = (static_cast<std::size_t>(c0 / 4) * plane +
+                                                static_cast<std::size_t>(2 * y) * out_w_full + 2 * x) / 2;
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+#pragma unroll
+                            for (int i = 0; i < 2; ++i) {
+                                const int j = 4 * q + 2 * i;
+                                o[at + (q * plane + static_cast<std::size_t>(i) * out_w_full) / 2] =
+                                    __floats2half2_rn(v[j], v[j + 1]);
+                            }
                         }
                     } else {
 #pragma unroll
