@@ -271,17 +271,16 @@ cudaError_t launch_stage(const void* in, int channels, int c_pad, int pixels, vo
 // How one position's activations are quantised in a tile.
 enum QuantMode : int { quant_skip = 0, quant_half = 1, quant_float = 2, quant_float_clamp = 3, quant_exact = 4 };
 
-// Quantises 16 channels of one tap of this position: the 16-byte pieces
-// first .. first + 16 / (channels per piece) - 1 of the halo record whose
-// swizzled base is `record` (piece b lives at record ^ (b << 4)). `high` gets
-// the 16 high-limb bytes (the whole q for 8-bit), `low` the low limbs.
+// Quantises 16 channels of one tap of this position from the halo pieces
+// d[0 .. 16 / (channels per piece) - 1] (8 FP16 or 4 FP32 channels each).
+// `high` gets the 16 high-limb bytes (the whole q for 8-bit), `low` the low limbs.
 template <int WL, int AL, bool SourceHalf>
-__device__ __forceinline__ void quantize_chunk(std::uint32_t record, int first, int mode, std::uint32_t scale_pair,
-                                               float scale, int exponent, std::uint32_t (&high)[4],
-                                               std::uint32_t (&low)[4], int& sum_high, int& sum_low) {
+__device__ __forceinline__ void quantize_chunk(const uint4* d, int mode, std::uint32_t scale_pair, float scale,
+                                               int exponent, std::uint32_t (&high)[4], std::uint32_t (&low)[4],
+                                               int& sum_high, int& sum_low) {
     constexpr int bits = AL == 2 ? 16 : 8;
     constexpr float limit = AL == 2 ? 32767.0f : 127.0f;
-    auto piece = [&](int b) { return load_shared_v4(record ^ (static_cast<std::uint32_t>(b) << 4)); };
+    auto piece = [&](int b) { return d[b]; };
     if (mode == quant_skip) {
         high[0] = high[1] = high[2] = high[3] = 0;
         low[0] = low[1] = low[2] = low[3] = 0;
@@ -289,8 +288,8 @@ __device__ __forceinline__ void quantize_chunk(std::uint32_t record, int first, 
     }
     if constexpr (SourceHalf && AL == 1) {
         if (mode == quant_half) {
-            const uint4 d0 = piece(first);
-            const uint4 d1 = piece(first + 1);
+            const uint4 d0 = piece(0);
+            const uint4 d1 = piece(1);
             const std::uint32_t x[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
             std::uint32_t y[8];
 #pragma unroll
@@ -305,8 +304,8 @@ __device__ __forceinline__ void quantize_chunk(std::uint32_t record, int first, 
     }
     float v[16];
     if constexpr (SourceHalf) {
-        const uint4 d0 = piece(first);
-        const uint4 d1 = piece(first + 1);
+        const uint4 d0 = piece(0);
+        const uint4 d1 = piece(1);
         const std::uint32_t x[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -316,7 +315,7 @@ __device__ __forceinline__ void quantize_chunk(std::uint32_t record, int first, 
     } else {
 #pragma unroll
         for (int b = 0; b < 4; ++b) {
-            const uint4 d = piece(first + b);
+            const uint4 d = piece(b);
             v[4 * b] = __uint_as_float(d.x);
             v[4 * b + 1] = __uint_as_float(d.y);
             v[4 * b + 2] = __uint_as_float(d.z);
@@ -566,6 +565,7 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
         const std::uint32_t swizzle_mask = static_cast<std::uint32_t>(record_bytes / 16 - 1);
         const int chunks_per_tap = a.group / 16;
         constexpr int pieces_per_chunk = SourceHalf ? 2 : 4;
+        const int pieces_per_tap = record_bytes / 16;
         const int base_record = py * a.window.stride_y * a.halo_box_w + px * a.window.stride_x;
         const std::uint32_t slot_key = static_cast<std::uint32_t>(row & 7);
         std::uint32_t g_stage = 0;  // K blocks issued so far (stage ring)
@@ -674,13 +674,21 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                     const int r = base_record + ky * a.halo_box_w + kx;
                     const std::uint32_t offset = static_cast<std::uint32_t>(r * record_bytes);
                     const std::uint32_t record = (halo + offset) ^ (((offset >> 7) & swizzle_mask) << 4);
-                    for (int q = 0; q < chunks_per_tap; ++q) {
+                    // The tap's whole record first (up to eight 16-byte loads in flight).
+                    uint4 pieces[8];
+#pragma unroll
+                    for (int b = 0; b < 8; ++b) {
+                        if (b < pieces_per_tap) pieces[b] = load_shared_v4(record ^ (static_cast<std::uint32_t>(b) << 4));
+                    }
+#pragma unroll
+                    for (int q = 0; q < 8 / pieces_per_chunk; ++q) {
+                        if (q >= chunks_per_tap) break;
                         if (chunk == 0 && !open_stage()) {
                             ok = false;
                             break;
                         }
                         std::uint32_t high[4], low[4];
-                        quantize_chunk<WL, AL, SourceHalf>(record, q * pieces_per_chunk, mode, scale_pair, scale,
+                        quantize_chunk<WL, AL, SourceHalf>(pieces + q * pieces_per_chunk, mode, scale_pair, scale,
                                                            exponent, high, low, sum_high, sum_low);
                         const std::uint32_t slot = (static_cast<std::uint32_t>(chunk) ^ slot_key) * 16u;
                         store_shared_v4(a_row + slot, high);
