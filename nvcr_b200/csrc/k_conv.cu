@@ -268,6 +268,38 @@ cudaError_t launch_stage(const void* in, int channels, int c_pad, int pixels, vo
 
 // ---------------------------------------------------------------- fused conv
 
+// Out-of-line helpers for the rare paths, so the hot loops stay compact in the
+// instruction cache.
+struct Sixteen {
+    float v[16];
+};
+struct SixteenWords {
+    std::uint32_t w[16];
+};
+
+// q of each element by the bit-level ldexp and rint (exponents whose 2^-e is
+// not a normal float).
+template <int Bits>
+__device__ __noinline__ SixteenWords quantize_exact16(Sixteen x, int exponent) {
+    SixteenWords q;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) q.w[j] = static_cast<std::uint32_t>(quantize_value<Bits>(x.v[j], exponent));
+    return q;
+}
+
+// ldexp(x, e) + bias per element, for e outside [-126, 127].
+__device__ __noinline__ Sixteen ldexp_add16(Sixteen x, Sixteen bias, int exponent) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) x.v[j] = __fadd_rn(exact_ldexp(x.v[j], exponent), bias.v[j]);
+    return x;
+}
+
+__device__ __noinline__ Sixteen wsilu16(Sixteen x, float k) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) x.v[j] = profile_wsilu(x.v[j], k);
+    return x;
+}
+
 // How one position's activations are quantised in a tile.
 enum QuantMode : int { quant_skip = 0, quant_half = 1, quant_float = 2, quant_float_clamp = 3, quant_exact = 4 };
 
@@ -324,8 +356,12 @@ __device__ __forceinline__ void quantize_chunk(const uint4* d, int mode, std::ui
     }
     std::uint32_t u[16];
     if (mode == quant_exact) {
+        Sixteen x;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) u[j] = static_cast<std::uint32_t>(quantize_value<bits>(v[j], exponent));
+        for (int j = 0; j < 16; ++j) x.v[j] = v[j];
+        const SixteenWords q = quantize_exact16<bits>(x, exponent);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) u[j] = q.w[j];
     } else {
         // The bits of magic + q: the low 16 bits are q in two's complement.
 #pragma unroll
@@ -819,12 +855,23 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
 #pragma unroll
                     for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(__fmul_rn(v[j], power), biases[j]);
                 } else {
+                    Sixteen x, bias;
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(exact_ldexp(v[j], exponent), biases[j]);
+                    for (int j = 0; j < 16; ++j) {
+                        x.v[j] = v[j];
+                        bias.v[j] = biases[j];
+                    }
+                    x = ldexp_add16(x, bias, exponent);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = x.v[j];
                 }
                 if (a.wsilu) {
+                    Sixteen x;
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) v[j] = profile_wsilu(v[j], a.wsilu_scale);
+                    for (int j = 0; j < 16; ++j) x.v[j] = v[j];
+                    x = wsilu16(x, a.wsilu_scale);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = x.v[j];
                 }
             };
 
