@@ -140,6 +140,61 @@ __device__ __forceinline__ int byte_sum(std::uint32_t w) { return __dp4a(static_
 
 // ---------------------------------------------------------------- prepass
 
+// One thread per pixel: the channels of its pixel in blocks of 16 bytes (8 FP16
+// or 4 FP32 channels), each element load coalesced across the warp's 32
+// consecutive pixels, each block one 16-byte store into the pixel's record; the
+// pixel's max |x| (+inf when any channel is non-finite) stays in a register.
+template <bool Half>
+__global__ void __launch_bounds__(256) stage_pixels_kernel(const void* __restrict__ in, int channels, int c_pad,
+                                                           int pixels, void* __restrict__ out,
+                                                           float* __restrict__ pixel_max) {
+    using T = std::conditional_t<Half, unsigned short, float>;
+    constexpr int per_block = 16 / static_cast<int>(sizeof(T));  // channels per 16-byte store
+    constexpr int blocks_per_pass = Half ? 2 : 4;                 // 16 loads in flight
+    const long long pixel = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (pixel >= pixels) return;
+    const T* source = static_cast<const T*>(in) + pixel;
+    uint4* record = reinterpret_cast<uint4*>(static_cast<T*>(out) + pixel * c_pad);
+    float maximum = 0.0f;
+    for (int c0 = 0; c0 < c_pad; c0 += per_block * blocks_per_pass) {
+        T v[blocks_per_pass][per_block];
+#pragma unroll
+        for (int b = 0; b < blocks_per_pass; ++b) {
+#pragma unroll
+            for (int i = 0; i < per_block; ++i) {
+                const int c = c0 + b * per_block + i;
+                v[b][i] = c < channels ? source[static_cast<std::size_t>(c) * pixels] : T(0);
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < blocks_per_pass; ++b) {
+            if (c0 + b * per_block >= c_pad) break;
+            std::uint32_t w[4];
+#pragma unroll
+            for (int i = 0; i < per_block; ++i) {
+                float x;
+                if constexpr (Half) {
+                    x = __half2float(__ushort_as_half(v[b][i]));
+                } else {
+                    x = v[b][i];
+                }
+                maximum = is_finite_value(x) ? fmaxf(maximum, fabsf(x)) : __uint_as_float(0x7f800000u);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                if constexpr (Half) {
+                    w[k] = static_cast<std::uint32_t>(v[b][2 * k]) | (static_cast<std::uint32_t>(v[b][2 * k + 1]) << 16);
+                } else {
+                    w[k] = __float_as_uint(v[b][k]);
+                }
+            }
+            record[(c0 + b * per_block) / per_block] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+    }
+    pixel_max[pixel] = maximum;
+}
+
+// Wide records (more than 32 channels): pixels through shared memory in slabs.
 template <bool Half>
 struct StageShape {
     static constexpr int max_slab = Half ? 256 : 128;  // channels per pass through shared memory
@@ -265,6 +320,7 @@ cudaError_t launch_stage(const void* in, int channels, int c_pad, int pixels, vo
     }
     return cudaGetLastError();
 }
+
 
 // ---------------------------------------------------------------- fused conv
 
@@ -1109,9 +1165,20 @@ cudaError_t encode_halo_map(CUtensorMap* map, const void* base, int half, std::u
 cudaError_t stage_source(const void* in, int source_half, int channels, int c_pad, int pixels, void* out,
                          float* pixel_max, cudaStream_t stream) {
     if (pixels <= 0) return cudaSuccess;
-    if (channels < 1 || c_pad < channels || c_pad % 16 != 0) return cudaErrorInvalidValue;
-    return source_half ? launch_stage<true>(in, channels, c_pad, pixels, out, pixel_max, stream)
-                       : launch_stage<false>(in, channels, c_pad, pixels, out, pixel_max, stream);
+    if (channels < 1 || c_pad < channels || c_pad % 16 != 0 || (reinterpret_cast<std::uintptr_t>(out) & 15u) != 0) {
+        return cudaErrorInvalidValue;
+    }
+    if (c_pad > 32) {
+        return source_half ? launch_stage<true>(in, channels, c_pad, pixels, out, pixel_max, stream)
+                           : launch_stage<false>(in, channels, c_pad, pixels, out, pixel_max, stream);
+    }
+    const unsigned blocks = static_cast<unsigned>((static_cast<long long>(pixels) + 255) / 256);
+    if (source_half) {
+        stage_pixels_kernel<true><<<blocks, 256, 0, stream>>>(in, channels, c_pad, pixels, out, pixel_max);
+    } else {
+        stage_pixels_kernel<false><<<blocks, 256, 0, stream>>>(in, channels, c_pad, pixels, out, pixel_max);
+    }
+    return cudaGetLastError();
 }
 
 cudaError_t fused_conv(const CUtensorMap& b_high, const CUtensorMap& b_low, const CUtensorMap& halo, int weight_limbs,
