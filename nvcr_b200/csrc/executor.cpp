@@ -435,14 +435,19 @@ Status Executor::prepare_integer_conv(std::size_t step_index) {
         }
         return best;
     };
-    // Shared memory: two A stages (filled by the producers), two to four B
-    // stages (TMA), the per-column parameters, and two halo buffers from what
-    // is left; the deepest B ring whose leftover holds a halo of both source
+    // Shared memory: two to four A stages (filled by the producers), two to
+    // four B stages (TMA), the per-column parameters, and two halo buffers from
+    // what is left; the deepest rings whose leftover holds a halo of both source
     // types, with smaller channel groups when none does.
     for (;;) {
         const int need = std::max(smallest_halo(conv.layouts[0].group, 4), smallest_halo(conv.layouts[1].group, 2));
         bool fits = false;
-        for (conv.b_stages = 4; conv.b_stages >= 2; --conv.b_stages) {
+        // Deeper rings first: each A or B stage in flight hides one producer -> MMA
+        // -> commit round trip.
+        constexpr int depths[][2] = {{4, 4}, {3, 4}, {4, 3}, {3, 3}, {2, 4}, {2, 3}, {2, 2}};
+        for (const auto& depth : depths) {
+            conv.a_stages = depth[0];
+            conv.b_stages = depth[1];
             const int fixed = kernels::fused_conv_shared_bytes(conv.weight_limbs, conv.activation_limbs, conv.n_tile,
                                                                conv.n_tiles, conv.a_stages, conv.b_stages, 0);
             conv.halo_budget = ((kernels::fused_conv_max_shared - fixed) / 2) / 1024 * 1024;

@@ -753,49 +753,61 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                 barrier_arrive(smem_address(&tail->full_a[stage]));
                 ++g_stage;
             };
-            for (int g = 0; g < a.groups && ok; ++g, ++job) {
-                const int h = static_cast<int>(job % halo_buffers);
-                if (*abort || !barrier_wait(smem_address(&tail->halo_full[h]), (job / halo_buffers) & 1u, a.status)) {
-                    ok = false;
-                    break;
-                }
-                const std::uint32_t halo = smem_address(halo_smem + h * a.halo_bytes);
-                int ky = 0;
-                int kx = 0;
-                for (int tap = 0; tap < taps && ok; ++tap) {
-                    const int r = base_record + ky * a.halo_box_w + kx;
-                    const std::uint32_t offset = static_cast<std::uint32_t>(r * record_bytes);
-                    const std::uint32_t record = (halo + offset) ^ (((offset >> 7) & swizzle_mask) << 4);
-                    // The tap's whole record first (up to eight 16-byte loads in flight).
-                    uint4 pieces[8];
-#pragma unroll
-                    for (int b = 0; b < 8; ++b) {
-                        if (b < pieces_per_tap) pieces[b] = load_shared_v4(record ^ (static_cast<std::uint32_t>(b) << 4));
+            // A warp whose positions all take the common rounding (or produce
+            // nothing) runs a copy of the walk with that mode fixed at compile time.
+            constexpr int fast_mode = (SourceHalf && AL == 1) ? quant_half : quant_float;
+            auto walk = [&](auto fast) {
+                constexpr bool Fast = decltype(fast)::value;
+                for (int g = 0; g < a.groups && ok; ++g, ++job) {
+                    const int h = static_cast<int>(job % halo_buffers);
+                    if (*abort || !barrier_wait(smem_address(&tail->halo_full[h]), (job / halo_buffers) & 1u, a.status)) {
+                        ok = false;
+                        break;
                     }
-#pragma unroll
-                    for (int q = 0; q < 8 / pieces_per_chunk; ++q) {
-                        if (q >= chunks_per_tap) break;
-                        if (chunk == 0 && !open_stage()) {
-                            ok = false;
-                            break;
+                    const std::uint32_t halo = smem_address(halo_smem + h * a.halo_bytes);
+                    int ky = 0;
+                    int kx = 0;
+                    for (int tap = 0; tap < taps && ok; ++tap) {
+                        const int r = base_record + ky * a.halo_box_w + kx;
+                        const std::uint32_t offset = static_cast<std::uint32_t>(r * record_bytes);
+                        const std::uint32_t record = (halo + offset) ^ (((offset >> 7) & swizzle_mask) << 4);
+                        // The tap's whole record first (up to eight 16-byte loads in flight).
+                        uint4 pieces[8];
+    #pragma unroll
+                        for (int b = 0; b < 8; ++b) {
+                            if (b < pieces_per_tap) pieces[b] = load_shared_v4(record ^ (static_cast<std::uint32_t>(b) << 4));
                         }
-                        std::uint32_t high[4], low[4];
-                        quantize_chunk<WL, AL, SourceHalf>(pieces + q * pieces_per_chunk, mode, scale_pair, scale,
-                                                           exponent, high, low, sum_high, sum_low);
-                        const std::uint32_t slot = (static_cast<std::uint32_t>(chunk) ^ slot_key) * 16u;
-                        store_shared_v4(a_row + slot, high);
-                        if constexpr (AL == 2) store_shared_v4(a_row + L::a_bytes + slot, low);
-                        if (++chunk == tile_k_bytes / 16) {
-                            close_stage();
-                            chunk = 0;
+    #pragma unroll
+                        for (int q = 0; q < 8 / pieces_per_chunk; ++q) {
+                            if (q >= chunks_per_tap) break;
+                            if (chunk == 0 && !open_stage()) {
+                                ok = false;
+                                break;
+                            }
+                            std::uint32_t high[4], low[4];
+                            quantize_chunk<WL, AL, SourceHalf>(pieces + q * pieces_per_chunk, Fast ? fast_mode : mode,
+                                                               scale_pair, scale,
+                                                               exponent, high, low, sum_high, sum_low);
+                            const std::uint32_t slot = (static_cast<std::uint32_t>(chunk) ^ slot_key) * 16u;
+                            store_shared_v4(a_row + slot, high);
+                            if constexpr (AL == 2) store_shared_v4(a_row + L::a_bytes + slot, low);
+                            if (++chunk == tile_k_bytes / 16) {
+                                close_stage();
+                                chunk = 0;
+                            }
+                        }
+                        if (++kx == kernel_w) {
+                            kx = 0;
+                            ++ky;
                         }
                     }
-                    if (++kx == kernel_w) {
-                        kx = 0;
-                        ++ky;
-                    }
+                    barrier_arrive(smem_address(&tail->halo_empty[h]));
                 }
-                barrier_arrive(smem_address(&tail->halo_empty[h]));
+            };
+            if (__all_sync(__activemask(), mode == fast_mode || mode == quant_skip)) {
+                walk(std::true_type{});
+            } else {
+                walk(std::false_type{});
             }
             if (ok && chunk > 0) {
                 // K past taps * c_pad: zero limbs (the weights are zero there too).
