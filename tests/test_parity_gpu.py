@@ -218,7 +218,7 @@ def test_many_tiles_per_cta(cuda, oracle, bits):
     ring (halo, A, B, TMEM, per-tile info) wraps around many times."""
     stream = SeededStream(90)
     program = conv_program(stream, 64, 64, (3, 3), (1, 1), (1, 1, 1, 1), bits)
-    x = stream.tensor(64, 160, 200, 2.0)
+    x = stream.tensor(64, 288, 288, 2.0)  # 648 tiles: four or five per CTA
     assert_parity(program, [x], oracle, f"many tiles w{bits[0]}a{bits[1]}")
 
 
@@ -226,7 +226,7 @@ def test_many_tiles_with_fusions_and_groups(cuda, oracle):
     """Several channel groups per tile (C = 256), chunk-add and residual, many tiles."""
     stream = SeededStream(91)
     program = conv_program(stream, 256, 128, (3, 3), (1, 1), (1, 1, 1, 1), (16, 16), chunk_add=True, residual=True)
-    x = stream.tensor(256, 48, 200, 2.0)
+    x = stream.tensor(256, 96, 224, 2.0)  # 168 tiles of 128 positions
     assert_parity(program, [x], oracle, "many tiles, groups, fusions")
 
 
@@ -335,3 +335,18 @@ def test_half_input_shared_with_other_ops(cuda, oracle):
     p.finish([s, y])
     xs = stream.tensor(48, 21, 37, 2.0)
     assert_half_parity(p, [xs], oracle, "shared input")
+
+
+@pytest.mark.parametrize("half", [False, True], ids=["f32", "f16"])
+def test_many_tiles_pointwise_and_strided(cuda, oracle, half):
+    """Several tiles per CTA on the pointwise and stride-2 shapes of config 2
+    (L1, L3), so every ring and the per-tile info buffers wrap many times."""
+    stream = SeededStream(92)
+    for cin, cout, kernel, stride, pads, h, w in ((3, 64, (3, 3), (2, 2), (1, 1, 1, 1), 260, 300),
+                                                  (128, 256, (1, 1), (1, 1), (0, 0, 0, 0), 72, 200)):
+        program = conv_program(stream, cin, cout, kernel, stride, pads, (8, 8))
+        x = stream.tensor(cin, h, w, 2.0)
+        if half:
+            assert_half_parity(program, [x], oracle, f"many tiles {cin}->{cout} half")
+        else:
+            assert_parity(program, [x], oracle, f"many tiles {cin}->{cout}")
