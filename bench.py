@@ -348,7 +348,7 @@ def main():
     else:
         achieved = all_ops / (all_ms / 1000.0) / 1e12 if all_ms else 0.0
     traffic = None
-    traffic_file = ROOT / "profiles" / "integer_gemm_traffic.json"
+    traffic_file = ROOT / "profiles" / "fused_conv_traffic.json"
     if traffic_file.exists():
         traffic = json.loads(traffic_file.read_text()).get("bytes_per_launch")
     roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(int8_peak, 1), "unit": "TOPS",

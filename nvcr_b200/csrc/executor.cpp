@@ -988,8 +988,11 @@ Status Executor::execute(const std::vector<TensorView>& inputs, const std::vecto
         }
         if (status != cudaSuccess) return cuda_error("input conversion", status);
     }
-    auto marked = mark("inputs", boundary == Boundary::half ? "half_to_float" : "copy", 0.0, input_bytes);
-    if (!marked) return marked;
+    // Segments only for conversions that ran (staged inputs and direct outputs have none).
+    if (input_bytes > 0.0) {
+        auto marked = mark("inputs", boundary == Boundary::half ? "half_to_float" : "copy", 0.0, input_bytes);
+        if (!marked) return marked;
+    }
     for (std::size_t s = 0; s < steps_.size(); ++s) {
         auto launched = launch_step(steps_[s], plan, s);
         if (!launched) return launched;
@@ -1013,8 +1016,10 @@ Status Executor::execute(const std::vector<TensorView>& inputs, const std::vecto
         }
         if (status != cudaSuccess) return cuda_error("output conversion", status);
     }
-    marked = mark("outputs", boundary == Boundary::half ? "float_to_half" : "copy", 0.0, output_bytes);
-    if (!marked) return marked;
+    if (output_bytes > 0.0) {
+        auto marked = mark("outputs", boundary == Boundary::half ? "float_to_half" : "copy", 0.0, output_bytes);
+        if (!marked) return marked;
+    }
     if (boundary == Boundary::host) return synchronize();
     return Ok{};
 }
