@@ -665,10 +665,10 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
         int local = 0;
         bool ok = true;
         // Pixel maxima of this position's window in the tile t: windows of up to
-        // nine taps load into registers one tile ahead (their latency hides
+        // 3x3 taps load into registers one tile ahead (their latency hides
         // behind the tile before); larger windows load when needed.
         constexpr int window_taps = 9;
-        const bool small_window = taps <= window_taps;
+        const bool small_window = a.window.kernel_h <= 3 && kernel_w <= 3;
         auto window_loads = [&](int t, float (&m)[window_taps]) {
             const int p_tile = t / a.n_tiles;
             const int ty = p_tile / a.tiles_x;
@@ -678,13 +678,16 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
             const int ix0 = ox * a.window.stride_x - a.window.pad_left;
             const bool real = oy < a.out_h && ox < a.out_w;
 #pragma unroll
-            for (int i = 0; i < window_taps; ++i) {
-                const int ky = i / kernel_w;
-                const int iy = iy0 + ky;
-                const int ix = ix0 + (i - ky * kernel_w);
-                m[i] = (real && i < taps && iy >= 0 && iy < a.in_h && ix >= 0 && ix < a.in_w)
-                    ? __ldg(a.pixel_max + static_cast<std::size_t>(iy) * a.in_w + ix)
-                    : 0.0f;
+            for (int ky = 0; ky < 3; ++ky) {
+#pragma unroll
+                for (int kx = 0; kx < 3; ++kx) {
+                    const int iy = iy0 + ky;
+                    const int ix = ix0 + kx;
+                    m[3 * ky + kx] = (real && ky < a.window.kernel_h && kx < kernel_w && iy >= 0 && iy < a.in_h &&
+                                      ix >= 0 && ix < a.in_w)
+                        ? __ldg(a.pixel_max + static_cast<std::size_t>(iy) * a.in_w + ix)
+                        : 0.0f;
+                }
             }
         };
         float next_window[window_taps];
