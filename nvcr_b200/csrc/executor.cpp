@@ -36,6 +36,7 @@ struct Executor::IntegerConv {
     // buffer may take.
     int taps{1};
     int a_stages{2}, b_stages{4};
+    bool b_resident{false};  // one N tile whose K blocks all stay in shared memory
     int halo_budget{0};
 };
 
@@ -442,12 +443,18 @@ Status Executor::prepare_integer_conv(std::size_t step_index) {
     for (;;) {
         const int need = std::max(smallest_halo(conv.layouts[0].group, 4), smallest_halo(conv.layouts[1].group, 2));
         bool fits = false;
-        // Deeper rings first: each A or B stage in flight hides one producer -> MMA
-        // -> commit round trip.
-        constexpr int depths[][2] = {{4, 4}, {3, 4}, {4, 3}, {3, 3}, {2, 4}, {2, 3}, {2, 2}};
+        // Resident weights when one N tile's K blocks fit (no weight ring at all),
+        // else deeper rings first: each A or B stage in flight hides one producer
+        // -> MMA -> commit round trip.
+        const int k_blocks = conv.k_padded / 128;
+        const bool can_reside = conv.n_tiles == 1 && k_blocks <= 8;
+        constexpr int depths[][3] = {{4, 0, 1}, {3, 0, 1}, {2, 0, 1}, {4, 4, 0}, {3, 4, 0}, {4, 3, 0},
+                                     {3, 3, 0}, {2, 4, 0}, {2, 3, 0}, {2, 2, 0}};
         for (const auto& depth : depths) {
+            if (depth[2] && !can_reside) continue;
+            conv.b_resident = depth[2] != 0;
             conv.a_stages = depth[0];
-            conv.b_stages = depth[1];
+            conv.b_stages = conv.b_resident ? k_blocks : depth[1];
             const int fixed = kernels::fused_conv_shared_bytes(conv.weight_limbs, conv.activation_limbs, conv.n_tile,
                                                                conv.n_tiles, conv.a_stages, conv.b_stages, 0);
             conv.halo_budget = ((kernels::fused_conv_max_shared - fixed) / 2) / 1024 * 1024;
@@ -804,6 +811,7 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
         f.halo_bytes = pc.halo_bytes;
         f.a_stages = conv.a_stages;
         f.b_stages = conv.b_stages;
+        f.b_resident = conv.b_resident ? 1 : 0;
         f.n_tile = conv.n_tile;
         f.n_tiles = conv.n_tiles;
         f.column_high_factor = conv.weight_limbs == 2 ? conv.column_high_factor : 0;

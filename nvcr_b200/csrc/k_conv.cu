@@ -520,7 +520,9 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
             std::uint32_t g = 0;
             std::uint32_t issued = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+            // Resident weights: the first tile's pass loads every K block into its own stage, once.
+            const int last = a.b_resident ? static_cast<int>(blockIdx.x) + 1 : total_tiles;
+            for (int t = blockIdx.x; t < last && ok; t += gridDim.x) {
                 const int n0 = (t % a.n_tiles) * n_tile;
                 for (int kb = 0; kb < k_blocks; ++kb, ++g) {
                     const int s = static_cast<int>(g % b_stages);
@@ -570,9 +572,10 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                 const std::uint32_t low = acc + static_cast<std::uint32_t>(2 * n_tile);
                 for (int kb = 0; kb < k_blocks; ++kb, ++g) {
                     const int sa = static_cast<int>(g % a_stages);
-                    const int sb = static_cast<int>(g % b_stages);
+                    const int sb = a.b_resident ? kb : static_cast<int>(g % b_stages);
+                    const std::uint32_t b_phase = a.b_resident ? 0u : (g / b_stages) & 1u;
                     if (*abort || !barrier_wait(smem_address(&tail->full_a[sa]), (g / a_stages) & 1u, a.status) ||
-                        !barrier_wait(smem_address(&tail->full_b[sb]), (g / b_stages) & 1u, a.status)) {
+                        !barrier_wait(smem_address(&tail->full_b[sb]), b_phase, a.status)) {
                         *abort = 1;
                         ok = false;
                         break;
@@ -599,7 +602,7 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                         }
                     }
                     mma_commit(smem_address(&tail->empty_a[sa]));
-                    mma_commit(smem_address(&tail->empty_b[sb]));
+                    if (!a.b_resident) mma_commit(smem_address(&tail->empty_b[sb]));
                 }
                 if (!ok) break;
                 mma_commit(smem_address(&tail->tmem_full[buffer]));
@@ -1081,7 +1084,8 @@ bool valid_geometry(const FusedConvArgs& a, int accumulators) {
         a.halo_box_w >= (a.patch_w - 1) * a.window.stride_x + a.window.kernel_w && a.halo_box_w <= 256 &&
         a.halo_rows <= 256 && a.halo_bytes % 1024 == 0 &&
         a.halo_bytes >= a.halo_rows * a.halo_box_w * a.record_bytes && a.a_stages >= 1 &&
-        a.a_stages <= max_stages && a.b_stages >= 1 && a.b_stages <= max_stages && a.tiles_y * a.patch_h >= a.out_h &&
+        a.a_stages <= max_stages && a.b_stages >= 1 && a.b_stages <= max_stages &&
+        (!a.b_resident || (a.n_tiles == 1 && a.b_stages == a.k_blocks)) && a.tiles_y * a.patch_h >= a.out_h &&
         a.tiles_x * a.patch_w >= a.out_w && a.p_tiles == a.tiles_y * a.tiles_x &&
         a.positions == a.out_h * a.out_w && a.d2s_block >= 0 &&
         (a.chunk_add ? a.out_channels <= a.n_tiles * a.n_tile / 2 : a.out_channels <= a.n_tiles * a.n_tile);

@@ -70,6 +70,7 @@ struct FusedConvArgs {
     int halo_rows, halo_box_w;     // halo box: halo_rows x halo_box_w pixels of `group` channels
     int halo_bytes;                // bytes per halo buffer (multiple of 1024)
     int a_stages, b_stages;        // shared-memory ring depths for activations and weights
+    int b_resident;                // weights stay in shared memory: one N tile, b_stages == k_blocks
     int n_tile, n_tiles;
     long long column_high_factor, column_low_factor;  // column term (two-limb weights), else 0
     const float* scales;           // [n_tiles * n_tile] per physical weight row (16-byte aligned)
