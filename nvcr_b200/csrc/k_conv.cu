@@ -555,6 +555,7 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
         if (lane == 0) {
             // ---------------- tensor-core issue
             const std::uint32_t idesc = i8_instruction(n_tile);
+            const int last_steps = (a.k_real - (k_blocks - 1) * tile_k_bytes + 31) / 32;
             const std::uint32_t buffer_columns = static_cast<std::uint32_t>(L::accumulators * n_tile);
             std::uint32_t g = 0;
             int local = 0;
@@ -585,8 +586,11 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                     const std::uint32_t a_lo = a_hi + L::a_bytes;
                     const std::uint32_t b_hi = smem_address(b_smem + sb * L::b_stage_bytes(n_tile));
                     const std::uint32_t b_lo = b_hi + static_cast<std::uint32_t>(L::b_bytes(n_tile));
+                    // The last K block issues only the 32-byte steps that hold K.
+                    const int steps = kb == k_blocks - 1 ? last_steps : tile_k_bytes / 32;
 #pragma unroll
                     for (int kk = 0; kk < tile_k_bytes / 32; ++kk) {
+                        if (kk >= steps) break;
                         const std::uint32_t step = static_cast<std::uint32_t>(kk * 32);
                         const std::uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
                         mma_i8(acc, sw128_descriptor(a_hi + step), sw128_descriptor(b_hi + step), idesc, first);
@@ -816,9 +820,11 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                 walk(std::false_type{});
             }
             if (ok && chunk > 0) {
-                // K past taps * c_pad: zero limbs (the weights are zero there too).
+                // K ends inside this stage: zero limbs up to the end of the last
+                // 32-byte MMA step (the MMA reads no further; the weights are zero there too).
                 const std::uint32_t zero[4] = {0, 0, 0, 0};
-                for (; chunk < tile_k_bytes / 16; ++chunk) {
+                const int used = (chunk + 1) & ~1;
+                for (; chunk < used; ++chunk) {
                     const std::uint32_t slot = (static_cast<std::uint32_t>(chunk) ^ slot_key) * 16u;
                     store_shared_v4(a_row + slot, zero);
                     if constexpr (AL == 2) store_shared_v4(a_row + L::a_bytes + slot, zero);
