@@ -12,9 +12,11 @@ limb expansion and padding are not counted). The step touches about 1 GB, far
 more than the 126 MB L2, so no L2 flush is inserted.
 
   value  whole-job int8 TOPS with inputs resident in HBM (device FP16 tensors);
-  e2e    the same through the C ABI with pinned host FP16 buffers, the
-         host->device input copy and device->host output copy inside the timing;
-  roofline  the integer GEMM kernel (CUDA events on its stream, timed region).
+  e2e    the same through the C ABI with pinned host FP16 buffers, every
+         step's host->device input copies and device->host output copies inside
+         the timing (uploads, runs and downloads of different layers overlap on
+         three streams);
+  roofline  the fused conv kernel (CUDA events on its stream, timed region).
 
 N > 1 (torchrun): every rank runs the same sweep on its own GPU (independent
 replicas, no collective on the data path); value = all ranks' ops / max time.
@@ -245,12 +247,34 @@ def main():
         for executor, xh, yh in zip(executors, inputs, outputs):
             executor.run_half({"x": xh}, {"y": yh})
 
+    # End to end: each layer's host input is copied in on one stream, run on the
+    # executors' stream and its result copied back on a third, ordered by events,
+    # so one layer's upload, another's compute and another's download overlap
+    # (PCIe moves both directions at once). Events also order the reuse of each
+    # layer's device buffers across steps.
+    copy_in = torch.cuda.Stream(device=device)
+    copy_out = torch.cuda.Stream(device=device)
+    in_done = [torch.cuda.Event() for _ in layers]
+    run_done = [torch.cuda.Event() for _ in layers]
+    out_done = [torch.cuda.Event() for _ in layers]
+    for events in (run_done, out_done):
+        for event in events:
+            event.record(stream)
+
     def step_e2e():
-        with torch.cuda.stream(stream):
-            for executor, xh, yh, hi, ho in zip(executors, inputs, outputs, pinned_in, pinned_out):
+        for i, (executor, xh, yh, hi, ho) in enumerate(zip(executors, inputs, outputs, pinned_in, pinned_out)):
+            copy_in.wait_event(run_done[i])      # the previous step's run has read xh
+            with torch.cuda.stream(copy_in):
                 xh.copy_(hi, non_blocking=True)
-                executor.run_half({"x": xh}, {"y": yh})
+            in_done[i].record(copy_in)
+            stream.wait_event(in_done[i])
+            stream.wait_event(out_done[i])       # the previous step's download has read yh
+            executor.run_half({"x": xh}, {"y": yh})
+            run_done[i].record(stream)
+            copy_out.wait_event(run_done[i])
+            with torch.cuda.stream(copy_out):
                 ho.copy_(yh, non_blocking=True)
+            out_done[i].record(copy_out)
 
     def barrier():
         if world > 1:
@@ -275,8 +299,13 @@ def main():
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
         start.record(stream)
+        copy_in.wait_event(start)
+        copy_out.wait_event(start)
         for _ in range(steps):
             function()
+        # The region ends when all three streams are done.
+        stream.wait_stream(copy_in)
+        stream.wait_stream(copy_out)
         end.record(stream)
         torch.cuda.synchronize(device)
         barrier()
