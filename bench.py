@@ -399,6 +399,8 @@ def main():
             cpu_baseline = {"value": None, "unit": "TOPS", "cores": 0, "kind": "reference",
                             "sample": f"unavailable: {error}"}
 
+    decoder = decoder_throughput(args, device, rank, world, max_over_ranks, barrier)
+
     if rank == 0:
         line = {
             "metric": "int8 conv TOPS (config 2 layer sweep, bit-exact intconv.v1)",
@@ -416,6 +418,7 @@ def main():
             "cpu_baseline": cpu_baseline,
             "clocks": clocks,
             "gpu_launches": launches,
+            "decoder": decoder,
         }
         print(json.dumps(line), flush=True)
     for executor in executors:
@@ -425,6 +428,66 @@ def main():
 
         dist.destroy_process_group()
     return 0
+
+
+def decoder_throughput(args, device, rank, world, max_over_ranks, barrier) -> dict:
+    """BASELINE configs 3 and 5 on the synthetic DCVC-RT intra decoder (1080p:
+    y_hat [256, 68, 120] -> frame [3, 1088, 1920], w8a8, FP16 boundary, device-resident
+    latents). Config 3: one stream's frame time. Config 5: 64 independent streams
+    x 16 GOP-1 frames, stream s on rank s mod world, aggregate frames/s over the
+    max-over-ranks device time (strong scaling: the 1024 frames are fixed)."""
+    import numpy as np
+    import torch
+
+    from nvcr_b200.executor import CudaExecutor
+    from nvcr_b200.program import SeededStream
+    from nvcr_b200.workloads import intra_decoder, laplace_latent
+
+    stack = intra_decoder()
+    streams, frames = 64, 16
+    mine = [s for s in range(streams) if s % world == rank]
+    torch_stream = torch.cuda.Stream(device=device)
+    with CudaExecutor.from_program(stack.program, stream=torch_stream.cuda_stream) as executor:
+        latents = [torch.from_numpy(laplace_latent(SeededStream(5000 + s), stack.input_shapes[0])
+                                    .astype(np.float16)).to(device) for s in mine]
+        (c, h, w), = executor.infer_output_extents(stack.input_shapes)
+        frame = torch.empty((c, h, w), dtype=torch.float16, device=device)
+
+        def decode(latent):
+            executor.run_half({"y_hat": latent}, {"frame": frame})
+
+        def timed(count, work):
+            barrier()
+            torch.cuda.synchronize(device)
+            start = torch.cuda.Event(enable_timing=True)
+            end = torch.cuda.Event(enable_timing=True)
+            start.record(torch_stream)
+            for i in range(count):
+                work(i)
+            end.record(torch_stream)
+            torch.cuda.synchronize(device)
+            executor.synchronize()
+            barrier()
+            return start.elapsed_time(end)
+
+        for _ in range(3):
+            decode(latents[0])
+        executor.synchronize()
+        single = 10
+        frame_ms = timed(single, lambda i: decode(latents[0])) / single
+        shard_ms = max_over_ranks(timed(len(mine) * frames, lambda i: decode(latents[i // frames])))
+        launches = executor.launches
+    return {
+        "workload": "synthetic DCVC-RT intra decoder (i.dec topology: subpel up + 14 DepthConvBlocks at "
+                    "256 ch, 1/8 res + d2s(8) head), 1088x1920 frame, w8a8, FP16 boundary",
+        "ops_per_frame": stack.ops,
+        "config3": {"ms_per_frame": round(frame_ms, 3), "frames_per_s": round(1000.0 / frame_ms, 1),
+                    "tops": round(stack.ops / (frame_ms / 1000.0) / 1e12, 1), "gpu_launches_per_frame": launches},
+        "config5": {"streams": streams, "frames_per_stream": frames, "n_gpus": world, "ms": round(shard_ms, 2),
+                    "frames_per_s": round(streams * frames / (shard_ms / 1000.0), 1),
+                    "tops_per_gpu": round(streams * frames * stack.ops / world / (shard_ms / 1000.0) / 1e12, 1),
+                    "scaling": "strong (1024 frames split round-robin by stream)"},
+    }
 
 
 if __name__ == "__main__":

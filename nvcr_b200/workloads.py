@@ -77,3 +77,126 @@ def layer_input(layer: Layer, seed: int, height: int | None = None) -> np.ndarra
     c, h, w = layer.input_shape
     h = h if height is None else height
     return _int_tensor(SeededStream(seed), c * h * w).reshape(c, h, w)
+
+
+# ---------------------------------------------------------------- DCVC-RT-style stacks
+
+# The reference pins the intra decoder's block topology by layer name
+# (i.dec.dec_1.0 = upsample + DepthConvBlock, i.dec.dec_1.1..12 = DepthConvBlocks,
+# i.dec.dec_2 = DepthConvBlock with an adaptor; configs/numerics/dcvcrt-fx.json)
+# and the DepthConvBlock structure (scripts/backends/dcvc_fx.py:178-188), but not
+# the upstream channel widths or weights. The stacks below use that topology with
+# widths chosen here (256 channels at 1/8 resolution) and seeded weights.
+
+DECODER_CHANNELS = 256
+DECODER_BLOCKS = 12
+WSILU_SCALE = 4.0
+
+
+class _StackBuilder:
+    """Appends DCVC-RT-style blocks to a Program, with seeded weights."""
+
+    def __init__(self, p: Program, stream: SeededStream, bits=(8, 8)) -> None:
+        self.p = p
+        self.stream = stream
+        self.bits = bits
+        self.ops = 0.0  # integer-conv MACs x 2 per output position (scaled by positions at the end)
+
+    def weights(self, count: int, fan_in: int) -> np.ndarray:
+        bound = 1.0 / np.sqrt(fan_in)
+        return self.stream.uniform(-bound, bound, count).astype(np.float16).astype(np.float32)
+
+    def bias(self, count: int) -> np.ndarray:
+        return self.stream.uniform(-0.05, 0.05, count).astype(np.float16).astype(np.float32)
+
+    def pointwise(self, x: int, cout: int, name: str) -> int:
+        cin = self.p.tensor_channels[x]
+        self.ops += 2.0 * cin * cout
+        return self.p.conv(x, cout, self.weights(cout * cin, cin), self.bias(cout), name, bits=self.bits)
+
+    def wsilu(self, y: int, name: str) -> int:
+        s = self.p.unary(OpKind.mul_scalar, y, f"{name}.scaled", scalar=WSILU_SCALE)
+        g = self.p.unary(OpKind.sigmoid, s, f"{name}.gate")
+        return self.p.binary(OpKind.mul, y, g, f"{name}.wsilu")
+
+    def chunk_add(self, y: int, name: str) -> int:
+        c = self.p.tensor_channels[y]
+        a = self.p.unary(OpKind.slice_channels, y, f"{name}.low", begin=0, end=c // 2)
+        b = self.p.unary(OpKind.slice_channels, y, f"{name}.high", begin=c // 2, end=c)
+        return self.p.binary(OpKind.add, a, b, f"{name}.sum")
+
+    def depthwise(self, x: int, name: str) -> int:
+        c = self.p.tensor_channels[x]
+        return self.p.conv(x, c, self.weights(c * 9, 9), self.bias(c), name, depthwise=True, kernel=(3, 3),
+                           pads=(1, 1, 1, 1))
+
+    def depth_conv_block(self, x: int, channels: int, name: str, *, adaptor: bool = False,
+                         shortcut: bool = False) -> int:
+        """adaptor 1x1 -> 1x1 + WSiLU -> depthwise 3x3 -> 1x1 + residual -> 1x1 + WSiLU
+        chunk-add -> 1x1 + residual (+ the block input when `shortcut`)."""
+        if adaptor:
+            x = self.pointwise(x, channels, f"{name}.adaptor")
+        t = self.wsilu(self.pointwise(x, channels, f"{name}.dc.0"), f"{name}.dc.1")
+        t = self.depthwise(t, f"{name}.dc.2")
+        out = self.p.binary(OpKind.add, self.pointwise(t, channels, f"{name}.dc.3"), x, f"{name}.dc.res")
+        t = self.pointwise(out, 4 * channels, f"{name}.ffn.0")
+        t = self.chunk_add(self.wsilu(t, f"{name}.ffn.1"), f"{name}.ffn.1")
+        y = self.p.binary(OpKind.add, self.pointwise(t, channels, f"{name}.ffn.2"), out, f"{name}.ffn.res")
+        if shortcut:
+            y = self.p.binary(OpKind.add, y, x, f"{name}.shortcut")
+        return y
+
+    def subpel_up(self, x: int, channels: int, name: str) -> int:
+        """SubpelConv2x: 1x1 conv to 4x the channels, then depth_to_space(2)."""
+        y = self.pointwise(x, 4 * channels, f"{name}.conv.0")
+        return self.p.unary(OpKind.depth_to_space, y, f"{name}.shuffle", block=2)
+
+
+@dataclasses.dataclass
+class Stack:
+    name: str
+    program: Program
+    input_shapes: list[tuple[int, int, int]]
+    ops: float          # algorithmic integer-conv ops per run (2 per MAC)
+
+
+def intra_decoder(latent_hw: tuple[int, int] = (68, 120), *, channels: int = DECODER_CHANNELS,
+                  blocks: int = DECODER_BLOCKS, bits=(8, 8), seed: int = 300,
+                  every_tensor: bool = False) -> Stack:
+    """a DCVC-RT-architecture intra decoder. y_hat
+    [256, h, w] (1/16 of the frame) -> dec_1.0 (SubpelConv2x up + DepthConvBlock)
+    -> dec_1.1..blocks (DepthConvBlocks at 1/8) -> dec_2 (DepthConvBlock with an
+    adaptor) -> 1x1 head to 3 x 8 x 8 channels -> depth_to_space(8): the
+    3 x 16h x 16w frame. `every_tensor` makes every block's output a program
+    output (for parity tests)."""
+    stream = SeededStream(seed)
+    p = Program(name="intra_decoder")
+    b = _StackBuilder(p, stream, bits)
+    y_hat = p.add_input("y_hat", 256)
+    taps = []
+    x = b.subpel_up(y_hat, channels, "i.dec.dec_1.0.up")
+    up_ops = b.ops  # at the latent resolution
+    b.ops = 0.0
+    x = b.depth_conv_block(x, channels, "i.dec.dec_1.0.conv")
+    taps.append(x)
+    for i in range(1, blocks + 1):
+        x = b.depth_conv_block(x, channels, f"i.dec.dec_1.{i}")
+        taps.append(x)
+    x = b.depth_conv_block(x, channels, "i.dec.dec_2", adaptor=True)
+    taps.append(x)
+    head = b.pointwise(x, 3 * 64, "i.dec.head")
+    frame = p.unary(OpKind.depth_to_space, head, "frame", block=8)
+    p.finish((taps + [frame]) if every_tensor else [frame])
+    h, w = latent_hw
+    ops = up_ops * h * w + b.ops * (2 * h) * (2 * w)
+    return Stack("config3_intra_decoder", p, [(256, h, w)], ops)
+
+
+def laplace_latent(stream: SeededStream, shape: tuple[int, int, int], scale: float = 4.0) -> np.ndarray:
+    """Integer latents: Laplace(0, scale) by inverse CDF of the stream's uniforms,
+    rounded to nearest and clamped to [-127, 127]."""
+    count = int(np.prod(shape))
+    u = stream.uniform(-0.5, 0.5, count).astype(np.float64)
+    u = np.clip(u, -0.5 + 1e-12, 0.5 - 1e-12)
+    x = -scale * np.sign(u) * np.log1p(-2.0 * np.abs(u))
+    return np.clip(np.rint(x), -127, 127).astype(np.float32).reshape(shape)

@@ -350,3 +350,26 @@ def test_many_tiles_pointwise_and_strided(cuda, oracle, half):
             assert_half_parity(program, [x], oracle, f"many tiles {cin}->{cout} half")
         else:
             assert_parity(program, [x], oracle, f"many tiles {cin}->{cout}")
+
+
+@pytest.mark.parametrize("bits", [(8, 8), (16, 16)], ids=["w8a8", "w16a16"])
+def test_intra_decoder_stack(cuda, oracle, bits):
+    """BASELINE config 3's stack (synthetic DCVC-RT intra decoder: subpel
+    upsample, 14 DepthConvBlocks with WSiLU, depthwise 3x3, residuals and
+    chunk-add, a depth_to_space(8) head) on a small latent; every block's output
+    is compared bit for bit. w8a8 is BASELINE's; w16a16 is the reference width
+    map's default for the decoder layers."""
+    from nvcr_b200.workloads import intra_decoder, laplace_latent
+
+    stack = intra_decoder((3, 5), bits=bits, every_tensor=True)
+    y_hat = laplace_latent(SeededStream(7), stack.input_shapes[0])
+    assert_parity(stack.program, [y_hat], oracle, f"intra decoder {bits}")
+
+
+def test_intra_decoder_stack_half(cuda, oracle):
+    """The same stack through run_half (FP16 latent in, FP16 tensors out)."""
+    from nvcr_b200.workloads import intra_decoder, laplace_latent
+
+    stack = intra_decoder((4, 6), every_tensor=True)
+    y_hat = laplace_latent(SeededStream(8), stack.input_shapes[0])
+    assert_half_parity(stack.program, [y_hat], oracle, "intra decoder half")
