@@ -240,6 +240,57 @@ __global__ void conv_fp32_kernel(const float* __restrict__ weights, const float*
     }
 }
 
+// Depthwise 3x3, stride 1, pad 1: a 32 x 32 output tile of one channel plane
+// per block from a 34 x 34 input tile in shared memory; each thread computes a
+// column of four outputs. Same fma order as conv_fp32_kernel (bias, then row,
+// column; padding taps multiply zeros).
+constexpr int dw_tile = 32;
+__global__ void __launch_bounds__(256) depthwise3x3_kernel(const float* __restrict__ weights,
+                                                           const float* __restrict__ bias,
+                                                           const float* __restrict__ in, float* __restrict__ out,
+                                                           int height, int width) {
+    __shared__ float tile[dw_tile + 2][dw_tile + 3];
+    const int c = blockIdx.z;
+    const int x0 = blockIdx.x * dw_tile;
+    const int y0 = blockIdx.y * dw_tile;
+    const float* plane = in + static_cast<std::size_t>(c) * height * width;
+    for (int i = threadIdx.x; i < (dw_tile + 2) * (dw_tile + 2); i += 256) {
+        const int ty = i / (dw_tile + 2);
+        const int tx = i - ty * (dw_tile + 2);
+        const int y = y0 + ty - 1;
+        const int x = x0 + tx - 1;
+        tile[ty][tx] = (y >= 0 && y < height && x >= 0 && x < width) ? __ldg(plane + static_cast<std::size_t>(y) * width + x)
+                                                                     : 0.0f;
+    }
+    float w[9];
+#pragma unroll
+    for (int k = 0; k < 9; ++k) w[k] = __ldg(weights + static_cast<std::size_t>(c) * 9 + k);
+    const float b = __ldg(bias + c);
+    __syncthreads();
+    const int tx = threadIdx.x & 31;
+    const int ty = (threadIdx.x >> 5) * 4;  // four output rows per thread
+    const int x = x0 + tx;
+    if (x >= width) return;
+    float column[6][3];
+#pragma unroll
+    for (int r = 0; r < 6; ++r) {
+#pragma unroll
+        for (int k = 0; k < 3; ++k) column[r][k] = tile[ty + r][tx + k];
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const int y = y0 + ty + r;
+        if (y >= height) break;
+        float acc = b;
+#pragma unroll
+        for (int ky = 0; ky < 3; ++ky) {
+#pragma unroll
+            for (int kx = 0; kx < 3; ++kx) acc = __fmaf_rn(w[3 * ky + kx], column[r + ky][kx], acc);
+        }
+        out[(static_cast<std::size_t>(c) * height + y) * width + x] = acc;
+    }
+}
+
 }  // namespace
 
 cudaError_t half_to_float(const std::uint16_t* in, float* out, std::size_t count, cudaStream_t stream) {
@@ -347,6 +398,15 @@ cudaError_t conv_fp32(const float* weights, const float* bias, const float* in, 
                       cudaStream_t stream) {
     const std::size_t count = static_cast<std::size_t>(shape.out_channels) * shape.out_h * shape.out_w;
     if (count == 0) return cudaSuccess;
+    const Window& w = shape.window;
+    if (shape.depthwise && w.kernel_h == 3 && w.kernel_w == 3 && w.stride_y == 1 && w.stride_x == 1 &&
+        w.pad_top == 1 && w.pad_left == 1 && shape.out_h == shape.in_h && shape.out_w == shape.in_w &&
+        shape.out_channels == shape.in_channels && shape.out_channels <= 65535) {
+        const dim3 grid((shape.out_w + dw_tile - 1) / dw_tile, (shape.out_h + dw_tile - 1) / dw_tile,
+                        shape.out_channels);
+        depthwise3x3_kernel<<<grid, 256, 0, stream>>>(weights, bias, in, out, shape.in_h, shape.in_w);
+        return cudaGetLastError();
+    }
     conv_fp32_kernel<<<grid_for(count), threads, 0, stream>>>(weights, bias, in, out, shape);
     return cudaGetLastError();
 }
