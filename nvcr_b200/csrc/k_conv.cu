@@ -57,12 +57,13 @@
 namespace nvcr_sm100::kernels {
 namespace {
 
-constexpr int conv_warps = 11;
+constexpr int conv_warps = 15;
 constexpr int conv_threads = conv_warps * 32;
-constexpr int tma_warp = 4;
-constexpr int mma_warp = 5;
-constexpr int first_producer_warp = 6;
-constexpr int halo_warp = 10;
+constexpr int epilogue_threads = 256;    // warps 0-7: two per TMEM lane quarter, each half of the columns
+constexpr int first_producer_warp = 8;   // warps 8-11
+constexpr int tma_warp = 12;
+constexpr int mma_warp = 13;
+constexpr int halo_warp = 14;
 constexpr int halo_buffers = 2;
 constexpr int max_stages = 8;
 constexpr float round_magic = 12582912.0f;              // 1.5 * 2^23
@@ -494,9 +495,9 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
         }
         for (int b = 0; b < 2; ++b) {
             barrier_init(smem_address(&tail->tmem_full[b]), 1);
-            barrier_init(smem_address(&tail->tmem_empty[b]), tile_positions_m);
+            barrier_init(smem_address(&tail->tmem_empty[b]), epilogue_threads);
             barrier_init(smem_address(&tail->info_full[b]), tile_positions_m);
-            barrier_init(smem_address(&tail->info_empty[b]), tile_positions_m);
+            barrier_init(smem_address(&tail->info_empty[b]), epilogue_threads);
         }
         for (int h = 0; h < halo_buffers; ++h) {
             barrier_init(smem_address(&tail->halo_full[h]), 1);
@@ -848,13 +849,19 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
         }
     } else {
         // ---------------- epilogue: thread <-> TMEM lane <-> position
-        const int row = threadIdx.x;  // warps 0-3
-        const std::uint32_t lane_base = static_cast<std::uint32_t>(warp * 32) << 16;
+        // Warps w and w + 4 read TMEM lane quarter w (positions 32w..32w+31) and
+        // take the first and second half of the tile's 16-column chunks.
+        const int row = threadIdx.x & (tile_positions_m - 1);
+        const int half = warp >> 2;
+        const std::uint32_t lane_base = static_cast<std::uint32_t>((warp & 3) * 32) << 16;
         const std::uint32_t buffer_columns = static_cast<std::uint32_t>(L::accumulators * n_tile);
         constexpr long long high_factor = (WL == 2 ? 256LL : 1LL) * (AL == 2 ? 256LL : 1LL);
         constexpr long long mid_factor = (WL == 2 && AL == 2) ? 256LL : 1LL;
         const int pair_offset = a.chunk_add ? n_tile / 2 : 0;
         const int columns = a.chunk_add ? n_tile / 2 : n_tile;
+        const int half_columns = (columns / 2 + 15) / 16 * 16;
+        const int first_column = half == 0 ? 0 : half_columns;
+        const int last_column = half == 0 ? half_columns : columns;
         const int b = a.d2s_block;
         const int out_w_full = a.out_w * (b > 0 ? b : 1);
         const int out_h_full = a.out_h * (b > 0 ? b : 1);
@@ -955,7 +962,7 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                 }
             };
 
-            for (int j0 = 0; j0 < columns; j0 += 16) {
+            for (int j0 = first_column; j0 < last_column; j0 += 16) {
                 float v[16];
                 values16(j0, v);
                 if (a.chunk_add) {
