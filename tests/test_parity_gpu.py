@@ -373,3 +373,38 @@ def test_intra_decoder_stack_half(cuda, oracle):
     stack = intra_decoder((4, 6), every_tensor=True)
     y_hat = laplace_latent(SeededStream(8), stack.input_shapes[0])
     assert_half_parity(stack.program, [y_hat], oracle, "intra decoder half")
+
+
+def chained_convs_program(stream: SeededStream, bits) -> Program:
+    """Integer convs feeding integer convs: the producer's epilogue writes the
+    consumer's staged source (64 and 32 channels), including through chunk-add
+    and a residual; a 40-channel source (not a multiple of 16) is staged by the
+    prepass instead."""
+    p = Program(name="chained")
+    x = p.add_input("x", 48)
+
+    def w(cout, cin, taps):
+        return stream.uniform(-0.3, 0.3, cout * cin * taps), stream.uniform(-0.1, 0.1, cout)
+
+    a = p.dense_conv(x, 64, *w(64, 48, 9), "a", bits=bits)
+    b = p.conv(a, 128, *w(128, 64, 1), "b", bits=bits)
+    lo = p.unary(OpKind.slice_channels, b, "b.lo", begin=0, end=64)
+    hi = p.unary(OpKind.slice_channels, b, "b.hi", begin=64, end=128)
+    c = p.binary(OpKind.add, lo, hi, "c")
+    d = p.conv(c, 32, *w(32, 64, 1), "d", bits=bits)
+    e = p.binary(OpKind.add, d, p.unary(OpKind.slice_channels, c, "c32", begin=0, end=32), "e")
+    f = p.conv(e, 40, *w(40, 32, 1), "f", bits=bits)
+    g = p.dense_conv(f, 16, *w(16, 40, 9), "g", bits=bits)
+    return p.finish([g, c])
+
+
+@pytest.mark.parametrize("bits", WIDTHS, ids=lambda b: f"w{b[0]}a{b[1]}")
+@pytest.mark.parametrize("half", [False, True], ids=["f32", "f16"])
+def test_chained_integer_convs(cuda, oracle, bits, half):
+    stream = SeededStream(55)
+    program = chained_convs_program(stream, bits)
+    x = stream.tensor(48, 37, 70, 2.0)
+    if half:
+        assert_half_parity(program, [x], oracle, f"chained w{bits[0]}a{bits[1]} half")
+    else:
+        assert_parity(program, [x], oracle, f"chained w{bits[0]}a{bits[1]}")
