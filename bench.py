@@ -127,10 +127,10 @@ class ClockSampler:
 
 
 def distributed():
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return world, rank, local
+    from nvcr_b200.replicas import rank_environment
+
+    env = rank_environment()
+    return env.world, env.rank, env.local
 
 
 def select_layers(spec: str):
@@ -214,15 +214,13 @@ def main():
     import numpy as np
     import torch
 
-    world, rank, local = distributed()
+    from nvcr_b200.replicas import Group, rank_environment
+
+    env = rank_environment()
+    world, rank, local = env.world, env.rank, env.local
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    group = Group(env, "nccl", device)
 
     from nvcr_b200.executor import CudaExecutor
     from nvcr_b200.workloads import layer_input
@@ -276,20 +274,8 @@ def main():
                 ho.copy_(yh, non_blocking=True)
             out_done[i].record(copy_out)
 
-    def barrier():
-        if world > 1:
-            import torch.distributed as dist
-
-            dist.barrier()
-
-    def max_over_ranks(value: float) -> float:
-        if world == 1:
-            return value
-        import torch.distributed as dist
-
-        t = torch.tensor([value], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    barrier = group.barrier
+    max_over_ranks = group.max
 
     def timed(function, steps, profile=False):
         for executor in executors:
@@ -423,10 +409,7 @@ def main():
         print(json.dumps(line), flush=True)
     for executor in executors:
         executor.close()
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.destroy_process_group()
+    group.close()
     return 0
 
 
@@ -443,9 +426,11 @@ def decoder_throughput(args, device, rank, world, max_over_ranks, barrier) -> di
     from nvcr_b200.program import SeededStream
     from nvcr_b200.workloads import intra_decoder, laplace_latent
 
+    from nvcr_b200.replicas import streams_of
+
     stack = intra_decoder()
     streams, frames = 64, 16
-    mine = [s for s in range(streams) if s % world == rank]
+    mine = streams_of(rank, world, streams)
     torch_stream = torch.cuda.Stream(device=device)
     with CudaExecutor.from_program(stack.program, stream=torch_stream.cuda_stream) as executor:
         latents = [torch.from_numpy(laplace_latent(SeededStream(5000 + s), stack.input_shapes[0])

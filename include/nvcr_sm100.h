@@ -151,6 +151,13 @@ int nvcr_sm100_run_host(nvcr_sm100_executor* executor, const nvcr_sm100_tensor* 
  * occurred or a device-side bounded wait gave up. */
 int nvcr_sm100_synchronize(nvcr_sm100_executor* executor);
 
+/* Failure-detection self-test (no counterpart in the reference): enqueues on the
+ * executor's stream one device wait on a barrier that nothing completes, bounded
+ * by limit_ms (1..4000), which gives up the way a kernel's wait does. The next
+ * nvcr_sm100_synchronize returns NVCR_SM100_BACKEND_ERROR ("a device-side wait
+ * gave up") and clears the status; the executor and its CUDA context stay usable. */
+int nvcr_sm100_test_wait_timeout(nvcr_sm100_executor* executor, unsigned int limit_ms);
+
 /* The stream all work is ordered on (a cudaStream_t). */
 void* nvcr_sm100_stream(const nvcr_sm100_executor* executor);
 

@@ -312,6 +312,15 @@ int nvcr_sm100_synchronize(nvcr_sm100_executor* executor) {
     });
 }
 
+int nvcr_sm100_test_wait_timeout(nvcr_sm100_executor* executor, unsigned int limit_ms) {
+    return guarded([&] {
+        if (executor == nullptr) return report(Code::invalid_argument, "null executor");
+        auto status = executor->executor->test_wait_timeout(limit_ms);
+        if (!status) return report(status.error());
+        return succeed();
+    });
+}
+
 void* nvcr_sm100_stream(const nvcr_sm100_executor* executor) {
     return executor == nullptr ? nullptr : static_cast<void*>(executor->executor->stream());
 }

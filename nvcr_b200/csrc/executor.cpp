@@ -1073,6 +1073,14 @@ Status Executor::run_host(const std::vector<TensorView>& inputs, const std::vect
     return execute(inputs, outputs, Boundary::host);
 }
 
+Status Executor::test_wait_timeout(unsigned int limit_ms) {
+    if (limit_ms == 0 || limit_ms > 4000) return fail(Code::invalid_argument, "wait limit must be 1..4000 ms");
+    const cudaError_t status =
+        kernels::wait_timeout(static_cast<unsigned long long>(limit_ms) * 1000000ull, status_, stream_);
+    if (status != cudaSuccess) return cuda_error("wait timeout launch", status);
+    return Ok{};
+}
+
 Status Executor::synchronize() {
     cudaError_t status = cudaStreamSynchronize(stream_);
     if (status != cudaSuccess) return cuda_error("cudaStreamSynchronize", status);

@@ -62,6 +62,9 @@ public:
                                  void* workspace, std::size_t bytes);
     // Waits for the stream and reports a device-side wait that gave up.
     Status synchronize();
+    // Diagnostics: enqueues a device wait that runs out after `limit_ms` and
+    // sets this executor's status word, as a kernel whose wait gives up does.
+    Status test_wait_timeout(unsigned int limit_ms);
 
     int launches_last_run() const { return launches_; }
     std::size_t workspace_bytes() const { return arena_bytes_; }

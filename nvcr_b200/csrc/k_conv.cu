@@ -1213,6 +1213,23 @@ cudaError_t stage_source(const void* in, int source_half, int channels, int c_pa
     return cudaGetLastError();
 }
 
+namespace {
+__global__ void wait_timeout_kernel(unsigned long long limit_ns, unsigned int* status) {
+    __shared__ unsigned long long never;
+    if (threadIdx.x == 0) {
+        barrier_init(smem_address(&never), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        barrier_wait_for(smem_address(&never), 0u, status, limit_ns);  // phase 0 never completes
+    }
+}
+}  // namespace
+
+cudaError_t wait_timeout(unsigned long long limit_ns, unsigned int* status, cudaStream_t stream) {
+    if (limit_ns > 4000000000ull) return cudaErrorInvalidValue;
+    wait_timeout_kernel<<<1, 32, 0, stream>>>(limit_ns, status);
+    return cudaGetLastError();
+}
+
 cudaError_t fused_conv(const CUtensorMap& b_high, const CUtensorMap& b_low, const CUtensorMap& halo, int weight_limbs,
                        int activation_limbs, const FusedConvArgs& args, cudaStream_t stream) {
     static int sm_count = [] {

@@ -110,4 +110,9 @@ cudaError_t encode_halo_map(CUtensorMap* map, const void* base, int half, std::u
 cudaError_t encode_int8_map(CUtensorMap* map, const void* base, std::uint64_t rows, std::uint64_t row_bytes,
                             std::uint32_t box_rows);
 
+// Diagnostics: one thread waits on an mbarrier that nothing arrives on, with the
+// kernels' bounded-wait loop and a limit of `limit_ns`, then sets bit 0 of
+// `status` and returns (the path every kernel takes when a wait runs out).
+cudaError_t wait_timeout(unsigned long long limit_ns, unsigned int* status, cudaStream_t stream);
+
 }  // namespace nvcr_sm100::kernels

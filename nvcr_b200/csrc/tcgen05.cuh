@@ -44,21 +44,27 @@ static __device__ __forceinline__ bool barrier_try_wait(std::uint32_t bar, std::
     return done != 0;
 }
 
-// Waits for the phase of `parity` to complete; false (and status bit 0) after
-// about two seconds.
-static __device__ bool barrier_wait(std::uint32_t bar, std::uint32_t parity, unsigned int* status) {
+// Waits for the phase of `parity` to complete; false (and status bit 0) once
+// `limit_ns` of the global timer have passed.
+static __device__ bool barrier_wait_for(std::uint32_t bar, std::uint32_t parity, unsigned int* status,
+                                        unsigned long long limit_ns) {
     if (barrier_try_wait(bar, parity)) return true;
     const unsigned long long start = global_timer();
     for (unsigned int spin = 0;; ++spin) {
         if (barrier_try_wait(bar, parity)) return true;
         if ((spin & 63u) == 63u) {
-            if (global_timer() - start > wait_limit_ns) {
+            if (global_timer() - start > limit_ns) {
                 atomicOr(status, 1u);
                 return false;
             }
             __nanosleep(128);
         }
     }
+}
+
+// The same with the kernels' limit of about two seconds.
+static __device__ bool barrier_wait(std::uint32_t bar, std::uint32_t parity, unsigned int* status) {
+    return barrier_wait_for(bar, parity, status, wait_limit_ns);
 }
 
 static __device__ __forceinline__ void tma_load_2d(std::uint32_t dst, const CUtensorMap* map, std::uint32_t bar, int x, int y) {

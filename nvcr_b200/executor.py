@@ -73,7 +73,7 @@ EXPORTS = [
     "nvcr_sm100_set_profiling", "nvcr_sm100_profile", "nvcr_sm100_program_load", "nvcr_sm100_program_load_memory",
     "nvcr_sm100_program_destroy", "nvcr_sm100_program_tensor_count", "nvcr_sm100_program_tensor_info",
     "nvcr_sm100_program_infer_output_extents", "nvcr_sm100_executor_create_from_program",
-    "nvcr_sm100_run_half_static",
+    "nvcr_sm100_run_half_static", "nvcr_sm100_test_wait_timeout",
 ]
 
 _lib: ctypes.CDLL | None = None
@@ -109,6 +109,7 @@ def library() -> ctypes.CDLL:
         "nvcr_sm100_run_float": (ctypes.c_int, [vp, tp, sz, tp, sz]),
         "nvcr_sm100_run_host": (ctypes.c_int, [vp, tp, sz, tp, sz]),
         "nvcr_sm100_synchronize": (ctypes.c_int, [vp]),
+        "nvcr_sm100_test_wait_timeout": (ctypes.c_int, [vp, ctypes.c_uint]),
         "nvcr_sm100_stream": (vp, [vp]),
         "nvcr_sm100_last_launch_count": (ctypes.c_int, [vp]),
         "nvcr_sm100_workspace_bytes": (sz, [vp]),
@@ -357,6 +358,11 @@ class CudaExecutor:
 
     def synchronize(self) -> None:
         _check(library().nvcr_sm100_synchronize(self._handle))
+
+    def test_wait_timeout(self, limit_ms: int) -> None:
+        """Enqueues a device wait that gives up after `limit_ms` (failure-detection
+        self-test); the next synchronize() raises backend_error."""
+        _check(library().nvcr_sm100_test_wait_timeout(self._handle, limit_ms))
 
     def set_profiling(self, enabled: bool) -> None:
         _check(library().nvcr_sm100_set_profiling(self._handle, int(enabled)))
