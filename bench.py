@@ -441,7 +441,7 @@ def decoder_throughput(args, device, rank, world, max_over_ranks, barrier) -> di
         def decode(latent):
             executor.run_half({"y_hat": latent}, {"frame": frame})
 
-        def timed(count, work):
+        def timed(count, work, executors=(executor,)):
             barrier()
             torch.cuda.synchronize(device)
             start = torch.cuda.Event(enable_timing=True)
@@ -451,7 +451,8 @@ def decoder_throughput(args, device, rank, world, max_over_ranks, barrier) -> di
                 work(i)
             end.record(torch_stream)
             torch.cuda.synchronize(device)
-            executor.synchronize()
+            for e in executors:
+                e.synchronize()
             barrier()
             return start.elapsed_time(end)
 
@@ -462,17 +463,57 @@ def decoder_throughput(args, device, rank, world, max_over_ranks, barrier) -> di
         frame_ms = timed(single, lambda i: decode(latents[0])) / single
         shard_ms = max_over_ranks(timed(len(mine) * frames, lambda i: decode(latents[i // frames])))
         launches = executor.launches
+    p_frames = p_frame_sequence(device, torch_stream, timed)
     return {
         "workload": "synthetic DCVC-RT intra decoder (i.dec topology: subpel up + 14 DepthConvBlocks at "
                     "256 ch, 1/8 res + d2s(8) head), 1088x1920 frame, w8a8, FP16 boundary",
         "ops_per_frame": stack.ops,
         "config3": {"ms_per_frame": round(frame_ms, 3), "frames_per_s": round(1000.0 / frame_ms, 1),
                     "tops": round(stack.ops / (frame_ms / 1000.0) / 1e12, 1), "gpu_launches_per_frame": launches},
+        "config4": p_frames,
         "config5": {"streams": streams, "frames_per_stream": frames, "n_gpus": world, "ms": round(shard_ms, 2),
                     "frames_per_s": round(streams * frames / (shard_ms / 1000.0), 1),
                     "tops_per_gpu": round(streams * frames * stack.ops / world / (shard_ms / 1000.0) / 1e12, 1),
                     "scaling": "strong (1024 frames split round-robin by stream)"},
     }
+
+
+def p_frame_sequence(device, torch_stream, timed) -> dict:
+    """BASELINE config 4 on the synthetic stacks: 1280x720 (padded to 768x1280), GOP
+    30 = one I-frame (intra decoder with a 64-channel feature output) and 29
+    P-frames whose temporal context is the previous frame's feature, run in order
+    on one GPU with one executor per mode (plans and scratch reused); FP16 stage
+    boundary, everything device-resident."""
+    import numpy as np
+    import torch
+
+    from nvcr_b200.executor import CudaExecutor
+    from nvcr_b200.program import SeededStream
+    from nvcr_b200.workloads import inter_decoder, intra_decoder, laplace_latent
+
+    intra = intra_decoder((48, 80), feature_channels=64)
+    inter = inter_decoder((48, 80))
+    gop = 30
+    with CudaExecutor.from_program(intra.program, stream=torch_stream.cuda_stream) as first, \
+            CudaExecutor.from_program(inter.program, stream=torch_stream.cuda_stream) as rest:
+        latents = [torch.from_numpy(laplace_latent(SeededStream(6000 + f), (256, 48, 80)).astype(np.float16))
+                   .to(device) for f in range(gop)]
+        frame = torch.empty((3, 768, 1280), dtype=torch.float16, device=device)
+        features = [torch.empty((64, 96, 160), dtype=torch.float16, device=device) for _ in range(2)]
+
+        def decode(f):
+            if f == 0:
+                first.run_half({"y_hat": latents[0]}, {"frame": frame, "feature": features[0]})
+            else:
+                rest.run_half({"y_hat": latents[f], "context": features[(f - 1) % 2]},
+                              {"frame": frame, "feature": features[f % 2]})
+
+        for f in range(3):
+            decode(f)
+        ms = timed(gop, decode, (first, rest))
+    ops = intra.ops + (gop - 1) * inter.ops
+    return {"frames": gop, "resolution": "768x1280 (720p padded to x64)", "ms": round(ms, 3),
+            "frames_per_s": round(gop / (ms / 1000.0), 1), "tops": round(ops / (ms / 1000.0) / 1e12, 1)}
 
 
 if __name__ == "__main__":

@@ -162,7 +162,7 @@ class Stack:
 
 def intra_decoder(latent_hw: tuple[int, int] = (68, 120), *, channels: int = DECODER_CHANNELS,
                   blocks: int = DECODER_BLOCKS, bits=(8, 8), seed: int = 300,
-                  every_tensor: bool = False) -> Stack:
+                  every_tensor: bool = False, feature_channels: int = 0) -> Stack:
     """a DCVC-RT-architecture intra decoder. y_hat
     [256, h, w] (1/16 of the frame) -> dec_1.0 (SubpelConv2x up + DepthConvBlock)
     -> dec_1.1..blocks (DepthConvBlocks at 1/8) -> dec_2 (DepthConvBlock with an
@@ -186,10 +186,47 @@ def intra_decoder(latent_hw: tuple[int, int] = (68, 120), *, channels: int = DEC
     taps.append(x)
     head = b.pointwise(x, 3 * 64, "i.dec.head")
     frame = p.unary(OpKind.depth_to_space, head, "frame", block=8)
-    p.finish((taps + [frame]) if every_tensor else [frame])
+    outputs = (taps + [frame]) if every_tensor else [frame]
+    if feature_channels:
+        # The reconstructed feature a following P-frame takes as temporal context.
+        outputs.append(b.pointwise(x, feature_channels, "feature"))
+    p.finish(outputs)
     h, w = latent_hw
     ops = up_ops * h * w + b.ops * (2 * h) * (2 * w)
     return Stack("config3_intra_decoder", p, [(256, h, w)], ops)
+
+
+def inter_decoder(latent_hw: tuple[int, int] = (48, 80), *, channels: int = DECODER_CHANNELS,
+                  context_channels: int = 64, blocks: int = 4, bits=(8, 8), seed: int = 400,
+                  every_tensor: bool = False) -> Stack:
+    """BASELINE config 4's P-frame decoder, synthetic with the reference's P-side
+    names (p.decoder.*, p.recon_generation_net.*, p.feature_adaptor_p): y_hat
+    [256, h, w] -> SubpelConv2x up to 1/8 -> concat the previous frame's feature
+    [64, 2h, 2w] (temporal context) -> DepthConvBlock with an adaptor -> `blocks`
+    DepthConvBlocks -> the next feature (1x1 to 64) and the frame (1x1 head,
+    depth_to_space(8))."""
+    stream = SeededStream(seed)
+    p = Program(name="inter_decoder")
+    b = _StackBuilder(p, stream, bits)
+    y_hat = p.add_input("y_hat", 256)
+    context = p.add_input("context", context_channels)
+    x = b.subpel_up(y_hat, channels, "p.decoder.up")
+    up_ops = b.ops
+    b.ops = 0.0
+    x = p.binary(OpKind.concat, x, context, "p.decoder.context")
+    taps = []
+    x = b.depth_conv_block(x, channels, "p.decoder.conv1.0", adaptor=True)
+    taps.append(x)
+    for i in range(blocks):
+        x = b.depth_conv_block(x, channels, f"p.recon_generation_net.conv.{i}")
+        taps.append(x)
+    feature = b.pointwise(x, context_channels, "feature")
+    head = b.pointwise(x, 3 * 64, "p.recon_generation_net.head")
+    frame = p.unary(OpKind.depth_to_space, head, "frame", block=8)
+    p.finish((taps + [frame, feature]) if every_tensor else [frame, feature])
+    h, w = latent_hw
+    ops = up_ops * h * w + b.ops * (2 * h) * (2 * w)
+    return Stack("config4_inter_decoder", p, [(256, h, w), (context_channels, 2 * h, 2 * w)], ops)
 
 
 def laplace_latent(stream: SeededStream, shape: tuple[int, int, int], scale: float = 4.0) -> np.ndarray:

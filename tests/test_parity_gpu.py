@@ -408,3 +408,39 @@ def test_chained_integer_convs(cuda, oracle, bits, half):
         assert_half_parity(program, [x], oracle, f"chained w{bits[0]}a{bits[1]} half")
     else:
         assert_parity(program, [x], oracle, f"chained w{bits[0]}a{bits[1]}")
+
+
+def test_p_frame_sequence(cuda, oracle):
+    """BASELINE config 4's shape of work, small: an I-frame (intra decoder with a
+    feature output) then P-frames whose temporal context is the previous frame's
+    feature, each P-frame's every block output compared; one executor per mode
+    reused across frames (its plans and scratch stay)."""
+    from nvcr_b200.workloads import inter_decoder, intra_decoder, laplace_latent
+
+    intra = intra_decoder((3, 5), feature_channels=64)
+    inter = inter_decoder((3, 5), every_tensor=True)
+    latents = [laplace_latent(SeededStream(60 + f), (256, 3, 5)) for f in range(4)]
+    with CudaExecutor.from_program(intra.program) as first, CudaExecutor.from_program(inter.program) as rest:
+        got = first.run([latents[0]])
+        want = oracle.run(intra.program, [latents[0]])
+        assert all(count_differing(g, e) == 0 for g, e in zip(got, want))
+        context_got, context_want = got[-1], want[-1]
+        for f in range(1, 4):
+            got = rest.run([latents[f], context_got])
+            want = oracle.run(inter.program, [latents[f], context_want])
+            for index, (g, e) in enumerate(zip(got, want)):
+                assert count_differing(g, e) == 0, f"P-frame {f} output {index}"
+            context_got, context_want = got[-1], want[-1]
+
+
+def test_p_frame_sequence_half(cuda, oracle):
+    """The same through run_half: the feature crosses each stage boundary in FP16."""
+    from nvcr_b200.workloads import inter_decoder, laplace_latent
+
+    inter = inter_decoder((4, 6), every_tensor=True)
+    stream = SeededStream(70)
+    context = stream.tensor(64, 8, 12, 2.0).astype(np.float16).astype(np.float32)
+    for f in range(2):
+        latent = laplace_latent(SeededStream(80 + f), (256, 4, 6))
+        assert_half_parity(inter.program, [latent, context], oracle, f"P-frame {f} half")
+        context = run_half_gpu(inter.program, [latent, context])[-1]
