@@ -1,6 +1,7 @@
 #include "executor.hpp"
 
 #include <algorithm>
+#include <functional>
 #include <climits>
 #include <cstring>
 #include <limits>
@@ -206,6 +207,7 @@ Result<std::unique_ptr<Executor>> Executor::create(Program program, cudaStream_t
 
 Executor::~Executor() {
     if (stream_ != nullptr) cudaStreamSynchronize(stream_);
+    clear_graphs();
     for (auto& conv : convs_) cudaFree(conv.allocation);
     for (auto event : events_) cudaEventDestroy(event);
     cudaFree(arena_);
@@ -727,9 +729,10 @@ Result<Executor::Plan*> Executor::plan_for(const std::vector<Extent>& input_exte
 Status Executor::ensure_arena(std::size_t bytes) {
     if (bytes <= arena_bytes_ && arena_ != nullptr) return Ok{};
     if (arena_ != nullptr) {
-        // In-flight work may still use the old arena.
+        // In-flight work may still use the old arena; graphs captured on it go.
         const cudaError_t synced = cudaStreamSynchronize(stream_);
         if (synced != cudaSuccess) return cuda_error("cudaStreamSynchronize", synced);
+        clear_graphs();
         cudaFree(arena_);
         arena_ = nullptr;
         arena_bytes_ = 0;
@@ -957,79 +960,146 @@ Status Executor::execute(const std::vector<TensorView>& inputs, const std::vecto
         run_base_ = static_cast<std::uint8_t*>(workspace);
     }
 
-    launches_ = 0;
-    run_started_ = false;
-    auto* base = run_base_;
-    // Device runs: integer convs stage their program inputs straight from the
-    // caller's buffers and store outputs that nothing reads straight into them.
-    const bool device = boundary != Boundary::host;
-    run_inputs_.assign(program_.tensor_names.size(), Direct{});
-    run_outputs_.assign(steps_.size(), Direct{});
-    if (device) {
+    // The launch sequence of this run; replayed from a CUDA graph when the same
+    // plan, workspace and tensors come again on a device boundary.
+    auto enqueue = [&]() -> Status {
+        launches_ = 0;
+        run_started_ = false;
+        auto* base = run_base_;
+        // Device runs: integer convs stage their program inputs straight from the
+        // caller's buffers and store outputs that nothing reads straight into them.
+        const bool device = boundary != Boundary::host;
+        run_inputs_.assign(program_.tensor_names.size(), Direct{});
+        run_outputs_.assign(steps_.size(), Direct{});
+        if (device) {
+            for (std::size_t slot = 0; slot < program_.inputs.size(); ++slot) {
+                run_inputs_[program_.inputs[slot]] = Direct{input_views[slot]->data, boundary == Boundary::half};
+            }
+            for (std::size_t slot = 0; slot < program_.outputs.size(); ++slot) {
+                if (output_step_[slot] < 0) continue;
+                run_outputs_[static_cast<std::size_t>(output_step_[slot])] =
+                    Direct{output_views[slot]->data, boundary == Boundary::half};
+            }
+        }
+        auto started = mark("", "", 0.0, 0.0);
+        if (!started) return started;
+        double input_bytes = 0.0;
         for (std::size_t slot = 0; slot < program_.inputs.size(); ++slot) {
-            run_inputs_[program_.inputs[slot]] = Direct{input_views[slot]->data, boundary == Boundary::half};
+            const auto id = program_.inputs[slot];
+            if (device && input_conv_only_[slot]) continue;
+            float* target = reinterpret_cast<float*>(base + plan.offsets[id]);
+            const std::size_t count = plan.extents[id].count();
+            input_bytes += static_cast<double>(count) * 6.0;
+            cudaError_t status;
+            if (boundary == Boundary::half) {
+                status = kernels::half_to_float(static_cast<const std::uint16_t*>(input_views[slot]->data), target, count,
+                                                stream_);
+                ++launches_;
+            } else {
+                status = cudaMemcpyAsync(target, input_views[slot]->data, count * sizeof(float),
+                                         boundary == Boundary::host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice,
+                                         stream_);
+            }
+            if (status != cudaSuccess) return cuda_error("input conversion", status);
         }
+        // Segments only for conversions that ran (staged inputs and direct outputs have none).
+        if (input_bytes > 0.0) {
+            auto marked = mark("inputs", boundary == Boundary::half ? "half_to_float" : "copy", 0.0, input_bytes);
+            if (!marked) return marked;
+        }
+        for (std::size_t s = 0; s < steps_.size(); ++s) {
+            auto launched = launch_step(steps_[s], plan, s);
+            if (!launched) return launched;
+        }
+        double output_bytes = 0.0;
         for (std::size_t slot = 0; slot < program_.outputs.size(); ++slot) {
-            if (output_step_[slot] < 0) continue;
-            run_outputs_[static_cast<std::size_t>(output_step_[slot])] =
-                Direct{output_views[slot]->data, boundary == Boundary::half};
+            const auto id = program_.outputs[slot];
+            if (device && output_step_[slot] >= 0) continue;
+            const float* source = reinterpret_cast<const float*>(base + plan.offsets[id]);
+            const std::size_t count = plan.extents[id].count();
+            output_bytes += static_cast<double>(count) * 6.0;
+            cudaError_t status;
+            if (boundary == Boundary::half) {
+                status = kernels::float_to_half(source, static_cast<std::uint16_t*>(output_views[slot]->data), count,
+                                                stream_);
+                ++launches_;
+            } else {
+                status = cudaMemcpyAsync(output_views[slot]->data, source, count * sizeof(float),
+                                         boundary == Boundary::host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice,
+                                         stream_);
+            }
+            if (status != cudaSuccess) return cuda_error("output conversion", status);
         }
-    }
-    auto started = mark("", "", 0.0, 0.0);
-    if (!started) return started;
-    double input_bytes = 0.0;
-    for (std::size_t slot = 0; slot < program_.inputs.size(); ++slot) {
-        const auto id = program_.inputs[slot];
-        if (device && input_conv_only_[slot]) continue;
-        float* target = reinterpret_cast<float*>(base + plan.offsets[id]);
-        const std::size_t count = plan.extents[id].count();
-        input_bytes += static_cast<double>(count) * 6.0;
-        cudaError_t status;
-        if (boundary == Boundary::half) {
-            status = kernels::half_to_float(static_cast<const std::uint16_t*>(input_views[slot]->data), target, count,
-                                            stream_);
-            ++launches_;
-        } else {
-            status = cudaMemcpyAsync(target, input_views[slot]->data, count * sizeof(float),
-                                     boundary == Boundary::host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice,
-                                     stream_);
+        if (output_bytes > 0.0) {
+            auto marked = mark("outputs", boundary == Boundary::half ? "float_to_half" : "copy", 0.0, output_bytes);
+            if (!marked) return marked;
         }
-        if (status != cudaSuccess) return cuda_error("input conversion", status);
+        return Ok{};
+    };
+    if (boundary != Boundary::host && !profiling_) {
+        GraphKey key{&plan, run_base_, static_cast<int>(boundary), {}};
+        for (const auto* view : input_views) key.tensors.push_back(view->data);
+        for (const auto* view : output_views) key.tensors.push_back(view->data);
+        auto replayed = run_graph(key, enqueue);
+        if (replayed) return Ok{};
+        if (replayed.error().code != Code::try_again) return replayed.error();
     }
-    // Segments only for conversions that ran (staged inputs and direct outputs have none).
-    if (input_bytes > 0.0) {
-        auto marked = mark("inputs", boundary == Boundary::half ? "half_to_float" : "copy", 0.0, input_bytes);
-        if (!marked) return marked;
-    }
-    for (std::size_t s = 0; s < steps_.size(); ++s) {
-        auto launched = launch_step(steps_[s], plan, s);
-        if (!launched) return launched;
-    }
-    double output_bytes = 0.0;
-    for (std::size_t slot = 0; slot < program_.outputs.size(); ++slot) {
-        const auto id = program_.outputs[slot];
-        if (device && output_step_[slot] >= 0) continue;
-        const float* source = reinterpret_cast<const float*>(base + plan.offsets[id]);
-        const std::size_t count = plan.extents[id].count();
-        output_bytes += static_cast<double>(count) * 6.0;
-        cudaError_t status;
-        if (boundary == Boundary::half) {
-            status = kernels::float_to_half(source, static_cast<std::uint16_t*>(output_views[slot]->data), count,
-                                            stream_);
-            ++launches_;
-        } else {
-            status = cudaMemcpyAsync(output_views[slot]->data, source, count * sizeof(float),
-                                     boundary == Boundary::host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice,
-                                     stream_);
-        }
-        if (status != cudaSuccess) return cuda_error("output conversion", status);
-    }
-    if (output_bytes > 0.0) {
-        auto marked = mark("outputs", boundary == Boundary::half ? "float_to_half" : "copy", 0.0, output_bytes);
-        if (!marked) return marked;
-    }
+    auto enqueued = enqueue();
+    if (!enqueued) return enqueued;
     if (boundary == Boundary::host) return synchronize();
     return Ok{};
+}
+
+// Runs `enqueue` through a cached CUDA graph for `key`: the first sighting of a
+// key runs normally (all lazy set-up happens there) and returns try_again; the
+// second is captured (thread-local mode) and replayed; later ones replay. A
+// stream the caller is itself capturing is left alone (try_again).
+Status Executor::run_graph(const GraphKey& key, const std::function<Status()>& enqueue) {
+    cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream_, &capturing) != cudaSuccess || capturing != cudaStreamCaptureStatusNone) {
+        cudaGetLastError();
+        return fail(Code::try_again, "stream is capturing");
+    }
+    auto found = graphs_.find(key);
+    if (found == graphs_.end()) {
+        if (graphs_.size() >= 32) clear_graphs();
+        graphs_.emplace(key, CachedGraph{});
+        return fail(Code::try_again, "first run of this plan and tensors");
+    }
+    CachedGraph& cached = found->second;
+    if (cached.exec == nullptr) {
+        cudaError_t status = cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal);
+        if (status != cudaSuccess) return cuda_error("cudaStreamBeginCapture", status);
+        Status enqueued = enqueue();
+        cudaGraph_t graph = nullptr;
+        status = cudaStreamEndCapture(stream_, &graph);
+        if (!enqueued) {
+            if (graph != nullptr) cudaGraphDestroy(graph);
+            return enqueued;
+        }
+        if (status != cudaSuccess || graph == nullptr) {
+            if (graph != nullptr) cudaGraphDestroy(graph);
+            return cuda_error("cudaStreamEndCapture", status);
+        }
+        status = cudaGraphInstantiate(&cached.exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (status != cudaSuccess) {
+            cached.exec = nullptr;
+            return cuda_error("cudaGraphInstantiate", status);
+        }
+        cached.launches = launches_;
+    }
+    const cudaError_t status = cudaGraphLaunch(cached.exec, stream_);
+    if (status != cudaSuccess) return cuda_error("cudaGraphLaunch", status);
+    launches_ = cached.launches;
+    return Ok{};
+}
+
+void Executor::clear_graphs() {
+    for (auto& [key, cached] : graphs_) {
+        if (cached.exec != nullptr) cudaGraphExecDestroy(cached.exec);
+    }
+    graphs_.clear();
 }
 
 // Records an event on the stream when profiling; the segment since the

@@ -20,7 +20,9 @@
 
 #include <cuda_runtime.h>
 
+#include <functional>
 #include <map>
+#include <tuple>
 #include <memory>
 #include <optional>
 #include <string>
@@ -89,6 +91,23 @@ private:
                    void* workspace = nullptr, std::size_t workspace_bytes = 0);
 
     Status launch_step(const Step& step, Plan& plan, std::size_t index);
+    struct GraphKey {
+        const Plan* plan;
+        const void* base;
+        int boundary;
+        std::vector<const void*> tensors;
+        bool operator<(const GraphKey& other) const {
+            return std::tie(plan, base, boundary, tensors) <
+                std::tie(other.plan, other.base, other.boundary, other.tensors);
+        }
+    };
+    struct CachedGraph {
+        cudaGraphExec_t exec{nullptr};
+        int launches{0};
+    };
+    Status run_graph(const GraphKey& key, const std::function<Status()>& enqueue);
+    void clear_graphs();
+    std::map<GraphKey, CachedGraph> graphs_;
     Status mark(const std::string& label, const std::string& kernel, double ops, double bytes);
 
     Program program_;
