@@ -54,6 +54,7 @@ def parse_args():
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--no-cpu-baseline", action="store_true", help="skip the reference CPU timing")
     parser.add_argument("--layers", type=str, default="", help="comma-separated layer indices (default: all)")
+    parser.add_argument("--no-decoder", action="store_true", help="skip the config 3-5 decoder measurements")
     return parser.parse_args()
 
 
@@ -389,7 +390,7 @@ def main():
             cpu_baseline = {"value": None, "unit": "TOPS", "cores": 0, "kind": "reference",
                             "sample": f"unavailable: {error}"}
 
-    decoder = decoder_throughput(args, device, rank, world, max_over_ranks, barrier)
+    decoder = None if args.no_decoder else decoder_throughput(args, device, rank, world, max_over_ranks, barrier)
 
     if rank == 0:
         line = {

@@ -357,6 +357,27 @@ __device__ __noinline__ Sixteen wsilu16(Sixteen x, float k) {
     return x;
 }
 
+// Quotient and remainder by a divisor fixed for the kernel: a float reciprocal
+// and one correction step, exact for 0 <= n < 2^22 (tile indices are far below).
+struct Divider {
+    int d;
+    float inverse;
+    __device__ explicit Divider(int divisor) : d(divisor), inverse(1.0f / static_cast<float>(divisor)) {}
+    __device__ __forceinline__ int divide(int n, int& remainder) const {
+        int q = __float2int_rz(__fmul_rn(__int2float_rn(n), inverse));
+        int r = n - q * d;
+        if (r < 0) {
+            --q;
+            r += d;
+        } else if (r >= d) {
+            ++q;
+            r -= d;
+        }
+        remainder = r;
+        return q;
+    }
+};
+
 // How one position's activations are quantised in a tile.
 enum QuantMode : int { quant_skip = 0, quant_half = 1, quant_float = 2, quant_float_clamp = 3, quant_exact = 4 };
 
@@ -472,6 +493,8 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
     const int lane = threadIdx.x & 31;
     const int total_tiles = a.p_tiles * a.n_tiles;
     const int k_blocks = a.k_blocks;
+    const Divider by_n_tiles(a.n_tiles);
+    const Divider by_tiles_x(a.tiles_x);
 
     for (int i = threadIdx.x; i < all_columns; i += conv_threads) {
         column_scale[i] = a.scales[i];
@@ -524,7 +547,9 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
             // Resident weights: the first tile's pass loads every K block into its own stage, once.
             const int last = a.b_resident ? static_cast<int>(blockIdx.x) + 1 : total_tiles;
             for (int t = blockIdx.x; t < last && ok; t += gridDim.x) {
-                const int n0 = (t % a.n_tiles) * n_tile;
+                int n_index;
+                by_n_tiles.divide(t, n_index);
+                const int n0 = n_index * n_tile;
                 for (int kb = 0; kb < k_blocks; ++kb, ++g) {
                     const int s = static_cast<int>(g % b_stages);
                     const std::uint32_t phase = (g / b_stages) & 1u;
@@ -625,9 +650,9 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
             const std::uint32_t box_bytes =
                 static_cast<std::uint32_t>(a.record_bytes) * static_cast<std::uint32_t>(a.halo_box_w * a.halo_rows);
             for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-                const int p_tile = t / a.n_tiles;
-                const int ty = p_tile / a.tiles_x;
-                const int tx = p_tile - ty * a.tiles_x;
+                int n_index, tx;
+                const int p_tile = by_n_tiles.divide(t, n_index);
+                const int ty = by_tiles_x.divide(p_tile, tx);
                 const int y0 = ty * a.patch_h * a.window.stride_y - a.window.pad_top;
                 const int x0 = tx * a.patch_w * a.window.stride_x - a.window.pad_left;
                 for (int g = 0; g < a.groups; ++g, ++job) {
@@ -678,10 +703,11 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
         constexpr int window_taps = 9;
         const bool small_window = a.window.kernel_h <= 3 && kernel_w <= 3;
         auto window_loads = [&](int t, float (&m)[window_taps]) {
-            const int p_tile = t / a.n_tiles;
-            const int ty = p_tile / a.tiles_x;
+            int n_index, tx;
+            const int p_tile = by_n_tiles.divide(t, n_index);
+            const int ty = by_tiles_x.divide(p_tile, tx);
             const int oy = ty * a.patch_h + py;
-            const int ox = (p_tile - ty * a.tiles_x) * a.patch_w + px;
+            const int ox = tx * a.patch_w + px;
             const int iy0 = oy * a.window.stride_y - a.window.pad_top;
             const int ix0 = ox * a.window.stride_x - a.window.pad_left;
             const bool real = oy < a.out_h && ox < a.out_w;
@@ -701,9 +727,9 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
         float next_window[window_taps];
         if (small_window && static_cast<int>(blockIdx.x) < total_tiles) window_loads(blockIdx.x, next_window);
         for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++local) {
-            const int p_tile = t / a.n_tiles;
-            const int ty = p_tile / a.tiles_x;
-            const int tx = p_tile - ty * a.tiles_x;
+            int n_index, tx;
+            const int p_tile = by_n_tiles.divide(t, n_index);
+            const int ty = by_tiles_x.divide(p_tile, tx);
             const int oy = ty * a.patch_h + py;
             const int ox = tx * a.patch_w + px;
             const bool real = oy < a.out_h && ox < a.out_w;
@@ -863,6 +889,8 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
         const int first_column = half == 0 ? 0 : half_columns;
         const int last_column = half == 0 ? half_columns : columns;
         const int b = a.d2s_block;
+        const int patch_y = row / a.patch_w;
+        const int patch_x = row - patch_y * a.patch_w;
         const int out_w_full = a.out_w * (b > 0 ? b : 1);
         const int out_h_full = a.out_h * (b > 0 ? b : 1);
         int local = 0;
@@ -882,11 +910,11 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
             const int exponent = tail->exponents[info][row];
             const long long column = tail->column_terms[info][row];
             barrier_arrive(smem_address(&tail->info_empty[info]));
-            const int p_tile = t / a.n_tiles;
-            const int n_index = t % a.n_tiles;
-            const int ty = p_tile / a.tiles_x;
-            const int y = ty * a.patch_h + row / a.patch_w;
-            const int x = (p_tile - ty * a.tiles_x) * a.patch_w + row % a.patch_w;
+            int n_index, tx;
+            const int p_tile = by_n_tiles.divide(t, n_index);
+            const int ty = by_tiles_x.divide(p_tile, tx);
+            const int y = ty * a.patch_h + patch_y;
+            const int x = tx * a.patch_w + patch_x;
             const bool real = y < a.out_h && x < a.out_w;
             const int p = real ? y * a.out_w + x : 0;
             const int physical0 = n_index * n_tile;
@@ -1087,7 +1115,7 @@ bool valid_geometry(const FusedConvArgs& a, int accumulators) {
         a.record_bytes == 128;
     const bool aligned = (reinterpret_cast<std::uintptr_t>(a.scales) & 15u) == 0 &&
         (reinterpret_cast<std::uintptr_t>(a.bias) & 15u) == 0;
-    return aligned && a.n_tile >= 16 && a.n_tile <= 256 && a.n_tile % 16 == 0 &&
+    return aligned && static_cast<long long>(a.p_tiles) * a.n_tiles < (1LL << 22) && a.n_tile >= 16 && a.n_tile <= 256 && a.n_tile % 16 == 0 &&
         (!a.chunk_add || a.n_tile % 32 == 0) && accumulators * a.n_tile <= 512 && a.k_blocks >= 1 &&
         a.p_tiles >= 1 && a.n_tiles >= 1 && taps >= 1 && a.patch_h * a.patch_w == tile_positions_m &&
         a.patch_w >= 1 && record_ok && a.group % 16 == 0 && a.group * element == a.record_bytes &&
