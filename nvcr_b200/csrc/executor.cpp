@@ -13,8 +13,14 @@ namespace nvcr_sm100 {
 
 struct Executor::IntegerConv {
     int weight_limbs{1}, activation_limbs{1}, activation_bits{8};
-    int channels{0}, c_pad{0};   // source channels, and padded to a multiple of 16
-    int k_real{0}, k_padded{0};  // K = taps * c_pad, and rounded up to 128-byte blocks
+    int channels{0}, c_pad{0};   // source channels; K channels per tap padded to a multiple of 16
+    int k_real{0}, k_padded{0};  // K = k_taps * c_pad, and rounded up to 128-byte blocks
+    // Few source channels: a prepass stages each output position's whole
+    // receptive field (channels * taps values in the node's k order), and the
+    // fused kernel runs a 1x1 conv over that grid, `window` being 1x1 then.
+    bool fields{false};
+    int k_taps{1};
+    kernels::Window window{1, 1, 1, 1, 0, 0};
     int n_tile{0}, n_tiles{0};
     int out_channels{0};  // logical output channels of the step (halved by chunk-add)
     bool chunk_add{false};
@@ -67,6 +73,7 @@ struct PlannedConv {
     int positions{0};
     int patch_h{0}, patch_w{0}, tiles_y{0}, tiles_x{0};
     int halo_rows{0}, halo_box_w{0}, halo_bytes{0};
+    int halo_buffers{2};  // halo ring depth: what the conv's halo region holds, up to 8
     CUtensorMap halo_map{};
     const void* halo_base{nullptr};  // staged address halo_map was encoded for
 };
@@ -397,8 +404,11 @@ Status Executor::prepare_integer_conv(std::size_t step_index) {
     if (taps <= 0 || node.in_channels % taps != 0) return fail(Code::internal_error, "integer conv window mismatch");
     conv.taps = taps;
     conv.channels = node.in_channels / taps;
-    conv.c_pad = round_up(conv.channels, 16);
-    conv.k_real = taps * conv.c_pad;
+    conv.fields = taps > 1 && conv.channels * taps <= 64;
+    conv.k_taps = conv.fields ? 1 : taps;
+    conv.window = conv.fields ? kernels::Window{1, 1, 1, 1, 0, 0} : step.window;
+    conv.c_pad = round_up(conv.fields ? conv.channels * taps : conv.channels, 16);
+    conv.k_real = conv.k_taps * conv.c_pad;
     if (conv.k_real > 65536) {
         return fail(Code::invalid_argument, "integer conv reduction length above 65536 is not supported");
     }
@@ -431,17 +441,18 @@ Status Executor::prepare_integer_conv(std::size_t step_index) {
         int best = INT_MAX;
         for (const int patch_w : {32, 16, 64, 8, 128}) {
             const int patch_h = 128 / patch_w;
-            const int halo_rows = (patch_h - 1) * step.window.stride_y + step.window.kernel_h;
-            const int halo_box_w = (patch_w - 1) * step.window.stride_x + step.window.kernel_w;
+            const int halo_rows = (patch_h - 1) * conv.window.stride_y + conv.window.kernel_h;
+            const int halo_box_w = (patch_w - 1) * conv.window.stride_x + conv.window.kernel_w;
             if (halo_box_w > 256 || halo_rows > 256) continue;
             best = std::min(best, round_up(halo_rows * halo_box_w * group * element, 1024));
         }
         return best;
     };
     // Shared memory: two to four A stages (filled by the producers), two to
-    // four B stages (TMA), the per-column parameters, and two halo buffers from
-    // what is left; the deepest rings whose leftover holds a halo of both source
-    // types, with smaller channel groups when none does.
+    // four B stages (TMA), the per-column parameters, and a halo region of what
+    // is left; the deepest rings whose leftover holds two halos of both source
+    // types, with smaller channel groups when none does. The region takes as
+    // many halo buffers (2..8) as fit once the patch shape is known.
     for (;;) {
         const int need = std::max(smallest_halo(conv.layouts[0].group, 4), smallest_halo(conv.layouts[1].group, 2));
         bool fits = false;
@@ -486,12 +497,13 @@ Status Executor::prepare_integer_conv(std::size_t step_index) {
     };
 
     const auto quantized = quantize_weights(program_, node);
-    // q of (row, channel c, tap) in the node's order k = c * taps + tap; the
-    // padded channels hold q = 0.
+    // q of (row, K channel c, K tap) from the node's order k = c * taps + tap;
+    // padding holds q = 0. A fields conv has one K tap whose channel is k itself.
     auto weight_q = [&](int row, int c, int tap) -> int {
+        const std::size_t at = static_cast<std::size_t>(row) * node.in_channels;
+        if (conv.fields) return c < node.in_channels ? quantized.values[at + static_cast<std::size_t>(c)] : 0;
         if (c >= conv.channels) return 0;
-        return quantized.values[static_cast<std::size_t>(row) * node.in_channels + static_cast<std::size_t>(c) * taps +
-                                tap];
+        return quantized.values[at + static_cast<std::size_t>(c) * taps + tap];
     };
     // Limbs of q: (q >> 8, (q & 255) - 128) for 16-bit weights, q for 8-bit.
     const bool two = conv.weight_limbs == 2;
@@ -512,13 +524,13 @@ Status Executor::prepare_integer_conv(std::size_t step_index) {
         long long high_sum = 0;
         long long low_sum = 0;
         for (int c = 0; c < conv.c_pad; ++c) {
-            for (int tap = 0; tap < taps; ++tap) {
+            for (int tap = 0; tap < conv.k_taps; ++tap) {
                 const int q = weight_q(row, c, tap);
                 high_sum += high_limb(q);
                 low_sum += low_limb(q);
             }
         }
-        // cx (aw sum Wh + sum Wl') + K cw cx, over all K = taps * c_pad entries.
+        // cx (aw sum Wh + sum Wl') + K cw cx, over all K = k_taps * c_pad entries.
         row_terms[physical] = cx * (aw * high_sum + low_sum) + static_cast<long long>(conv.k_real) * cw * cx;
     }
     // column term factors: cw (ax sum Xh + sum Xl')
@@ -527,7 +539,7 @@ Status Executor::prepare_integer_conv(std::size_t step_index) {
     conv.column_low_factor = conv.activation_limbs == 2 ? cw : 0;
 
     // Weight matrices [n_padded][k_padded] in a layout's K order:
-    // k = g * (taps * group) + tap * group + (c - g * group); zero bytes past K.
+    // k = g * (k_taps * group) + tap * group + (c - g * group); zero bytes past K.
     const std::size_t matrix = static_cast<std::size_t>(n_padded) * conv.k_padded;
     auto build = [&](int group, std::vector<std::int8_t>& high, std::vector<std::int8_t>& low) {
         high.assign(matrix, 0);
@@ -537,10 +549,10 @@ Status Executor::prepare_integer_conv(std::size_t step_index) {
             if (row < 0) continue;
             for (int c = 0; c < conv.c_pad; ++c) {
                 const int g = c / group;
-                for (int tap = 0; tap < taps; ++tap) {
+                for (int tap = 0; tap < conv.k_taps; ++tap) {
                     const int q = weight_q(row, c, tap);
                     const std::size_t at = static_cast<std::size_t>(physical) * conv.k_padded +
-                        static_cast<std::size_t>(g) * taps * group + static_cast<std::size_t>(tap) * group +
+                        static_cast<std::size_t>(g) * conv.k_taps * group + static_cast<std::size_t>(tap) * group +
                         (c - g * group);
                     high[at] = static_cast<std::int8_t>(high_limb(q));
                     if (two) low[at] = static_cast<std::int8_t>(low_limb(q));
@@ -685,8 +697,8 @@ Result<Executor::Plan*> Executor::plan_for(const std::vector<Extent>& input_exte
                 const int patch_h = 128 / patch_w;
                 const int tiles_y = (out.height + patch_h - 1) / patch_h;
                 const int tiles_x = (out.width + patch_w - 1) / patch_w;
-                const int halo_rows = (patch_h - 1) * step.window.stride_y + step.window.kernel_h;
-                const int halo_box_w = (patch_w - 1) * step.window.stride_x + step.window.kernel_w;
+                const int halo_rows = (patch_h - 1) * conv.window.stride_y + conv.window.kernel_h;
+                const int halo_box_w = (patch_w - 1) * conv.window.stride_x + conv.window.kernel_w;
                 const int bytes = round_up(halo_rows * halo_box_w * record_bytes, 1024);
                 if (bytes > conv.halo_budget || halo_box_w > 256 || halo_rows > 256) continue;
                 const long long covered = static_cast<long long>(tiles_y) * tiles_x * 128;
@@ -704,7 +716,10 @@ Result<Executor::Plan*> Executor::plan_for(const std::vector<Extent>& input_exte
                 }
             }
             if (pc.patch_w == 0) return fail(Code::invalid_argument, "integer conv window is too large for the halo");
-            const std::size_t pixels = static_cast<std::size_t>(source.height) * source.width;
+            pc.halo_buffers = std::min(8, 2 * conv.halo_budget / pc.halo_bytes);
+            // Staged grid: the source pixels, or the output positions of a fields conv.
+            const std::size_t pixels = conv.fields ? static_cast<std::size_t>(pc.positions)
+                                                   : static_cast<std::size_t>(source.height) * source.width;
             pc.staged = allocator.allocate(pixels * conv.c_pad * element);
             pc.pixel_max = allocator.allocate(pixels * sizeof(float));
             scratch = {pc.staged, pc.pixel_max};
@@ -771,9 +786,19 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
         if (direct_in.data != nullptr && direct_in.half != pc.source_half) {
             return fail(Code::internal_error, "integer conv source type does not match its plan");
         }
-        const int pixels = source.height * source.width;
-        status = kernels::stage_source(from, pc.source_half ? 1 : 0, source.channels, conv.c_pad, pixels, staged,
-                                       pixel_max, stream_);
+        // The grid the fused kernel reads: source pixels, or output positions
+        // whose records are receptive fields.
+        const int grid_h = conv.fields ? conv_out.height : source.height;
+        const int grid_w = conv.fields ? conv_out.width : source.width;
+        const int pixels = grid_h * grid_w;
+        if (conv.fields) {
+            status = kernels::stage_receptive_fields(from, pc.source_half ? 1 : 0, source.channels, source.height,
+                                                     source.width, step.window, conv_out.height, conv_out.width,
+                                                     conv.c_pad, staged, pixel_max, stream_);
+        } else {
+            status = kernels::stage_source(from, pc.source_half ? 1 : 0, source.channels, conv.c_pad, pixels, staged,
+                                           pixel_max, stream_);
+        }
         if (status != cudaSuccess) return cuda_error("source staging launch", status);
         const std::string label = program_.tensor_names[step.output];
         const double positions = static_cast<double>(pc.positions);
@@ -782,8 +807,8 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
                                static_cast<double>(pixels) * (conv.c_pad * element + 4.0));
         if (!marked) return marked;
         if (pc.halo_base != staged) {
-            status = kernels::encode_halo_map(&pc.halo_map, staged, pc.source_half ? 1 : 0, conv.c_pad, source.height,
-                                              source.width, layout.group, pc.halo_box_w, pc.halo_rows);
+            status = kernels::encode_halo_map(&pc.halo_map, staged, pc.source_half ? 1 : 0, conv.c_pad, grid_h, grid_w,
+                                              layout.group, pc.halo_box_w, pc.halo_rows);
             if (status != cudaSuccess) return cuda_error("cuTensorMapEncodeTiled halo", status);
             pc.halo_base = staged;
         }
@@ -791,13 +816,13 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
         kernels::FusedConvArgs f{};
         f.source_half = pc.source_half ? 1 : 0;
         f.pixel_max = pixel_max;
-        f.channels = source.channels;
+        f.channels = conv.fields ? conv.channels * conv.taps : conv.channels;
         f.c_pad = conv.c_pad;
-        f.in_h = source.height;
-        f.in_w = source.width;
+        f.in_h = grid_h;
+        f.in_w = grid_w;
         f.out_h = conv_out.height;
         f.out_w = conv_out.width;
-        f.window = step.window;
+        f.window = conv.window;
         f.k_real = conv.k_real;
         f.k_blocks = conv.k_padded / 128;
         f.positions = pc.positions;
@@ -812,6 +837,7 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
         f.halo_rows = pc.halo_rows;
         f.halo_box_w = pc.halo_box_w;
         f.halo_bytes = pc.halo_bytes;
+        f.halo_buffers = pc.halo_buffers;
         f.a_stages = conv.a_stages;
         f.b_stages = conv.b_stages;
         f.b_resident = conv.b_resident ? 1 : 0;

@@ -64,7 +64,7 @@ constexpr int first_producer_warp = 8;   // warps 8-11
 constexpr int tma_warp = 12;
 constexpr int mma_warp = 13;
 constexpr int halo_warp = 14;
-constexpr int halo_buffers = 2;
+constexpr int max_halo_buffers = 8;  // halo ring depth: as many buffers as shared memory holds, 2..8
 constexpr int max_stages = 8;
 constexpr float round_magic = 12582912.0f;              // 1.5 * 2^23
 constexpr std::uint32_t half_magic_pair = 0x66006600u;  // (1536, 1536) as an FP16 pair
@@ -78,8 +78,8 @@ struct ConvTail {
     unsigned long long tmem_empty[2];
     unsigned long long info_full[2];
     unsigned long long info_empty[2];
-    unsigned long long halo_full[halo_buffers];
-    unsigned long long halo_empty[halo_buffers];
+    unsigned long long halo_full[max_halo_buffers];
+    unsigned long long halo_empty[max_halo_buffers];
     unsigned long long drain;
     std::uint32_t tmem_base;
     int abort;
@@ -323,6 +323,76 @@ cudaError_t launch_stage(const void* in, int channels, int c_pad, int pixels, vo
 }
 
 
+// One thread per output position: its receptive field in k = c * taps + tap
+// order as 16-byte stores, zeros for padding taps and past channels * taps.
+// A per-block table holds each k's channel plane offset and (ky, kx), so the
+// per-element work is two adds, a bounds test and a load.
+constexpr int max_field = 64;  // K values per staged receptive field
+
+template <bool Half>
+__global__ void __launch_bounds__(256) stage_fields_kernel(const void* __restrict__ in, int channels, int in_h,
+                                                           int in_w, Window w, int out_h, int out_w, int c_pad,
+                                                           void* __restrict__ out, float* __restrict__ field_max) {
+    using T = std::conditional_t<Half, unsigned short, float>;
+    constexpr int per_store = 16 / static_cast<int>(sizeof(T));
+    __shared__ long long plane_at[max_field];  // c * in_h * in_w, or -1 for padding
+    __shared__ short2 tap_at[max_field];       // (ky, kx)
+    const int taps = w.kernel_h * w.kernel_w;
+    for (int k = threadIdx.x; k < c_pad; k += blockDim.x) {
+        const int c = k / taps;
+        const int tap = k - c * taps;
+        const int ky = tap / w.kernel_w;
+        plane_at[k] = k < channels * taps ? static_cast<long long>(c) * in_h * in_w : -1;
+        tap_at[k] = make_short2(static_cast<short>(ky), static_cast<short>(tap - ky * w.kernel_w));
+    }
+    __syncthreads();
+    const long long position = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (position >= static_cast<long long>(out_h) * out_w) return;
+    const int oy = static_cast<int>(position / out_w);
+    const int ox = static_cast<int>(position - static_cast<long long>(oy) * out_w);
+    const int iy0 = oy * w.stride_y - w.pad_top;
+    const int ix0 = ox * w.stride_x - w.pad_left;
+    const T* source = static_cast<const T*>(in);
+    uint4* record = reinterpret_cast<uint4*>(static_cast<T*>(out) + position * c_pad);
+    float maximum = 0.0f;
+#pragma unroll
+    for (int k0 = 0; k0 < max_field; k0 += per_store) {
+        if (k0 >= c_pad) break;
+        T v[per_store];
+#pragma unroll
+        for (int i = 0; i < per_store; ++i) {
+            const long long plane = plane_at[k0 + i];
+            const short2 d = tap_at[k0 + i];
+            const int iy = iy0 + d.x;
+            const int ix = ix0 + d.y;
+            const bool inside = plane >= 0 && static_cast<unsigned>(iy) < static_cast<unsigned>(in_h) &&
+                static_cast<unsigned>(ix) < static_cast<unsigned>(in_w);
+            v[i] = inside ? source[plane + static_cast<long long>(iy) * in_w + ix] : T(0);
+        }
+#pragma unroll
+        for (int i = 0; i < per_store; ++i) {
+            float x;
+            if constexpr (Half) {
+                x = __half2float(__ushort_as_half(v[i]));
+            } else {
+                x = v[i];
+            }
+            maximum = is_finite_value(x) ? fmaxf(maximum, fabsf(x)) : __uint_as_float(0x7f800000u);
+        }
+        std::uint32_t word[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            if constexpr (Half) {
+                word[q] = static_cast<std::uint32_t>(v[2 * q]) | (static_cast<std::uint32_t>(v[2 * q + 1]) << 16);
+            } else {
+                word[q] = __float_as_uint(v[q]);
+            }
+        }
+        record[k0 / per_store] = make_uint4(word[0], word[1], word[2], word[3]);
+    }
+    field_max[position] = maximum;
+}
+
 // ---------------------------------------------------------------- fused conv
 
 // Out-of-line helpers for the rare paths, so the hot loops stay compact in the
@@ -466,6 +536,27 @@ __device__ __forceinline__ void quantize_chunk(const uint4* d, int mode, std::ui
     }
 }
 
+struct ChunkLimbs {
+    std::uint32_t high[4];
+    std::uint32_t low[4];
+    int sum_high;
+    int sum_low;
+};
+
+// quantize_chunk for any mode, out of line: only warps in which some position
+// leaves the common rounding call it, so the common path keeps its registers.
+// FP16 sources use d0 and d1 only.
+template <int WL, int AL, bool SourceHalf>
+__device__ __noinline__ ChunkLimbs quantize_chunk_any(uint4 d0, uint4 d1, uint4 d2, uint4 d3, int mode,
+                                                      std::uint32_t scale_pair, float scale, int exponent) {
+    const uint4 d[4] = {d0, d1, d2, d3};
+    ChunkLimbs r;
+    r.sum_high = 0;
+    r.sum_low = 0;
+    quantize_chunk<WL, AL, SourceHalf>(d, mode, scale_pair, scale, exponent, r.high, r.low, r.sum_high, r.sum_low);
+    return r;
+}
+
 template <int WL, int AL, bool SourceHalf>
 __global__ void __launch_bounds__(conv_threads, 1)
 fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_constant__ CUtensorMap b_low,
@@ -483,6 +574,7 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
     // the first three 1 KiB aligned.
     std::uint8_t* b_smem = smem + a_stages * L::a_stage_bytes;
     std::uint8_t* halo_smem = b_smem + b_stages * L::b_stage_bytes(n_tile);
+    const int halo_buffers = a.halo_buffers;
     ConvTail* tail = reinterpret_cast<ConvTail*>(halo_smem + halo_buffers * a.halo_bytes);
     const int all_columns = a.n_tiles * n_tile;
     float* column_scale = reinterpret_cast<float*>(reinterpret_cast<std::uint8_t*>(tail) +
@@ -671,9 +763,10 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                 }
             }
             if (!ok) {
-                const std::uint32_t first = issued > halo_buffers ? issued - halo_buffers : 0;
+                const std::uint32_t depth = static_cast<std::uint32_t>(halo_buffers);
+                const std::uint32_t first = issued > depth ? issued - depth : 0;
                 for (std::uint32_t j = first; j < issued; ++j) {
-                    barrier_wait(smem_address(&tail->halo_full[j % halo_buffers]), (j / halo_buffers) & 1u, a.status);
+                    barrier_wait(smem_address(&tail->halo_full[j % depth]), (j / depth) & 1u, a.status);
                 }
             }
         }
@@ -702,7 +795,10 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
         // behind the tile before); larger windows load when needed.
         constexpr int window_taps = 9;
         const bool small_window = a.window.kernel_h <= 3 && kernel_w <= 3;
-        auto window_loads = [&](int t, float (&m)[window_taps]) {
+        // The loads are unconditional (pixel 0 stands in outside the window) and
+        // the returned mask marks the taps inside it: the mask is applied one
+        // tile later, so no select waits for the loads before then.
+        auto window_loads = [&](int t, float (&m)[window_taps]) -> std::uint32_t {
             int n_index, tx;
             const int p_tile = by_n_tiles.divide(t, n_index);
             const int ty = by_tiles_x.divide(p_tile, tx);
@@ -711,21 +807,24 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
             const int iy0 = oy * a.window.stride_y - a.window.pad_top;
             const int ix0 = ox * a.window.stride_x - a.window.pad_left;
             const bool real = oy < a.out_h && ox < a.out_w;
+            std::uint32_t inside_mask = 0;
 #pragma unroll
             for (int ky = 0; ky < 3; ++ky) {
 #pragma unroll
                 for (int kx = 0; kx < 3; ++kx) {
                     const int iy = iy0 + ky;
                     const int ix = ix0 + kx;
-                    m[3 * ky + kx] = (real && ky < a.window.kernel_h && kx < kernel_w && iy >= 0 && iy < a.in_h &&
-                                      ix >= 0 && ix < a.in_w)
-                        ? __ldg(a.pixel_max + static_cast<std::size_t>(iy) * a.in_w + ix)
-                        : 0.0f;
+                    const bool inside = real && ky < a.window.kernel_h && kx < kernel_w && iy >= 0 && iy < a.in_h &&
+                        ix >= 0 && ix < a.in_w;
+                    m[3 * ky + kx] = __ldg(a.pixel_max + (inside ? static_cast<std::size_t>(iy) * a.in_w + ix : 0));
+                    inside_mask |= inside ? 1u << (3 * ky + kx) : 0u;
                 }
             }
+            return inside_mask;
         };
         float next_window[window_taps];
-        if (small_window && static_cast<int>(blockIdx.x) < total_tiles) window_loads(blockIdx.x, next_window);
+        std::uint32_t next_mask = 0;
+        if (small_window && static_cast<int>(blockIdx.x) < total_tiles) next_mask = window_loads(blockIdx.x, next_window);
         for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++local) {
             int n_index, tx;
             const int p_tile = by_n_tiles.divide(t, n_index);
@@ -738,8 +837,10 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
             float maximum = 0.0f;
             if (small_window) {
 #pragma unroll
-                for (int i = 0; i < window_taps; ++i) maximum = fmaxf(maximum, next_window[i]);
-                if (t + static_cast<int>(gridDim.x) < total_tiles) window_loads(t + gridDim.x, next_window);
+                for (int i = 0; i < window_taps; ++i) {
+                    if ((next_mask >> i) & 1u) maximum = fmaxf(maximum, next_window[i]);
+                }
+                if (t + static_cast<int>(gridDim.x) < total_tiles) next_mask = window_loads(t + gridDim.x, next_window);
             } else if (real) {
                 for (int ky = 0; ky < a.window.kernel_h; ++ky) {
                     const int iy = iy0 + ky;
@@ -791,10 +892,11 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                 ++g_stage;
             };
             // A warp whose positions all take the common rounding (or produce
-            // nothing) runs a copy of the walk with that mode fixed at compile time.
+            // nothing) quantises inline with that mode fixed at compile time;
+            // other warps call the out-of-line any-mode quantiser.
             constexpr int fast_mode = (SourceHalf && AL == 1) ? quant_half : quant_float;
-            auto walk = [&](auto fast) {
-                constexpr bool Fast = decltype(fast)::value;
+            const bool fast = __all_sync(__activemask(), mode == fast_mode || mode == quant_skip);
+            {
                 for (int g = 0; g < a.groups && ok; ++g, ++job) {
                     const int h = static_cast<int>(job % halo_buffers);
                     if (*abort || !barrier_wait(smem_address(&tail->halo_full[h]), (job / halo_buffers) & 1u, a.status)) {
@@ -822,9 +924,22 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                                 break;
                             }
                             std::uint32_t high[4], low[4];
-                            quantize_chunk<WL, AL, SourceHalf>(pieces + q * pieces_per_chunk, Fast ? fast_mode : mode,
-                                                               scale_pair, scale,
-                                                               exponent, high, low, sum_high, sum_low);
+                            const int first = q * pieces_per_chunk;
+                            if (fast) {
+                                quantize_chunk<WL, AL, SourceHalf>(pieces + first, fast_mode, scale_pair, scale,
+                                                                   exponent, high, low, sum_high, sum_low);
+                            } else {
+                                const ChunkLimbs limbs = quantize_chunk_any<WL, AL, SourceHalf>(
+                                    pieces[first], pieces[first + 1], pieces[first + (SourceHalf ? 0 : 2)],
+                                    pieces[first + (SourceHalf ? 1 : 3)], mode, scale_pair, scale, exponent);
+#pragma unroll
+                                for (int w = 0; w < 4; ++w) {
+                                    high[w] = limbs.high[w];
+                                    low[w] = limbs.low[w];
+                                }
+                                sum_high += limbs.sum_high;
+                                sum_low += limbs.sum_low;
+                            }
                             const std::uint32_t slot = (static_cast<std::uint32_t>(chunk) ^ slot_key) * 16u;
                             store_shared_v4(a_row + slot, high);
                             if constexpr (AL == 2) store_shared_v4(a_row + L::a_bytes + slot, low);
@@ -840,11 +955,6 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                     }
                     barrier_arrive(smem_address(&tail->halo_empty[h]));
                 }
-            };
-            if (__all_sync(__activemask(), mode == fast_mode || mode == quant_skip)) {
-                walk(std::true_type{});
-            } else {
-                walk(std::false_type{});
             }
             if (ok && chunk > 0) {
                 // K ends inside this stage: zero limbs up to the end of the last
@@ -1101,9 +1211,9 @@ EncodeTiled encoder() {
 }
 
 int shared_bytes(int weight_limbs, int activation_limbs, int n_tile, int n_tiles, int a_stages, int b_stages,
-                 int halo_bytes) {
+                 int halo_region) {
     return 1024 + a_stages * activation_limbs * tile_positions_m * tile_k_bytes +
-        b_stages * weight_limbs * n_tile * tile_k_bytes + halo_buffers * halo_bytes +
+        b_stages * weight_limbs * n_tile * tile_k_bytes + halo_region +
         static_cast<int>((sizeof(ConvTail) + 15) / 16 * 16) + parameter_bytes(n_tile * n_tiles, activation_limbs);
 }
 
@@ -1123,7 +1233,8 @@ bool valid_geometry(const FusedConvArgs& a, int accumulators) {
         a.k_real == taps * a.c_pad && a.k_blocks == (a.k_real + tile_k_bytes - 1) / tile_k_bytes &&
         a.halo_rows == (a.patch_h - 1) * a.window.stride_y + a.window.kernel_h &&
         a.halo_box_w >= (a.patch_w - 1) * a.window.stride_x + a.window.kernel_w && a.halo_box_w <= 256 &&
-        a.halo_rows <= 256 && a.halo_bytes % 1024 == 0 &&
+        a.halo_rows <= 256 && a.halo_bytes % 1024 == 0 && a.halo_buffers >= 2 &&
+        a.halo_buffers <= max_halo_buffers &&
         a.halo_bytes >= a.halo_rows * a.halo_box_w * a.record_bytes && a.a_stages >= 1 &&
         a.a_stages <= max_stages && a.b_stages >= 1 && a.b_stages <= max_stages &&
         (!a.b_resident || (a.n_tiles == 1 && a.b_stages == a.k_blocks)) && a.tiles_y * a.patch_h >= a.out_h &&
@@ -1148,7 +1259,8 @@ cudaError_t launch_fused(const CUtensorMap& b_high, const CUtensorMap& b_low, co
         while (static_cast<int>(columns) < L::accumulators * n_tile) columns <<= 1;
         if (columns > 512) return cudaErrorInvalidValue;
     }
-    const int smem = shared_bytes(WL, AL, n_tile, args.n_tiles, args.a_stages, args.b_stages, args.halo_bytes);
+    const int smem = shared_bytes(WL, AL, n_tile, args.n_tiles, args.a_stages, args.b_stages,
+                                  args.halo_buffers * args.halo_bytes);
     if (smem > max_dynamic) return cudaErrorInvalidValue;
     static bool configured = false;
     if (!configured) {
@@ -1192,8 +1304,8 @@ cudaError_t encode_int8_map(CUtensorMap* map, const void* base, std::uint64_t ro
 }
 
 int fused_conv_shared_bytes(int weight_limbs, int activation_limbs, int n_tile, int n_tiles, int a_stages,
-                            int b_stages, int halo_bytes) {
-    return shared_bytes(weight_limbs, activation_limbs, n_tile, n_tiles, a_stages, b_stages, halo_bytes);
+                            int b_stages, int halo_region) {
+    return shared_bytes(weight_limbs, activation_limbs, n_tile, n_tiles, a_stages, b_stages, halo_region);
 }
 
 cudaError_t encode_halo_map(CUtensorMap* map, const void* base, int half, std::uint64_t c_pad, std::uint64_t height,
@@ -1255,6 +1367,26 @@ __global__ void wait_timeout_kernel(unsigned long long limit_ns, unsigned int* s
 cudaError_t wait_timeout(unsigned long long limit_ns, unsigned int* status, cudaStream_t stream) {
     if (limit_ns > 4000000000ull) return cudaErrorInvalidValue;
     wait_timeout_kernel<<<1, 32, 0, stream>>>(limit_ns, status);
+    return cudaGetLastError();
+}
+
+cudaError_t stage_receptive_fields(const void* in, int source_half, int channels, int in_h, int in_w,
+                                   Window window, int out_h, int out_w, int c_pad, void* out, float* field_max,
+                                   cudaStream_t stream) {
+    const long long positions = static_cast<long long>(out_h) * out_w;
+    if (positions <= 0) return cudaSuccess;
+    if (channels < 1 || c_pad % 16 != 0 || c_pad > max_field || c_pad < channels * window.kernel_h * window.kernel_w ||
+        (reinterpret_cast<std::uintptr_t>(out) & 15u) != 0) {
+        return cudaErrorInvalidValue;
+    }
+    const unsigned blocks = static_cast<unsigned>((positions + 255) / 256);
+    if (source_half) {
+        stage_fields_kernel<true><<<blocks, 256, 0, stream>>>(in, channels, in_h, in_w, window, out_h, out_w, c_pad,
+                                                              out, field_max);
+    } else {
+        stage_fields_kernel<false><<<blocks, 256, 0, stream>>>(in, channels, in_h, in_w, window, out_h, out_w,
+                                                               c_pad, out, field_max);
+    }
     return cudaGetLastError();
 }
 

@@ -69,6 +69,7 @@ struct FusedConvArgs {
     int record_bytes;              // group * element bytes: 16, 32, 64 or 128 (the halo swizzle span)
     int halo_rows, halo_box_w;     // halo box: halo_rows x halo_box_w pixels of `group` channels
     int halo_bytes;                // bytes per halo buffer (multiple of 1024)
+    int halo_buffers;              // halo ring depth, 2..8
     int a_stages, b_stages;        // shared-memory ring depths for activations and weights
     int b_resident;                // weights stay in shared memory: one N tile, b_stages == k_blocks
     int n_tile, n_tiles;
@@ -92,12 +93,19 @@ struct FusedConvArgs {
 // channel is non-finite).
 cudaError_t stage_source(const void* in, int source_half, int channels, int c_pad, int pixels, void* out,
                          float* pixel_max, cudaStream_t stream);
+// For convs with few input channels: per output position its whole receptive
+// field, [out_h][out_w][c_pad] with k = c * taps + tap (padding taps and k past
+// channels * taps zero), in the source's type, and the max |x| over the field
+// (+inf when a value is non-finite). The conv then runs as a 1x1 conv on it.
+cudaError_t stage_receptive_fields(const void* in, int source_half, int channels, int in_h, int in_w,
+                                   Window window, int out_h, int out_w, int c_pad, void* out, float* field_max,
+                                   cudaStream_t stream);
 cudaError_t fused_conv(const CUtensorMap& b_high, const CUtensorMap& b_low, const CUtensorMap& halo, int weight_limbs,
                        int activation_limbs, const FusedConvArgs& args, cudaStream_t stream);
 // Dynamic shared memory the fused conv needs for these ring depths and halo
 // buffers, with the per-column parameters of all n_tiles * n_tile columns.
 int fused_conv_shared_bytes(int weight_limbs, int activation_limbs, int n_tile, int n_tiles, int a_stages,
-                            int b_stages, int halo_bytes);
+                            int b_stages, int halo_region);
 constexpr int fused_conv_max_shared = 232448;
 // Encodes the 3-D halo map over a staged [height][width][c_pad] tensor with a
 // box of box_h x box_w pixels x `group` channels, zero fill outside the tensor,

@@ -111,6 +111,11 @@ CONV_CASES = [
     (16, 24, (2, 2), (2, 2), (0, 0, 0, 0), 10, 14),      # 2x2 stride 2
     (20, 40, (3, 5), (1, 2), (2, 0, 1, 3), 13, 21),      # asymmetric window and pads
     (200, 48, (3, 3), (1, 1), (1, 1, 1, 1), 5, 7),       # K = 1800, ragged
+    # few channels: the receptive field of a position staged as one record
+    (1, 24, (3, 3), (1, 1), (1, 1, 1, 1), 19, 33),      # K = 9
+    (7, 40, (3, 3), (2, 2), (1, 1, 1, 1), 23, 37),      # K = 63
+    (2, 32, (5, 5), (2, 1), (2, 2, 2, 2), 17, 26),      # K = 50
+    (3, 33, (3, 5), (1, 2), (2, 0, 1, 3), 13, 21),      # K = 45, asymmetric
 ]
 
 

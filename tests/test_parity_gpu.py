@@ -171,6 +171,24 @@ def test_activation_edge_values(cuda, oracle, bits):
     assert_parity(program, [x], oracle, f"edge values pointwise w{bits[0]}a{bits[1]}")
 
 
+@pytest.mark.parametrize("bits", WIDTHS, ids=lambda b: f"w{b[0]}a{b[1]}")
+@pytest.mark.parametrize("half", [False, True], ids=["f32", "f16"])
+def test_receptive_field_edge_values(cuda, oracle, bits, half):
+    """The few-channel path (whole receptive field per staged record): NaN and
+    inf in a field, all-zero fields, subnormal and huge maxima, ties."""
+    stream = SeededStream(6)
+    x = np.ascontiguousarray(edge_value_input(stream, 9)[[0, 3, 7, 8]])
+    if half:
+        x = x.astype(np.float16).astype(np.float32)
+    for kernel, stride, pads in (((3, 3), (1, 1), (1, 1, 1, 1)), ((3, 3), (2, 2), (0, 1, 1, 0))):
+        program = conv_program(stream, 4, 40, kernel, stride, pads, bits)
+        label = f"fields {kernel} s{stride[0]} w{bits[0]}a{bits[1]}"
+        if half:
+            assert_half_parity(program, [x], oracle, label)
+        else:
+            assert_parity(program, [x], oracle, label)
+
+
 def test_weight_edge_values(cuda, oracle):
     """A zero weight row (scale 1), FP16-subnormal weights, +-65504 weights."""
     stream = SeededStream(9)
