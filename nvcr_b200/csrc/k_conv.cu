@@ -783,11 +783,12 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
         const std::uint32_t swizzle_mask = static_cast<std::uint32_t>(record_bytes / 16 - 1);
         const int chunks_per_tap = a.group / 16;
         constexpr int pieces_per_chunk = SourceHalf ? 2 : 4;
-        const int pieces_per_tap = record_bytes / 16;
         const int base_record = py * a.window.stride_y * a.halo_box_w + px * a.window.stride_x;
         const std::uint32_t slot_key = static_cast<std::uint32_t>(row & 7);
-        std::uint32_t g_stage = 0;  // K blocks issued so far (stage ring)
-        std::uint32_t job = 0;      // halo groups consumed so far (halo ring)
+        int stage_index = 0;           // A stage ring: next stage and its phase
+        std::uint32_t stage_phase = 0;
+        int halo_index = 0;            // halo ring: next buffer and its phase
+        std::uint32_t halo_phase = 0;
         int local = 0;
         bool ok = true;
         // Pixel maxima of this position's window in the tile t: windows of up to
@@ -877,84 +878,117 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
             int sum_high = 0;
             int sum_low = 0;
             int chunk = 0;            // 16-byte chunk of the open A stage, 0..7
-            int stage = 0;
-            std::uint32_t a_row = 0;  // this position's row in the open A stage
+            std::uint32_t a_key = 0;  // this position's row in the open A stage, xor its swizzle key
             auto open_stage = [&]() -> bool {
-                stage = static_cast<int>(g_stage % a_stages);
-                const std::uint32_t phase = (g_stage / a_stages) & 1u;
-                if (*abort || !barrier_wait(smem_address(&tail->empty_a[stage]), phase ^ 1u, a.status)) return false;
-                a_row = smem_address(smem + stage * L::a_stage_bytes + row * tile_k_bytes);
+                if (*abort || !barrier_wait(smem_address(&tail->empty_a[stage_index]), stage_phase ^ 1u, a.status)) {
+                    return false;
+                }
+                // Rows are 128-byte aligned: row + ((chunk ^ key) << 4) == (row ^ (key << 4)) ^ (chunk << 4).
+                a_key = smem_address(smem + stage_index * L::a_stage_bytes + row * tile_k_bytes) ^ (slot_key << 4);
                 return true;
             };
             auto close_stage = [&]() {
                 fence_proxy_async_shared();
-                barrier_arrive(smem_address(&tail->full_a[stage]));
-                ++g_stage;
+                barrier_arrive(smem_address(&tail->full_a[stage_index]));
+                if (++stage_index == a_stages) {
+                    stage_index = 0;
+                    stage_phase ^= 1u;
+                }
             };
             // A warp whose positions all take the common rounding (or produce
             // nothing) quantises inline with that mode fixed at compile time;
             // other warps call the out-of-line any-mode quantiser.
             constexpr int fast_mode = (SourceHalf && AL == 1) ? quant_half : quant_float;
             const bool fast = __all_sync(__activemask(), mode == fast_mode || mode == quant_skip);
-            {
-                for (int g = 0; g < a.groups && ok; ++g, ++job) {
-                    const int h = static_cast<int>(job % halo_buffers);
-                    if (*abort || !barrier_wait(smem_address(&tail->halo_full[h]), (job / halo_buffers) & 1u, a.status)) {
+            auto walk = [&](auto fast_tag) {
+                constexpr bool Fast = decltype(fast_tag)::value;
+                // One 16-channel chunk from its pieces (FP16: p0, p1; FP32: p0..p3) into the A row at `at`.
+                auto emit = [&](std::uint32_t at, const uint4& p0, const uint4& p1, const uint4& p2, const uint4& p3) {
+                    std::uint32_t high[4], low[4];
+                    if constexpr (Fast) {
+                        const uint4 d[4] = {p0, p1, p2, p3};
+                        quantize_chunk<WL, AL, SourceHalf>(d, fast_mode, scale_pair, scale, exponent, high, low,
+                                                           sum_high, sum_low);
+                    } else {
+                        const ChunkLimbs limbs =
+                            quantize_chunk_any<WL, AL, SourceHalf>(p0, p1, p2, p3, mode, scale_pair, scale, exponent);
+#pragma unroll
+                        for (int w = 0; w < 4; ++w) {
+                            high[w] = limbs.high[w];
+                            low[w] = limbs.low[w];
+                        }
+                        sum_high += limbs.sum_high;
+                        sum_low += limbs.sum_low;
+                    }
+                    store_shared_v4(at, high);
+                    if constexpr (AL == 2) store_shared_v4(at + L::a_bytes, low);
+                };
+                for (int g = 0; g < a.groups && ok; ++g) {
+                    if (*abort || !barrier_wait(smem_address(&tail->halo_full[halo_index]), halo_phase, a.status)) {
                         ok = false;
                         break;
                     }
-                    const std::uint32_t halo = smem_address(halo_smem + h * a.halo_bytes);
+                    const std::uint32_t halo = smem_address(halo_smem + halo_index * a.halo_bytes);
                     int ky = 0;
                     int kx = 0;
-                    for (int tap = 0; tap < taps && ok; ++tap) {
+                    for (int tap = 0; tap < taps; ++tap) {
                         const int r = base_record + ky * a.halo_box_w + kx;
                         const std::uint32_t offset = static_cast<std::uint32_t>(r * record_bytes);
                         const std::uint32_t record = (halo + offset) ^ (((offset >> 7) & swizzle_mask) << 4);
-                        // The tap's whole record first (up to eight 16-byte loads in flight).
-                        uint4 pieces[8];
-    #pragma unroll
-                        for (int b = 0; b < 8; ++b) {
-                            if (b < pieces_per_tap) pieces[b] = load_shared_v4(record ^ (static_cast<std::uint32_t>(b) << 4));
+                        auto piece = [&](std::uint32_t b) { return load_shared_v4(record ^ (b << 4)); };
+                        // A tap's chunks never straddle a K block: chunks per tap (1, 2 or 4) divide 8.
+                        if (chunk == 0 && !open_stage()) {
+                            ok = false;
+                            break;
                         }
-    #pragma unroll
-                        for (int q = 0; q < 8 / pieces_per_chunk; ++q) {
-                            if (q >= chunks_per_tap) break;
-                            if (chunk == 0 && !open_stage()) {
-                                ok = false;
-                                break;
-                            }
-                            std::uint32_t high[4], low[4];
-                            const int first = q * pieces_per_chunk;
-                            if (fast) {
-                                quantize_chunk<WL, AL, SourceHalf>(pieces + first, fast_mode, scale_pair, scale,
-                                                                   exponent, high, low, sum_high, sum_low);
+                        // chunk is a multiple of the chunks per tap, so chunk + q == chunk ^ q.
+                        const std::uint32_t at = a_key ^ (static_cast<std::uint32_t>(chunk) << 4);
+                        // The tap's whole record is loaded before its chunks.
+                        if (chunks_per_tap * pieces_per_chunk == 8) {
+                            const uint4 p0 = piece(0), p1 = piece(1), p2 = piece(2), p3 = piece(3);
+                            const uint4 p4 = piece(4), p5 = piece(5), p6 = piece(6), p7 = piece(7);
+                            if constexpr (SourceHalf) {
+                                emit(at, p0, p1, p0, p1);
+                                emit(at ^ 16u, p2, p3, p2, p3);
+                                emit(at ^ 32u, p4, p5, p4, p5);
+                                emit(at ^ 48u, p6, p7, p6, p7);
                             } else {
-                                const ChunkLimbs limbs = quantize_chunk_any<WL, AL, SourceHalf>(
-                                    pieces[first], pieces[first + 1], pieces[first + (SourceHalf ? 0 : 2)],
-                                    pieces[first + (SourceHalf ? 1 : 3)], mode, scale_pair, scale, exponent);
-#pragma unroll
-                                for (int w = 0; w < 4; ++w) {
-                                    high[w] = limbs.high[w];
-                                    low[w] = limbs.low[w];
-                                }
-                                sum_high += limbs.sum_high;
-                                sum_low += limbs.sum_low;
+                                emit(at, p0, p1, p2, p3);
+                                emit(at ^ 16u, p4, p5, p6, p7);
                             }
-                            const std::uint32_t slot = (static_cast<std::uint32_t>(chunk) ^ slot_key) * 16u;
-                            store_shared_v4(a_row + slot, high);
-                            if constexpr (AL == 2) store_shared_v4(a_row + L::a_bytes + slot, low);
-                            if (++chunk == tile_k_bytes / 16) {
-                                close_stage();
-                                chunk = 0;
+                        } else if (chunks_per_tap * pieces_per_chunk == 4) {
+                            const uint4 p0 = piece(0), p1 = piece(1), p2 = piece(2), p3 = piece(3);
+                            if constexpr (SourceHalf) {
+                                emit(at, p0, p1, p0, p1);
+                                emit(at ^ 16u, p2, p3, p2, p3);
+                            } else {
+                                emit(at, p0, p1, p2, p3);
                             }
+                        } else {
+                            const uint4 p0 = piece(0), p1 = piece(1);
+                            emit(at, p0, p1, p0, p1);  // FP16 only: 16 channels in two pieces
+                        }
+                        chunk += chunks_per_tap;
+                        if (chunk == tile_k_bytes / 16) {
+                            close_stage();
+                            chunk = 0;
                         }
                         if (++kx == kernel_w) {
                             kx = 0;
                             ++ky;
                         }
                     }
-                    barrier_arrive(smem_address(&tail->halo_empty[h]));
+                    barrier_arrive(smem_address(&tail->halo_empty[halo_index]));
+                    if (++halo_index == halo_buffers) {
+                        halo_index = 0;
+                        halo_phase ^= 1u;
+                    }
                 }
+            };
+            if (fast) {
+                walk(std::true_type{});
+            } else {
+                walk(std::false_type{});
             }
             if (ok && chunk > 0) {
                 // K ends inside this stage: zero limbs up to the end of the last
@@ -962,9 +996,9 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                 const std::uint32_t zero[4] = {0, 0, 0, 0};
                 const int used = (chunk + 1) & ~1;
                 for (; chunk < used; ++chunk) {
-                    const std::uint32_t slot = (static_cast<std::uint32_t>(chunk) ^ slot_key) * 16u;
-                    store_shared_v4(a_row + slot, zero);
-                    if constexpr (AL == 2) store_shared_v4(a_row + L::a_bytes + slot, zero);
+                    const std::uint32_t at = a_key ^ (static_cast<std::uint32_t>(chunk) << 4);
+                    store_shared_v4(at, zero);
+                    if constexpr (AL == 2) store_shared_v4(at + L::a_bytes, zero);
                 }
                 close_stage();
                 chunk = 0;
