@@ -3,6 +3,7 @@
 #include <algorithm>
 #include <functional>
 #include <climits>
+#include <cstdlib>
 #include <cstring>
 #include <limits>
 #include <set>
@@ -45,6 +46,7 @@ struct Executor::IntegerConv {
     int a_stages{2}, b_stages{4};
     bool b_resident{false};  // one N tile whose K blocks all stay in shared memory
     int halo_budget{0};
+    int producer_sets{1};    // 2: eight producer warps on alternate tiles, four epilogue warps
 };
 
 enum class StepKind { generic, integer_conv, chunk_add };
@@ -484,6 +486,24 @@ Status Executor::prepare_integer_conv(std::size_t step_index) {
         wider.group /= 2;
     }
     for (auto& layout : conv.layouts) layout.groups = conv.c_pad / layout.group;
+    // Producer time per tile grows with the 16-byte chunks each position
+    // quantises (plus a fixed per-tile cost), epilogue time with the output
+    // columns: a second producer set (and four epilogue warps instead of eight)
+    // when the producers have about twice the epilogue's work and a tile has at
+    // most 128 accumulator columns. Measured on the 1920x1088 sweep: the 3x3
+    // 64->64 conv gains 21 % with two sets, the 3x3 256->256 convs lose 7 %.
+    // NVCR_SM100_PRODUCER_SETS=1|2 overrides (for tuning).
+    {
+        const int producer_work = conv.k_real / 16 + 12;
+        const int epilogue_work = conv.n_tile * accumulators / 4;
+        conv.producer_sets = producer_work >= 2 * epilogue_work && conv.n_tile * accumulators <= 128 ? 2 : 1;
+        if (const char* forced = std::getenv("NVCR_SM100_PRODUCER_SETS")) {
+            if (forced[0] == '1' && forced[1] == 0) conv.producer_sets = 1;
+            if (forced[0] == '2' && forced[1] == 0) conv.producer_sets = 2;
+        }
+        // Each set takes half of the A stages.
+        if (conv.a_stages % 2 != 0) conv.producer_sets = 1;
+    }
     // Physical weight row -> node row (-1: zero padding). A chunk-add conv puts
     // pair (c, c + C/2) in columns j and j + n_tile/2 of one tile.
     auto source_row = [&](int physical) -> int {
@@ -838,6 +858,7 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
         f.halo_box_w = pc.halo_box_w;
         f.halo_bytes = pc.halo_bytes;
         f.halo_buffers = pc.halo_buffers;
+        f.producer_sets = conv.producer_sets;
         f.a_stages = conv.a_stages;
         f.b_stages = conv.b_stages;
         f.b_resident = conv.b_resident ? 1 : 0;

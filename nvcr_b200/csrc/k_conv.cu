@@ -2,20 +2,27 @@
 //
 // A prepass (stage_source) rewrites the conv's source channel-innermost,
 // [in_h][in_w][c_pad] in its own type (FP16 stays FP16), and writes the
-// per-pixel max |x|. Then one persistent CTA per SM walks tiles of 128 output
+// per-pixel max |x| (a conv with channels * taps <= 64 instead stages each
+// output position's whole receptive field as one record, stage_receptive_fields,
+// and runs here as a 1x1 conv). Then one persistent CTA per SM walks tiles of 128 output
 // positions (a 2-D patch of patch_h x patch_w output pixels) x n_tile output
-// channels. Warp roles:
-//   warps 0-3  epilogue: one TMEM lane (= one position) per thread, the
-//              profile's output arithmetic and the folded ops, then the store;
-//   warp 4     TMA: int8 weight tiles (n_tile x 128 B per K block);
-//   warp 5     allocates TMEM and issues the tcgen05 MMAs (one thread);
-//   warps 6-9  producers: one thread per position quantises its receptive
-//              field from the shared-memory halo into the 128-byte-swizzled A
-//              tile, 16 channels of one tap per 16-byte A chunk; the im2col
-//              tensor and the quantised activation matrix never exist in memory;
-//   warp 10    TMA: the activation halo of the tile, `group` channels at a
-//              time, into a double-buffered shared-memory ring. Padding taps
-//              and the image border come back as the TMA's zero fill.
+// channels. Warp roles (15 warps, 128 registers each):
+//   warps 0..E-1    epilogue: one TMEM lane (= one position) per thread, the
+//                   profile's output arithmetic and the folded ops, then the
+//                   store; E = 8 (two warps per TMEM lane quarter, each half of
+//                   the columns) or E = 4 (one per quarter, all columns);
+//   warps E..11     producers, one or two sets of four warps (a set takes the
+//                   CTA's tiles s, s + sets, ...; each set has its own A-stage
+//                   ring and halo ring): one thread per position quantises its
+//                   receptive field from the shared-memory halo into the
+//                   128-byte-swizzled A tile, 16 channels of one tap per 16-byte
+//                   A chunk; the im2col tensor and the quantised activation
+//                   matrix never exist in memory;
+//   warp 12         TMA: int8 weight tiles (n_tile x 128 B per K block);
+//   warp 13         allocates TMEM and issues the tcgen05 MMAs (one thread);
+//   warp 14         TMA: the activation halo of each tile, `group` channels at a
+//                   time, into the halo rings (2..8 buffers). Padding taps and
+//                   the image border come back as the TMA's zero fill.
 // The accumulators are double-buffered in TMEM when they fit, so the epilogue
 // of one tile overlaps the main loop of the next. The per-column scale, bias
 // and row term of every output column are copied to shared memory once.
@@ -59,8 +66,10 @@ namespace {
 
 constexpr int conv_warps = 15;
 constexpr int conv_threads = conv_warps * 32;
-constexpr int epilogue_threads = 256;    // warps 0-7: two per TMEM lane quarter, each half of the columns
-constexpr int first_producer_warp = 8;   // warps 8-11
+// Warps 0-11 split between the epilogue and the producers at launch: eight
+// epilogue warps (two per TMEM lane quarter) and one producer set of four, or
+// four epilogue warps and two producer sets that take alternate tiles.
+constexpr int role_warps = 12;
 constexpr int tma_warp = 12;
 constexpr int mma_warp = 13;
 constexpr int halo_warp = 14;
@@ -536,6 +545,22 @@ __device__ __forceinline__ void quantize_chunk(const uint4* d, int mode, std::ui
     }
 }
 
+// Next use of a ring of `depth` slots starting at slot `base`: its slot and
+// the mbarrier phase parity of that use, advanced one use at a time.
+struct RingCursor {
+    int base;
+    int depth;
+    int index;
+    std::uint32_t phase;
+    __device__ int slot() const { return base + index; }
+    __device__ void advance() {
+        if (++index == depth) {
+            index = 0;
+            phase ^= 1u;
+        }
+    }
+};
+
 struct ChunkLimbs {
     std::uint32_t high[4];
     std::uint32_t low[4];
@@ -585,6 +610,14 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
     const int lane = threadIdx.x & 31;
     const int total_tiles = a.p_tiles * a.n_tiles;
     const int k_blocks = a.k_blocks;
+    const int producer_sets = a.producer_sets;
+    const int epilogue_warps = role_warps - 4 * producer_sets;
+    const int epilogue_threads = epilogue_warps * 32;
+    // Each producer set has its own A-stage ring and halo ring (the set's
+    // tiles use them in order, as do the MMA and halo TMA for that set's tiles),
+    // so every mbarrier wait is for the current or the previous phase.
+    const int ring_stages = a_stages / producer_sets;
+    const int ring_halos = halo_buffers / producer_sets;
     const Divider by_n_tiles(a.n_tiles);
     const Divider by_tiles_x(a.tiles_x);
 
@@ -675,10 +708,14 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
             const std::uint32_t idesc = i8_instruction(n_tile);
             const int last_steps = (a.k_real - (k_blocks - 1) * tile_k_bytes + 31) / 32;
             const std::uint32_t buffer_columns = static_cast<std::uint32_t>(L::accumulators * n_tile);
-            std::uint32_t g = 0;
+            std::uint32_t g = 0;  // K blocks so far (weight ring)
+            RingCursor rings0{0, ring_stages, 0, 0u};  // per producer set, kept in registers
+            RingCursor rings1{ring_stages, ring_stages, 0, 0u};
             int local = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++local) {
+                const bool second = producer_sets == 2 && (local & 1) != 0;
+                RingCursor a_ring = second ? rings1 : rings0;
                 const int buffer = local % tmem_buffers;
                 const std::uint32_t use = static_cast<std::uint32_t>(local / tmem_buffers);
                 if (*abort || !barrier_wait(smem_address(&tail->tmem_empty[buffer]), (use & 1u) ^ 1u, a.status)) {
@@ -690,10 +727,12 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                 const std::uint32_t mid = acc + static_cast<std::uint32_t>(n_tile);
                 const std::uint32_t low = acc + static_cast<std::uint32_t>(2 * n_tile);
                 for (int kb = 0; kb < k_blocks; ++kb, ++g) {
-                    const int sa = static_cast<int>(g % a_stages);
+                    const int sa = a_ring.slot();
+                    const std::uint32_t a_phase = a_ring.phase;
+                    a_ring.advance();
                     const int sb = a.b_resident ? kb : static_cast<int>(g % b_stages);
                     const std::uint32_t b_phase = a.b_resident ? 0u : (g / b_stages) & 1u;
-                    if (*abort || !barrier_wait(smem_address(&tail->full_a[sa]), (g / a_stages) & 1u, a.status) ||
+                    if (*abort || !barrier_wait(smem_address(&tail->full_a[sa]), a_phase, a.status) ||
                         !barrier_wait(smem_address(&tail->full_b[sb]), b_phase, a.status)) {
                         *abort = 1;
                         ok = false;
@@ -726,6 +765,11 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                     mma_commit(smem_address(&tail->empty_a[sa]));
                     if (!a.b_resident) mma_commit(smem_address(&tail->empty_b[sb]));
                 }
+                if (second) {
+                    rings1 = a_ring;
+                } else {
+                    rings0 = a_ring;
+                }
                 if (!ok) break;
                 mma_commit(smem_address(&tail->tmem_full[buffer]));
             }
@@ -736,21 +780,28 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
     } else if (warp == halo_warp) {
         if (lane == 0) {
             // ---------------- activation halo by TMA, one channel group per load
-            std::uint32_t job = 0;
-            std::uint32_t issued = 0;
+            // The two rings' cursors stay in registers: a tile works on a copy of
+            // its ring's cursor, written back after the tile.
+            RingCursor ring0{0, ring_halos, 0, 0u};
+            RingCursor ring1{ring_halos, ring_halos, 0, 0u};
+            std::uint32_t issued0 = 0;
+            std::uint32_t issued1 = 0;
             bool ok = true;
             const std::uint32_t box_bytes =
                 static_cast<std::uint32_t>(a.record_bytes) * static_cast<std::uint32_t>(a.halo_box_w * a.halo_rows);
-            for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+            int local = 0;
+            for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++local) {
+                const bool second = producer_sets == 2 && (local & 1) != 0;
+                RingCursor cursor = second ? ring1 : ring0;
+                std::uint32_t count = second ? issued1 : issued0;
                 int n_index, tx;
                 const int p_tile = by_n_tiles.divide(t, n_index);
                 const int ty = by_tiles_x.divide(p_tile, tx);
                 const int y0 = ty * a.patch_h * a.window.stride_y - a.window.pad_top;
                 const int x0 = tx * a.patch_w * a.window.stride_x - a.window.pad_left;
-                for (int g = 0; g < a.groups; ++g, ++job) {
-                    const int h = static_cast<int>(job % halo_buffers);
-                    const std::uint32_t phase = (job / halo_buffers) & 1u;
-                    if (*abort || !barrier_wait(smem_address(&tail->halo_empty[h]), phase ^ 1u, a.status)) {
+                for (int g = 0; g < a.groups; ++g) {
+                    const int h = cursor.slot();
+                    if (*abort || !barrier_wait(smem_address(&tail->halo_empty[h]), cursor.phase ^ 1u, a.status)) {
                         *abort = 1;
                         ok = false;
                         break;
@@ -759,20 +810,37 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                     barrier_expect_bytes(full, box_bytes);
                     // Innermost coordinate: the group's first channel, a multiple of 16 bytes.
                     tma_load_3d(smem_address(halo_smem + h * a.halo_bytes), &halo_map, full, g * a.group, x0, y0);
-                    issued = job + 1;
+                    cursor.advance();
+                    ++count;
+                }
+                if (second) {
+                    ring1 = cursor;
+                    issued1 = count;
+                } else {
+                    ring0 = cursor;
+                    issued0 = count;
                 }
             }
             if (!ok) {
-                const std::uint32_t depth = static_cast<std::uint32_t>(halo_buffers);
-                const std::uint32_t first = issued > depth ? issued - depth : 0;
-                for (std::uint32_t j = first; j < issued; ++j) {
-                    barrier_wait(smem_address(&tail->halo_full[j % depth]), (j / depth) & 1u, a.status);
+                // Every issued load must land before the CTA may exit: the last
+                // (up to depth) uses of each ring.
+                const std::uint32_t depth = static_cast<std::uint32_t>(ring_halos);
+                for (int r = 0; r < producer_sets; ++r) {
+                    const std::uint32_t n = r == 0 ? issued0 : issued1;
+                    const std::uint32_t first = n > depth ? n - depth : 0;
+                    for (std::uint32_t u = first; u < n; ++u) {
+                        const int h = r * ring_halos + static_cast<int>(u % depth);
+                        barrier_wait(smem_address(&tail->halo_full[h]), (u / depth) & 1u, a.status);
+                    }
                 }
             }
         }
-    } else if (warp >= first_producer_warp) {
-        // ---------------- activation producers: thread <-> position
-        const int row = threadIdx.x - first_producer_warp * 32;
+    } else if (warp >= epilogue_warps) {
+        // ---------------- activation producers: thread <-> position; set s of
+        // the producer_sets takes the CTA's tiles s, s + sets, ...
+        const int producer_thread = threadIdx.x - epilogue_threads;
+        const int set = producer_thread >> 7;
+        const int row = producer_thread & (tile_positions_m - 1);
         const int py = row / a.patch_w;
         const int px = row - py * a.patch_w;
         const int kernel_w = a.window.kernel_w;
@@ -785,11 +853,10 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
         constexpr int pieces_per_chunk = SourceHalf ? 2 : 4;
         const int base_record = py * a.window.stride_y * a.halo_box_w + px * a.window.stride_x;
         const std::uint32_t slot_key = static_cast<std::uint32_t>(row & 7);
-        int stage_index = 0;           // A stage ring: next stage and its phase
-        std::uint32_t stage_phase = 0;
-        int halo_index = 0;            // halo ring: next buffer and its phase
-        std::uint32_t halo_phase = 0;
-        int local = 0;
+        RingCursor stages{set * ring_stages, ring_stages, 0, 0u};  // this set's A-stage ring
+        RingCursor halos{set * ring_halos, ring_halos, 0, 0u};     // this set's halo ring
+        int local = set;  // the CTA's tile index
+        const int tile_step = producer_sets * static_cast<int>(gridDim.x);
         bool ok = true;
         // Pixel maxima of this position's window in the tile t: windows of up to
         // 3x3 taps load into registers one tile ahead (their latency hides
@@ -825,8 +892,9 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
         };
         float next_window[window_taps];
         std::uint32_t next_mask = 0;
-        if (small_window && static_cast<int>(blockIdx.x) < total_tiles) next_mask = window_loads(blockIdx.x, next_window);
-        for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++local) {
+        const int first_tile = static_cast<int>(blockIdx.x) + set * static_cast<int>(gridDim.x);
+        if (small_window && first_tile < total_tiles) next_mask = window_loads(first_tile, next_window);
+        for (int t = first_tile; t < total_tiles && ok; t += tile_step, local += producer_sets) {
             int n_index, tx;
             const int p_tile = by_n_tiles.divide(t, n_index);
             const int ty = by_tiles_x.divide(p_tile, tx);
@@ -841,7 +909,7 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                 for (int i = 0; i < window_taps; ++i) {
                     if ((next_mask >> i) & 1u) maximum = fmaxf(maximum, next_window[i]);
                 }
-                if (t + static_cast<int>(gridDim.x) < total_tiles) next_mask = window_loads(t + gridDim.x, next_window);
+                if (t + tile_step < total_tiles) next_mask = window_loads(t + tile_step, next_window);
             } else if (real) {
                 for (int ky = 0; ky < a.window.kernel_h; ++ky) {
                     const int iy = iy0 + ky;
@@ -880,20 +948,17 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
             int chunk = 0;            // 16-byte chunk of the open A stage, 0..7
             std::uint32_t a_key = 0;  // this position's row in the open A stage, xor its swizzle key
             auto open_stage = [&]() -> bool {
-                if (*abort || !barrier_wait(smem_address(&tail->empty_a[stage_index]), stage_phase ^ 1u, a.status)) {
+                if (*abort || !barrier_wait(smem_address(&tail->empty_a[stages.slot()]), stages.phase ^ 1u, a.status)) {
                     return false;
                 }
                 // Rows are 128-byte aligned: row + ((chunk ^ key) << 4) == (row ^ (key << 4)) ^ (chunk << 4).
-                a_key = smem_address(smem + stage_index * L::a_stage_bytes + row * tile_k_bytes) ^ (slot_key << 4);
+                a_key = smem_address(smem + stages.slot() * L::a_stage_bytes + row * tile_k_bytes) ^ (slot_key << 4);
                 return true;
             };
             auto close_stage = [&]() {
                 fence_proxy_async_shared();
-                barrier_arrive(smem_address(&tail->full_a[stage_index]));
-                if (++stage_index == a_stages) {
-                    stage_index = 0;
-                    stage_phase ^= 1u;
-                }
+                barrier_arrive(smem_address(&tail->full_a[stages.slot()]));
+                stages.advance();
             };
             // A warp whose positions all take the common rounding (or produce
             // nothing) quantises inline with that mode fixed at compile time;
@@ -924,11 +989,11 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                     if constexpr (AL == 2) store_shared_v4(at + L::a_bytes, low);
                 };
                 for (int g = 0; g < a.groups && ok; ++g) {
-                    if (*abort || !barrier_wait(smem_address(&tail->halo_full[halo_index]), halo_phase, a.status)) {
+                    if (*abort || !barrier_wait(smem_address(&tail->halo_full[halos.slot()]), halos.phase, a.status)) {
                         ok = false;
                         break;
                     }
-                    const std::uint32_t halo = smem_address(halo_smem + halo_index * a.halo_bytes);
+                    const std::uint32_t halo = smem_address(halo_smem + halos.slot() * a.halo_bytes);
                     int ky = 0;
                     int kx = 0;
                     for (int tap = 0; tap < taps; ++tap) {
@@ -978,11 +1043,8 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                             ++ky;
                         }
                     }
-                    barrier_arrive(smem_address(&tail->halo_empty[halo_index]));
-                    if (++halo_index == halo_buffers) {
-                        halo_index = 0;
-                        halo_phase ^= 1u;
-                    }
+                    barrier_arrive(smem_address(&tail->halo_empty[halos.slot()]));
+                    halos.advance();
                 }
             };
             if (fast) {
@@ -1019,10 +1081,11 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
         }
     } else {
         // ---------------- epilogue: thread <-> TMEM lane <-> position
-        // Warps w and w + 4 read TMEM lane quarter w (positions 32w..32w+31) and
-        // take the first and second half of the tile's 16-column chunks.
+        // Warp w reads TMEM lane quarter w % 4 (positions 32(w % 4) .. +31); with
+        // eight epilogue warps, w and w + 4 take the first and second half of the
+        // tile's 16-column chunks, with four each warp takes them all.
         const int row = threadIdx.x & (tile_positions_m - 1);
-        const int half = warp >> 2;
+        const int half = epilogue_warps == 8 ? warp >> 2 : -1;
         const std::uint32_t lane_base = static_cast<std::uint32_t>((warp & 3) * 32) << 16;
         const std::uint32_t buffer_columns = static_cast<std::uint32_t>(L::accumulators * n_tile);
         constexpr long long high_factor = (WL == 2 ? 256LL : 1LL) * (AL == 2 ? 256LL : 1LL);
@@ -1030,7 +1093,7 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
         const int pair_offset = a.chunk_add ? n_tile / 2 : 0;
         const int columns = a.chunk_add ? n_tile / 2 : n_tile;
         const int half_columns = (columns / 2 + 15) / 16 * 16;
-        const int first_column = half == 0 ? 0 : half_columns;
+        const int first_column = half == 1 ? half_columns : 0;
         const int last_column = half == 0 ? half_columns : columns;
         const int b = a.d2s_block;
         const int patch_y = row / a.patch_w;
@@ -1268,6 +1331,7 @@ bool valid_geometry(const FusedConvArgs& a, int accumulators) {
         a.halo_rows == (a.patch_h - 1) * a.window.stride_y + a.window.kernel_h &&
         a.halo_box_w >= (a.patch_w - 1) * a.window.stride_x + a.window.kernel_w && a.halo_box_w <= 256 &&
         a.halo_rows <= 256 && a.halo_bytes % 1024 == 0 && a.halo_buffers >= 2 &&
+        (a.producer_sets == 1 || a.producer_sets == 2) && a.a_stages % a.producer_sets == 0 &&
         a.halo_buffers <= max_halo_buffers &&
         a.halo_bytes >= a.halo_rows * a.halo_box_w * a.record_bytes && a.a_stages >= 1 &&
         a.a_stages <= max_stages && a.b_stages >= 1 && a.b_stages <= max_stages &&

@@ -70,6 +70,7 @@ struct FusedConvArgs {
     int halo_rows, halo_box_w;     // halo box: halo_rows x halo_box_w pixels of `group` channels
     int halo_bytes;                // bytes per halo buffer (multiple of 1024)
     int halo_buffers;              // halo ring depth, 2..8
+    int producer_sets;             // 1: eight epilogue + four producer warps; 2: four + eight (alternate tiles)
     int a_stages, b_stages;        // shared-memory ring depths for activations and weights
     int b_resident;                // weights stay in shared memory: one N tile, b_stages == k_blocks
     int n_tile, n_tiles;
