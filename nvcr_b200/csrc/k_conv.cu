@@ -150,6 +150,30 @@ __device__ __forceinline__ int byte_sum(std::uint32_t w) { return __dp4a(static_
 
 // ---------------------------------------------------------------- prepass
 
+// Maxima of |x| on bit patterns: non-negative floats (and halves) order as
+// their bits, and a NaN or infinity has bits at or above the infinity
+// pattern, so max |x| is one integer max per value (two per packed FP16
+// word) and a non-finite value anywhere gives +inf.
+__device__ __forceinline__ float max_from_half_bits(std::uint32_t m) {
+    return m >= 0x7c00u ? __uint_as_float(0x7f800000u) : __half2float(__ushort_as_half(static_cast<unsigned short>(m)));
+}
+__device__ __forceinline__ float max_from_float_bits(std::uint32_t m) {
+    return m >= 0x7f800000u ? __uint_as_float(0x7f800000u) : __uint_as_float(m);
+}
+// |x| bits of one FP16 (in the low 16 bits) or FP32 value.
+template <bool Half, typename T>
+__device__ __forceinline__ std::uint32_t magnitude_bits(T v) {
+    if constexpr (Half) {
+        return static_cast<std::uint32_t>(v) & 0x7fffu;
+    } else {
+        return __float_as_uint(v) & 0x7fffffffu;
+    }
+}
+template <bool Half>
+__device__ __forceinline__ float max_from_bits(std::uint32_t m) {
+    return Half ? max_from_half_bits(m) : max_from_float_bits(m);
+}
+
 // One thread per pixel: the channels of its pixel in blocks of 16 bytes (8 FP16
 // or 4 FP32 channels), each element load coalesced across the warp's 32
 // consecutive pixels, each block one 16-byte store into the pixel's record; the
@@ -165,7 +189,7 @@ __global__ void __launch_bounds__(256) stage_pixels_kernel(const void* __restric
     if (pixel >= pixels) return;
     const T* source = static_cast<const T*>(in) + pixel;
     uint4* record = reinterpret_cast<uint4*>(static_cast<T*>(out) + pixel * c_pad);
-    float maximum = 0.0f;
+    std::uint32_t maximum = 0;  // max |x| bits
     for (int c0 = 0; c0 < c_pad; c0 += per_block * blocks_per_pass) {
         T v[blocks_per_pass][per_block];
 #pragma unroll
@@ -181,15 +205,7 @@ __global__ void __launch_bounds__(256) stage_pixels_kernel(const void* __restric
             if (c0 + b * per_block >= c_pad) break;
             std::uint32_t w[4];
 #pragma unroll
-            for (int i = 0; i < per_block; ++i) {
-                float x;
-                if constexpr (Half) {
-                    x = __half2float(__ushort_as_half(v[b][i]));
-                } else {
-                    x = v[b][i];
-                }
-                maximum = is_finite_value(x) ? fmaxf(maximum, fabsf(x)) : __uint_as_float(0x7f800000u);
-            }
+            for (int i = 0; i < per_block; ++i) maximum = max(maximum, magnitude_bits<Half>(v[b][i]));
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 if constexpr (Half) {
@@ -201,7 +217,7 @@ __global__ void __launch_bounds__(256) stage_pixels_kernel(const void* __restric
             record[(c0 + b * per_block) / per_block] = make_uint4(w[0], w[1], w[2], w[3]);
         }
     }
-    pixel_max[pixel] = maximum;
+    pixel_max[pixel] = max_from_bits<Half>(maximum);
 }
 
 // Wide records (more than 32 channels): pixels through shared memory in slabs.
@@ -234,7 +250,7 @@ __global__ void __launch_bounds__(256) stage_source_kernel(const void* __restric
     constexpr int groups = Pixels / 32;                     // pixel groups of 32 per thread
     constexpr int batch = groups >= 16 ? 1 : 16 / groups;  // channels per thread per pass
     __shared__ __align__(16) T tile[S::tile_elements];
-    __shared__ float partial[8][Pixels];
+    __shared__ std::uint32_t partial[8][Pixels];  // max |x| bits per warp
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int slab = c_pad < S::max_slab ? c_pad : S::max_slab;
@@ -243,9 +259,9 @@ __global__ void __launch_bounds__(256) stage_source_kernel(const void* __restric
     const int valid = static_cast<int>(pixels - first < Pixels ? pixels - first : Pixels);
     const T* source = static_cast<const T*>(in);
     std::uint32_t* target = static_cast<std::uint32_t*>(out);
-    float maximum[groups];
+    std::uint32_t maximum[groups];  // max |x| bits
 #pragma unroll
-    for (int k = 0; k < groups; ++k) maximum[k] = 0.0f;
+    for (int k = 0; k < groups; ++k) maximum[k] = 0;
     for (int base = 0; base < c_pad; base += slab) {
         const int count = c_pad - base < slab ? c_pad - base : slab;
         for (int c0 = warp; c0 < count; c0 += 8 * batch) {
@@ -267,13 +283,7 @@ __global__ void __launch_bounds__(256) stage_source_kernel(const void* __restric
                 if (c >= count) break;
 #pragma unroll
                 for (int k = 0; k < groups; ++k) {
-                    float x;
-                    if constexpr (Half) {
-                        x = __half2float(__ushort_as_half(v[u][k]));
-                    } else {
-                        x = v[u][k];
-                    }
-                    maximum[k] = is_finite_value(x) ? fmaxf(maximum[k], fabsf(x)) : __uint_as_float(0x7f800000u);
+                    maximum[k] = max(maximum[k], magnitude_bits<Half>(v[u][k]));
                     tile[(k * 32 + lane) * pitch + c] = v[u][k];
                 }
             }
@@ -305,9 +315,9 @@ __global__ void __launch_bounds__(256) stage_source_kernel(const void* __restric
     for (int k = 0; k < groups; ++k) partial[warp][k * 32 + lane] = maximum[k];
     __syncthreads();
     for (int p = threadIdx.x; p < valid; p += 256) {
-        float m = partial[0][p];
-        for (int g = 1; g < 8; ++g) m = fmaxf(m, partial[g][p]);
-        pixel_max[first + p] = m;
+        std::uint32_t m = partial[0][p];
+        for (int g = 1; g < 8; ++g) m = max(m, partial[g][p]);
+        pixel_max[first + p] = max_from_bits<Half>(m);
     }
 }
 
@@ -363,7 +373,7 @@ __global__ void __launch_bounds__(256) stage_fields_kernel(const void* __restric
     const int ix0 = ox * w.stride_x - w.pad_left;
     const T* source = static_cast<const T*>(in);
     uint4* record = reinterpret_cast<uint4*>(static_cast<T*>(out) + position * c_pad);
-    float maximum = 0.0f;
+    std::uint32_t maximum = 0;  // max |x| bits
 #pragma unroll
     for (int k0 = 0; k0 < max_field; k0 += per_store) {
         if (k0 >= c_pad) break;
@@ -379,15 +389,7 @@ __global__ void __launch_bounds__(256) stage_fields_kernel(const void* __restric
             v[i] = inside ? source[plane + static_cast<long long>(iy) * in_w + ix] : T(0);
         }
 #pragma unroll
-        for (int i = 0; i < per_store; ++i) {
-            float x;
-            if constexpr (Half) {
-                x = __half2float(__ushort_as_half(v[i]));
-            } else {
-                x = v[i];
-            }
-            maximum = is_finite_value(x) ? fmaxf(maximum, fabsf(x)) : __uint_as_float(0x7f800000u);
-        }
+        for (int i = 0; i < per_store; ++i) maximum = max(maximum, magnitude_bits<Half>(v[i]));
         std::uint32_t word[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -399,7 +401,7 @@ __global__ void __launch_bounds__(256) stage_fields_kernel(const void* __restric
         }
         record[k0 / per_store] = make_uint4(word[0], word[1], word[2], word[3]);
     }
-    field_max[position] = maximum;
+    field_max[position] = max_from_bits<Half>(maximum);
 }
 
 // ---------------------------------------------------------------- fused conv

@@ -189,6 +189,25 @@ def test_receptive_field_edge_values(cuda, oracle, bits, half):
             assert_parity(program, [x], oracle, label)
 
 
+@pytest.mark.parametrize("half", [False, True], ids=["f32", "f16"])
+@pytest.mark.parametrize("cin,h,w", [(40, 8, 16), (96, 12, 20), (200, 8, 8), (64, 3, 136)])
+def test_vector_staging(cuda, oracle, half, cin, h, w):
+    """Sources whose pixel count allows 16-byte plane loads (one or more full
+    128-pixel blocks, ragged last blocks, several channel slabs), with NaN,
+    inf, huge and subnormal values in the planes."""
+    stream = SeededStream(7000 + cin + h)
+    x = stream.tensor(cin, h, w, 2.0)
+    x[cin // 3, 0, 3] = np.nan
+    x[cin - 1, h - 1, w - 1] = np.inf
+    x[cin // 2, h // 2, :] = np.float32(60000.0)
+    x[:, 1, 5] *= np.float32(2.0 ** -20)
+    program = conv_program(stream, cin, 48, (3, 3), (1, 1), (1, 1, 1, 1), (8, 8))
+    if half:
+        assert_half_parity(program, [x], oracle, f"vector staging half {cin}x{h}x{w}")
+    else:
+        assert_parity(program, [x], oracle, f"vector staging {cin}x{h}x{w}")
+
+
 def test_weight_edge_values(cuda, oracle):
     """A zero weight row (scale 1), FP16-subnormal weights, +-65504 weights."""
     stream = SeededStream(9)
