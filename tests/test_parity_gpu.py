@@ -191,10 +191,11 @@ def test_receptive_field_edge_values(cuda, oracle, bits, half):
 
 @pytest.mark.parametrize("half", [False, True], ids=["f32", "f16"])
 @pytest.mark.parametrize("cin,h,w", [(40, 8, 16), (96, 12, 20), (200, 8, 8), (64, 3, 136)])
-def test_vector_staging(cuda, oracle, half, cin, h, w):
-    """Sources whose pixel count allows 16-byte plane loads (one or more full
-    128-pixel blocks, ragged last blocks, several channel slabs), with NaN,
-    inf, huge and subnormal values in the planes."""
+def test_wide_record_staging(cuda, oracle, half, cin, h, w):
+    """Wide-record staging (48..208 padded channels: one or several channel
+    slabs, full and ragged last pixel blocks) with NaN, inf, huge and
+    subnormal values in the planes; the pixel maxima come from integer maxima
+    of the |x| bit patterns."""
     stream = SeededStream(7000 + cin + h)
     x = stream.tensor(cin, h, w, 2.0)
     x[cin // 3, 0, 3] = np.nan
@@ -203,9 +204,9 @@ def test_vector_staging(cuda, oracle, half, cin, h, w):
     x[:, 1, 5] *= np.float32(2.0 ** -20)
     program = conv_program(stream, cin, 48, (3, 3), (1, 1), (1, 1, 1, 1), (8, 8))
     if half:
-        assert_half_parity(program, [x], oracle, f"vector staging half {cin}x{h}x{w}")
+        assert_half_parity(program, [x], oracle, f"wide staging half {cin}x{h}x{w}")
     else:
-        assert_parity(program, [x], oracle, f"vector staging {cin}x{h}x{w}")
+        assert_parity(program, [x], oracle, f"wide staging {cin}x{h}x{w}")
 
 
 def test_weight_edge_values(cuda, oracle):
