@@ -130,10 +130,9 @@ __device__ __forceinline__ float integer_output32(int accumulator, float scale, 
 // form with float coefficients 1/n!, times 2^k built from bits. The constants
 // and the operation order are part of the profile: any other evaluation gives
 // other bits. NaN passes through, x >= 88 gives +inf, x < -87 gives 0.
-__device__ __forceinline__ float profile_exp(float x) {
-    if (!(x == x)) return x;
-    if (x >= 88.0f) return __uint_as_float(0x7f800000u);
-    if (x < -87.0f) return 0.0f;
+
+// exp on [-87, 88): the profile's Cody-Waite reduction and Taylor polynomial.
+__device__ __forceinline__ float profile_exp_inside(float x) {
     const float k = rintf(__fmul_rn(x, 1.44269502162933349609375f));
     float r = __fmaf_rn(-k, 0.693359375f, x);
     r = __fmaf_rn(-k, -2.12194440e-4f, r);
@@ -146,6 +145,16 @@ __device__ __forceinline__ float profile_exp(float x) {
     p = __fmaf_rn(p, r, 1.0f);
     p = __fmaf_rn(p, r, 1.0f);
     return __fmul_rn(p, __uint_as_float(static_cast<std::uint32_t>(static_cast<int>(k) + 127) << 23));
+}
+
+// The polynomial runs on every argument (0 stands in outside [-87, 88)) and
+// the special cases are selected afterwards: straight-line code, so several
+// values' evaluations interleave; in-range arguments take the same operations.
+__device__ __forceinline__ float profile_exp(float x) {
+    const bool inside = x >= -87.0f && x < 88.0f;  // false for NaN
+    const float y = profile_exp_inside(inside ? x : 0.0f);
+    const float outside = x >= 88.0f ? __uint_as_float(0x7f800000u) : (x < -87.0f ? 0.0f : x);
+    return inside ? y : outside;
 }
 
 // sigmoid(x) = 1 / (1 + exp(-x)) with an IEEE division.
