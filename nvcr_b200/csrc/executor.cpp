@@ -70,6 +70,7 @@ struct Executor::Step {
 
 struct PlannedConv {
     bool source_half{false};       // the conv reads an FP16 program input directly
+    bool source_staged{false};     // the source tensor is stored channel-innermost already
     std::size_t staged{0};         // arena offset of the channel-innermost copy of the source
     std::size_t pixel_max{0};      // arena offset of the per-input-pixel maxima
     int positions{0};
@@ -260,6 +261,29 @@ Status Executor::prepare() {
                 !(step.residual && *step.residual == id);
         }
         input_conv_only_[slot] = only;
+    }
+    // Tensors an integer conv produces (without a depth_to_space fold) and only
+    // integer convs read, as a multi-tap or pointwise source (not a receptive-
+    // field source) or as the residual: stored channel-innermost by the producing
+    // epilogue, with the per-pixel maxima.
+    staged_tensor_.assign(tensor_count, false);
+    for (std::size_t s = 0; s < steps_.size(); ++s) {
+        const Step& producer = steps_[s];
+        if (producer.kind != StepKind::integer_conv || producer.d2s_block != 0) continue;
+        const auto id = producer.output;
+        if (output_uses[id] != 0 || readers[id].empty()) continue;
+        if (std::find(program_.inputs.begin(), program_.inputs.end(), id) != program_.inputs.end()) continue;
+        bool only = true;
+        for (const auto r : readers[id]) {
+            const Step& reader = steps_[r];
+            if (reader.kind != StepKind::integer_conv) {
+                only = false;
+                break;
+            }
+            const bool as_source = reader.source == id;
+            if (as_source && convs_[static_cast<std::size_t>(reader.conv)].fields) only = false;
+        }
+        staged_tensor_[id] = only;
     }
     output_step_.assign(program_.outputs.size(), -1);
     for (std::size_t slot = 0; slot < program_.outputs.size(); ++slot) {
@@ -646,6 +670,17 @@ Status Executor::prepare_integer_conv(std::size_t step_index) {
 
 // ---------------------------------------------------------------- planning
 
+// Arena bytes of a tensor: NCHW FP32, or a staged tensor's records followed by its maxima.
+std::size_t Executor::tensor_bytes(const Extent& extent, std::size_t id) const {
+    if (!staged_tensor_[id]) return extent.count() * sizeof(float);
+    return staged_max_offset(extent, id) + static_cast<std::size_t>(extent.height) * extent.width * sizeof(float);
+}
+
+std::size_t Executor::staged_max_offset(const Extent& extent, std::size_t id) const {
+    const std::size_t pixels = static_cast<std::size_t>(extent.height) * extent.width;
+    return align_up(pixels * static_cast<std::size_t>(round_up(extent.channels, 16)) * sizeof(float), alignment);
+}
+
 Result<Executor::Plan*> Executor::plan_for(const std::vector<Extent>& input_extents, Boundary boundary) {
     std::vector<std::int32_t> key{static_cast<std::int32_t>(boundary)};
     for (const auto& e : input_extents) {
@@ -689,7 +724,7 @@ Result<Executor::Plan*> Executor::plan_for(const std::vector<Extent>& input_exte
     for (const auto id : program_.inputs) pinned[id] = pinned[id] || last_read[id] < 0;
 
     OffsetAllocator allocator;
-    auto tensor_bytes = [&](std::size_t id) { return plan->extents[id].count() * sizeof(float); };
+    auto tensor_bytes = [&](std::size_t id) { return this->tensor_bytes(plan->extents[id], id); };
     for (const auto id : program_.inputs) {
         if (plan->offsets[id] == npos) plan->offsets[id] = allocator.allocate(tensor_bytes(id));
     }
@@ -737,12 +772,16 @@ Result<Executor::Plan*> Executor::plan_for(const std::vector<Extent>& input_exte
             }
             if (pc.patch_w == 0) return fail(Code::invalid_argument, "integer conv window is too large for the halo");
             pc.halo_buffers = std::min(8, 2 * conv.halo_budget / pc.halo_bytes);
-            // Staged grid: the source pixels, or the output positions of a fields conv.
-            const std::size_t pixels = conv.fields ? static_cast<std::size_t>(pc.positions)
-                                                   : static_cast<std::size_t>(source.height) * source.width;
-            pc.staged = allocator.allocate(pixels * conv.c_pad * element);
-            pc.pixel_max = allocator.allocate(pixels * sizeof(float));
-            scratch = {pc.staged, pc.pixel_max};
+            // Staged grid: the source pixels, or the output positions of a fields conv;
+            // a staged source tensor is read in place.
+            pc.source_staged = staged_tensor_[step.source];
+            if (!pc.source_staged) {
+                const std::size_t pixels = conv.fields ? static_cast<std::size_t>(pc.positions)
+                                                       : static_cast<std::size_t>(source.height) * source.width;
+                pc.staged = allocator.allocate(pixels * conv.c_pad * element);
+                pc.pixel_max = allocator.allocate(pixels * sizeof(float));
+                scratch = {pc.staged, pc.pixel_max};
+            }
         }
         allocator.note_peak();
         for (const auto offset : scratch) allocator.release(offset);
@@ -801,6 +840,11 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
         const int element = pc.source_half ? 2 : 4;
         float* pixel_max = reinterpret_cast<float*>(base + pc.pixel_max);
         void* staged = base + pc.staged;
+        if (pc.source_staged) {
+            staged = base + plan.offsets[step.source];
+            pixel_max = reinterpret_cast<float*>(base + plan.offsets[step.source] +
+                                                 staged_max_offset(plan.extents[step.source], step.source));
+        }
         const Direct& direct_in = run_inputs_[step.source];
         const void* from = direct_in.data != nullptr ? direct_in.data : tensor(step.source);
         if (direct_in.data != nullptr && direct_in.half != pc.source_half) {
@@ -811,21 +855,24 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
         const int grid_h = conv.fields ? conv_out.height : source.height;
         const int grid_w = conv.fields ? conv_out.width : source.width;
         const int pixels = grid_h * grid_w;
-        if (conv.fields) {
-            status = kernels::stage_receptive_fields(from, pc.source_half ? 1 : 0, source.channels, source.height,
-                                                     source.width, step.window, conv_out.height, conv_out.width,
-                                                     conv.c_pad, staged, pixel_max, stream_);
-        } else {
-            status = kernels::stage_source(from, pc.source_half ? 1 : 0, source.channels, conv.c_pad, pixels, staged,
-                                           pixel_max, stream_);
-        }
-        if (status != cudaSuccess) return cuda_error("source staging launch", status);
         const std::string label = program_.tensor_names[step.output];
         const double positions = static_cast<double>(pc.positions);
-        auto marked = mark("stage_source:" + label, "stage_source", 0.0,
-                           static_cast<double>(source.count()) * element +
-                               static_cast<double>(pixels) * (conv.c_pad * element + 4.0));
-        if (!marked) return marked;
+        if (!pc.source_staged) {
+            if (conv.fields) {
+                status = kernels::stage_receptive_fields(from, pc.source_half ? 1 : 0, source.channels, source.height,
+                                                         source.width, step.window, conv_out.height, conv_out.width,
+                                                         conv.c_pad, staged, pixel_max, stream_);
+            } else {
+                status = kernels::stage_source(from, pc.source_half ? 1 : 0, source.channels, conv.c_pad, pixels,
+                                               staged, pixel_max, stream_);
+            }
+            if (status != cudaSuccess) return cuda_error("source staging launch", status);
+            ++launches_;
+            auto marked = mark("stage_source:" + label, "stage_source", 0.0,
+                               static_cast<double>(source.count()) * element +
+                                   static_cast<double>(pixels) * (conv.c_pad * element + 4.0));
+            if (!marked) return marked;
+        }
         if (pc.halo_base != staged) {
             status = kernels::encode_halo_map(&pc.halo_map, staged, pc.source_half ? 1 : 0, conv.c_pad, grid_h, grid_w,
                                               layout.group, pc.halo_box_w, pc.halo_rows);
@@ -873,15 +920,29 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
         f.wsilu_scale = step.wsilu_scale;
         f.chunk_add = step.chunk_add ? 1 : 0;
         f.residual = step.residual ? tensor(*step.residual) : nullptr;
+        f.residual_c_pad = step.residual && staged_tensor_[*step.residual]
+            ? round_up(plan.extents[*step.residual].channels, 16) : 0;
         f.out = direct_out.data != nullptr ? direct_out.data : tensor(step.output);
         f.out_half = direct_out.data != nullptr && direct_out.half ? 1 : 0;
+        f.out_max = nullptr;
+        f.out_c_pad = 0;
+        if (staged_tensor_[step.output]) {
+            const Extent staged_out = plan.extents[step.output];
+            f.out_c_pad = round_up(staged_out.channels, 16);
+            f.out_max = reinterpret_cast<float*>(base + plan.offsets[step.output] +
+                                                 staged_max_offset(staged_out, step.output));
+            status = cudaMemsetAsync(f.out_max, 0,
+                                     static_cast<std::size_t>(staged_out.height) * staged_out.width * sizeof(float),
+                                     stream_);
+            if (status != cudaSuccess) return cuda_error("cudaMemsetAsync staged maxima", status);
+        }
         f.out_channels = conv.out_channels;
         f.d2s_block = step.d2s_block;
         f.status = status_;
         status = kernels::fused_conv(layout.b_high_map, layout.b_low_map, pc.halo_map, conv.weight_limbs,
                                      conv.activation_limbs, f, stream_);
         if (status != cudaSuccess) return cuda_error("integer conv launch", status);
-        launches_ += 2;
+        launches_ += 1;
         const double ops = 2.0 * conv.channels * conv.taps * static_cast<double>(node.out_channels) * positions;
         const double out_bytes = static_cast<double>(out_extent.count()) * (f.out_half ? 2.0 : 4.0) +
             (step.residual ? static_cast<double>(out_extent.count()) * 4.0 : 0.0);

@@ -123,6 +123,12 @@ private:
     // Per program output: the integer conv step that produces it when no step
     // reads it (the epilogue stores into the caller's buffer), else -1.
     std::vector<std::ptrdiff_t> output_step_;
+    // Per tensor: kept channel-innermost ([H][W][c_pad] FP32, then the per-pixel
+    // maxima) because an integer conv produces it and only integer convs read
+    // it, as their source or residual; their staging prepass is skipped.
+    std::vector<bool> staged_tensor_;
+    std::size_t tensor_bytes(const Extent& extent, std::size_t id) const;
+    std::size_t staged_max_offset(const Extent& extent, std::size_t id) const;
     // The run in progress: caller buffers for direct inputs (by tensor id) and
     // direct outputs (by step), with their element type.
     struct Direct {

@@ -1199,6 +1199,7 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                 }
             };
 
+            std::uint32_t staged_max = 0;  // max |x| bits of this position's staged outputs
             for (int j0 = first_column; j0 < last_column; j0 += 16) {
                 float v[16];
                 values16(j0, v);
@@ -1216,14 +1217,48 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                         for (int j = 0; j < 16; ++j) v[j] = canonical_nan();
                     }
                     if (a.residual != nullptr) {
-                        const float* r = a.residual + static_cast<std::size_t>(c0) * a.positions + p;
                         float add[16];
+                        if (a.residual_c_pad > 0) {
+                            // Channel-innermost residual: the position's 16 channels are contiguous.
+                            if (count > 0) {
+                                const float4* r = reinterpret_cast<const float4*>(
+                                    a.residual + static_cast<std::size_t>(p) * a.residual_c_pad + c0);
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) add[j] = j < count ? __ldg(r + static_cast<std::size_t>(j) * a.positions) : 0.0f;
+                                for (int q = 0; q < 4; ++q) {
+                                    const float4 f = __ldg(r + q);
+                                    add[4 * q] = f.x;
+                                    add[4 * q + 1] = f.y;
+                                    add[4 * q + 2] = f.z;
+                                    add[4 * q + 3] = f.w;
+                                }
+                            }
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) add[j] = j < count ? add[j] : 0.0f;
+                        } else {
+                            const float* r = a.residual + static_cast<std::size_t>(c0) * a.positions + p;
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) {
+                                add[j] = j < count ? __ldg(r + static_cast<std::size_t>(j) * a.positions) : 0.0f;
+                            }
+                        }
 #pragma unroll
                         for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], add[j]);
                     }
-                    if (b == 0 && count == 16) {
+                    if (a.out_max != nullptr) {
+                        // Staged store: the position's 16 channels as four 16-byte stores,
+                        // zeros past out_channels (up to out_c_pad), and their max |x| bits.
+                        if (c0 < a.out_c_pad) {
+                            float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.out) +
+                                                                  static_cast<std::size_t>(p) * a.out_c_pad + c0);
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) {
+                                v[j] = j < count ? v[j] : 0.0f;
+                                staged_max = max(staged_max, __float_as_uint(v[j]) & 0x7fffffffu);
+                            }
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) o[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                        }
+                    } else if (b == 0 && count == 16) {
                         // Sixteen channel planes of this position.
                         const std::size_t stride = static_cast<std::size_t>(a.positions);
                         const std::size_t at = static_cast<std::size_t>(c0) * stride + p;
@@ -1276,6 +1311,11 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                     }
                 }
                 __syncwarp();  // tcgen05.ld is warp-aligned: reconverge before the next columns
+            }
+            if (a.out_max != nullptr && real) {
+                // Non-negative floats order as their bits; NaN bits become +inf.
+                atomicMax(reinterpret_cast<unsigned int*>(a.out_max) + p,
+                          __float_as_uint(max_from_float_bits(staged_max)));
             }
             tmem_fence_before();
             barrier_arrive(smem_address(&tail->tmem_empty[buffer]));
@@ -1334,6 +1374,12 @@ bool valid_geometry(const FusedConvArgs& a, int accumulators) {
         a.halo_box_w >= (a.patch_w - 1) * a.window.stride_x + a.window.kernel_w && a.halo_box_w <= 256 &&
         a.halo_rows <= 256 && a.halo_bytes % 1024 == 0 && a.halo_buffers >= 2 &&
         (a.producer_sets == 1 || a.producer_sets == 2) && a.a_stages % a.producer_sets == 0 &&
+        (a.out_max == nullptr ||
+         (!a.out_half && a.d2s_block == 0 && a.out_c_pad % 16 == 0 && a.out_c_pad >= a.out_channels &&
+          (reinterpret_cast<std::uintptr_t>(a.out) & 15u) == 0)) &&
+        (a.residual_c_pad == 0 ||
+         (a.residual_c_pad % 16 == 0 && a.residual_c_pad >= a.out_channels &&
+          (reinterpret_cast<std::uintptr_t>(a.residual) & 15u) == 0)) &&
         a.halo_buffers <= max_halo_buffers &&
         a.halo_bytes >= a.halo_rows * a.halo_box_w * a.record_bytes && a.a_stages >= 1 &&
         a.a_stages <= max_stages && a.b_stages >= 1 && a.b_stages <= max_stages &&

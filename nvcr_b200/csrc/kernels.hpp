@@ -82,8 +82,15 @@ struct FusedConvArgs {
     float wsilu_scale;
     int chunk_add;
     const float* residual;         // [out_channels][positions] FP32, or null
+    int residual_c_pad;            // 0: residual as above; else [positions][residual_c_pad] FP32
     void* out;                     // FP32, or FP16 when out_half
     int out_half;
+    // Staged output: out is [positions][out_c_pad] FP32 (the layout an integer
+    // conv reads its source in, padding channels zero) and out_max gets each
+    // position's max |x| (+inf when a value is non-finite) by atomic max into a
+    // zeroed buffer. Null for the NCHW store.
+    float* out_max;
+    int out_c_pad;
     int out_channels;              // logical channels stored (after chunk-add)
     int d2s_block;                 // 0: NCHW store; b: store through depth_to_space(b)
     unsigned int* status;

@@ -209,6 +209,52 @@ def test_wide_record_staging(cuda, oracle, half, cin, h, w):
         assert_parity(program, [x], oracle, f"wide staging {cin}x{h}x{w}")
 
 
+def staged_chain_program(stream: SeededStream, bits) -> Program:
+    """Intermediates that only integer convs read (stored channel-innermost by
+    the producing epilogue): 1x1 40->48 (read by a 3x3 conv and, later, as a
+    residual), 3x3 48->40, 1x1 40->96 + WSiLU + chunk-add -> 48, 1x1 48->48 +
+    residual of the first conv's output; ragged channel counts so the padding
+    channels of the staged records matter."""
+    p = Program(name="staged_chain")
+    x = p.add_input("x", 24)
+
+    def conv(src, cin, cout, name, kernel=(1, 1), pads=(0, 0, 0, 0)):
+        taps = kernel[0] * kernel[1]
+        w = stream.uniform(-0.5, 0.5, cout * cin * taps)
+        b = stream.uniform(-0.2, 0.2, cout)
+        return p.dense_conv(src, cout, w, b, name, kernel=kernel, stride=(1, 1), pads=pads, bits=bits)
+
+    a = conv(x, 24, 48, "a")
+    t = conv(a, 48, 40, "t", kernel=(3, 3), pads=(1, 1, 1, 1))
+    u = conv(t, 40, 96, "u")
+    s = p.unary(OpKind.mul_scalar, u, "us", scalar=4.0)
+    g = p.unary(OpKind.sigmoid, s, "ug")
+    u = p.binary(OpKind.mul, u, g, "uw")
+    h1 = p.unary(OpKind.slice_channels, u, "u0", begin=0, end=48)
+    h2 = p.unary(OpKind.slice_channels, u, "u1", begin=48, end=96)
+    v = p.binary(OpKind.add, h1, h2, "v")
+    y = conv(v, 48, 48, "y")
+    y = p.binary(OpKind.add, y, a, "out")
+    return p.finish([y])
+
+
+@pytest.mark.parametrize("bits", WIDTHS, ids=lambda b: f"w{b[0]}a{b[1]}")
+@pytest.mark.parametrize("half", [False, True], ids=["f32", "f16"])
+def test_staged_intermediates(cuda, oracle, bits, half):
+    """Chains whose intermediates skip the staging prepass, with NaN, inf and
+    all-zero positions propagating through the staged maxima."""
+    stream = SeededStream(8100)
+    program = staged_chain_program(stream, bits)
+    x = stream.tensor(24, 19, 37, 2.0)
+    x[3, 4, 5] = np.nan
+    x[7, 10, 20] = np.inf
+    x[:, 15, 30] = 0.0
+    if half:
+        assert_half_parity(program, [x], oracle, f"staged chain half w{bits[0]}a{bits[1]}")
+    else:
+        assert_parity(program, [x], oracle, f"staged chain w{bits[0]}a{bits[1]}")
+
+
 def test_weight_edge_values(cuda, oracle):
     """A zero weight row (scale 1), FP16-subnormal weights, +-65504 weights."""
     stream = SeededStream(9)
