@@ -132,8 +132,14 @@ __device__ __forceinline__ float integer_output32(int accumulator, float scale, 
 // other bits. NaN passes through, x >= 88 gives +inf, x < -87 gives 0.
 
 // exp on [-87, 88): the profile's Cody-Waite reduction and Taylor polynomial.
+// k = rint(x log2 e) by the round-to-nearest-even of adding 1.5 * 2^23 (exact
+// for |x log2 e| < 2^22; here it is below 127), which leaves the integer k in
+// the low bits of the sum: no conversion instruction for k or for 2^k.
 __device__ __forceinline__ float profile_exp_inside(float x) {
-    const float k = rintf(__fmul_rn(x, 1.44269502162933349609375f));
+    constexpr float magic = 12582912.0f;  // 1.5 * 2^23
+    const float shifted = __fadd_rn(__fmul_rn(x, 1.44269502162933349609375f), magic);
+    const float k = __fsub_rn(shifted, magic);
+    const int k_int = static_cast<int>(__float_as_uint(shifted) - __float_as_uint(magic));
     float r = __fmaf_rn(-k, 0.693359375f, x);
     r = __fmaf_rn(-k, -2.12194440e-4f, r);
     float p = 1.98412698e-4f;
@@ -144,7 +150,7 @@ __device__ __forceinline__ float profile_exp_inside(float x) {
     p = __fmaf_rn(p, r, 0.5f);
     p = __fmaf_rn(p, r, 1.0f);
     p = __fmaf_rn(p, r, 1.0f);
-    return __fmul_rn(p, __uint_as_float(static_cast<std::uint32_t>(static_cast<int>(k) + 127) << 23));
+    return __fmul_rn(p, __uint_as_float(static_cast<std::uint32_t>(k_int + 127) << 23));
 }
 
 // The polynomial runs on every argument (0 stands in outside [-87, 88)) and
