@@ -95,6 +95,12 @@ constexpr std::size_t npos = std::numeric_limits<std::size_t>::max();
 constexpr std::size_t alignment = 1024;
 
 std::size_t align_up(std::size_t value, std::size_t to) { return (value + to - 1) / to * to; }
+
+// A conv with few channels (channels * taps <= 64, more than one tap) stages
+// each output position's whole receptive field and runs as a 1x1 conv over it.
+bool receptive_field_staging(const kernels::Window& window, int in_channels) {
+    return window.kernel_h * window.kernel_w > 1 && in_channels <= 64;
+}
 int round_up(int value, int to) { return (value + to - 1) / to * to; }
 
 Error cuda_error(const char* what, cudaError_t status) {
@@ -262,28 +268,55 @@ Status Executor::prepare() {
         }
         input_conv_only_[slot] = only;
     }
-    // Tensors an integer conv produces (without a depth_to_space fold) and only
-    // integer convs read, as a multi-tap or pointwise source (not a receptive-
-    // field source) or as the residual: stored channel-innermost by the producing
-    // epilogue, with the per-pixel maxima.
+    // Staged tensors, stored channel-innermost ([H][W][c_pad] FP32, then the
+    // per-pixel maxima) instead of NCHW. A tensor qualifies when it is no program
+    // input or output and its producer is an integer conv (without a
+    // depth_to_space fold) or a channel-innermost depthwise 3x3 whose input is
+    // staged, and every reader is an integer conv reading it as a multi-tap or
+    // pointwise source (not a receptive-field source) or as the residual, or a
+    // channel-innermost depthwise 3x3 whose output is staged. The largest such
+    // set: start from every candidate and drop violators until none is left.
+    auto staged_depthwise = [&](const Step& st) {
+        if (st.kind != StepKind::generic) return false;
+        const Node& n = program_.nodes[st.node];
+        const int c_pad = round_up(n.out_channels, 16);
+        return n.op == Op::conv && n.depthwise && n.kernel[0] == 3 && n.kernel[1] == 3 && n.stride[0] == 1 &&
+            n.stride[1] == 1 && n.pads[0] == 1 && n.pads[1] == 1 && n.pads[2] == 1 && n.pads[3] == 1 &&
+            n.in_channels == n.out_channels && (c_pad == 128 || c_pad == 256);
+    };
+    std::vector<std::ptrdiff_t> produced_by(tensor_count, -1);
+    for (std::size_t s = 0; s < steps_.size(); ++s) produced_by[steps_[s].output] = static_cast<std::ptrdiff_t>(s);
     staged_tensor_.assign(tensor_count, false);
-    for (std::size_t s = 0; s < steps_.size(); ++s) {
-        const Step& producer = steps_[s];
-        if (producer.kind != StepKind::integer_conv || producer.d2s_block != 0) continue;
-        const auto id = producer.output;
-        if (output_uses[id] != 0 || readers[id].empty()) continue;
+    for (std::size_t id = 0; id < tensor_count; ++id) {
+        const auto s = produced_by[id];
+        if (s < 0 || output_uses[id] != 0 || readers[id].empty()) continue;
         if (std::find(program_.inputs.begin(), program_.inputs.end(), id) != program_.inputs.end()) continue;
-        bool only = true;
-        for (const auto r : readers[id]) {
-            const Step& reader = steps_[r];
-            if (reader.kind != StepKind::integer_conv) {
-                only = false;
-                break;
+        const Step& producer = steps_[static_cast<std::size_t>(s)];
+        staged_tensor_[id] = (producer.kind == StepKind::integer_conv && producer.d2s_block == 0) ||
+            staged_depthwise(producer);
+    }
+    for (bool changed = true; changed;) {
+        changed = false;
+        for (std::size_t id = 0; id < tensor_count; ++id) {
+            if (!staged_tensor_[id]) continue;
+            const Step& producer = steps_[static_cast<std::size_t>(produced_by[id])];
+            bool ok = producer.kind == StepKind::integer_conv || staged_tensor_[producer.reads[0]];
+            for (const auto r : readers[id]) {
+                const Step& reader = steps_[r];
+                if (reader.kind == StepKind::integer_conv) {
+                    if (reader.source == id &&
+                        receptive_field_staging(reader.window, program_.nodes[reader.node].in_channels)) {
+                        ok = false;
+                    }
+                } else if (!(staged_depthwise(reader) && staged_tensor_[reader.output])) {
+                    ok = false;
+                }
             }
-            const bool as_source = reader.source == id;
-            if (as_source && convs_[static_cast<std::size_t>(reader.conv)].fields) only = false;
+            if (!ok) {
+                staged_tensor_[id] = false;
+                changed = true;
+            }
         }
-        staged_tensor_[id] = only;
     }
     output_step_.assign(program_.outputs.size(), -1);
     for (std::size_t slot = 0; slot < program_.outputs.size(); ++slot) {
@@ -430,7 +463,7 @@ Status Executor::prepare_integer_conv(std::size_t step_index) {
     if (taps <= 0 || node.in_channels % taps != 0) return fail(Code::internal_error, "integer conv window mismatch");
     conv.taps = taps;
     conv.channels = node.in_channels / taps;
-    conv.fields = taps > 1 && conv.channels * taps <= 64;
+    conv.fields = receptive_field_staging(step.window, node.in_channels);
     conv.k_taps = conv.fields ? 1 : taps;
     conv.window = conv.fields ? kernels::Window{1, 1, 1, 1, 0, 0} : step.window;
     conv.c_pad = round_up(conv.fields ? conv.channels * taps : conv.channels, 16);
@@ -959,6 +992,16 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
         float* out = tensor(step.output);
         switch (node.op) {
         case Op::conv: {
+            if (staged_tensor_[step.output]) {
+                // Channel-innermost depthwise 3x3: the planner stages its input too.
+                const float* staged_in = tensor(node.inputs[0]);
+                float* staged_max = reinterpret_cast<float*>(base + plan.offsets[step.output] +
+                                                             staged_max_offset(out_extent, step.output));
+                status = kernels::depthwise3x3_staged(weights_ + node.weight_offset, weights_ + node.bias_offset,
+                                                      node.out_channels, round_up(node.out_channels, 16), staged_in,
+                                                      out, staged_max, out_extent.height, out_extent.width, stream_);
+                break;
+            }
             kernels::ConvShape shape{node.in_channels, node.out_channels, node.depthwise ? 1 : 0, in.height, in.width,
                                      out_extent.height, out_extent.width,
                                      kernels::Window{node.kernel[0], node.kernel[1], node.stride[0], node.stride[1],

@@ -291,7 +291,130 @@ __global__ void __launch_bounds__(256) depthwise3x3_kernel(const float* __restri
     }
 }
 
+// The same depthwise 3x3 on channel-innermost tensors ([H][W][c_pad] FP32,
+// padding channels zero, the layout an integer conv reads its source in). A
+// block takes an 8 x 32 output tile of one 32-channel slab: it stages the
+// 10 x 34 input halo of the slab in shared memory (each pixel's 32 channels
+// as 128-byte runs, 36 floats apart so the reads below are conflict-free),
+// then thread (x, quad) computes output rows 0..7 of column x for channels
+// 4 quad .. 4 quad + 3 with the same fma order as conv_fp32_kernel (bias, then
+// row, column; padding taps multiply zeros); padding channels stay zero. Each
+// pixel's max |x| over the slab (bit patterns: non-negative floats order as
+// their bits; +inf for a non-finite value) goes into the zeroed maxima by an
+// atomic max, so the slabs combine.
+constexpr int dws_rows = 8;
+constexpr int dws_cols = 32;
+constexpr int dws_slab = 32;
+constexpr int dws_stride = dws_slab + 4;  // floats per staged pixel
+
+__global__ void __launch_bounds__(256) depthwise3x3_staged_kernel(const float* __restrict__ weights,
+                                                                  const float* __restrict__ bias, int channels,
+                                                                  int c_pad, const float* __restrict__ in,
+                                                                  float* __restrict__ out,
+                                                                  float* __restrict__ pixel_max, int height,
+                                                                  int width) {
+    __shared__ __align__(16) float tile[(dws_rows + 2) * (dws_cols + 2) * dws_stride];
+    const int x0 = static_cast<int>(blockIdx.x) * dws_cols;
+    const int y0 = static_cast<int>(blockIdx.y) * dws_rows;
+    const int c0 = static_cast<int>(blockIdx.z) * dws_slab;
+    constexpr int halo_pixels = (dws_rows + 2) * (dws_cols + 2);
+    for (int i = threadIdx.x; i < halo_pixels * 8; i += 256) {
+        const int pixel = i >> 3;
+        const int quad = i & 7;
+        const int ty = pixel / (dws_cols + 2);
+        const int tx = pixel - ty * (dws_cols + 2);
+        const int y = y0 + ty - 1;
+        const int x = x0 + tx - 1;
+        const float4 v = (y >= 0 && y < height && x >= 0 && x < width)
+            ? __ldg(reinterpret_cast<const float4*>(in + (static_cast<std::size_t>(y) * width + x) * c_pad + c0) + quad)
+            : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        *reinterpret_cast<float4*>(tile + pixel * dws_stride + 4 * quad) = v;
+    }
+    const int quad = threadIdx.x & 7;
+    const int col = threadIdx.x >> 3;  // 0..31
+    float w[4][9];
+    float b[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int c = c0 + 4 * quad + j;
+#pragma unroll
+        for (int k = 0; k < 9; ++k) w[j][k] = c < channels ? __ldg(weights + static_cast<std::size_t>(c) * 9 + k) : 0.0f;
+        b[j] = c < channels ? __ldg(bias + c) : 0.0f;
+    }
+    __syncthreads();
+    const int x = x0 + col;
+    // window[r][kx]: staged input row r of columns col .. col + 2 (4 channels each).
+    float4 window[3][3];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+#pragma unroll
+        for (int kx = 0; kx < 3; ++kx) {
+            window[r][kx] = *reinterpret_cast<const float4*>(tile + (r * (dws_cols + 2) + col + kx) * dws_stride + 4 * quad);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < dws_rows; ++r) {
+#pragma unroll
+        for (int kx = 0; kx < 3; ++kx) {
+            window[2][kx] =
+                *reinterpret_cast<const float4*>(tile + ((r + 2) * (dws_cols + 2) + col + kx) * dws_stride + 4 * quad);
+        }
+        const int y = y0 + r;
+        float acc[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            acc[j] = b[j];
+#pragma unroll
+            for (int ky = 0; ky < 3; ++ky) {
+#pragma unroll
+                for (int kx = 0; kx < 3; ++kx) {
+                    const float4& v = window[ky][kx];
+                    const float in_value = j == 0 ? v.x : (j == 1 ? v.y : (j == 2 ? v.z : v.w));
+                    acc[j] = __fmaf_rn(w[j][3 * ky + kx], in_value, acc[j]);
+                }
+            }
+            if (c0 + 4 * quad + j >= channels) acc[j] = 0.0f;
+        }
+        std::uint32_t bits = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) bits = max(bits, __float_as_uint(acc[j]) & 0x7fffffffu);
+        // The eight quads of a pixel are lanes 8 m .. 8 m + 7 of the warp.
+#pragma unroll
+        for (int offset = 4; offset > 0; offset >>= 1) bits = max(bits, __shfl_xor_sync(0xffffffffu, bits, offset));
+        if (y < height && x < width) {
+            *(reinterpret_cast<float4*>(out + (static_cast<std::size_t>(y) * width + x) * c_pad + c0) + quad) =
+                make_float4(acc[0], acc[1], acc[2], acc[3]);
+            if (quad == 0) {
+                const std::uint32_t m = bits >= 0x7f800000u ? 0x7f800000u : bits;
+                atomicMax(reinterpret_cast<unsigned int*>(pixel_max) + static_cast<std::size_t>(y) * width + x, m);
+            }
+        }
+#pragma unroll
+        for (int kx = 0; kx < 3; ++kx) {
+            window[0][kx] = window[1][kx];
+            window[1][kx] = window[2][kx];
+        }
+    }
+}
+
 }  // namespace
+
+cudaError_t depthwise3x3_staged(const float* weights, const float* bias, int channels, int c_pad, const float* in,
+                                float* out, float* pixel_max, int height, int width, cudaStream_t stream) {
+    if (height <= 0 || width <= 0) return cudaSuccess;
+    if (channels < 1 || channels > c_pad || c_pad % dws_slab != 0 || (reinterpret_cast<std::uintptr_t>(in) & 15u) != 0 ||
+        (reinterpret_cast<std::uintptr_t>(out) & 15u) != 0) {
+        return cudaErrorInvalidValue;
+    }
+    cudaError_t status =
+        cudaMemsetAsync(pixel_max, 0, static_cast<std::size_t>(height) * width * sizeof(float), stream);
+    if (status != cudaSuccess) return status;
+    const dim3 grid(static_cast<unsigned>((width + dws_cols - 1) / dws_cols),
+                    static_cast<unsigned>((height + dws_rows - 1) / dws_rows), static_cast<unsigned>(c_pad / dws_slab));
+    depthwise3x3_staged_kernel<<<grid, 256, 0, stream>>>(weights, bias, channels, c_pad, in, out, pixel_max, height,
+                                                         width);
+    return cudaGetLastError();
+}
 
 cudaError_t half_to_float(const std::uint16_t* in, float* out, std::size_t count, cudaStream_t stream) {
     if (count == 0) return cudaSuccess;

@@ -49,6 +49,11 @@ struct ConvShape {
 };
 cudaError_t conv_fp32(const float* weights, const float* bias, const float* in, float* out, ConvShape shape,
                       cudaStream_t stream);
+// Depthwise 3x3 s1 p1 on channel-innermost FP32 tensors [H][W][c_pad] (c_pad
+// 128 or 256, padding channels zero), with each pixel's max |x| (+inf when a
+// value is non-finite): the layout and maxima an integer conv reads.
+cudaError_t depthwise3x3_staged(const float* weights, const float* bias, int channels, int c_pad, const float* in,
+                                float* out, float* pixel_max, int height, int width, cudaStream_t stream);
 
 // ---- integer conv: fused quantise-on-load implicit GEMM (persistent, tcgen05) ----
 // The conv reads its source from a channel-innermost copy [in_h][in_w][c_pad]

@@ -255,6 +255,43 @@ def test_staged_intermediates(cuda, oracle, bits, half):
         assert_parity(program, [x], oracle, f"staged chain w{bits[0]}a{bits[1]}")
 
 
+def staged_depthwise_program(stream: SeededStream, channels: int, bits) -> Program:
+    """1x1 24->C + WSiLU -> depthwise 3x3 -> 1x1 C->40: the WSiLU conv's output and
+    the depthwise output are read only by the depthwise and the last conv, so both
+    stay channel-innermost and the depthwise runs on that layout."""
+    p = Program(name="staged_depthwise")
+    x = p.add_input("x", 24)
+    t = p.dense_conv(x, channels, stream.uniform(-0.5, 0.5, channels * 24), stream.uniform(-0.2, 0.2, channels),
+                     "t", kernel=(1, 1), stride=(1, 1), pads=(0, 0, 0, 0), bits=bits)
+    s = p.unary(OpKind.mul_scalar, t, "ts", scalar=4.0)
+    g = p.unary(OpKind.sigmoid, s, "tg")
+    t = p.binary(OpKind.mul, t, g, "tw")
+    d = p.conv(t, channels, stream.uniform(-0.5, 0.5, channels * 9), stream.uniform(-0.2, 0.2, channels), "d",
+               depthwise=True, kernel=(3, 3), pads=(1, 1, 1, 1))
+    y = p.dense_conv(d, 40, stream.uniform(-0.5, 0.5, 40 * channels), stream.uniform(-0.2, 0.2, 40), "y",
+                     kernel=(1, 1), stride=(1, 1), pads=(0, 0, 0, 0), bits=bits)
+    return p.finish([y])
+
+
+@pytest.mark.parametrize("bits", [(8, 8), (16, 16)], ids=["w8a8", "w16a16"])
+@pytest.mark.parametrize("half", [False, True], ids=["f32", "f16"])
+@pytest.mark.parametrize("channels", [120, 250])
+def test_staged_depthwise(cuda, oracle, bits, half, channels):
+    """The channel-innermost depthwise between integer convs (128 and 256 padded
+    channels, ragged real counts), with NaN, inf and zero inputs."""
+    stream = SeededStream(8200 + channels)
+    program = staged_depthwise_program(stream, channels, bits)
+    x = stream.tensor(24, 17, 29, 2.0)
+    x[3, 4, 5] = np.nan
+    x[7, 10, 20] = np.inf
+    x[:, 15, 28] = 0.0
+    label = f"staged depthwise {channels} w{bits[0]}a{bits[1]}"
+    if half:
+        assert_half_parity(program, [x], oracle, label + " half")
+    else:
+        assert_parity(program, [x], oracle, label)
+
+
 def test_weight_edge_values(cuda, oracle):
     """A zero weight row (scale 1), FP16-subnormal weights, +-65504 weights."""
     stream = SeededStream(9)
