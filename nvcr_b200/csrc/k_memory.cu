@@ -318,17 +318,25 @@ __global__ void __launch_bounds__(256) depthwise3x3_staged_kernel(const float* _
     const int y0 = static_cast<int>(blockIdx.y) * dws_rows;
     const int c0 = static_cast<int>(blockIdx.z) * dws_slab;
     constexpr int halo_pixels = (dws_rows + 2) * (dws_cols + 2);
-    for (int i = threadIdx.x; i < halo_pixels * 8; i += 256) {
+    // All of a thread's halo loads are in flight before any shared-memory store.
+    constexpr int halo_loads = (halo_pixels * 8 + 255) / 256;
+    float4 staged[halo_loads];
+#pragma unroll
+    for (int u = 0; u < halo_loads; ++u) {
+        const int i = static_cast<int>(threadIdx.x) + 256 * u;
         const int pixel = i >> 3;
-        const int quad = i & 7;
         const int ty = pixel / (dws_cols + 2);
         const int tx = pixel - ty * (dws_cols + 2);
         const int y = y0 + ty - 1;
         const int x = x0 + tx - 1;
-        const float4 v = (y >= 0 && y < height && x >= 0 && x < width)
-            ? __ldg(reinterpret_cast<const float4*>(in + (static_cast<std::size_t>(y) * width + x) * c_pad + c0) + quad)
+        staged[u] = (i < halo_pixels * 8 && y >= 0 && y < height && x >= 0 && x < width)
+            ? __ldg(reinterpret_cast<const float4*>(in + (static_cast<std::size_t>(y) * width + x) * c_pad + c0) + (i & 7))
             : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        *reinterpret_cast<float4*>(tile + pixel * dws_stride + 4 * quad) = v;
+    }
+#pragma unroll
+    for (int u = 0; u < halo_loads; ++u) {
+        const int i = static_cast<int>(threadIdx.x) + 256 * u;
+        if (i < halo_pixels * 8) *reinterpret_cast<float4*>(tile + (i >> 3) * dws_stride + 4 * (i & 7)) = staged[u];
     }
     const int quad = threadIdx.x & 7;
     const int col = threadIdx.x >> 3;  // 0..31
