@@ -868,15 +868,49 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
         // The loads are unconditional (pixel 0 stands in outside the window) and
         // the returned mask marks the taps inside it: the mask is applied one
         // tile later, so no select waits for the loads before then.
-        auto window_loads = [&](int t, float (&m)[window_taps]) -> std::uint32_t {
-            int n_index, tx;
-            const int p_tile = by_n_tiles.divide(t, n_index);
-            const int ty = by_tiles_x.divide(p_tile, tx);
-            const int oy = ty * a.patch_h + py;
-            const int ox = tx * a.patch_w + px;
+        // Tile coordinates (N tile, patch column, patch row) of the tiles this set
+        // walks, advanced by the constant tile step instead of divided out per tile.
+        struct TileAt {
+            int n_index, tx, ty;
+        };
+        const int first_tile = static_cast<int>(blockIdx.x) + set * static_cast<int>(gridDim.x);
+        int step_n;
+        const int step_p = by_n_tiles.divide(tile_step, step_n);
+        int step_x;
+        const int step_y = by_tiles_x.divide(step_p, step_x);
+        auto tile_at = [&](int t) {
+            TileAt c;
+            const int p_tile = by_n_tiles.divide(t, c.n_index);
+            c.ty = by_tiles_x.divide(p_tile, c.tx);
+            return c;
+        };
+        auto advance = [&](TileAt& c) {
+            int carry = 0;
+            c.n_index += step_n;
+            if (c.n_index >= a.n_tiles) {
+                c.n_index -= a.n_tiles;
+                carry = 1;
+            }
+            c.tx += step_x + carry;  // < 2 tiles_x: one wrap at most
+            c.ty += step_y;
+            if (c.tx >= a.tiles_x) {
+                c.tx -= a.tiles_x;
+                c.ty += 1;
+            }
+        };
+        const bool pointwise = a.window.kernel_h == 1 && kernel_w == 1;
+        auto window_loads = [&](const TileAt& c, float (&m)[window_taps]) -> std::uint32_t {
+            const int oy = c.ty * a.patch_h + py;
+            const int ox = c.tx * a.patch_w + px;
             const int iy0 = oy * a.window.stride_y - a.window.pad_top;
             const int ix0 = ox * a.window.stride_x - a.window.pad_left;
             const bool real = oy < a.out_h && ox < a.out_w;
+            if (pointwise) {
+                // One pixel: one load.
+                const bool inside = real && iy0 >= 0 && iy0 < a.in_h && ix0 >= 0 && ix0 < a.in_w;
+                m[0] = __ldg(a.pixel_max + (inside ? static_cast<std::size_t>(iy0) * a.in_w + ix0 : 0));
+                return inside ? 1u : 0u;
+            }
             std::uint32_t inside_mask = 0;
 #pragma unroll
             for (int ky = 0; ky < 3; ++ky) {
@@ -894,12 +928,13 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
         };
         float next_window[window_taps];
         std::uint32_t next_mask = 0;
-        const int first_tile = static_cast<int>(blockIdx.x) + set * static_cast<int>(gridDim.x);
-        if (small_window && first_tile < total_tiles) next_mask = window_loads(first_tile, next_window);
+        TileAt next_at = tile_at(first_tile < total_tiles ? first_tile : 0);
+        if (small_window && first_tile < total_tiles) next_mask = window_loads(next_at, next_window);
         for (int t = first_tile; t < total_tiles && ok; t += tile_step, local += producer_sets) {
-            int n_index, tx;
-            const int p_tile = by_n_tiles.divide(t, n_index);
-            const int ty = by_tiles_x.divide(p_tile, tx);
+            const TileAt at = next_at;
+            advance(next_at);
+            const int ty = at.ty;
+            const int tx = at.tx;
             const int oy = ty * a.patch_h + py;
             const int ox = tx * a.patch_w + px;
             const bool real = oy < a.out_h && ox < a.out_w;
@@ -911,7 +946,7 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                 for (int i = 0; i < window_taps; ++i) {
                     if ((next_mask >> i) & 1u) maximum = fmaxf(maximum, next_window[i]);
                 }
-                if (t + tile_step < total_tiles) next_mask = window_loads(t + tile_step, next_window);
+                if (t + tile_step < total_tiles) next_mask = window_loads(next_at, next_window);
             } else if (real) {
                 for (int ky = 0; ky < a.window.kernel_h; ++ky) {
                     const int iy = iy0 + ky;
