@@ -154,3 +154,18 @@ def test_program_handle_without_gpu_refuses_executor(built_library, tmp_path):
     with pytest.raises(ex.ExecutorError) as error:
         loaded.executor()
     assert error.value.code in (ex.ErrorCode.backend_error, ex.ErrorCode.incompatible_target)
+
+
+def test_stack_profile_report_folds_blocks():
+    """The per-op report folds DepthConvBlock indices and sums per run."""
+    from nvcr_b200.stack_profile import report
+
+    segments = [
+        {"label": "integer_conv:i.dec.dec_1.3.ffn.1.sum", "kernel": "integer_conv", "ms": 0.1, "ops": 1e10, "bytes": 1e8},
+        {"label": "integer_conv:i.dec.dec_1.4.ffn.1.sum", "kernel": "integer_conv", "ms": 0.1, "ops": 1e10, "bytes": 1e8},
+        {"label": "conv:i.dec.dec_1.4.dc.2", "kernel": "conv", "ms": 0.05, "ops": 0.0, "bytes": 5e7},
+    ]
+    text = report(segments, 1.0)
+    assert "total 0.250 ms per run" in text
+    assert "| integer_conv:i.dec.dec_1.ffn.1.sum | 2 | 0.200 | 100.0 | 1000 |" in text
+    assert "| conv:i.dec.dec_1.dc.2 | 1 | 0.050 | 0.0 | 1000 |" in text
