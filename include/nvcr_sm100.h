@@ -158,6 +158,14 @@ int nvcr_sm100_synchronize(nvcr_sm100_executor* executor);
  * gave up") and clears the status; the executor and its CUDA context stay usable. */
 int nvcr_sm100_test_wait_timeout(nvcr_sm100_executor* executor, unsigned int limit_ms);
 
+/* Arithmetic self-test (no counterpart in the reference): the sigmoid in the
+ * fused WSiLU epilogues takes 1 / d for d = 1 + exp(-x) in [1, 2^126) as a
+ * refined hardware reciprocal instead of an IEEE division. This counts, in
+ * *mismatches, the floats d with bit patterns first_bits .. first_bits + count - 1
+ * (within [1, 2^126): 0x3f800000 .. 0x7e7fffff) for which the two differ in any
+ * bit. Uses the current device; allocates and frees eight bytes of device memory. */
+int nvcr_sm100_test_reciprocal(unsigned int first_bits, unsigned int count, unsigned long long* mismatches);
+
 /* The stream all work is ordered on (a cudaStream_t). */
 void* nvcr_sm100_stream(const nvcr_sm100_executor* executor);
 

@@ -321,6 +321,26 @@ int nvcr_sm100_test_wait_timeout(nvcr_sm100_executor* executor, unsigned int lim
     });
 }
 
+int nvcr_sm100_test_reciprocal(unsigned int first_bits, unsigned int count, unsigned long long* mismatches) {
+    return guarded([&] {
+        if (mismatches == nullptr) return report(Code::invalid_argument, "null mismatch count");
+        if (first_bits < 0x3f800000u || count > 0x7e800000u - first_bits) {
+            return report(Code::invalid_argument, "the range must lie within [1, 2^126)");
+        }
+        unsigned long long* device = nullptr;
+        cudaError_t status = cudaMalloc(reinterpret_cast<void**>(&device), sizeof(unsigned long long));
+        if (status != cudaSuccess) return report(Code::backend_error, std::string("cudaMalloc: ") + cudaGetErrorString(status));
+        status = cudaMemset(device, 0, sizeof(unsigned long long));
+        if (status == cudaSuccess) status = nvcr_sm100::kernels::check_reciprocal(first_bits, count, device, nullptr);
+        if (status == cudaSuccess) {
+            status = cudaMemcpy(mismatches, device, sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+        }
+        cudaFree(device);
+        if (status != cudaSuccess) return report(Code::backend_error, std::string("reciprocal check: ") + cudaGetErrorString(status));
+        return succeed();
+    });
+}
+
 void* nvcr_sm100_stream(const nvcr_sm100_executor* executor) {
     return executor == nullptr ? nullptr : static_cast<void*>(executor->executor->stream());
 }

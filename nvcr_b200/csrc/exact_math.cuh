@@ -163,9 +163,28 @@ __device__ __forceinline__ float profile_exp(float x) {
     return inside ? y : outside;
 }
 
-// sigmoid(x) = 1 / (1 + exp(-x)) with an IEEE division.
+// 1 / d rounded to nearest-even for d in [1, 2^126) (the sigmoid's denominator
+// 1 + exp(-x) outside its rare extremes), as straight-line code: the hardware
+// approximate reciprocal refined by two Newton-Raphson steps whose residuals
+// 1 - d y come exact from a fused multiply-add (Markstein's method, IBM J. Res.
+// Dev. 34(1), 1990). Checked against the IEEE division for every float in
+// [1, 2^126) by nvcr_sm100_test_reciprocal.
+__device__ __forceinline__ float sigmoid_reciprocal(float d) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(d));
+    float e = __fmaf_rn(-d, y, 1.0f);
+    y = __fmaf_rn(y, e, y);
+    e = __fmaf_rn(-d, y, 1.0f);
+    return __fmaf_rn(y, e, y);
+}
+constexpr float sigmoid_reciprocal_limit = 8.50705917302346158659e37f;  // 2^126
+
+// sigmoid(x) = 1 / (1 + exp(-x)) with the IEEE division's bits: the refined
+// reciprocal for denominators in [1, 2^126), the division itself beyond (a
+// subnormal or zero quotient) and for NaN.
 __device__ __forceinline__ float profile_sigmoid(float x) {
-    return __fdiv_rn(1.0f, __fadd_rn(1.0f, profile_exp(-x)));
+    const float d = __fadd_rn(1.0f, profile_exp(-x));
+    return d < sigmoid_reciprocal_limit ? sigmoid_reciprocal(d) : __fdiv_rn(1.0f, d);
 }
 
 // WSiLU as the reference graph computes it: mul(sigmoid(mul(v, k)), v).

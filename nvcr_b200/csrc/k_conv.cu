@@ -432,9 +432,24 @@ __device__ __noinline__ Sixteen ldexp_add16(Sixteen x, Sixteen bias, int exponen
     return x;
 }
 
+// profile_wsilu of 16 values as straight-line code: each value with the refined
+// reciprocal when its denominator lies in [1, 2^126), the others (kept as the
+// input, marked in a mask) redone with the IEEE division afterwards.
 __device__ __noinline__ Sixteen wsilu16(Sixteen x, float k) {
+    std::uint32_t rare = 0;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) x.v[j] = profile_wsilu(x.v[j], k);
+    for (int j = 0; j < 16; ++j) {
+        const float d = __fadd_rn(1.0f, profile_exp(-__fmul_rn(x.v[j], k)));
+        const bool inside = d < sigmoid_reciprocal_limit;
+        rare |= inside ? 0u : 1u << j;
+        x.v[j] = inside ? __fmul_rn(sigmoid_reciprocal(d), x.v[j]) : x.v[j];
+    }
+    if (rare != 0) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            if ((rare >> j) & 1u) x.v[j] = profile_wsilu(x.v[j], k);
+        }
+    }
     return x;
 }
 
@@ -1544,6 +1559,28 @@ __global__ void wait_timeout_kernel(unsigned long long limit_ns, unsigned int* s
     }
 }
 }  // namespace
+
+namespace {
+// Counts the floats d with bit patterns first .. first + count - 1 for which the
+// sigmoid's reciprocal differs in any bit from the IEEE division 1 / d.
+__global__ void reciprocal_check_kernel(std::uint32_t first, std::uint32_t count, unsigned long long* mismatches) {
+    unsigned int local = 0;
+    for (std::uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x) {
+        const float d = __uint_as_float(first + i);
+        local += __float_as_uint(sigmoid_reciprocal(d)) != __float_as_uint(__fdiv_rn(1.0f, d)) ? 1u : 0u;
+    }
+    local = __reduce_add_sync(0xffffffffu, local);
+    if ((threadIdx.x & 31) == 0 && local != 0) atomicAdd(mismatches, static_cast<unsigned long long>(local));
+}
+}  // namespace
+
+cudaError_t check_reciprocal(std::uint32_t first, std::uint32_t count, unsigned long long* mismatches,
+                             cudaStream_t stream) {
+    // Only the range the sigmoid uses it on: 1 <= d < 2^126.
+    if (first < 0x3f800000u || count > 0x7e800000u - first) return cudaErrorInvalidValue;
+    reciprocal_check_kernel<<<1184, 256, 0, stream>>>(first, count, mismatches);
+    return cudaGetLastError();
+}
 
 cudaError_t wait_timeout(unsigned long long limit_ns, unsigned int* status, cudaStream_t stream) {
     if (limit_ns > 4000000000ull) return cudaErrorInvalidValue;

@@ -136,4 +136,10 @@ cudaError_t encode_int8_map(CUtensorMap* map, const void* base, std::uint64_t ro
 // `status` and returns (the path every kernel takes when a wait runs out).
 cudaError_t wait_timeout(unsigned long long limit_ns, unsigned int* status, cudaStream_t stream);
 
+// Diagnostics: adds to *mismatches (device memory) the count of floats d with
+// bit patterns first .. first + count - 1 (within [1, 2^126)) whose sigmoid
+// reciprocal differs from the IEEE division 1 / d.
+cudaError_t check_reciprocal(std::uint32_t first, std::uint32_t count, unsigned long long* mismatches,
+                             cudaStream_t stream);
+
 }  // namespace nvcr_sm100::kernels

@@ -73,7 +73,7 @@ EXPORTS = [
     "nvcr_sm100_set_profiling", "nvcr_sm100_profile", "nvcr_sm100_program_load", "nvcr_sm100_program_load_memory",
     "nvcr_sm100_program_destroy", "nvcr_sm100_program_tensor_count", "nvcr_sm100_program_tensor_info",
     "nvcr_sm100_program_infer_output_extents", "nvcr_sm100_executor_create_from_program",
-    "nvcr_sm100_run_half_static", "nvcr_sm100_test_wait_timeout",
+    "nvcr_sm100_run_half_static", "nvcr_sm100_test_wait_timeout", "nvcr_sm100_test_reciprocal",
 ]
 
 _lib: ctypes.CDLL | None = None
@@ -110,6 +110,7 @@ def library() -> ctypes.CDLL:
         "nvcr_sm100_run_host": (ctypes.c_int, [vp, tp, sz, tp, sz]),
         "nvcr_sm100_synchronize": (ctypes.c_int, [vp]),
         "nvcr_sm100_test_wait_timeout": (ctypes.c_int, [vp, ctypes.c_uint]),
+        "nvcr_sm100_test_reciprocal": (ctypes.c_int, [ctypes.c_uint, ctypes.c_uint, ctypes.POINTER(ctypes.c_ulonglong)]),
         "nvcr_sm100_stream": (vp, [vp]),
         "nvcr_sm100_last_launch_count": (ctypes.c_int, [vp]),
         "nvcr_sm100_workspace_bytes": (sz, [vp]),
@@ -375,3 +376,12 @@ class CudaExecutor:
         return [{"label": steps[i].label.decode(), "kernel": steps[i].kernel.decode(),
                  "ms": steps[i].milliseconds, "ops": steps[i].algorithmic_ops,
                  "bytes": steps[i].algorithmic_bytes} for i in range(min(count.value, capacity))]
+
+
+def reciprocal_mismatches(first_bits: int, count: int) -> int:
+    """Floats d with bit patterns first_bits .. first_bits + count - 1 (within
+    [1, 2^126)) for which the sigmoid's refined reciprocal differs from the IEEE
+    division 1 / d (arithmetic self-test; runs on the current device)."""
+    mismatches = ctypes.c_ulonglong(0)
+    _check(library().nvcr_sm100_test_reciprocal(first_bits, count, ctypes.byref(mismatches)))
+    return int(mismatches.value)

@@ -12,7 +12,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from nvcr_b200.executor import CudaExecutor
+from nvcr_b200.executor import CudaExecutor, reciprocal_mismatches
 from nvcr_b200.program import OpKind, Program, SeededStream
 from nvcr_b200.workloads import config1, layer_input
 from oracle.oracle import count_differing, same_bits
@@ -586,3 +586,10 @@ def test_graph_replay_half(cuda, oracle):
             executor.synchronize()
             expected = oracle.run(program, [x.astype(np.float32)])[0].astype(np.float16).astype(np.float32)
             assert count_differing(yh.float().cpu().numpy(), expected) == 0, f"call {call}"
+
+
+def test_sigmoid_reciprocal_exhaustive(cuda):
+    """The sigmoid's 1 / (1 + exp(-x)) takes a refined hardware reciprocal for
+    denominators in [1, 2^126): every float there gives the IEEE division's bits."""
+    first, end = 0x3F800000, 0x7E800000  # 1.0 and 2^126
+    assert reciprocal_mismatches(first, end - first) == 0
