@@ -54,6 +54,7 @@
 
 #include "exact_math.cuh"
 #include "kernels.hpp"
+#include "launch.cuh"
 #include "tcgen05.cuh"
 
 #include <climits>
@@ -182,6 +183,8 @@ template <bool Half>
 __global__ void __launch_bounds__(256) stage_pixels_kernel(const void* __restrict__ in, int channels, int c_pad,
                                                            int pixels, void* __restrict__ out,
                                                            float* __restrict__ pixel_max) {
+    grid_dependency_wait();  // the source may come from the kernel before
+    launch_dependents();
     using T = std::conditional_t<Half, unsigned short, float>;
     constexpr int per_block = 16 / static_cast<int>(sizeof(T));  // channels per 16-byte store
     constexpr int blocks_per_pass = Half ? 2 : 4;                 // 16 loads in flight
@@ -244,6 +247,8 @@ template <bool Half, int Pixels>
 __global__ void __launch_bounds__(256) stage_source_kernel(const void* __restrict__ in, int channels, int c_pad,
                                                            int pixels, void* __restrict__ out,
                                                            float* __restrict__ pixel_max) {
+    grid_dependency_wait();  // the source may come from the kernel before
+    launch_dependents();
     using T = std::conditional_t<Half, unsigned short, float>;
     using S = StageShape<Half>;
     constexpr int per_word = Half ? 2 : 1;
@@ -327,13 +332,18 @@ cudaError_t launch_stage(const void* in, int channels, int c_pad, int pixels, vo
     const int block = StageShape<Half>::pixels(c_pad);
     const unsigned blocks = static_cast<unsigned>((static_cast<long long>(pixels) + block - 1) / block);
     switch (block) {
-    case 32: stage_source_kernel<Half, 32><<<blocks, 256, 0, stream>>>(in, channels, c_pad, pixels, out, pixel_max); break;
-    case 64: stage_source_kernel<Half, 64><<<blocks, 256, 0, stream>>>(in, channels, c_pad, pixels, out, pixel_max); break;
-    case 128: stage_source_kernel<Half, 128><<<blocks, 256, 0, stream>>>(in, channels, c_pad, pixels, out, pixel_max); break;
-    case 256: stage_source_kernel<Half, 256><<<blocks, 256, 0, stream>>>(in, channels, c_pad, pixels, out, pixel_max); break;
+    case 32: return launch_overlapped(stage_source_kernel<Half, 32>, dim3(blocks), dim3(256), 0, stream, in, channels,
+                                      c_pad, pixels, out, pixel_max);
+    case 64: return launch_overlapped(stage_source_kernel<Half, 64>, dim3(blocks), dim3(256), 0, stream, in, channels,
+                                       c_pad, pixels, out, pixel_max);
+    case 128: return launch_overlapped(stage_source_kernel<Half, 128>, dim3(blocks), dim3(256), 0, stream, in, channels,
+                                       c_pad, pixels, out, pixel_max);
+    case 256: return launch_overlapped(stage_source_kernel<Half, 256>, dim3(blocks), dim3(256), 0, stream, in, channels,
+                                       c_pad, pixels, out, pixel_max);
     default:
         if constexpr (Half) {
-            stage_source_kernel<Half, 512><<<blocks, 256, 0, stream>>>(in, channels, c_pad, pixels, out, pixel_max);
+            return launch_overlapped(stage_source_kernel<Half, 512>, dim3(blocks), dim3(256), 0, stream, in, channels,
+                                     c_pad, pixels, out, pixel_max);
         } else {
             return cudaErrorInvalidValue;
         }
@@ -352,6 +362,8 @@ template <bool Half>
 __global__ void __launch_bounds__(256) stage_fields_kernel(const void* __restrict__ in, int channels, int in_h,
                                                            int in_w, Window w, int out_h, int out_w, int c_pad,
                                                            void* __restrict__ out, float* __restrict__ field_max) {
+    grid_dependency_wait();  // the source may come from the kernel before
+    launch_dependents();
     using T = std::conditional_t<Half, unsigned short, float>;
     constexpr int per_store = 16 / static_cast<int>(sizeof(T));
     __shared__ long long plane_at[max_field];  // c * in_h * in_w, or -1 for padding
@@ -677,6 +689,9 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
     __syncthreads();
     tmem_fence_after();
     const std::uint32_t tmem = tail->tmem_base;
+    // The weight TMA and the MMA touch only constant weights, shared memory and
+    // TMEM; the other roles wait for the kernels before this one first.
+    launch_dependents();
     volatile int* abort = &tail->abort;
 
     if (warp == tma_warp) {
@@ -795,6 +810,7 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
             barrier_wait(smem_address(&tail->drain), 0u, a.status);
         }
     } else if (warp == halo_warp) {
+        grid_dependency_wait();
         if (lane == 0) {
             // ---------------- activation halo by TMA, one channel group per load
             // The two rings' cursors stay in registers: a tile works on a copy of
@@ -853,6 +869,7 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
             }
         }
     } else if (warp >= epilogue_warps) {
+        grid_dependency_wait();
         // ---------------- activation producers: thread <-> position; set s of
         // the producer_sets takes the CTA's tiles s, s + sets, ...
         const int producer_thread = threadIdx.x - epilogue_threads;
@@ -1133,6 +1150,7 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
         }
     } else {
         // ---------------- epilogue: thread <-> TMEM lane <-> position
+        grid_dependency_wait();
         // Warp w reads TMEM lane quarter w % 4 (positions 32(w % 4) .. +31); with
         // eight epilogue warps, w and w + 4 take the first and second half of the
         // tile's 16-column chunks, with four each warp takes them all.
@@ -1467,9 +1485,8 @@ cudaError_t launch_fused(const CUtensorMap& b_high, const CUtensorMap& b_low, co
     }
     const int tiles = args.p_tiles * args.n_tiles;
     const int grid = tiles < sm_count ? tiles : sm_count;
-    fused_conv_kernel<WL, AL, SourceHalf><<<grid, conv_threads, smem, stream>>>(b_high, b_low, halo, args, buffers,
-                                                                                columns);
-    return cudaGetLastError();
+    return launch_overlapped(fused_conv_kernel<WL, AL, SourceHalf>, dim3(grid), dim3(conv_threads), smem, stream,
+                             b_high, b_low, halo, args, buffers, columns);
 }
 
 template <int WL, int AL>
@@ -1542,9 +1559,11 @@ cudaError_t stage_source(const void* in, int source_half, int channels, int c_pa
     }
     const unsigned blocks = static_cast<unsigned>((static_cast<long long>(pixels) + 255) / 256);
     if (source_half) {
-        stage_pixels_kernel<true><<<blocks, 256, 0, stream>>>(in, channels, c_pad, pixels, out, pixel_max);
+        return launch_overlapped(stage_pixels_kernel<true>, dim3(blocks), dim3(256), 0, stream, in, channels, c_pad,
+                                 pixels, out, pixel_max);
     } else {
-        stage_pixels_kernel<false><<<blocks, 256, 0, stream>>>(in, channels, c_pad, pixels, out, pixel_max);
+        return launch_overlapped(stage_pixels_kernel<false>, dim3(blocks), dim3(256), 0, stream, in, channels, c_pad,
+                                 pixels, out, pixel_max);
     }
     return cudaGetLastError();
 }
@@ -1599,11 +1618,11 @@ cudaError_t stage_receptive_fields(const void* in, int source_half, int channels
     }
     const unsigned blocks = static_cast<unsigned>((positions + 255) / 256);
     if (source_half) {
-        stage_fields_kernel<true><<<blocks, 256, 0, stream>>>(in, channels, in_h, in_w, window, out_h, out_w, c_pad,
-                                                              out, field_max);
+        return launch_overlapped(stage_fields_kernel<true>, dim3(blocks), dim3(256), 0, stream, in, channels, in_h,
+                                 in_w, window, out_h, out_w, c_pad, out, field_max);
     } else {
-        stage_fields_kernel<false><<<blocks, 256, 0, stream>>>(in, channels, in_h, in_w, window, out_h, out_w,
-                                                               c_pad, out, field_max);
+        return launch_overlapped(stage_fields_kernel<false>, dim3(blocks), dim3(256), 0, stream, in, channels, in_h,
+                                 in_w, window, out_h, out_w, c_pad, out, field_max);
     }
     return cudaGetLastError();
 }

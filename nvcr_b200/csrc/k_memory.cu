@@ -7,6 +7,7 @@
 
 #include "exact_math.cuh"
 #include "kernels.hpp"
+#include "launch.cuh"
 
 #include <cuda_fp16.h>
 
@@ -313,6 +314,8 @@ __global__ void __launch_bounds__(256) depthwise3x3_staged_kernel(const float* _
                                                                   float* __restrict__ out,
                                                                   float* __restrict__ pixel_max, int height,
                                                                   int width) {
+    grid_dependency_wait();  // the input may come from the kernel before
+    launch_dependents();
     __shared__ __align__(16) float tile[(dws_rows + 2) * (dws_cols + 2) * dws_stride];
     const int x0 = static_cast<int>(blockIdx.x) * dws_cols;
     const int y0 = static_cast<int>(blockIdx.y) * dws_rows;
@@ -419,9 +422,8 @@ cudaError_t depthwise3x3_staged(const float* weights, const float* bias, int cha
     if (status != cudaSuccess) return status;
     const dim3 grid(static_cast<unsigned>((width + dws_cols - 1) / dws_cols),
                     static_cast<unsigned>((height + dws_rows - 1) / dws_rows), static_cast<unsigned>(c_pad / dws_slab));
-    depthwise3x3_staged_kernel<<<grid, 256, 0, stream>>>(weights, bias, channels, c_pad, in, out, pixel_max, height,
-                                                         width);
-    return cudaGetLastError();
+    return launch_overlapped(depthwise3x3_staged_kernel, grid, dim3(256), 0, stream, weights, bias, channels, c_pad, in,
+                             out, pixel_max, height, width);
 }
 
 cudaError_t half_to_float(const std::uint16_t* in, float* out, std::size_t count, cudaStream_t stream) {
