@@ -964,10 +964,10 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
             f.out_c_pad = round_up(staged_out.channels, 16);
             f.out_max = reinterpret_cast<float*>(base + plan.offsets[step.output] +
                                                  staged_max_offset(staged_out, step.output));
-            status = cudaMemsetAsync(f.out_max, 0,
-                                     static_cast<std::size_t>(staged_out.height) * staged_out.width * sizeof(float),
-                                     stream_);
-            if (status != cudaSuccess) return cuda_error("cudaMemsetAsync staged maxima", status);
+            status = kernels::zero_floats(f.out_max, static_cast<std::size_t>(staged_out.height) * staged_out.width,
+                                          stream_);
+            if (status != cudaSuccess) return cuda_error("zeroing staged maxima", status);
+            ++launches_;
         }
         f.out_channels = conv.out_channels;
         f.d2s_block = step.d2s_block;
@@ -1000,6 +1000,7 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
                 status = kernels::depthwise3x3_staged(weights_ + node.weight_offset, weights_ + node.bias_offset,
                                                       node.out_channels, round_up(node.out_channels, 16), staged_in,
                                                       out, staged_max, out_extent.height, out_extent.width, stream_);
+                launched = 2;  // zeroing of the maxima, then the depthwise
                 break;
             }
             kernels::ConvShape shape{node.in_channels, node.out_channels, node.depthwise ? 1 : 0, in.height, in.width,

@@ -11,6 +11,8 @@
 
 #include <cuda_fp16.h>
 
+#include <algorithm>
+
 namespace nvcr_sm100::kernels {
 namespace {
 
@@ -410,6 +412,25 @@ __global__ void __launch_bounds__(256) depthwise3x3_staged_kernel(const float* _
 
 }  // namespace
 
+namespace {
+// Zeroes `count` floats after the kernels before it in the stream finish (it
+// may be launched early, overlapped with them, like the kernels that follow).
+__global__ void __launch_bounds__(256) zero_floats_kernel(float* __restrict__ out, std::size_t count) {
+    grid_dependency_wait();
+    launch_dependents();
+    for (std::size_t i = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+         i += static_cast<std::size_t>(gridDim.x) * blockDim.x) {
+        out[i] = 0.0f;
+    }
+}
+}  // namespace
+
+cudaError_t zero_floats(float* out, std::size_t count, cudaStream_t stream) {
+    if (count == 0) return cudaSuccess;
+    const unsigned blocks = static_cast<unsigned>(std::min<std::size_t>((count + 255) / 256, 4 * 148));
+    return launch_overlapped(zero_floats_kernel, dim3(blocks), dim3(256), 0, stream, out, count);
+}
+
 cudaError_t depthwise3x3_staged(const float* weights, const float* bias, int channels, int c_pad, const float* in,
                                 float* out, float* pixel_max, int height, int width, cudaStream_t stream) {
     if (height <= 0 || width <= 0) return cudaSuccess;
@@ -417,8 +438,7 @@ cudaError_t depthwise3x3_staged(const float* weights, const float* bias, int cha
         (reinterpret_cast<std::uintptr_t>(out) & 15u) != 0) {
         return cudaErrorInvalidValue;
     }
-    cudaError_t status =
-        cudaMemsetAsync(pixel_max, 0, static_cast<std::size_t>(height) * width * sizeof(float), stream);
+    const cudaError_t status = zero_floats(pixel_max, static_cast<std::size_t>(height) * width, stream);
     if (status != cudaSuccess) return status;
     const dim3 grid(static_cast<unsigned>((width + dws_cols - 1) / dws_cols),
                     static_cast<unsigned>((height + dws_rows - 1) / dws_rows), static_cast<unsigned>(c_pad / dws_slab));

@@ -49,6 +49,9 @@ struct ConvShape {
 };
 cudaError_t conv_fp32(const float* weights, const float* bias, const float* in, float* out, ConvShape shape,
                       cudaStream_t stream);
+// Zeroes `count` floats once the kernels before it in the stream are done
+// (launched overlapped, so the chain of early-starting kernels is not broken).
+cudaError_t zero_floats(float* out, std::size_t count, cudaStream_t stream);
 // Depthwise 3x3 s1 p1 on channel-innermost FP32 tensors [H][W][c_pad] (c_pad
 // 128 or 256, padding channels zero), with each pixel's max |x| (+inf when a
 // value is non-finite): the layout and maxima an integer conv reads.
