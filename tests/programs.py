@@ -135,3 +135,50 @@ def edge_value_input(stream: SeededStream, cin: int = 40) -> np.ndarray:
     x[:, 4, :] = (np.round(x[:, 4, :] * 64) + 0.5) / 64
     x[0, 5, :] = np.float32(3.4e38)
     return x
+
+
+def staged_chain_program(stream: SeededStream, bits) -> Program:
+    """Intermediates that only integer convs read (stored channel-innermost by
+    the producing epilogue): 1x1 40->48 (read by a 3x3 conv and, later, as a
+    residual), 3x3 48->40, 1x1 40->96 + WSiLU + chunk-add -> 48, 1x1 48->48 +
+    residual of the first conv's output; ragged channel counts so the padding
+    channels of the staged records matter."""
+    p = Program(name="staged_chain")
+    x = p.add_input("x", 24)
+
+    def conv(src, cin, cout, name, kernel=(1, 1), pads=(0, 0, 0, 0)):
+        taps = kernel[0] * kernel[1]
+        w = stream.uniform(-0.5, 0.5, cout * cin * taps)
+        b = stream.uniform(-0.2, 0.2, cout)
+        return p.dense_conv(src, cout, w, b, name, kernel=kernel, stride=(1, 1), pads=pads, bits=bits)
+
+    a = conv(x, 24, 48, "a")
+    t = conv(a, 48, 40, "t", kernel=(3, 3), pads=(1, 1, 1, 1))
+    u = conv(t, 40, 96, "u")
+    s = p.unary(OpKind.mul_scalar, u, "us", scalar=4.0)
+    g = p.unary(OpKind.sigmoid, s, "ug")
+    u = p.binary(OpKind.mul, u, g, "uw")
+    h1 = p.unary(OpKind.slice_channels, u, "u0", begin=0, end=48)
+    h2 = p.unary(OpKind.slice_channels, u, "u1", begin=48, end=96)
+    v = p.binary(OpKind.add, h1, h2, "v")
+    y = conv(v, 48, 48, "y")
+    y = p.binary(OpKind.add, y, a, "out")
+    return p.finish([y])
+
+
+def staged_depthwise_program(stream: SeededStream, channels: int, bits) -> Program:
+    """1x1 24->C + WSiLU -> depthwise 3x3 -> 1x1 C->40: the WSiLU conv's output and
+    the depthwise output are read only by the depthwise and the last conv, so both
+    stay channel-innermost and the depthwise runs on that layout."""
+    p = Program(name="staged_depthwise")
+    x = p.add_input("x", 24)
+    t = p.dense_conv(x, channels, stream.uniform(-0.5, 0.5, channels * 24), stream.uniform(-0.2, 0.2, channels),
+                     "t", kernel=(1, 1), stride=(1, 1), pads=(0, 0, 0, 0), bits=bits)
+    s = p.unary(OpKind.mul_scalar, t, "ts", scalar=4.0)
+    g = p.unary(OpKind.sigmoid, s, "tg")
+    t = p.binary(OpKind.mul, t, g, "tw")
+    d = p.conv(t, channels, stream.uniform(-0.5, 0.5, channels * 9), stream.uniform(-0.2, 0.2, channels), "d",
+               depthwise=True, kernel=(3, 3), pads=(1, 1, 1, 1))
+    y = p.dense_conv(d, 40, stream.uniform(-0.5, 0.5, 40 * channels), stream.uniform(-0.2, 0.2, 40), "y",
+                     kernel=(1, 1), stride=(1, 1), pads=(0, 0, 0, 0), bits=bits)
+    return p.finish([y])

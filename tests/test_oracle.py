@@ -21,7 +21,8 @@ import pytest
 from nvcr_b200.program import OpKind, Program, SeededStream
 from oracle.oracle import canonical_digest, count_differing, same_bits
 from tests.golden.cases import program_cases, scalar_inputs, weight_cases
-from tests.programs import CONV_CASES, conv_program, data_movement_program, op_program
+from tests.programs import (CONV_CASES, conv_program, data_movement_program, op_program, staged_chain_program,
+                            staged_depthwise_program)
 
 GOLDEN = json.loads((Path(__file__).resolve().parent / "golden" / "intconv_golden.json").read_text())
 
@@ -177,6 +178,27 @@ def test_oracle_matches_live_reference(oracle, reference, tmp_path, case, bits):
         expected = reference.run(path, [x], weights=weights)
         got = oracle.run(program, [x], weights=weights)
         assert all(count_differing(a, b) == 0 for a, b in zip(expected, got))
+
+
+@pytest.mark.parametrize("bits", [(16, 16), (8, 8)], ids=["w16a16", "w8a8"])
+@pytest.mark.parametrize("which", ["chain", "depthwise120", "depthwise250"])
+def test_oracle_matches_live_reference_on_chains(oracle, reference, tmp_path, bits, which):
+    """The chains behind the staged-intermediate GPU tests (1x1 -> 3x3 -> WSiLU
+    chunk-add -> residual; WSiLU -> depthwise 3x3 -> 1x1), with NaN, inf and zero
+    inputs, agree with the reference bit for bit (NaN equals NaN)."""
+    stream = SeededStream(9100 + bits[0])
+    if which == "chain":
+        program = staged_chain_program(stream, bits)
+    else:
+        program = staged_depthwise_program(stream, int(which[len("depthwise"):]), bits)
+    x = stream.tensor(24, 9, 13, 2.0)
+    x[3, 4, 5] = np.nan
+    x[7, 2, 11] = np.inf
+    x[:, 6, 12] = 0.0
+    path = program.write(tmp_path)
+    expected = reference.run(path, [x])
+    got = oracle.run(program, [x])
+    assert all(count_differing(a, b) == 0 for a, b in zip(expected, got))
 
 
 def test_reference_output_extents(reference, tmp_path):

@@ -17,6 +17,7 @@ from nvcr_b200.program import OpKind, Program, SeededStream
 from nvcr_b200.workloads import config1, layer_input
 from oracle.oracle import count_differing, same_bits
 from tests.programs import (CONV_CASES, conv_program, data_movement_program, edge_value_input, op_program,
+                            staged_chain_program, staged_depthwise_program,
                             sigmoid_program, sigmoid_sweep_values)
 
 pytestmark = pytest.mark.gpu
@@ -209,35 +210,6 @@ def test_wide_record_staging(cuda, oracle, half, cin, h, w):
         assert_parity(program, [x], oracle, f"wide staging {cin}x{h}x{w}")
 
 
-def staged_chain_program(stream: SeededStream, bits) -> Program:
-    """Intermediates that only integer convs read (stored channel-innermost by
-    the producing epilogue): 1x1 40->48 (read by a 3x3 conv and, later, as a
-    residual), 3x3 48->40, 1x1 40->96 + WSiLU + chunk-add -> 48, 1x1 48->48 +
-    residual of the first conv's output; ragged channel counts so the padding
-    channels of the staged records matter."""
-    p = Program(name="staged_chain")
-    x = p.add_input("x", 24)
-
-    def conv(src, cin, cout, name, kernel=(1, 1), pads=(0, 0, 0, 0)):
-        taps = kernel[0] * kernel[1]
-        w = stream.uniform(-0.5, 0.5, cout * cin * taps)
-        b = stream.uniform(-0.2, 0.2, cout)
-        return p.dense_conv(src, cout, w, b, name, kernel=kernel, stride=(1, 1), pads=pads, bits=bits)
-
-    a = conv(x, 24, 48, "a")
-    t = conv(a, 48, 40, "t", kernel=(3, 3), pads=(1, 1, 1, 1))
-    u = conv(t, 40, 96, "u")
-    s = p.unary(OpKind.mul_scalar, u, "us", scalar=4.0)
-    g = p.unary(OpKind.sigmoid, s, "ug")
-    u = p.binary(OpKind.mul, u, g, "uw")
-    h1 = p.unary(OpKind.slice_channels, u, "u0", begin=0, end=48)
-    h2 = p.unary(OpKind.slice_channels, u, "u1", begin=48, end=96)
-    v = p.binary(OpKind.add, h1, h2, "v")
-    y = conv(v, 48, 48, "y")
-    y = p.binary(OpKind.add, y, a, "out")
-    return p.finish([y])
-
-
 @pytest.mark.parametrize("bits", WIDTHS, ids=lambda b: f"w{b[0]}a{b[1]}")
 @pytest.mark.parametrize("half", [False, True], ids=["f32", "f16"])
 def test_staged_intermediates(cuda, oracle, bits, half):
@@ -253,24 +225,6 @@ def test_staged_intermediates(cuda, oracle, bits, half):
         assert_half_parity(program, [x], oracle, f"staged chain half w{bits[0]}a{bits[1]}")
     else:
         assert_parity(program, [x], oracle, f"staged chain w{bits[0]}a{bits[1]}")
-
-
-def staged_depthwise_program(stream: SeededStream, channels: int, bits) -> Program:
-    """1x1 24->C + WSiLU -> depthwise 3x3 -> 1x1 C->40: the WSiLU conv's output and
-    the depthwise output are read only by the depthwise and the last conv, so both
-    stay channel-innermost and the depthwise runs on that layout."""
-    p = Program(name="staged_depthwise")
-    x = p.add_input("x", 24)
-    t = p.dense_conv(x, channels, stream.uniform(-0.5, 0.5, channels * 24), stream.uniform(-0.2, 0.2, channels),
-                     "t", kernel=(1, 1), stride=(1, 1), pads=(0, 0, 0, 0), bits=bits)
-    s = p.unary(OpKind.mul_scalar, t, "ts", scalar=4.0)
-    g = p.unary(OpKind.sigmoid, s, "tg")
-    t = p.binary(OpKind.mul, t, g, "tw")
-    d = p.conv(t, channels, stream.uniform(-0.5, 0.5, channels * 9), stream.uniform(-0.2, 0.2, channels), "d",
-               depthwise=True, kernel=(3, 3), pads=(1, 1, 1, 1))
-    y = p.dense_conv(d, 40, stream.uniform(-0.5, 0.5, 40 * channels), stream.uniform(-0.2, 0.2, 40), "y",
-                     kernel=(1, 1), stride=(1, 1), pads=(0, 0, 0, 0), bits=bits)
-    return p.finish([y])
 
 
 @pytest.mark.parametrize("bits", [(8, 8), (16, 16)], ids=["w8a8", "w16a16"])
