@@ -33,6 +33,7 @@ extern "C" {
 #define NVCR_SM100_INVALID_ARGUMENT 1
 #define NVCR_SM100_INVALID_STATE 2
 #define NVCR_SM100_IO_ERROR 3
+#define NVCR_SM100_MALFORMED_BITSTREAM 4
 #define NVCR_SM100_RESOURCE_EXHAUSTED 5
 #define NVCR_SM100_BACKEND_ERROR 7
 #define NVCR_SM100_NOT_IMPLEMENTED 8
@@ -179,6 +180,27 @@ int nvcr_sm100_set_profiling(nvcr_sm100_executor* executor, int enabled);
  * the profiled runs since the previous call (which are then forgotten);
  * *count receives the number of segments. */
 int nvcr_sm100_profile(nvcr_sm100_executor* executor, nvcr_sm100_step_time* steps, size_t capacity, size_t* count);
+
+/* The numerics-identity payload (reference include/nvcr/bitstream/
+ * numerics_identity.hpp, NumericsIdentityIO::make + serialize,
+ * src/bitstream/numerics_identity.cpp): names the numerics profile and the
+ * exact programs of the codec's normative stages. stage_ids[i] with the 32-byte
+ * program SHA-256 stage_digests[32 i .. 32 i + 31], in the codec's stage order;
+ * ids are 1..128 bytes of printable ASCII without space, 1..64 unique stages.
+ * Writes u8 profile length, the profile id and the 32-byte program-set digest
+ * (SHA-256 of, per stage, u8 id length, id bytes, program digest) to payload;
+ * *payload_size gets its length (at most 161 bytes). Errors:
+ * NVCR_SM100_INVALID_ARGUMENT for bad ids, a duplicate stage, a stage count
+ * outside 1..64 or a payload buffer that is too small. */
+int nvcr_sm100_numerics_identity(const char* profile, const char* const* stage_ids, const unsigned char* stage_digests,
+                                 size_t stage_count, unsigned char* payload, size_t capacity, size_t* payload_size);
+
+/* Reads a numerics-identity payload (reference NumericsIdentityIO::deserialize):
+ * profile gets the NUL-terminated profile id (profile_capacity >= 129 always
+ * suffices), program_set_digest its 32 bytes. NVCR_SM100_MALFORMED_BITSTREAM
+ * for a truncated payload, trailing bytes or an invalid profile id. */
+int nvcr_sm100_numerics_identity_parse(const unsigned char* payload, size_t size, char* profile,
+                                       size_t profile_capacity, unsigned char* program_set_digest);
 
 /* run_half without device allocation. No counterpart in the reference: it
  * exists for hosts that cannot call cudaMalloc while they run (an enqueue

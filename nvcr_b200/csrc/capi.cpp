@@ -4,6 +4,7 @@
 #include "../../include/nvcr_sm100.h"
 
 #include "capi_internal.hpp"
+#include "numerics_identity.hpp"
 #include "sha256.hpp"
 
 #include <cstdio>
@@ -337,6 +338,45 @@ int nvcr_sm100_test_reciprocal(unsigned int first_bits, unsigned int count, unsi
         }
         cudaFree(device);
         if (status != cudaSuccess) return report(Code::backend_error, std::string("reciprocal check: ") + cudaGetErrorString(status));
+        return succeed();
+    });
+}
+
+int nvcr_sm100_numerics_identity(const char* profile, const char* const* stage_ids, const unsigned char* stage_digests,
+                                 size_t stage_count, unsigned char* payload, size_t capacity, size_t* payload_size) {
+    return guarded([&] {
+        if (profile == nullptr || payload == nullptr || payload_size == nullptr ||
+            (stage_count > 0 && (stage_ids == nullptr || stage_digests == nullptr))) {
+            return report(Code::invalid_argument, "null argument");
+        }
+        std::vector<nvcr_sm100::StageDigest> stages(stage_count);
+        for (std::size_t i = 0; i < stage_count; ++i) {
+            if (stage_ids[i] == nullptr) return report(Code::invalid_argument, "null stage id");
+            stages[i].stage_id = stage_ids[i];
+            std::memcpy(stages[i].program_digest.data(), stage_digests + 32 * i, 32);
+        }
+        auto identity = nvcr_sm100::make_numerics_identity(profile, stages);
+        if (!identity) return report(identity.error());
+        auto bytes = nvcr_sm100::serialize_numerics_identity(identity.value());
+        if (!bytes) return report(bytes.error());
+        if (bytes.value().size() > capacity) return report(Code::invalid_argument, "payload buffer is too small");
+        std::memcpy(payload, bytes.value().data(), bytes.value().size());
+        *payload_size = bytes.value().size();
+        return succeed();
+    });
+}
+
+int nvcr_sm100_numerics_identity_parse(const unsigned char* payload, size_t size, char* profile,
+                                       size_t profile_capacity, unsigned char* program_set_digest) {
+    return guarded([&] {
+        if (profile == nullptr || program_set_digest == nullptr) return report(Code::invalid_argument, "null argument");
+        auto identity = nvcr_sm100::parse_numerics_identity(payload, size);
+        if (!identity) return report(identity.error());
+        if (identity.value().profile.size() + 1 > profile_capacity) {
+            return report(Code::invalid_argument, "profile buffer is too small");
+        }
+        std::memcpy(profile, identity.value().profile.c_str(), identity.value().profile.size() + 1);
+        std::memcpy(program_set_digest, identity.value().program_set_digest.data(), 32);
         return succeed();
     });
 }

@@ -74,6 +74,7 @@ EXPORTS = [
     "nvcr_sm100_program_destroy", "nvcr_sm100_program_tensor_count", "nvcr_sm100_program_tensor_info",
     "nvcr_sm100_program_infer_output_extents", "nvcr_sm100_executor_create_from_program",
     "nvcr_sm100_run_half_static", "nvcr_sm100_test_wait_timeout", "nvcr_sm100_test_reciprocal",
+    "nvcr_sm100_numerics_identity", "nvcr_sm100_numerics_identity_parse",
 ]
 
 _lib: ctypes.CDLL | None = None
@@ -111,6 +112,11 @@ def library() -> ctypes.CDLL:
         "nvcr_sm100_synchronize": (ctypes.c_int, [vp]),
         "nvcr_sm100_test_wait_timeout": (ctypes.c_int, [vp, ctypes.c_uint]),
         "nvcr_sm100_test_reciprocal": (ctypes.c_int, [ctypes.c_uint, ctypes.c_uint, ctypes.POINTER(ctypes.c_ulonglong)]),
+        "nvcr_sm100_numerics_identity": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_char_p), ctypes.c_char_p,
+                                                         ctypes.c_size_t, ctypes.c_char_p, ctypes.c_size_t,
+                                                         ctypes.POINTER(ctypes.c_size_t)]),
+        "nvcr_sm100_numerics_identity_parse": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_size_t, ctypes.c_char_p,
+                                                               ctypes.c_size_t, ctypes.c_char_p]),
         "nvcr_sm100_stream": (vp, [vp]),
         "nvcr_sm100_last_launch_count": (ctypes.c_int, [vp]),
         "nvcr_sm100_workspace_bytes": (sz, [vp]),
@@ -385,3 +391,27 @@ def reciprocal_mismatches(first_bits: int, count: int) -> int:
     mismatches = ctypes.c_ulonglong(0)
     _check(library().nvcr_sm100_test_reciprocal(first_bits, count, ctypes.byref(mismatches)))
     return int(mismatches.value)
+
+
+def numerics_identity(profile: str, stages: Sequence[tuple[str, bytes]]) -> bytes:
+    """The numerics-identity payload naming `profile` and the normative stages
+    (id, 32-byte program SHA-256) in the codec's order; raises ExecutorError
+    (invalid_argument) for invalid ids, duplicates or a count outside 1..64."""
+    ids = (ctypes.c_char_p * max(1, len(stages)))(*[sid.encode() for sid, _ in stages])
+    digests = b"".join(bytes(d) for _, d in stages)
+    if any(len(bytes(d)) != 32 for _, d in stages):
+        raise ValueError("program digests are 32 bytes")
+    payload = ctypes.create_string_buffer(1 + 128 + 32)
+    size = ctypes.c_size_t(0)
+    _check(library().nvcr_sm100_numerics_identity(profile.encode(), ids, digests, len(stages), payload,
+                                                  len(payload), ctypes.byref(size)))
+    return payload.raw[:size.value]
+
+
+def parse_numerics_identity(payload: bytes) -> tuple[str, bytes]:
+    """(profile, 32-byte program-set digest) of a numerics-identity payload;
+    raises ExecutorError (malformed_bitstream) for a malformed one."""
+    profile = ctypes.create_string_buffer(129)
+    digest = ctypes.create_string_buffer(32)
+    _check(library().nvcr_sm100_numerics_identity_parse(bytes(payload), len(payload), profile, len(profile), digest))
+    return profile.value.decode(), digest.raw

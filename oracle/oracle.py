@@ -171,6 +171,13 @@ class Reference:
         lib.ref_time_run.restype = ctypes.c_double
         lib.ref_time_run.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(ctypes.c_int32),
                                      ctypes.POINTER(f32p), ctypes.c_int]
+        lib.ref_numerics_identity.restype = ctypes.c_int
+        lib.ref_numerics_identity.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_char_p), ctypes.c_char_p,
+                                              ctypes.c_size_t, ctypes.c_char_p, ctypes.c_size_t,
+                                              ctypes.POINTER(ctypes.c_size_t)]
+        lib.ref_numerics_identity_parse.restype = ctypes.c_int
+        lib.ref_numerics_identity_parse.argtypes = [ctypes.c_char_p, ctypes.c_size_t, ctypes.c_char_p,
+                                                    ctypes.c_size_t, ctypes.c_char_p]
         lib.ref_infer_extents.restype = ctypes.c_int
         lib.ref_infer_extents.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(ctypes.c_int32),
                                           ctypes.c_int, ctypes.POINTER(ctypes.c_int32),
@@ -250,6 +257,23 @@ class Reference:
         if status != 0:
             return status, error.value.decode()  # 1 + ErrorCode
         return 0, [tuple(out[3 * i: 3 * i + 3]) for i in range(max_outputs) if out[3 * i] != 0]
+
+    def numerics_identity(self, profile: str, stages):
+        """(status, payload): NumericsIdentityIO::make + serialize; status 0 or 1 + ErrorCode."""
+        ids = (ctypes.c_char_p * max(1, len(stages)))(*[sid.encode() for sid, _ in stages])
+        digests = b"".join(bytes(d) for _, d in stages)
+        payload = ctypes.create_string_buffer(256)
+        size = ctypes.c_size_t(0)
+        status = self.lib.ref_numerics_identity(profile.encode(), ids, digests, len(stages), payload, len(payload),
+                                                ctypes.byref(size))
+        return status, payload.raw[:size.value] if status == 0 else b""
+
+    def parse_numerics_identity(self, payload: bytes):
+        """(status, profile, digest): NumericsIdentityIO::deserialize."""
+        profile = ctypes.create_string_buffer(256)
+        digest = ctypes.create_string_buffer(32)
+        status = self.lib.ref_numerics_identity_parse(bytes(payload), len(payload), profile, len(profile), digest)
+        return (status, profile.value.decode(), digest.raw) if status == 0 else (status, "", b"")
 
     def quantize_weights(self, weights: np.ndarray, weight_bits: int):
         w = np.ascontiguousarray(weights, np.float32)

@@ -1,7 +1,8 @@
 // C entry points over the reference's own CPU executor, for tests and the CPU
 // baseline only. TEST INFRASTRUCTURE: compiled by oracle/Makefile together with
 // the reference sources it names (src/deterministic/program.cpp,
-// normative_stage.cpp, src/common/{json,sha256,error}.cpp) into
+// normative_stage.cpp, src/common/{json,sha256,error}.cpp,
+// src/bitstream/numerics_identity.cpp) into
 // oracle/_ref/libnvcr_ref.so. Nothing in the product links or loads it.
 //
 // Programs reach the reference through its own loader (load_program,
@@ -10,6 +11,7 @@
 #include "deterministic/det_math.hpp"
 #include "deterministic/normative_stage.hpp"
 #include "deterministic/program.hpp"
+#include "nvcr/bitstream/numerics_identity.hpp"
 
 #include <chrono>
 #include <cstdint>
@@ -164,6 +166,37 @@ float ref_det_int_output(long long acc, float scale, int e, float bias) {
 }
 float ref_half_to_float(std::uint16_t h) { return det::det_half_bits_to_float(h); }
 std::uint16_t ref_float_to_half(float x) { return det::det_float_to_half_bits(x); }
+
+// NumericsIdentityIO::make + serialize (src/bitstream/numerics_identity.cpp):
+// 0 and the payload, or the reference's ErrorCode value plus one.
+int ref_numerics_identity(const char* profile, const char* const* stage_ids, const unsigned char* digests,
+                          std::size_t count, unsigned char* payload, std::size_t capacity, std::size_t* size) {
+    std::vector<nvcr::NormativeStageIdentity> stages(count);
+    for (std::size_t i = 0; i < count; ++i) {
+        stages[i].stage_id = stage_ids[i];
+        std::memcpy(stages[i].program_digest.data(), digests + 32 * i, 32);
+    }
+    auto identity = nvcr::NumericsIdentityIO::make(profile, stages);
+    if (!identity) return static_cast<int>(identity.error().code()) + 1;
+    auto bytes = nvcr::NumericsIdentityIO::serialize(identity.value());
+    if (!bytes) return static_cast<int>(bytes.error().code()) + 1;
+    if (bytes.value().size() > capacity) return -1;
+    std::memcpy(payload, bytes.value().data(), bytes.value().size());
+    *size = bytes.value().size();
+    return 0;
+}
+
+// NumericsIdentityIO::deserialize: 0 with the profile and digest, or ErrorCode + 1.
+int ref_numerics_identity_parse(const unsigned char* payload, std::size_t size, char* profile,
+                                std::size_t profile_capacity, unsigned char* digest) {
+    auto identity = nvcr::NumericsIdentityIO::deserialize(
+        std::span(reinterpret_cast<const std::byte*>(payload), size));
+    if (!identity) return static_cast<int>(identity.error().code()) + 1;
+    if (identity.value().profile.size() + 1 > profile_capacity) return -1;
+    std::memcpy(profile, identity.value().profile.c_str(), identity.value().profile.size() + 1);
+    std::memcpy(digest, identity.value().program_set_digest.data(), 32);
+    return 0;
+}
 
 void ref_free(void* pointer) { std::free(pointer); }
 
