@@ -2,17 +2,20 @@
 // baseline only. TEST INFRASTRUCTURE: compiled by oracle/Makefile together with
 // the reference sources it names (src/deterministic/program.cpp,
 // normative_stage.cpp, src/common/{json,sha256,error}.cpp,
-// src/bitstream/numerics_identity.cpp) into
+// src/bitstream/numerics_identity.cpp, src/deterministic/fx.cpp,
+// src/deterministic/fx_program.cpp) into
 // oracle/_ref/libnvcr_ref.so. Nothing in the product links or loads it.
 //
 // Programs reach the reference through its own loader (load_program,
 // src/deterministic/program.cpp:537-626) from the .detprog.json/.detw files the
 // tests write, so the reference also checks the files' format and digests.
 #include "deterministic/det_math.hpp"
+#include "deterministic/fx_program.hpp"
 #include "deterministic/normative_stage.hpp"
 #include "deterministic/program.hpp"
 #include "nvcr/bitstream/numerics_identity.hpp"
 
+#include <algorithm>
 #include <chrono>
 #include <cstdint>
 #include <cstdio>
@@ -195,6 +198,70 @@ int ref_numerics_identity_parse(const unsigned char* payload, std::size_t size, 
     if (identity.value().profile.size() + 1 > profile_capacity) return -1;
     std::memcpy(profile, identity.value().profile.c_str(), identity.value().profile.size() + 1);
     std::memcpy(digest, identity.value().program_set_digest.data(), 32);
+    return 0;
+}
+
+// nvcr.fx.v1 scalar rules (src/deterministic/fx.cpp:29-37).
+std::int64_t ref_fx_rsr(std::int64_t a, int s) { return det::fx::rsr(a, s); }
+
+std::int64_t ref_fx_delta_act(std::int64_t r, std::int64_t h, int shift, const std::int16_t* dc, std::size_t count) {
+    const det::fx::DeltaTable table{h, shift, std::vector<std::int16_t>(dc, dc + count)};
+    return det::fx::delta_act(r, table);
+}
+
+// fx::load_program (src/deterministic/fx_program.cpp:398-466): 0, or ErrorCode + 1
+// with the reference's message.
+int ref_fx_load_check(const char* directory, const char* stage, char* error, std::size_t error_size) {
+    auto program = det::fx::load_program(directory, stage);
+    if (program) return 0;
+    write_error(error, error_size, program.error().message());
+    return static_cast<int>(program.error().code()) + 1;
+}
+
+// fx::program_digest: 0 and 64 lowercase hex digits plus a terminator, or ErrorCode + 1.
+int ref_fx_program_digest(const char* directory, const char* stage, char* digest) {
+    auto hex = det::fx::program_digest(directory, stage);
+    if (!hex) return static_cast<int>(hex.error().code()) + 1;
+    std::snprintf(digest, 65, "%s", hex.value().c_str());
+    return 0;
+}
+
+// fx::load_program then fx::run (fx_program.cpp:468-525) on int32 NCHW inputs
+// (program.inputs order; extents are (c, h, w) per input). Outputs are malloc'd;
+// output_extents receive (c, h, w) per output. 0, or ErrorCode + 1 with the
+// reference's message (a stage failure is malformed_bitstream).
+int ref_fx_run(const char* directory, const char* stage, int input_count, const std::int32_t* input_extents,
+               const std::int32_t* const* inputs, int output_capacity, std::int32_t* output_extents,
+               std::int32_t** outputs, char* error, std::size_t error_size) {
+    auto program = det::fx::load_program(directory, stage);
+    if (!program) {
+        write_error(error, error_size, program.error().message());
+        return static_cast<int>(program.error().code()) + 1;
+    }
+    std::vector<det::fx::Tensor> tensors;
+    for (int index = 0; index < input_count; ++index) {
+        det::fx::Tensor tensor{input_extents[3 * index], input_extents[3 * index + 1], input_extents[3 * index + 2], {}};
+        tensor.values.assign(inputs[index], inputs[index] + static_cast<std::size_t>(tensor.channels) * tensor.plane());
+        tensors.push_back(std::move(tensor));
+    }
+    auto result = det::fx::run(program.value(), tensors);
+    if (!result) {
+        write_error(error, error_size, result.error().message());
+        return static_cast<int>(result.error().code()) + 1;
+    }
+    const auto& produced = result.value();
+    if (static_cast<int>(produced.size()) > output_capacity) {
+        write_error(error, error_size, "too many outputs");
+        return -1;
+    }
+    for (std::size_t index = 0; index < produced.size(); ++index) {
+        const auto& y = produced[index];
+        output_extents[3 * index] = y.channels;
+        output_extents[3 * index + 1] = y.height;
+        output_extents[3 * index + 2] = y.width;
+        outputs[index] = static_cast<std::int32_t*>(std::malloc(std::max<std::size_t>(1, y.values.size()) * 4));
+        std::memcpy(outputs[index], y.values.data(), y.values.size() * 4);
+    }
     return 0;
 }
 

@@ -38,6 +38,26 @@ def reference():
 
 
 @pytest.fixture(scope="session")
+def fx_oracle():
+    from oracle.fx import FxOracle
+    from oracle.oracle import build
+
+    build(reference=True)
+    return FxOracle()
+
+
+@pytest.fixture(scope="session")
+def fx_reference():
+    from oracle.fx import FxReference
+    from oracle.oracle import Reference, build
+
+    build(reference=True)
+    if not Reference.available():
+        pytest.skip("the reference CPU executor (oracle/_ref) is not built here")
+    return FxReference()
+
+
+@pytest.fixture(scope="session")
 def cuda(built_library):
     import torch
 
