@@ -217,6 +217,31 @@ int nvcr_sm100_numerics_identity_parse(const unsigned char* payload, size_t size
 int nvcr_sm100_run_half_static(nvcr_sm100_executor* executor, const nvcr_sm100_tensor* inputs, size_t input_count,
                                const nvcr_sm100_tensor* outputs, size_t output_count);
 
+/* nvcr.fx.v1 stage programs (format nvcr.fx-program.v1): the reference's
+ * fx::load_program and fx::program_digest (src/deterministic/fx_program.hpp:
+ * 70-75, fx_program.cpp:394-466). */
+typedef struct nvcr_sm100_fx_program nvcr_sm100_fx_program;
+
+/* Loads <directory>/<stage>.fxprog.json and the data file it names, with the
+ * profile's load-time refusals (weight, bias, shift and table bounds, every
+ * tensor and data reference in range). Errors as the reference's loader:
+ * NVCR_SM100_MISSING_ARTIFACT (no program file), NVCR_SM100_IO_ERROR (no data
+ * file), NVCR_SM100_DIGEST_MISMATCH (the data file's SHA-256 differs from the
+ * one the JSON pins), NVCR_SM100_INVALID_ARGUMENT (any other refusal). */
+int nvcr_sm100_fx_program_load(const char* directory, const char* stage, nvcr_sm100_fx_program** program);
+void nvcr_sm100_fx_program_destroy(nvcr_sm100_fx_program* program);
+/* Lowercase hex SHA-256 of <directory>/<stage>.fxprog.json, NUL-terminated
+ * (65 bytes): the program's identity. */
+int nvcr_sm100_fx_program_digest(const char* directory, const char* stage, char* digest_hex);
+/* Counts of a loaded program, and its digest (65 bytes). No counterpart in the
+ * reference (its Program fields are read directly). */
+int nvcr_sm100_fx_program_summary(const nvcr_sm100_fx_program* program, size_t* tensor_count, size_t* node_count,
+                                  size_t* input_count, size_t* output_count, char* digest_hex);
+/* Node `index` of a loaded program: its op name (as in the program file), the
+ * number of inputs and the output tensor id. No counterpart in the reference. */
+int nvcr_sm100_fx_program_node(const nvcr_sm100_fx_program* program, size_t index, const char** op,
+                               size_t* input_count, uint32_t* output);
+
 #ifdef __cplusplus
 }
 #endif

@@ -4,6 +4,7 @@
 #include "../../include/nvcr_sm100.h"
 
 #include "capi_internal.hpp"
+#include "fx_program.hpp"
 #include "numerics_identity.hpp"
 #include "sha256.hpp"
 
@@ -17,6 +18,10 @@
 
 struct nvcr_sm100_program {
     nvcr_sm100::Program program;
+};
+
+struct nvcr_sm100_fx_program {
+    nvcr_sm100::fx::FxProgram program;
 };
 
 namespace {
@@ -415,6 +420,61 @@ int nvcr_sm100_profile(nvcr_sm100_executor* executor, nvcr_sm100_step_time* step
         }
         return succeed();
     });
+}
+
+int nvcr_sm100_fx_program_load(const char* directory, const char* stage, nvcr_sm100_fx_program** program) {
+    return guarded([&] {
+        if (directory == nullptr || stage == nullptr || program == nullptr) {
+            return report(Code::invalid_argument, "null argument");
+        }
+        *program = nullptr;
+        auto loaded = nvcr_sm100::fx::load_fx_program(directory, stage);
+        if (!loaded) return report(loaded.error());
+        *program = new nvcr_sm100_fx_program{std::move(loaded.value())};
+        return succeed();
+    });
+}
+
+void nvcr_sm100_fx_program_destroy(nvcr_sm100_fx_program* program) { delete program; }
+
+int nvcr_sm100_fx_program_digest(const char* directory, const char* stage, char* digest_hex) {
+    return guarded([&] {
+        if (directory == nullptr || stage == nullptr || digest_hex == nullptr) {
+            return report(Code::invalid_argument, "null argument");
+        }
+        auto digest = nvcr_sm100::fx::fx_program_digest(directory, stage);
+        if (!digest) return report(digest.error());
+        std::memcpy(digest_hex, digest.value().c_str(), digest.value().size() + 1);
+        return succeed();
+    });
+}
+
+int nvcr_sm100_fx_program_summary(const nvcr_sm100_fx_program* program, size_t* tensor_count, size_t* node_count,
+                                  size_t* input_count, size_t* output_count, char* digest_hex) {
+    if (program == nullptr || tensor_count == nullptr || node_count == nullptr || input_count == nullptr ||
+        output_count == nullptr || digest_hex == nullptr) {
+        return report(Code::invalid_argument, "null argument");
+    }
+    const auto& p = program->program;
+    *tensor_count = p.tensor_names.size();
+    *node_count = p.nodes.size();
+    *input_count = p.inputs.size();
+    *output_count = p.outputs.size();
+    std::memcpy(digest_hex, p.digest_hex.c_str(), p.digest_hex.size() + 1);
+    return succeed();
+}
+
+int nvcr_sm100_fx_program_node(const nvcr_sm100_fx_program* program, size_t index, const char** op,
+                               size_t* input_count, uint32_t* output) {
+    if (program == nullptr || op == nullptr || input_count == nullptr || output == nullptr) {
+        return report(Code::invalid_argument, "null argument");
+    }
+    if (index >= program->program.nodes.size()) return report(Code::invalid_argument, "node index out of range");
+    const auto& node = program->program.nodes[index];
+    *op = nvcr_sm100::fx::op_name(node.op);
+    *input_count = node.inputs.size();
+    *output = node.output;
+    return succeed();
 }
 
 }  // extern "C"

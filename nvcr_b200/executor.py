@@ -74,7 +74,9 @@ EXPORTS = [
     "nvcr_sm100_program_destroy", "nvcr_sm100_program_tensor_count", "nvcr_sm100_program_tensor_info",
     "nvcr_sm100_program_infer_output_extents", "nvcr_sm100_executor_create_from_program",
     "nvcr_sm100_run_half_static", "nvcr_sm100_test_wait_timeout", "nvcr_sm100_test_reciprocal",
-    "nvcr_sm100_numerics_identity", "nvcr_sm100_numerics_identity_parse",
+    "nvcr_sm100_numerics_identity", "nvcr_sm100_numerics_identity_parse", "nvcr_sm100_fx_program_load",
+    "nvcr_sm100_fx_program_destroy", "nvcr_sm100_fx_program_digest", "nvcr_sm100_fx_program_summary",
+    "nvcr_sm100_fx_program_node",
 ]
 
 _lib: ctypes.CDLL | None = None
@@ -132,6 +134,13 @@ def library() -> ctypes.CDLL:
         "nvcr_sm100_program_infer_output_extents": (ctypes.c_int, [vp, tp, sz, tp, sz]),
         "nvcr_sm100_executor_create_from_program": (ctypes.c_int, [vp, vp, handle_out]),
         "nvcr_sm100_run_half_static": (ctypes.c_int, [vp, tp, sz, tp, sz]),
+        "nvcr_sm100_fx_program_load": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, handle_out]),
+        "nvcr_sm100_fx_program_destroy": (None, [vp]),
+        "nvcr_sm100_fx_program_digest": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p]),
+        "nvcr_sm100_fx_program_summary": (ctypes.c_int, [vp, ctypes.POINTER(sz), ctypes.POINTER(sz), ctypes.POINTER(sz),
+                                                         ctypes.POINTER(sz), ctypes.c_char_p]),
+        "nvcr_sm100_fx_program_node": (ctypes.c_int, [vp, sz, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(sz),
+                                                      ctypes.POINTER(ctypes.c_uint32)]),
     }
     for name, (restype, argtypes) in signatures.items():
         function = getattr(lib, name)
