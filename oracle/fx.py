@@ -195,8 +195,10 @@ class FxOracle:
     def im2col(x: np.ndarray, k: int, stride: int) -> np.ndarray:
         pad = 1 if k == 3 else 0
         c, h, w = x.shape
-        out_h = (h + 2 * pad - k) // stride + 1
-        out_w = (w + 2 * pad - k) // stride + 1
+        # The reference sizes the output with C++ integer division, which truncates
+        # toward zero: a 2x2 stride-2 im2col of a 1-pixel-high input has one row.
+        out_h = int((h + 2 * pad - k) / stride) + 1
+        out_w = int((w + 2 * pad - k) / stride) + 1
         padded = np.zeros((c, h + 2 * pad + stride, w + 2 * pad + stride), np.int32)
         padded[:, pad:pad + h, pad:pad + w] = x
         y = np.zeros((c, k, k, out_h, out_w), np.int32)

@@ -225,6 +225,20 @@ def test_sat_table_and_param_row_edges(fx_oracle, fx_reference, tmp_path):
             assert status == STAGE_FAILURE and reason == "qp outside the parameter table"
 
 
+def test_im2col_of_thin_inputs_matches_reference(fx_oracle, fx_reference, tmp_path):
+    """Output sizes use C++ truncating division: a 2x2 stride-2 im2col of a
+    1-pixel-high or -wide input keeps one row or column."""
+    rng = np.random.default_rng(5)
+    for k, stride in ((2, 2), (3, 2), (3, 1)):
+        for h, w in ((1, 1), (1, 5), (4, 1), (2, 3), (3, 3)):
+            x = rng.integers(-100, 100, (2, h, w)).astype(np.int32)
+            status, outputs, _ = agree(fx_oracle, fx_reference, tmp_path,
+                                       one_op_program({"op": "im2col", "kernel": k, "stride": stride}, [2], 2 * k * k),
+                                       [x], stage=f"i{k}{stride}{h}{w}")
+            assert status == 0 and outputs[0].shape[1:] == (int((h + 2 * (k == 3) - k) / stride) + 1,
+                                                            int((w + 2 * (k == 3) - k) / stride) + 1)
+
+
 def test_run_time_refusals_match_reference(fx_oracle, fx_reference, tmp_path):
     """Shapes a valid program cannot run on: both sides refuse (invalid_argument)."""
     cases = [
@@ -310,8 +324,7 @@ def random_single_op(rng: np.random.Generator):
         return {"op": kind, "factor": r}, [c], c * r * r, [tensor(c, h * r, w * r)], tables
     if kind == "im2col":
         k, stride = [(3, 1), (3, 2), (2, 2)][int(rng.integers(0, 3))]
-        hh, ww = max(h, k - 1 if k == 3 else 2), max(w, 2)
-        return {"op": kind, "kernel": k, "stride": stride}, [c], c * k * k, [tensor(c, hh, ww)], tables
+        return {"op": kind, "kernel": k, "stride": stride}, [c], c * k * k, [tensor(c)], tables
     crop = (int(rng.integers(1, h + 1)), int(rng.integers(1, w + 1)))
     return {"op": "crop_like"}, [c, 1], c, [tensor(c), tensor(1, *crop)], tables
 
