@@ -242,6 +242,34 @@ int nvcr_sm100_fx_program_summary(const nvcr_sm100_fx_program* program, size_t* 
 int nvcr_sm100_fx_program_node(const nvcr_sm100_fx_program* program, size_t index, const char** op,
                                size_t* input_count, uint32_t* output);
 
+/* An executor of one loaded fx program on the current device and `stream`
+ * (a cudaStream_t; NULL for the default stream). It replaces the reference's
+ * fx::run (src/deterministic/fx_program.cpp:468-525): the same int32 outputs,
+ * and on any input the same outcome. The executor keeps a copy of the program
+ * (the handle may be destroyed afterwards) and uploads its parameters at the
+ * first run; creation and extent inference touch no device. */
+typedef struct nvcr_sm100_fx_executor nvcr_sm100_fx_executor;
+int nvcr_sm100_fx_executor_create(const nvcr_sm100_fx_program* program, void* stream,
+                                  nvcr_sm100_fx_executor** executor);
+void nvcr_sm100_fx_executor_destroy(nvcr_sm100_fx_executor* executor);
+/* (channels, height, width) of each output for these input extents (3 int32
+ * per tensor, program.inputs / program.outputs order). No counterpart in the
+ * reference (its run sizes outputs as it goes). */
+int nvcr_sm100_fx_infer_output_extents(nvcr_sm100_fx_executor* executor, const int32_t* input_extents,
+                                       size_t input_count, int32_t* output_extents, size_t output_count);
+/* Runs the program on batch-1 NCHW int32 tensors: host memory when
+ * device_memory is 0 (copies inside the call), device memory otherwise. Returns
+ * after the run (the stream is synchronised). NVCR_SM100_MALFORMED_BITSTREAM
+ * for a stage failure (a gemm pre-activation with |r| >= 2^29 - 1, a stored
+ * value outside [-2^30, 2^30], an input outside that bound, a qp outside a
+ * param_row table): the failure the reference meets first, outputs
+ * unspecified. NVCR_SM100_INVALID_ARGUMENT for inputs whose count or shapes the
+ * program cannot take. */
+int nvcr_sm100_fx_run(nvcr_sm100_fx_executor* executor, const int32_t* const* inputs, const int32_t* input_extents,
+                      size_t input_count, int32_t* const* outputs, size_t output_count, int device_memory);
+/* Kernels launched by the last run. No counterpart in the reference. */
+int nvcr_sm100_fx_last_launch_count(const nvcr_sm100_fx_executor* executor);
+
 #ifdef __cplusplus
 }
 #endif

@@ -4,6 +4,7 @@
 #include "../../include/nvcr_sm100.h"
 
 #include "capi_internal.hpp"
+#include "fx_executor.hpp"
 #include "fx_program.hpp"
 #include "numerics_identity.hpp"
 #include "sha256.hpp"
@@ -22,6 +23,10 @@ struct nvcr_sm100_program {
 
 struct nvcr_sm100_fx_program {
     nvcr_sm100::fx::FxProgram program;
+};
+
+struct nvcr_sm100_fx_executor {
+    std::unique_ptr<nvcr_sm100::fx::FxExecutor> executor;
 };
 
 namespace {
@@ -475,6 +480,68 @@ int nvcr_sm100_fx_program_node(const nvcr_sm100_fx_program* program, size_t inde
     *input_count = node.inputs.size();
     *output = node.output;
     return succeed();
+}
+
+int nvcr_sm100_fx_executor_create(const nvcr_sm100_fx_program* program, void* stream,
+                                   nvcr_sm100_fx_executor** executor) {
+    return guarded([&] {
+        if (program == nullptr || executor == nullptr) return report(Code::invalid_argument, "null argument");
+        *executor = nullptr;
+        auto created = nvcr_sm100::fx::FxExecutor::create(program->program, static_cast<cudaStream_t>(stream));
+        if (!created) return report(created.error());
+        *executor = new nvcr_sm100_fx_executor{std::move(created.value())};
+        return succeed();
+    });
+}
+
+void nvcr_sm100_fx_executor_destroy(nvcr_sm100_fx_executor* executor) { delete executor; }
+
+namespace {
+
+std::vector<nvcr_sm100::fx::FxExtent> fx_extents(const int32_t* extents, size_t count) {
+    std::vector<nvcr_sm100::fx::FxExtent> out(count);
+    for (size_t i = 0; i < count; ++i) out[i] = {extents[3 * i], extents[3 * i + 1], extents[3 * i + 2]};
+    return out;
+}
+
+}  // namespace
+
+int nvcr_sm100_fx_infer_output_extents(nvcr_sm100_fx_executor* executor, const int32_t* input_extents,
+                                       size_t input_count, int32_t* output_extents, size_t output_count) {
+    return guarded([&] {
+        if (executor == nullptr || (input_count > 0 && input_extents == nullptr) ||
+            (output_count > 0 && output_extents == nullptr)) {
+            return report(Code::invalid_argument, "null argument");
+        }
+        auto inferred = executor->executor->infer_output_extents(fx_extents(input_extents, input_count));
+        if (!inferred) return report(inferred.error());
+        if (inferred.value().size() != output_count) return report(Code::invalid_argument, "wrong number of outputs");
+        for (size_t i = 0; i < output_count; ++i) {
+            output_extents[3 * i] = inferred.value()[i].channels;
+            output_extents[3 * i + 1] = inferred.value()[i].height;
+            output_extents[3 * i + 2] = inferred.value()[i].width;
+        }
+        return succeed();
+    });
+}
+
+int nvcr_sm100_fx_run(nvcr_sm100_fx_executor* executor, const int32_t* const* inputs, const int32_t* input_extents,
+                      size_t input_count, int32_t* const* outputs, size_t output_count, int device_memory) {
+    return guarded([&] {
+        if (executor == nullptr || (input_count > 0 && (inputs == nullptr || input_extents == nullptr)) ||
+            (output_count > 0 && outputs == nullptr)) {
+            return report(Code::invalid_argument, "null argument");
+        }
+        std::vector<const std::int32_t*> in(inputs, inputs + input_count);
+        std::vector<std::int32_t*> out(outputs, outputs + output_count);
+        auto ran = executor->executor->run(in, fx_extents(input_extents, input_count), out, device_memory != 0);
+        if (!ran) return report(ran.error());
+        return succeed();
+    });
+}
+
+int nvcr_sm100_fx_last_launch_count(const nvcr_sm100_fx_executor* executor) {
+    return executor == nullptr ? -1 : executor->executor->last_launch_count();
 }
 
 }  // extern "C"

@@ -229,3 +229,38 @@ def test_malformed_json_matches_reference(fx_reference, tmp_path):
         broken = text[:cut] + rng.choice(["", "}", "{", ",", "\"", "]", "nul", "1e999"]) + text[cut + rng.randint(0, 3):]
         (tmp_path / "k.fxprog.json").write_text(broken)
         same_decision(fx_reference, tmp_path, "k")
+
+
+def test_executor_extents_match_oracle_shapes(fx_oracle, tmp_path):
+    """The executor's host planning (no GPU): output extents equal the oracle's
+    output shapes on seeded single ops and whole programs, and inputs the
+    oracle refuses for their shapes are refused the same way."""
+    from nvcr_b200.fx import FxExecutor
+    from tests.fx_programs import decoder_like_inputs
+    from tests.test_fx_oracle import random_single_op
+
+    rng = np.random.default_rng(2026)
+    cases = []
+    for _ in range(300):
+        op, ins, out, inputs, tables = random_single_op(rng)
+        cases.append((one_op_program(op, ins, out, tables), inputs))
+    for seed in range(20):
+        generator = np.random.default_rng(seed)
+        program = decoder_like(generator, channels=4 * (1 + seed % 4))
+        cases.append((program, decoder_like_inputs(generator, program, 1 + seed % 9, 2 + seed % 5)))
+    cases.append((one_op_program({"op": "add"}, [2, 2], 2),
+                  [np.zeros((2, 2, 2), np.int32), np.zeros((2, 2, 3), np.int32)]))
+    cases.append((one_op_program({"op": "pixel_unshuffle", "factor": 2}, [1], 4), [np.zeros((1, 3, 4), np.int32)]))
+    for index, (program, inputs) in enumerate(cases):
+        write_program(tmp_path, f"e{index % 5}", program)
+        status, outputs, _ = fx_oracle.run(program, inputs)
+        with load_program(tmp_path, f"e{index % 5}") as loaded, FxExecutor(loaded) as executor:
+            try:
+                extents = executor.infer_output_extents([x.shape for x in inputs])
+            except ExecutorError as error:
+                assert status == ErrorCode.invalid_argument + 1 and error.code == ErrorCode.invalid_argument
+                continue
+            if status == 0:
+                assert extents == [y.shape for y in outputs]
+            else:
+                assert status != ErrorCode.invalid_argument + 1  # only value-dependent failures remain
