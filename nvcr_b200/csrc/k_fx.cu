@@ -57,43 +57,46 @@ __global__ void __launch_bounds__(gemm_pixels) gemm_kernel(GemmArgs a, unsigned 
                                                            unsigned long long* failure) {
     const std::size_t p = static_cast<std::size_t>(blockIdx.x) * gemm_pixels + threadIdx.x;
     if (p >= a.pixels) return;
-    const int g0 = static_cast<int>(blockIdx.y) * gemm_groups;
-    const int owned = min(gemm_groups, a.groups - g0);  // >= 1: gridDim.y = ceil(groups / 4)
     constexpr int rows = gemm_groups * G;
-    std::int64_t acc[rows];
+    // Group tiles stride over gridDim.y (at most 65535), so any row count runs.
+    for (int g0 = static_cast<int>(blockIdx.y) * gemm_groups; g0 < a.groups;
+         g0 += static_cast<int>(gridDim.y) * gemm_groups) {
+        const int owned = min(gemm_groups, a.groups - g0);  // >= 1 inside the loop
+        std::int64_t acc[rows];
 #pragma unroll
-    for (int r = 0; r < rows; ++r) acc[r] = 0;
-    const std::int16_t* w = a.weights + static_cast<std::size_t>(g0) * G * a.in_channels;
-    for (int k = 0; k < a.in_channels; ++k) {
-        std::int64_t digit = rsr(a.x[static_cast<std::size_t>(k) * a.pixels + p], a.input_shift);
-        digit = digit > digit2_max ? digit2_max : digit < -digit2_max ? -digit2_max : digit;
-        const int xi = static_cast<int>(digit);
+        for (int r = 0; r < rows; ++r) acc[r] = 0;
+        const std::int16_t* w = a.weights + static_cast<std::size_t>(g0) * G * a.in_channels;
+        for (int k = 0; k < a.in_channels; ++k) {
+            std::int64_t digit = rsr(a.x[static_cast<std::size_t>(k) * a.pixels + p], a.input_shift);
+            digit = digit > digit2_max ? digit2_max : digit < -digit2_max ? -digit2_max : digit;
+            const int xi = static_cast<int>(digit);
 #pragma unroll
-        for (int r = 0; r < rows; ++r) {
-            if (r < owned * G) {
-                const int wk = w[static_cast<std::size_t>(r) * a.in_channels + k];
-                acc[r] += static_cast<std::int64_t>(wk) * xi;
+            for (int r = 0; r < rows; ++r) {
+                if (r < owned * G) {
+                    const int wk = w[static_cast<std::size_t>(r) * a.in_channels + k];
+                    acc[r] += static_cast<std::int64_t>(wk) * xi;
+                }
             }
         }
-    }
 #pragma unroll
-    for (int gi = 0; gi < gemm_groups; ++gi) {
-        if (gi < owned) {
-            const int g = g0 + gi;
-            const unsigned long long position = static_cast<unsigned long long>(p) * a.groups + g;
-            std::int64_t sum = 0;
+        for (int gi = 0; gi < gemm_groups; ++gi) {
+            if (gi < owned) {
+                const int g = g0 + gi;
+                const unsigned long long position = static_cast<unsigned long long>(p) * a.groups + g;
+                std::int64_t sum = 0;
 #pragma unroll
-            for (int j = 0; j < G; ++j) {
-                const int o = g * G + j;
-                const std::int64_t r = rsr(acc[gi * G + j] + a.bias[o], a.shifts[o]);
-                if (r >= gemm_limit || r <= -gemm_limit) record(failure, node_key | (position << 1));
-                sum += a.table.dc != nullptr ? delta_act(r, a.table) : r;
+                for (int j = 0; j < G; ++j) {
+                    const int o = g * G + j;
+                    const std::int64_t r = rsr(acc[gi * G + j] + a.bias[o], a.shifts[o]);
+                    if (r >= gemm_limit || r <= -gemm_limit) record(failure, node_key | (position << 1));
+                    sum += a.table.dc != nullptr ? delta_act(r, a.table) : r;
+                }
+                const std::size_t at = static_cast<std::size_t>(g) * a.pixels + p;
+                if (a.residual0 != nullptr) sum += a.residual0[at];
+                if (a.residual1 != nullptr) sum += a.residual1[at];
+                if (outside_stored(sum)) record(failure, node_key | (position << 1) | 1u);
+                a.y[at] = static_cast<std::int32_t>(sum);
             }
-            const std::size_t at = static_cast<std::size_t>(g) * a.pixels + p;
-            if (a.residual0 != nullptr) sum += a.residual0[at];
-            if (a.residual1 != nullptr) sum += a.residual1[at];
-            if (outside_stored(sum)) record(failure, node_key | (position << 1) | 1u);
-            a.y[at] = static_cast<std::int32_t>(sum);
         }
     }
 }
@@ -271,9 +274,10 @@ cudaError_t check_input(const std::int32_t* x, std::size_t count, unsigned long 
 cudaError_t gemm(const GemmArgs& args, unsigned long long node_key, unsigned long long* failure, cudaStream_t stream) {
     if (args.pixels == 0 || args.groups == 0) return cudaSuccess;
     if (args.in_channels < 1 || (args.group != 1 && args.group != 2 && args.group != 4)) return cudaErrorInvalidValue;
-    const dim3 grid(static_cast<unsigned>((args.pixels + gemm_pixels - 1) / gemm_pixels),
-                    static_cast<unsigned>((args.groups + gemm_groups - 1) / gemm_groups));
-    if (grid.y > 65535u) return cudaErrorInvalidValue;
+    const std::size_t pixel_tiles = (args.pixels + gemm_pixels - 1) / gemm_pixels;
+    const int group_tiles = (args.groups + gemm_groups - 1) / gemm_groups;
+    if (pixel_tiles > 0x7fffffffu) return cudaErrorInvalidValue;
+    const dim3 grid(static_cast<unsigned>(pixel_tiles), static_cast<unsigned>(std::min(group_tiles, 65535)));
     switch (args.group) {
     case 1: gemm_kernel<1><<<grid, gemm_pixels, 0, stream>>>(args, node_key, failure); break;
     case 2: gemm_kernel<2><<<grid, gemm_pixels, 0, stream>>>(args, node_key, failure); break;
