@@ -10,6 +10,8 @@
  *   reference src/provider/tensorrt/session.cpp:1464-1467,1526-1594 (exact stages)
  * Every output is bit-identical to the reference's CPU executor run_cpu
  * (src/deterministic/program.cpp:702-820); NaN payloads are unspecified.
+ * The nvcr_sm100_fx_* functions at the end load and run programs of the other
+ * profile, nvcr.fx.v1 (reference src/deterministic/fx_program.hpp:70-79).
  *
  * Plain C types only. Every function returns NVCR_SM100_OK (0) or
  * 1 + the reference's nvcr::ErrorCode value (include/nvcr/common/error.hpp:11-34),
@@ -241,6 +243,13 @@ int nvcr_sm100_fx_program_summary(const nvcr_sm100_fx_program* program, size_t* 
  * number of inputs and the output tensor id. No counterpart in the reference. */
 int nvcr_sm100_fx_program_node(const nvcr_sm100_fx_program* program, size_t index, const char** op,
                                size_t* input_count, uint32_t* output);
+
+/* Name and channel count of a loaded program's input (is_output = 0) or output
+ * (is_output = 1) `index`, in program.inputs / program.outputs order: the order
+ * nvcr_sm100_fx_run takes tensors in. `name` lives as long as the program
+ * handle. The reference reads these as Program fields (fx_program.hpp:62-66). */
+int nvcr_sm100_fx_program_tensor(const nvcr_sm100_fx_program* program, int is_output, size_t index,
+                                 const char** name, int32_t* channels);
 
 /* An executor of one loaded fx program on the current device and `stream`
  * (a cudaStream_t; NULL for the default stream). It replaces the reference's

@@ -482,6 +482,19 @@ int nvcr_sm100_fx_program_node(const nvcr_sm100_fx_program* program, size_t inde
     return succeed();
 }
 
+int nvcr_sm100_fx_program_tensor(const nvcr_sm100_fx_program* program, int is_output, size_t index,
+                                 const char** name, int32_t* channels) {
+    if (program == nullptr || name == nullptr || channels == nullptr) {
+        return report(Code::invalid_argument, "null argument");
+    }
+    const auto& p = program->program;
+    const auto& ids = is_output ? p.outputs : p.inputs;
+    if (index >= ids.size()) return report(Code::invalid_argument, "tensor index out of range");
+    *name = p.tensor_names[ids[index]].c_str();
+    *channels = p.tensor_channels[ids[index]];
+    return succeed();
+}
+
 int nvcr_sm100_fx_executor_create(const nvcr_sm100_fx_program* program, void* stream,
                                    nvcr_sm100_fx_executor** executor) {
     return guarded([&] {

@@ -76,7 +76,7 @@ EXPORTS = [
     "nvcr_sm100_run_half_static", "nvcr_sm100_test_wait_timeout", "nvcr_sm100_test_reciprocal",
     "nvcr_sm100_numerics_identity", "nvcr_sm100_numerics_identity_parse", "nvcr_sm100_fx_program_load",
     "nvcr_sm100_fx_program_destroy", "nvcr_sm100_fx_program_digest", "nvcr_sm100_fx_program_summary",
-    "nvcr_sm100_fx_program_node", "nvcr_sm100_fx_executor_create", "nvcr_sm100_fx_executor_destroy",
+    "nvcr_sm100_fx_program_node", "nvcr_sm100_fx_program_tensor", "nvcr_sm100_fx_executor_create", "nvcr_sm100_fx_executor_destroy",
     "nvcr_sm100_fx_infer_output_extents", "nvcr_sm100_fx_run", "nvcr_sm100_fx_last_launch_count",
 ]
 
@@ -142,6 +142,7 @@ def library() -> ctypes.CDLL:
                                                          ctypes.POINTER(sz), ctypes.c_char_p]),
         "nvcr_sm100_fx_program_node": (ctypes.c_int, [vp, sz, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(sz),
                                                       ctypes.POINTER(ctypes.c_uint32)]),
+        "nvcr_sm100_fx_program_tensor": (ctypes.c_int, [vp, ctypes.c_int, sz, ctypes.POINTER(ctypes.c_char_p), i32p]),
         "nvcr_sm100_fx_executor_create": (ctypes.c_int, [vp, vp, handle_out]),
         "nvcr_sm100_fx_executor_destroy": (None, [vp]),
         "nvcr_sm100_fx_infer_output_extents": (ctypes.c_int, [vp, i32p, sz, i32p, sz]),

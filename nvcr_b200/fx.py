@@ -40,6 +40,19 @@ class FxProgram:
                                                   ctypes.byref(output)))
             nodes.append(FxNodeInfo(op.value.decode(), inputs.value, output.value))
         self.nodes = nodes
+        self.inputs = self._tensors(0, self.input_count)
+        self.outputs = self._tensors(1, self.output_count)
+
+    def _tensors(self, is_output: int, count: int) -> list[tuple[str, int]]:
+        """(name, channels) of the program's inputs or outputs, in run order."""
+        tensors = []
+        for index in range(count):
+            name = ctypes.c_char_p()
+            channels = ctypes.c_int32(0)
+            _check(library().nvcr_sm100_fx_program_tensor(self._handle, is_output, index, ctypes.byref(name),
+                                                          ctypes.byref(channels)))
+            tensors.append((name.value.decode(), channels.value))
+        return tensors
 
     def close(self) -> None:
         if self._handle:

@@ -70,6 +70,8 @@ def test_valid_programs_load_like_the_reference(fx_reference, tmp_path):
         loaded = load_program(tmp_path, "v")
         assert [n.op for n in loaded.nodes] == [n["op"] for n in program["nodes"]]
         assert [n.output for n in loaded.nodes] == [n["output"] for n in program["nodes"]]
+        assert loaded.inputs == [program["tensors"][i] for i in program["inputs"]]
+        assert loaded.outputs == [program["tensors"][i] for i in program["outputs"]]
         status, digest = fx_reference.program_digest(tmp_path, "v")
         assert status == 0 and loaded.digest == digest
 
