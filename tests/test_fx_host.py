@@ -129,3 +129,10 @@ def test_stage_failure_before_a_shape_refusal(fx_host, fx_oracle, tmp_path):
     for value, expected in ((1 << 30, STAGE_FAILURE), (1, INVALID)):
         status, _, _ = matches_oracle(fx_host, fx_oracle, tmp_path, program, [pixel(value), wide])
         assert status == expected
+
+
+def test_empty_and_thin_tensors(fx_host, fx_oracle, tmp_path):
+    from tests.test_fx_oracle import empty_and_thin_cases
+
+    for index, (program, inputs) in enumerate(empty_and_thin_cases()):
+        matches_oracle(fx_host, fx_oracle, tmp_path, program, inputs, stage=f"z{index % 3}")

@@ -384,3 +384,46 @@ def test_golden_fx_programs(fx_oracle, tmp_path, entry):
     for y, golden in zip(outputs, entry["outputs"]):
         assert y.reshape(-1)[:6].tolist() == golden["head"]
         assert arrays_digest([y]) == golden["sha256"]
+
+
+def empty_and_thin_cases():
+    """(program, inputs): each op on zero-height, zero-width and 1-pixel tensors."""
+    rng = np.random.default_rng(1)
+    ops = [
+        ({"op": "im2col", "kernel": 3, "stride": 1}, [2], 18),
+        ({"op": "im2col", "kernel": 3, "stride": 2}, [2], 18),
+        ({"op": "im2col", "kernel": 2, "stride": 2}, [2], 8),
+        ({"op": "depthwise3x3", "weights": np.ones((2, 3, 3), np.int32), "bias": np.ones(2, np.int64),
+          "shift": np.ones(2, np.int32)}, [2], 2),
+        ({"op": "affine", "alpha": 3, "beta": 1, "shift": 1}, [2], 2),
+        ({"op": "pixel_shuffle", "factor": 2}, [8], 2),
+        ({"op": "pixel_unshuffle", "factor": 2}, [2], 8),
+        ({"op": "slice", "begin": 1, "end": 2}, [2], 1),
+        ({"op": "concat"}, [2, 2], 4),
+        ({"op": "add"}, [2, 2], 2),
+        ({"op": "mul", "shift": 2}, [2, 1], 2),
+        ({"op": "crop_like"}, [2, 1], 2),
+        (dict(gemm_1x1(5), in_channels=2, out_channels=2, weights=np.ones((2, 2), np.int16),
+              bias=np.ones(2, np.int64), shift=np.ones(2, np.int32)), [2], 2),
+        ({"op": "param_row", "rows": np.arange(6, dtype=np.int64).reshape(3, 2)}, [1], 2),
+    ]
+    cases = []
+    for op, ins, out in ops:
+        for height, width in ((0, 0), (0, 3), (3, 0), (1, 1), (1, 2), (2, 1), (0, 1)):
+            inputs = []
+            for index, channels in enumerate(ins):
+                h, w = height, width
+                if op["op"] == "crop_like" and index == 1:
+                    h, w = min(height, 1), min(width, 1)
+                if op["op"] == "mul" and index == 1:
+                    h, w = 1, 1
+                inputs.append(rng.integers(-5, 5, (channels, h, w)).astype(np.int32))
+            cases.append((one_op_program(op, ins, out), inputs))
+    return cases
+
+
+def test_empty_and_thin_tensors_match_reference(fx_oracle, fx_reference, tmp_path):
+    """Zero-size images run (im2col of an empty image can still have a row:
+    sizes use truncating division); a param_row on an empty input fails."""
+    for index, (program, inputs) in enumerate(empty_and_thin_cases()):
+        agree(fx_oracle, fx_reference, tmp_path, program, inputs, stage=f"z{index % 3}")
