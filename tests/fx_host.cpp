@@ -177,12 +177,14 @@ cudaError_t cudaMemsetAsync(void* to, int value, size_t size, cudaStream_t) {
 cudaError_t cudaStreamSynchronize(cudaStream_t) { return cudaSuccess; }
 const char* cudaGetErrorString(cudaError_t) { return "host build"; }
 
-// Loads <directory>/<stage> and runs it on int32 NCHW host tensors through the
-// executor, as nvcr_b200.fx.FxExecutor.run does: outputs are malloc'd with
-// their extents in out_extents. Returns 0 or ErrorCode + 1, with the message.
+// Loads <directory>/<stage> and runs it on int32 NCHW tensors through the
+// executor, as nvcr_b200.fx.FxExecutor.run does, taking the executor's
+// host-memory branch (device_memory 0) or its device-memory branch (here both
+// are host memory): outputs are malloc'd with their extents in out_extents.
+// Returns 0 or ErrorCode + 1, with the message.
 int fxh_run(const char* directory, const char* stage, int input_count, const std::int32_t* extents,
             const std::int32_t* const* inputs, int output_capacity, std::int32_t* out_extents, std::int32_t** outputs,
-            char* message, size_t message_size) {
+            char* message, size_t message_size, int device_memory) {
     using namespace nvcr_sm100;
     const auto report = [&](const Error& error) {
         std::snprintf(message, message_size, "%s", error.message.c_str());
@@ -202,7 +204,7 @@ int fxh_run(const char* directory, const char* stage, int input_count, const std
     auto inferred = executor.infer_output_extents(shapes);
     if (!inferred) {
         // Run anyway, so a stage failure met before the refusal is what is reported.
-        auto ran = executor.run(in, shapes, {}, true);
+        auto ran = executor.run(in, shapes, {}, device_memory != 0);
         return report(ran ? inferred.error() : ran.error());
     }
     if (static_cast<int>(inferred.value().size()) > output_capacity) return -1;
@@ -215,7 +217,7 @@ int fxh_run(const char* directory, const char* stage, int input_count, const std
         outputs[i] = static_cast<std::int32_t*>(std::malloc((e.count() == 0 ? 1 : e.count()) * sizeof(std::int32_t)));
         out.push_back(outputs[i]);
     }
-    auto ran = executor.run(in, shapes, out, true);
+    auto ran = executor.run(in, shapes, out, device_memory != 0);
     if (!ran) return report(ran.error());
     return 0;
 }

@@ -37,12 +37,14 @@ class FxHost:
         lib = ctypes.CDLL(str(build()))
         lib.fxh_run.restype = ctypes.c_int
         lib.fxh_run.argtypes = [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_int, _i32p, ctypes.POINTER(_i32p),
-                                ctypes.c_int, _i32p, ctypes.POINTER(_i32p), ctypes.c_char_p, ctypes.c_size_t]
+                                ctypes.c_int, _i32p, ctypes.POINTER(_i32p), ctypes.c_char_p, ctypes.c_size_t,
+                                ctypes.c_int]
         lib.fxh_free.argtypes = [ctypes.c_void_p]
         self.lib = lib
 
-    def run(self, directory, stage: str, inputs, capacity: int = 16):
-        """(status, outputs, message): status 0 or ErrorCode + 1."""
+    def run(self, directory, stage: str, inputs, capacity: int = 16, device_memory: bool = True):
+        """(status, outputs, message): status 0 or ErrorCode + 1; device_memory
+        picks the executor's branch (both run on host memory here)."""
         keep = [np.ascontiguousarray(x, np.int32) for x in inputs]
         extents = np.array([d for x in keep for d in x.shape] or [0], np.int32)
         pointers = (_i32p * max(1, len(keep)))(*[x.ctypes.data_as(_i32p) for x in keep])
@@ -51,7 +53,8 @@ class FxHost:
         message = ctypes.create_string_buffer(512)
         status = self.lib.fxh_run(str(directory).encode(), stage.encode(), len(keep),
                                   extents.ctypes.data_as(_i32p), pointers, capacity,
-                                  out_extents.ctypes.data_as(_i32p), outputs, message, 512)
+                                  out_extents.ctypes.data_as(_i32p), outputs, message, 512,
+                                  1 if device_memory else 0)
         result = []
         for index in range(capacity):
             if not outputs[index]:

@@ -26,7 +26,10 @@ def fx_host():
 def matches_oracle(fx_host, fx_oracle, tmp_path, program, inputs, stage="h"):
     write_program(tmp_path, stage, program)
     expected = fx_oracle.run(program, inputs)
-    got = fx_host.run(tmp_path, stage, inputs)
+    got = fx_host.run(tmp_path, stage, inputs, device_memory=True)
+    host_branch = fx_host.run(tmp_path, stage, inputs, device_memory=False)
+    assert host_branch[0] == got[0] and host_branch[2] == got[2]
+    assert all(np.array_equal(a, b) for a, b in zip(host_branch[1], got[1]))
     assert got[0] == expected[0], (got[2], expected[2])
     if expected[0] == 0:
         assert len(got[1]) == len(expected[1])

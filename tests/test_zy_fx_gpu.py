@@ -16,8 +16,9 @@ from tests.test_fx_oracle import (gemm_1x1, one_op_program, pixel, random_single
                                   reference_program_test_program)
 
 # Skipped until these tests have run on a B200: the fx device path compiles for
-# sm_100a and its host planning is tested on CPU (tests/test_fx_program.py), but
-# no GPU time was left to run the kernels when it was written.
+# sm_100a, and its code compiled for the host passes these same cases on CPU
+# (tests/test_fx_host.py), but no GPU time was left to run the kernels when it
+# was written.
 pytestmark = [pytest.mark.gpu, pytest.mark.skip(reason="nvcr.fx.v1 device path not yet run on a B200")]
 
 
@@ -149,3 +150,10 @@ def test_stage_failure_before_a_shape_refusal(cuda, fx_oracle, tmp_path):
     for value, expected in ((1 << 30, STAGE_FAILURE), (1, INVALID)):
         status, _, _ = matches_oracle(fx_oracle, tmp_path, program, [pixel(value), wide])
         assert status == expected
+
+
+def test_empty_and_thin_tensors(cuda, fx_oracle, tmp_path):
+    from tests.test_fx_oracle import empty_and_thin_cases
+
+    for index, (program, inputs) in enumerate(empty_and_thin_cases()):
+        matches_oracle(fx_oracle, tmp_path, program, inputs, stage=f"z{index % 3}", device_memory=index % 2 == 0)
