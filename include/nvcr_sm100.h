@@ -279,6 +279,35 @@ int nvcr_sm100_fx_run(nvcr_sm100_fx_executor* executor, const int32_t* const* in
 /* Kernels launched by the last run. No counterpart in the reference. */
 int nvcr_sm100_fx_last_launch_count(const nvcr_sm100_fx_executor* executor);
 
+/* DCVC-RT inter-stage glue on the device, exact numerics: the steps between a
+ * decoder's spatial stages, on the caller's stream (a cudaStream_t; NULL for
+ * the default stream), so no host round trip is needed between steps. FP16
+ * tensors are bit patterns, batch-first NCHW, in device memory. Each returns
+ * once its kernel is enqueued; NVCR_SM100_INVALID_ARGUMENT for what the
+ * reference's host ops refuse. */
+
+/* Reference build_decode_indexes(..., exact = true) (src/dcvcrt/host_ops.cpp:
+ * 542-556; GPU form src/dcvcrt/backend/tensorrt/cuda_ops.cu:463-476, 807-820):
+ * the entropy table of each scale, #{ i : clamp(scale, 0.11, 16) >= T[i] } over
+ * the 127 exact thresholds, or 0 where a positive force-zero threshold is not
+ * exceeded. */
+int nvcr_sm100_dcvc_build_decode_indexes(const uint16_t* scales, uint8_t* indexes, size_t count,
+                                         float force_zero_threshold, void* stream);
+/* Reference build_encode_indexes(..., exact = true) (host_ops.cpp:523-540):
+ * (symbol << 8) | table, 0 where forced to zero; symbols are integers in
+ * [-128, 127]. */
+int nvcr_sm100_dcvc_build_encode_indexes(const uint16_t* symbols, const uint16_t* scales, int16_t* indexes,
+                                         size_t count, float force_zero_threshold, void* stream);
+/* Reference make_four_way_mask / make_two_way_mask (host_ops.cpp:307-349):
+ * ways 4 (stage 0..3) or 2 (stage 0..1); channels a multiple of ways. */
+int nvcr_sm100_dcvc_make_mask(uint16_t* mask, int32_t batch, int32_t channels, int32_t height, int32_t width,
+                              int ways, int stage, void* stream);
+/* Reference restore_four_way / restore_two_way (host_ops.cpp:412-428, 456-472):
+ * output[d] = (symbol + mean[d]) * mask[d] for the `ways` destinations of each
+ * symbol; symbols hold volume / ways values, the rest the full output shape. */
+int nvcr_sm100_dcvc_restore(const uint16_t* symbols, const uint16_t* means, const uint16_t* mask, uint16_t* output,
+                            int32_t batch, int32_t channels, int32_t height, int32_t width, int ways, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -5,6 +5,7 @@
 
 #include "capi_internal.hpp"
 #include "fx_executor.hpp"
+#include "glue_kernels.hpp"
 #include "fx_program.hpp"
 #include "numerics_identity.hpp"
 #include "sha256.hpp"
@@ -555,6 +556,44 @@ int nvcr_sm100_fx_run(nvcr_sm100_fx_executor* executor, const int32_t* const* in
 
 int nvcr_sm100_fx_last_launch_count(const nvcr_sm100_fx_executor* executor) {
     return executor == nullptr ? -1 : executor->executor->last_launch_count();
+}
+
+namespace {
+
+int glue_status(cudaError_t status, const char* refusal) {
+    if (status == cudaErrorInvalidValue) return report(Code::invalid_argument, refusal);
+    if (status != cudaSuccess) return report(Code::backend_error, cudaGetErrorString(status));
+    return succeed();
+}
+
+}  // namespace
+
+int nvcr_sm100_dcvc_build_decode_indexes(const uint16_t* scales, uint8_t* indexes, size_t count,
+                                         float force_zero_threshold, void* stream) {
+    return glue_status(nvcr_sm100::glue::build_decode_indexes(scales, indexes, count, force_zero_threshold,
+                                                               static_cast<cudaStream_t>(stream)),
+                       "empty or null tensor");
+}
+
+int nvcr_sm100_dcvc_build_encode_indexes(const uint16_t* symbols, const uint16_t* scales, int16_t* indexes,
+                                         size_t count, float force_zero_threshold, void* stream) {
+    return glue_status(nvcr_sm100::glue::build_encode_indexes(symbols, scales, indexes, count, force_zero_threshold,
+                                                               static_cast<cudaStream_t>(stream)),
+                       "empty or null tensor");
+}
+
+int nvcr_sm100_dcvc_make_mask(uint16_t* mask, int32_t batch, int32_t channels, int32_t height, int32_t width,
+                              int ways, int stage, void* stream) {
+    return glue_status(nvcr_sm100::glue::make_mask(mask, batch, channels, height, width, ways, stage,
+                                                   static_cast<cudaStream_t>(stream)),
+                       "mask shape, ways or stage invalid");
+}
+
+int nvcr_sm100_dcvc_restore(const uint16_t* symbols, const uint16_t* means, const uint16_t* mask, uint16_t* output,
+                            int32_t batch, int32_t channels, int32_t height, int32_t width, int ways, void* stream) {
+    return glue_status(nvcr_sm100::glue::restore(symbols, means, mask, output, batch, channels, height, width, ways,
+                                                 static_cast<cudaStream_t>(stream)),
+                       "restore shape or ways invalid");
 }
 
 }  // extern "C"

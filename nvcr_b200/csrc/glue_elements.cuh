@@ -1,0 +1,191 @@
+#pragma once
+
+// DCVC-RT's inter-stage glue under an exact numerics profile, per output
+// element: the exact scale-to-entropy-table index, the four- and two-way
+// checkerboard masks and the restore of the masked latents (reference
+// src/dcvcrt/host_ops.cpp:307-349, 412-472, 523-556 and scale_index.hpp).
+// Tensors are FP16 bit patterns; every arithmetic step is one IEEE binary32
+// operation rounded to nearest even, as the reference's host code does, and
+// FP16 stores round to nearest even with NaN stored as 0x7e00 (sign kept).
+// The kernels (k_glue.cu) are grid-stride loops over these functions, which
+// are also compiled for the host so the same code can be checked on CPU.
+
+#include <cstddef>
+#include <cstdint>
+#include <cstring>
+
+#if defined(__CUDACC__)
+#define GLUE_HD __host__ __device__ __forceinline__
+#else
+#define GLUE_HD inline
+#endif
+
+namespace nvcr_sm100::glue {
+
+using Half = std::uint16_t;
+
+GLUE_HD std::uint32_t float_bits(float value) {
+#if defined(__CUDA_ARCH__)
+    return __float_as_uint(value);
+#else
+    std::uint32_t bits;
+    std::memcpy(&bits, &value, 4);
+    return bits;
+#endif
+}
+
+GLUE_HD float bits_float(std::uint32_t bits) {
+#if defined(__CUDA_ARCH__)
+    return __uint_as_float(bits);
+#else
+    float value;
+    std::memcpy(&value, &bits, 4);
+    return value;
+#endif
+}
+
+// One binary32 operation each, never contracted into an FMA.
+GLUE_HD float add(float a, float b) {
+#if defined(__CUDA_ARCH__)
+    return __fadd_rn(a, b);
+#else
+    return a + b;
+#endif
+}
+
+GLUE_HD float mul(float a, float b) {
+#if defined(__CUDA_ARCH__)
+    return __fmul_rn(a, b);
+#else
+    return a * b;
+#endif
+}
+
+// binary16 -> binary32, exact.
+GLUE_HD float to_float(Half h) {
+    const std::uint32_t sign = static_cast<std::uint32_t>(h & 0x8000u) << 16;
+    const std::uint32_t exponent = (h >> 10) & 0x1fu;
+    std::uint32_t mantissa = h & 0x3ffu;
+    if (exponent == 31u) return bits_float(sign | 0x7f800000u | (mantissa << 13));
+    if (exponent != 0u) return bits_float(sign | ((exponent + 112u) << 23) | (mantissa << 13));
+    if (mantissa == 0u) return bits_float(sign);
+    // Subnormal: normalise the mantissa into an implicit-one float.
+    int shift = 0;
+    while ((mantissa & 0x400u) == 0u) {
+        mantissa <<= 1;
+        ++shift;
+    }
+    return bits_float(sign | (static_cast<std::uint32_t>(113 - shift) << 23) | ((mantissa & 0x3ffu) << 13));
+}
+
+// binary32 -> binary16, round to nearest even; overflow to infinity, NaN to 0x7e00.
+GLUE_HD Half to_half(float value) {
+    const std::uint32_t bits = float_bits(value);
+    const std::uint32_t sign = (bits >> 16) & 0x8000u;
+    const std::uint32_t magnitude = bits & 0x7fffffffu;
+    if (magnitude > 0x7f800000u) return static_cast<Half>(sign | 0x7e00u);
+    if (magnitude >= 0x477ff000u) return static_cast<Half>(sign | 0x7c00u);  // 65520 and up round to infinity
+    if (magnitude < 0x38800000u) {                                          // below 2^-14: a subnormal half
+        if (magnitude < 0x33000000u) return static_cast<Half>(sign);         // at most 2^-25: rounds to zero
+        const std::uint32_t exponent = magnitude >> 23;                      // 102..112
+        const std::uint32_t significand = (magnitude & 0x7fffffu) | 0x800000u;
+        const std::uint32_t shift = 126u - exponent;                         // 14..24: units of 2^-24
+        std::uint32_t q = significand >> shift;
+        const std::uint32_t rest = significand & ((1u << shift) - 1u);
+        const std::uint32_t half = 1u << (shift - 1u);
+        if (rest > half || (rest == half && (q & 1u))) ++q;
+        return static_cast<Half>(sign | q);
+    }
+    std::uint32_t q = ((magnitude >> 23) - 112u) << 10 | ((magnitude >> 13) & 0x3ffu);
+    const std::uint32_t rest = magnitude & 0x1fffu;
+    if (rest > 0x1000u || (rest == 0x1000u && (q & 1u))) ++q;  // a carry steps the exponent, as it should
+    return static_cast<Half>(sign | q);
+}
+
+// The shapes the reference's host ops accept: positive extents, channels a
+// multiple of `ways` (2 or 4).
+GLUE_HD bool valid_shape(int batch, int channels, int height, int width, int ways) {
+    return batch > 0 && channels > 0 && height > 0 && width > 0 && (ways == 2 || ways == 4) && channels % ways == 0;
+}
+
+inline constexpr float scale_min = 0.11f;
+inline constexpr float scale_max = 16.0f;
+
+// #{ i in 1..127 : clamp(scale) >= thresholds[i - 1] }; NaN maps to table 0.
+GLUE_HD std::uint8_t exact_scale_index(float scale, const float* thresholds) {
+    if (!(scale >= scale_min)) scale = scale_min;
+    if (scale > scale_max) scale = scale_max;
+    int low = 0;
+    int high = 127;
+    while (low < high) {
+        const int middle = (low + high + 1) / 2;
+        if (thresholds[middle - 1] <= scale) {
+            low = middle;
+        } else {
+            high = middle - 1;
+        }
+    }
+    return static_cast<std::uint8_t>(low);
+}
+
+// Decode indexes: the table of each scale, 0 where a positive force-zero
+// threshold is not exceeded.
+GLUE_HD void decode_index(const Half* scales, std::uint8_t* out, float force_zero, const float* thresholds,
+                          std::size_t i) {
+    const float scale = to_float(scales[i]);
+    out[i] = force_zero > 0.0f && scale <= force_zero ? 0 : exact_scale_index(scale, thresholds);
+}
+
+// Encode indexes: symbol in the high byte, table in the low byte (0 where
+// forced to zero). Symbols are integers in [-128, 127].
+GLUE_HD void encode_index(const Half* symbols, const Half* scales, std::int16_t* out, float force_zero,
+                          const float* thresholds, std::size_t i) {
+    const float scale = to_float(scales[i]);
+    if (force_zero > 0.0f && scale <= force_zero) {
+        out[i] = 0;
+        return;
+    }
+    const auto symbol = static_cast<std::int16_t>(static_cast<int>(to_float(symbols[i])));
+    out[i] = static_cast<std::int16_t>(static_cast<std::uint16_t>(static_cast<std::uint16_t>(symbol) << 8) |
+                                       exact_scale_index(scale, thresholds));
+}
+
+// Element i of a [batch][channels][height][width] mask: channel quarter q is
+// selected where the pixel's parity (y & 1) * 2 + (x & 1) is pattern[stage][q],
+// with the patterns {0,1,2,3}, {3,2,1,0}, {2,3,0,1}, {1,0,3,2} of the four
+// stages, i.e. q ^ s with s = 0, 3, 2, 1 = (4 - stage) & 3.
+GLUE_HD void four_way_mask(Half* mask, int channels, int height, int width, int stage, std::size_t i) {
+    const std::size_t plane = static_cast<std::size_t>(height) * width;
+    const int channel = static_cast<int>((i / plane) % channels);
+    const int y = static_cast<int>((i % plane) / width);
+    const int x = static_cast<int>(i % width);
+    const int quarter = channel / (channels / 4);
+    const int parity = (y & 1) * 2 + (x & 1);
+    mask[i] = (quarter ^ ((4 - stage) & 3)) == parity ? 0x3c00u : 0x0000u;  // 1.0 or 0.0
+}
+
+// Two-way: the first channel half takes the diagonal pixels at stage 0 and the
+// off-diagonal ones at stage 1; the second half the others.
+GLUE_HD void two_way_mask(Half* mask, int channels, int height, int width, int stage, std::size_t i) {
+    const std::size_t plane = static_cast<std::size_t>(height) * width;
+    const int channel = static_cast<int>((i / plane) % channels);
+    const int y = static_cast<int>((i % plane) / width);
+    const int x = static_cast<int>(i % width);
+    const bool first_half = channel < channels / 2;
+    const bool diagonal = (y & 1) == (x & 1);
+    const bool selected = stage == 0 ? first_half == diagonal : first_half != diagonal;
+    mask[i] = selected ? 0x3c00u : 0x0000u;
+}
+
+// Restore: output[d] = (symbol[i] + mean[d]) * mask[d] for each of the `parts`
+// (4 or 2) destinations d = i + part * part_size of symbol i.
+GLUE_HD void restore(const Half* symbols, const Half* means, const Half* mask, Half* out, std::size_t part_size,
+                     int parts, std::size_t i) {
+    const float symbol = to_float(symbols[i]);
+    for (int part = 0; part < parts; ++part) {
+        const std::size_t d = i + static_cast<std::size_t>(part) * part_size;
+        out[d] = to_half(mul(add(symbol, to_float(means[d])), to_float(mask[d])));
+    }
+}
+
+}  // namespace nvcr_sm100::glue

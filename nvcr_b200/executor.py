@@ -78,6 +78,8 @@ EXPORTS = [
     "nvcr_sm100_fx_program_destroy", "nvcr_sm100_fx_program_digest", "nvcr_sm100_fx_program_summary",
     "nvcr_sm100_fx_program_node", "nvcr_sm100_fx_program_tensor", "nvcr_sm100_fx_executor_create", "nvcr_sm100_fx_executor_destroy",
     "nvcr_sm100_fx_infer_output_extents", "nvcr_sm100_fx_run", "nvcr_sm100_fx_last_launch_count",
+    "nvcr_sm100_dcvc_build_decode_indexes", "nvcr_sm100_dcvc_build_encode_indexes", "nvcr_sm100_dcvc_make_mask",
+    "nvcr_sm100_dcvc_restore",
 ]
 
 _lib: ctypes.CDLL | None = None
@@ -148,6 +150,10 @@ def library() -> ctypes.CDLL:
         "nvcr_sm100_fx_infer_output_extents": (ctypes.c_int, [vp, i32p, sz, i32p, sz]),
         "nvcr_sm100_fx_run": (ctypes.c_int, [vp, ctypes.POINTER(vp), i32p, sz, ctypes.POINTER(vp), sz, ctypes.c_int]),
         "nvcr_sm100_fx_last_launch_count": (ctypes.c_int, [vp]),
+        "nvcr_sm100_dcvc_build_decode_indexes": (ctypes.c_int, [vp, vp, sz, ctypes.c_float, vp]),
+        "nvcr_sm100_dcvc_build_encode_indexes": (ctypes.c_int, [vp, vp, vp, sz, ctypes.c_float, vp]),
+        "nvcr_sm100_dcvc_make_mask": (ctypes.c_int, [vp] + [ctypes.c_int32] * 4 + [ctypes.c_int, ctypes.c_int, vp]),
+        "nvcr_sm100_dcvc_restore": (ctypes.c_int, [vp] * 4 + [ctypes.c_int32] * 4 + [ctypes.c_int, vp]),
     }
     for name, (restype, argtypes) in signatures.items():
         function = getattr(lib, name)

@@ -3,7 +3,7 @@
 // the reference sources it names (src/deterministic/program.cpp,
 // normative_stage.cpp, src/common/{json,sha256,error}.cpp,
 // src/bitstream/numerics_identity.cpp, src/deterministic/fx.cpp,
-// src/deterministic/fx_program.cpp) into
+// src/deterministic/fx_program.cpp, src/dcvcrt/host_ops.cpp) into
 // oracle/_ref/libnvcr_ref.so. Nothing in the product links or loads it.
 //
 // Programs reach the reference through its own loader (load_program,
@@ -11,6 +11,8 @@
 // tests write, so the reference also checks the files' format and digests.
 #include "deterministic/det_math.hpp"
 #include "deterministic/fx_program.hpp"
+#include "dcvcrt/host_ops.hpp"
+#include "dcvcrt/scale_index.hpp"
 #include "deterministic/normative_stage.hpp"
 #include "deterministic/program.hpp"
 #include "nvcr/bitstream/numerics_identity.hpp"
@@ -263,6 +265,49 @@ int ref_fx_run(const char* directory, const char* stage, int input_count, const 
         std::memcpy(outputs[index], y.values.data(), y.values.size() * 4);
     }
     return 0;
+}
+
+// DCVC-RT inter-stage glue on the host (src/dcvcrt/host_ops.cpp), exact
+// numerics. Each returns the reference's bool as 1 or 0.
+namespace glue = nvcr::dcvcrt::host_ops;
+
+void ref_glue_to_half(const float* in, std::uint16_t* out, std::size_t count) {
+    for (std::size_t i = 0; i < count; ++i) out[i] = glue::to_half(in[i]);
+}
+void ref_glue_to_float(const std::uint16_t* in, float* out, std::size_t count) {
+    for (std::size_t i = 0; i < count; ++i) out[i] = glue::to_float(in[i]);
+}
+// exact_scale_index (src/dcvcrt/scale_index.hpp:153-169) on float scales.
+void ref_glue_exact_scale_indexes(const float* in, std::uint8_t* out, std::size_t count) {
+    for (std::size_t i = 0; i < count; ++i) out[i] = nvcr::dcvcrt::exact_scale_index(in[i]);
+}
+
+int ref_glue_decode_indexes(const std::uint16_t* scales, std::uint8_t* out, std::size_t count, float force_zero) {
+    return glue::build_decode_indexes(std::span(scales, count), std::span(out, count), force_zero, true) ? 1 : 0;
+}
+
+int ref_glue_encode_indexes(const std::uint16_t* symbols, const std::uint16_t* scales, std::int16_t* out,
+                            std::size_t count, float force_zero) {
+    return glue::build_encode_indexes(std::span(symbols, count), std::span(scales, count), std::span(out, count),
+                                      force_zero, true) ? 1 : 0;
+}
+
+int ref_glue_mask(std::uint16_t* mask, std::size_t capacity, int batch, int channels, int height, int width, int ways,
+                  int stage) {
+    const glue::Shape4D shape{batch, channels, height, width};
+    return (ways == 4 ? glue::make_four_way_mask(std::span(mask, capacity), shape, stage)
+                      : glue::make_two_way_mask(std::span(mask, capacity), shape, stage)) ? 1 : 0;
+}
+
+int ref_glue_restore(const std::uint16_t* symbols, const std::uint16_t* means, const std::uint16_t* mask,
+                     std::uint16_t* out, std::size_t capacity, int batch, int channels, int height, int width,
+                     int ways) {
+    const glue::Shape4D shape{batch, channels, height, width};
+    const std::size_t part = capacity / static_cast<std::size_t>(ways);
+    return (ways == 4 ? glue::restore_four_way(std::span(symbols, part), std::span(means, capacity),
+                                               std::span(mask, capacity), std::span(out, capacity), shape)
+                      : glue::restore_two_way(std::span(symbols, part), std::span(means, capacity),
+                                              std::span(mask, capacity), std::span(out, capacity), shape)) ? 1 : 0;
 }
 
 void ref_free(void* pointer) { std::free(pointer); }

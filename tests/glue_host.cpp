@@ -1,0 +1,68 @@
+// Host build of the DCVC-RT glue element functions (nvcr_b200/csrc/
+// glue_elements.cuh), for CPU tests only. TEST INFRASTRUCTURE: built by
+// tests/glue_host.py into tests/_build/libglue_host.so; the product never links
+// or loads it. Each entry point visits every index the matching kernel in
+// k_glue.cu visits, with the kernels' own argument checks.
+#include "glue_elements.cuh"
+
+namespace glue = nvcr_sm100::glue;
+
+namespace {
+
+const float thresholds[127] = {
+#include "scale_thresholds.inc"
+};
+
+std::size_t volume(int batch, int channels, int height, int width) {
+    return static_cast<std::size_t>(batch) * channels * height * width;
+}
+
+}  // namespace
+
+extern "C" {
+
+void gh_to_half(const float* in, std::uint16_t* out, std::size_t count) {
+    for (std::size_t i = 0; i < count; ++i) out[i] = glue::to_half(in[i]);
+}
+void gh_to_float(const std::uint16_t* in, float* out, std::size_t count) {
+    for (std::size_t i = 0; i < count; ++i) out[i] = glue::to_float(in[i]);
+}
+void gh_exact_scale_indexes(const float* in, std::uint8_t* out, std::size_t count) {
+    for (std::size_t i = 0; i < count; ++i) out[i] = glue::exact_scale_index(in[i], thresholds);
+}
+
+int gh_decode_indexes(const std::uint16_t* scales, std::uint8_t* out, std::size_t count, float force_zero) {
+    if (count == 0) return 0;
+    for (std::size_t i = 0; i < count; ++i) glue::decode_index(scales, out, force_zero, thresholds, i);
+    return 1;
+}
+
+int gh_encode_indexes(const std::uint16_t* symbols, const std::uint16_t* scales, std::int16_t* out, std::size_t count,
+                      float force_zero) {
+    if (count == 0) return 0;
+    for (std::size_t i = 0; i < count; ++i) glue::encode_index(symbols, scales, out, force_zero, thresholds, i);
+    return 1;
+}
+
+int gh_mask(std::uint16_t* mask, int batch, int channels, int height, int width, int ways, int stage) {
+    if (!glue::valid_shape(batch, channels, height, width, ways) || stage < 0 || stage >= ways) return 0;
+    const std::size_t count = volume(batch, channels, height, width);
+    for (std::size_t i = 0; i < count; ++i) {
+        if (ways == 4) {
+            glue::four_way_mask(mask, channels, height, width, stage, i);
+        } else {
+            glue::two_way_mask(mask, channels, height, width, stage, i);
+        }
+    }
+    return 1;
+}
+
+int gh_restore(const std::uint16_t* symbols, const std::uint16_t* means, const std::uint16_t* mask,
+               std::uint16_t* out, int batch, int channels, int height, int width, int ways) {
+    if (!glue::valid_shape(batch, channels, height, width, ways)) return 0;
+    const std::size_t part = volume(batch, channels, height, width) / static_cast<std::size_t>(ways);
+    for (std::size_t i = 0; i < part; ++i) glue::restore(symbols, means, mask, out, part, ways, i);
+    return 1;
+}
+
+}  // extern "C"

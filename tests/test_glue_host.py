@@ -1,0 +1,169 @@
+"""DCVC-RT inter-stage glue (no GPU): the element functions the kernels in
+nvcr_b200/csrc/k_glue.cu run, compiled for the host (tests/glue_host.cpp),
+bit for bit against the reference's own host ops (src/dcvcrt/host_ops.cpp and
+scale_index.hpp, compiled from its sources into oracle/_ref): the FP16
+conversions on every half and on every rounding boundary, the exact
+scale-to-table index on every threshold and its neighbours, the decode and
+encode index builds on every half scale, the four- and two-way masks on every
+stage, and the restore on seeded halves with specials; the generated threshold
+table against the reference's."""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def ptr(array: np.ndarray):
+    return array.ctypes.data_as(ctypes.c_void_p)
+
+
+@pytest.fixture(scope="module")
+def sides(reference):
+    from tests.glue_host import load
+
+    mine = load()
+    theirs = reference.lib
+    for lib, prefix in ((mine, "gh"), (theirs, "ref_glue")):
+        for name in ("to_half", "to_float", "exact_scale_indexes"):
+            getattr(lib, f"{prefix}_{name}").restype = None
+            getattr(lib, f"{prefix}_{name}").argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t]
+        getattr(lib, f"{prefix}_decode_indexes").argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                                             ctypes.c_float]
+        getattr(lib, f"{prefix}_encode_indexes").argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                                             ctypes.c_size_t, ctypes.c_float]
+    mine.gh_mask.argtypes = [ctypes.c_void_p] + [ctypes.c_int] * 6
+    theirs.ref_glue_mask.argtypes = [ctypes.c_void_p, ctypes.c_size_t] + [ctypes.c_int] * 6
+    mine.gh_restore.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 5
+    theirs.ref_glue_restore.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_size_t] + [ctypes.c_int] * 5
+    return mine, theirs
+
+
+def test_generated_thresholds_equal_the_reference_table():
+    """nvcr_b200/csrc/make_scale_thresholds.py derives the table from its
+    definition; the reference ships it as constants (read here as text)."""
+    ref = re.findall(r"(0x[0-9a-f.]+p[+-]?\d+)F", (Path("/root/reference/src/dcvcrt/scale_index.hpp")).read_text()) \
+        if Path("/root/reference/src/dcvcrt/scale_index.hpp").exists() else None
+    if ref is None:
+        pytest.skip("reference sources not present")
+    mine = [line.strip().rstrip("f,") for line in (ROOT / "nvcr_b200" / "csrc" / "scale_thresholds.inc").read_text()
+            .splitlines() if line.startswith("0x")]
+    assert len(mine) == 127 and [float.fromhex(v) for v in mine] == [float.fromhex(v) for v in ref]
+
+
+def test_half_to_float_every_pattern(sides):
+    mine, theirs = sides
+    halves = np.arange(65536, dtype=np.uint16)
+    a = np.zeros(65536, np.float32)
+    b = np.zeros(65536, np.float32)
+    mine.gh_to_float(ptr(halves), ptr(a), 65536)
+    theirs.ref_glue_to_float(ptr(halves), ptr(b), 65536)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def test_float_to_half_on_every_boundary(sides):
+    mine, theirs = sides
+    halves = np.arange(0, 0x7c01, dtype=np.uint32)  # every finite magnitude and infinity
+    as_float = np.zeros(halves.size, np.float32)
+    mine.gh_to_float(ptr(halves.astype(np.uint16)), ptr(as_float), halves.size)
+    bits = as_float.view(np.uint32)
+    # each half, the midpoints to its neighbours and one float ulp either side of them
+    midpoints = ((as_float[:-1].astype(np.float64) + as_float[1:].astype(np.float64)) / 2).astype(np.float32)
+    mid_bits = midpoints.view(np.uint32)
+    candidates = np.concatenate([bits, bits + 1, bits - 1, mid_bits, mid_bits + 1, mid_bits - 1,
+                                 np.array([0x7f800000, 0x7fc00000, 0x7f800001, 0x477fefff, 0x477ff000, 0x477ff001,
+                                           0x33000000, 0x33000001, 0x32ffffff, 0x38800000, 0x387fffff],
+                                          np.uint32)])
+    rng = np.random.default_rng(3)
+    candidates = np.concatenate([candidates, rng.integers(0, 2 ** 31, 200000, dtype=np.uint32)])
+    candidates = np.concatenate([candidates, candidates | np.uint32(0x80000000)]).astype(np.uint32)
+    values = candidates.view(np.float32)
+    a = np.zeros(values.size, np.uint16)
+    b = np.zeros(values.size, np.uint16)
+    mine.gh_to_half(ptr(values), ptr(a), values.size)
+    theirs.ref_glue_to_half(ptr(values), ptr(b), values.size)
+    assert np.array_equal(a, b)
+
+
+def test_exact_scale_index_on_every_threshold(sides):
+    mine, theirs = sides
+    thresholds = np.array([float.fromhex(line.strip().rstrip("f,")) for line in
+                           (ROOT / "nvcr_b200" / "csrc" / "scale_thresholds.inc").read_text().splitlines()
+                           if line.startswith("0x")], np.float32)
+    bits = thresholds.view(np.uint32)
+    specials = np.array([0.0, -0.0, -1.0, 0.11, 0.10999999, 16.0, 16.000002, 1e30, np.inf, -np.inf, np.nan],
+                        np.float32)
+    rng = np.random.default_rng(4)
+    scales = np.concatenate([thresholds, (bits + 1).view(np.float32), (bits - 1).view(np.float32), specials,
+                             rng.uniform(0.05, 20.0, 100000).astype(np.float32)]).astype(np.float32)
+    a = np.zeros(scales.size, np.uint8)
+    b = np.zeros(scales.size, np.uint8)
+    mine.gh_exact_scale_indexes(ptr(scales), ptr(a), scales.size)
+    theirs.ref_glue_exact_scale_indexes(ptr(scales), ptr(b), scales.size)
+    assert np.array_equal(a, b)
+    assert set(a.tolist()) == set(range(128))
+
+
+@pytest.mark.parametrize("force_zero", [0.0, 0.11, 0.5, -1.0])
+def test_index_builds_on_every_half_scale(sides, force_zero):
+    mine, theirs = sides
+    scales = np.arange(65536, dtype=np.uint16)
+    a = np.zeros(65536, np.uint8)
+    b = np.zeros(65536, np.uint8)
+    assert mine.gh_decode_indexes(ptr(scales), ptr(a), 65536, force_zero) == 1
+    assert theirs.ref_glue_decode_indexes(ptr(scales), ptr(b), 65536, force_zero) == 1
+    assert np.array_equal(a, b)
+    rng = np.random.default_rng(5)
+    symbol_halves = np.zeros(65536, np.uint16)
+    values = rng.integers(-128, 128, 65536).astype(np.float32)
+    mine.gh_to_half(ptr(values), ptr(symbol_halves), 65536)  # symbols: integers in [-128, 127] as FP16
+    ea = np.zeros(65536, np.int16)
+    eb = np.zeros(65536, np.int16)
+    assert mine.gh_encode_indexes(ptr(symbol_halves), ptr(scales), ptr(ea), 65536, force_zero) == 1
+    assert theirs.ref_glue_encode_indexes(ptr(symbol_halves), ptr(scales), ptr(eb), 65536, force_zero) == 1
+    assert np.array_equal(ea, eb)
+
+
+def test_masks_on_every_stage(sides):
+    mine, theirs = sides
+    for ways in (4, 2):
+        for batch, channels, height, width in ((1, 4, 1, 1), (1, 8, 3, 5), (2, 12, 4, 4), (1, 4, 7, 2), (2, 2, 2, 3)):
+            for stage in range(-1, ways + 1):
+                count = batch * channels * height * width
+                a = np.full(count, 0x1234, np.uint16)
+                b = np.full(count, 0x1234, np.uint16)
+                ok_a = mine.gh_mask(ptr(a), batch, channels, height, width, ways, stage)
+                ok_b = theirs.ref_glue_mask(ptr(b), count, batch, channels, height, width, ways, stage)
+                assert ok_a == ok_b, (ways, batch, channels, height, width, stage)
+                if ok_a:
+                    assert np.array_equal(a, b)
+    for shape in ((0, 4, 2, 2), (1, 6, 2, 2), (1, 4, 0, 2), (1, 4, 2, -1)):
+        a = np.zeros(64, np.uint16)
+        assert mine.gh_mask(ptr(a), *shape, 4, 0) == theirs.ref_glue_mask(ptr(a), 64, *shape, 4, 0) == 0
+
+
+def test_restore_on_seeded_halves(sides):
+    mine, theirs = sides
+    rng = np.random.default_rng(6)
+    specials = np.array([0x7c00, 0xfc00, 0x7e00, 0x7c01, 0x0000, 0x8000, 0x0001, 0x7bff, 0xfbff, 0x3c00], np.uint16)
+    for ways in (4, 2):
+        for batch, channels, height, width in ((1, 4, 2, 3), (2, 8, 5, 5), (1, 12, 1, 7)):
+            count = batch * channels * height * width
+            part = count // ways
+            symbols = rng.integers(0, 65536, part, dtype=np.uint16)
+            means = rng.integers(0, 65536, count, dtype=np.uint16)
+            mask = rng.choice(np.array([0x0000, 0x3c00], np.uint16), count)
+            symbols[: min(part, specials.size)] = specials[: min(part, specials.size)]
+            means[: specials.size] = specials[::-1]
+            a = np.zeros(count, np.uint16)
+            b = np.zeros(count, np.uint16)
+            assert mine.gh_restore(ptr(symbols), ptr(means), ptr(mask), ptr(a), batch, channels, height, width,
+                                   ways) == 1
+            assert theirs.ref_glue_restore(ptr(symbols), ptr(means), ptr(mask), ptr(b), count, batch, channels,
+                                           height, width, ways) == 1
+            assert np.array_equal(a, b)
