@@ -308,6 +308,22 @@ int nvcr_sm100_dcvc_make_mask(uint16_t* mask, int32_t batch, int32_t channels, i
 int nvcr_sm100_dcvc_restore(const uint16_t* symbols, const uint16_t* means, const uint16_t* mask, uint16_t* output,
                             int32_t batch, int32_t channels, int32_t height, int32_t width, int ways, void* stream);
 
+/* Reference process_with_mask (host_ops.cpp:351-377): per element, the masked
+ * scale, mean and residual (values - mean) * mask, the symbol round(residual)
+ * (half away from zero; 0 where a positive force-zero threshold is not
+ * exceeded) clamped to [-128, 127], and symbol + mean. `residual` may be NULL;
+ * every tensor holds `count` values. */
+int nvcr_sm100_dcvc_process_with_mask(const uint16_t* values, const uint16_t* scales, const uint16_t* means,
+                                      const uint16_t* mask, uint16_t* residual, uint16_t* symbols,
+                                      uint16_t* reconstructed, uint16_t* masked_scales, size_t count,
+                                      float force_zero_threshold, void* stream);
+/* Reference reduce_channel_quarters / _halves (mask NULL) and
+ * reduce_masked_quarters / _halves (host_ops.cpp:379-454): the ways (4 or 2)
+ * channel slices of the input shape summed into one, each multiplied by the
+ * mask first when it is given. */
+int nvcr_sm100_dcvc_reduce(const uint16_t* input, const uint16_t* mask, uint16_t* output, int32_t batch,
+                           int32_t channels, int32_t height, int32_t width, int ways, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

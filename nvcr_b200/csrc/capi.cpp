@@ -596,4 +596,21 @@ int nvcr_sm100_dcvc_restore(const uint16_t* symbols, const uint16_t* means, cons
                        "restore shape or ways invalid");
 }
 
+int nvcr_sm100_dcvc_process_with_mask(const uint16_t* values, const uint16_t* scales, const uint16_t* means,
+                                      const uint16_t* mask, uint16_t* residual, uint16_t* symbols,
+                                      uint16_t* reconstructed, uint16_t* masked_scales, size_t count,
+                                      float force_zero_threshold, void* stream) {
+    return glue_status(nvcr_sm100::glue::process_with_mask(values, scales, means, mask, residual, symbols, reconstructed,
+                                                            masked_scales, count, force_zero_threshold,
+                                                            static_cast<cudaStream_t>(stream)),
+                       "empty or null tensor");
+}
+
+int nvcr_sm100_dcvc_reduce(const uint16_t* input, const uint16_t* mask, uint16_t* output, int32_t batch,
+                           int32_t channels, int32_t height, int32_t width, int ways, void* stream) {
+    return glue_status(nvcr_sm100::glue::reduce(input, mask, output, batch, channels, height, width, ways,
+                                                static_cast<cudaStream_t>(stream)),
+                       "reduce shape or ways invalid");
+}
+
 }  // extern "C"

@@ -61,6 +61,40 @@ GLUE_HD float mul(float a, float b) {
 #endif
 }
 
+GLUE_HD float sub(float a, float b) {
+#if defined(__CUDA_ARCH__)
+    return __fsub_rn(a, b);
+#else
+    return a - b;
+#endif
+}
+
+// Round half away from zero, and the IEEE minimum / maximum that ignore a NaN
+// operand: exact operations, as the reference's std::round, std::fmin, std::fmax.
+GLUE_HD float round_away(float v) {
+#if defined(__CUDA_ARCH__)
+    return roundf(v);
+#else
+    return __builtin_roundf(v);
+#endif
+}
+
+GLUE_HD float fmin_ieee(float a, float b) {
+#if defined(__CUDA_ARCH__)
+    return fminf(a, b);
+#else
+    return __builtin_fminf(a, b);
+#endif
+}
+
+GLUE_HD float fmax_ieee(float a, float b) {
+#if defined(__CUDA_ARCH__)
+    return fmaxf(a, b);
+#else
+    return __builtin_fmaxf(a, b);
+#endif
+}
+
 // binary16 -> binary32, exact.
 GLUE_HD float to_float(Half h) {
     const std::uint32_t sign = static_cast<std::uint32_t>(h & 0x8000u) << 16;
@@ -186,6 +220,50 @@ GLUE_HD void restore(const Half* symbols, const Half* means, const Half* mask, H
         const std::size_t d = i + static_cast<std::size_t>(part) * part_size;
         out[d] = to_half(mul(add(symbol, to_float(means[d])), to_float(mask[d])));
     }
+}
+
+// process_with_mask, element i: the masked scale, mean and residual, the
+// symbol round(residual) (0 where a positive force-zero threshold is not
+// exceeded) clamped to [-128, 127], and the reconstruction symbol + mean;
+// `residual` may be null.
+GLUE_HD void process_with_mask(const Half* values, const Half* scales, const Half* means, const Half* mask,
+                               Half* residual, Half* symbols, Half* reconstructed, Half* masked_scales,
+                               float force_zero, std::size_t i) {
+    const float mask_value = to_float(mask[i]);
+    const float scale = mul(to_float(scales[i]), mask_value);
+    const float mean = mul(to_float(means[i]), mask_value);
+    const float value_residual = mul(sub(to_float(values[i]), mean), mask_value);
+    float symbol = round_away(value_residual);
+    if (force_zero > 0.0f && scale <= force_zero) symbol = 0.0f;
+    symbol = fmin_ieee(127.0f, fmax_ieee(-128.0f, symbol));
+    if (residual != nullptr) residual[i] = to_half(value_residual);
+    symbols[i] = to_half(symbol);
+    reconstructed[i] = to_half(add(symbol, mean));
+    masked_scales[i] = to_half(scale);
+}
+
+// Sum of the `parts` (4 or 2) channel slices at element i, each optionally
+// multiplied by the mask first, added in slice order from 0 (quarters) or as
+// first + second (halves), as the reference's reduce_* host ops do.
+GLUE_HD void reduce_parts(const Half* input, const Half* mask, Half* output, std::size_t part_size, int parts,
+                          std::size_t i) {
+    if (parts == 2) {
+        float first = to_float(input[i]);
+        float second = to_float(input[i + part_size]);
+        if (mask != nullptr) {
+            first = mul(first, to_float(mask[i]));
+            second = mul(second, to_float(mask[i + part_size]));
+        }
+        output[i] = to_half(add(first, second));
+        return;
+    }
+    float value = 0.0f;
+    for (int part = 0; part < parts; ++part) {
+        const std::size_t source = i + static_cast<std::size_t>(part) * part_size;
+        const float term = mask != nullptr ? mul(to_float(input[source]), to_float(mask[source])) : to_float(input[source]);
+        value = add(value, term);
+    }
+    output[i] = to_half(value);
 }
 
 }  // namespace nvcr_sm100::glue

@@ -55,6 +55,20 @@ __global__ void restore_kernel(const Half* __restrict__ symbols, const Half* __r
     GLUE_GRID_STRIDE(i, part_size) restore(symbols, means, mask, out, part_size, parts, i);
 }
 
+__global__ void process_kernel(const Half* __restrict__ values, const Half* __restrict__ scales,
+                               const Half* __restrict__ means, const Half* __restrict__ mask, Half* residual,
+                               Half* __restrict__ symbols, Half* __restrict__ reconstructed,
+                               Half* __restrict__ masked_scales, std::size_t count, float force_zero) {
+    GLUE_GRID_STRIDE(i, count) {
+        process_with_mask(values, scales, means, mask, residual, symbols, reconstructed, masked_scales, force_zero, i);
+    }
+}
+
+__global__ void reduce_kernel(const Half* __restrict__ input, const Half* mask, Half* __restrict__ output,
+                              std::size_t part_size, int parts) {
+    GLUE_GRID_STRIDE(i, part_size) reduce_parts(input, mask, output, part_size, parts, i);
+}
+
 #undef GLUE_GRID_STRIDE
 
 std::size_t volume(int batch, int channels, int height, int width) {
@@ -96,6 +110,28 @@ cudaError_t restore(const Half* symbols, const Half* means, const Half* mask, Ha
     }
     const std::size_t part_size = volume(batch, channels, height, width) / static_cast<std::size_t>(ways);
     restore_kernel<<<grid_for(part_size), threads, 0, stream>>>(symbols, means, mask, out, part_size, ways);
+    return cudaGetLastError();
+}
+
+cudaError_t process_with_mask(const Half* values, const Half* scales, const Half* means, const Half* mask,
+                              Half* residual, Half* symbols, Half* reconstructed, Half* masked_scales,
+                              std::size_t count, float force_zero, cudaStream_t stream) {
+    if (count == 0 || values == nullptr || scales == nullptr || means == nullptr || mask == nullptr ||
+        symbols == nullptr || reconstructed == nullptr || masked_scales == nullptr) {
+        return cudaErrorInvalidValue;
+    }
+    process_kernel<<<grid_for(count), threads, 0, stream>>>(values, scales, means, mask, residual, symbols,
+                                                            reconstructed, masked_scales, count, force_zero);
+    return cudaGetLastError();
+}
+
+cudaError_t reduce(const Half* input, const Half* mask, Half* output, int batch, int channels, int height, int width,
+                   int ways, cudaStream_t stream) {
+    if (input == nullptr || output == nullptr || !valid_shape(batch, channels, height, width, ways)) {
+        return cudaErrorInvalidValue;
+    }
+    const std::size_t part_size = volume(batch, channels, height, width) / static_cast<std::size_t>(ways);
+    reduce_kernel<<<grid_for(part_size), threads, 0, stream>>>(input, mask, output, part_size, ways);
     return cudaGetLastError();
 }
 

@@ -79,7 +79,7 @@ EXPORTS = [
     "nvcr_sm100_fx_program_node", "nvcr_sm100_fx_program_tensor", "nvcr_sm100_fx_executor_create", "nvcr_sm100_fx_executor_destroy",
     "nvcr_sm100_fx_infer_output_extents", "nvcr_sm100_fx_run", "nvcr_sm100_fx_last_launch_count",
     "nvcr_sm100_dcvc_build_decode_indexes", "nvcr_sm100_dcvc_build_encode_indexes", "nvcr_sm100_dcvc_make_mask",
-    "nvcr_sm100_dcvc_restore",
+    "nvcr_sm100_dcvc_restore", "nvcr_sm100_dcvc_process_with_mask", "nvcr_sm100_dcvc_reduce",
 ]
 
 _lib: ctypes.CDLL | None = None
@@ -154,6 +154,8 @@ def library() -> ctypes.CDLL:
         "nvcr_sm100_dcvc_build_encode_indexes": (ctypes.c_int, [vp, vp, vp, sz, ctypes.c_float, vp]),
         "nvcr_sm100_dcvc_make_mask": (ctypes.c_int, [vp] + [ctypes.c_int32] * 4 + [ctypes.c_int, ctypes.c_int, vp]),
         "nvcr_sm100_dcvc_restore": (ctypes.c_int, [vp] * 4 + [ctypes.c_int32] * 4 + [ctypes.c_int, vp]),
+        "nvcr_sm100_dcvc_process_with_mask": (ctypes.c_int, [vp] * 8 + [sz, ctypes.c_float, vp]),
+        "nvcr_sm100_dcvc_reduce": (ctypes.c_int, [vp] * 3 + [ctypes.c_int32] * 4 + [ctypes.c_int, vp]),
     }
     for name, (restype, argtypes) in signatures.items():
         function = getattr(lib, name)

@@ -310,6 +310,31 @@ int ref_glue_restore(const std::uint16_t* symbols, const std::uint16_t* means, c
                                               std::span(mask, capacity), std::span(out, capacity), shape)) ? 1 : 0;
 }
 
+int ref_glue_process(const std::uint16_t* values, const std::uint16_t* scales, const std::uint16_t* means,
+                     const std::uint16_t* mask, std::uint16_t* residual, std::uint16_t* symbols,
+                     std::uint16_t* reconstructed, std::uint16_t* masked_scales, std::size_t count, float force_zero) {
+    return glue::process_with_mask(std::span(values, count), std::span(scales, count), std::span(means, count),
+                                   std::span(mask, count),
+                                   residual != nullptr ? std::span(residual, count) : std::span<std::uint16_t>(),
+                                   std::span(symbols, count), std::span(reconstructed, count),
+                                   std::span(masked_scales, count), force_zero) ? 1 : 0;
+}
+
+// reduce_channel_quarters / _halves (mask null) and reduce_masked_quarters / _halves.
+int ref_glue_reduce(const std::uint16_t* input, const std::uint16_t* mask, std::uint16_t* output, std::size_t capacity,
+                    int batch, int channels, int height, int width, int ways) {
+    const glue::Shape4D shape{batch, channels, height, width};
+    const auto in = std::span(input, capacity);
+    const auto out = std::span(output, capacity / static_cast<std::size_t>(ways));
+    if (mask == nullptr) {
+        return (ways == 4 ? glue::reduce_channel_quarters(in, out, shape) : glue::reduce_channel_halves(in, out, shape))
+            ? 1 : 0;
+    }
+    const auto m = std::span(mask, capacity);
+    return (ways == 4 ? glue::reduce_masked_quarters(in, m, out, shape) : glue::reduce_masked_halves(in, m, out, shape))
+        ? 1 : 0;
+}
+
 void ref_free(void* pointer) { std::free(pointer); }
 
 }  // extern "C"

@@ -65,4 +65,23 @@ int gh_restore(const std::uint16_t* symbols, const std::uint16_t* means, const s
     return 1;
 }
 
+int gh_process(const std::uint16_t* values, const std::uint16_t* scales, const std::uint16_t* means,
+               const std::uint16_t* mask, std::uint16_t* residual, std::uint16_t* symbols, std::uint16_t* reconstructed,
+               std::uint16_t* masked_scales, std::size_t count, float force_zero) {
+    if (count == 0) return 0;
+    for (std::size_t i = 0; i < count; ++i) {
+        glue::process_with_mask(values, scales, means, mask, residual, symbols, reconstructed, masked_scales,
+                                force_zero, i);
+    }
+    return 1;
+}
+
+int gh_reduce(const std::uint16_t* input, const std::uint16_t* mask, std::uint16_t* output, int batch, int channels,
+              int height, int width, int ways) {
+    if (!glue::valid_shape(batch, channels, height, width, ways)) return 0;
+    const std::size_t part = volume(batch, channels, height, width) / static_cast<std::size_t>(ways);
+    for (std::size_t i = 0; i < part; ++i) glue::reduce_parts(input, mask, output, part, ways, i);
+    return 1;
+}
+
 }  // extern "C"

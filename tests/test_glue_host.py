@@ -40,6 +40,10 @@ def sides(reference):
     mine.gh_mask.argtypes = [ctypes.c_void_p] + [ctypes.c_int] * 6
     theirs.ref_glue_mask.argtypes = [ctypes.c_void_p, ctypes.c_size_t] + [ctypes.c_int] * 6
     mine.gh_restore.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 5
+    mine.gh_process.argtypes = [ctypes.c_void_p] * 8 + [ctypes.c_size_t, ctypes.c_float]
+    theirs.ref_glue_process.argtypes = [ctypes.c_void_p] * 8 + [ctypes.c_size_t, ctypes.c_float]
+    mine.gh_reduce.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 5
+    theirs.ref_glue_reduce.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_size_t] + [ctypes.c_int] * 5
     theirs.ref_glue_restore.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_size_t] + [ctypes.c_int] * 5
     return mine, theirs
 
@@ -167,3 +171,53 @@ def test_restore_on_seeded_halves(sides):
             assert theirs.ref_glue_restore(ptr(symbols), ptr(means), ptr(mask), ptr(b), count, batch, channels,
                                            height, width, ways) == 1
             assert np.array_equal(a, b)
+
+
+def random_halves(rng, count: int) -> np.ndarray:
+    """Seeded FP16 patterns: mostly moderate values, with specials mixed in."""
+    values = rng.normal(0.0, 40.0, count).astype(np.float16).view(np.uint16)
+    specials = np.array([0x7c00, 0xfc00, 0x7e00, 0x7c01, 0x0000, 0x8000, 0x0001, 0x7bff, 0xfbff, 0x3800, 0xb800,
+                         0x3e00, 0xbe00], np.uint16)
+    values[rng.integers(0, count, count // 20)] = rng.choice(specials, count // 20)
+    return values
+
+
+@pytest.mark.parametrize("force_zero", [0.0, 0.11, 2.0])
+def test_process_with_mask(sides, force_zero):
+    """Ties of the rounding (x.5 residuals), the clamp at -128 / 127, NaN and
+    infinities, with and without the residual output."""
+    mine, theirs = sides
+    rng = np.random.default_rng(7)
+    count = 40000
+    values = random_halves(rng, count)
+    values[:200] = (np.arange(200, dtype=np.float32) / 2 - 50).astype(np.float16).view(np.uint16)
+    scales = np.abs(rng.normal(0.0, 3.0, count)).astype(np.float16).view(np.uint16)
+    means = random_halves(rng, count)
+    mask = rng.choice(np.array([0x0000, 0x3c00], np.uint16), count)
+    for with_residual in (True, False):
+        outs = [[np.zeros(count, np.uint16) for _ in range(4)] for _ in range(2)]
+        for lib, name, out in ((mine, "gh_process", outs[0]), (theirs, "ref_glue_process", outs[1])):
+            residual = ptr(out[0]) if with_residual else None
+            assert getattr(lib, name)(ptr(values), ptr(scales), ptr(means), ptr(mask), residual, ptr(out[1]),
+                                      ptr(out[2]), ptr(out[3]), count, force_zero) == 1
+        for a, b in zip(*outs):
+            assert np.array_equal(a, b)
+
+
+def test_reductions(sides):
+    mine, theirs = sides
+    rng = np.random.default_rng(8)
+    for ways in (4, 2):
+        for batch, channels, height, width in ((1, 4, 3, 5), (2, 8, 4, 4), (1, 12, 1, 9)):
+            count = batch * channels * height * width
+            source = random_halves(rng, count)
+            mask = rng.choice(np.array([0x0000, 0x3c00], np.uint16), count)
+            for masked in (False, True):
+                a = np.zeros(count // ways, np.uint16)
+                b = np.zeros(count // ways, np.uint16)
+                m = ptr(mask) if masked else None
+                assert mine.gh_reduce(ptr(source), m, ptr(a), batch, channels, height, width, ways) == 1
+                assert theirs.ref_glue_reduce(ptr(source), m, ptr(b), count, batch, channels, height, width, ways) == 1
+                assert np.array_equal(a, b)
+    bad = np.zeros(16, np.uint16)
+    assert mine.gh_reduce(ptr(bad), None, ptr(bad), 1, 6, 1, 1, 4) == theirs.ref_glue_reduce(ptr(bad), None, ptr(bad), 16, 1, 6, 1, 1, 4) == 0

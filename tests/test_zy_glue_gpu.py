@@ -30,6 +30,8 @@ def host():
                                       ctypes.c_float]
     lib.gh_mask.argtypes = [ctypes.c_void_p] + [ctypes.c_int] * 6
     lib.gh_restore.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 5
+    lib.gh_process.argtypes = [ctypes.c_void_p] * 8 + [ctypes.c_size_t, ctypes.c_float]
+    lib.gh_reduce.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 5
     return lib
 
 
@@ -88,3 +90,37 @@ def test_masks_and_restore(cuda, host):
                                                      batch, channels, height, width, ways, None))
             torch.cuda.synchronize()
             assert np.array_equal(out.cpu().numpy().view(np.uint16), expected)
+
+
+def test_process_and_reduce(cuda, host):
+    import torch
+
+    from nvcr_b200.executor import _check, library
+
+    rng = np.random.default_rng(9)
+    batch, channels, height, width = 1, 128, 68, 120
+    count = batch * channels * height * width
+    values = rng.normal(0.0, 40.0, count).astype(np.float16).view(np.uint16)
+    scales = np.abs(rng.normal(0.0, 3.0, count)).astype(np.float16).view(np.uint16)
+    means = rng.normal(0.0, 10.0, count).astype(np.float16).view(np.uint16)
+    mask = rng.choice(np.array([0x0000, 0x3c00], np.uint16), count)
+    expected = [np.zeros(count, np.uint16) for _ in range(4)]
+    host.gh_process(values.ctypes.data, scales.ctypes.data, means.ctypes.data, mask.ctypes.data,
+                    *[e.ctypes.data for e in expected], count, 0.11)
+    device = [torch.from_numpy(a.view(np.int16)).cuda() for a in (values, scales, means, mask)]
+    outs = [torch.zeros(count, dtype=torch.int16, device="cuda") for _ in range(4)]
+    _check(library().nvcr_sm100_dcvc_process_with_mask(*[ptr(t) for t in device], *[ptr(t) for t in outs], count,
+                                                       0.11, None))
+    torch.cuda.synchronize()
+    for out, want in zip(outs, expected):
+        assert np.array_equal(out.cpu().numpy().view(np.uint16), want)
+    for ways in (4, 2):
+        for masked in (False, True):
+            want = np.zeros(count // ways, np.uint16)
+            host.gh_reduce(values.ctypes.data, mask.ctypes.data if masked else None, want.ctypes.data, batch, channels,
+                           height, width, ways)
+            out = torch.zeros(count // ways, dtype=torch.int16, device="cuda")
+            _check(library().nvcr_sm100_dcvc_reduce(ptr(device[0]), ptr(device[3]) if masked else None, ptr(out),
+                                                    batch, channels, height, width, ways, None))
+            torch.cuda.synchronize()
+            assert np.array_equal(out.cpu().numpy().view(np.uint16), want)
