@@ -324,6 +324,33 @@ int nvcr_sm100_dcvc_process_with_mask(const uint16_t* values, const uint16_t* sc
 int nvcr_sm100_dcvc_reduce(const uint16_t* input, const uint16_t* mask, uint16_t* output, int32_t batch,
                            int32_t channels, int32_t height, int32_t width, int ways, void* stream);
 
+/* The elementwise steps between stages (reference host_ops.cpp:101-118,
+ * 474-521), in place where the reference works in place; each value rounds to
+ * FP16 after every step, and min / max follow IEEE 754-2008 minNum / maxNum.
+ * round_to_int8: values = clamp(round(values), -128, 127), also as int8.
+ * int8_to_half: output = values. clamp_min: values = max(values, minimum).
+ * clamp_reciprocal_with_quant: quant_step = max(quant_step, 0.5), values *=
+ * the FP16 reciprocal of it. add_in_place: first += second.
+ * multiply_broadcast (reference multiply_broadcast_in_place): values[c][p] *=
+ * factors[p] for each of `channels` planes of spatial_count values.
+ * add_and_multiply: first = FP16(first + second) * quant_step. */
+int nvcr_sm100_dcvc_round_to_int8(uint16_t* values, int8_t* quantized, size_t count, void* stream);
+int nvcr_sm100_dcvc_int8_to_half(const int8_t* values, uint16_t* output, size_t count, void* stream);
+int nvcr_sm100_dcvc_clamp_min(uint16_t* values, size_t count, float minimum, void* stream);
+int nvcr_sm100_dcvc_clamp_reciprocal_with_quant(uint16_t* quant_step, uint16_t* values, size_t count, void* stream);
+int nvcr_sm100_dcvc_add_in_place(uint16_t* first, const uint16_t* second, size_t count, void* stream);
+int nvcr_sm100_dcvc_multiply_broadcast(uint16_t* values, const uint16_t* factors, size_t spatial_count,
+                                       int32_t channels, void* stream);
+int nvcr_sm100_dcvc_add_and_multiply(uint16_t* first, const uint16_t* second, const uint16_t* quant_step, size_t count,
+                                     void* stream);
+/* Reference replicate_pad and crop_spatial (host_ops.cpp:120-167): edge
+ * replication up to padded_height x padded_width, or the crop from the origin. */
+int nvcr_sm100_dcvc_replicate_pad(const uint16_t* input, uint16_t* output, int32_t batch, int32_t channels,
+                                  int32_t height, int32_t width, int32_t padded_height, int32_t padded_width,
+                                  void* stream);
+int nvcr_sm100_dcvc_crop_spatial(const uint16_t* input, uint16_t* output, int32_t batch, int32_t channels,
+                                 int32_t height, int32_t width, int32_t out_height, int32_t out_width, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

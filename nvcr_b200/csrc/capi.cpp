@@ -613,4 +613,68 @@ int nvcr_sm100_dcvc_reduce(const uint16_t* input, const uint16_t* mask, uint16_t
                        "reduce shape or ways invalid");
 }
 
+namespace {
+
+int glue_pointwise(nvcr_sm100::glue::PointwiseOp op, uint16_t* a, uint16_t* b, const uint16_t* c, int8_t* q,
+                   size_t count, float scalar, size_t spatial_count, void* stream) {
+    return glue_status(nvcr_sm100::glue::pointwise(op, a, b, c, q, count, scalar, spatial_count,
+                                                   static_cast<cudaStream_t>(stream)),
+                       "empty or null tensor");
+}
+
+}  // namespace
+
+int nvcr_sm100_dcvc_round_to_int8(uint16_t* values, int8_t* quantized, size_t count, void* stream) {
+    return glue_pointwise(nvcr_sm100::glue::PointwiseOp::round_to_int8, values, nullptr, nullptr, quantized, count, 0.0f,
+                          0, stream);
+}
+
+int nvcr_sm100_dcvc_int8_to_half(const int8_t* values, uint16_t* output, size_t count, void* stream) {
+    return glue_pointwise(nvcr_sm100::glue::PointwiseOp::int8_to_half, output, nullptr, nullptr,
+                          const_cast<int8_t*>(values), count, 0.0f, 0, stream);
+}
+
+int nvcr_sm100_dcvc_clamp_min(uint16_t* values, size_t count, float minimum, void* stream) {
+    return glue_pointwise(nvcr_sm100::glue::PointwiseOp::clamp_min, values, nullptr, nullptr, nullptr, count, minimum, 0,
+                          stream);
+}
+
+int nvcr_sm100_dcvc_clamp_reciprocal_with_quant(uint16_t* quant_step, uint16_t* values, size_t count, void* stream) {
+    return glue_pointwise(nvcr_sm100::glue::PointwiseOp::clamp_reciprocal_with_quant, quant_step, values, nullptr,
+                          nullptr, count, 0.0f, 0, stream);
+}
+
+int nvcr_sm100_dcvc_add_in_place(uint16_t* first, const uint16_t* second, size_t count, void* stream) {
+    return glue_pointwise(nvcr_sm100::glue::PointwiseOp::add_in_place, first, const_cast<uint16_t*>(second), nullptr,
+                          nullptr, count, 0.0f, 0, stream);
+}
+
+int nvcr_sm100_dcvc_multiply_broadcast(uint16_t* values, const uint16_t* factors, size_t spatial_count,
+                                       int32_t channels, void* stream) {
+    if (channels <= 0) return report(Code::invalid_argument, "channels must be positive");
+    return glue_pointwise(nvcr_sm100::glue::PointwiseOp::multiply_broadcast, values, const_cast<uint16_t*>(factors),
+                          nullptr, nullptr, spatial_count * static_cast<size_t>(channels), 0.0f, spatial_count, stream);
+}
+
+int nvcr_sm100_dcvc_add_and_multiply(uint16_t* first, const uint16_t* second, const uint16_t* quant_step, size_t count,
+                                     void* stream) {
+    return glue_pointwise(nvcr_sm100::glue::PointwiseOp::add_and_multiply, first, const_cast<uint16_t*>(second),
+                          quant_step, nullptr, count, 0.0f, 0, stream);
+}
+
+int nvcr_sm100_dcvc_replicate_pad(const uint16_t* input, uint16_t* output, int32_t batch, int32_t channels,
+                                  int32_t height, int32_t width, int32_t padded_height, int32_t padded_width,
+                                  void* stream) {
+    return glue_status(nvcr_sm100::glue::replicate_pad(input, output, batch, channels, height, width, padded_height,
+                                                       padded_width, static_cast<cudaStream_t>(stream)),
+                       "pad shape invalid");
+}
+
+int nvcr_sm100_dcvc_crop_spatial(const uint16_t* input, uint16_t* output, int32_t batch, int32_t channels,
+                                 int32_t height, int32_t width, int32_t out_height, int32_t out_width, void* stream) {
+    return glue_status(nvcr_sm100::glue::crop_spatial(input, output, batch, channels, height, width, out_height,
+                                                      out_width, static_cast<cudaStream_t>(stream)),
+                       "crop shape invalid");
+}
+
 }  // extern "C"

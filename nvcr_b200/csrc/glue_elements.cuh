@@ -61,6 +61,14 @@ GLUE_HD float mul(float a, float b) {
 #endif
 }
 
+GLUE_HD float div(float a, float b) {
+#if defined(__CUDA_ARCH__)
+    return __fdiv_rn(a, b);
+#else
+    return a / b;
+#endif
+}
+
 GLUE_HD float sub(float a, float b) {
 #if defined(__CUDA_ARCH__)
     return __fsub_rn(a, b);
@@ -69,8 +77,7 @@ GLUE_HD float sub(float a, float b) {
 #endif
 }
 
-// Round half away from zero, and the IEEE minimum / maximum that ignore a NaN
-// operand: exact operations, as the reference's std::round, std::fmin, std::fmax.
+// Round half away from zero (exact, as the reference's std::round).
 GLUE_HD float round_away(float v) {
 #if defined(__CUDA_ARCH__)
     return roundf(v);
@@ -79,20 +86,36 @@ GLUE_HD float round_away(float v) {
 #endif
 }
 
+// Minimum and maximum as the reference's std::fmin / std::fmax give them on
+// its x86-64 host (IEEE 754-2008 minNum / maxNum): a signaling NaN operand
+// gives that NaN quieted, a quiet NaN operand is ignored, and of two operands
+// that compare equal (+0 and -0) the second is returned. IEEE 754 leaves the
+// sign of equal zeros open, so all of it is spelled out here rather than left
+// to a library or an instruction. (FP16 signaling NaNs such as 0x7c01 widen to
+// signaling float NaNs, so they do reach these.)
+GLUE_HD bool is_nan(float v) { return v != v; }
+
+GLUE_HD bool is_signaling(float v) {
+    const std::uint32_t bits = float_bits(v);
+    return (bits & 0x7fc00000u) == 0x7f800000u && (bits & 0x003fffffu) != 0u;
+}
+
+GLUE_HD float quieted(float v) { return bits_float(float_bits(v) | 0x00400000u); }
+
 GLUE_HD float fmin_ieee(float a, float b) {
-#if defined(__CUDA_ARCH__)
-    return fminf(a, b);
-#else
-    return __builtin_fminf(a, b);
-#endif
+    if (is_signaling(a)) return quieted(a);
+    if (is_signaling(b)) return quieted(b);
+    if (is_nan(a)) return b;
+    if (is_nan(b)) return a;
+    return a < b ? a : b;
 }
 
 GLUE_HD float fmax_ieee(float a, float b) {
-#if defined(__CUDA_ARCH__)
-    return fmaxf(a, b);
-#else
-    return __builtin_fmaxf(a, b);
-#endif
+    if (is_signaling(a)) return quieted(a);
+    if (is_signaling(b)) return quieted(b);
+    if (is_nan(a)) return b;
+    if (is_nan(b)) return a;
+    return a > b ? a : b;
 }
 
 // binary16 -> binary32, exact.
@@ -264,6 +287,61 @@ GLUE_HD void reduce_parts(const Half* input, const Half* mask, Half* output, std
         value = add(value, term);
     }
     output[i] = to_half(value);
+}
+
+// The elementwise steps between stages (reference host_ops.cpp:101-167,
+// 474-521), element i each.
+
+// values[i] = round(values[i]) clamped to [-128, 127]; also stored as int8.
+GLUE_HD void round_to_int8(Half* values, std::int8_t* quantized, std::size_t i) {
+    const float value = fmin_ieee(127.0f, fmax_ieee(-128.0f, round_away(to_float(values[i]))));
+    values[i] = to_half(value);
+    quantized[i] = static_cast<std::int8_t>(static_cast<int>(value));
+}
+
+GLUE_HD void int8_to_half(const std::int8_t* values, Half* output, std::size_t i) {
+    output[i] = to_half(static_cast<float>(values[i]));
+}
+
+GLUE_HD void clamp_min(Half* values, float minimum, std::size_t i) {
+    values[i] = to_half(fmax_ieee(to_float(values[i]), minimum));
+}
+
+// quant[i] = max(quant[i], 0.5) in FP16; values[i] *= the FP16 reciprocal of it.
+GLUE_HD void clamp_reciprocal_with_quant(Half* quant_step, Half* values, std::size_t i) {
+    const Half quant = to_half(fmax_ieee(to_float(quant_step[i]), 0.5f));
+    quant_step[i] = quant;
+    const Half reciprocal = to_half(div(1.0f, to_float(quant)));
+    values[i] = to_half(mul(to_float(values[i]), to_float(reciprocal)));
+}
+
+GLUE_HD void add_in_place(Half* first, const Half* second, std::size_t i) {
+    first[i] = to_half(add(to_float(first[i]), to_float(second[i])));
+}
+
+// values[i] *= factors[i % spatial_count] (one factor plane for every channel).
+GLUE_HD void multiply_broadcast(Half* values, const Half* factors, std::size_t spatial_count, std::size_t i) {
+    values[i] = to_half(mul(to_float(values[i]), to_float(factors[i % spatial_count])));
+}
+
+// first[i] = FP16(first[i] + second[i]) * quant_step[i], rounded to FP16 after each step.
+GLUE_HD void add_and_multiply(Half* first, const Half* second, const Half* quant_step, std::size_t i) {
+    const Half sum = to_half(add(to_float(first[i]), to_float(second[i])));
+    first[i] = to_half(mul(to_float(sum), to_float(quant_step[i])));
+}
+
+// Output element i of a (planes, out_h, out_w) tensor: the input pixel at the
+// clamped coordinates (edge replication), or, with out_h <= height and
+// out_w <= width, the crop from the origin.
+GLUE_HD void replicate_or_crop(const Half* input, Half* output, int height, int width, int out_h, int out_w,
+                               std::size_t i) {
+    const std::size_t out_plane = static_cast<std::size_t>(out_h) * out_w;
+    const std::size_t plane = i / out_plane;
+    const int y = static_cast<int>((i % out_plane) / out_w);
+    const int x = static_cast<int>(i % out_w);
+    const int sy = y < height ? y : height - 1;
+    const int sx = x < width ? x : width - 1;
+    output[i] = input[(plane * height + sy) * width + sx];
 }
 
 }  // namespace nvcr_sm100::glue

@@ -33,4 +33,25 @@ cudaError_t process_with_mask(const std::uint16_t* values, const std::uint16_t* 
 cudaError_t reduce(const std::uint16_t* input, const std::uint16_t* mask, std::uint16_t* output, int batch,
                    int channels, int height, int width, int ways, cudaStream_t stream);
 
+// The elementwise steps between stages; which operands each reads is in
+// glue_elements.cuh (a: the tensor updated or written; b: the second operand,
+// which clamp_reciprocal_with_quant also updates (a is its quant step, b its
+// values); c: the third operand; q: the int8 tensor of round_to_int8 /
+// int8_to_half).
+enum class PointwiseOp : int {
+    round_to_int8,
+    int8_to_half,
+    clamp_min,
+    clamp_reciprocal_with_quant,
+    add_in_place,
+    multiply_broadcast,
+    add_and_multiply,
+};
+cudaError_t pointwise(PointwiseOp op, std::uint16_t* a, std::uint16_t* b, const std::uint16_t* c,
+                      std::int8_t* q, std::size_t count, float scalar, std::size_t spatial_count, cudaStream_t stream);
+cudaError_t replicate_pad(const std::uint16_t* input, std::uint16_t* output, int batch, int channels, int height,
+                          int width, int padded_height, int padded_width, cudaStream_t stream);
+cudaError_t crop_spatial(const std::uint16_t* input, std::uint16_t* output, int batch, int channels, int height,
+                         int width, int out_height, int out_width, cudaStream_t stream);
+
 }  // namespace nvcr_sm100::glue

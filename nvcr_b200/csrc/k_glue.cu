@@ -69,6 +69,27 @@ __global__ void reduce_kernel(const Half* __restrict__ input, const Half* mask, 
     GLUE_GRID_STRIDE(i, part_size) reduce_parts(input, mask, output, part_size, parts, i);
 }
 
+// The elementwise steps, one kernel for all (the op is uniform per launch).
+__global__ void pointwise_kernel(PointwiseOp op, Half* a, Half* b, const Half* c, std::int8_t* q,
+                                 std::size_t count, float scalar, std::size_t spatial_count) {
+    GLUE_GRID_STRIDE(i, count) {
+        switch (op) {
+        case PointwiseOp::round_to_int8: round_to_int8(a, q, i); break;
+        case PointwiseOp::int8_to_half: int8_to_half(q, a, i); break;
+        case PointwiseOp::clamp_min: clamp_min(a, scalar, i); break;
+        case PointwiseOp::clamp_reciprocal_with_quant: clamp_reciprocal_with_quant(a, b, i); break;
+        case PointwiseOp::add_in_place: add_in_place(a, b, i); break;
+        case PointwiseOp::multiply_broadcast: multiply_broadcast(a, b, spatial_count, i); break;
+        case PointwiseOp::add_and_multiply: add_and_multiply(a, b, c, i); break;
+        }
+    }
+}
+
+__global__ void resize_kernel(const Half* __restrict__ input, Half* __restrict__ output, std::size_t count, int height,
+                              int width, int out_h, int out_w) {
+    GLUE_GRID_STRIDE(i, count) replicate_or_crop(input, output, height, width, out_h, out_w, i);
+}
+
 #undef GLUE_GRID_STRIDE
 
 std::size_t volume(int batch, int channels, int height, int width) {
@@ -132,6 +153,43 @@ cudaError_t reduce(const Half* input, const Half* mask, Half* output, int batch,
     }
     const std::size_t part_size = volume(batch, channels, height, width) / static_cast<std::size_t>(ways);
     reduce_kernel<<<grid_for(part_size), threads, 0, stream>>>(input, mask, output, part_size, ways);
+    return cudaGetLastError();
+}
+
+cudaError_t pointwise(PointwiseOp op, Half* a, Half* b, const Half* c, std::int8_t* q, std::size_t count,
+                      float scalar, std::size_t spatial_count, cudaStream_t stream) {
+    if (count == 0 || a == nullptr) return cudaErrorInvalidValue;
+    const bool needs_b = op == PointwiseOp::clamp_reciprocal_with_quant || op == PointwiseOp::add_in_place ||
+        op == PointwiseOp::multiply_broadcast || op == PointwiseOp::add_and_multiply;
+    const bool needs_q = op == PointwiseOp::round_to_int8 || op == PointwiseOp::int8_to_half;
+    if ((needs_b && b == nullptr) || (op == PointwiseOp::add_and_multiply && c == nullptr) || (needs_q && q == nullptr) ||
+        (op == PointwiseOp::multiply_broadcast && spatial_count == 0)) {
+        return cudaErrorInvalidValue;
+    }
+    pointwise_kernel<<<grid_for(count), threads, 0, stream>>>(op, a, b, c, q, count, scalar, spatial_count);
+    return cudaGetLastError();
+}
+
+cudaError_t replicate_pad(const Half* input, Half* output, int batch, int channels, int height, int width,
+                          int padded_height, int padded_width, cudaStream_t stream) {
+    if (input == nullptr || output == nullptr || batch <= 0 || channels <= 0 || height <= 0 || width <= 0 ||
+        padded_height < height || padded_width < width) {
+        return cudaErrorInvalidValue;
+    }
+    const std::size_t count = static_cast<std::size_t>(batch) * channels * padded_height * padded_width;
+    resize_kernel<<<grid_for(count), threads, 0, stream>>>(input, output, count, height, width, padded_height,
+                                                           padded_width);
+    return cudaGetLastError();
+}
+
+cudaError_t crop_spatial(const Half* input, Half* output, int batch, int channels, int height, int width,
+                         int out_height, int out_width, cudaStream_t stream) {
+    if (input == nullptr || output == nullptr || batch <= 0 || channels <= 0 || height <= 0 || width <= 0 ||
+        out_height <= 0 || out_width <= 0 || out_height > height || out_width > width) {
+        return cudaErrorInvalidValue;
+    }
+    const std::size_t count = static_cast<std::size_t>(batch) * channels * out_height * out_width;
+    resize_kernel<<<grid_for(count), threads, 0, stream>>>(input, output, count, height, width, out_height, out_width);
     return cudaGetLastError();
 }
 

@@ -80,6 +80,9 @@ EXPORTS = [
     "nvcr_sm100_fx_infer_output_extents", "nvcr_sm100_fx_run", "nvcr_sm100_fx_last_launch_count",
     "nvcr_sm100_dcvc_build_decode_indexes", "nvcr_sm100_dcvc_build_encode_indexes", "nvcr_sm100_dcvc_make_mask",
     "nvcr_sm100_dcvc_restore", "nvcr_sm100_dcvc_process_with_mask", "nvcr_sm100_dcvc_reduce",
+    "nvcr_sm100_dcvc_round_to_int8", "nvcr_sm100_dcvc_int8_to_half", "nvcr_sm100_dcvc_clamp_min",
+    "nvcr_sm100_dcvc_clamp_reciprocal_with_quant", "nvcr_sm100_dcvc_add_in_place", "nvcr_sm100_dcvc_multiply_broadcast",
+    "nvcr_sm100_dcvc_add_and_multiply", "nvcr_sm100_dcvc_replicate_pad", "nvcr_sm100_dcvc_crop_spatial",
 ]
 
 _lib: ctypes.CDLL | None = None
@@ -156,6 +159,15 @@ def library() -> ctypes.CDLL:
         "nvcr_sm100_dcvc_restore": (ctypes.c_int, [vp] * 4 + [ctypes.c_int32] * 4 + [ctypes.c_int, vp]),
         "nvcr_sm100_dcvc_process_with_mask": (ctypes.c_int, [vp] * 8 + [sz, ctypes.c_float, vp]),
         "nvcr_sm100_dcvc_reduce": (ctypes.c_int, [vp] * 3 + [ctypes.c_int32] * 4 + [ctypes.c_int, vp]),
+        "nvcr_sm100_dcvc_round_to_int8": (ctypes.c_int, [vp, vp, sz, vp]),
+        "nvcr_sm100_dcvc_int8_to_half": (ctypes.c_int, [vp, vp, sz, vp]),
+        "nvcr_sm100_dcvc_clamp_min": (ctypes.c_int, [vp, sz, ctypes.c_float, vp]),
+        "nvcr_sm100_dcvc_clamp_reciprocal_with_quant": (ctypes.c_int, [vp, vp, sz, vp]),
+        "nvcr_sm100_dcvc_add_in_place": (ctypes.c_int, [vp, vp, sz, vp]),
+        "nvcr_sm100_dcvc_multiply_broadcast": (ctypes.c_int, [vp, vp, sz, ctypes.c_int32, vp]),
+        "nvcr_sm100_dcvc_add_and_multiply": (ctypes.c_int, [vp, vp, vp, sz, vp]),
+        "nvcr_sm100_dcvc_replicate_pad": (ctypes.c_int, [vp, vp] + [ctypes.c_int32] * 6 + [vp]),
+        "nvcr_sm100_dcvc_crop_spatial": (ctypes.c_int, [vp, vp] + [ctypes.c_int32] * 6 + [vp]),
     }
     for name, (restype, argtypes) in signatures.items():
         function = getattr(lib, name)

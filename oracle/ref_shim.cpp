@@ -335,6 +335,38 @@ int ref_glue_reduce(const std::uint16_t* input, const std::uint16_t* mask, std::
         ? 1 : 0;
 }
 
+// The elementwise steps (host_ops.cpp:101-118, 474-521), op numbered as
+// nvcr_sm100::glue::PointwiseOp; a, b, c, q as there.
+int ref_glue_pointwise(int op, std::uint16_t* a, std::uint16_t* b, const std::uint16_t* c, std::int8_t* q,
+                       std::size_t count, float scalar, std::size_t spatial_count) {
+    const auto A = std::span(a, count);
+    switch (op) {
+    case 0: return glue::round_to_int8(A, std::span(q, count)) ? 1 : 0;
+    case 1: return glue::int8_to_half(std::span<const std::int8_t>(q, count), A) ? 1 : 0;
+    case 2: return glue::clamp_min(A, scalar) ? 1 : 0;
+    case 3: return glue::clamp_reciprocal_with_quant(A, std::span(b, count)) ? 1 : 0;
+    case 4: return glue::add_in_place(A, std::span<const std::uint16_t>(b, count)) ? 1 : 0;
+    case 5: {
+        const std::size_t channels = spatial_count == 0 ? 0 : count / spatial_count;
+        return glue::multiply_broadcast_in_place(A, std::span<const std::uint16_t>(b, spatial_count), spatial_count,
+                                                 static_cast<std::int32_t>(channels)) ? 1 : 0;
+    }
+    case 6: return glue::add_and_multiply(A, std::span<const std::uint16_t>(b, count), std::span(c, count)) ? 1 : 0;
+    default: return -1;
+    }
+}
+
+int ref_glue_pad_or_crop(const std::uint16_t* input, std::uint16_t* output, std::size_t out_capacity, int batch,
+                         int channels, int height, int width, int out_height, int out_width, int pad) {
+    const glue::Shape4D shape{batch, channels, height, width};
+    const std::size_t in_count = static_cast<std::size_t>(batch > 0 ? batch : 0) * (channels > 0 ? channels : 0) *
+        (height > 0 ? height : 0) * (width > 0 ? width : 0);
+    return (pad ? glue::replicate_pad(std::span(input, in_count), std::span(output, out_capacity), shape, out_height,
+                                      out_width)
+                : glue::crop_spatial(std::span(input, in_count), std::span(output, out_capacity), shape, out_height,
+                                     out_width)) ? 1 : 0;
+}
+
 void ref_free(void* pointer) { std::free(pointer); }
 
 }  // extern "C"

@@ -84,4 +84,34 @@ int gh_reduce(const std::uint16_t* input, const std::uint16_t* mask, std::uint16
     return 1;
 }
 
+int gh_pointwise(int op, std::uint16_t* a, std::uint16_t* b, const std::uint16_t* c, std::int8_t* q, std::size_t count,
+                 float scalar, std::size_t spatial_count) {
+    if (count == 0) return 0;
+    for (std::size_t i = 0; i < count; ++i) {
+        switch (op) {
+        case 0: glue::round_to_int8(a, q, i); break;
+        case 1: glue::int8_to_half(q, a, i); break;
+        case 2: glue::clamp_min(a, scalar, i); break;
+        case 3: glue::clamp_reciprocal_with_quant(a, b, i); break;
+        case 4: glue::add_in_place(a, b, i); break;
+        case 5: glue::multiply_broadcast(a, b, spatial_count, i); break;
+        case 6: glue::add_and_multiply(a, b, c, i); break;
+        default: return -1;
+        }
+    }
+    return 1;
+}
+
+int gh_pad_or_crop(const std::uint16_t* input, std::uint16_t* output, int batch, int channels, int height, int width,
+                   int out_height, int out_width, int pad) {
+    if (batch <= 0 || channels <= 0 || height <= 0 || width <= 0) return 0;
+    if (pad ? (out_height < height || out_width < width)
+            : (out_height <= 0 || out_width <= 0 || out_height > height || out_width > width)) {
+        return 0;
+    }
+    const std::size_t count = static_cast<std::size_t>(batch) * channels * out_height * out_width;
+    for (std::size_t i = 0; i < count; ++i) glue::replicate_or_crop(input, output, height, width, out_height, out_width, i);
+    return 1;
+}
+
 }  // extern "C"

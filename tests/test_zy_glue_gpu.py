@@ -124,3 +124,42 @@ def test_process_and_reduce(cuda, host):
                                                     batch, channels, height, width, ways, None))
             torch.cuda.synchronize()
             assert np.array_equal(out.cpu().numpy().view(np.uint16), want)
+
+
+def test_pointwise_steps(cuda, host):
+    """Each elementwise step on the device against the host build (NaN equal to NaN)."""
+    import torch
+
+    from nvcr_b200.executor import _check, library
+    from tests.test_glue_host import POINTWISE, random_halves, same_halves
+
+    host.gh_pointwise.argtypes = [ctypes.c_int] + [ctypes.c_void_p] * 4 + [ctypes.c_size_t, ctypes.c_float,
+                                                                           ctypes.c_size_t]
+    rng = np.random.default_rng(12)
+    spatial, channels = 8160, 16
+    count = spatial * channels
+    base = [random_halves(rng, count) for _ in range(3)]
+    q = rng.integers(-128, 128, count).astype(np.int8)
+    lib = library()
+    for op, code in POINTWISE.items():
+        a, b, c, qq = base[0].copy(), base[1].copy(), base[2].copy(), q.copy()
+        assert host.gh_pointwise(code, a.ctypes.data, b.ctypes.data, c.ctypes.data, qq.ctypes.data, count, 0.11,
+                                 spatial) == 1
+        da, db, dc = (torch.from_numpy(x.view(np.int16).copy()).cuda() for x in base)
+        dq = torch.from_numpy(q.copy()).cuda()
+        calls = {
+            "round_to_int8": lambda: lib.nvcr_sm100_dcvc_round_to_int8(ptr(da), ptr(dq), count, None),
+            "int8_to_half": lambda: lib.nvcr_sm100_dcvc_int8_to_half(ptr(dq), ptr(da), count, None),
+            "clamp_min": lambda: lib.nvcr_sm100_dcvc_clamp_min(ptr(da), count, 0.11, None),
+            "clamp_reciprocal_with_quant": lambda: lib.nvcr_sm100_dcvc_clamp_reciprocal_with_quant(ptr(da), ptr(db),
+                                                                                                  count, None),
+            "add_in_place": lambda: lib.nvcr_sm100_dcvc_add_in_place(ptr(da), ptr(db), count, None),
+            "multiply_broadcast": lambda: lib.nvcr_sm100_dcvc_multiply_broadcast(ptr(da), ptr(db), spatial, channels,
+                                                                                 None),
+            "add_and_multiply": lambda: lib.nvcr_sm100_dcvc_add_and_multiply(ptr(da), ptr(db), ptr(dc), count, None),
+        }
+        _check(calls[op]())
+        torch.cuda.synchronize()
+        assert same_halves(da.cpu().numpy(), a), op
+        assert same_halves(db.cpu().numpy(), b), op
+        assert np.array_equal(dq.cpu().numpy(), qq), op
