@@ -351,6 +351,19 @@ int nvcr_sm100_dcvc_replicate_pad(const uint16_t* input, uint16_t* output, int32
 int nvcr_sm100_dcvc_crop_spatial(const uint16_t* input, uint16_t* output, int32_t batch, int32_t channels,
                                  int32_t height, int32_t width, int32_t out_height, int32_t out_width, void* stream);
 
+/* Picture conversions at the codec's edges (reference host_ops.cpp:198-305):
+ * RGB24 (interleaved, width x height) or YUV 4:2:0 8-bit (planar Y, U, V; even
+ * width and height) to a 3-plane FP16 YCbCr picture of padded_height x
+ * padded_width with the last row and column replicated (BT.709 weights), and a
+ * 1 x 3 x height x width YCbCr picture back to the visible (even) 4:2:0 planes. */
+int nvcr_sm100_dcvc_rgb24_to_ycbcr_padded(const uint8_t* input, int32_t width, int32_t height, uint16_t* output,
+                                          int32_t padded_height, int32_t padded_width, void* stream);
+int nvcr_sm100_dcvc_yuv420p8_to_ycbcr_padded(const uint8_t* input, int32_t width, int32_t height, uint16_t* output,
+                                             int32_t padded_height, int32_t padded_width, void* stream);
+int nvcr_sm100_dcvc_ycbcr_padded_to_yuv420p8(const uint16_t* input, int32_t batch, int32_t channels, int32_t height,
+                                             int32_t width, int32_t visible_width, int32_t visible_height,
+                                             uint8_t* output, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

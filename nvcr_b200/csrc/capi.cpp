@@ -677,4 +677,27 @@ int nvcr_sm100_dcvc_crop_spatial(const uint16_t* input, uint16_t* output, int32_
                        "crop shape invalid");
 }
 
+int nvcr_sm100_dcvc_rgb24_to_ycbcr_padded(const uint8_t* input, int32_t width, int32_t height, uint16_t* output,
+                                          int32_t padded_height, int32_t padded_width, void* stream) {
+    return glue_status(nvcr_sm100::glue::to_ycbcr_padded(input, width, height, output, padded_height, padded_width,
+                                                         false, static_cast<cudaStream_t>(stream)),
+                       "picture size invalid");
+}
+
+int nvcr_sm100_dcvc_yuv420p8_to_ycbcr_padded(const uint8_t* input, int32_t width, int32_t height, uint16_t* output,
+                                             int32_t padded_height, int32_t padded_width, void* stream) {
+    return glue_status(nvcr_sm100::glue::to_ycbcr_padded(input, width, height, output, padded_height, padded_width,
+                                                         true, static_cast<cudaStream_t>(stream)),
+                       "picture size invalid");
+}
+
+int nvcr_sm100_dcvc_ycbcr_padded_to_yuv420p8(const uint16_t* input, int32_t batch, int32_t channels, int32_t height,
+                                             int32_t width, int32_t visible_width, int32_t visible_height,
+                                             uint8_t* output, void* stream) {
+    return glue_status(nvcr_sm100::glue::ycbcr_padded_to_yuv420p8(input, batch, channels, height, width, visible_width,
+                                                                  visible_height, output,
+                                                                  static_cast<cudaStream_t>(stream)),
+                       "picture size invalid");
+}
+
 }  // extern "C"

@@ -344,4 +344,80 @@ GLUE_HD void replicate_or_crop(const Half* input, Half* output, int height, int 
     output[i] = input[(plane * height + sy) * width + sx];
 }
 
+// Colour conversion at the picture edges (reference host_ops.cpp:198-305), one
+// output pixel each. The padded planes replicate the last row and column.
+// BT.709 luma weights; every step is one binary32 operation in the reference's
+// order.
+GLUE_HD void rgb24_to_ycbcr(const std::uint8_t* input, int width, int height, Half* output, int out_h, int out_w,
+                            std::size_t i) {
+    const std::size_t plane = static_cast<std::size_t>(out_h) * out_w;
+    const int y = static_cast<int>(i / out_w);
+    const int x = static_cast<int>(i % out_w);
+    const int sy = y < height ? y : height - 1;
+    const int sx = x < width ? x : width - 1;
+    const std::size_t source = (static_cast<std::size_t>(sy) * width + sx) * 3u;
+    const float kr = 0.2126f;
+    const float kg = 0.7152f;
+    const float kb = 0.0722f;
+    const float r = div(static_cast<float>(input[source]), 255.0f);
+    const float g = div(static_cast<float>(input[source + 1]), 255.0f);
+    const float b = div(static_cast<float>(input[source + 2]), 255.0f);
+    const float luma = add(add(mul(kr, r), mul(kg, g)), mul(kb, b));
+    const float cb = add(div(mul(0.5f, sub(b, luma)), sub(1.0f, kb)), 0.5f);
+    const float cr = add(div(mul(0.5f, sub(r, luma)), sub(1.0f, kr)), 0.5f);
+    output[i] = to_half(luma);
+    output[plane + i] = to_half(cb);
+    output[2 * plane + i] = to_half(cr);
+}
+
+// YUV 4:2:0 (8-bit planes Y, U, V; even width and height) to padded YCbCr.
+GLUE_HD void yuv420p8_to_ycbcr(const std::uint8_t* input, int width, int height, Half* output, int out_h, int out_w,
+                               std::size_t i) {
+    const std::size_t plane = static_cast<std::size_t>(out_h) * out_w;
+    const int y = static_cast<int>(i / out_w);
+    const int x = static_cast<int>(i % out_w);
+    const std::size_t sy = static_cast<std::size_t>(y < height ? y : height - 1);
+    const std::size_t sx = static_cast<std::size_t>(x < width ? x : width - 1);
+    const std::size_t y_size = static_cast<std::size_t>(width) * height;
+    const std::size_t uv_width = static_cast<std::size_t>(width) / 2;
+    const std::size_t uv_size = uv_width * (static_cast<std::size_t>(height) / 2);
+    const std::size_t uv_index = (sy / 2) * uv_width + sx / 2;
+    output[i] = to_half(div(static_cast<float>(input[sy * width + sx]), 255.0f));
+    output[plane + i] = to_half(div(static_cast<float>(input[y_size + uv_index]), 255.0f));
+    output[2 * plane + i] = to_half(div(static_cast<float>(input[y_size + uv_size + uv_index]), 255.0f));
+}
+
+// Padded YCbCr back to YUV 4:2:0: luma element i of the visible width x height
+// picture (round(clamp(v, 0, 1) * 255)), or chroma element i (the mean of a
+// 2x2 block, clamp(v * 255, 0, 255) truncated). `stride` is the padded width
+// and `plane` the padded plane size.
+GLUE_HD void ycbcr_luma_to_y(const Half* input, std::size_t stride, int width, std::uint8_t* output, std::size_t i) {
+    const std::size_t y = i / width;
+    const std::size_t x = i % width;
+    const float v = fmin_ieee(1.0f, fmax_ieee(0.0f, to_float(input[y * stride + x])));
+    output[i] = static_cast<std::uint8_t>(static_cast<int>(round_away(mul(v, 255.0f))));
+}
+
+GLUE_HD void ycbcr_chroma_to_uv(const Half* input, std::size_t plane, std::size_t stride, int width, int height,
+                                std::uint8_t* output, std::size_t i) {
+    const std::size_t uv_width = static_cast<std::size_t>(width) / 2;
+    const std::size_t uv_size = uv_width * (static_cast<std::size_t>(height) / 2);
+    const std::size_t uv_y = i / uv_width;
+    const std::size_t uv_x = i % uv_width;
+    float cb_sum = 0.0f;
+    float cr_sum = 0.0f;
+    for (int dy = 0; dy < 2; ++dy) {
+        for (int dx = 0; dx < 2; ++dx) {
+            const std::size_t spatial = (uv_y * 2 + dy) * stride + uv_x * 2 + dx;
+            cb_sum = add(cb_sum, to_float(input[plane + spatial]));
+            cr_sum = add(cr_sum, to_float(input[2 * plane + spatial]));
+        }
+    }
+    const std::size_t y_size = static_cast<std::size_t>(width) * height;
+    output[y_size + i] =
+        static_cast<std::uint8_t>(static_cast<int>(fmin_ieee(255.0f, fmax_ieee(0.0f, mul(mul(cb_sum, 0.25f), 255.0f)))));
+    output[y_size + uv_size + i] =
+        static_cast<std::uint8_t>(static_cast<int>(fmin_ieee(255.0f, fmax_ieee(0.0f, mul(mul(cr_sum, 0.25f), 255.0f)))));
+}
+
 }  // namespace nvcr_sm100::glue

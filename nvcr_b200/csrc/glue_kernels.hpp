@@ -54,4 +54,12 @@ cudaError_t replicate_pad(const std::uint16_t* input, std::uint16_t* output, int
 cudaError_t crop_spatial(const std::uint16_t* input, std::uint16_t* output, int batch, int channels, int height,
                          int width, int out_height, int out_width, cudaStream_t stream);
 
+// RGB24 (interleaved) or YUV 4:2:0 8-bit (planar, even size) to a padded
+// 3-plane YCbCr FP16 picture, edges replicated.
+cudaError_t to_ycbcr_padded(const std::uint8_t* input, int width, int height, std::uint16_t* output, int padded_height,
+                            int padded_width, bool yuv420, cudaStream_t stream);
+// A 1 x 3 x height x width YCbCr FP16 picture to the visible (even) YUV 4:2:0 8-bit planes.
+cudaError_t ycbcr_padded_to_yuv420p8(const std::uint16_t* input, int batch, int channels, int height, int width,
+                                     int visible_width, int visible_height, std::uint8_t* output, cudaStream_t stream);
+
 }  // namespace nvcr_sm100::glue

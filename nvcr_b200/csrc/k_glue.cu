@@ -90,6 +90,29 @@ __global__ void resize_kernel(const Half* __restrict__ input, Half* __restrict__
     GLUE_GRID_STRIDE(i, count) replicate_or_crop(input, output, height, width, out_h, out_w, i);
 }
 
+__global__ void to_ycbcr_kernel(const std::uint8_t* __restrict__ input, int width, int height, Half* __restrict__ output,
+                                int out_h, int out_w, bool yuv) {
+    GLUE_GRID_STRIDE(i, static_cast<std::size_t>(out_h) * out_w) {
+        if (yuv) {
+            yuv420p8_to_ycbcr(input, width, height, output, out_h, out_w, i);
+        } else {
+            rgb24_to_ycbcr(input, width, height, output, out_h, out_w, i);
+        }
+    }
+}
+
+__global__ void to_yuv_kernel(const Half* __restrict__ input, std::size_t plane, std::size_t stride, int width,
+                              int height, std::uint8_t* __restrict__ output) {
+    const std::size_t y_size = static_cast<std::size_t>(width) * height;
+    GLUE_GRID_STRIDE(i, y_size + y_size / 4) {
+        if (i < y_size) {
+            ycbcr_luma_to_y(input, stride, width, output, i);
+        } else {
+            ycbcr_chroma_to_uv(input, plane, stride, width, height, output, i - y_size);
+        }
+    }
+}
+
 #undef GLUE_GRID_STRIDE
 
 std::size_t volume(int batch, int channels, int height, int width) {
@@ -190,6 +213,32 @@ cudaError_t crop_spatial(const Half* input, Half* output, int batch, int channel
     }
     const std::size_t count = static_cast<std::size_t>(batch) * channels * out_height * out_width;
     resize_kernel<<<grid_for(count), threads, 0, stream>>>(input, output, count, height, width, out_height, out_width);
+    return cudaGetLastError();
+}
+
+cudaError_t to_ycbcr_padded(const std::uint8_t* input, int width, int height, Half* output, int padded_height,
+                            int padded_width, bool yuv420, cudaStream_t stream) {
+    if (input == nullptr || output == nullptr || width <= 0 || height <= 0 || padded_height < height ||
+        padded_width < width || (yuv420 && ((width & 1) != 0 || (height & 1) != 0))) {
+        return cudaErrorInvalidValue;
+    }
+    const std::size_t count = static_cast<std::size_t>(padded_height) * padded_width;
+    to_ycbcr_kernel<<<grid_for(count), threads, 0, stream>>>(input, width, height, output, padded_height, padded_width,
+                                                             yuv420);
+    return cudaGetLastError();
+}
+
+cudaError_t ycbcr_padded_to_yuv420p8(const Half* input, int batch, int channels, int height, int width,
+                                     int visible_width, int visible_height, std::uint8_t* output, cudaStream_t stream) {
+    if (input == nullptr || output == nullptr || batch != 1 || channels != 3 || height <= 0 || width <= 0 ||
+        visible_width <= 0 || visible_height <= 0 || (visible_width & 1) != 0 || (visible_height & 1) != 0 ||
+        visible_width > width || visible_height > height) {
+        return cudaErrorInvalidValue;
+    }
+    const std::size_t y_size = static_cast<std::size_t>(visible_width) * visible_height;
+    to_yuv_kernel<<<grid_for(y_size + y_size / 4), threads, 0, stream>>>(
+        input, static_cast<std::size_t>(height) * width, static_cast<std::size_t>(width), visible_width,
+        visible_height, output);
     return cudaGetLastError();
 }
 

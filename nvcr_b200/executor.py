@@ -83,6 +83,8 @@ EXPORTS = [
     "nvcr_sm100_dcvc_round_to_int8", "nvcr_sm100_dcvc_int8_to_half", "nvcr_sm100_dcvc_clamp_min",
     "nvcr_sm100_dcvc_clamp_reciprocal_with_quant", "nvcr_sm100_dcvc_add_in_place", "nvcr_sm100_dcvc_multiply_broadcast",
     "nvcr_sm100_dcvc_add_and_multiply", "nvcr_sm100_dcvc_replicate_pad", "nvcr_sm100_dcvc_crop_spatial",
+    "nvcr_sm100_dcvc_rgb24_to_ycbcr_padded", "nvcr_sm100_dcvc_yuv420p8_to_ycbcr_padded",
+    "nvcr_sm100_dcvc_ycbcr_padded_to_yuv420p8",
 ]
 
 _lib: ctypes.CDLL | None = None
@@ -168,6 +170,11 @@ def library() -> ctypes.CDLL:
         "nvcr_sm100_dcvc_add_and_multiply": (ctypes.c_int, [vp, vp, vp, sz, vp]),
         "nvcr_sm100_dcvc_replicate_pad": (ctypes.c_int, [vp, vp] + [ctypes.c_int32] * 6 + [vp]),
         "nvcr_sm100_dcvc_crop_spatial": (ctypes.c_int, [vp, vp] + [ctypes.c_int32] * 6 + [vp]),
+        "nvcr_sm100_dcvc_rgb24_to_ycbcr_padded": (ctypes.c_int, [vp, ctypes.c_int32, ctypes.c_int32, vp,
+                                                                 ctypes.c_int32, ctypes.c_int32, vp]),
+        "nvcr_sm100_dcvc_yuv420p8_to_ycbcr_padded": (ctypes.c_int, [vp, ctypes.c_int32, ctypes.c_int32, vp,
+                                                                    ctypes.c_int32, ctypes.c_int32, vp]),
+        "nvcr_sm100_dcvc_ycbcr_padded_to_yuv420p8": (ctypes.c_int, [vp] + [ctypes.c_int32] * 6 + [vp, vp]),
     }
     for name, (restype, argtypes) in signatures.items():
         function = getattr(lib, name)

@@ -367,6 +367,23 @@ int ref_glue_pad_or_crop(const std::uint16_t* input, std::uint16_t* output, std:
                                      out_width)) ? 1 : 0;
 }
 
+int ref_glue_to_ycbcr(const std::uint8_t* input, std::size_t input_size, int width, int height, std::uint16_t* output,
+                      std::size_t output_size, int padded_height, int padded_width, int yuv) {
+    return (yuv ? glue::yuv420p8_to_ycbcr_padded(std::span(input, input_size), width, height,
+                                                 std::span(output, output_size), padded_height, padded_width)
+                : glue::rgb24_to_ycbcr_padded(std::span(input, input_size), width, height,
+                                              std::span(output, output_size), padded_height, padded_width)) ? 1 : 0;
+}
+
+int ref_glue_to_yuv(const std::uint16_t* input, int batch, int channels, int height, int width, int visible_width,
+                    int visible_height, std::uint8_t* output, std::size_t output_size) {
+    const glue::Shape4D shape{batch, channels, height, width};
+    const std::size_t in_count = static_cast<std::size_t>(batch > 0 ? batch : 0) * (channels > 0 ? channels : 0) *
+        (height > 0 ? height : 0) * (width > 0 ? width : 0);
+    return glue::ycbcr_padded_to_yuv420p8(std::span(input, in_count), shape, visible_width, visible_height,
+                                          std::span(output, output_size)) ? 1 : 0;
+}
+
 void ref_free(void* pointer) { std::free(pointer); }
 
 }  // extern "C"

@@ -114,4 +114,40 @@ int gh_pad_or_crop(const std::uint16_t* input, std::uint16_t* output, int batch,
     return 1;
 }
 
+int gh_to_ycbcr(const std::uint8_t* input, int width, int height, std::uint16_t* output, int padded_height,
+                int padded_width, int yuv) {
+    if (width <= 0 || height <= 0 || padded_height < height || padded_width < width ||
+        (yuv && ((width & 1) != 0 || (height & 1) != 0))) {
+        return 0;
+    }
+    const std::size_t count = static_cast<std::size_t>(padded_height) * padded_width;
+    for (std::size_t i = 0; i < count; ++i) {
+        if (yuv) {
+            glue::yuv420p8_to_ycbcr(input, width, height, output, padded_height, padded_width, i);
+        } else {
+            glue::rgb24_to_ycbcr(input, width, height, output, padded_height, padded_width, i);
+        }
+    }
+    return 1;
+}
+
+int gh_to_yuv(const std::uint16_t* input, int batch, int channels, int height, int width, int visible_width,
+              int visible_height, std::uint8_t* output) {
+    if (batch != 1 || channels != 3 || height <= 0 || width <= 0 || visible_width <= 0 || visible_height <= 0 ||
+        (visible_width & 1) != 0 || (visible_height & 1) != 0 || visible_width > width || visible_height > height) {
+        return 0;
+    }
+    const std::size_t y_size = static_cast<std::size_t>(visible_width) * visible_height;
+    const std::size_t plane = static_cast<std::size_t>(height) * width;
+    for (std::size_t i = 0; i < y_size + y_size / 4; ++i) {
+        if (i < y_size) {
+            glue::ycbcr_luma_to_y(input, static_cast<std::size_t>(width), visible_width, output, i);
+        } else {
+            glue::ycbcr_chroma_to_uv(input, plane, static_cast<std::size_t>(width), visible_width, visible_height, output,
+                                     i - y_size);
+        }
+    }
+    return 1;
+}
+
 }  // extern "C"

@@ -284,3 +284,44 @@ def test_replicate_pad_and_crop(sides):
             assert ok_a == ok_b, (pad, out_h, out_w)
             if ok_a:
                 assert np.array_equal(a, b)
+
+
+def test_picture_conversions(sides):
+    """RGB24 and YUV 4:2:0 into padded YCbCr (every 8-bit value, odd and even
+    sizes, padding), and YCbCr back to YUV 4:2:0 from seeded halves with
+    values outside [0, 1] and specials; refusals of odd or oversized pictures."""
+    mine, theirs = sides
+    mine.gh_to_ycbcr.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p] + [ctypes.c_int] * 3
+    theirs.ref_glue_to_ycbcr.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_int,
+                                         ctypes.c_void_p, ctypes.c_size_t] + [ctypes.c_int] * 3
+    mine.gh_to_yuv.argtypes = [ctypes.c_void_p] + [ctypes.c_int] * 6 + [ctypes.c_void_p]
+    theirs.ref_glue_to_yuv.argtypes = [ctypes.c_void_p] + [ctypes.c_int] * 6 + [ctypes.c_void_p, ctypes.c_size_t]
+    rng = np.random.default_rng(13)
+    for yuv in (0, 1):
+        for width, height, padded_h, padded_w in ((16, 16, 16, 16), (24, 10, 16, 32), (7, 5, 8, 8), (2, 2, 4, 6),
+                                                  (3, 4, 2, 4)):
+            size = width * height * 3 if not yuv else width * height + 2 * ((width // 2) * (height // 2))
+            picture = rng.integers(0, 256, size, dtype=np.uint8)
+            picture[: min(size, 256)] = np.arange(min(size, 256), dtype=np.uint8)
+            capacity = 3 * max(padded_h, 1) * max(padded_w, 1)
+            a = np.zeros(capacity, np.uint16)
+            b = np.zeros(capacity, np.uint16)
+            ok_a = mine.gh_to_ycbcr(ptr(picture), width, height, ptr(a), padded_h, padded_w, yuv)
+            ok_b = theirs.ref_glue_to_ycbcr(ptr(picture), size, width, height, ptr(b), capacity, padded_h, padded_w,
+                                            yuv)
+            assert ok_a == ok_b, (yuv, width, height, padded_h, padded_w)
+            if ok_a:
+                assert np.array_equal(a, b)
+    for height, width, visible_w, visible_h in ((16, 16, 16, 16), (10, 24, 20, 8), (9, 9, 8, 8), (8, 8, 7, 8),
+                                                (8, 8, 10, 8)):
+        source = random_halves(rng, 3 * height * width)
+        source[: 3 * height * width // 2] = rng.uniform(-0.2, 1.2, 3 * height * width // 2).astype(np.float16) \
+            .view(np.uint16)
+        capacity = visible_w * visible_h + 2 * (visible_w // 2) * (visible_h // 2) + 8
+        a = np.zeros(capacity, np.uint8)
+        b = np.zeros(capacity, np.uint8)
+        ok_a = mine.gh_to_yuv(ptr(source), 1, 3, height, width, visible_w, visible_h, ptr(a))
+        ok_b = theirs.ref_glue_to_yuv(ptr(source), 1, 3, height, width, visible_w, visible_h, ptr(b), capacity)
+        assert ok_a == ok_b, (height, width, visible_w, visible_h)
+        if ok_a:
+            assert np.array_equal(a, b)

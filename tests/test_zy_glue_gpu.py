@@ -163,3 +163,33 @@ def test_pointwise_steps(cuda, host):
         assert same_halves(da.cpu().numpy(), a), op
         assert same_halves(db.cpu().numpy(), b), op
         assert np.array_equal(dq.cpu().numpy(), qq), op
+
+
+def test_picture_conversions(cuda, host):
+    import torch
+
+    from nvcr_b200.executor import _check, library
+
+    host.gh_to_ycbcr.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p] + [ctypes.c_int] * 3
+    host.gh_to_yuv.argtypes = [ctypes.c_void_p] + [ctypes.c_int] * 6 + [ctypes.c_void_p]
+    rng = np.random.default_rng(14)
+    width, height, padded_h, padded_w = 1920, 1080, 1088, 1920
+    lib = library()
+    for yuv in (0, 1):
+        size = width * height * 3 if not yuv else width * height * 3 // 2
+        picture = rng.integers(0, 256, size, dtype=np.uint8)
+        expected = np.zeros(3 * padded_h * padded_w, np.uint16)
+        assert host.gh_to_ycbcr(picture.ctypes.data, width, height, expected.ctypes.data, padded_h, padded_w, yuv) == 1
+        device_picture = torch.from_numpy(picture).cuda()
+        out = torch.zeros(3 * padded_h * padded_w, dtype=torch.int16, device="cuda")
+        convert = lib.nvcr_sm100_dcvc_yuv420p8_to_ycbcr_padded if yuv else lib.nvcr_sm100_dcvc_rgb24_to_ycbcr_padded
+        _check(convert(ptr(device_picture), width, height, ptr(out), padded_h, padded_w, None))
+        torch.cuda.synchronize()
+        assert np.array_equal(out.cpu().numpy().view(np.uint16), expected)
+    back = np.zeros(width * height * 3 // 2, np.uint8)
+    assert host.gh_to_yuv(expected.ctypes.data, 1, 3, padded_h, padded_w, width, height, back.ctypes.data) == 1
+    device_back = torch.zeros(width * height * 3 // 2, dtype=torch.uint8, device="cuda")
+    _check(lib.nvcr_sm100_dcvc_ycbcr_padded_to_yuv420p8(ptr(out), 1, 3, padded_h, padded_w, width, height,
+                                                        ptr(device_back), None))
+    torch.cuda.synchronize()
+    assert np.array_equal(device_back.cpu().numpy(), back)
