@@ -65,10 +65,12 @@ def sides(reference):
 def test_generated_thresholds_equal_the_reference_table():
     """nvcr_b200/csrc/make_scale_thresholds.py derives the table from its
     definition; the reference ships it as constants (read here as text)."""
-    ref = re.findall(r"(0x[0-9a-f.]+p[+-]?\d+)F", (Path("/root/reference/src/dcvcrt/scale_index.hpp")).read_text()) \
-        if Path("/root/reference/src/dcvcrt/scale_index.hpp").exists() else None
-    if ref is None:
+    from oracle.oracle import REFERENCE_SOURCES
+
+    header = REFERENCE_SOURCES / "src" / "dcvcrt" / "scale_index.hpp"
+    if not header.exists():
         pytest.skip("reference sources not present")
+    ref = re.findall(r"(0x[0-9a-f.]+p[+-]?\d+)F", header.read_text())
     mine = [line.strip().rstrip("f,") for line in (ROOT / "nvcr_b200" / "csrc" / "scale_thresholds.inc").read_text()
             .splitlines() if line.startswith("0x")]
     assert len(mine) == 127 and [float.fromhex(v) for v in mine] == [float.fromhex(v) for v in ref]
