@@ -232,13 +232,15 @@ Result<FxExecutor::Plan*> FxExecutor::plan_for(const std::vector<FxExtent>& inpu
     auto found = plans_.find(inputs);
     if (found != plans_.end()) return found->second.get();
     auto plan = std::make_unique<Plan>(make_plan(inputs));
+    // Node values get buffers now; the inputs' values are the caller's buffers
+    // on device-memory runs, and get buffers at the first host-memory run.
     plan->values.assign(plan->value_extents.size(), nullptr);
-    for (std::size_t v = 0; v < plan->value_extents.size(); ++v) {
+    for (std::size_t v = plan->input_stop; v < plan->value_extents.size(); ++v) {
         void* device = nullptr;
         const cudaError_t status =
             cudaMalloc(&device, std::max<std::size_t>(1, plan->value_extents[v].count()) * sizeof(std::int32_t));
         if (status != cudaSuccess) {
-            for (std::size_t i = 0; i < v; ++i) cudaFree(plan->values[i]);
+            for (std::size_t i = plan->input_stop; i < v; ++i) cudaFree(plan->values[i]);
             return cuda_error(status, "cudaMalloc");
         }
         plan->values[v] = static_cast<std::int32_t*>(device);
@@ -382,8 +384,18 @@ Status FxExecutor::run(const std::vector<const std::int32_t*>& inputs, const std
     if (!uploaded) return uploaded.error();
     auto planned = plan_for(extents);
     if (!planned) return planned.error();
-    const Plan& plan = *planned.value();
+    Plan& plan = *planned.value();
     if (!plan.stopped && outputs.size() != plan.output_values.size()) return invalid("wrong number of outputs");
+    if (!device) {
+        for (std::size_t slot = 0; slot < plan.input_stop; ++slot) {
+            if (plan.values[slot] != nullptr) continue;
+            void* buffer = nullptr;
+            const cudaError_t status =
+                cudaMalloc(&buffer, std::max<std::size_t>(1, extents[slot].count()) * sizeof(std::int32_t));
+            if (status != cudaSuccess) return cuda_error(status, "cudaMalloc");
+            plan.values[slot] = static_cast<std::int32_t*>(buffer);
+        }
+    }
     launches_ = 0;
     std::vector<std::int32_t*> values = plan.values;
     cudaError_t status = cudaMemsetAsync(failure_, 0xFF, sizeof(unsigned long long), stream_);

@@ -77,7 +77,7 @@ private:
         std::size_t nodes_run{0};    // nodes [0, nodes_run) are launched
         bool stopped{false};
         Error stop;                  // the error the reference reports if no earlier stage failure
-        std::vector<std::int32_t*> values;  // device buffers (inputs only for host runs)
+        std::vector<std::int32_t*> values;  // device buffers; inputs' only after a host-memory run
     };
 
     FxExecutor(FxProgram program, cudaStream_t stream) : program_(std::move(program)), stream_(stream) {}
