@@ -179,8 +179,9 @@ const char* cudaGetErrorString(cudaError_t) { return "host build"; }
 
 // Loads <directory>/<stage> and runs it on int32 NCHW tensors through the
 // executor, as nvcr_b200.fx.FxExecutor.run does, taking the executor's
-// host-memory branch (device_memory 0) or its device-memory branch (here both
-// are host memory): outputs are malloc'd with their extents in out_extents.
+// host-memory branch (device_memory 0) or its device-memory branch (1; here both
+// are host memory), or the device branch and then the host branch twice on the
+// same executor (2): outputs are malloc'd with their extents in out_extents.
 // Returns 0 or ErrorCode + 1, with the message.
 int fxh_run(const char* directory, const char* stage, int input_count, const std::int32_t* extents,
             const std::int32_t* const* inputs, int output_capacity, std::int32_t* out_extents, std::int32_t** outputs,
@@ -219,6 +220,27 @@ int fxh_run(const char* directory, const char* stage, int input_count, const std
     }
     auto ran = executor.run(in, shapes, out, device_memory != 0);
     if (!ran) return report(ran.error());
+    if (device_memory == 2) {
+        // Again on the same executor through the host-memory branch, twice (the
+        // cached plan, its input buffers made at the first of these runs): the
+        // outputs must not change.
+        for (int again = 0; again < 2; ++again) {
+            std::vector<std::vector<std::int32_t>> copies;
+            std::vector<std::int32_t*> second;
+            for (std::size_t i = 0; i < inferred.value().size(); ++i) {
+                copies.emplace_back(std::max<std::size_t>(1, inferred.value()[i].count()), 0);
+                second.push_back(copies.back().data());
+            }
+            auto rerun = executor.run(in, shapes, second, false);
+            if (!rerun) return report(rerun.error());
+            for (std::size_t i = 0; i < second.size(); ++i) {
+                if (std::memcmp(second[i], out[i], inferred.value()[i].count() * sizeof(std::int32_t)) != 0) {
+                    std::snprintf(message, message_size, "repeated run differs");
+                    return -2;
+                }
+            }
+        }
+    }
     return 0;
 }
 

@@ -42,9 +42,10 @@ class FxHost:
         lib.fxh_free.argtypes = [ctypes.c_void_p]
         self.lib = lib
 
-    def run(self, directory, stage: str, inputs, capacity: int = 16, device_memory: bool = True):
+    def run(self, directory, stage: str, inputs, capacity: int = 16, device_memory=True):
         """(status, outputs, message): status 0 or ErrorCode + 1; device_memory
-        picks the executor's branch (both run on host memory here)."""
+        picks the executor's branch (both run on host memory here), or "both"
+        for the device branch then the host branch twice on one executor."""
         keep = [np.ascontiguousarray(x, np.int32) for x in inputs]
         extents = np.array([d for x in keep for d in x.shape] or [0], np.int32)
         pointers = (_i32p * max(1, len(keep)))(*[x.ctypes.data_as(_i32p) for x in keep])
@@ -54,7 +55,7 @@ class FxHost:
         status = self.lib.fxh_run(str(directory).encode(), stage.encode(), len(keep),
                                   extents.ctypes.data_as(_i32p), pointers, capacity,
                                   out_extents.ctypes.data_as(_i32p), outputs, message, 512,
-                                  1 if device_memory else 0)
+                                  2 if device_memory == "both" else 1 if device_memory else 0)
         result = []
         for index in range(capacity):
             if not outputs[index]:

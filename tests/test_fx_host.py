@@ -139,3 +139,18 @@ def test_empty_and_thin_tensors(fx_host, fx_oracle, tmp_path):
 
     for index, (program, inputs) in enumerate(empty_and_thin_cases()):
         matches_oracle(fx_host, fx_oracle, tmp_path, program, inputs, stage=f"z{index % 3}")
+
+
+def test_cached_plan_across_both_branches(fx_host, fx_oracle, tmp_path):
+    """One executor: a device-memory run, then host-memory runs that reuse its
+    plan (input buffers made late); all equal the oracle."""
+    for seed in range(8):
+        rng = np.random.default_rng(100 + seed)
+        program = decoder_like(rng, channels=8)
+        inputs = decoder_like_inputs(rng, program, 3 + seed, 4 + seed)
+        write_program(tmp_path, "c", program)
+        expected = fx_oracle.run(program, inputs)
+        got = fx_host.run(tmp_path, "c", inputs, device_memory="both")
+        assert got[0] == expected[0], got[2]
+        for mine, want in zip(got[1], expected[1]):
+            assert np.array_equal(mine, want)
