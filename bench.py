@@ -55,7 +55,18 @@ def parse_args():
     parser.add_argument("--no-cpu-baseline", action="store_true", help="skip the reference CPU timing")
     parser.add_argument("--layers", type=str, default="", help="comma-separated layer indices (default: all)")
     parser.add_argument("--no-decoder", action="store_true", help="skip the config 3-5 decoder measurements")
+    parser.add_argument("--no-reference-gpu", action="store_true",
+                        help="skip timing the reference's own CUDA executor (the GPU comparator)")
     return parser.parse_args()
+
+
+GOLDEN = ROOT / "tests" / "golden" / "fullsize_digests.json"
+
+
+def golden_digests() -> dict:
+    """The reference run_cpu's digests of the benchmark's outputs at full size
+    (tests/golden/make_fullsize_digests.py); empty when the file is absent."""
+    return json.loads(GOLDEN.read_text()) if GOLDEN.exists() else {}
 
 
 def peaks():
@@ -143,6 +154,13 @@ def select_layers(spec: str):
     return layers
 
 
+def input_seed(layer) -> int:
+    """Config 2 layer i's input comes from seed 200 + i, whichever layers run."""
+    from nvcr_b200.workloads import config2
+
+    return 200 + [candidate.name for candidate in config2()].index(layer.name)
+
+
 def reference_sample(layers, directory: Path, fraction: int, repeats: int = 1):
     """Times the reference's run_cpu on the first 1/`fraction` of each layer's
     output rows (the input rows that feed them); returns (TOPS, seconds, ops, sample text)."""
@@ -163,7 +181,7 @@ def reference_sample(layers, directory: Path, fraction: int, repeats: int = 1):
         out_h = (h + (2 if node else 0) - kernel) // stride + 1
         rows_out = max(1, out_h // fraction)
         rows_in = min(h, rows_out * stride + (kernel - 1))
-        x = layer_input(layer, seed=200 + index, height=rows_in)
+        x = layer_input(layer, seed=input_seed(layer), height=rows_in)
         path = layer.program.write(directory, layer.name)
         seconds = reference.time_run(path, [x], repeats=repeats)
         sample_out_h = (rows_in + (2 if node else 0) - kernel) // stride + 1
@@ -231,7 +249,7 @@ def main():
     executors, inputs, outputs, pinned_in, pinned_out = [], [], [], [], []
     for index, layer in enumerate(layers):
         executor = CudaExecutor.from_program(layer.program, stream=stream.cuda_stream)
-        x = layer_input(layer, seed=200 + index)
+        x = layer_input(layer, seed=input_seed(layer))
         (c, h, w), = executor.infer_output_extents([x.shape])
         xh = torch.from_numpy(x.astype(np.float16)).to(device)
         yh = torch.empty((c, h, w), dtype=torch.float16, device=device)
@@ -331,6 +349,21 @@ def main():
     h2d = sum(t.numel() * 2 for t in pinned_in)
     d2h = sum(t.numel() * 2 for t in pinned_out)
 
+    # Parity at full size: every layer's output as the last end-to-end step left
+    # it in host memory, against the reference's digest of the same layer.
+    from nvcr_b200.workloads import half_digest
+
+    golden = golden_digests()
+    expected = golden.get("config2", {})
+    unchecked = [layer.name for layer in layers if layer.name not in expected]
+    differing = [layer.name for layer, host in zip(layers, pinned_out)
+                 if layer.name in expected and half_digest(host.numpy()) != expected[layer.name]["digest"]]
+    parity = {"checker": "SHA-256 of each FP16 output against the reference run_cpu's (tests/golden/"
+                         "fullsize_digests.json, NaN as 0x7e00), every rank",
+              "config2": {"outputs_checked": int(group.sum(len(layers) - len(unchecked))),
+                          "differing": int(group.sum(len(differing))), "differing_here": differing,
+                          "unchecked": unchecked}}
+
     # Roofline of the integer GEMM kernel and per-layer bounds.
     hbm, bf16, source = peaks()
     int8_peak = 2.0 * bf16  # B200's dense int8 rate is twice its dense bf16 rate
@@ -390,7 +423,17 @@ def main():
             cpu_baseline = {"value": None, "unit": "TOPS", "cores": 0, "kind": "reference",
                             "sample": f"unavailable: {error}"}
 
-    decoder = None if args.no_decoder else decoder_throughput(args, device, rank, world, max_over_ranks, barrier)
+    reference_gpu = None
+    if rank == 0 and world == 1 and not args.no_reference_gpu:
+        try:
+            reference_gpu = reference_gpu_leg(layers, device, golden, args.no_decoder)
+        except Exception as error:  # the comparator build may be absent
+            reference_gpu = {"unavailable": str(error)}
+
+    decoder = None
+    if not args.no_decoder:
+        decoder = decoder_throughput(args, device, rank, world, group, golden)
+        parity.update(decoder.pop("parity"))
 
     if rank == 0:
         line = {
@@ -409,7 +452,9 @@ def main():
             "cpu_baseline": cpu_baseline,
             "clocks": clocks,
             "gpu_launches": launches,
+            "parity": parity,
             "decoder": decoder,
+            "reference_gpu": reference_gpu,
         }
         print(json.dumps(line), flush=True)
     for executor in executors:
@@ -418,87 +463,236 @@ def main():
     return 0
 
 
-def decoder_throughput(args, device, rank, world, max_over_ranks, barrier) -> dict:
+def reference_gpu_leg(layers, device, golden, skip_decoder: bool) -> dict:
+    """The GPU comparator: the reference's own CUDA executor (CudaExecutor, its
+    cuda_executor.cu built for sm_100a with its flags into
+    oracle/_ref/libnvcr_ref_cuda.so) through its public run_half, on the same
+    device-resident FP16 inputs as this path, timed with CUDA events on its
+    stream after warm-up: the config-2 layers one by one and one config-3
+    frame. Its outputs are checked against the reference run_cpu's digests."""
+    import numpy as np
+    import torch
+
+    from nvcr_b200.program import SeededStream
+    from nvcr_b200.workloads import half_digest, intra_decoder, laplace_latent, layer_input
+    from oracle.oracle import ReferenceGpu
+
+    if not ReferenceGpu.available():
+        return {"unavailable": "oracle/_ref/libnvcr_ref_cuda.so is not built"}
+    stream = torch.cuda.Stream(device=device)
+
+    def time_runs(run, count):
+        for _ in range(2):
+            run()
+        torch.cuda.synchronize(device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(count):
+            run()
+        end.record(stream)
+        torch.cuda.synchronize(device)
+        return start.elapsed_time(end) / count
+
+    rows = []
+    total_ms = total_ops = 0.0
+    differing = []
+    with tempfile.TemporaryDirectory() as directory:
+        for layer in layers:
+            x = layer_input(layer, seed=input_seed(layer))
+            path = layer.program.write(directory, layer.name)
+            shape = tuple(golden.get("config2", {}).get(layer.name, {}).get("shape", ()))
+            with ReferenceGpu(path, stream.cuda_stream) as executor:
+                xh = torch.from_numpy(x.astype(np.float16)).to(device)
+                if not shape:
+                    continue
+                yh = torch.empty(shape, dtype=torch.float16, device=device)
+                ms = time_runs(lambda: executor.run_half({"x": xh}, {"y": yh}), 3)
+                if half_digest(yh.cpu().numpy()) != golden["config2"][layer.name]["digest"]:
+                    differing.append(layer.name)
+            rows.append({"layer": layer.name, "ms": round(ms, 4), "tops": round(layer.ops / (ms / 1000.0) / 1e12, 2)})
+            total_ms += ms
+            total_ops += layer.ops
+        result = {"what": "reference CudaExecutor::run_half (sm_80-style mma.sync int8 kernels) on this B200",
+                  "config2": {"tops": round(total_ops / (total_ms / 1000.0) / 1e12, 2) if total_ms else None,
+                              "ms_per_step": round(total_ms, 3), "layers": rows, "differing": differing}}
+        if not skip_decoder:
+            stack = intra_decoder()
+            path = stack.program.write(directory, "intra_1080p")
+            latent = torch.from_numpy(laplace_latent(SeededStream(5000), stack.input_shapes[0])
+                                      .astype(np.float16)).to(device)
+            frame = torch.empty((3, 1088, 1920), dtype=torch.float16, device=device)
+            with ReferenceGpu(path, stream.cuda_stream) as executor:
+                ms = time_runs(lambda: executor.run_half({"y_hat": latent}, {"frame": frame}), 3)
+                same = half_digest(frame.cpu().numpy()) == golden.get("config3", {}).get("0", {}).get("digest")
+            result["config3"] = {"ms_per_frame": round(ms, 3), "frames_per_s": round(1000.0 / ms, 2),
+                                 "tops": round(stack.ops / (ms / 1000.0) / 1e12, 2), "matches_reference_cpu": same}
+    return result
+
+
+def decoder_throughput(args, device, rank, world, group, golden) -> dict:
     """BASELINE configs 3 and 5 on the synthetic DCVC-RT intra decoder (1080p:
-    y_hat [256, 68, 120] -> frame [3, 1088, 1920], w8a8, FP16 boundary, device-resident
-    latents). Config 3: one stream's frame time. Config 5: 64 independent streams
-    x 16 GOP-1 frames, stream s on rank s mod world, aggregate frames/s over the
-    max-over-ranks device time (strong scaling: the 1024 frames are fixed)."""
+    y_hat [256, 68, 120] -> frame [3, 1088, 1920], FP16 boundary).
+
+    Config 3: one stream's frame time with the latent resident on the device,
+    at w8a8 (BASELINE) and at w16a16 (the reference width map's default for the
+    intra decoder). Config 5: 64 independent streams x 16 GOP-1 frames, stream
+    s on rank s mod world, aggregate frames/s over the max-over-ranks device
+    time (strong scaling: the 1024 frames are fixed); once with the latents
+    resident on the device, and once end to end: every frame's latent copied in
+    from pinned host memory and its frame copied back out inside the timing
+    (copies and decodes of different frames overlap on three streams). Parity:
+    every stream's frame, as the end-to-end run left it in host memory, against
+    the reference's digest; config 3's frame likewise."""
     import numpy as np
     import torch
 
     from nvcr_b200.executor import CudaExecutor
     from nvcr_b200.program import SeededStream
-    from nvcr_b200.workloads import intra_decoder, laplace_latent
-
     from nvcr_b200.replicas import streams_of
+    from nvcr_b200.workloads import half_digest, intra_decoder, laplace_latent
 
+    barrier = group.barrier
     stack = intra_decoder()
     streams, frames = 64, 16
     mine = streams_of(rank, world, streams)
     torch_stream = torch.cuda.Stream(device=device)
+    copy_in = torch.cuda.Stream(device=device)
+    copy_out = torch.cuda.Stream(device=device)
+    expected = golden.get("config3", {})
+
+    def timed(count, work, executors=()):
+        barrier()
+        torch.cuda.synchronize(device)
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(torch_stream)
+        copy_in.wait_event(start)
+        copy_out.wait_event(start)
+        for i in range(count):
+            work(i)
+        torch_stream.wait_stream(copy_in)
+        torch_stream.wait_stream(copy_out)
+        end.record(torch_stream)
+        torch.cuda.synchronize(device)
+        for e in executors:
+            e.synchronize()
+        barrier()
+        return start.elapsed_time(end)
+
     with CudaExecutor.from_program(stack.program, stream=torch_stream.cuda_stream) as executor:
-        latents = [torch.from_numpy(laplace_latent(SeededStream(5000 + s), stack.input_shapes[0])
-                                    .astype(np.float16)).to(device) for s in mine]
+        host_latents = [torch.from_numpy(laplace_latent(SeededStream(5000 + s), stack.input_shapes[0])
+                                         .astype(np.float16)).pin_memory() for s in mine]
+        latents = [h.to(device) for h in host_latents]
         (c, h, w), = executor.infer_output_extents(stack.input_shapes)
         frame = torch.empty((c, h, w), dtype=torch.float16, device=device)
 
-        def decode(latent):
-            executor.run_half({"y_hat": latent}, {"frame": frame})
-
-        def timed(count, work, executors=(executor,)):
-            barrier()
-            torch.cuda.synchronize(device)
-            start = torch.cuda.Event(enable_timing=True)
-            end = torch.cuda.Event(enable_timing=True)
-            start.record(torch_stream)
-            for i in range(count):
-                work(i)
-            end.record(torch_stream)
-            torch.cuda.synchronize(device)
-            for e in executors:
-                e.synchronize()
-            barrier()
-            return start.elapsed_time(end)
+        def decode(latent, out=frame):
+            executor.run_half({"y_hat": latent}, {"frame": out})
 
         for _ in range(3):
             decode(latents[0])
         executor.synchronize()
         single = 10
-        frame_ms = timed(single, lambda i: decode(latents[0])) / single
-        shard_ms = max_over_ranks(timed(len(mine) * frames, lambda i: decode(latents[i // frames])))
+        frame_ms = timed(single, lambda i: decode(latents[0]), (executor,)) / single
+        config3_ok = half_digest(frame.cpu().numpy()) == expected.get(str(mine[0]), {}).get("digest")
+        shard_ms = group.max(timed(len(mine) * frames, lambda i: decode(latents[i // frames]), (executor,)))
         launches = executor.launches
-    p_frames = p_frame_sequence(device, torch_stream, timed)
+
+        # End to end: two device latent/frame slots; frame i uses slot i % 2.
+        slots = 2
+        latent_slots = [torch.empty_like(latents[0]) for _ in range(slots)]
+        frame_slots = [torch.empty_like(frame) for _ in range(slots)]
+        host_frames = [torch.empty((c, h, w), dtype=torch.float16).pin_memory() for _ in mine]
+        in_done = [torch.cuda.Event() for _ in range(slots)]
+        run_done = [torch.cuda.Event() for _ in range(slots)]
+        out_done = [torch.cuda.Event() for _ in range(slots)]
+        for events in (run_done, out_done):
+            for event in events:
+                event.record(torch_stream)
+
+        def decode_e2e(i):
+            k = i % slots
+            s = i // frames
+            copy_in.wait_event(run_done[k])      # the decode that read this slot is done
+            with torch.cuda.stream(copy_in):
+                latent_slots[k].copy_(host_latents[s], non_blocking=True)
+            in_done[k].record(copy_in)
+            torch_stream.wait_event(in_done[k])
+            torch_stream.wait_event(out_done[k])  # the download from this slot is done
+            decode(latent_slots[k], frame_slots[k])
+            run_done[k].record(torch_stream)
+            copy_out.wait_event(run_done[k])
+            with torch.cuda.stream(copy_out):
+                host_frames[s].copy_(frame_slots[k], non_blocking=True)
+            out_done[k].record(copy_out)
+
+        for i in range(2 * slots):
+            decode_e2e(i)
+        e2e_ms = group.max(timed(len(mine) * frames, decode_e2e, (executor,)))
+        differing = [s for s, host in zip(mine, host_frames)
+                     if half_digest(host.numpy()) != expected.get(str(s), {}).get("digest")]
+        h2d = host_latents[0].numel() * 2
+        d2h = c * h * w * 2
+
+    # w16a16, the width the reference's width map gives the intra decoder.
+    stack16 = intra_decoder(bits=(16, 16))
+    with CudaExecutor.from_program(stack16.program, stream=torch_stream.cuda_stream) as executor16:
+        for _ in range(3):
+            executor16.run_half({"y_hat": latents[0]}, {"frame": frame})
+        executor16.synchronize()
+        frame16_ms = timed(single, lambda i: executor16.run_half({"y_hat": latents[0]}, {"frame": frame}),
+                           (executor16,)) / single
+
+    p_frames, p_parity = p_frame_sequence(device, torch_stream, timed, golden)
+    checked5 = sum(1 for s in mine if str(s) in expected)
+    parity = {
+        "config3": {"outputs_checked": int(group.sum(1 if str(mine[0]) in expected else 0)),
+                    "differing": int(group.sum(0 if config3_ok else 1))},
+        "config4": p_parity,
+        "config5": {"outputs_checked": int(group.sum(checked5)), "differing": int(group.sum(len(differing))),
+                    "differing_here": differing, "what": "each stream's frame as the end-to-end run left it "
+                                                         "in host memory"},
+    }
     return {
         "workload": "synthetic DCVC-RT intra decoder (i.dec topology: subpel up + 14 DepthConvBlocks at "
-                    "256 ch, 1/8 res + d2s(8) head), 1088x1920 frame, w8a8, FP16 boundary",
+                    "256 ch, 1/8 res + d2s(8) head), 1088x1920 frame, FP16 boundary",
         "ops_per_frame": stack.ops,
         "config3": {"ms_per_frame": round(frame_ms, 3), "frames_per_s": round(1000.0 / frame_ms, 1),
-                    "tops": round(stack.ops / (frame_ms / 1000.0) / 1e12, 1), "gpu_launches_per_frame": launches},
+                    "tops": round(stack.ops / (frame_ms / 1000.0) / 1e12, 1), "gpu_launches_per_frame": launches,
+                    "widths": "w8a8"},
+        "config3_w16a16": {"ms_per_frame": round(frame16_ms, 3), "frames_per_s": round(1000.0 / frame16_ms, 1),
+                           "tops": round(stack.ops / (frame16_ms / 1000.0) / 1e12, 1),
+                           "widths": "w16a16 (the reference width map's default)"},
         "config4": p_frames,
         "config5": {"streams": streams, "frames_per_stream": frames, "n_gpus": world, "ms": round(shard_ms, 2),
                     "frames_per_s": round(streams * frames / (shard_ms / 1000.0), 1),
                     "tops_per_gpu": round(streams * frames * stack.ops / world / (shard_ms / 1000.0) / 1e12, 1),
-                    "scaling": "strong (1024 frames split round-robin by stream)"},
+                    "scaling": "strong (1024 frames split round-robin by stream)",
+                    "e2e": {"ms": round(e2e_ms, 2), "frames_per_s": round(streams * frames / (e2e_ms / 1000.0), 1),
+                            "h2d_bytes_per_frame": h2d, "d2h_bytes_per_frame": d2h}},
+        "parity": parity,
     }
 
 
-def p_frame_sequence(device, torch_stream, timed) -> dict:
+def p_frame_sequence(device, torch_stream, timed, golden) -> tuple[dict, dict]:
     """BASELINE config 4 on the synthetic stacks: 1280x720 (padded to 768x1280), GOP
     30 = one I-frame (intra decoder with a 64-channel feature output) and 29
     P-frames whose temporal context is the previous frame's feature, run in order
     on one GPU with one executor per mode (plans and scratch reused); FP16 stage
-    boundary, everything device-resident."""
+    boundary, everything device-resident. After the timing the sequence runs
+    once more and every frame and feature is checked against the reference's
+    digests."""
     import numpy as np
     import torch
 
     from nvcr_b200.executor import CudaExecutor
     from nvcr_b200.program import SeededStream
-    from nvcr_b200.workloads import inter_decoder, intra_decoder, laplace_latent
+    from nvcr_b200.workloads import half_digest, inter_decoder, intra_decoder, laplace_latent
 
     intra = intra_decoder((48, 80), feature_channels=64)
     inter = inter_decoder((48, 80))
     gop = 30
+    expected = golden.get("config4", [])
     with CudaExecutor.from_program(intra.program, stream=torch_stream.cuda_stream) as first, \
             CudaExecutor.from_program(inter.program, stream=torch_stream.cuda_stream) as rest:
         latents = [torch.from_numpy(laplace_latent(SeededStream(6000 + f), (256, 48, 80)).astype(np.float16))
@@ -516,9 +710,20 @@ def p_frame_sequence(device, torch_stream, timed) -> dict:
         for f in range(3):
             decode(f)
         ms = timed(gop, decode, (first, rest))
+        differing = []
+        for f in range(gop if len(expected) == gop else 0):
+            decode(f)
+            torch.cuda.synchronize(device)
+            if half_digest(frame.cpu().numpy()) != expected[f]["frame"]:
+                differing.append(f"frame {f}")
+            if half_digest(features[f % 2].cpu().numpy()) != expected[f]["feature"]:
+                differing.append(f"feature {f}")
     ops = intra.ops + (gop - 1) * inter.ops
-    return {"frames": gop, "resolution": "768x1280 (720p padded to x64)", "ms": round(ms, 3),
-            "frames_per_s": round(gop / (ms / 1000.0), 1), "tops": round(ops / (ms / 1000.0) / 1e12, 1)}
+    result = {"frames": gop, "resolution": "768x1280 (720p padded to x64)", "ms": round(ms, 3),
+              "frames_per_s": round(gop / (ms / 1000.0), 1), "tops": round(ops / (ms / 1000.0) / 1e12, 1)}
+    parity = {"outputs_checked": 2 * gop if len(expected) == gop else 0, "differing": len(differing),
+              "differing_here": differing, "what": "every frame and feature of the GOP (rank 0's run)"}
+    return result, parity
 
 
 if __name__ == "__main__":

@@ -211,7 +211,9 @@ int nvcr_sm100_numerics_identity_parse(const unsigned char* payload, size_t size
  * in one file-scope static device array of NVCR_SM100_STATIC_WORKSPACE_BYTES,
  * which each GPU that loads the library keeps until exit. The first call on a
  * device looks the array's address up (cudaGetSymbolAddress): make it before
- * any stream capture. All calls share the array: calls whose work overlaps on
+ * any stream capture. The executor's device (current at create) must be
+ * current: otherwise NVCR_SM100_INVALID_STATE, with nothing enqueued. All
+ * calls share the array: calls whose work overlaps on
  * the GPU race and must be ordered by the caller. A run needing more than the
  * array holds fails with NVCR_SM100_INVALID_ARGUMENT before enqueuing work.
  * Inputs, outputs and their meaning are those of nvcr_sm100_run_half. */

@@ -205,6 +205,7 @@ Result<std::unique_ptr<Executor>> Executor::create(Program program, cudaStream_t
     if (status == cudaSuccess) status = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
     if (status == cudaSuccess) status = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
     if (status != cudaSuccess) return cuda_error("cudaDeviceGetAttribute", status);
+    executor->device_ = device;
     if (major != 10 || minor != 0) {
         return fail(Code::incompatible_target,
                     std::string(intconv_profile) + " on this provider needs an sm_100 (B200-class) GPU");
@@ -1188,7 +1189,9 @@ Status Executor::execute(const std::vector<TensorView>& inputs, const std::vecto
         }
         return Ok{};
     };
-    if (boundary != Boundary::host && !profiling_) {
+    // Runs in a caller's workspace are never captured: instantiating a graph
+    // may allocate device memory, which those callers cannot allow.
+    if (boundary != Boundary::host && !profiling_ && workspace == nullptr) {
         GraphKey key{&plan, run_base_, static_cast<int>(boundary), {}};
         for (const auto* view : input_views) key.tensors.push_back(view->data);
         for (const auto* view : output_views) key.tensors.push_back(view->data);

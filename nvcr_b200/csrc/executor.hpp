@@ -53,6 +53,9 @@ public:
 
     const Program& program() const { return program_; }
     cudaStream_t stream() const { return stream_; }
+    // The device that was current at create: the stream, weights and tensor
+    // maps belong to it.
+    int device() const { return device_; }
 
     Status run_half(const std::vector<TensorView>& inputs, const std::vector<TensorView>& outputs);
     Status run_float(const std::vector<TensorView>& inputs, const std::vector<TensorView>& outputs);
@@ -111,6 +114,7 @@ private:
     Status mark(const std::string& label, const std::string& kernel, double ops, double bytes);
 
     Program program_;
+    int device_{0};
     cudaStream_t stream_{nullptr};
     bool owns_stream_{false};
     float* weights_{nullptr};

@@ -14,7 +14,10 @@
 // NVCR_SM100_STATIC_WORKSPACE_BYTES (64 MiB). Every GPU that loads this code
 // holds it until the process exits. Its address is looked up once per device
 // with cudaGetSymbolAddress, with that device current, by the first call made
-// on the device: make that first call before any stream capture begins. All
+// on the device: make that first call before any stream capture begins. The
+// executor's own device (the one current when it was created) must be current
+// for every call; with another device current the call is refused with
+// NVCR_SM100_INVALID_STATE and nothing is enqueued. All
 // calls on a device share the one array and it keeps the previous call's
 // contents; every byte a run reads is written earlier in the same run, so
 // nothing needs clearing, but two calls whose work overlaps on the GPU (other
@@ -41,11 +44,20 @@ int static_report(nvcr_sm100::Code code, const std::string& message) {
     return nvcr_sm100::report_error(nvcr_sm100::Error{code, message});
 }
 
-// The device address of static_workspace on the current device, looked up once.
-int workspace_for_current_device(void** address) {
+// The device address of static_workspace on the executor's device, looked up
+// once. That device must be the current one: cudaGetSymbolAddress answers for
+// the current device, and the executor's stream, weights and tensor maps live
+// on its own device, so a call made with another device current is refused
+// before anything is enqueued.
+int workspace_for_device(int executor_device, void** address) {
     int device = 0;
     cudaError_t status = cudaGetDevice(&device);
     if (status != cudaSuccess) return static_report(nvcr_sm100::Code::backend_error, cudaGetErrorString(status));
+    if (device != executor_device) {
+        return static_report(nvcr_sm100::Code::invalid_state,
+                             "the current device (" + std::to_string(device) + ") is not the executor's device (" +
+                                 std::to_string(executor_device) + "); make it current before the call");
+    }
     if (device < 0 || device >= max_devices) {
         return static_report(nvcr_sm100::Code::invalid_state, "device index outside the static workspace table");
     }
@@ -72,7 +84,7 @@ extern "C" int nvcr_sm100_run_half_static(nvcr_sm100_executor* executor, const n
             return static_report(nvcr_sm100::Code::invalid_argument, "null executor or tensor array");
         }
         void* workspace = nullptr;
-        const int found = workspace_for_current_device(&workspace);
+        const int found = workspace_for_device(executor->executor->device(), &workspace);
         if (found != NVCR_SM100_OK) return found;
         std::vector<nvcr_sm100::TensorView> in, out;
         for (size_t i = 0; i < input_count; ++i) {

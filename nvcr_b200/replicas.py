@@ -3,8 +3,9 @@
 
 The path does not shard within a stage. Independent streams do: stream s runs
 on rank s mod world (round-robin), each rank with its own executor and
-weights. The only cross-rank traffic is a barrier around timed regions and
-one max-reduction of the elapsed time, so the slowest rank sets the number.
+weights. The only cross-rank traffic is a barrier around timed regions, one
+max-reduction of the elapsed time, so the slowest rank sets the number, and a
+sum of the outputs each rank found differing from the reference's digests.
 """
 from __future__ import annotations
 
@@ -62,6 +63,15 @@ class Group:
 
         t = torch.tensor([value], dtype=torch.float64, device=self.device if self.device is not None else "cpu")
         self._dist.all_reduce(t, op=self._dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, value: float) -> float:
+        if self._dist is None:
+            return value
+        import torch
+
+        t = torch.tensor([value], dtype=torch.float64, device=self.device if self.device is not None else "cpu")
+        self._dist.all_reduce(t, op=self._dist.ReduceOp.SUM)
         return float(t.item())
 
     def close(self) -> None:

@@ -237,3 +237,18 @@ def laplace_latent(stream: SeededStream, shape: tuple[int, int, int], scale: flo
     u = np.clip(u, -0.5 + 1e-12, 0.5 - 1e-12)
     x = -scale * np.sign(u) * np.log1p(-2.0 * np.abs(u))
     return np.clip(np.rint(x), -127, 127).astype(np.float32).reshape(shape)
+
+
+def half_digest(values) -> str:
+    """SHA-256 of an FP16 tensor's bytes (C order) with every NaN stored as
+    0x7e00, so digests compare under the profile's rule that any NaN equals any
+    NaN. Accepts FP16 arrays, or FP32 arrays, which are first rounded to FP16
+    (round to nearest even, as at a stage boundary)."""
+    import hashlib
+
+    array = np.ascontiguousarray(values)
+    if array.dtype != np.float16:
+        array = array.astype(np.float32).astype(np.float16)
+    bits = array.view(np.uint16).copy()
+    bits[((bits & 0x7C00) == 0x7C00) & ((bits & 0x03FF) != 0)] = 0x7E00
+    return hashlib.sha256(bits.tobytes()).hexdigest()

@@ -1,7 +1,9 @@
-"""ctypes access to the two CPU checkers. TEST INFRASTRUCTURE ONLY.
+"""ctypes access to the CPU checkers and the reference's GPU comparator. TEST
+AND BENCHMARK INFRASTRUCTURE ONLY.
 
-Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline leg import
-this module, and only to check or time; the product never does.
+Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline, reference and
+reference-GPU legs import this module, and only to check or time; the product
+never does.
 
 * ``Oracle``: this repo's C restatement (intconv_oracle.c), built into
   oracle/_build/liboracle.so. It is pinned against the reference below and
@@ -9,6 +11,9 @@ this module, and only to check or time; the product never does.
 * ``Reference``: the reference's own CPU executor (run_cpu,
   src/deterministic/program.cpp:702-820) compiled from its sources into
   oracle/_ref/libnvcr_ref.so, reached through its own program loader.
+* ``ReferenceGpu``: the reference's own CUDA executor (CudaExecutor,
+  src/deterministic/cuda_executor.cu) built for sm_100a into
+  oracle/_ref/libnvcr_ref_cuda.so, the GPU comparator.
 """
 from __future__ import annotations
 
@@ -23,14 +28,16 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 ORACLE_LIB = HERE / "_build" / "liboracle.so"
 REFERENCE_LIB = HERE / "_ref" / "libnvcr_ref.so"
-REFERENCE_SOURCES = Path(os.environ.get("NVCR_REFERENCE", "/root/reference"))
+# The reference checkout: $NVCR_REFERENCE when set, else a directory named
+# `reference` beside this repository.
+REFERENCE_SOURCES = Path(os.environ.get("NVCR_REFERENCE", HERE.parent.parent / "reference"))
 
 
 def build(reference: bool = True) -> None:
     """Builds the C restatement, and the reference shim when its sources exist."""
     targets = ["oracle"]
     if reference and (REFERENCE_SOURCES / "src" / "deterministic" / "program.cpp").exists():
-        targets.append("ref")
+        targets += ["ref", "refgpu"]
     subprocess.run(["make", "-s", "-C", str(HERE), f"REF={REFERENCE_SOURCES}", *targets], check=True)
 
 
@@ -318,3 +325,70 @@ def canonical_digest(array: np.ndarray) -> str:
     bits = a.view(np.uint32)
     bits[np.isnan(a)] = 0x7FC00000
     return hashlib.sha256(bits.tobytes()).hexdigest()
+
+
+REFERENCE_GPU_LIB = HERE / "_ref" / "libnvcr_ref_cuda.so"
+
+
+class ReferenceGpu:
+    """The reference's own CUDA executor (CudaExecutor, src/deterministic/
+    cuda_executor.cu) built for sm_100a with its kernel flags into
+    oracle/_ref/libnvcr_ref_cuda.so: the GPU comparator, timed beside the new
+    path in the benchmark. One executor per program, on a given CUDA stream."""
+
+    _lib = None
+
+    @classmethod
+    def available(cls) -> bool:
+        return REFERENCE_GPU_LIB.exists()
+
+    @classmethod
+    def library(cls):
+        if cls._lib is None:
+            lib = ctypes.CDLL(str(REFERENCE_GPU_LIB))
+            vp, cp = ctypes.c_void_p, ctypes.c_char_p
+            i32p = ctypes.POINTER(ctypes.c_int32)
+            lib.refgpu_create.restype = ctypes.c_int
+            lib.refgpu_create.argtypes = [cp, vp, ctypes.POINTER(vp), cp, ctypes.c_size_t]
+            lib.refgpu_run_half.restype = ctypes.c_int
+            lib.refgpu_run_half.argtypes = [vp, ctypes.c_int, ctypes.POINTER(cp), i32p, ctypes.POINTER(vp),
+                                            ctypes.c_int, ctypes.POINTER(cp), i32p, ctypes.POINTER(vp), cp,
+                                            ctypes.c_size_t]
+            lib.refgpu_destroy.argtypes = [vp]
+            cls._lib = lib
+        return cls._lib
+
+    def __init__(self, program_json, stream: int | None = None) -> None:
+        lib = self.library()
+        handle = ctypes.c_void_p()
+        error = ctypes.create_string_buffer(512)
+        status = lib.refgpu_create(str(program_json).encode(), stream, ctypes.byref(handle), error, 512)
+        if status != 0:
+            raise RuntimeError(f"reference CudaExecutor::create: {error.value.decode()} (code {status - 1})")
+        self._handle = handle
+
+    @staticmethod
+    def _pack(named):
+        names = list(named)
+        name_array = (ctypes.c_char_p * max(1, len(names)))(*[n.encode() for n in names])
+        extents = _i32([d for n in names for d in tuple(named[n].shape)])
+        data = (ctypes.c_void_p * max(1, len(names)))(*[named[n].data_ptr() for n in names])
+        return len(names), name_array, extents, data
+
+    def run_half(self, inputs, outputs) -> None:
+        """CudaExecutor::run_half on dicts name -> contiguous FP16 CUDA tensor (c, h, w)."""
+        error = ctypes.create_string_buffer(512)
+        status = self.library().refgpu_run_half(self._handle, *self._pack(inputs), *self._pack(outputs), error, 512)
+        if status != 0:
+            raise RuntimeError(f"reference CudaExecutor::run_half: {error.value.decode()} (code {status - 1})")
+
+    def close(self) -> None:
+        if self._handle:
+            self.library().refgpu_destroy(self._handle)
+            self._handle = ctypes.c_void_p()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()

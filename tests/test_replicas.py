@@ -33,9 +33,10 @@ def _rank(rank: int, world: int, port: int, results) -> None:
     mine = streams_of(env.rank, env.world, 64)
     group.barrier()
     slowest = group.max(float(10 + env.rank))
+    differing = group.sum(float(env.rank + 1))
     group.barrier()
     group.close()
-    results.put((env.rank, mine, slowest))
+    results.put((env.rank, mine, slowest, differing))
 
 
 def test_streams_split_round_robin():
@@ -66,6 +67,7 @@ def test_two_gloo_ranks_agree():
     assert [g[0] for g in got] == [0, 1]
     assert got[0][1] == list(range(0, 64, 2)) and got[1][1] == list(range(1, 64, 2))
     assert got[0][2] == got[1][2] == 11.0  # the max over ranks
+    assert got[0][3] == got[1][3] == 3.0   # the sum over ranks
 
 
 def _lonely(port: int, results) -> None:

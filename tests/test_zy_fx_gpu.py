@@ -15,11 +15,7 @@ from tests.fx_programs import decoder_like, decoder_like_inputs, write_program
 from tests.test_fx_oracle import (gemm_1x1, one_op_program, pixel, random_single_op,
                                   reference_program_test_program)
 
-# Skipped until these tests have run on a B200: the fx device path compiles for
-# sm_100a, and its code compiled for the host passes these same cases on CPU
-# (tests/test_fx_host.py), but no GPU time was left to run the kernels when it
-# was written.
-pytestmark = [pytest.mark.gpu, pytest.mark.skip(reason="nvcr.fx.v1 device path not yet run on a B200")]
+pytestmark = pytest.mark.gpu
 
 
 def device_run(tmp_path, program: dict, inputs, stage: str = "g", device_memory: bool = False):

@@ -9,11 +9,7 @@ import ctypes
 import numpy as np
 import pytest
 
-# Skipped until these tests have run on a B200: the glue kernels compile for
-# sm_100a and their element functions pass on CPU against the reference
-# (tests/test_glue_host.py), but no GPU time was left to run them when they
-# were written.
-pytestmark = [pytest.mark.gpu, pytest.mark.skip(reason="DCVC glue kernels not yet run on a B200")]
+pytestmark = pytest.mark.gpu
 
 
 def ptr(tensor):

@@ -6,9 +6,12 @@ thread that must not block on the driver's allocator. They create the executor
 at set-up and then run through nvcr_sm100_run_half_static, which keeps every
 scratch tensor in the library's fixed static device array. This file checks,
 through the C ABI, that two calls in a row give the same bits as the ordinary
-nvcr_sm100_run_half (the suite's tolerance: bit-exact, any NaN equals any NaN)
-and that a run too large for the array is refused. It is named to be collected
-last and passes alone in a fresh process or after the other tests.
+nvcr_sm100_run_half (the suite's tolerance: bit-exact, any NaN equals any NaN),
+that an executor which only ever runs this way gets no workspace of its own and
+leaves the device's free memory unchanged, that a run too large for the array
+is refused, and that a call made with another device current is refused. It is
+named to be collected last and passes alone in a fresh process or after the
+other tests.
 """
 from __future__ import annotations
 
@@ -72,3 +75,54 @@ def test_static_run_refuses_a_plan_larger_than_the_array(cuda):
             executor.run_half_static({"x": x}, {"y": y})
         assert error.value.code == ErrorCode.invalid_argument
         assert "bytes of workspace" in error.value.message
+
+
+def test_static_only_executor_allocates_nothing(cuda):
+    """An executor that never calls run_half: after two static calls it has no
+    workspace of its own, and the second call leaves the free device memory as
+    it found it; both calls give run_half's bits (from a second executor)."""
+    import torch
+
+    layer = config1()
+    x = layer_input(layer, seed=1)
+    with CudaExecutor.from_program(layer.program) as reference, CudaExecutor.from_program(layer.program) as executor:
+        (c, h, w), = executor.infer_output_extents([x.shape])
+        ins = _half_tensors(torch, {"x": x}, cuda)
+        expected = torch.empty((c, h, w), dtype=torch.float16, device=cuda)
+        reference.run_half(ins, {"y": expected})
+        reference.synchronize()
+        outputs = [torch.full((c, h, w), float("nan"), dtype=torch.float16, device=cuda) for _ in range(2)]
+        torch.cuda.synchronize()
+        executor.run_half_static(ins, {"y": outputs[0]})
+        executor.synchronize()
+        free_before, _ = torch.cuda.mem_get_info(cuda)
+        executor.run_half_static(ins, {"y": outputs[1]})
+        executor.synchronize()
+        free_after, _ = torch.cuda.mem_get_info(cuda)
+        assert executor.workspace_bytes == 0
+        assert free_after == free_before
+        for call, got in enumerate(outputs):
+            bad = count_differing(got.float().cpu().numpy(), expected.float().cpu().numpy())
+            assert bad == 0, f"static call {call + 1}: {bad} elements differ from run_half"
+
+
+def test_static_run_refuses_another_current_device(cuda):
+    """The array is looked up for the current device, and the executor's work
+    belongs to its own: with another device current the call is refused and
+    nothing runs."""
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    layer = config1()
+    x = layer_input(layer, seed=1)
+    with CudaExecutor.from_program(layer.program) as executor:
+        (c, h, w), = executor.infer_output_extents([x.shape])
+        ins = _half_tensors(torch, {"x": x}, cuda)
+        y = torch.zeros((c, h, w), dtype=torch.float16, device=cuda)
+        torch.cuda.synchronize()
+        with torch.cuda.device(1):
+            with pytest.raises(ExecutorError) as error:
+                executor.run_half_static(ins, {"y": y})
+        assert error.value.code == ErrorCode.invalid_state
+        assert float(y.abs().max()) == 0.0
