@@ -8,264 +8,320 @@
 #include <cstring>
 #include <fstream>
 #include <iterator>
-#include <map>
+#include <optional>
 #include <sstream>
+#include <unordered_map>
 
 namespace nvcr_sm100 {
 namespace {
 
 Error invalid(const std::string& message) { return fail(Code::invalid_argument, message); }
 
-Result<std::int64_t> get_int(const json::Value& object, std::string_view key) {
-    const auto* v = object.get(key);
-    if (v == nullptr || v->kind != json::Value::Kind::number || !v->integer) {
-        return invalid("program field '" + std::string(key) + "' must be an integer");
-    }
-    return *v->integer;
-}
+// ------------------------------------------------------------ node schema
+//
+// A node is read in two passes. First every key its op's schema lists is
+// fetched from the JSON object into a Fields record, checking only the JSON
+// shape of each (an integer, a fixed-length integer array, a boolean, a number
+// that is exactly a float32). Then the op's rule turns the record into the
+// Node, refusing values the profile does not allow, and names the output's
+// channel count. The node's inputs and output are resolved around the two
+// passes against the tensors defined so far.
 
-Result<std::string> get_text(const json::Value& object, std::string_view key) {
-    const auto* v = object.get(key);
-    if (v == nullptr || v->kind != json::Value::Kind::string) {
-        return invalid("program field '" + std::string(key) + "' must be a string");
-    }
-    return v->text;
-}
+enum class Shape : std::uint8_t { integer, pair, quad, flag, exact_float, number };
 
-template <std::size_t N>
-Result<std::array<std::int32_t, N>> get_ints(const json::Value& object, std::string_view key) {
-    const auto* v = object.get(key);
-    if (v == nullptr || v->kind != json::Value::Kind::array || v->items.size() != N) {
-        return invalid("program field '" + std::string(key) + "' has the wrong length");
-    }
-    std::array<std::int32_t, N> out{};
-    for (std::size_t i = 0; i < N; ++i) {
-        if (v->items[i].kind != json::Value::Kind::number || !v->items[i].integer) {
-            return invalid("program field '" + std::string(key) + "' must hold integers");
-        }
-        out[i] = static_cast<std::int32_t>(*v->items[i].integer);
-    }
-    return out;
-}
-
-// A float32 field whose JSON number must be exactly representable.
-Result<float> get_exact_float(const json::Value& object, std::string_view key, std::string_view what) {
-    const auto* v = object.get(key);
-    if (v == nullptr || v->kind != json::Value::Kind::number) {
-        return invalid(std::string(what) + " needs a numeric '" + std::string(key) + "'");
-    }
-    const auto f = static_cast<float>(v->number);
-    if (static_cast<double>(f) != v->number) {
-        return invalid(std::string(what) + " value is not exactly representable in float32");
-    }
-    return f;
-}
-
-Result<Op> op_from_name(std::string_view name) {
-    static const std::pair<std::string_view, Op> table[] = {
-        {"conv", Op::conv}, {"mul", Op::mul}, {"add", Op::add}, {"mul_scalar", Op::mul_scalar},
-        {"sigmoid", Op::sigmoid}, {"slice_channels", Op::slice_channels},
-        {"depth_to_space", Op::depth_to_space}, {"scale_channels", Op::scale_channels},
-        {"clamp", Op::clamp}, {"concat", Op::concat}, {"crop", Op::crop},
-        {"space_to_depth", Op::space_to_depth}, {"im2col", Op::im2col}};
-    for (const auto& [text, op] : table) {
-        if (text == name) return op;
-    }
-    return invalid("unsupported deterministic op '" + std::string(name) + "'");
-}
-
-class Tensors {
-public:
-    explicit Tensors(Program& program) : program_(program) {}
-    std::size_t define(const std::string& name, std::int32_t channels) {
-        const auto id = program_.tensor_names.size();
-        program_.tensor_names.push_back(name);
-        program_.tensor_channels.push_back(channels);
-        ids_.emplace(name, id);
-        return id;
-    }
-    Result<std::size_t> find(const std::string& name) const {
-        auto it = ids_.find(name);
-        if (it == ids_.end()) return invalid("program reads undefined tensor '" + name + "'");
-        return it->second;
-    }
-    bool contains(const std::string& name) const { return ids_.count(name) != 0; }
-    std::int32_t channels(std::size_t id) const { return program_.tensor_channels[id]; }
-
-private:
-    Program& program_;
-    std::map<std::string, std::size_t, std::less<>> ids_;
+enum Key : std::uint8_t {
+    k_in_channels, k_out_channels, k_kernel, k_stride, k_pads, k_weight_offset, k_bias_offset, k_depthwise,
+    k_value, k_begin, k_end, k_block, k_min, k_max, k_axis, key_count
 };
 
-bool binary_op(Op op) {
-    return op == Op::mul || op == Op::add || op == Op::scale_channels || op == Op::concat || op == Op::crop;
+constexpr struct {
+    std::string_view json;
+    Shape shape;
+} keys[key_count] = {
+    {"in_channels", Shape::integer}, {"out_channels", Shape::integer}, {"kernel", Shape::pair},
+    {"stride", Shape::pair},         {"pads", Shape::quad},            {"weight_offset", Shape::integer},
+    {"bias_offset", Shape::integer}, {"depthwise", Shape::flag},       {"value", Shape::exact_float},
+    {"begin", Shape::integer},       {"end", Shape::integer},          {"block", Shape::integer},
+    {"min", Shape::number},          {"max", Shape::number},           {"axis", Shape::integer},
+};
+
+// The values of one node's keys, by Key.
+struct Fields {
+    std::int64_t integer[key_count]{};
+    std::array<std::int32_t, 4> list[key_count]{};
+    bool flag[key_count]{};
+    double number[key_count]{};
+};
+
+std::string quoted(Key key) { return "'" + std::string(keys[key].json) + "'"; }
+
+// Fetches `key` from a node object into `fields`, checking its JSON shape.
+std::optional<Error> fetch(const json::Value& object, Key key, std::string_view op, Fields& fields) {
+    const json::Value* v = object.get(keys[key].json);
+    const auto is_integer = [](const json::Value* x) {
+        return x != nullptr && x->kind == json::Value::Kind::number && x->integer.has_value();
+    };
+    switch (keys[key].shape) {
+    case Shape::integer:
+        if (!is_integer(v)) return invalid(std::string(op) + " field " + quoted(key) + " is not an integer");
+        fields.integer[key] = *v->integer;
+        return std::nullopt;
+    case Shape::pair:
+    case Shape::quad: {
+        const std::size_t length = keys[key].shape == Shape::pair ? 2 : 4;
+        if (v == nullptr || v->kind != json::Value::Kind::array || v->items.size() != length) {
+            return invalid(std::string(op) + " field " + quoted(key) + " is not a list of " +
+                           std::to_string(length) + " values");
+        }
+        for (std::size_t i = 0; i < length; ++i) {
+            if (!is_integer(&v->items[i])) {
+                return invalid(std::string(op) + " field " + quoted(key) + " holds a non-integer");
+            }
+            fields.list[key][i] = static_cast<std::int32_t>(*v->items[i].integer);
+        }
+        return std::nullopt;
+    }
+    case Shape::flag:
+        if (v == nullptr || v->kind != json::Value::Kind::boolean) {
+            return invalid(std::string(op) + " field " + quoted(key) + " is not a boolean");
+        }
+        fields.flag[key] = v->boolean;
+        return std::nullopt;
+    case Shape::exact_float:
+    case Shape::number:
+        if (v == nullptr || v->kind != json::Value::Kind::number) {
+            return invalid(std::string(op) + " field " + quoted(key) + " is not a number");
+        }
+        if (keys[key].shape == Shape::exact_float && static_cast<double>(static_cast<float>(v->number)) != v->number) {
+            return invalid(std::string(op) + " field " + quoted(key) + " is not exactly a float32");
+        }
+        fields.number[key] = v->number;
+        return std::nullopt;
+    }
+    return invalid("unknown field shape");
 }
 
-Result<Node> parse_node(const json::Value& value, Tensors& tensors, std::size_t weight_count) {
-    auto op_name = get_text(value, "op");
-    if (!op_name) return op_name.error();
-    auto op = op_from_name(op_name.value());
-    if (!op) return op.error();
-    Node node;
-    node.op = op.value();
-    if (binary_op(node.op)) {
-        const auto* inputs = value.get("inputs");
-        if (inputs == nullptr || inputs->items.size() != 2) return invalid("binary op needs two inputs");
-        for (std::size_t i = 0; i < 2; ++i) {
-            auto id = tensors.find(inputs->items[i].text);
+// Reading context of the op rules: the channels of the node's first input and
+// second input (0 when unary), and the weights the file holds.
+struct Context {
+    std::int32_t first_channels;
+    std::int32_t second_channels;
+    std::size_t weight_count;
+};
+
+// An op rule fills the node's op-specific members from the fetched fields and
+// returns the output's channel count, or refuses the node.
+using Rule = Result<std::int32_t> (*)(const Fields&, const Context&, Node&);
+
+bool any_negative(const std::array<std::int32_t, 4>& values) {
+    return values[0] < 0 || values[1] < 0 || values[2] < 0 || values[3] < 0;
+}
+
+Result<std::int32_t> conv_rule(const Fields& f, const Context& context, Node& node) {
+    const std::int64_t weight_offset = f.integer[k_weight_offset];
+    const std::int64_t bias_offset = f.integer[k_bias_offset];
+    node.in_channels = static_cast<std::int32_t>(f.integer[k_in_channels]);
+    node.out_channels = static_cast<std::int32_t>(f.integer[k_out_channels]);
+    node.depthwise = f.flag[k_depthwise];
+    node.kernel = {f.list[k_kernel][0], f.list[k_kernel][1]};
+    node.stride = {f.list[k_stride][0], f.list[k_stride][1]};
+    node.pads = f.list[k_pads];
+    const bool positive = node.in_channels > 0 && node.out_channels > 0 && node.kernel[0] > 0 && node.kernel[1] > 0 &&
+        node.stride[0] > 0 && node.stride[1] > 0;
+    if (!positive || any_negative(node.pads) || weight_offset < 0 || bias_offset < 0 ||
+        (node.depthwise && node.in_channels != node.out_channels)) {
+        return invalid("conv geometry or offsets out of range");
+    }
+    node.weight_offset = static_cast<std::size_t>(weight_offset);
+    node.bias_offset = static_cast<std::size_t>(bias_offset);
+    // [out][in or 1][kh][kw] weights from weight_offset, out_channels biases from bias_offset.
+    const std::size_t fan_in = static_cast<std::size_t>(node.depthwise ? 1 : node.in_channels) *
+        static_cast<std::size_t>(node.kernel[0]) * static_cast<std::size_t>(node.kernel[1]);
+    const std::size_t total = context.weight_count;
+    const auto fits = [total](std::size_t at, std::size_t count) { return at <= total && count <= total - at; };
+    if (!fits(node.weight_offset, static_cast<std::size_t>(node.out_channels) * fan_in) ||
+        !fits(node.bias_offset, static_cast<std::size_t>(node.out_channels))) {
+        return invalid("conv reads past the end of the weights file");
+    }
+    return node.out_channels;
+}
+
+Result<std::int32_t> scalar_rule(const Fields& f, const Context& context, Node& node) {
+    node.scalar = static_cast<float>(f.number[k_value]);
+    return context.first_channels;
+}
+
+Result<std::int32_t> slice_rule(const Fields& f, const Context&, Node& node) {
+    node.begin = static_cast<std::int32_t>(f.integer[k_begin]);
+    node.end = static_cast<std::int32_t>(f.integer[k_end]);
+    return node.end - node.begin;
+}
+
+Result<std::int32_t> block_rule(const Fields& f, const Context& context, Node& node) {
+    node.block = static_cast<std::int32_t>(f.integer[k_block]);
+    if (node.block < 1 || node.block > 64) return invalid("block must lie in 1..64");
+    const std::int32_t area = node.block * node.block;
+    return node.op == Op::space_to_depth ? context.first_channels * area : context.first_channels / area;
+}
+
+Result<std::int32_t> clamp_rule(const Fields& f, const Context& context, Node& node) {
+    node.minimum = static_cast<float>(f.number[k_min]);
+    node.maximum = static_cast<float>(f.number[k_max]);
+    const bool exact = static_cast<double>(node.minimum) == f.number[k_min] &&
+        static_cast<double>(node.maximum) == f.number[k_max];
+    if (!exact || !(node.minimum <= node.maximum)) return invalid("clamp needs ordered, exactly float32 bounds");
+    return context.first_channels;
+}
+
+Result<std::int32_t> im2col_rule(const Fields& f, const Context& context, Node& node) {
+    node.kernel = {f.list[k_kernel][0], f.list[k_kernel][1]};
+    node.stride = {f.list[k_stride][0], f.list[k_stride][1]};
+    node.pads = f.list[k_pads];
+    const std::int32_t taps = node.kernel[0] * node.kernel[1];
+    if (node.kernel[0] < 1 || node.kernel[1] < 1 || taps > 64 || node.stride[0] < 1 || node.stride[1] < 1 ||
+        any_negative(node.pads)) {
+        return invalid("im2col geometry out of range");
+    }
+    return context.first_channels * taps;
+}
+
+Result<std::int32_t> crop_rule(const Fields& f, const Context& context, Node& node) {
+    if (f.integer[k_axis] != 2 && f.integer[k_axis] != 3) return invalid("crop axis is neither 2 nor 3");
+    node.axis = static_cast<std::int32_t>(f.integer[k_axis]);
+    return context.first_channels;
+}
+
+Result<std::int32_t> concat_rule(const Fields&, const Context& context, Node&) {
+    return context.first_channels + context.second_channels;
+}
+
+Result<std::int32_t> same_rule(const Fields&, const Context& context, Node&) { return context.first_channels; }
+
+struct OpSchema {
+    std::string_view name;
+    Op op;
+    bool binary;
+    std::uint32_t keys;  // bit k: Key k is required
+    Rule rule;
+};
+
+constexpr std::uint32_t bits() { return 0; }
+template <typename... Rest>
+constexpr std::uint32_t bits(Key first, Rest... rest) {
+    return (1u << first) | bits(rest...);
+}
+
+constexpr OpSchema schemas[] = {
+    {"conv", Op::conv, false,
+     bits(k_in_channels, k_out_channels, k_kernel, k_stride, k_pads, k_weight_offset, k_bias_offset, k_depthwise),
+     conv_rule},
+    {"mul", Op::mul, true, 0, same_rule},
+    {"add", Op::add, true, 0, same_rule},
+    {"mul_scalar", Op::mul_scalar, false, bits(k_value), scalar_rule},
+    {"sigmoid", Op::sigmoid, false, 0, same_rule},
+    {"slice_channels", Op::slice_channels, false, bits(k_begin, k_end), slice_rule},
+    {"depth_to_space", Op::depth_to_space, false, bits(k_block), block_rule},
+    {"scale_channels", Op::scale_channels, true, 0, same_rule},
+    {"clamp", Op::clamp, false, bits(k_min, k_max), clamp_rule},
+    {"concat", Op::concat, true, 0, concat_rule},
+    {"crop", Op::crop, true, bits(k_axis), crop_rule},
+    {"space_to_depth", Op::space_to_depth, false, bits(k_block), block_rule},
+    {"im2col", Op::im2col, false, bits(k_kernel, k_stride, k_pads), im2col_rule},
+};
+
+// Names to tensor ids while a program is read; also owns the growing Program.
+class ProgramBuilder {
+public:
+    Program program;
+
+    std::size_t add_tensor(const std::string& name, std::int32_t channels) {
+        const std::size_t id = program.tensor_names.size();
+        program.tensor_names.push_back(name);
+        program.tensor_channels.push_back(channels);
+        by_name_[name] = id;
+        return id;
+    }
+    std::optional<std::size_t> lookup(const std::string& name) const {
+        const auto found = by_name_.find(name);
+        return found == by_name_.end() ? std::nullopt : std::optional<std::size_t>(found->second);
+    }
+    Result<std::size_t> existing(const std::string& name) const {
+        if (auto id = lookup(name)) return *id;
+        return invalid("no tensor named '" + name + "' is defined before this use");
+    }
+
+    // One node object: schema lookup, inputs, fields, rule, widths, output.
+    std::optional<Error> read_node(const json::Value& object) {
+        const json::Value* op_value = object.get("op");
+        if (op_value == nullptr || op_value->kind != json::Value::Kind::string) {
+            return invalid("node without a string 'op'");
+        }
+        const OpSchema* schema = nullptr;
+        for (const auto& candidate : schemas) {
+            if (candidate.name == op_value->text) schema = &candidate;
+        }
+        if (schema == nullptr) return invalid("op '" + op_value->text + "' is not part of nvcr.intconv.v1");
+        Node node;
+        node.op = schema->op;
+        node.input_count = schema->binary ? 2 : 1;
+        if (schema->binary) {
+            const json::Value* list = object.get("inputs");
+            if (list == nullptr || list->items.size() != 2) return invalid(std::string(schema->name) + " takes two inputs");
+            for (std::size_t i = 0; i < 2; ++i) {
+                auto id = existing(list->items[i].text);
+                if (!id) return id.error();
+                node.inputs[i] = id.value();
+            }
+        } else {
+            const json::Value* single = object.get("input");
+            if (single == nullptr || single->kind != json::Value::Kind::string) {
+                return invalid(std::string(schema->name) + " needs a string 'input'");
+            }
+            auto id = existing(single->text);
             if (!id) return id.error();
-            node.inputs[i] = id.value();
+            node.inputs[0] = id.value();
         }
-        node.input_count = 2;
-    } else {
-        auto input = get_text(value, "input");
-        if (!input) return input.error();
-        auto id = tensors.find(input.value());
-        if (!id) return id.error();
-        node.inputs[0] = id.value();
+        Fields fields;
+        for (int key = 0; key < key_count; ++key) {
+            if ((schema->keys >> key) & 1u) {
+                if (auto error = fetch(object, static_cast<Key>(key), schema->name, fields)) return error;
+            }
+        }
+        const Context context{program.tensor_channels[node.inputs[0]],
+                              schema->binary ? program.tensor_channels[node.inputs[1]] : 0,
+                              program.weights.size()};
+        auto channels = schema->rule(fields, context, node);
+        if (!channels) return channels.error();
+        if (const json::Value* widths = object.get("integer"); widths != nullptr) {
+            std::int32_t chosen[2] = {0, 0};
+            const std::string_view names[2] = {"weight_bits", "activation_bits"};
+            for (int i = 0; i < 2; ++i) {
+                const json::Value* v = widths->get(names[i]);
+                if (v == nullptr || v->kind != json::Value::Kind::number || !v->integer) {
+                    return invalid("integer width '" + std::string(names[i]) + "' is not an integer");
+                }
+                chosen[i] = static_cast<std::int32_t>(*v->integer);
+            }
+            const auto allowed = [](std::int32_t b) { return b == 8 || b == 16; };
+            if (node.op != Op::conv || !allowed(chosen[0]) || !allowed(chosen[1])) {
+                return invalid("integer widths must be 8 or 16 and belong to a conv");
+            }
+            node.weight_bits = chosen[0];
+            node.activation_bits = chosen[1];
+        }
+        const json::Value* output = object.get("output");
+        if (output == nullptr || output->kind != json::Value::Kind::string) {
+            return invalid(std::string(schema->name) + " needs a string 'output'");
+        }
+        if (lookup(output->text)) return invalid("tensor '" + output->text + "' is written by two nodes");
+        node.output = add_tensor(output->text, channels.value());
+        program.nodes.push_back(node);
+        return std::nullopt;
     }
 
-    std::int32_t channels = 0;  // 0: inherit the first input's channels
-    switch (node.op) {
-    case Op::conv: {
-        auto in_channels = get_int(value, "in_channels");
-        auto out_channels = get_int(value, "out_channels");
-        auto kernel = get_ints<2>(value, "kernel");
-        auto stride = get_ints<2>(value, "stride");
-        auto pads = get_ints<4>(value, "pads");
-        auto weight_offset = get_int(value, "weight_offset");
-        auto bias_offset = get_int(value, "bias_offset");
-        const auto* depthwise = value.get("depthwise");
-        if (!in_channels) return in_channels.error();
-        if (!out_channels) return out_channels.error();
-        if (!kernel) return kernel.error();
-        if (!stride) return stride.error();
-        if (!pads) return pads.error();
-        if (!weight_offset) return weight_offset.error();
-        if (!bias_offset) return bias_offset.error();
-        if (depthwise == nullptr || depthwise->kind != json::Value::Kind::boolean) {
-            return invalid("conv needs a boolean 'depthwise'");
-        }
-        node.in_channels = static_cast<std::int32_t>(in_channels.value());
-        node.out_channels = static_cast<std::int32_t>(out_channels.value());
-        node.depthwise = depthwise->boolean;
-        node.kernel = kernel.value();
-        node.stride = stride.value();
-        node.pads = pads.value();
-        const bool bad_pad = std::any_of(node.pads.begin(), node.pads.end(), [](std::int32_t p) { return p < 0; });
-        if (node.in_channels <= 0 || node.out_channels <= 0 || node.kernel[0] <= 0 || node.kernel[1] <= 0 ||
-            node.stride[0] <= 0 || node.stride[1] <= 0 || bad_pad ||
-            (node.depthwise && node.in_channels != node.out_channels) || weight_offset.value() < 0 ||
-            bias_offset.value() < 0) {
-            return invalid("conv has an invalid geometry");
-        }
-        node.weight_offset = static_cast<std::size_t>(weight_offset.value());
-        node.bias_offset = static_cast<std::size_t>(bias_offset.value());
-        const std::size_t per_output = static_cast<std::size_t>(node.depthwise ? 1 : node.in_channels) *
-            static_cast<std::size_t>(node.kernel[0]) * static_cast<std::size_t>(node.kernel[1]);
-        const std::size_t count = static_cast<std::size_t>(node.out_channels) * per_output;
-        if (node.weight_offset > weight_count || count > weight_count - node.weight_offset ||
-            node.bias_offset > weight_count ||
-            static_cast<std::size_t>(node.out_channels) > weight_count - node.bias_offset) {
-            return invalid("conv weights exceed the weights file");
-        }
-        channels = node.out_channels;
-        break;
-    }
-    case Op::mul_scalar: {
-        auto scalar = get_exact_float(value, "value", "mul_scalar");
-        if (!scalar) return scalar.error();
-        node.scalar = scalar.value();
-        break;
-    }
-    case Op::slice_channels: {
-        auto begin = get_int(value, "begin");
-        auto end = get_int(value, "end");
-        if (!begin) return begin.error();
-        if (!end) return end.error();
-        node.begin = static_cast<std::int32_t>(begin.value());
-        node.end = static_cast<std::int32_t>(end.value());
-        channels = node.end - node.begin;
-        break;
-    }
-    case Op::depth_to_space:
-    case Op::space_to_depth: {
-        auto block = get_int(value, "block");
-        if (!block) return block.error();
-        node.block = static_cast<std::int32_t>(block.value());
-        if (node.block <= 0 || node.block > 64) return invalid("block size must be in [1, 64]");
-        if (node.op == Op::space_to_depth) channels = tensors.channels(node.inputs[0]) * node.block * node.block;
-        break;
-    }
-    case Op::clamp: {
-        const auto* lo = value.get("min");
-        const auto* hi = value.get("max");
-        if (lo == nullptr || hi == nullptr || lo->kind != json::Value::Kind::number ||
-            hi->kind != json::Value::Kind::number) {
-            return invalid("clamp needs numeric 'min' and 'max'");
-        }
-        node.minimum = static_cast<float>(lo->number);
-        node.maximum = static_cast<float>(hi->number);
-        if (static_cast<double>(node.minimum) != lo->number || static_cast<double>(node.maximum) != hi->number ||
-            !(node.minimum <= node.maximum)) {
-            return invalid("clamp bounds must be ordered float32 values");
-        }
-        break;
-    }
-    case Op::concat:
-        channels = tensors.channels(node.inputs[0]) + tensors.channels(node.inputs[1]);
-        break;
-    case Op::im2col: {
-        auto kernel = get_ints<2>(value, "kernel");
-        auto stride = get_ints<2>(value, "stride");
-        auto pads = get_ints<4>(value, "pads");
-        if (!kernel) return kernel.error();
-        if (!stride) return stride.error();
-        if (!pads) return pads.error();
-        node.kernel = kernel.value();
-        node.stride = stride.value();
-        node.pads = pads.value();
-        const bool bad_pad = std::any_of(node.pads.begin(), node.pads.end(), [](std::int32_t p) { return p < 0; });
-        if (node.kernel[0] <= 0 || node.kernel[1] <= 0 || node.kernel[0] * node.kernel[1] > 64 ||
-            node.stride[0] <= 0 || node.stride[1] <= 0 || bad_pad) {
-            return invalid("im2col has an invalid geometry");
-        }
-        channels = tensors.channels(node.inputs[0]) * node.kernel[0] * node.kernel[1];
-        break;
-    }
-    case Op::crop: {
-        auto axis = get_int(value, "axis");
-        if (!axis) return axis.error();
-        if (axis.value() != 2 && axis.value() != 3) return invalid("crop axis must be 2 or 3");
-        node.axis = static_cast<std::int32_t>(axis.value());
-        break;
-    }
-    case Op::mul:
-    case Op::add:
-    case Op::scale_channels:
-    case Op::sigmoid:
-        break;
-    }
-
-    if (const auto* integer = value.get("integer"); integer != nullptr) {
-        auto weight_bits = get_int(*integer, "weight_bits");
-        auto activation_bits = get_int(*integer, "activation_bits");
-        if (!weight_bits) return weight_bits.error();
-        if (!activation_bits) return activation_bits.error();
-        node.weight_bits = static_cast<std::int32_t>(weight_bits.value());
-        node.activation_bits = static_cast<std::int32_t>(activation_bits.value());
-        const auto valid_bits = [](std::int32_t bits) { return bits == 8 || bits == 16; };
-        if (node.op != Op::conv || !valid_bits(node.weight_bits) || !valid_bits(node.activation_bits)) {
-            return invalid("invalid integer widths on a node");
-        }
-    }
-
-    auto output = get_text(value, "output");
-    if (!output) return output.error();
-    if (tensors.contains(output.value())) return invalid("tensor '" + output.value() + "' is defined twice");
-    node.output = tensors.define(output.value(), channels);
-    return node;
-}
+private:
+    std::unordered_map<std::string, std::size_t> by_name_;
+};
 
 Result<std::string> read_file(const std::string& path) {
     std::ifstream stream(path, std::ios::binary);
@@ -329,98 +385,117 @@ std::uint16_t float_to_half(float value) {
     return static_cast<std::uint16_t>(sign | out);
 }
 
+namespace {
+
+// A top-level string or integer member of the program document, or nothing.
+const std::string* text_member(const json::Value& object, std::string_view key) {
+    const json::Value* v = object.get(key);
+    return v != nullptr && v->kind == json::Value::Kind::string ? &v->text : nullptr;
+}
+std::optional<std::int64_t> integer_member(const json::Value& object, std::string_view key) {
+    const json::Value* v = object.get(key);
+    if (v == nullptr || v->kind != json::Value::Kind::number || !v->integer) return std::nullopt;
+    return v->integer;
+}
+
+// The weights block: in-memory values, or the FP16 file beside the program,
+// which must hash to the declared SHA-256 and hold exactly `count` values.
+std::optional<Error> read_weights(const json::Value& root, const std::string& directory, const float* weights,
+                                  std::size_t weight_count, Program& program) {
+    const json::Value* block = root.get("weights");
+    if (block == nullptr) return invalid("the program declares no weights");
+    const std::string* file = text_member(*block, "file");
+    const auto count = integer_member(*block, "count");
+    const std::string* digest = text_member(*block, "sha256");
+    if (file == nullptr) return invalid("weights 'file' is not a string");
+    if (!count || *count < 0) return invalid("weights 'count' is not a non-negative integer");
+    if (digest == nullptr) return invalid("weights 'sha256' is not a string");
+    if (file->find_first_of("/\\") != std::string::npos) return invalid("the weights file must sit beside the program");
+    const auto declared = static_cast<std::size_t>(*count);
+    if (weights != nullptr) {
+        if (weight_count != declared) return invalid("in-memory weights disagree with the declared count");
+        program.weights.assign(weights, weights + weight_count);
+    } else {
+        const std::string path = (directory.empty() ? std::string(".") : directory) + "/" + *file;
+        auto blob = read_file(path);
+        if (!blob) return blob.error();
+        const std::string& bytes = blob.value();
+        if (sha256_hex(bytes.data(), bytes.size()) != *digest) {
+            return fail(Code::digest_mismatch, "weights file does not match its declared SHA-256: " + path);
+        }
+        if (bytes.size() != 2 * declared) return invalid("weights file length disagrees with the declared count");
+        program.weights.resize(declared);
+        for (std::size_t i = 0; i < declared; ++i) {
+            const std::uint16_t bits = static_cast<std::uint16_t>(static_cast<unsigned char>(bytes[2 * i]) |
+                                                                  (static_cast<unsigned char>(bytes[2 * i + 1]) << 8));
+            program.weights[i] = half_to_float(bits);
+        }
+    }
+    program.weights_sha256 = *digest;
+    return std::nullopt;
+}
+
+}  // namespace
+
 Result<Program> load_program_text(std::string_view text, const std::string& directory, const float* weights,
                                   std::size_t weight_count) {
     auto parsed = json::parse(text);
     if (!parsed) return parsed.error();
-    const auto& root = parsed.value();
-    auto format = get_text(root, "format");
-    auto numerics = get_text(root, "numerics");
-    auto version = get_int(root, "version");
-    if (!format || format.value() != "nvcr.deterministic-program" || !version || version.value() != 1) {
-        return invalid("not an NVCR deterministic program v1");
-    }
-    if (!numerics || numerics.value() != intconv_profile) return invalid("unsupported deterministic numerics");
-    Program program;
-    program.numerics = numerics.value();
-    auto name = get_text(root, "name");
-    if (!name) return name.error();
-    program.name = name.value();
+    const json::Value& root = parsed.value();
 
-    const auto* weight_info = root.get("weights");
-    if (weight_info == nullptr) return invalid("program has no weights");
-    auto file = get_text(*weight_info, "file");
-    auto count = get_int(*weight_info, "count");
-    auto digest = get_text(*weight_info, "sha256");
-    if (!file) return file.error();
-    if (!count || count.value() < 0) return invalid("invalid weights count");
-    if (!digest) return digest.error();
-    if (file.value().find('/') != std::string::npos || file.value().find('\\') != std::string::npos) {
-        return invalid("weights file must sit next to the program");
+    // Header: format, version, profile, name.
+    const std::string* format = text_member(root, "format");
+    const auto version = integer_member(root, "version");
+    if (format == nullptr || *format != "nvcr.deterministic-program" || version != std::optional<std::int64_t>(1)) {
+        return invalid("the document is not an nvcr.deterministic-program of version 1");
     }
-    if (weights != nullptr) {
-        if (weight_count != static_cast<std::size_t>(count.value())) {
-            return invalid("in-memory weights do not match the declared count");
-        }
-        program.weights.assign(weights, weights + weight_count);
-    } else {
-        const std::string path = (directory.empty() ? std::string(".") : directory) + "/" + file.value();
-        auto blob = read_file(path);
-        if (!blob) return blob.error();
-        if (sha256_hex(blob.value().data(), blob.value().size()) != digest.value()) {
-            return fail(Code::digest_mismatch, "deterministic weights digest mismatch: " + path);
-        }
-        if (blob.value().size() != static_cast<std::size_t>(count.value()) * 2) {
-            return invalid("weights file size does not match the declared count");
-        }
-        program.weights.resize(static_cast<std::size_t>(count.value()));
-        for (std::size_t i = 0; i < program.weights.size(); ++i) {
-            const auto lo = static_cast<unsigned char>(blob.value()[2 * i]);
-            const auto hi = static_cast<unsigned char>(blob.value()[2 * i + 1]);
-            program.weights[i] = half_to_float(static_cast<std::uint16_t>(lo | (hi << 8)));
-        }
-    }
-    program.weights_sha256 = digest.value();
+    const std::string* numerics = text_member(root, "numerics");
+    if (numerics == nullptr || *numerics != intconv_profile) return invalid("the program's numerics is not nvcr.intconv.v1");
+    const std::string* name = text_member(root, "name");
+    if (name == nullptr) return invalid("the program's 'name' is not a string");
 
-    Tensors tensors(program);
-    const auto* inputs = root.get("inputs");
-    const auto* outputs = root.get("outputs");
-    const auto* nodes = root.get("nodes");
-    if (inputs == nullptr || outputs == nullptr || nodes == nullptr) {
-        return invalid("program needs inputs, outputs, and nodes");
+    ProgramBuilder builder;
+    builder.program.numerics = *numerics;
+    builder.program.name = *name;
+    if (auto error = read_weights(root, directory, weights, weight_count, builder.program)) return *error;
+
+    // Graph: inputs define tensors, nodes read defined tensors and define one
+    // more each, outputs name defined tensors.
+    const json::Value* inputs = root.get("inputs");
+    const json::Value* nodes = root.get("nodes");
+    const json::Value* outputs = root.get("outputs");
+    if (inputs == nullptr || nodes == nullptr || outputs == nullptr) {
+        return invalid("the program lacks 'inputs', 'nodes' or 'outputs'");
     }
-    for (const auto& input : inputs->items) {
-        auto input_name = get_text(input, "name");
-        auto channels = get_int(input, "channels");
-        if (!input_name) return input_name.error();
-        if (!channels || channels.value() <= 0) return invalid("input channels must be positive");
-        program.inputs.push_back(tensors.define(input_name.value(), static_cast<std::int32_t>(channels.value())));
+    for (const json::Value& input : inputs->items) {
+        const std::string* input_name = text_member(input, "name");
+        if (input_name == nullptr) return invalid("an input's 'name' is not a string");
+        const auto channels = integer_member(input, "channels");
+        if (!channels || *channels <= 0) return invalid("an input's 'channels' is not a positive integer");
+        builder.program.inputs.push_back(builder.add_tensor(*input_name, static_cast<std::int32_t>(*channels)));
     }
-    for (const auto& item : nodes->items) {
-        auto node = parse_node(item, tensors, program.weights.size());
-        if (!node) return node.error();
-        auto& channels = program.tensor_channels[node.value().output];
-        if (channels == 0) {
-            const auto source = program.tensor_channels[node.value().inputs[0]];
-            channels = node.value().op == Op::depth_to_space ? source / (node.value().block * node.value().block)
-                                                            : source;
-        }
-        program.nodes.push_back(node.value());
+    for (const json::Value& node : nodes->items) {
+        if (auto error = builder.read_node(node)) return *error;
     }
-    for (const auto& output : outputs->items) {
-        auto output_name = get_text(output, "name");
-        if (!output_name) return output_name.error();
-        auto id = tensors.find(output_name.value());
+    for (const json::Value& output : outputs->items) {
+        const std::string* output_name = text_member(output, "name");
+        if (output_name == nullptr) return invalid("an output's 'name' is not a string");
+        auto id = builder.existing(*output_name);
         if (!id) return id.error();
-        program.outputs.push_back(id.value());
+        builder.program.outputs.push_back(id.value());
     }
+
+    // Liveness: the index of each tensor's last reading node; stage outputs
+    // live to the end.
+    Program& program = builder.program;
     program.last_use.assign(program.tensor_names.size(), 0);
     for (std::size_t index = 0; index < program.nodes.size(); ++index) {
-        const auto& node = program.nodes[index];
-        for (std::size_t i = 0; i < node.input_count; ++i) program.last_use[node.inputs[i]] = index;
+        for (std::size_t i = 0; i < program.nodes[index].input_count; ++i) {
+            program.last_use[program.nodes[index].inputs[i]] = index;
+        }
     }
-    for (const auto id : program.outputs) program.last_use[id] = program.nodes.size();
-    return program;
+    for (const std::size_t id : program.outputs) program.last_use[id] = program.nodes.size();
+    return std::move(builder.program);
 }
 
 Result<Program> load_program_file(const std::string& path) {

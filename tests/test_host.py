@@ -169,3 +169,69 @@ def test_stack_profile_report_folds_blocks():
     assert "total 0.250 ms per run" in text
     assert "| integer_conv:i.dec.dec_1.ffn.1.sum | 2 | 0.200 | 100.0 | 1000 |" in text
     assert "| conv:i.dec.dec_1.dc.2 | 1 | 0.050 | 0.0 | 1000 |" in text
+
+
+def _corruption_value(rng):
+    return rng.choice([0, -1, 1, 2, 3, 16, 64, 65, 70, 1 << 20, 1 << 40, -(1 << 31), 0.5, 1.0, 0.1, 1e39, "x",
+                       "x_in", None, [], {}, [1, 1], [3, 3], [0, 1], [1, 1, 1, 1], [-1, 0, 0, 0], [1, 2, 3], True,
+                       False, {"weight_bits": 8, "activation_bits": 8}, {"weight_bits": 16}])
+
+
+def test_random_corruptions_load_like_the_reference(built_library, reference, tmp_path):
+    """Seeded random edits of a valid program's JSON (a node field set to an odd
+    value or removed, a top-level member replaced): every edit is accepted or
+    refused with the reference loader's code, and an accepted program infers the
+    reference's output extents."""
+    import random
+
+    rng = random.Random(2027)
+    stream = SeededStream(5)
+    program = op_program(stream).with_widths(8, 16)
+    base_path = program.write(tmp_path / "base", "ops")
+    base = json.loads(base_path.read_text())
+    blob = (tmp_path / "base" / "ops.detw").read_bytes()
+    directory = tmp_path / "edit"
+    directory.mkdir()
+    (directory / "ops.detw").write_bytes(blob)
+    outcomes = {}
+    for trial in range(400):
+        document = json.loads(json.dumps(base))
+        for _ in range(rng.randint(1, 2)):
+            if rng.random() < 0.2:
+                key = rng.choice(["inputs", "outputs", "nodes", "name", "numerics", "version", "weights"])
+                if rng.random() < 0.3:
+                    document.pop(key, None)
+                else:
+                    document[key] = _corruption_value(rng)
+                continue
+            nodes = document.get("nodes")
+            if not isinstance(nodes, list) or not nodes or not isinstance(nodes[0], dict):
+                continue
+            node = rng.choice([n for n in nodes if isinstance(n, dict)])
+            key = rng.choice(sorted(node.keys()) + ["integer", "inputs", "input", "depthwise"])
+            if rng.random() < 0.2:
+                node.pop(key, None)
+            else:
+                node[key] = _corruption_value(rng)
+        path = directory / "ops.detprog.json"
+        path.write_text(json.dumps(document))
+        ref_code, ref_message = reference.load_check(path)
+        try:
+            loaded = ex.LoadedProgram.load(path)
+            ours = 0
+        except ex.ExecutorError as error:
+            ours = int(error.code) + 1
+            loaded = None
+        assert ours == ref_code, f"trial {trial}: reference {ref_code} ({ref_message}), ours {ours}"
+        outcomes[ours] = outcomes.get(ours, 0) + 1
+        if loaded is not None:
+            for extent in [(70, 11, 18), (70, 3, 5)]:
+                if len(loaded.input_names) != 1:
+                    break
+                code, value = reference.infer_extents(path, [extent])
+                try:
+                    assert code == 0 and loaded.infer_output_extents([extent]) == value, (trial, extent)
+                except ex.ExecutorError as error:
+                    assert code == int(error.code) + 1, (trial, extent, code, str(error))
+            loaded.close()
+    assert outcomes.get(0, 0) > 20 and outcomes.get(int(ex.ErrorCode.invalid_argument) + 1, 0) > 150, outcomes

@@ -60,6 +60,7 @@ def test_masks_and_restore(cuda, host):
     import torch
 
     from nvcr_b200.executor import _check, library
+    from tests.test_glue_host import same_halves
 
     rng = np.random.default_rng(6)
     for ways in (4, 2):
@@ -85,7 +86,10 @@ def test_masks_and_restore(cuda, host):
             _check(library().nvcr_sm100_dcvc_restore(ptr(device_symbols), ptr(device_means), ptr(mask), ptr(out),
                                                      batch, channels, height, width, ways, None))
             torch.cuda.synchronize()
-            assert np.array_equal(out.cpu().numpy().view(np.uint16), expected)
+            # Restore adds a mean to a symbol: a NaN result's sign follows x86
+            # operand order on the host and is canonical on the GPU, so NaN
+            # equals NaN here (the profile's rule).
+            assert same_halves(out.cpu().numpy().view(np.uint16), expected)
 
 
 def test_process_and_reduce(cuda, host):
