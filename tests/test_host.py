@@ -230,8 +230,10 @@ def test_random_corruptions_load_like_the_reference(built_library, reference, tm
                     break
                 code, value = reference.infer_extents(path, [extent])
                 try:
-                    assert code == 0 and loaded.infer_output_extents([extent]) == value, (trial, extent)
+                    ours_extents = loaded.infer_output_extents([extent])
                 except ex.ExecutorError as error:
                     assert code == int(error.code) + 1, (trial, extent, code, str(error))
+                else:
+                    assert code == 0 and ours_extents == value, (trial, extent, code, value)
             loaded.close()
     assert outcomes.get(0, 0) > 20 and outcomes.get(int(ex.ErrorCode.invalid_argument) + 1, 0) > 150, outcomes
