@@ -47,6 +47,18 @@ struct Executor::IntegerConv {
     bool b_resident{false};  // one N tile whose K blocks all stay in shared memory
     int halo_budget{0};
     int producer_sets{1};    // 2: eight producer warps on alternate tiles, four epilogue warps
+    // Direct path (w8a8, stride-1 windows up to 3x3, or receptive fields): the
+    // activations are quantised per pixel into int8 [pixels][c8] and loaded by
+    // TMA; K is tap-major, k = tap * c8 + c, in k_block-byte stages. A
+    // multi-tap window falls back to the quantise-on-load path above when its
+    // pixels' exponents differ.
+    bool direct{false};
+    int c8{0};
+    int k_block{0}, c_blocks{0}, direct_k_blocks{0};
+    int direct_a_stages{0}, direct_b_stages{0};
+    bool direct_b_resident{false};
+    void* direct_allocation{nullptr};
+    CUtensorMap direct_b_map{};
 };
 
 enum class StepKind { generic, integer_conv, chunk_add };
@@ -79,6 +91,13 @@ struct PlannedConv {
     int halo_buffers{2};  // halo ring depth: what the conv's halo region holds, up to 8
     CUtensorMap halo_map{};
     const void* halo_base{nullptr};  // staged address halo_map was encoded for
+    // Direct path: the int8 per-pixel copy, the fallback word (multi-tap
+    // windows), the patch shape of the direct conv and its activation map.
+    std::size_t quantised{0};
+    std::size_t fallback{0};
+    int d_patch_h{0}, d_patch_w{0}, d_tiles_y{0}, d_tiles_x{0};
+    CUtensorMap a_map{};
+    const void* a_base{nullptr};
 };
 
 struct Executor::Plan {
@@ -225,7 +244,10 @@ Result<std::unique_ptr<Executor>> Executor::create(Program program, cudaStream_t
 Executor::~Executor() {
     if (stream_ != nullptr) cudaStreamSynchronize(stream_);
     clear_graphs();
-    for (auto& conv : convs_) cudaFree(conv.allocation);
+    for (auto& conv : convs_) {
+        cudaFree(conv.allocation);
+        cudaFree(conv.direct_allocation);
+    }
     for (auto event : events_) cudaEventDestroy(event);
     cudaFree(arena_);
     cudaFree(weights_);
@@ -697,8 +719,106 @@ Status Executor::prepare_integer_conv(std::size_t step_index) {
             return cuda_error("cuTensorMapEncodeTiled weights", status);
         }
     }
+    auto direct = prepare_direct(conv, step, node, quantized);
+    if (!direct) {
+        cudaFree(conv.allocation);
+        return direct;
+    }
     step.conv = static_cast<int>(convs_.size());
     convs_.push_back(conv);
+    return Ok{};
+}
+
+// The direct path of a w8a8 conv when its window allows it: the tap-major int8
+// weight matrix [n_tiles * n_tile][taps * c8] (zero rows and channels as
+// padding), its TMA map, and the ring depths that fit in shared memory.
+Status Executor::prepare_direct(IntegerConv& conv, const Step& step, const Node& node,
+                                const IntegerWeights& quantized) {
+    if (conv.weight_limbs != 1 || conv.activation_limbs != 1) return Ok{};
+    if (const char* forced = std::getenv("NVCR_SM100_DIRECT"); forced != nullptr && forced[0] == '0') return Ok{};
+    const kernels::Window& w = step.window;
+    const int taps = conv.k_taps;
+    if (conv.fields) {
+        conv.c8 = round_up(conv.channels * conv.taps, 32);
+        if (conv.c8 > 64) return Ok{};
+    } else {
+        const bool window_ok = w.kernel_h <= 3 && w.kernel_w <= 3 && w.stride_y == 1 && w.stride_x == 1;
+        // The plane prepass keeps all channels of 64 pixels in shared memory.
+        if (!window_ok || conv.channels > 780) return Ok{};
+        conv.c8 = round_up(conv.channels, 32);
+    }
+    conv.k_block = conv.c8 % 128 == 0 ? 128 : (conv.c8 % 64 == 0 ? 64 : 32);
+    conv.c_blocks = conv.c8 / conv.k_block;
+    conv.direct_k_blocks = taps * conv.c_blocks;
+    const int n_padded = conv.n_tiles * conv.n_tile;
+    // Ring depths: resident weights when one N tile's K blocks fit, else the
+    // deepest rings that fit.
+    bool fits = false;
+    if (conv.n_tiles == 1 && conv.direct_k_blocks <= 8) {
+        for (const int a_stages : {6, 4, 3, 2}) {
+            if (kernels::direct_conv_shared_bytes(conv.k_block, conv.n_tile, conv.n_tiles, a_stages,
+                                                  conv.direct_k_blocks) <= kernels::direct_conv_max_shared) {
+                conv.direct_a_stages = a_stages;
+                conv.direct_b_stages = conv.direct_k_blocks;
+                conv.direct_b_resident = true;
+                fits = true;
+                break;
+            }
+        }
+    }
+    if (!fits) {
+        constexpr int depths[][2] = {{6, 6}, {4, 6}, {6, 4}, {4, 4}, {4, 3}, {3, 3}, {3, 2}, {2, 2}};
+        for (const auto& depth : depths) {
+            if (kernels::direct_conv_shared_bytes(conv.k_block, conv.n_tile, conv.n_tiles, depth[0], depth[1]) <=
+                kernels::direct_conv_max_shared) {
+                conv.direct_a_stages = depth[0];
+                conv.direct_b_stages = depth[1];
+                fits = true;
+                break;
+            }
+        }
+    }
+    if (!fits) return Ok{};
+    const std::size_t row_bytes = static_cast<std::size_t>(taps) * conv.c8;
+    std::vector<std::int8_t> matrix(static_cast<std::size_t>(n_padded) * row_bytes, 0);
+    const int rows = node.out_channels;
+    for (int physical = 0; physical < n_padded; ++physical) {
+        int row = physical < rows ? physical : -1;
+        if (conv.chunk_add) {
+            const int tile = physical / conv.n_tile;
+            const int local = physical % conv.n_tile;
+            const int half = conv.n_tile / 2;
+            const int pair = tile * half + (local % half);
+            row = pair >= rows / 2 ? -1 : (local < half ? pair : rows / 2 + pair);
+        }
+        if (row < 0) continue;
+        const std::size_t at = static_cast<std::size_t>(row) * node.in_channels;
+        for (int tap = 0; tap < taps; ++tap) {
+            for (int c = 0; c < conv.c8; ++c) {
+                int q = 0;
+                if (conv.fields) {
+                    q = c < node.in_channels ? quantized.values[at + static_cast<std::size_t>(c)] : 0;
+                } else if (c < conv.channels) {
+                    q = quantized.values[at + static_cast<std::size_t>(c) * conv.taps + tap];
+                }
+                matrix[static_cast<std::size_t>(physical) * row_bytes + static_cast<std::size_t>(tap) * conv.c8 + c] =
+                    static_cast<std::int8_t>(q);
+            }
+        }
+    }
+    cudaError_t status = cudaMalloc(&conv.direct_allocation, matrix.size());
+    if (status != cudaSuccess) return cuda_error("cudaMalloc direct weights", status);
+    status = cudaMemcpy(conv.direct_allocation, matrix.data(), matrix.size(), cudaMemcpyHostToDevice);
+    if (status == cudaSuccess) {
+        status = kernels::encode_weight_map(&conv.direct_b_map, conv.direct_allocation, n_padded, row_bytes,
+                                            conv.k_block, conv.n_tile);
+    }
+    if (status != cudaSuccess) {
+        cudaFree(conv.direct_allocation);
+        conv.direct_allocation = nullptr;
+        return cuda_error("direct weights", status);
+    }
+    conv.direct = true;
     return Ok{};
 }
 
@@ -809,12 +929,41 @@ Result<Executor::Plan*> Executor::plan_for(const std::vector<Extent>& input_exte
             // Staged grid: the source pixels, or the output positions of a fields conv;
             // a staged source tensor is read in place.
             pc.source_staged = staged_tensor_[step.source];
+            const bool multi_tap = !conv.fields && conv.k_taps > 1;
+            const std::size_t grid_pixels = conv.fields ? static_cast<std::size_t>(pc.positions)
+                                                        : static_cast<std::size_t>(source.height) * source.width;
             if (!pc.source_staged) {
-                const std::size_t pixels = conv.fields ? static_cast<std::size_t>(pc.positions)
-                                                       : static_cast<std::size_t>(source.height) * source.width;
-                pc.staged = allocator.allocate(pixels * conv.c_pad * element);
-                pc.pixel_max = allocator.allocate(pixels * sizeof(float));
-                scratch = {pc.staged, pc.pixel_max};
+                // The quantise-on-load copy: the conv itself, or a direct conv's fallback.
+                if (!conv.direct || multi_tap) {
+                    pc.staged = allocator.allocate(grid_pixels * conv.c_pad * element);
+                    scratch.push_back(pc.staged);
+                }
+                pc.pixel_max = allocator.allocate(grid_pixels * sizeof(float));
+                scratch.push_back(pc.pixel_max);
+            }
+            if (conv.direct) {
+                pc.quantised = allocator.allocate(grid_pixels * conv.c8);
+                scratch.push_back(pc.quantised);
+                if (multi_tap) {
+                    pc.fallback = allocator.allocate(sizeof(unsigned int));
+                    scratch.push_back(pc.fallback);
+                }
+                // Patch shape of the direct conv: least padding waste.
+                int least = INT_MAX;
+                for (const int patch_w : {32, 16, 64, 8, 128}) {
+                    const int patch_h = 128 / patch_w;
+                    const int tiles_y = (out.height + patch_h - 1) / patch_h;
+                    const int tiles_x = (out.width + patch_w - 1) / patch_w;
+                    const long long covered = static_cast<long long>(tiles_y) * tiles_x * 128;
+                    const int waste = static_cast<int>((covered - pc.positions) * 1000 / std::max(pc.positions, 1));
+                    if (waste < least) {
+                        least = waste;
+                        pc.d_patch_h = patch_h;
+                        pc.d_patch_w = patch_w;
+                        pc.d_tiles_y = tiles_y;
+                        pc.d_tiles_x = tiles_x;
+                    }
+                }
             }
         }
         allocator.note_peak();
@@ -884,105 +1033,211 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
         if (direct_in.data != nullptr && direct_in.half != pc.source_half) {
             return fail(Code::internal_error, "integer conv source type does not match its plan");
         }
-        // The grid the fused kernel reads: source pixels, or output positions
+        // The grid the conv kernels read: source pixels, or output positions
         // whose records are receptive fields.
         const int grid_h = conv.fields ? conv_out.height : source.height;
         const int grid_w = conv.fields ? conv_out.width : source.width;
         const int pixels = grid_h * grid_w;
         const std::string label = program_.tensor_names[step.output];
         const double positions = static_cast<double>(pc.positions);
-        if (!pc.source_staged) {
-            if (conv.fields) {
-                status = kernels::stage_receptive_fields(from, pc.source_half ? 1 : 0, source.channels, source.height,
-                                                         source.width, step.window, conv_out.height, conv_out.width,
-                                                         conv.c_pad, staged, pixel_max, stream_);
-            } else {
-                status = kernels::stage_source(from, pc.source_half ? 1 : 0, source.channels, conv.c_pad, pixels,
-                                               staged, pixel_max, stream_);
-            }
-            if (status != cudaSuccess) return cuda_error("source staging launch", status);
-            ++launches_;
-            auto marked = mark("stage_source:" + label, "stage_source", 0.0,
-                               static_cast<double>(source.count()) * element +
-                                   static_cast<double>(pixels) * (conv.c_pad * element + 4.0));
-            if (!marked) return marked;
-        }
-        if (pc.halo_base != staged) {
-            status = kernels::encode_halo_map(&pc.halo_map, staged, pc.source_half ? 1 : 0, conv.c_pad, grid_h, grid_w,
-                                              layout.group, pc.halo_box_w, pc.halo_rows);
-            if (status != cudaSuccess) return cuda_error("cuTensorMapEncodeTiled halo", status);
-            pc.halo_base = staged;
-        }
         const Direct& direct_out = run_outputs_[index];
-        kernels::FusedConvArgs f{};
-        f.source_half = pc.source_half ? 1 : 0;
-        f.pixel_max = pixel_max;
-        f.channels = conv.fields ? conv.channels * conv.taps : conv.channels;
-        f.c_pad = conv.c_pad;
-        f.in_h = grid_h;
-        f.in_w = grid_w;
-        f.out_h = conv_out.height;
-        f.out_w = conv_out.width;
-        f.window = conv.window;
-        f.k_real = conv.k_real;
-        f.k_blocks = conv.k_padded / 128;
-        f.positions = pc.positions;
-        f.patch_h = pc.patch_h;
-        f.patch_w = pc.patch_w;
-        f.tiles_y = pc.tiles_y;
-        f.tiles_x = pc.tiles_x;
-        f.p_tiles = pc.tiles_y * pc.tiles_x;
-        f.group = layout.group;
-        f.groups = layout.groups;
-        f.record_bytes = layout.group * element;
-        f.halo_rows = pc.halo_rows;
-        f.halo_box_w = pc.halo_box_w;
-        f.halo_bytes = pc.halo_bytes;
-        f.halo_buffers = pc.halo_buffers;
-        f.producer_sets = conv.producer_sets;
-        f.a_stages = conv.a_stages;
-        f.b_stages = conv.b_stages;
-        f.b_resident = conv.b_resident ? 1 : 0;
-        f.n_tile = conv.n_tile;
-        f.n_tiles = conv.n_tiles;
-        f.column_high_factor = conv.weight_limbs == 2 ? conv.column_high_factor : 0;
-        f.column_low_factor = conv.weight_limbs == 2 ? conv.column_low_factor : 0;
-        f.scales = conv.scales;
-        f.bias = conv.bias;
-        f.row_terms = conv.activation_limbs == 2 ? conv.row_terms : nullptr;
-        f.wsilu = step.wsilu ? 1 : 0;
-        f.wsilu_scale = step.wsilu_scale;
-        f.chunk_add = step.chunk_add ? 1 : 0;
-        f.residual = step.residual ? tensor(*step.residual) : nullptr;
-        f.residual_c_pad = step.residual && staged_tensor_[*step.residual]
+        void* out = direct_out.data != nullptr ? direct_out.data : tensor(step.output);
+        const int out_half = direct_out.data != nullptr && direct_out.half ? 1 : 0;
+        float* out_max = nullptr;
+        int out_c_pad = 0;
+        const double ops = 2.0 * conv.channels * conv.taps * static_cast<double>(node.out_channels) * positions;
+        const double out_bytes = static_cast<double>(out_extent.count()) * (out_half ? 2.0 : 4.0) +
+            (step.residual ? static_cast<double>(out_extent.count()) * 4.0 : 0.0);
+        const float* residual = step.residual ? tensor(*step.residual) : nullptr;
+        const int residual_c_pad = step.residual && staged_tensor_[*step.residual]
             ? round_up(plan.extents[*step.residual].channels, 16) : 0;
-        f.out = direct_out.data != nullptr ? direct_out.data : tensor(step.output);
-        f.out_half = direct_out.data != nullptr && direct_out.half ? 1 : 0;
-        f.out_max = nullptr;
-        f.out_c_pad = 0;
         if (staged_tensor_[step.output]) {
             const Extent staged_out = plan.extents[step.output];
-            f.out_c_pad = round_up(staged_out.channels, 16);
-            f.out_max = reinterpret_cast<float*>(base + plan.offsets[step.output] +
-                                                 staged_max_offset(staged_out, step.output));
-            status = kernels::zero_floats(f.out_max, static_cast<std::size_t>(staged_out.height) * staged_out.width,
-                                          stream_);
-            if (status != cudaSuccess) return cuda_error("zeroing staged maxima", status);
-            ++launches_;
+            out_c_pad = round_up(staged_out.channels, 16);
+            out_max = reinterpret_cast<float*>(base + plan.offsets[step.output] +
+                                               staged_max_offset(staged_out, step.output));
         }
-        f.out_channels = conv.out_channels;
-        f.d2s_block = step.d2s_block;
-        f.status = status_;
-        status = kernels::fused_conv(layout.b_high_map, layout.b_low_map, pc.halo_map, conv.weight_limbs,
-                                     conv.activation_limbs, f, stream_);
-        if (status != cudaSuccess) return cuda_error("integer conv launch", status);
-        launches_ += 1;
-        const double ops = 2.0 * conv.channels * conv.taps * static_cast<double>(node.out_channels) * positions;
-        const double out_bytes = static_cast<double>(out_extent.count()) * (f.out_half ? 2.0 : 4.0) +
-            (step.residual ? static_cast<double>(out_extent.count()) * 4.0 : 0.0);
-        return mark("integer_conv:" + label, "integer_conv", ops,
-                    static_cast<double>(pixels) * (conv.c_pad * element + 4.0) +
-                        static_cast<double>(node.out_channels) * conv.k_real * conv.weight_limbs + out_bytes);
+        auto zero_out_max = [&]() -> Status {
+            if (out_max == nullptr) return Ok{};
+            const Extent staged_out = plan.extents[step.output];
+            const cudaError_t zeroed =
+                kernels::zero_floats(out_max, static_cast<std::size_t>(staged_out.height) * staged_out.width, stream_);
+            if (zeroed != cudaSuccess) return cuda_error("zeroing staged maxima", zeroed);
+            ++launches_;
+            return Ok{};
+        };
+        // The quantise-on-load conv: the conv itself, or (gate not null) a direct
+        // conv's fallback that runs only when that conv found a mixed window.
+        auto launch_fused = [&](const unsigned int* gate) -> Status {
+            cudaError_t launched_status = cudaSuccess;
+            if (!pc.source_staged) {
+                if (conv.fields) {
+                    launched_status = kernels::stage_receptive_fields(
+                        from, pc.source_half ? 1 : 0, source.channels, source.height, source.width, step.window,
+                        conv_out.height, conv_out.width, conv.c_pad, staged, pixel_max, stream_);
+                } else {
+                    launched_status = kernels::stage_source(from, pc.source_half ? 1 : 0, source.channels, conv.c_pad,
+                                                            pixels, staged, pixel_max, stream_, gate);
+                }
+                if (launched_status != cudaSuccess) return cuda_error("source staging launch", launched_status);
+                ++launches_;
+                auto marked = mark((gate ? "fallback_stage:" : "stage_source:") + label,
+                                   gate ? "fallback" : "stage_source", 0.0,
+                                   static_cast<double>(source.count()) * element +
+                                       static_cast<double>(pixels) * (conv.c_pad * element + 4.0));
+                if (!marked) return marked;
+            }
+            if (pc.halo_base != staged) {
+                launched_status = kernels::encode_halo_map(&pc.halo_map, staged, pc.source_half ? 1 : 0, conv.c_pad,
+                                                           grid_h, grid_w, layout.group, pc.halo_box_w, pc.halo_rows);
+                if (launched_status != cudaSuccess) return cuda_error("cuTensorMapEncodeTiled halo", launched_status);
+                pc.halo_base = staged;
+            }
+            kernels::FusedConvArgs f{};
+            f.source_half = pc.source_half ? 1 : 0;
+            f.pixel_max = pixel_max;
+            f.channels = conv.fields ? conv.channels * conv.taps : conv.channels;
+            f.c_pad = conv.c_pad;
+            f.in_h = grid_h;
+            f.in_w = grid_w;
+            f.out_h = conv_out.height;
+            f.out_w = conv_out.width;
+            f.window = conv.window;
+            f.k_real = conv.k_real;
+            f.k_blocks = conv.k_padded / 128;
+            f.positions = pc.positions;
+            f.patch_h = pc.patch_h;
+            f.patch_w = pc.patch_w;
+            f.tiles_y = pc.tiles_y;
+            f.tiles_x = pc.tiles_x;
+            f.p_tiles = pc.tiles_y * pc.tiles_x;
+            f.group = layout.group;
+            f.groups = layout.groups;
+            f.record_bytes = layout.group * element;
+            f.halo_rows = pc.halo_rows;
+            f.halo_box_w = pc.halo_box_w;
+            f.halo_bytes = pc.halo_bytes;
+            f.halo_buffers = pc.halo_buffers;
+            f.producer_sets = conv.producer_sets;
+            f.a_stages = conv.a_stages;
+            f.b_stages = conv.b_stages;
+            f.b_resident = conv.b_resident ? 1 : 0;
+            f.n_tile = conv.n_tile;
+            f.n_tiles = conv.n_tiles;
+            f.column_high_factor = conv.weight_limbs == 2 ? conv.column_high_factor : 0;
+            f.column_low_factor = conv.weight_limbs == 2 ? conv.column_low_factor : 0;
+            f.scales = conv.scales;
+            f.bias = conv.bias;
+            f.row_terms = conv.activation_limbs == 2 ? conv.row_terms : nullptr;
+            f.wsilu = step.wsilu ? 1 : 0;
+            f.wsilu_scale = step.wsilu_scale;
+            f.chunk_add = step.chunk_add ? 1 : 0;
+            f.residual = residual;
+            f.residual_c_pad = residual_c_pad;
+            f.out = out;
+            f.out_half = out_half;
+            f.out_max = out_max;
+            f.out_c_pad = out_c_pad;
+            f.out_channels = conv.out_channels;
+            f.d2s_block = step.d2s_block;
+            f.status = status_;
+            f.gate = gate;
+            launched_status = kernels::fused_conv(layout.b_high_map, layout.b_low_map, pc.halo_map, conv.weight_limbs,
+                                                  conv.activation_limbs, f, stream_);
+            if (launched_status != cudaSuccess) return cuda_error("integer conv launch", launched_status);
+            ++launches_;
+            if (gate != nullptr) return mark("fallback_conv:" + label, "fallback", 0.0, 0.0);
+            return mark("integer_conv:" + label, "integer_conv", ops,
+                        static_cast<double>(pixels) * (conv.c_pad * element + 4.0) +
+                            static_cast<double>(node.out_channels) * conv.k_real * conv.weight_limbs + out_bytes);
+        };
+        if (!conv.direct) {
+            auto zeroed = zero_out_max();
+            if (!zeroed) return zeroed;
+            return launch_fused(nullptr);
+        }
+
+        // ---- direct path: per-pixel int8 activations, TMA-fed GEMM
+        const bool multi_tap = !conv.fields && conv.k_taps > 1;
+        auto* quantised = reinterpret_cast<std::int8_t*>(base + pc.quantised);
+        auto* fallback = multi_tap ? reinterpret_cast<unsigned int*>(base + pc.fallback) : nullptr;
+        if (conv.fields) {
+            status = kernels::quantise_fields(from, pc.source_half ? 1 : 0, source.channels, source.height,
+                                              source.width, step.window, conv_out.height, conv_out.width, conv.c8,
+                                              quantised, pixel_max, stream_);
+        } else if (pc.source_staged) {
+            status = kernels::quantise_pixels(staged, kernels::PixelSource::staged_f32, conv.channels,
+                                              round_up(source.channels, 16), conv.c8, pixels, quantised, pixel_max,
+                                              fallback, stream_);
+        } else {
+            status = kernels::quantise_pixels(from, pc.source_half ? kernels::PixelSource::planes_f16
+                                                                   : kernels::PixelSource::planes_f32,
+                                              conv.channels, 0, conv.c8, pixels, quantised, pixel_max, fallback,
+                                              stream_);
+        }
+        if (status != cudaSuccess) return cuda_error("activation quantisation launch", status);
+        ++launches_;
+        {
+            const double read = conv.fields ? static_cast<double>(source.count()) * element
+                : (pc.source_staged ? static_cast<double>(pixels) * (round_up(source.channels, 16) * 4.0 + 4.0)
+                                    : static_cast<double>(source.count()) * element);
+            auto marked = mark("quantise:" + label, "quantise", 0.0,
+                               read + static_cast<double>(pixels) * (conv.c8 + (pc.source_staged ? 0.0 : 4.0)));
+            if (!marked) return marked;
+        }
+        if (pc.a_base != quantised) {
+            status = kernels::encode_activation_map(&pc.a_map, quantised, conv.c8, grid_h, grid_w, conv.k_block,
+                                                    pc.d_patch_w, pc.d_patch_h);
+            if (status != cudaSuccess) return cuda_error("cuTensorMapEncodeTiled activations", status);
+            pc.a_base = quantised;
+        }
+        auto zeroed = zero_out_max();
+        if (!zeroed) return zeroed;
+        kernels::DirectConvArgs d{};
+        d.pixel_max = pixel_max;
+        d.in_h = grid_h;
+        d.in_w = grid_w;
+        d.out_h = conv_out.height;
+        d.out_w = conv_out.width;
+        d.window = conv.window;
+        d.k_block = conv.k_block;
+        d.c_blocks = conv.c_blocks;
+        d.k_blocks = conv.direct_k_blocks;
+        d.positions = pc.positions;
+        d.patch_h = pc.d_patch_h;
+        d.patch_w = pc.d_patch_w;
+        d.tiles_y = pc.d_tiles_y;
+        d.tiles_x = pc.d_tiles_x;
+        d.p_tiles = pc.d_tiles_y * pc.d_tiles_x;
+        d.a_stages = conv.direct_a_stages;
+        d.b_stages = conv.direct_b_stages;
+        d.b_resident = conv.direct_b_resident ? 1 : 0;
+        d.n_tile = conv.n_tile;
+        d.n_tiles = conv.n_tiles;
+        d.scales = conv.scales;
+        d.bias = conv.bias;
+        d.wsilu = step.wsilu ? 1 : 0;
+        d.wsilu_scale = step.wsilu_scale;
+        d.chunk_add = step.chunk_add ? 1 : 0;
+        d.residual = residual;
+        d.residual_c_pad = residual_c_pad;
+        d.out = out;
+        d.out_half = out_half;
+        d.out_max = out_max;
+        d.out_c_pad = out_c_pad;
+        d.out_channels = conv.out_channels;
+        d.d2s_block = step.d2s_block;
+        d.fallback = fallback;
+        d.status = status_;
+        status = kernels::direct_conv(pc.a_map, conv.direct_b_map, d, stream_);
+        if (status != cudaSuccess) return cuda_error("direct integer conv launch", status);
+        ++launches_;
+        auto marked = mark("integer_conv:" + label, "integer_conv", ops,
+                           static_cast<double>(pixels) * (conv.c8 + 4.0) +
+                               static_cast<double>(node.out_channels) * conv.k_taps * conv.c8 + out_bytes);
+        if (!marked) return marked;
+        if (multi_tap) return launch_fused(fallback);
+        return Ok{};
     }
     case StepKind::chunk_add:
         status = kernels::chunk_add(tensor(step.source), tensor(step.output), count, stream_);

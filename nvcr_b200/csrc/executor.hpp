@@ -86,6 +86,7 @@ private:
     Executor() = default;
     Status prepare();
     Status prepare_integer_conv(std::size_t step_index);
+    Status prepare_direct(IntegerConv& conv, const Step& step, const Node& node, const IntegerWeights& quantized);
     void plan_fusions();
     enum class Boundary { half, float32, host };
     Result<Plan*> plan_for(const std::vector<Extent>& input_extents, Boundary boundary);

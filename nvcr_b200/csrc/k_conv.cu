@@ -182,9 +182,11 @@ __device__ __forceinline__ float max_from_bits(std::uint32_t m) {
 template <bool Half>
 __global__ void __launch_bounds__(256) stage_pixels_kernel(const void* __restrict__ in, int channels, int c_pad,
                                                            int pixels, void* __restrict__ out,
-                                                           float* __restrict__ pixel_max) {
+                                                           float* __restrict__ pixel_max,
+                                                           const unsigned int* __restrict__ gate) {
     grid_dependency_wait();  // the source may come from the kernel before
     launch_dependents();
+    if (gate != nullptr && *gate == 0u) return;  // a direct conv's fallback that is not needed
     using T = std::conditional_t<Half, unsigned short, float>;
     constexpr int per_block = 16 / static_cast<int>(sizeof(T));  // channels per 16-byte store
     constexpr int blocks_per_pass = Half ? 2 : 4;                 // 16 loads in flight
@@ -246,9 +248,11 @@ struct StageShape {
 template <bool Half, int Pixels>
 __global__ void __launch_bounds__(256) stage_source_kernel(const void* __restrict__ in, int channels, int c_pad,
                                                            int pixels, void* __restrict__ out,
-                                                           float* __restrict__ pixel_max) {
+                                                           float* __restrict__ pixel_max,
+                                                           const unsigned int* __restrict__ gate) {
     grid_dependency_wait();  // the source may come from the kernel before
     launch_dependents();
+    if (gate != nullptr && *gate == 0u) return;  // a direct conv's fallback that is not needed
     using T = std::conditional_t<Half, unsigned short, float>;
     using S = StageShape<Half>;
     constexpr int per_word = Half ? 2 : 1;
@@ -328,22 +332,22 @@ __global__ void __launch_bounds__(256) stage_source_kernel(const void* __restric
 
 template <bool Half>
 cudaError_t launch_stage(const void* in, int channels, int c_pad, int pixels, void* out, float* pixel_max,
-                         cudaStream_t stream) {
+                         const unsigned int* gate, cudaStream_t stream) {
     const int block = StageShape<Half>::pixels(c_pad);
     const unsigned blocks = static_cast<unsigned>((static_cast<long long>(pixels) + block - 1) / block);
     switch (block) {
     case 32: return launch_overlapped(stage_source_kernel<Half, 32>, dim3(blocks), dim3(256), 0, stream, in, channels,
-                                      c_pad, pixels, out, pixel_max);
+                                      c_pad, pixels, out, pixel_max, gate);
     case 64: return launch_overlapped(stage_source_kernel<Half, 64>, dim3(blocks), dim3(256), 0, stream, in, channels,
-                                       c_pad, pixels, out, pixel_max);
+                                       c_pad, pixels, out, pixel_max, gate);
     case 128: return launch_overlapped(stage_source_kernel<Half, 128>, dim3(blocks), dim3(256), 0, stream, in, channels,
-                                       c_pad, pixels, out, pixel_max);
+                                       c_pad, pixels, out, pixel_max, gate);
     case 256: return launch_overlapped(stage_source_kernel<Half, 256>, dim3(blocks), dim3(256), 0, stream, in, channels,
-                                       c_pad, pixels, out, pixel_max);
+                                       c_pad, pixels, out, pixel_max, gate);
     default:
         if constexpr (Half) {
             return launch_overlapped(stage_source_kernel<Half, 512>, dim3(blocks), dim3(256), 0, stream, in, channels,
-                                     c_pad, pixels, out, pixel_max);
+                                     c_pad, pixels, out, pixel_max, gate);
         } else {
             return cudaErrorInvalidValue;
         }
@@ -618,6 +622,12 @@ fused_conv_kernel(const __grid_constant__ CUtensorMap b_high, const __grid_const
                   std::uint32_t tmem_columns) {
     using L = ConvLayout<WL, AL>;
     constexpr int bits = AL == 2 ? 16 : 8;
+    if (a.gate != nullptr) {
+        // A direct conv's fallback: runs only when that conv found a window whose
+        // pixels have different exponents.
+        grid_dependency_wait();
+        if (*a.gate == 0u) return;
+    }
     extern __shared__ std::uint8_t dynamic_smem[];
     const std::uint32_t raw = smem_address(dynamic_smem);
     std::uint8_t* smem = dynamic_smem + (((raw + 1023u) & ~1023u) - raw);
@@ -1548,22 +1558,22 @@ cudaError_t encode_halo_map(CUtensorMap* map, const void* base, int half, std::u
 }
 
 cudaError_t stage_source(const void* in, int source_half, int channels, int c_pad, int pixels, void* out,
-                         float* pixel_max, cudaStream_t stream) {
+                         float* pixel_max, cudaStream_t stream, const unsigned int* gate) {
     if (pixels <= 0) return cudaSuccess;
     if (channels < 1 || c_pad < channels || c_pad % 16 != 0 || (reinterpret_cast<std::uintptr_t>(out) & 15u) != 0) {
         return cudaErrorInvalidValue;
     }
     if (c_pad > 32) {
-        return source_half ? launch_stage<true>(in, channels, c_pad, pixels, out, pixel_max, stream)
-                           : launch_stage<false>(in, channels, c_pad, pixels, out, pixel_max, stream);
+        return source_half ? launch_stage<true>(in, channels, c_pad, pixels, out, pixel_max, gate, stream)
+                           : launch_stage<false>(in, channels, c_pad, pixels, out, pixel_max, gate, stream);
     }
     const unsigned blocks = static_cast<unsigned>((static_cast<long long>(pixels) + 255) / 256);
     if (source_half) {
         return launch_overlapped(stage_pixels_kernel<true>, dim3(blocks), dim3(256), 0, stream, in, channels, c_pad,
-                                 pixels, out, pixel_max);
+                                 pixels, out, pixel_max, gate);
     } else {
         return launch_overlapped(stage_pixels_kernel<false>, dim3(blocks), dim3(256), 0, stream, in, channels, c_pad,
-                                 pixels, out, pixel_max);
+                                 pixels, out, pixel_max, gate);
     }
     return cudaGetLastError();
 }

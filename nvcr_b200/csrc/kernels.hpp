@@ -102,13 +102,16 @@ struct FusedConvArgs {
     int out_channels;              // logical channels stored (after chunk-add)
     int d2s_block;                 // 0: NCHW store; b: store through depth_to_space(b)
     unsigned int* status;
+    // When not null, the kernel runs only if *gate is non-zero (read once the
+    // kernels before it are done): the fallback of a direct conv.
+    const unsigned int* gate;
 };
 // Channel-innermost copy of a [channels][pixels] FP16 or FP32 tensor with
 // c_pad >= channels channels per pixel (c_pad a multiple of 16, the extra
 // channels zero), and per pixel max |x| over the channels (+inf when any
 // channel is non-finite).
 cudaError_t stage_source(const void* in, int source_half, int channels, int c_pad, int pixels, void* out,
-                         float* pixel_max, cudaStream_t stream);
+                         float* pixel_max, cudaStream_t stream, const unsigned int* gate = nullptr);
 // For convs with few input channels: per output position its whole receptive
 // field, [out_h][out_w][c_pad] with k = c * taps + tap (padding taps and k past
 // channels * taps zero), in the source's type, and the max |x| over the field
@@ -133,6 +136,71 @@ cudaError_t encode_halo_map(CUtensorMap* map, const void* base, int half, std::u
 // boxes and 128-byte swizzle, the layout the MMA's shared-memory descriptors expect.
 cudaError_t encode_int8_map(CUtensorMap* map, const void* base, std::uint64_t rows, std::uint64_t row_bytes,
                             std::uint32_t box_rows);
+
+// ---- integer conv on pre-quantised activations (w8a8; persistent, tcgen05) ----
+// When every window of a conv takes its activation exponent from pixels that
+// share one exponent, the profile's per-position quantisation of the window
+// equals each pixel quantised with its own exponent. A prepass writes that
+// per-pixel int8 copy, channel-innermost [pixels][c8] (c8 = channels rounded up
+// to 32, padding zero), with each pixel's max |x|; the conv then loads its A
+// operand by TMA straight from it, one (tap, channel block) box of 128 output
+// positions at a time, and checks every window: a window whose non-zero pixels
+// have different exponents sets *fallback, and the quantise-on-load path is
+// then run for the whole conv (it gates on the same word and otherwise returns
+// at once). A 1x1 conv, or a conv over staged receptive fields, has one pixel
+// per window and never falls back.
+struct DirectConvArgs {
+    const float* pixel_max;        // [in_h][in_w] per-pixel max |x| (+inf when non-finite)
+    int in_h, in_w, out_h, out_w;
+    Window window;                 // stride 1 (any window up to 3x3), or 1x1
+    int k_block;                   // K bytes per stage: 32, 64 or 128 (the A and B swizzle span)
+    int c_blocks;                  // K blocks per tap: c8 / k_block
+    int k_blocks;                  // taps * c_blocks
+    int positions, p_tiles;        // out_h * out_w; tiles_y * tiles_x
+    int patch_h, patch_w, tiles_y, tiles_x;
+    int a_stages, b_stages;
+    int b_resident;                // one N tile whose K blocks all stay in shared memory
+    int n_tile, n_tiles;
+    const float* scales;           // [n_tiles * n_tile] per physical weight row (16-byte aligned)
+    const float* bias;             // (16-byte aligned)
+    int wsilu;
+    float wsilu_scale;
+    int chunk_add;
+    const float* residual;         // as FusedConvArgs
+    int residual_c_pad;
+    void* out;
+    int out_half;
+    float* out_max;
+    int out_c_pad;
+    int out_channels;
+    int d2s_block;
+    unsigned int* fallback;        // multi-tap windows: set to 1 when a window mixes exponents; else null
+    unsigned int* status;
+};
+// Source forms of quantise_pixels: NCHW FP32 or FP16 planes, or a staged FP32
+// tensor [pixels][c_pad] whose per-pixel maxima are already known.
+enum class PixelSource { planes_f32, planes_f16, staged_f32 };
+// Per-pixel int8 quantisation into [pixels][c8] (c8 a multiple of 32, >= channels)
+// with each pixel's max |x| written to pixel_max (read from it for staged_f32);
+// clears *clear_word (when not null) for the conv that follows.
+cudaError_t quantise_pixels(const void* in, PixelSource form, int channels, int c_pad_in, int c8, int pixels,
+                            std::int8_t* out, float* pixel_max, unsigned int* clear_word, cudaStream_t stream);
+// The receptive field of each output position (k = c * taps + tap, padding
+// taps zero) quantised with the field's own exponent into [out_h][out_w][c8],
+// and the field's max |x|.
+cudaError_t quantise_fields(const void* in, int source_half, int channels, int in_h, int in_w, Window window,
+                            int out_h, int out_w, int c8, std::int8_t* out, float* field_max, cudaStream_t stream);
+// Tensor maps: the int8 activations [height][width][c8] with a box of k_block
+// bytes x box_w x box_h pixels, and the int8 weights [rows][row_bytes] with a
+// box of k_block bytes x box_rows rows; both with the swizzle of span k_block.
+cudaError_t encode_activation_map(CUtensorMap* map, const void* base, std::uint64_t c8, std::uint64_t height,
+                                  std::uint64_t width, std::uint32_t k_block, std::uint32_t box_w, std::uint32_t box_h);
+cudaError_t encode_weight_map(CUtensorMap* map, const void* base, std::uint64_t rows, std::uint64_t row_bytes,
+                              std::uint32_t k_block, std::uint32_t box_rows);
+cudaError_t direct_conv(const CUtensorMap& a_map, const CUtensorMap& b_map, const DirectConvArgs& args,
+                        cudaStream_t stream);
+int direct_conv_shared_bytes(int k_block, int n_tile, int n_tiles, int a_stages, int b_stages);
+constexpr int direct_conv_max_shared = 232448;
 
 // Diagnostics: one thread waits on an mbarrier that nothing arrives on, with the
 // kernels' bounded-wait loop and a limit of `limit_ns`, then sets bit 0 of
