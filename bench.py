@@ -69,6 +69,18 @@ def golden_digests() -> dict:
     return json.loads(GOLDEN.read_text()) if GOLDEN.exists() else {}
 
 
+INT8_PEAK = ROOT / "profiles" / "int8_peak_cublaslt.json"
+
+
+def int8_peak_tops(bf16: float, source: str) -> tuple[float, str]:
+    """The dense int8 rate measured on this pool (cuBLASLt int8 GEMM burst,
+    profiles/int8_peak_cublaslt.md), else twice the bf16 figure."""
+    if INT8_PEAK.exists():
+        data = json.loads(INT8_PEAK.read_text())
+        return data["int8_tops_burst"], f"measured: cuBLASLt int8 8192^3 burst ({INT8_PEAK.name})"
+    return 2.0 * bf16, f"2 x bf16 dense ({source} MEASURED_PEAKS bf16_tflops={bf16})"
+
+
 def peaks():
     if MEASURED_PEAKS.exists():
         data = json.loads(MEASURED_PEAKS.read_text())
@@ -364,9 +376,12 @@ def main():
                           "differing": int(group.sum(len(differing))), "differing_here": differing,
                           "unchecked": unchecked}}
 
-    # Roofline of the integer GEMM kernel and per-layer bounds.
+    # Roofline of the integer conv kernel and per-layer bounds. A layer's time is
+    # all of its kernels (activation quantisation or staging, the conv, and the
+    # gated fallback launches); its algorithmic bytes are the FP16 input once,
+    # the int8 weights once and the FP16 output once.
     hbm, bf16, source = peaks()
-    int8_peak = 2.0 * bf16  # B200's dense int8 rate is twice its dense bf16 rate
+    int8_peak, int8_source = int8_peak_tops(bf16, source)
     ridge = int8_peak * 1e12 / (hbm * 1e9)  # ops per byte
     kernel_ms: dict[str, float] = {}
     for segments in per_layer_segments:
@@ -377,25 +392,35 @@ def main():
         if total_ms else {}
     layer_rows = []
     tensor_ops = tensor_ms = all_ops = all_ms = 0.0
-    for layer, segments in zip(layers, per_layer_segments):
+    for layer, segments, yh in zip(layers, per_layer_segments, outputs):
         gemms = [seg for seg in segments if seg["kernel"] == "integer_conv"]
-        quants = [seg for seg in segments if seg["kernel"] == "stage_source"]
         if not gemms:
             continue
-        ms = sum(seg["ms"] for seg in gemms) / len(gemms)
-        q_ms = sum(seg["ms"] for seg in quants) / max(1, len(quants))
-        ops, bytes_ = gemms[0]["ops"], gemms[0]["bytes"]
-        bound = "tensor" if ops / bytes_ > ridge else "hbm"
-        tops = ops / (ms / 1000.0) / 1e12
-        gbs = bytes_ / (ms / 1000.0) / 1e9
-        layer_rows.append({"layer": layer.name, "conv_ms": round(ms, 4), "stage_ms": round(q_ms, 4),
-                           "conv_tops": round(tops, 1), "conv_gbs": round(gbs, 1), "bound": bound,
-                           "frac": round(tops / int8_peak if bound == "tensor" else gbs / hbm, 3)})
-        all_ops += ops * len(gemms)
-        all_ms += ms * len(gemms)
+        runs = len(gemms)
+        conv_ms = sum(seg["ms"] for seg in gemms) / runs
+        prep_ms = sum(seg["ms"] for seg in segments if seg["kernel"] in ("quantise", "stage_source")) / runs
+        fallback_ms = sum(seg["ms"] for seg in segments if seg["kernel"] == "fallback") / runs
+        layer_ms = conv_ms + prep_ms + fallback_ms
+        ops = gemms[0]["ops"]
+        cin, h, w = layer.input_shape
+        pointwise = [n for n in layer.program.nodes if n.kind.name == "conv"][0]  # K = cin * taps inputs
+        algorithmic = 2.0 * cin * h * w + pointwise.in_channels * pointwise.out_channels + 2.0 * yh.numel()
+        bound = "tensor" if ops / algorithmic > ridge else "hbm"
+        conv_tops = ops / (conv_ms / 1000.0) / 1e12
+        layer_tops = ops / (layer_ms / 1000.0) / 1e12
+        layer_gbs = algorithmic / (layer_ms / 1000.0) / 1e9
+        layer_rows.append({"layer": layer.name, "conv_ms": round(conv_ms, 4), "prep_ms": round(prep_ms, 4),
+                           "fallback_ms": round(fallback_ms, 4), "layer_ms": round(layer_ms, 4),
+                           "conv_tops": round(conv_tops, 1), "layer_tops": round(layer_tops, 1),
+                           "algorithmic_bytes": algorithmic, "layer_gbs": round(layer_gbs, 1), "bound": bound,
+                           "frac": round(conv_tops / int8_peak if bound == "tensor" else layer_gbs / hbm, 3),
+                           "frac_basis": ("conv kernel ops / int8 peak" if bound == "tensor"
+                                          else "whole-layer algorithmic bytes / HBM peak")})
+        all_ops += ops
+        all_ms += conv_ms
         if bound == "tensor":
-            tensor_ops += ops * len(gemms)
-            tensor_ms += ms * len(gemms)
+            tensor_ops += ops
+            tensor_ms += conv_ms
     if tensor_ms > 0:
         achieved = tensor_ops / (tensor_ms / 1000.0) / 1e12
     else:
@@ -406,8 +431,8 @@ def main():
         traffic = json.loads(traffic_file.read_text()).get("bytes_per_launch")
     roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(int8_peak, 1), "unit": "TOPS",
                 "frac": round(achieved / int8_peak, 4), "traffic": traffic,
-                "kernel": "integer_conv: fused quantise-on-load tcgen05 kind::i8 implicit GEMM, tensor-bound layers",
-                "peak_source": f"2 x bf16 dense ({source} MEASURED_PEAKS bf16_tflops={bf16})",
+                "kernel": "integer_conv on the tensor-bound layers (L4, L5): tcgen05 kind::i8 implicit GEMM",
+                "peak_source": int8_source,
                 "time_share": shares,
                 "layers": layer_rows}
 

@@ -753,9 +753,12 @@ Status Executor::prepare_direct(IntegerConv& conv, const Step& step, const Node&
     const int n_padded = conv.n_tiles * conv.n_tile;
     // Ring depths: resident weights when one N tile's K blocks fit, else the
     // deepest rings that fit.
+    // Small stages (short K blocks, narrow N) take deeper rings: a stage in
+    // flight hides one TMA round trip, which costs far more than the few MMAs
+    // of such a stage.
     bool fits = false;
-    if (conv.n_tiles == 1 && conv.direct_k_blocks <= 8) {
-        for (const int a_stages : {6, 4, 3, 2}) {
+    if (conv.n_tiles == 1 && conv.direct_k_blocks <= 16) {
+        for (const int a_stages : {16, 12, 8, 6, 4, 3, 2}) {
             if (kernels::direct_conv_shared_bytes(conv.k_block, conv.n_tile, conv.n_tiles, a_stages,
                                                   conv.direct_k_blocks) <= kernels::direct_conv_max_shared) {
                 conv.direct_a_stages = a_stages;
@@ -767,7 +770,8 @@ Status Executor::prepare_direct(IntegerConv& conv, const Step& step, const Node&
         }
     }
     if (!fits) {
-        constexpr int depths[][2] = {{6, 6}, {4, 6}, {6, 4}, {4, 4}, {4, 3}, {3, 3}, {3, 2}, {2, 2}};
+        constexpr int depths[][2] = {{16, 16}, {12, 12}, {8, 8}, {6, 6}, {4, 6}, {6, 4},
+                                     {4, 4}, {4, 3}, {3, 3}, {3, 2}, {2, 2}};
         for (const auto& depth : depths) {
             if (kernels::direct_conv_shared_bytes(conv.k_block, conv.n_tile, conv.n_tiles, depth[0], depth[1]) <=
                 kernels::direct_conv_max_shared) {

@@ -52,7 +52,7 @@ constexpr int epilogue_threads = epilogue_warps * 32;
 constexpr int weight_warp = 12;
 constexpr int mma_warp = 13;
 constexpr int activation_warp = 14;
-constexpr int max_direct_stages = 8;
+constexpr int max_direct_stages = 16;
 constexpr float round_magic = 12582912.0f;  // 1.5 * 2^23
 
 struct DirectTail {
@@ -570,6 +570,7 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
             // non-zero pixel whose exponent differs from the largest marks the
             // window as mixed.
             int exponent = INT_MIN;
+            bool mixed = false;  // the fallback conv writes this position
             if (real) {
                 float largest = 0.0f;
                 float smallest = __uint_as_float(0x7f800000u);  // smallest non-zero
@@ -588,12 +589,15 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
                 }
                 if (largest != __uint_as_float(0x7f800000u)) {
                     exponent = activation_exponent(largest, 8);
-                    if (a.fallback != nullptr && largest > 0.0f && part == 0 &&
-                        frexp_exponent(smallest) != frexp_exponent(largest)) {
-                        atomicOr(a.fallback, 1u);
-                    }
+                    mixed = a.fallback != nullptr && largest > 0.0f &&
+                        frexp_exponent(smallest) != frexp_exponent(largest);
+                    if (mixed && part == 0) atomicOr(a.fallback, 1u);
                 }
             }
+            // A mixed window's accumulators are not this position's result:
+            // nothing is stored for it (nor added to a staged maximum, which
+            // can only grow), and the fallback conv writes it instead.
+            const bool store = real && !mixed;
             const int buffer = local % tmem_buffers;
             const std::uint32_t use = static_cast<std::uint32_t>(local / tmem_buffers);
             bool waited = *abort == 0 && barrier_wait(smem_address(&tail->tmem_full[buffer]), use & 1u, a.status);
@@ -669,7 +673,7 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
                 }
                 const int c0 = logical0 + j0;
                 const int count = a.out_channels - c0 < 16 ? a.out_channels - c0 : 16;
-                if (real) {
+                if (store) {
                     if (exponent == INT_MIN) {
 #pragma unroll
                         for (int j = 0; j < 16; ++j) v[j] = canonical_nan();
@@ -766,7 +770,7 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
                 }
                 __syncwarp();  // tcgen05.ld is warp-aligned: reconverge before the next columns
             }
-            if (a.out_max != nullptr && real && first_column < last_column) {
+            if (a.out_max != nullptr && store && first_column < last_column) {
                 atomicMax(reinterpret_cast<unsigned int*>(a.out_max) + p,
                           __float_as_uint(max_from_magnitude_bits(staged_max)));
             }
