@@ -20,15 +20,17 @@
 //       bytes x patch_w x patch_h pixels, shifted by the tap; the image border
 //       and padding taps come back as the TMA's zero fill), already in the
 //       swizzled K-major layout the MMA reads. No thread touches an activation.
-//       The epilogue threads compute each position's exponent from the window's
-//       pixel maxima; a window whose non-zero pixels have different exponents
-//       sets the fallback word, and the quantise-on-load conv (k_conv.cu),
-//       gated on that word, then recomputes the whole conv.
+//       One warp computes each position's exponent from the window's pixel
+//       maxima, tiles ahead of the epilogue; a window whose non-zero pixels have
+//       different exponents sets the fallback word, and the quantise-on-load
+//       conv (k_conv.cu), gated on that word, then recomputes the whole conv.
 //
-// Warp roles (15 warps, 128 registers each): warps 0-11 epilogue (three per
-// TMEM lane quarter, each a third of the tile's 16-column chunks), warp 12 the
-// weight TMA, warp 13 TMEM allocation and the MMA issue (one thread), warp 14
-// the activation TMA. Accumulators are double-buffered in TMEM when they fit.
+// Warp roles (16 warps, 128 registers each): warps 0-11 epilogue (three groups
+// of four, one warp per TMEM lane quarter; the groups take alternate tiles when
+// four or more accumulator buffers fit, else a third of every tile's 16-column
+// chunks each), warp 12 the weight TMA, warp 13 TMEM allocation and the MMA
+// issue (one thread), warp 14 the activation TMA, warp 15 the window exponents.
+// Accumulators take as many TMEM buffers as fit (2 to 8).
 // Every wait is bounded (about 2 s of the global timer); after a timeout the
 // CTA sets bit 0 of the status word, stops issuing, drains its MMAs and TMA
 // loads, frees its TMEM and returns. No multicast load is used.
@@ -45,23 +47,34 @@
 namespace nvcr_sm100::kernels {
 namespace {
 
-constexpr int direct_warps = 15;
+constexpr int direct_warps = 16;
 constexpr int direct_threads = direct_warps * 32;
 constexpr int epilogue_warps = 12;
 constexpr int epilogue_threads = epilogue_warps * 32;
 constexpr int weight_warp = 12;
 constexpr int mma_warp = 13;
 constexpr int activation_warp = 14;
+constexpr int window_warp = 15;
+constexpr int window_slots = 6;  // tiles whose halo of pixel maxima is staged ahead
 constexpr int max_direct_stages = 16;
+constexpr int max_tmem_buffers = 8;
 constexpr float round_magic = 12582912.0f;  // 1.5 * 2^23
+
+// Epilogue groups: with four or more accumulator buffers the three groups of
+// four warps (each covering the 128 TMEM lanes) take alternate tiles, all
+// columns each, so three tiles' epilogues run at once; with fewer, the three
+// take every tile, a third of its 16-column chunks each.
+__host__ __device__ constexpr int epilogue_groups(int tmem_buffers) { return tmem_buffers >= 4 ? 3 : 1; }
 
 struct DirectTail {
     unsigned long long full_a[max_direct_stages];
     unsigned long long empty_a[max_direct_stages];
     unsigned long long full_b[max_direct_stages];
     unsigned long long empty_b[max_direct_stages];
-    unsigned long long tmem_full[2];
-    unsigned long long tmem_empty[2];
+    unsigned long long tmem_full[max_tmem_buffers];
+    unsigned long long tmem_empty[max_tmem_buffers];
+    unsigned long long window_full[window_slots];
+    unsigned long long window_empty[window_slots];
     unsigned long long drain;
     std::uint32_t tmem_base;
     int abort;
@@ -82,6 +95,26 @@ __device__ __forceinline__ std::uint64_t swizzled_descriptor(std::uint32_t addre
 __host__ __device__ constexpr int column_bytes(int columns) { return columns * 8; }
 
 __host__ __device__ constexpr int tail_bytes() { return static_cast<int>((sizeof(DirectTail) + 15) / 16 * 16); }
+
+// The window warp stages each tile's halo of pixel maxima ((patch_h + 2) x
+// (patch_w + 2) at most: 390 floats for a 1 x 128 patch) in one of
+// window_slots slots, that many tiles ahead.
+constexpr int halo_slot_floats = 400;
+constexpr int halo_lane_items = (halo_slot_floats + 31) / 32;
+__host__ __device__ constexpr int halo_ring_bytes() { return window_slots * halo_slot_floats * 4; }
+
+__device__ __forceinline__ void cp_async4(std::uint32_t dst, const void* src, int src_bytes) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+// An arrival on the mbarrier once all of this thread's earlier cp.async copies
+// have landed (the barrier's count includes it).
+__device__ __forceinline__ void cp_async_arrive(std::uint32_t bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Exponent of a window with a non-finite value: the row is NaN.
+constexpr int window_nan = INT_MIN;
 
 // ---------------------------------------------------------------- prepass
 
@@ -240,6 +273,329 @@ __global__ void __launch_bounds__(256) quantise_staged_kernel(const float* __res
 
 constexpr int max_field_values = 64;
 
+// NCHW planes (FP16 or FP32) -> per-pixel int8, for planes whose length is a
+// multiple of one 16-byte vector. A block takes 256 bytes of every plane (128
+// FP16 or 64 FP32 pixels): each thread keeps eight 16-byte loads in flight, and
+// vector v of channel c goes to shared slot v ^ ((c / 16) mod 16), so the
+// threads that later read sixteen channels of one pixel, or one channel of 32
+// pixels, hit different banks. Each pixel's record is then stored as
+// consecutive 16-byte pieces: a block writes one contiguous run.
+template <bool Half>
+__global__ void __launch_bounds__(256) quantise_planes_wide_kernel(const void* __restrict__ in, int channels, int c8,
+                                                                   int pixels, std::int8_t* __restrict__ out,
+                                                                   float* __restrict__ pixel_max,
+                                                                   unsigned int* __restrict__ clear_word) {
+    constexpr int element = Half ? 2 : 4;
+    constexpr int block_pixels = 256 / element;
+    constexpr int per_vector = 16 / element;
+    constexpr int threads_per_pixel = 256 / block_pixels;
+    grid_dependency_wait();
+    launch_dependents();
+    if (clear_word != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *clear_word = 0u;
+    extern __shared__ uint4 planes[];  // [channels][16] swizzled vectors
+    __shared__ std::uint32_t partial[threads_per_pixel][block_pixels];
+    __shared__ float maxima[block_pixels];
+    const long long first = static_cast<long long>(blockIdx.x) * block_pixels;
+    const int valid = static_cast<int>(pixels - first < block_pixels ? pixels - first : block_pixels);
+    const int valid_vectors = valid / per_vector;
+    const long long plane_vectors = pixels / per_vector;
+    const uint4* source = reinterpret_cast<const uint4*>(in) + first / per_vector;
+    const int items = channels * 16;
+    for (int base = threadIdx.x; base < items; base += 256 * 8) {
+        uint4 r[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = base + u * 256;
+            const int c = i >> 4;
+            const int v = i & 15;
+            r[u] = make_uint4(0u, 0u, 0u, 0u);
+            if (i < items && v < valid_vectors) r[u] = __ldg(source + c * plane_vectors + v);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = base + u * 256;
+            const int c = i >> 4;
+            if (i < items) planes[c * 16 + ((i & 15) ^ (c >> 4 & 15))] = r[u];
+        }
+    }
+    __syncthreads();
+    // Element (c, p) of the swizzled tile, as magnitude bits (FP16 bits for Half).
+    auto element_at = [&](int c, int p) -> std::uint32_t {
+        const int slot = c * 16 + ((p / per_vector) ^ (c >> 4 & 15));
+        if constexpr (Half) {
+            return reinterpret_cast<const std::uint16_t*>(planes + slot)[p % per_vector];
+        } else {
+            return reinterpret_cast<const std::uint32_t*>(planes + slot)[p % per_vector];
+        }
+    };
+    {
+        const int p = threadIdx.x % block_pixels;
+        const int part = threadIdx.x / block_pixels;
+        std::uint32_t m = 0;
+        for (int c = part; c < channels; c += threads_per_pixel) {
+            m = max(m, element_at(c, p) & (Half ? 0x7fffu : 0x7fffffffu));
+        }
+        partial[part][p] = m;
+    }
+    __syncthreads();
+    if (threadIdx.x < block_pixels) {
+        const int p = threadIdx.x;
+        std::uint32_t m = partial[0][p];
+#pragma unroll
+        for (int k = 1; k < threads_per_pixel; ++k) m = max(m, partial[k][p]);
+        float maximum;
+        if constexpr (Half) {
+            maximum = m >= 0x7c00u ? __uint_as_float(0x7f800000u) : __half2float(__ushort_as_half(static_cast<unsigned short>(m)));
+        } else {
+            maximum = max_from_magnitude_bits(m);
+        }
+        maxima[p] = maximum;
+        if (p < valid) pixel_max[first + p] = maximum;
+    }
+    __syncthreads();
+    const int pieces = c8 / 16;
+    uint4* target = reinterpret_cast<uint4*>(out + first * c8);
+    for (int item = threadIdx.x; item < valid * pieces; item += 256) {
+        const int p = item / pieces;
+        const int c0 = (item - p * pieces) * 16;
+        const PixelScale s = pixel_scale(maxima[p]);
+        int q[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int c = c0 + j;
+            float x = 0.0f;
+            if (c < channels) {
+                const std::uint32_t bits = element_at(c, p);
+                if constexpr (Half) {
+                    x = __half2float(__ushort_as_half(static_cast<unsigned short>(bits)));
+                } else {
+                    x = __uint_as_float(bits);
+                }
+            }
+            q[j] = (c < channels && s.finite) ? quantise_one(x, s.normal, s.scale, s.exponent) : 0;
+        }
+        target[item] = pack16(q);
+    }
+}
+
+// FP16 NCHW planes -> per-pixel int8, for up to 256 channels (c8 <= 256) and
+// planes whose length is a multiple of 8. Thread (sub-tile s, channel group
+// cg, vector v) holds channels 16 cg .. 16 cg + 15 of pixels 8 v .. 8 v + 7 of
+// its 128-pixel sub-tile in registers (one 16-byte load per channel; the 16
+// threads of a group read 256 contiguous bytes of a plane). Per-pixel maxima
+// are magnitude bits reduced two pixels to a word, then across the channel
+// groups through shared memory. Quantisation, for a pixel whose 2^-e is a
+// normal half and whose max * 2^-e < 127.5: fma.rn.f16x2(x, 2^-e, 1536) per
+// pixel pair of one channel. x * 2^-e is exact and |x * 2^-e| < 127.5, so the
+// single rounding of the sum lands in [1024, 2048), where halves are the
+// integers and rounding to nearest-even is rint; the low byte of each half is
+// then rint(x * 2^-e) and no clamp can act. Other pixels (non-finite ones
+// write zeros) take the float path. Byte permutes turn the per-channel words
+// into per-pixel records, stored as one 16-byte piece per pixel and group.
+constexpr int half_planes_max_c8 = 256;
+
+__device__ __forceinline__ std::uint32_t hfma2_bits(std::uint32_t x, std::uint32_t s, std::uint32_t c) {
+    std::uint32_t r;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(x), "r"(s), "r"(c));
+    return r;
+}
+
+__device__ __forceinline__ std::uint32_t byte_perm(std::uint32_t a, std::uint32_t b, std::uint32_t selector) {
+    return __byte_perm(a, b, selector);
+}
+
+__device__ __forceinline__ std::uint32_t word_of(const uint4& v, int w) {
+    return w == 0 ? v.x : (w == 1 ? v.y : (w == 2 ? v.z : v.w));
+}
+
+__global__ void __launch_bounds__(256) quantise_half_planes_kernel(const __half* __restrict__ in, int channels,
+                                                                   int c8, int pixels, int sub_tiles,
+                                                                   std::int8_t* __restrict__ out,
+                                                                   float* __restrict__ pixel_max,
+                                                                   unsigned int* __restrict__ clear_word) {
+    grid_dependency_wait();
+    launch_dependents();
+    if (clear_word != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *clear_word = 0u;
+    extern __shared__ uint4 group_maxima[];  // [sub_tiles][groups][16]
+    const int groups = c8 / 16;
+    const int per_tile = 16 * groups;
+    const int s = static_cast<int>(threadIdx.x) / per_tile;
+    const int r = static_cast<int>(threadIdx.x) - s * per_tile;
+    const int cg = r >> 4;
+    const int v = r & 15;
+    const long long p0 = (static_cast<long long>(blockIdx.x) * sub_tiles + s) * 128 + v * 8;
+    const bool live = p0 < pixels;
+    uint4 x[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        const int c = cg * 16 + j;
+        x[j] = make_uint4(0u, 0u, 0u, 0u);
+        if (live && c < channels) x[j] = __ldg(reinterpret_cast<const uint4*>(in + static_cast<std::size_t>(c) * pixels + p0));
+    }
+    std::uint32_t m[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+#pragma unroll
+        for (int w = 0; w < 4; ++w) m[w] = __vmaxu2(m[w], word_of(x[j], w) & 0x7fff7fffu);
+    }
+    group_maxima[(s * groups + cg) * 16 + v] = make_uint4(m[0], m[1], m[2], m[3]);
+    __syncthreads();
+    if (!live) return;
+    for (int g = 0; g < groups; ++g) {
+        const uint4 q = group_maxima[(s * groups + g) * 16 + v];
+        m[0] = __vmaxu2(m[0], q.x);
+        m[1] = __vmaxu2(m[1], q.y);
+        m[2] = __vmaxu2(m[2], q.z);
+        m[3] = __vmaxu2(m[3], q.w);
+    }
+    float maxima[8];
+    std::uint32_t scale_bits[4] = {0u, 0u, 0u, 0u};  // 2^-e of pixels 2w, 2w + 1 as a half pair
+    std::uint32_t slow = 0;                          // bit p: pixel p takes the float path
+#pragma unroll
+    for (int p = 0; p < 8; ++p) {
+        const std::uint32_t magnitude = (m[p >> 1] >> (16 * (p & 1))) & 0xffffu;
+        const bool finite = magnitude < 0x7c00u;
+        const float maximum = finite ? __half2float(__ushort_as_half(static_cast<unsigned short>(magnitude)))
+                                     : __uint_as_float(0x7f800000u);
+        maxima[p] = maximum;
+        const int e = activation_exponent(maximum, 8);
+        const bool fast = finite && e >= -15 && e <= 14 && __fmul_rn(maximum, power_of_two(-e)) < 127.5f;
+        slow |= fast ? 0u : 1u << p;
+        scale_bits[p >> 1] |= (fast ? static_cast<std::uint32_t>(15 - e) << 10 : 0u) << (16 * (p & 1));
+    }
+    if (cg == 0) {
+        float4* target = reinterpret_cast<float4*>(pixel_max + p0);
+        target[0] = make_float4(maxima[0], maxima[1], maxima[2], maxima[3]);
+        target[1] = make_float4(maxima[4], maxima[5], maxima[6], maxima[7]);
+    }
+    constexpr std::uint32_t magic = 0x66006600u;  // 1536 in both halves
+    std::int8_t* row = out + p0 * c8 + cg * 16;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        std::uint32_t even[4], odd[4];  // records of pixels 2w and 2w + 1, channels 4k .. 4k + 3 in word k
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const std::uint32_t r0 = hfma2_bits(word_of(x[4 * k], w), scale_bits[w], magic);
+            const std::uint32_t r1 = hfma2_bits(word_of(x[4 * k + 1], w), scale_bits[w], magic);
+            const std::uint32_t r2 = hfma2_bits(word_of(x[4 * k + 2], w), scale_bits[w], magic);
+            const std::uint32_t r3 = hfma2_bits(word_of(x[4 * k + 3], w), scale_bits[w], magic);
+            const std::uint32_t lo = byte_perm(r0, r1, 0x6240u);  // r0.b0 r1.b0 r0.b2 r1.b2
+            const std::uint32_t hi = byte_perm(r2, r3, 0x6240u);
+            even[k] = byte_perm(lo, hi, 0x5410u);
+            odd[k] = byte_perm(lo, hi, 0x7632u);
+        }
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int p = 2 * w + e;
+            std::uint32_t* words = e == 0 ? even : odd;
+            if ((slow >> p) & 1u) {
+                const PixelScale sc = pixel_scale(maxima[p]);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    std::uint32_t word = 0;
+#pragma unroll
+                    for (int b = 0; b < 4; ++b) {
+                        const std::uint32_t bits = (word_of(x[4 * k + b], w) >> (16 * e)) & 0xffffu;
+                        const float value = __half2float(__ushort_as_half(static_cast<unsigned short>(bits)));
+                        const int q = sc.finite ? quantise_one(value, sc.normal, sc.scale, sc.exponent) : 0;
+                        word |= (static_cast<std::uint32_t>(q) & 0xffu) << (8 * b);
+                    }
+                    words[k] = word;
+                }
+            }
+            *reinterpret_cast<uint4*>(row + static_cast<std::size_t>(p) * c8) =
+                make_uint4(words[0], words[1], words[2], words[3]);
+        }
+    }
+}
+
+constexpr int field_run = 128;  // output positions per block of the row-staged field prepass
+
+// Receptive fields of a run of 128 output positions of one output row: the
+// block first copies the input rows the run's windows cover ([channels]
+// [kernel_h][span] floats, zero outside the image) with coalesced loads, then
+// each thread builds its position's field from shared memory through a table
+// of offsets (k = c * taps + tap, -1 past channels * taps), its max |x|, and the
+// field quantised with its own exponent into C8 bytes.
+template <bool Half, int C8>
+__global__ void __launch_bounds__(field_run) quantise_fields_rows_kernel(const void* __restrict__ in, int channels,
+                                                                         int in_h, int in_w, Window w, int out_h,
+                                                                         int out_w, int span,
+                                                                         std::int8_t* __restrict__ out,
+                                                                         float* __restrict__ field_max) {
+    grid_dependency_wait();
+    launch_dependents();
+    extern __shared__ float rows[];  // [channels * kernel_h][span]
+    __shared__ int offset_of[C8];
+    const int kh = w.kernel_h;
+    const int kw = w.kernel_w;
+    const int taps = kh * kw;
+    const int oy = blockIdx.y;
+    const int ox0 = blockIdx.x * field_run;
+    const int iy0 = oy * w.stride_y - w.pad_top;
+    const int ix0 = ox0 * w.stride_x - w.pad_left;
+    for (int k = threadIdx.x; k < C8; k += field_run) {
+        const int c = k / taps;
+        const int tap = k - c * taps;
+        const int ky = tap / kw;
+        offset_of[k] = k < channels * taps ? (c * kh + ky) * span + (tap - ky * kw) : -1;
+    }
+    // Columns of this thread in every staged row (span <= 4 * field_run).
+    int column[4];
+    bool column_inside[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        column[u] = static_cast<int>(threadIdx.x) + u * field_run;
+        const int ix = ix0 + column[u];
+        column_inside[u] = column[u] < span && ix >= 0 && ix < in_w;
+    }
+    const unsigned plane = static_cast<unsigned>(in_h) * static_cast<unsigned>(in_w);
+    for (int rc = 0; rc < channels * kh; ++rc) {
+        const int c = rc / kh;
+        const int iy = iy0 + (rc - c * kh);
+        const bool row_inside = iy >= 0 && iy < in_h;
+        const unsigned row_at = static_cast<unsigned>(c) * plane + static_cast<unsigned>(row_inside ? iy : 0) * in_w +
+            static_cast<unsigned>(ix0);
+        float v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            v[u] = 0.0f;
+            if (row_inside && column_inside[u]) {
+                const unsigned at = row_at + static_cast<unsigned>(column[u]);
+                v[u] = Half ? __half2float(static_cast<const __half*>(in)[at]) : static_cast<const float*>(in)[at];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            if (column[u] < span) rows[rc * span + column[u]] = v[u];
+        }
+    }
+    __syncthreads();
+    const int ox = ox0 + static_cast<int>(threadIdx.x);
+    if (ox >= out_w) return;
+    const int col0 = static_cast<int>(threadIdx.x) * w.stride_x;
+    float v[C8];
+    std::uint32_t m = 0;
+#pragma unroll
+    for (int k = 0; k < C8; ++k) {
+        const int at = offset_of[k];
+        v[k] = at >= 0 ? rows[at + col0] : 0.0f;
+        m = max(m, magnitude_bits_of(v[k]));
+    }
+    const float maximum = max_from_magnitude_bits(m);
+    const long long position = static_cast<long long>(oy) * out_w + ox;
+    field_max[position] = maximum;
+    const PixelScale sc = pixel_scale(maximum);
+    uint4* record = reinterpret_cast<uint4*>(out + position * C8);
+#pragma unroll
+    for (int k0 = 0; k0 < C8; k0 += 16) {
+        int q[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) q[j] = sc.finite ? quantise_one(v[k0 + j], sc.normal, sc.scale, sc.exponent) : 0;
+        record[k0 / 16] = pack16(q);
+    }
+}
+
 // One thread per output position: its receptive field in k = c * taps + tap
 // order (padding taps and k past channels * taps zero), the field's max |x|,
 // and the field quantised with its own exponent into c8 bytes.
@@ -352,6 +708,58 @@ __device__ __noinline__ Sixteen16 direct_wsilu16(Sixteen16 x, float k) {
     return x;
 }
 
+// One warp issues the TMA copies of a ring of `ring` stages (ring <= 32): lane
+// j owns stage j and issues items j, j + ring, j + 2 ring, ... of the sequence as
+// soon as its stage is free (the empty barrier's previous phase completed). A
+// copy instruction occupies the issuing warp for hundreds of cycles whatever
+// the number of lanes that carry a copy in it, so the lanes whose stages came
+// free issue together. `issue(item, stage)` arms the full barrier and starts
+// the copy. After an abort or a wait that runs out (status bit 0, abort set),
+// each lane waits, bounded, for its last copy to land and the warp returns.
+template <typename Issue>
+__device__ __forceinline__ void ring_issue(int lane, int ring, int items, std::uint32_t empty_base,
+                                           std::uint32_t full_base, volatile int* abort, unsigned int* status,
+                                           Issue issue) {
+    const bool owner = lane < ring;
+    int item = lane;
+    bool failed = false;
+    unsigned long long since = global_timer();
+    for (unsigned int spin = 0;; ++spin) {
+        const bool pending = owner && item < items && !failed;
+        if (!__any_sync(0xffffffffu, pending)) break;
+        const std::uint32_t phase = static_cast<std::uint32_t>(item / ring) & 1u;
+        const std::uint32_t empty = empty_base + 8u * static_cast<std::uint32_t>(lane);
+        const bool ready = pending && barrier_test_wait(empty, phase ^ 1u);
+        if (__any_sync(0xffffffffu, ready)) {
+            if (ready) {
+                issue(item, lane);
+                item += ring;
+                since = global_timer();
+            }
+            continue;
+        }
+        // No stage is free: the lane whose item comes next (stages free in
+        // order) sleeps on its stage, then every lane tests again.
+        const int next = __reduce_min_sync(0xffffffffu, pending ? item : INT_MAX);
+        if (pending && item == next) barrier_try_wait_hint(empty, phase ^ 1u, 20000u);
+        if (pending && (spin & 15u) == 15u) {
+            if (*abort) {
+                failed = true;
+            } else if (global_timer() - since > wait_limit_ns) {
+                atomicOr(status, 1u);
+                *abort = 1;
+                failed = true;
+            }
+        }
+    }
+    if (failed && item >= ring) {
+        const int last = item - ring;
+        barrier_sleep_wait(full_base + 8u * static_cast<std::uint32_t>(lane), static_cast<std::uint32_t>(last / ring) & 1u,
+                     status);
+    }
+    __syncwarp();
+}
+
 __global__ void __launch_bounds__(direct_threads, 1)
 direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map,
                    DirectConvArgs a, int tmem_buffers, std::uint32_t tmem_columns) {
@@ -362,12 +770,14 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
     const int k_block = a.k_block;
     const int a_stage_bytes = tile_positions_m * k_block;
     const int b_stage_bytes = n_tile * k_block;
-    // Shared memory: [A stages][B stages][tail][column parameters]; stage sizes are
-    // multiples of 1024 bytes, so every stage keeps the 1 KiB swizzle alignment.
+    // Shared memory: [A stages][B stages][tail][halo ring][column parameters];
+    // stage sizes are multiples of 1024 bytes, so every stage keeps the 1 KiB
+    // swizzle alignment.
     std::uint8_t* b_smem = smem + a.a_stages * a_stage_bytes;
     auto* tail = reinterpret_cast<DirectTail*>(b_smem + a.b_stages * b_stage_bytes);
     const int all_columns = a.n_tiles * n_tile;
-    float* column_scale = reinterpret_cast<float*>(reinterpret_cast<std::uint8_t*>(tail) + tail_bytes());
+    float* halo_maxima = reinterpret_cast<float*>(reinterpret_cast<std::uint8_t*>(tail) + tail_bytes());
+    float* column_scale = reinterpret_cast<float*>(reinterpret_cast<std::uint8_t*>(halo_maxima) + halo_ring_bytes());
     float* column_bias = column_scale + all_columns;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -395,9 +805,13 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
             barrier_init(smem_address(&tail->full_b[s]), 1);
             barrier_init(smem_address(&tail->empty_b[s]), 1);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < tmem_buffers; ++b) {
             barrier_init(smem_address(&tail->tmem_full[b]), 1);
-            barrier_init(smem_address(&tail->tmem_empty[b]), epilogue_threads);
+            barrier_init(smem_address(&tail->tmem_empty[b]), epilogue_threads / epilogue_groups(tmem_buffers));
+        }
+        for (int w = 0; w < window_slots; ++w) {
+            barrier_init(smem_address(&tail->window_full[w]), 32);
+            barrier_init(smem_address(&tail->window_empty[w]), epilogue_threads / epilogue_groups(tmem_buffers));
         }
         barrier_init(smem_address(&tail->drain), 1);
         tail->abort = 0;
@@ -413,83 +827,49 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
     launch_dependents();
     volatile int* abort = &tail->abort;
 
+    // Tiles of this CTA (t = blockIdx.x, blockIdx.x + gridDim.x, ...) and the
+    // (tile, K block) items of its A and B sequences.
+    const int my_tiles = total_tiles > static_cast<int>(blockIdx.x)
+        ? (total_tiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x)
+        : 0;
     if (warp == weight_warp) {
-        if (lane == 0) {
-            // ---------------- weights by TMA
-            const std::uint32_t bytes = static_cast<std::uint32_t>(b_stage_bytes);
-            std::uint32_t g = 0;
-            std::uint32_t issued = 0;
-            bool ok = true;
-            const int last = a.b_resident ? static_cast<int>(blockIdx.x) + 1 : total_tiles;
-            for (int t = blockIdx.x; t < last && ok; t += gridDim.x) {
-                int n_index;
-                by_n_tiles.divide(t, n_index);
-                const int n0 = n_index * n_tile;
-                for (int kb = 0; kb < k_blocks; ++kb, ++g) {
-                    const int s = static_cast<int>(g % a.b_stages);
-                    const std::uint32_t phase = (g / a.b_stages) & 1u;
-                    if (*abort || !barrier_wait(smem_address(&tail->empty_b[s]), phase ^ 1u, a.status)) {
-                        *abort = 1;
-                        ok = false;
-                        break;
-                    }
-                    const std::uint32_t full = smem_address(&tail->full_b[s]);
-                    barrier_expect_bytes(full, bytes);
-                    tma_load_2d(smem_address(b_smem + s * b_stage_bytes), &b_map, full, kb * k_block, n0);
-                    issued = g + 1;
-                }
-            }
-            if (!ok) {
-                const std::uint32_t first = issued > static_cast<std::uint32_t>(a.b_stages) ? issued - a.b_stages : 0;
-                for (std::uint32_t h = first; h < issued; ++h) {
-                    barrier_wait(smem_address(&tail->full_b[h % a.b_stages]), (h / a.b_stages) & 1u, a.status);
-                }
-            }
-        }
+        // ---------------- weights by TMA (resident weights: the first tile's K blocks, once)
+        const std::uint32_t bytes = static_cast<std::uint32_t>(b_stage_bytes);
+        const int items = a.b_resident ? (my_tiles > 0 ? k_blocks : 0) : my_tiles * k_blocks;
+        ring_issue(lane, a.b_stages, items, smem_address(&tail->empty_b[0]), smem_address(&tail->full_b[0]), abort,
+                   a.status, [&](int item, int stage) {
+                       const int local_tile = item / k_blocks;
+                       const int kb = item - local_tile * k_blocks;
+                       int n_index;
+                       by_n_tiles.divide(static_cast<int>(blockIdx.x) + local_tile * static_cast<int>(gridDim.x),
+                                         n_index);
+                       const std::uint32_t full = smem_address(&tail->full_b[stage]);
+                       barrier_expect_bytes(full, bytes);
+                       tma_load_2d(smem_address(b_smem + stage * b_stage_bytes), &b_map, full, kb * k_block,
+                                   n_index * n_tile);
+                   });
     } else if (warp == activation_warp) {
+        // ---------------- activations by TMA: one box per (tap, channel block)
         grid_dependency_wait();
-        if (lane == 0) {
-            // ---------------- activations by TMA: one box per (tap, channel block)
-            const std::uint32_t bytes = static_cast<std::uint32_t>(a_stage_bytes);
-            std::uint32_t g = 0;
-            std::uint32_t issued = 0;
-            bool ok = true;
-            for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-                int n_index, tx;
-                const int p_tile = by_n_tiles.divide(t, n_index);
-                const int ty = by_tiles_x.divide(p_tile, tx);
-                const int y0 = ty * a.patch_h - a.window.pad_top;
-                const int x0 = tx * a.patch_w - a.window.pad_left;
-                int ky = 0, kx = 0, cb = 0;
-                for (int kb = 0; kb < k_blocks; ++kb, ++g) {
-                    const int s = static_cast<int>(g % a.a_stages);
-                    const std::uint32_t phase = (g / a.a_stages) & 1u;
-                    if (*abort || !barrier_wait(smem_address(&tail->empty_a[s]), phase ^ 1u, a.status)) {
-                        *abort = 1;
-                        ok = false;
-                        break;
-                    }
-                    const std::uint32_t full = smem_address(&tail->full_a[s]);
-                    barrier_expect_bytes(full, bytes);
-                    // Innermost coordinate: the channel block's first byte, a multiple of k_block.
-                    tma_load_3d(smem_address(smem + s * a_stage_bytes), &a_map, full, cb * k_block, x0 + kx, y0 + ky);
-                    issued = g + 1;
-                    if (++cb == a.c_blocks) {
-                        cb = 0;
-                        if (++kx == a.window.kernel_w) {
-                            kx = 0;
-                            ++ky;
-                        }
-                    }
-                }
-            }
-            if (!ok) {
-                const std::uint32_t first = issued > static_cast<std::uint32_t>(a.a_stages) ? issued - a.a_stages : 0;
-                for (std::uint32_t h = first; h < issued; ++h) {
-                    barrier_wait(smem_address(&tail->full_a[h % a.a_stages]), (h / a.a_stages) & 1u, a.status);
-                }
-            }
-        }
+        const std::uint32_t bytes = static_cast<std::uint32_t>(a_stage_bytes);
+        ring_issue(lane, a.a_stages, my_tiles * k_blocks, smem_address(&tail->empty_a[0]),
+                   smem_address(&tail->full_a[0]), abort, a.status, [&](int item, int stage) {
+                       const int local_tile = item / k_blocks;
+                       const int kb = item - local_tile * k_blocks;
+                       int n_unused, tx;
+                       const int p_tile = by_n_tiles.divide(
+                           static_cast<int>(blockIdx.x) + local_tile * static_cast<int>(gridDim.x), n_unused);
+                       const int ty = by_tiles_x.divide(p_tile, tx);
+                       const int tap = kb / a.c_blocks;
+                       const int cb = kb - tap * a.c_blocks;
+                       const int ky = tap / a.window.kernel_w;
+                       const int kx = tap - ky * a.window.kernel_w;
+                       const std::uint32_t full = smem_address(&tail->full_a[stage]);
+                       barrier_expect_bytes(full, bytes);
+                       // Innermost coordinate: the channel block's first byte, a multiple of k_block.
+                       tma_load_3d(smem_address(smem + stage * a_stage_bytes), &a_map, full, cb * k_block,
+                                   tx * a.patch_w - a.window.pad_left + kx, ty * a.patch_h - a.window.pad_top + ky);
+                   });
     } else if (warp == mma_warp) {
         if (lane == 0) {
             // ---------------- tensor-core issue
@@ -498,27 +878,28 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
             std::uint32_t g = 0;
             int local = 0;
             bool ok = true;
+            int sa = 0, sb_ring = 0;                   // ring stages of the next A and B blocks
+            std::uint32_t a_phase = 0, b_ring_phase = 0;
             for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++local) {
                 const int buffer = local % tmem_buffers;
                 const std::uint32_t use = static_cast<std::uint32_t>(local / tmem_buffers);
-                if (*abort || !barrier_wait(smem_address(&tail->tmem_empty[buffer]), (use & 1u) ^ 1u, a.status)) {
+                if (*abort || !barrier_sleep_wait(smem_address(&tail->tmem_empty[buffer]), (use & 1u) ^ 1u, a.status)) {
                     *abort = 1;
                     break;
                 }
                 tmem_fence_after();
                 const std::uint32_t acc = tmem + static_cast<std::uint32_t>(buffer * n_tile);
                 for (int kb = 0; kb < k_blocks; ++kb, ++g) {
-                    const int sa = static_cast<int>(g % a.a_stages);
-                    const std::uint32_t a_phase = (g / a.a_stages) & 1u;
-                    const int sb = a.b_resident ? kb : static_cast<int>(g % a.b_stages);
-                    const std::uint32_t b_phase = a.b_resident ? 0u : (g / a.b_stages) & 1u;
-                    if (*abort || !barrier_wait(smem_address(&tail->full_a[sa]), a_phase, a.status) ||
-                        !barrier_wait(smem_address(&tail->full_b[sb]), b_phase, a.status)) {
+                    const int sb = a.b_resident ? kb : sb_ring;
+                    const std::uint32_t b_phase = a.b_resident ? 0u : b_ring_phase;
+                    // (TMA writes are ordered before the MMA's reads by the full
+                    // barriers; only TMEM reuse needs a tcgen05 fence, above.)
+                    if (!barrier_sleep_wait(smem_address(&tail->full_a[sa]), a_phase, a.status) ||
+                        !barrier_sleep_wait(smem_address(&tail->full_b[sb]), b_phase, a.status)) {
                         *abort = 1;
                         ok = false;
                         break;
                     }
-                    tmem_fence_after();
                     const std::uint32_t a_base = smem_address(smem + sa * a_stage_bytes);
                     const std::uint32_t b_base = smem_address(b_smem + sb * b_stage_bytes);
                     for (int kk = 0; kk < steps; ++kk) {
@@ -529,24 +910,86 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
                     }
                     mma_commit(smem_address(&tail->empty_a[sa]));
                     if (!a.b_resident) mma_commit(smem_address(&tail->empty_b[sb]));
+                    if (++sa == a.a_stages) {
+                        sa = 0;
+                        a_phase ^= 1u;
+                    }
+                    if (++sb_ring == a.b_stages) {
+                        sb_ring = 0;
+                        b_ring_phase ^= 1u;
+                    }
                 }
                 if (!ok) break;
                 mma_commit(smem_address(&tail->tmem_full[buffer]));
             }
             mma_commit(smem_address(&tail->drain));
-            barrier_wait(smem_address(&tail->drain), 0u, a.status);
+            barrier_sleep_wait(smem_address(&tail->drain), 0u, a.status);
         }
+    } else if (warp == window_warp) {
+        // ---------------- halos of pixel maxima, up to window_slots tiles ahead
+        // Each tile's halo of pixel maxima is copied by cp.async into a shared
+        // slot (zero outside the image, which changes neither the largest maximum
+        // of a window nor its smallest non-zero one); every lane's copies complete
+        // the slot's full barrier by themselves, so this warp never waits for them.
+        grid_dependency_wait();
+        const int halo_h = a.patch_h + a.window.kernel_h - 1;
+        const int halo_w = a.patch_w + a.window.kernel_w - 1;
+        const int halo_count = halo_h * halo_w;
+        // This lane's halo elements i = lane + 32 j as (row, column) in the halo.
+        short2 at[halo_lane_items];
+        {
+            const TileDivider by_halo_w(halo_w);
+#pragma unroll
+            for (int j = 0; j < halo_lane_items; ++j) {
+                int hx;
+                const int hy = by_halo_w.divide(lane + 32 * j, hx);
+                at[j] = make_short2(static_cast<short>(hy), static_cast<short>(hx));
+            }
+        }
+        for (int l = 0; l < my_tiles; ++l) {
+            const int slot = l % window_slots;
+            const std::uint32_t phase = static_cast<std::uint32_t>(l / window_slots) & 1u;
+            const bool waited =
+                *abort == 0 && barrier_sleep_wait(smem_address(&tail->window_empty[slot]), phase ^ 1u, a.status);
+            if (!__all_sync(0xffffffffu, waited)) {
+                *abort = 1;
+                break;
+            }
+            int n_unused, tx;
+            const int p_tile =
+                by_n_tiles.divide(static_cast<int>(blockIdx.x) + l * static_cast<int>(gridDim.x), n_unused);
+            const int ty = by_tiles_x.divide(p_tile, tx);
+            const int iy0 = ty * a.patch_h - a.window.pad_top;
+            const int ix0 = tx * a.patch_w - a.window.pad_left;
+            float* halo = halo_maxima + slot * halo_slot_floats;
+#pragma unroll
+            for (int j = 0; j < halo_lane_items; ++j) {
+                const int i = lane + 32 * j;
+                if (i < halo_count) {
+                    const int iy = iy0 + at[j].x;
+                    const int ix = ix0 + at[j].y;
+                    const bool inside = iy >= 0 && iy < a.in_h && ix >= 0 && ix < a.in_w;
+                    cp_async4(smem_address(halo + i),
+                              a.pixel_max + (inside ? static_cast<std::size_t>(iy) * a.in_w + ix : 0), inside ? 4 : 0);
+                }
+            }
+            cp_async_arrive(smem_address(&tail->window_full[slot]));
+        }
+        cp_async_wait_all();
     } else if (warp < epilogue_warps) {
         // ---------------- epilogue: thread <-> TMEM lane <-> position
         grid_dependency_wait();
         const int quarter = warp & 3;
-        const int part = warp >> 2;  // third of the columns
+        const int groups = epilogue_groups(tmem_buffers);
+        const int group = warp >> 2;
+        const int part = groups == 3 ? 0 : group;  // column third (one group: all columns)
+        const int parts = 3 / groups;
         const int row = quarter * 32 + lane;
         const std::uint32_t lane_base = static_cast<std::uint32_t>(quarter * 32) << 16;
         const int pair_offset = a.chunk_add ? n_tile / 2 : 0;
         const int columns = a.chunk_add ? n_tile / 2 : n_tile;
         const int chunks = columns / 16;
-        const int per_part = (chunks + 2) / 3;
+        const int per_part = (chunks + parts - 1) / parts;
         const int first_column = min(part * per_part, chunks) * 16;
         const int last_column = min((part + 1) * per_part, chunks) * 16;
         const int b = a.d2s_block;
@@ -554,10 +997,14 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
         const int patch_x = row - patch_y * a.patch_w;
         const int out_w_full = a.out_w * (b > 0 ? b : 1);
         const int out_h_full = a.out_h * (b > 0 ? b : 1);
+        const int first_local = groups == 3 ? group : 0;
+        const int tile_step = groups * static_cast<int>(gridDim.x);
         const int kernel_h = a.window.kernel_h;
         const int kernel_w = a.window.kernel_w;
-        int local = 0;
-        for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+        const int halo_w = a.patch_w + kernel_w - 1;
+        int local = first_local;
+        for (int t = static_cast<int>(blockIdx.x) + first_local * static_cast<int>(gridDim.x); t < total_tiles;
+             t += tile_step, local += groups) {
             int n_index, tx;
             const int p_tile = by_n_tiles.divide(t, n_index);
             const int ty = by_tiles_x.divide(p_tile, tx);
@@ -565,34 +1012,42 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
             const int x = tx * a.patch_w + patch_x;
             const bool real = y < a.out_h && x < a.out_w;
             const int p = real ? y * a.out_w + x : 0;
-            // The window's exponent from its pixels' maxima (while the MMA runs):
-            // the largest maximum sets it; a non-finite pixel makes the row NaN; a
-            // non-zero pixel whose exponent differs from the largest marks the
-            // window as mixed.
-            int exponent = INT_MIN;
-            bool mixed = false;  // the fallback conv writes this position
-            if (real) {
-                float largest = 0.0f;
-                float smallest = __uint_as_float(0x7f800000u);  // smallest non-zero
-                const int iy0 = y - a.window.pad_top;
-                const int ix0 = x - a.window.pad_left;
-                for (int ky = 0; ky < kernel_h; ++ky) {
-                    const int iy = iy0 + ky;
-                    if (iy < 0 || iy >= a.in_h) continue;
-                    for (int kx = 0; kx < kernel_w; ++kx) {
-                        const int ix = ix0 + kx;
-                        if (ix < 0 || ix >= a.in_w) continue;
-                        const float m = __ldg(a.pixel_max + static_cast<std::size_t>(iy) * a.in_w + ix);
-                        largest = fmaxf(largest, m);
-                        if (m > 0.0f) smallest = fminf(smallest, m);
+            // This position's window from the tile's halo of pixel maxima: the
+            // largest maximum sets the exponent, a non-finite pixel makes the row
+            // NaN, and a non-zero pixel whose exponent differs from the largest
+            // marks the window as mixed (its result comes from the fallback).
+            const int slot = local % window_slots;
+            const bool ready = barrier_sleep_wait(smem_address(&tail->window_full[slot]),
+                                                  static_cast<std::uint32_t>(local / window_slots) & 1u, a.status);
+            if (!__all_sync(0xffffffffu, ready)) {
+                *abort = 1;
+                break;
+            }
+            float largest = 0.0f;
+            float smallest = __uint_as_float(0x7f800000u);  // smallest non-zero
+            {
+                const float* halo = halo_maxima + slot * halo_slot_floats + patch_y * halo_w + patch_x;
+#pragma unroll
+                for (int ky = 0; ky < 3; ++ky) {
+#pragma unroll
+                    for (int kx = 0; kx < 3; ++kx) {
+                        if (ky < kernel_h && kx < kernel_w) {
+                            const float m = halo[ky * halo_w + kx];
+                            largest = fmaxf(largest, m);
+                            if (m > 0.0f) smallest = fminf(smallest, m);
+                        }
                     }
                 }
-                if (largest != __uint_as_float(0x7f800000u)) {
-                    exponent = activation_exponent(largest, 8);
-                    mixed = a.fallback != nullptr && largest > 0.0f &&
-                        frexp_exponent(smallest) != frexp_exponent(largest);
-                    if (mixed && part == 0) atomicOr(a.fallback, 1u);
-                }
+            }
+            barrier_arrive(smem_address(&tail->window_empty[slot]));
+            int exponent = window_nan;
+            bool mixed = false;
+            if (real && largest != __uint_as_float(0x7f800000u)) {
+                exponent = activation_exponent(largest, 8);
+                mixed = largest > 0.0f && frexp_exponent(smallest) != frexp_exponent(largest);
+            }
+            if (a.fallback != nullptr && part == 0 && __any_sync(0xffffffffu, mixed) && lane == 0) {
+                atomicOr(a.fallback, 1u);
             }
             // A mixed window's accumulators are not this position's result:
             // nothing is stored for it (nor added to a staged maximum, which
@@ -600,7 +1055,7 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
             const bool store = real && !mixed;
             const int buffer = local % tmem_buffers;
             const std::uint32_t use = static_cast<std::uint32_t>(local / tmem_buffers);
-            bool waited = *abort == 0 && barrier_wait(smem_address(&tail->tmem_full[buffer]), use & 1u, a.status);
+            bool waited = *abort == 0 && barrier_sleep_wait(smem_address(&tail->tmem_full[buffer]), use & 1u, a.status);
             waited = __all_sync(0xffffffffu, waited);  // tcgen05.ld is warp-aligned
             if (!waited) {
                 *abort = 1;
@@ -823,6 +1278,7 @@ bool valid_direct(const DirectConvArgs& a) {
         a.n_tile >= 16 && a.n_tile <= 256 && a.n_tile % 16 == 0 && (!a.chunk_add || a.n_tile % 32 == 0) &&
         a.n_tiles >= 1 && a.p_tiles >= 1 && static_cast<long long>(a.p_tiles) * a.n_tiles < (1LL << 22) &&
         a.patch_h * a.patch_w == tile_positions_m && a.patch_w >= 1 && a.patch_w <= 256 && a.patch_h <= 256 &&
+        (a.patch_h + a.window.kernel_h - 1) * (a.patch_w + a.window.kernel_w - 1) <= halo_slot_floats &&
         a.tiles_y * a.patch_h >= a.out_h && a.tiles_x * a.patch_w >= a.out_w && a.p_tiles == a.tiles_y * a.tiles_x &&
         a.positions == a.out_h * a.out_w && a.a_stages >= 2 && a.a_stages <= max_direct_stages && a.b_stages >= 1 &&
         a.b_stages <= max_direct_stages && (!a.b_resident || (a.n_tiles == 1 && a.b_stages == a.k_blocks)) &&
@@ -841,7 +1297,7 @@ bool valid_direct(const DirectConvArgs& a) {
 
 int direct_conv_shared_bytes(int k_block, int n_tile, int n_tiles, int a_stages, int b_stages) {
     return 1024 + a_stages * tile_positions_m * k_block + b_stages * n_tile * k_block + tail_bytes() +
-        column_bytes(n_tile * n_tiles);
+        halo_ring_bytes() + column_bytes(n_tile * n_tiles);
 }
 
 cudaError_t encode_activation_map(CUtensorMap* map, const void* base, std::uint64_t c8, std::uint64_t height,
@@ -895,10 +1351,42 @@ cudaError_t quantise_pixels(const void* in, PixelSource form, int channels, int 
                                  0, stream, static_cast<const float*>(in), channels, c_pad_in, c8, pixels,
                                  static_cast<const float*>(pixel_max), out, clear_word);
     }
+    const bool half = form == PixelSource::planes_f16;
+    if (half && c8 <= half_planes_max_c8 && pixels % 8 == 0 && (reinterpret_cast<std::uintptr_t>(in) & 15u) == 0 &&
+        (reinterpret_cast<std::uintptr_t>(pixel_max) & 15u) == 0) {
+        const int per_tile = c8;  // 16 threads per channel group of 16
+        const int sub_tiles = per_tile >= 256 ? 1 : 256 / per_tile;
+        const long long block_pixels = 128LL * sub_tiles;
+        const unsigned blocks = static_cast<unsigned>((pixels + block_pixels - 1) / block_pixels);
+        const std::size_t bytes = static_cast<std::size_t>(sub_tiles) * per_tile * sizeof(uint4);
+        return launch_overlapped(quantise_half_planes_kernel, dim3(blocks), dim3(static_cast<unsigned>(per_tile * sub_tiles)),
+                                 bytes, stream, static_cast<const __half*>(in), channels, c8, pixels, sub_tiles, out,
+                                 pixel_max, clear_word);
+    }
+    // Planes whose length is a whole number of 16-byte vectors and whose base is
+    // 16-byte aligned take the vector-load kernel.
+    const int per_vector = half ? 8 : 4;
+    if (pixels % per_vector == 0 && (reinterpret_cast<std::uintptr_t>(in) & 15u) == 0 && channels * 256 <= 200 * 1024) {
+        const int block_pixels = half ? 128 : 64;
+        const unsigned wide_blocks = static_cast<unsigned>((static_cast<long long>(pixels) + block_pixels - 1) / block_pixels);
+        const int bytes = channels * 256;
+        static bool wide_configured = false;
+        if (!wide_configured) {
+            cudaFuncSetAttribute(quantise_planes_wide_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+            cudaFuncSetAttribute(quantise_planes_wide_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+            wide_configured = true;
+        }
+        if (half) {
+            return launch_overlapped(quantise_planes_wide_kernel<true>, dim3(wide_blocks), dim3(256), bytes, stream, in,
+                                     channels, c8, pixels, out, pixel_max, clear_word);
+        }
+        return launch_overlapped(quantise_planes_wide_kernel<false>, dim3(wide_blocks), dim3(256), bytes, stream, in,
+                                 channels, c8, pixels, out, pixel_max, clear_word);
+    }
     const int tile_bytes = channels * (plane_pixels + 1) * static_cast<int>(sizeof(float));
     if (tile_bytes > 200 * 1024) return cudaErrorInvalidValue;
     const unsigned blocks = static_cast<unsigned>((static_cast<long long>(pixels) + plane_pixels - 1) / plane_pixels);
-    if (form == PixelSource::planes_f16) {
+    if (half) {
         static bool configured = false;
         if (!configured) {
             cudaFuncSetAttribute(quantise_planes_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
@@ -924,6 +1412,29 @@ cudaError_t quantise_fields(const void* in, int source_half, int channels, int i
         (reinterpret_cast<std::uintptr_t>(out) & 15u) != 0) {
         return cudaErrorInvalidValue;
     }
+    // Row-staged kernel when a run's input rows fit in shared memory.
+    const int span = (field_run - 1) * window.stride_x + window.kernel_w;
+    const long long row_bytes = static_cast<long long>(channels) * window.kernel_h * span * 4;
+    const long long planes = static_cast<long long>(channels) * in_h * in_w;
+    if (window.stride_x >= 1 && window.stride_y >= 1 && span <= 4 * field_run && row_bytes <= 48 * 1024 &&
+        out_h <= 65535 && planes < (1LL << 31)) {
+        const dim3 grid(static_cast<unsigned>((out_w + field_run - 1) / field_run), static_cast<unsigned>(out_h));
+        const std::size_t bytes = static_cast<std::size_t>(row_bytes);
+        if (c8 == 32) {
+            return source_half ? launch_overlapped(quantise_fields_rows_kernel<true, 32>, grid, dim3(field_run), bytes,
+                                                   stream, in, channels, in_h, in_w, window, out_h, out_w, span, out,
+                                                   field_max)
+                               : launch_overlapped(quantise_fields_rows_kernel<false, 32>, grid, dim3(field_run), bytes,
+                                                   stream, in, channels, in_h, in_w, window, out_h, out_w, span, out,
+                                                   field_max);
+        }
+        return source_half ? launch_overlapped(quantise_fields_rows_kernel<true, 64>, grid, dim3(field_run), bytes,
+                                               stream, in, channels, in_h, in_w, window, out_h, out_w, span, out,
+                                               field_max)
+                           : launch_overlapped(quantise_fields_rows_kernel<false, 64>, grid, dim3(field_run), bytes,
+                                               stream, in, channels, in_h, in_w, window, out_h, out_w, span, out,
+                                               field_max);
+    }
     const unsigned blocks = static_cast<unsigned>((positions + 255) / 256);
     if (source_half) {
         return launch_overlapped(quantise_fields_kernel<true>, dim3(blocks), dim3(256), 0, stream, in, channels, in_h,
@@ -942,14 +1453,11 @@ cudaError_t direct_conv(const CUtensorMap& a_map, const CUtensorMap& b_map, cons
         return count;
     }();
     if (!valid_direct(args)) return cudaErrorInvalidValue;
-    int buffers = 2;
+    // As many accumulator buffers as fit in TMEM's 512 columns (n_tile <= 256: two
+    // at least), up to eight; the allocation is the next power of two.
+    const int buffers = std::min(max_tmem_buffers, 512 / args.n_tile);
     std::uint32_t columns = 32;
-    while (static_cast<int>(columns) < 2 * args.n_tile) columns <<= 1;
-    if (columns > 512) {
-        buffers = 1;
-        columns = 32;
-        while (static_cast<int>(columns) < args.n_tile) columns <<= 1;
-    }
+    while (static_cast<int>(columns) < buffers * args.n_tile) columns <<= 1;
     const int smem = direct_conv_shared_bytes(args.k_block, args.n_tile, args.n_tiles, args.a_stages, args.b_stages);
     if (smem > direct_conv_max_shared) return cudaErrorInvalidValue;
     static bool configured = false;

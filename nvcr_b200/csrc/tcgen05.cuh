@@ -44,6 +44,19 @@ static __device__ __forceinline__ bool barrier_try_wait(std::uint32_t bar, std::
     return done != 0;
 }
 
+// Non-blocking: whether the phase of `parity` has completed.
+static __device__ __forceinline__ bool barrier_test_wait(std::uint32_t bar, std::uint32_t parity) {
+    std::uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
 // Waits for the phase of `parity` to complete; false (and status bit 0) once
 // `limit_ns` of the global timer have passed.
 static __device__ bool barrier_wait_for(std::uint32_t bar, std::uint32_t parity, unsigned int* status,
@@ -65,6 +78,37 @@ static __device__ bool barrier_wait_for(std::uint32_t bar, std::uint32_t parity,
 // The same with the kernels' limit of about two seconds.
 static __device__ bool barrier_wait(std::uint32_t bar, std::uint32_t parity, unsigned int* status) {
     return barrier_wait_for(bar, parity, status, wait_limit_ns);
+}
+
+// try_wait with a suspend-time hint: the thread sleeps until the phase
+// completes or about `hint_ns` have passed, issuing nothing meanwhile.
+static __device__ __forceinline__ bool barrier_try_wait_hint(std::uint32_t bar, std::uint32_t parity,
+                                                             std::uint32_t hint_ns) {
+    std::uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return done != 0;
+}
+
+// barrier_wait for warps that share a sub-partition with a latency-critical
+// thread: the waiting thread is suspended in hardware (woken when the phase
+// completes) instead of polling, so it takes no issue slots; the same limit of
+// about two seconds, after which status bit 0 is set and false returned.
+static __device__ bool barrier_sleep_wait(std::uint32_t bar, std::uint32_t parity, unsigned int* status) {
+    if (barrier_try_wait_hint(bar, parity, 50000u)) return true;
+    const unsigned long long start = global_timer();
+    for (;;) {
+        if (barrier_try_wait_hint(bar, parity, 50000u)) return true;
+        if (global_timer() - start > wait_limit_ns) {
+            atomicOr(status, 1u);
+            return false;
+        }
+    }
 }
 
 static __device__ __forceinline__ void tma_load_2d(std::uint32_t dst, const CUtensorMap* map, std::uint32_t bar, int x, int y) {
