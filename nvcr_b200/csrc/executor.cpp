@@ -55,7 +55,7 @@ struct Executor::IntegerConv {
     bool direct{false};
     int c8{0};
     int k_block{0}, c_blocks{0}, direct_k_blocks{0};
-    int direct_a_stages{0}, direct_b_stages{0};
+    int direct_a_stages{0}, direct_b_stages{0}, direct_group{1};
     bool direct_b_resident{false};
     void* direct_allocation{nullptr};
     CUtensorMap direct_b_map{};
@@ -751,16 +751,25 @@ Status Executor::prepare_direct(IntegerConv& conv, const Step& step, const Node&
     conv.c_blocks = conv.c8 / conv.k_block;
     conv.direct_k_blocks = taps * conv.c_blocks;
     const int n_padded = conv.n_tiles * conv.n_tile;
+    // K blocks per pipeline stage: each stage costs the MMA thread a wait and a
+    // commit (a few hundred cycles), so stages whose MMAs are short (an MMA
+    // issues in about max(60, n_tile / 2) cycles) take several K blocks.
+    const int block_cycles = (conv.k_block / 32) * std::max(60, conv.n_tile / 2);
+    conv.direct_group = 1;
+    for (const int group : {1, 2, 3, 4}) {
+        if (conv.direct_k_blocks % group != 0) continue;
+        conv.direct_group = group;
+        if (group * block_cycles >= 500) break;
+    }
+    bool fits = false;
     // Ring depths: resident weights when one N tile's K blocks fit, else the
     // deepest rings that fit.
-    // Small stages (short K blocks, narrow N) take deeper rings: a stage in
-    // flight hides one TMA round trip, which costs far more than the few MMAs
-    // of such a stage.
-    bool fits = false;
-    if (conv.n_tiles == 1 && conv.direct_k_blocks <= 16) {
+    if (!fits && conv.n_tiles == 1 && conv.direct_k_blocks <= 16) {
         for (const int a_stages : {16, 12, 8, 6, 4, 3, 2}) {
+            if (a_stages * conv.direct_group > 32) continue;  // one issuing lane per copy of a stage
             if (kernels::direct_conv_shared_bytes(conv.k_block, conv.n_tile, conv.n_tiles, a_stages,
-                                                  conv.direct_k_blocks) <= kernels::direct_conv_max_shared) {
+                                                  conv.direct_k_blocks, conv.direct_group, true) <=
+                kernels::direct_conv_max_shared) {
                 conv.direct_a_stages = a_stages;
                 conv.direct_b_stages = conv.direct_k_blocks;
                 conv.direct_b_resident = true;
@@ -772,13 +781,18 @@ Status Executor::prepare_direct(IntegerConv& conv, const Step& step, const Node&
     if (!fits) {
         constexpr int depths[][2] = {{16, 16}, {12, 12}, {8, 8}, {6, 6}, {4, 6}, {6, 4},
                                      {4, 4}, {4, 3}, {3, 3}, {3, 2}, {2, 2}};
-        for (const auto& depth : depths) {
-            if (kernels::direct_conv_shared_bytes(conv.k_block, conv.n_tile, conv.n_tiles, depth[0], depth[1]) <=
-                kernels::direct_conv_max_shared) {
-                conv.direct_a_stages = depth[0];
-                conv.direct_b_stages = depth[1];
-                fits = true;
-                break;
+        for (const int group : {conv.direct_group, 1}) {
+            if (fits) break;
+            for (const auto& depth : depths) {
+                if ((depth[0] > depth[1] ? depth[0] : depth[1]) * group > 32) continue;
+                if (kernels::direct_conv_shared_bytes(conv.k_block, conv.n_tile, conv.n_tiles, depth[0], depth[1],
+                                                      group, false) <= kernels::direct_conv_max_shared) {
+                    conv.direct_a_stages = depth[0];
+                    conv.direct_b_stages = depth[1];
+                    conv.direct_group = group;
+                    fits = true;
+                    break;
+                }
             }
         }
     }
@@ -1213,6 +1227,7 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
         d.tiles_y = pc.d_tiles_y;
         d.tiles_x = pc.d_tiles_x;
         d.p_tiles = pc.d_tiles_y * pc.d_tiles_x;
+        d.group = conv.direct_group;
         d.a_stages = conv.direct_a_stages;
         d.b_stages = conv.direct_b_stages;
         d.b_resident = conv.direct_b_resident ? 1 : 0;

@@ -708,40 +708,78 @@ __device__ __noinline__ Sixteen16 direct_wsilu16(Sixteen16 x, float k) {
     return x;
 }
 
-// One warp issues the TMA copies of a ring of `ring` stages (ring <= 32): lane
-// j owns stage j and issues items j, j + ring, j + 2 ring, ... of the sequence as
-// soon as its stage is free (the empty barrier's previous phase completed). A
-// copy instruction occupies the issuing warp for hundreds of cycles whatever
-// the number of lanes that carry a copy in it, so the lanes whose stages came
-// free issue together. `issue(item, stage)` arms the full barrier and starts
-// the copy. After an abort or a wait that runs out (status bit 0, abort set),
-// each lane waits, bounded, for its last copy to land and the warp returns.
+// One pipeline stage's MMAs as straight-line code: Group K blocks of Steps
+// MMAs each (K = 32 per MMA), descriptors at compile-time offsets from the
+// stage's first A and B blocks. The issuing thread is latency-bound, so any
+// run-time arithmetic between MMAs slows the tensor pipe.
+template <int Steps, int Group>
+__device__ __forceinline__ void issue_stage(std::uint32_t acc, std::uint64_t a_desc, std::uint64_t b_desc,
+                                            std::uint32_t idesc, std::uint32_t first, int a_block16,
+                                            int b_block16) {
+#pragma unroll
+    for (int i = 0; i < Group; ++i) {
+#pragma unroll
+        for (int kk = 0; kk < Steps; ++kk) {
+            mma_i8(acc, a_desc + static_cast<std::uint64_t>(i * a_block16 + 2 * kk),
+                   b_desc + static_cast<std::uint64_t>(i * b_block16 + 2 * kk), idesc,
+                   (i == 0 && kk == 0) ? first : 1u);
+        }
+    }
+}
+
+template <int Steps>
+__device__ __forceinline__ void issue_stage_group(int group, std::uint32_t acc, std::uint64_t a_desc,
+                                                  std::uint64_t b_desc, std::uint32_t idesc, std::uint32_t first,
+                                                  int a_block16, int b_block16) {
+    switch (group) {
+    case 1: issue_stage<Steps, 1>(acc, a_desc, b_desc, idesc, first, a_block16, b_block16); break;
+    case 2: issue_stage<Steps, 2>(acc, a_desc, b_desc, idesc, first, a_block16, b_block16); break;
+    case 3: issue_stage<Steps, 3>(acc, a_desc, b_desc, idesc, first, a_block16, b_block16); break;
+    default: issue_stage<Steps, 4>(acc, a_desc, b_desc, idesc, first, a_block16, b_block16); break;
+    }
+}
+
+// One warp issues the TMA copies of a ring of `ring` stages, each filled by
+// `per_item` copies (ring * per_item <= 32): lanes slot * per_item ..
+// slot * per_item + per_item - 1 own stage `slot` and issue copy `part` of items
+// slot, slot + ring, slot + 2 ring, ... of the sequence as soon as the stage is
+// free (its empty barrier's previous phase completed). A copy instruction
+// occupies the issuing warp for hundreds of cycles whatever the number of lanes
+// that carry a copy in it, so all copies of the stages that came free go out
+// in one instruction. `issue(item, stage, part)` starts copy `part` (part 0
+// first arms the full barrier with the whole stage's bytes). After an abort or
+// a wait that runs out (status bit 0, abort set), each stage's part-0 lane waits,
+// bounded, for its last copies to land and the warp returns.
 template <typename Issue>
-__device__ __forceinline__ void ring_issue(int lane, int ring, int items, std::uint32_t empty_base,
+__device__ __forceinline__ void ring_issue(int lane, int ring, int per_item, int items, std::uint32_t empty_base,
                                            std::uint32_t full_base, volatile int* abort, unsigned int* status,
                                            Issue issue) {
-    const bool owner = lane < ring;
-    int item = lane;
+    const int slot = lane / per_item;
+    const int part = lane - slot * per_item;
+    const bool owner = slot < ring;
+    const int leader = owner ? slot * per_item : lane;
+    int item = slot;
     bool failed = false;
     unsigned long long since = global_timer();
     for (unsigned int spin = 0;; ++spin) {
         const bool pending = owner && item < items && !failed;
         if (!__any_sync(0xffffffffu, pending)) break;
         const std::uint32_t phase = static_cast<std::uint32_t>(item / ring) & 1u;
-        const std::uint32_t empty = empty_base + 8u * static_cast<std::uint32_t>(lane);
-        const bool ready = pending && barrier_test_wait(empty, phase ^ 1u);
+        const std::uint32_t empty = empty_base + 8u * static_cast<std::uint32_t>(slot);
+        bool ready = pending && part == 0 && barrier_test_wait(empty, phase ^ 1u);
+        ready = __shfl_sync(0xffffffffu, ready, leader) && pending;  // one answer per stage
         if (__any_sync(0xffffffffu, ready)) {
             if (ready) {
-                issue(item, lane);
+                issue(item, slot, part);
                 item += ring;
                 since = global_timer();
             }
             continue;
         }
-        // No stage is free: the lane whose item comes next (stages free in
-        // order) sleeps on its stage, then every lane tests again.
+        // No stage is free: the leader of the stage whose item comes next (stages
+        // free in order) sleeps on it, then every lane tests again.
         const int next = __reduce_min_sync(0xffffffffu, pending ? item : INT_MAX);
-        if (pending && item == next) barrier_try_wait_hint(empty, phase ^ 1u, 20000u);
+        if (pending && part == 0 && item == next) barrier_try_wait_hint(empty, phase ^ 1u, 20000u);
         if (pending && (spin & 15u) == 15u) {
             if (*abort) {
                 failed = true;
@@ -752,10 +790,10 @@ __device__ __forceinline__ void ring_issue(int lane, int ring, int items, std::u
             }
         }
     }
-    if (failed && item >= ring) {
+    if (failed && part == 0 && item >= ring) {
         const int last = item - ring;
-        barrier_sleep_wait(full_base + 8u * static_cast<std::uint32_t>(lane), static_cast<std::uint32_t>(last / ring) & 1u,
-                     status);
+        barrier_sleep_wait(full_base + 8u * static_cast<std::uint32_t>(slot),
+                           static_cast<std::uint32_t>(last / ring) & 1u, status);
     }
     __syncwarp();
 }
@@ -768,8 +806,13 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
     std::uint8_t* smem = dynamic_smem + (((raw + 1023u) & ~1023u) - raw);
     const int n_tile = a.n_tile;
     const int k_block = a.k_block;
-    const int a_stage_bytes = tile_positions_m * k_block;
-    const int b_stage_bytes = n_tile * k_block;
+    // A stage holds `group` consecutive K blocks of one tile (their A boxes, and
+    // their B boxes unless the weights are resident, one K block per stage).
+    const int group = a.group;
+    const int a_block_bytes = tile_positions_m * k_block;
+    const int b_block_bytes = n_tile * k_block;
+    const int a_stage_bytes = group * a_block_bytes;
+    const int b_stage_bytes = (a.b_resident ? 1 : group) * b_block_bytes;
     // Shared memory: [A stages][B stages][tail][halo ring][column parameters];
     // stage sizes are multiples of 1024 bytes, so every stage keeps the 1 KiB
     // swizzle alignment.
@@ -832,30 +875,34 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
     const int my_tiles = total_tiles > static_cast<int>(blockIdx.x)
         ? (total_tiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x)
         : 0;
+    const int stages_per_tile = k_blocks / group;
     if (warp == weight_warp) {
         // ---------------- weights by TMA (resident weights: the first tile's K blocks, once)
-        const std::uint32_t bytes = static_cast<std::uint32_t>(b_stage_bytes);
-        const int items = a.b_resident ? (my_tiles > 0 ? k_blocks : 0) : my_tiles * k_blocks;
-        ring_issue(lane, a.b_stages, items, smem_address(&tail->empty_b[0]), smem_address(&tail->full_b[0]), abort,
-                   a.status, [&](int item, int stage) {
-                       const int local_tile = item / k_blocks;
-                       const int kb = item - local_tile * k_blocks;
-                       int n_index;
-                       by_n_tiles.divide(static_cast<int>(blockIdx.x) + local_tile * static_cast<int>(gridDim.x),
-                                         n_index);
+        const int items = a.b_resident ? (my_tiles > 0 ? k_blocks : 0) : my_tiles * stages_per_tile;
+        const int boxes = a.b_resident ? 1 : group;
+        ring_issue(lane, a.b_stages, boxes, items, smem_address(&tail->empty_b[0]), smem_address(&tail->full_b[0]),
+                   abort, a.status, [&](int item, int stage, int part) {
+                       int n_index = 0;
+                       int kb0 = item;
+                       if (!a.b_resident) {
+                           const int local_tile = item / stages_per_tile;
+                           kb0 = (item - local_tile * stages_per_tile) * group;
+                           by_n_tiles.divide(static_cast<int>(blockIdx.x) + local_tile * static_cast<int>(gridDim.x),
+                                             n_index);
+                       }
                        const std::uint32_t full = smem_address(&tail->full_b[stage]);
-                       barrier_expect_bytes(full, bytes);
-                       tma_load_2d(smem_address(b_smem + stage * b_stage_bytes), &b_map, full, kb * k_block,
-                                   n_index * n_tile);
+                       if (part == 0) barrier_expect_bytes(full, static_cast<std::uint32_t>(b_stage_bytes));
+                       __syncwarp(__activemask());  // the stage's bytes are armed before any copy
+                       tma_load_2d(smem_address(b_smem + stage * b_stage_bytes + part * b_block_bytes), &b_map, full,
+                                   (kb0 + part) * k_block, n_index * n_tile);
                    });
     } else if (warp == activation_warp) {
         // ---------------- activations by TMA: one box per (tap, channel block)
         grid_dependency_wait();
-        const std::uint32_t bytes = static_cast<std::uint32_t>(a_stage_bytes);
-        ring_issue(lane, a.a_stages, my_tiles * k_blocks, smem_address(&tail->empty_a[0]),
-                   smem_address(&tail->full_a[0]), abort, a.status, [&](int item, int stage) {
-                       const int local_tile = item / k_blocks;
-                       const int kb = item - local_tile * k_blocks;
+        ring_issue(lane, a.a_stages, group, my_tiles * stages_per_tile, smem_address(&tail->empty_a[0]),
+                   smem_address(&tail->full_a[0]), abort, a.status, [&](int item, int stage, int part) {
+                       const int local_tile = item / stages_per_tile;
+                       const int kb = (item - local_tile * stages_per_tile) * group + part;
                        int n_unused, tx;
                        const int p_tile = by_n_tiles.divide(
                            static_cast<int>(blockIdx.x) + local_tile * static_cast<int>(gridDim.x), n_unused);
@@ -865,16 +912,22 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
                        const int ky = tap / a.window.kernel_w;
                        const int kx = tap - ky * a.window.kernel_w;
                        const std::uint32_t full = smem_address(&tail->full_a[stage]);
-                       barrier_expect_bytes(full, bytes);
+                       if (part == 0) barrier_expect_bytes(full, static_cast<std::uint32_t>(a_stage_bytes));
+                       __syncwarp(__activemask());  // the stage's bytes are armed before any copy
                        // Innermost coordinate: the channel block's first byte, a multiple of k_block.
-                       tma_load_3d(smem_address(smem + stage * a_stage_bytes), &a_map, full, cb * k_block,
-                                   tx * a.patch_w - a.window.pad_left + kx, ty * a.patch_h - a.window.pad_top + ky);
+                       tma_load_3d(smem_address(smem + stage * a_stage_bytes + part * a_block_bytes), &a_map, full,
+                                   cb * k_block, tx * a.patch_w - a.window.pad_left + kx,
+                                   ty * a.patch_h - a.window.pad_top + ky);
                    });
     } else if (warp == mma_warp) {
         if (lane == 0) {
             // ---------------- tensor-core issue
             const std::uint32_t idesc = i8_instruction(n_tile);
             const int steps = k_block / 32;
+            const std::uint64_t a_desc0 = swizzled_descriptor(smem_address(smem), k_block);
+            const std::uint64_t b_desc0 = swizzled_descriptor(smem_address(b_smem), k_block);
+            const int a_block16 = a_block_bytes >> 4;
+            const int b_block16 = b_block_bytes >> 4;
             std::uint32_t g = 0;
             int local = 0;
             bool ok = true;
@@ -889,27 +942,36 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
                 }
                 tmem_fence_after();
                 const std::uint32_t acc = tmem + static_cast<std::uint32_t>(buffer * n_tile);
-                for (int kb = 0; kb < k_blocks; ++kb, ++g) {
-                    const int sb = a.b_resident ? kb : sb_ring;
-                    const std::uint32_t b_phase = a.b_resident ? 0u : b_ring_phase;
+                for (int kb0 = 0; kb0 < k_blocks; kb0 += group, ++g) {
                     // (TMA writes are ordered before the MMA's reads by the full
                     // barriers; only TMEM reuse needs a tcgen05 fence, above.)
-                    if (!barrier_sleep_wait(smem_address(&tail->full_a[sa]), a_phase, a.status) ||
-                        !barrier_sleep_wait(smem_address(&tail->full_b[sb]), b_phase, a.status)) {
+                    bool ready = barrier_sleep_wait(smem_address(&tail->full_a[sa]), a_phase, a.status);
+                    if (ready && !a.b_resident) {
+                        ready = barrier_sleep_wait(smem_address(&tail->full_b[sb_ring]), b_ring_phase, a.status);
+                    }
+                    for (int i = 0; ready && a.b_resident && local == 0 && i < group; ++i) {
+                        ready = barrier_sleep_wait(smem_address(&tail->full_b[kb0 + i]), 0u, a.status);
+                    }
+                    if (!ready) {
                         *abort = 1;
                         ok = false;
                         break;
                     }
-                    const std::uint32_t a_base = smem_address(smem + sa * a_stage_bytes);
-                    const std::uint32_t b_base = smem_address(b_smem + sb * b_stage_bytes);
-                    for (int kk = 0; kk < steps; ++kk) {
-                        const std::uint32_t step = static_cast<std::uint32_t>(kk * 32);
-                        const std::uint32_t accumulate = (kb == 0 && kk == 0) ? 0u : 1u;
-                        mma_i8(acc, swizzled_descriptor(a_base + step, k_block),
-                               swizzled_descriptor(b_base + step, k_block), idesc, accumulate);
+                    // Descriptors advance by address / 16 in their low bits (the
+                    // address field cannot carry: shared addresses are below 2^18).
+                    const std::uint64_t a_desc = a_desc0 + static_cast<std::uint64_t>((sa * a_stage_bytes) >> 4);
+                    const std::uint64_t b_desc = b_desc0 +
+                        static_cast<std::uint64_t>(((a.b_resident ? kb0 * b_block_bytes : sb_ring * b_stage_bytes)) >> 4);
+                    const std::uint32_t first = kb0 == 0 ? 0u : 1u;
+                    if (steps == 4) {
+                        issue_stage_group<4>(group, acc, a_desc, b_desc, idesc, first, a_block16, b_block16);
+                    } else if (steps == 2) {
+                        issue_stage_group<2>(group, acc, a_desc, b_desc, idesc, first, a_block16, b_block16);
+                    } else {
+                        issue_stage_group<1>(group, acc, a_desc, b_desc, idesc, first, a_block16, b_block16);
                     }
                     mma_commit(smem_address(&tail->empty_a[sa]));
-                    if (!a.b_resident) mma_commit(smem_address(&tail->empty_b[sb]));
+                    if (!a.b_resident) mma_commit(smem_address(&tail->empty_b[sb_ring]));
                     if (++sa == a.a_stages) {
                         sa = 0;
                         a_phase ^= 1u;
@@ -1280,7 +1342,11 @@ bool valid_direct(const DirectConvArgs& a) {
         a.patch_h * a.patch_w == tile_positions_m && a.patch_w >= 1 && a.patch_w <= 256 && a.patch_h <= 256 &&
         (a.patch_h + a.window.kernel_h - 1) * (a.patch_w + a.window.kernel_w - 1) <= halo_slot_floats &&
         a.tiles_y * a.patch_h >= a.out_h && a.tiles_x * a.patch_w >= a.out_w && a.p_tiles == a.tiles_y * a.tiles_x &&
-        a.positions == a.out_h * a.out_w && a.a_stages >= 2 && a.a_stages <= max_direct_stages && a.b_stages >= 1 &&
+        a.positions == a.out_h * a.out_w &&
+        a.group >= 1 && a.group <= 4 &&
+        a.k_blocks % a.group == 0 &&
+        a.a_stages * a.group <= 32 && (a.b_resident || a.b_stages * a.group <= 32) &&
+        a.a_stages >= 2 && a.a_stages <= max_direct_stages && a.b_stages >= 1 &&
         a.b_stages <= max_direct_stages && (!a.b_resident || (a.n_tiles == 1 && a.b_stages == a.k_blocks)) &&
         (a.b_resident || a.b_stages >= 2) && a.d2s_block >= 0 &&
         (a.out_max == nullptr ||
@@ -1295,8 +1361,10 @@ bool valid_direct(const DirectConvArgs& a) {
 
 }  // namespace
 
-int direct_conv_shared_bytes(int k_block, int n_tile, int n_tiles, int a_stages, int b_stages) {
-    return 1024 + a_stages * tile_positions_m * k_block + b_stages * n_tile * k_block + tail_bytes() +
+int direct_conv_shared_bytes(int k_block, int n_tile, int n_tiles, int a_stages, int b_stages, int group,
+                             bool b_resident) {
+    return 1024 + a_stages * group * tile_positions_m * k_block + b_stages * (b_resident ? 1 : group) * n_tile * k_block +
+        tail_bytes() +
         halo_ring_bytes() + column_bytes(n_tile * n_tiles);
 }
 
@@ -1458,7 +1526,8 @@ cudaError_t direct_conv(const CUtensorMap& a_map, const CUtensorMap& b_map, cons
     const int buffers = std::min(max_tmem_buffers, 512 / args.n_tile);
     std::uint32_t columns = 32;
     while (static_cast<int>(columns) < buffers * args.n_tile) columns <<= 1;
-    const int smem = direct_conv_shared_bytes(args.k_block, args.n_tile, args.n_tiles, args.a_stages, args.b_stages);
+    const int smem = direct_conv_shared_bytes(args.k_block, args.n_tile, args.n_tiles, args.a_stages, args.b_stages,
+                                              args.group, args.b_resident != 0);
     if (smem > direct_conv_max_shared) return cudaErrorInvalidValue;
     static bool configured = false;
     if (!configured) {

@@ -156,6 +156,8 @@ struct DirectConvArgs {
     int k_block;                   // K bytes per stage: 32, 64 or 128 (the A and B swizzle span)
     int c_blocks;                  // K blocks per tap: c8 / k_block
     int k_blocks;                  // taps * c_blocks
+    int group;                     // K blocks per pipeline stage (1-4, dividing k_blocks; resident weights stay
+                                   // one block per stage)
     int positions, p_tiles;        // out_h * out_w; tiles_y * tiles_x
     int patch_h, patch_w, tiles_y, tiles_x;
     int a_stages, b_stages;
@@ -199,7 +201,8 @@ cudaError_t encode_weight_map(CUtensorMap* map, const void* base, std::uint64_t 
                               std::uint32_t k_block, std::uint32_t box_rows);
 cudaError_t direct_conv(const CUtensorMap& a_map, const CUtensorMap& b_map, const DirectConvArgs& args,
                         cudaStream_t stream);
-int direct_conv_shared_bytes(int k_block, int n_tile, int n_tiles, int a_stages, int b_stages);
+int direct_conv_shared_bytes(int k_block, int n_tile, int n_tiles, int a_stages, int b_stages, int group,
+                             bool b_resident);
 constexpr int direct_conv_max_shared = 232448;
 
 // Diagnostics: one thread waits on an mbarrier that nothing arrives on, with the
