@@ -252,6 +252,7 @@ Executor::~Executor() {
     cudaFree(arena_);
     cudaFree(weights_);
     cudaFree(status_);
+    if (fallback_stream_ != nullptr) cudaStreamDestroy(fallback_stream_);
     if (owns_stream_ && stream_ != nullptr) cudaStreamDestroy(stream_);
 }
 
@@ -1086,16 +1087,16 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
         };
         // The quantise-on-load conv: the conv itself, or (gate not null) a direct
         // conv's fallback that runs only when that conv found a mixed window.
-        auto launch_fused = [&](const unsigned int* gate) -> Status {
+        auto launch_fused = [&](const unsigned int* gate, cudaStream_t on) -> Status {
             cudaError_t launched_status = cudaSuccess;
             if (!pc.source_staged) {
                 if (conv.fields) {
                     launched_status = kernels::stage_receptive_fields(
                         from, pc.source_half ? 1 : 0, source.channels, source.height, source.width, step.window,
-                        conv_out.height, conv_out.width, conv.c_pad, staged, pixel_max, stream_);
+                        conv_out.height, conv_out.width, conv.c_pad, staged, pixel_max, on);
                 } else {
                     launched_status = kernels::stage_source(from, pc.source_half ? 1 : 0, source.channels, conv.c_pad,
-                                                            pixels, staged, pixel_max, stream_, gate);
+                                                            pixels, staged, pixel_max, on, gate);
                 }
                 if (launched_status != cudaSuccess) return cuda_error("source staging launch", launched_status);
                 ++launches_;
@@ -1161,7 +1162,7 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
             f.status = status_;
             f.gate = gate;
             launched_status = kernels::fused_conv(layout.b_high_map, layout.b_low_map, pc.halo_map, conv.weight_limbs,
-                                                  conv.activation_limbs, f, stream_);
+                                                  conv.activation_limbs, f, on);
             if (launched_status != cudaSuccess) return cuda_error("integer conv launch", launched_status);
             ++launches_;
             if (gate != nullptr) return mark("fallback_conv:" + label, "fallback", 0.0, 0.0);
@@ -1172,7 +1173,7 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
         if (!conv.direct) {
             auto zeroed = zero_out_max();
             if (!zeroed) return zeroed;
-            return launch_fused(nullptr);
+            return launch_fused(nullptr, stream_);
         }
 
         // ---- direct path: per-pixel int8 activations, TMA-fed GEMM
@@ -1248,14 +1249,63 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
         d.d2s_block = step.d2s_block;
         d.fallback = fallback;
         d.status = status_;
+        // In a captured run the fallback becomes a conditional node: the conv
+        // sets its condition when it meets a mixed window, and a replay of a run
+        // without one launches nothing more.
+        cudaGraph_t captured = nullptr;
+        if (multi_tap && capturing_) {
+            cudaStreamCaptureStatus capture_status = cudaStreamCaptureStatusNone;
+            status = cudaStreamGetCaptureInfo_v3(stream_, &capture_status, nullptr, &captured);
+            if (status != cudaSuccess || capture_status != cudaStreamCaptureStatusActive || captured == nullptr) {
+                return cuda_error("cudaStreamGetCaptureInfo", status == cudaSuccess ? cudaErrorStreamCaptureInvalidated
+                                                                                    : status);
+            }
+            cudaGraphConditionalHandle condition = 0;
+            status = cudaGraphConditionalHandleCreate(&condition, captured, 0u, cudaGraphCondAssignDefault);
+            if (status != cudaSuccess) return cuda_error("cudaGraphConditionalHandleCreate", status);
+            d.condition = condition;
+        }
         status = kernels::direct_conv(pc.a_map, conv.direct_b_map, d, stream_);
         if (status != cudaSuccess) return cuda_error("direct integer conv launch", status);
         ++launches_;
+        if (d.condition != 0) {
+            cudaStreamCaptureStatus capture_status = cudaStreamCaptureStatusNone;
+            const cudaGraphNode_t* after_conv = nullptr;
+            std::size_t count_after = 0;
+            status = cudaStreamGetCaptureInfo_v3(stream_, &capture_status, nullptr, &captured, &after_conv, nullptr,
+                                                 &count_after);
+            if (status != cudaSuccess) return cuda_error("cudaStreamGetCaptureInfo", status);
+            cudaGraphNodeParams params{};
+            params.type = cudaGraphNodeTypeConditional;
+            params.conditional.handle = d.condition;
+            params.conditional.type = cudaGraphCondTypeIf;
+            params.conditional.size = 1;
+            cudaGraphNode_t node = nullptr;
+            status = cudaGraphAddNode(&node, captured, after_conv, count_after, &params);
+            if (status != cudaSuccess) return cuda_error("cudaGraphAddNode conditional", status);
+            if (fallback_stream_ == nullptr) {
+                status = cudaStreamCreateWithFlags(&fallback_stream_, cudaStreamNonBlocking);
+                if (status != cudaSuccess) return cuda_error("cudaStreamCreateWithFlags", status);
+            }
+            status = cudaStreamBeginCaptureToGraph(fallback_stream_, params.conditional.phGraph_out[0], nullptr, nullptr,
+                                                   0, cudaStreamCaptureModeThreadLocal);
+            if (status != cudaSuccess) return cuda_error("cudaStreamBeginCaptureToGraph", status);
+            const int launched_before = launches_;  // the body's kernels run only after a mixed window
+            Status body = launch_fused(nullptr, fallback_stream_);
+            launches_ = launched_before;
+            cudaGraph_t ended = nullptr;
+            const cudaError_t end_status = cudaStreamEndCapture(fallback_stream_, &ended);
+            if (!body) return body;
+            if (end_status != cudaSuccess) return cuda_error("cudaStreamEndCapture fallback", end_status);
+            status = cudaStreamUpdateCaptureDependencies(stream_, &node, 1, cudaStreamSetCaptureDependencies);
+            if (status != cudaSuccess) return cuda_error("cudaStreamUpdateCaptureDependencies", status);
+            return mark("integer_conv:" + label, "integer_conv", ops, 0.0);
+        }
         auto marked = mark("integer_conv:" + label, "integer_conv", ops,
                            static_cast<double>(pixels) * (conv.c8 + 4.0) +
                                static_cast<double>(node.out_channels) * conv.k_taps * conv.c8 + out_bytes);
         if (!marked) return marked;
-        if (multi_tap) return launch_fused(fallback);
+        if (multi_tap) return launch_fused(fallback, stream_);
         return Ok{};
     }
     case StepKind::chunk_add:
@@ -1499,7 +1549,9 @@ Status Executor::run_graph(const GraphKey& key, const std::function<Status()>& e
     if (cached.exec == nullptr) {
         cudaError_t status = cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal);
         if (status != cudaSuccess) return cuda_error("cudaStreamBeginCapture", status);
+        capturing_ = true;
         Status enqueued = enqueue();
+        capturing_ = false;
         cudaGraph_t graph = nullptr;
         status = cudaStreamEndCapture(stream_, &graph);
         if (!enqueued) {

@@ -149,6 +149,11 @@ private:
     std::uint64_t arena_generation_{0};
     int launches_{0};
     bool profiling_{false};
+    // Set while run_graph captures a run: a direct conv's fallback then goes into
+    // a conditional graph node (captured on fallback_stream_) that runs only when
+    // the conv found a window whose pixels have different exponents.
+    bool capturing_{false};
+    cudaStream_t fallback_stream_{nullptr};
     std::vector<cudaEvent_t> events_;
     std::size_t marks_{0};
     bool run_started_{false};

@@ -1110,6 +1110,7 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
             }
             if (a.fallback != nullptr && part == 0 && __any_sync(0xffffffffu, mixed) && lane == 0) {
                 atomicOr(a.fallback, 1u);
+                if (a.condition != 0) cudaGraphSetConditional(a.condition, 1u);
             }
             // A mixed window's accumulators are not this position's result:
             // nothing is stored for it (nor added to a staged maximum, which

@@ -178,6 +178,9 @@ struct DirectConvArgs {
     int d2s_block;
     unsigned int* fallback;        // multi-tap windows: set to 1 when a window mixes exponents; else null
     unsigned int* status;
+    // When not zero, a conditional-node handle of the graph this launch belongs
+    // to: set to 1 (cudaGraphSetConditional) when a window mixes exponents.
+    unsigned long long condition;
 };
 // Source forms of quantise_pixels: NCHW FP32 or FP16 planes, or a staged FP32
 // tensor [pixels][c_pad] whose per-pixel maxima are already known.

@@ -547,3 +547,34 @@ def test_sigmoid_reciprocal_exhaustive(cuda):
     denominators in [1, 2^126): every float there gives the IEEE division's bits."""
     first, end = 0x3F800000, 0x7E800000  # 1.0 and 2^126
     assert reciprocal_mismatches(first, end - first) == 0
+
+
+def test_fallback_in_captured_runs(cuda, oracle):
+    """A w8a8 3x3 conv run repeatedly on the same device tensors: the first run
+    is launched directly, later ones are captured into a CUDA graph and
+    replayed, where the quantise-on-load fallback is a conditional node that the
+    conv sets only when a window mixes exponents. Inputs alternate between
+    windows that never mix (every pixel's largest value is 100) and windows
+    that do (some pixels scaled down), so replays must both skip and take the
+    fallback, and every run must equal the oracle."""
+    import torch
+
+    stream = SeededStream(95)
+    program = conv_program(stream, 64, 64, (3, 3), (1, 1), (1, 1, 1, 1), (8, 8))
+    base = np.clip(np.rint(stream.tensor(64, 40, 72, 30.0)), -50, 50).astype(np.float32)
+    base[0] = 100.0  # one channel sets every pixel's maximum: one exponent everywhere
+    mixed = base.copy()
+    mixed[:, 5:9, 10:13] *= 0.125  # pixels whose exponent is lower by three
+    mixed[:, 30, 60] *= 0.25
+    with CudaExecutor.from_program(program) as executor:
+        (c, h, w), = executor.infer_output_extents([base.shape])
+        xh = torch.empty(base.shape, dtype=torch.float16, device=cuda)
+        yh = torch.empty((c, h, w), dtype=torch.float16, device=cuda)
+        for run, x in enumerate([base, mixed, base, mixed, mixed, base, mixed]):
+            xh.copy_(torch.from_numpy(x.astype(np.float16)))
+            yh.fill_(float("nan"))
+            executor.run_half({executor.input_names[0]: xh}, {executor.output_names[0]: yh})
+            executor.synchronize()
+            expected = oracle.run(program, [x])[0].astype(np.float16).astype(np.float32)
+            bad = count_differing(yh.float().cpu().numpy(), expected)
+            assert bad == 0, f"run {run}: {bad} of {expected.size} values differ"
