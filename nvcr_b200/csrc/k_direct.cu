@@ -596,6 +596,132 @@ __global__ void __launch_bounds__(field_run) quantise_fields_rows_kernel(const v
     }
 }
 
+// The receptive-field prepass for a fixed small window (C channels, KH x KW
+// taps; C * KH * KW <= C8 <= 64): gather offsets are compile-time, FP16 rows are
+// staged with 16-byte loads when the rows allow it, and the common
+// quantisation is one fused multiply-add per value, q = y - 1.5 * 2^23 for
+// y = fma(x, 2^-e, 1.5 * 2^23): with |x * 2^-e| < 127.5 the single rounding is
+// rint and q's low byte is the low byte of y's bits, packed four at a time by
+// byte permutes. A position whose max * 2^-e reaches 127.5 (the clamp may act),
+// whose 2^-e is not a normal float, or whose field is non-finite takes the
+// general path.
+template <bool Half, int C, int KH, int KW, int C8>
+__global__ void __launch_bounds__(field_run) quantise_fields_fixed_kernel(const void* __restrict__ in, int in_h,
+                                                                          int in_w, Window w, int out_h, int out_w,
+                                                                          int span, int vector_rows,
+                                                                          std::int8_t* __restrict__ out,
+                                                                          float* __restrict__ field_max) {
+    grid_dependency_wait();
+    launch_dependents();
+    extern __shared__ float rows[];  // [C * KH][span]
+    constexpr int values = C * KH * KW;
+    static_assert(values <= C8 && C8 % 32 == 0 && C8 <= 64, "field width");
+    const int oy = blockIdx.y;
+    const int ox0 = blockIdx.x * field_run;
+    const int iy0 = oy * w.stride_y - w.pad_top;
+    const int ix0 = ox0 * w.stride_x - w.pad_left;
+    const unsigned plane = static_cast<unsigned>(in_h) * static_cast<unsigned>(in_w);
+    if (Half && vector_rows) {
+        // 16-byte loads from the aligned column at or before ix0 (in_w is a
+        // multiple of 8, so every row starts 16-byte aligned).
+        const int a0 = ix0 >= 0 ? (ix0 & ~7) : -((-ix0 + 7) & ~7);
+        const int vectors = (ix0 + span - a0 + 7) / 8;
+        for (int i = threadIdx.x; i < C * KH * vectors; i += field_run) {
+            const int rc = i / vectors;
+            const int vcol = i - rc * vectors;
+            const int c = rc / KH;
+            const int iy = iy0 + (rc - c * KH);
+            const int x0 = a0 + 8 * vcol;
+            uint4 raw = make_uint4(0u, 0u, 0u, 0u);
+            const bool row_inside = iy >= 0 && iy < in_h;
+            if (row_inside && x0 >= 0 && x0 + 8 <= in_w) {
+                raw = __ldg(reinterpret_cast<const uint4*>(static_cast<const __half*>(in) + static_cast<unsigned>(c) * plane +
+                                                           static_cast<unsigned>(iy) * in_w + x0));
+            } else if (row_inside) {
+                unsigned short h[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const int x = x0 + j;
+                    h[j] = (x >= 0 && x < in_w)
+                        ? __half_as_ushort(static_cast<const __half*>(in)[static_cast<unsigned>(c) * plane +
+                                                                           static_cast<unsigned>(iy) * in_w + x])
+                        : static_cast<unsigned short>(0);
+                }
+                raw = make_uint4(h[0] | (static_cast<unsigned>(h[1]) << 16), h[2] | (static_cast<unsigned>(h[3]) << 16),
+                                 h[4] | (static_cast<unsigned>(h[5]) << 16), h[6] | (static_cast<unsigned>(h[7]) << 16));
+            }
+            const std::uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int col = x0 + j - ix0;
+                if (col >= 0 && col < span) {
+                    rows[rc * span + col] =
+                        __half2float(__ushort_as_half(static_cast<unsigned short>(words[j >> 1] >> (16 * (j & 1)))));
+                }
+            }
+        }
+    } else {
+        for (int i = threadIdx.x; i < C * KH * span; i += field_run) {
+            const int rc = i / span;
+            const int col = i - rc * span;
+            const int c = rc / KH;
+            const int iy = iy0 + (rc - c * KH);
+            const int ix = ix0 + col;
+            float v = 0.0f;
+            if (iy >= 0 && iy < in_h && ix >= 0 && ix < in_w) {
+                const unsigned at = static_cast<unsigned>(c) * plane + static_cast<unsigned>(iy) * in_w + ix;
+                v = Half ? __half2float(static_cast<const __half*>(in)[at]) : static_cast<const float*>(in)[at];
+            }
+            rows[i] = v;
+        }
+    }
+    __syncthreads();
+    const int ox = ox0 + static_cast<int>(threadIdx.x);
+    if (ox >= out_w) return;
+    const float* base = rows + static_cast<int>(threadIdx.x) * w.stride_x;
+    float v[C8];
+    std::uint32_t m = 0;
+#pragma unroll
+    for (int k = 0; k < C8; ++k) {
+        if (k < values) {
+            const int c = k / (KH * KW);
+            const int tap = k % (KH * KW);
+            v[k] = base[(c * KH + tap / KW) * span + tap % KW];
+            m = max(m, magnitude_bits_of(v[k]));
+        } else {
+            v[k] = 0.0f;
+        }
+    }
+    const float maximum = max_from_magnitude_bits(m);
+    const long long position = static_cast<long long>(oy) * out_w + ox;
+    field_max[position] = maximum;
+    const PixelScale sc = pixel_scale(maximum);
+    uint4* record = reinterpret_cast<uint4*>(out + position * C8);
+    const bool fast = sc.finite && sc.normal && __fmul_rn(maximum, sc.scale) < 127.5f;
+    if (fast) {
+        std::uint32_t words[C8 / 4];
+#pragma unroll
+        for (int k = 0; k < C8 / 4; ++k) {
+            std::uint32_t y[4];
+#pragma unroll
+            for (int b = 0; b < 4; ++b) y[b] = __float_as_uint(__fmaf_rn(v[4 * k + b], sc.scale, round_magic));
+            words[k] = __byte_perm(__byte_perm(y[0], y[1], 0x0040u), __byte_perm(y[2], y[3], 0x0040u), 0x5410u);
+        }
+#pragma unroll
+        for (int k = 0; k < C8 / 16; ++k) {
+            record[k] = make_uint4(words[4 * k], words[4 * k + 1], words[4 * k + 2], words[4 * k + 3]);
+        }
+    } else {
+#pragma unroll
+        for (int k0 = 0; k0 < C8; k0 += 16) {
+            int q[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) q[j] = sc.finite ? quantise_one(v[k0 + j], sc.normal, sc.scale, sc.exponent) : 0;
+            record[k0 / 16] = pack16(q);
+        }
+    }
+}
+
 // One thread per output position: its receptive field in k = c * taps + tap
 // order (padding taps and k past channels * taps zero), the field's max |x|,
 // and the field quantised with its own exponent into c8 bytes.
@@ -1483,6 +1609,18 @@ cudaError_t quantise_fields(const void* in, int source_half, int channels, int i
     }
     // Row-staged kernel when a run's input rows fit in shared memory.
     const int span = (field_run - 1) * window.stride_x + window.kernel_w;
+    if (channels == 3 && window.kernel_h == 3 && window.kernel_w == 3 && c8 == 32 && span <= 4 * field_run &&
+        out_h <= 65535 && static_cast<long long>(channels) * in_h * in_w < (1LL << 31)) {
+        const dim3 grid(static_cast<unsigned>((out_w + field_run - 1) / field_run), static_cast<unsigned>(out_h));
+        const std::size_t bytes = static_cast<std::size_t>(channels) * window.kernel_h * span * 4;
+        const int vector_rows = source_half && in_w % 8 == 0 && (reinterpret_cast<std::uintptr_t>(in) & 15u) == 0;
+        return source_half ? launch_overlapped(quantise_fields_fixed_kernel<true, 3, 3, 3, 32>, grid, dim3(field_run),
+                                               bytes, stream, in, in_h, in_w, window, out_h, out_w, span, vector_rows,
+                                               out, field_max)
+                           : launch_overlapped(quantise_fields_fixed_kernel<false, 3, 3, 3, 32>, grid,
+                                               dim3(field_run), bytes, stream, in, in_h, in_w, window, out_h, out_w,
+                                               span, 0, out, field_max);
+    }
     const long long row_bytes = static_cast<long long>(channels) * window.kernel_h * span * 4;
     const long long planes = static_cast<long long>(channels) * in_h * in_w;
     if (window.stride_x >= 1 && window.stride_y >= 1 && span <= 4 * field_run && row_bytes <= 48 * 1024 &&

@@ -578,3 +578,24 @@ def test_fallback_in_captured_runs(cuda, oracle):
             expected = oracle.run(program, [x])[0].astype(np.float16).astype(np.float32)
             bad = count_differing(yh.float().cpu().numpy(), expected)
             assert bad == 0, f"run {run}: {bad} of {expected.size} values differ"
+
+
+@pytest.mark.parametrize("half", [False, True], ids=["f32", "f16"])
+@pytest.mark.parametrize("width", [64, 50, 72])
+@pytest.mark.parametrize("stride", [1, 2])
+def test_three_channel_fields(cuda, oracle, half, width, stride):
+    """The compile-time receptive-field prepass (3 channels, 3x3 windows, w8a8):
+    widths that allow 16-byte row loads (64, 72) and one that does not (50),
+    rows and columns past the image, and positions whose fields are all zero,
+    non-finite, subnormal, huge or on rounding ties (the general quantisation)."""
+    stream = SeededStream(97 + width + stride)
+    x = np.ascontiguousarray(np.tile(edge_value_input(stream, 9)[[0, 3, 7]], (1, 3, 2))[:, :17, :width])
+    x[:, 9:, :] = np.rint(stream.tensor(3, 8, width, 60.0))  # ordinary values: the one-fma path
+    if half:
+        x = x.astype(np.float16).astype(np.float32)
+    program = conv_program(stream, 3, 40, (3, 3), (stride, stride), (1, 1, 1, 1), (8, 8))
+    label = f"3-channel fields w{width} s{stride}"
+    if half:
+        assert_half_parity(program, [x], oracle, label)
+    else:
+        assert_parity(program, [x], oracle, label)
