@@ -57,6 +57,10 @@ struct Executor::IntegerConv {
     int k_block{0}, c_blocks{0}, direct_k_blocks{0};
     int direct_a_stages{0}, direct_b_stages{0}, direct_group{1};
     bool direct_b_resident{false};
+    // Ring depths for tiles of two patches sharing each weight block (deep-K
+    // convs with k_block 128 and at most 256 columns); 0 when not prepared.
+    int pair_a_stages{0}, pair_b_stages{0}, pair_group{1};
+    bool pair_b_resident{false};
     void* direct_allocation{nullptr};
     CUtensorMap direct_b_map{};
 };
@@ -96,6 +100,7 @@ struct PlannedConv {
     std::size_t quantised{0};
     std::size_t fallback{0};
     int d_patch_h{0}, d_patch_w{0}, d_tiles_y{0}, d_tiles_x{0};
+    int m_tiles{1};  // patches per tile sharing each weight block
     CUtensorMap a_map{};
     const void* a_base{nullptr};
 };
@@ -223,6 +228,9 @@ Result<std::unique_ptr<Executor>> Executor::create(Program program, cudaStream_t
     int minor = 0;
     if (status == cudaSuccess) status = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
     if (status == cudaSuccess) status = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
+    if (status == cudaSuccess) {
+        status = cudaDeviceGetAttribute(&executor->sm_count_, cudaDevAttrMultiProcessorCount, device);
+    }
     if (status != cudaSuccess) return cuda_error("cudaDeviceGetAttribute", status);
     executor->device_ = device;
     if (major != 10 || minor != 0) {
@@ -769,7 +777,7 @@ Status Executor::prepare_direct(IntegerConv& conv, const Step& step, const Node&
         for (const int a_stages : {16, 12, 8, 6, 4, 3, 2}) {
             if (a_stages * conv.direct_group > 32) continue;  // one issuing lane per copy of a stage
             if (kernels::direct_conv_shared_bytes(conv.k_block, conv.n_tile, conv.n_tiles, a_stages,
-                                                  conv.direct_k_blocks, conv.direct_group, true) <=
+                                                  conv.direct_k_blocks, conv.direct_group, true, 1) <=
                 kernels::direct_conv_max_shared) {
                 conv.direct_a_stages = a_stages;
                 conv.direct_b_stages = conv.direct_k_blocks;
@@ -787,7 +795,7 @@ Status Executor::prepare_direct(IntegerConv& conv, const Step& step, const Node&
             for (const auto& depth : depths) {
                 if ((depth[0] > depth[1] ? depth[0] : depth[1]) * group > 32) continue;
                 if (kernels::direct_conv_shared_bytes(conv.k_block, conv.n_tile, conv.n_tiles, depth[0], depth[1],
-                                                      group, false) <= kernels::direct_conv_max_shared) {
+                                                      group, false, 1) <= kernels::direct_conv_max_shared) {
                     conv.direct_a_stages = depth[0];
                     conv.direct_b_stages = depth[1];
                     conv.direct_group = group;
@@ -798,6 +806,30 @@ Status Executor::prepare_direct(IntegerConv& conv, const Step& step, const Node&
         }
     }
     if (!fits) return Ok{};
+    // Pairs of patches per tile share each weight block between two
+    // accumulators: half the weight rows the TMA moves per MAC (deep-K convs
+    // with up to 256 columns), and half the MMA thread's waits, commits and tile
+    // hand-offs per position (narrow convs). The planner decides per plan.
+    const bool narrow = 2 * conv.n_tile <= 256;
+    if (narrow || (conv.k_block == 128 && 2 * conv.n_tile <= 512 && conv.direct_k_blocks >= 8)) {
+        constexpr int depths[][2] = {{8, 8}, {6, 6}, {4, 4}, {4, 3}, {3, 3}, {3, 2}, {2, 2}};
+        const bool resident = conv.n_tiles == 1 && conv.direct_k_blocks <= 16;
+        for (const int group : {conv.direct_group == 3 ? 3 : 1, 1}) {  // paired kernels take groups of 1 or 3
+            if (conv.pair_a_stages > 0) break;
+            for (const auto& depth : depths) {
+                const int b_stages = resident ? conv.direct_k_blocks : depth[1];
+                if (depth[0] * group * 2 > 32 || (!resident && depth[1] * group > 32)) continue;
+                if (kernels::direct_conv_shared_bytes(conv.k_block, conv.n_tile, conv.n_tiles, depth[0], b_stages,
+                                                      group, resident, 2) <= kernels::direct_conv_max_shared) {
+                    conv.pair_a_stages = depth[0];
+                    conv.pair_b_stages = b_stages;
+                    conv.pair_group = group;
+                    conv.pair_b_resident = resident;
+                    break;
+                }
+            }
+        }
+    }
     const std::size_t row_bytes = static_cast<std::size_t>(taps) * conv.c8;
     std::vector<std::int8_t> matrix(static_cast<std::size_t>(n_padded) * row_bytes, 0);
     const int rows = node.out_channels;
@@ -982,6 +1014,15 @@ Result<Executor::Plan*> Executor::plan_for(const std::vector<Extent>& input_exte
                         pc.d_tiles_y = tiles_y;
                         pc.d_tiles_x = tiles_x;
                     }
+                }
+                // Tiles of two patches (plain or depth_to_space outputs only) when
+                // two accumulators still leave TMEM two buffers, or when the conv
+                // has about two tiles per SM or fewer (then one tile per SM needs
+                // no second buffer).
+                const long long tiles = static_cast<long long>(pc.d_tiles_y) * pc.d_tiles_x * conv.n_tiles;
+                if (conv.pair_a_stages > 0 && !step.wsilu && !step.chunk_add && !step.residual &&
+                    !staged_tensor_[step.output] && (4 * conv.n_tile <= 512 || tiles <= 2LL * sm_count_)) {
+                    pc.m_tiles = 2;
                 }
             }
         }
@@ -1228,10 +1269,11 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
         d.tiles_y = pc.d_tiles_y;
         d.tiles_x = pc.d_tiles_x;
         d.p_tiles = pc.d_tiles_y * pc.d_tiles_x;
-        d.group = conv.direct_group;
-        d.a_stages = conv.direct_a_stages;
-        d.b_stages = conv.direct_b_stages;
-        d.b_resident = conv.direct_b_resident ? 1 : 0;
+        d.m_tiles = pc.m_tiles;
+        d.group = pc.m_tiles == 2 ? conv.pair_group : conv.direct_group;
+        d.a_stages = pc.m_tiles == 2 ? conv.pair_a_stages : conv.direct_a_stages;
+        d.b_stages = pc.m_tiles == 2 ? conv.pair_b_stages : conv.direct_b_stages;
+        d.b_resident = (pc.m_tiles == 2 ? conv.pair_b_resident : conv.direct_b_resident) ? 1 : 0;
         d.n_tile = conv.n_tile;
         d.n_tiles = conv.n_tiles;
         d.scales = conv.scales;

@@ -116,6 +116,7 @@ private:
 
     Program program_;
     int device_{0};
+    int sm_count_{148};  // streaming multiprocessors of device_
     cudaStream_t stream_{nullptr};
     bool owns_stream_{false};
     float* weights_{nullptr};

@@ -101,7 +101,7 @@ __host__ __device__ constexpr int tail_bytes() { return static_cast<int>((sizeof
 // window_slots slots, that many tiles ahead.
 constexpr int halo_slot_floats = 400;
 constexpr int halo_lane_items = (halo_slot_floats + 31) / 32;
-__host__ __device__ constexpr int halo_ring_bytes() { return window_slots * halo_slot_floats * 4; }
+__host__ __device__ constexpr int halo_ring_bytes(int m_tiles) { return window_slots * m_tiles * halo_slot_floats * 4; }
 
 __device__ __forceinline__ void cp_async4(std::uint32_t dst, const void* src, int src_bytes) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
@@ -113,8 +113,10 @@ __device__ __forceinline__ void cp_async_arrive(std::uint32_t bar) {
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-// Exponent of a window with a non-finite value: the row is NaN.
+// Exponent of a window with a non-finite value (the row is NaN), and the code
+// of a window whose pixels have different exponents (the fallback writes it).
 constexpr int window_nan = INT_MIN;
+constexpr int window_mixed = INT_MAX;
 
 // ---------------------------------------------------------------- prepass
 
@@ -834,34 +836,62 @@ __device__ __noinline__ Sixteen16 direct_wsilu16(Sixteen16 x, float k) {
     return x;
 }
 
-// One pipeline stage's MMAs as straight-line code: Group K blocks of Steps
-// MMAs each (K = 32 per MMA), descriptors at compile-time offsets from the
-// stage's first A and B blocks. The issuing thread is latency-bound, so any
-// run-time arithmetic between MMAs slows the tensor pipe.
-template <int Steps, int Group>
-__device__ __forceinline__ void issue_stage(std::uint32_t acc, std::uint64_t a_desc, std::uint64_t b_desc,
-                                            std::uint32_t idesc, std::uint32_t first, int a_block16,
-                                            int b_block16) {
+// Position in a ring of `size` slots, advanced without divisions (the roles'
+// single threads are latency-bound): slot and the parity of the pass.
+struct RingPosition {
+    int slot;
+    std::uint32_t phase;
+    __device__ __forceinline__ void advance(int step, int size) {
+        slot += step;
+        while (slot >= size) {
+            slot -= size;
+            phase ^= 1u;
+        }
+    }
+};
+
+// One pipeline stage's MMAs as straight-line code: Group K blocks, each for
+// MTiles sub-tiles of 128 positions (accumulators n_tile columns apart), of
+// Steps MMAs each (K = 32 per MMA), descriptors at compile-time offsets from the
+// stage's first A block (blocks ordered K block-major, sub-tile-minor) and first
+// B block. The issuing thread is latency-bound, so any run-time arithmetic
+// between MMAs slows the tensor pipe.
+template <int Steps, int Group, int MTiles>
+__device__ __forceinline__ void issue_stage(std::uint32_t acc, std::uint32_t sub_columns, std::uint64_t a_desc,
+                                            std::uint64_t b_desc, std::uint32_t idesc, std::uint32_t first,
+                                            int a_block16, int b_block16) {
 #pragma unroll
     for (int i = 0; i < Group; ++i) {
 #pragma unroll
-        for (int kk = 0; kk < Steps; ++kk) {
-            mma_i8(acc, a_desc + static_cast<std::uint64_t>(i * a_block16 + 2 * kk),
-                   b_desc + static_cast<std::uint64_t>(i * b_block16 + 2 * kk), idesc,
-                   (i == 0 && kk == 0) ? first : 1u);
+        for (int m = 0; m < MTiles; ++m) {
+#pragma unroll
+            for (int kk = 0; kk < Steps; ++kk) {
+                mma_i8(acc + static_cast<std::uint32_t>(m) * sub_columns,
+                       a_desc + static_cast<std::uint64_t>((i * MTiles + m) * a_block16 + 2 * kk),
+                       b_desc + static_cast<std::uint64_t>(i * b_block16 + 2 * kk), idesc,
+                       (i == 0 && kk == 0) ? first : 1u);
+            }
         }
     }
 }
 
-template <int Steps>
-__device__ __forceinline__ void issue_stage_group(int group, std::uint32_t acc, std::uint64_t a_desc,
-                                                  std::uint64_t b_desc, std::uint32_t idesc, std::uint32_t first,
-                                                  int a_block16, int b_block16) {
-    switch (group) {
-    case 1: issue_stage<Steps, 1>(acc, a_desc, b_desc, idesc, first, a_block16, b_block16); break;
-    case 2: issue_stage<Steps, 2>(acc, a_desc, b_desc, idesc, first, a_block16, b_block16); break;
-    case 3: issue_stage<Steps, 3>(acc, a_desc, b_desc, idesc, first, a_block16, b_block16); break;
-    default: issue_stage<Steps, 4>(acc, a_desc, b_desc, idesc, first, a_block16, b_block16); break;
+template <int Steps, int MTiles>
+__device__ __forceinline__ void issue_stage_group(int group, std::uint32_t acc, std::uint32_t sub_columns,
+                                                  std::uint64_t a_desc, std::uint64_t b_desc, std::uint32_t idesc,
+                                                  std::uint32_t first, int a_block16, int b_block16) {
+    if constexpr (MTiles == 2) {  // paired tiles use groups of 1 or 3 K blocks
+        if (group == 3) {
+            issue_stage<Steps, 3, 2>(acc, sub_columns, a_desc, b_desc, idesc, first, a_block16, b_block16);
+        } else {
+            issue_stage<Steps, 1, 2>(acc, sub_columns, a_desc, b_desc, idesc, first, a_block16, b_block16);
+        }
+    } else {
+        switch (group) {
+        case 1: issue_stage<Steps, 1, 1>(acc, sub_columns, a_desc, b_desc, idesc, first, a_block16, b_block16); break;
+        case 2: issue_stage<Steps, 2, 1>(acc, sub_columns, a_desc, b_desc, idesc, first, a_block16, b_block16); break;
+        case 3: issue_stage<Steps, 3, 1>(acc, sub_columns, a_desc, b_desc, idesc, first, a_block16, b_block16); break;
+        default: issue_stage<Steps, 4, 1>(acc, sub_columns, a_desc, b_desc, idesc, first, a_block16, b_block16); break;
+        }
     }
 }
 
@@ -885,19 +915,20 @@ __device__ __forceinline__ void ring_issue(int lane, int ring, int per_item, int
     const bool owner = slot < ring;
     const int leader = owner ? slot * per_item : lane;
     int item = slot;
+    std::uint32_t phase = 0;  // parity of the stage's pass: (item / ring) & 1
     bool failed = false;
     unsigned long long since = global_timer();
+    const std::uint32_t empty = empty_base + 8u * static_cast<std::uint32_t>(slot);
     for (unsigned int spin = 0;; ++spin) {
         const bool pending = owner && item < items && !failed;
         if (!__any_sync(0xffffffffu, pending)) break;
-        const std::uint32_t phase = static_cast<std::uint32_t>(item / ring) & 1u;
-        const std::uint32_t empty = empty_base + 8u * static_cast<std::uint32_t>(slot);
         bool ready = pending && part == 0 && barrier_test_wait(empty, phase ^ 1u);
         ready = __shfl_sync(0xffffffffu, ready, leader) && pending;  // one answer per stage
         if (__any_sync(0xffffffffu, ready)) {
             if (ready) {
                 issue(item, slot, part);
                 item += ring;
+                phase ^= 1u;
                 since = global_timer();
             }
             continue;
@@ -916,14 +947,16 @@ __device__ __forceinline__ void ring_issue(int lane, int ring, int per_item, int
             }
         }
     }
-    if (failed && part == 0 && item >= ring) {
-        const int last = item - ring;
-        barrier_sleep_wait(full_base + 8u * static_cast<std::uint32_t>(slot),
-                           static_cast<std::uint32_t>(last / ring) & 1u, status);
+    if (failed && part == 0 && item >= ring) {  // the last copy's pass has parity phase ^ 1
+        barrier_sleep_wait(full_base + 8u * static_cast<std::uint32_t>(slot), phase ^ 1u, status);
     }
     __syncwarp();
 }
 
+// MTiles = 2: two patches per tile sharing each B block; that instance carries
+// no WSiLU, chunk-add, residual or staged output (the planner pairs only plain
+// and depth_to_space stores), which keeps it within the register budget.
+template <int MTiles>
 __global__ void __launch_bounds__(direct_threads, 1)
 direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map,
                    DirectConvArgs a, int tmem_buffers, std::uint32_t tmem_columns) {
@@ -935,9 +968,11 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
     // A stage holds `group` consecutive K blocks of one tile (their A boxes, and
     // their B boxes unless the weights are resident, one K block per stage).
     const int group = a.group;
+    constexpr int m_tiles = MTiles;  // sub-tiles of 128 positions sharing each B stage
+    constexpr bool fusions = MTiles == 1;
     const int a_block_bytes = tile_positions_m * k_block;
     const int b_block_bytes = n_tile * k_block;
-    const int a_stage_bytes = group * a_block_bytes;
+    const int a_stage_bytes = group * m_tiles * a_block_bytes;
     const int b_stage_bytes = (a.b_resident ? 1 : group) * b_block_bytes;
     // Shared memory: [A stages][B stages][tail][halo ring][column parameters];
     // stage sizes are multiples of 1024 bytes, so every stage keeps the 1 KiB
@@ -946,11 +981,15 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
     auto* tail = reinterpret_cast<DirectTail*>(b_smem + a.b_stages * b_stage_bytes);
     const int all_columns = a.n_tiles * n_tile;
     float* halo_maxima = reinterpret_cast<float*>(reinterpret_cast<std::uint8_t*>(tail) + tail_bytes());
-    float* column_scale = reinterpret_cast<float*>(reinterpret_cast<std::uint8_t*>(halo_maxima) + halo_ring_bytes());
+    float* column_scale =
+        reinterpret_cast<float*>(reinterpret_cast<std::uint8_t*>(halo_maxima) + halo_ring_bytes(m_tiles));
+    const int halo_slot = m_tiles * halo_slot_floats;  // floats of one tile's halos
     float* column_bias = column_scale + all_columns;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int total_tiles = a.p_tiles * a.n_tiles;
+    // A tile: m_tiles consecutive patches (p_tile = pg * m_tiles + m) of one N tile.
+    const int p_groups = (a.p_tiles + m_tiles - 1) / m_tiles;
+    const int total_tiles = p_groups * a.n_tiles;
     const int k_blocks = a.k_blocks;
     const TileDivider by_n_tiles(a.n_tiles);
     const TileDivider by_tiles_x(a.tiles_x);
@@ -1025,14 +1064,17 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
     } else if (warp == activation_warp) {
         // ---------------- activations by TMA: one box per (tap, channel block)
         grid_dependency_wait();
-        ring_issue(lane, a.a_stages, group, my_tiles * stages_per_tile, smem_address(&tail->empty_a[0]),
+        ring_issue(lane, a.a_stages, group * m_tiles, my_tiles * stages_per_tile, smem_address(&tail->empty_a[0]),
                    smem_address(&tail->full_a[0]), abort, a.status, [&](int item, int stage, int part) {
                        const int local_tile = item / stages_per_tile;
-                       const int kb = (item - local_tile * stages_per_tile) * group + part;
+                       const int block = part / m_tiles;  // K block of the stage
+                       const int m = part - block * m_tiles;
+                       const int kb = (item - local_tile * stages_per_tile) * group + block;
                        int n_unused, tx;
-                       const int p_tile = by_n_tiles.divide(
+                       const int pg = by_n_tiles.divide(
                            static_cast<int>(blockIdx.x) + local_tile * static_cast<int>(gridDim.x), n_unused);
-                       const int ty = by_tiles_x.divide(p_tile, tx);
+                       // A sub-tile past the last patch loads rows below the image: zero fill.
+                       const int ty = by_tiles_x.divide(pg * m_tiles + m, tx);
                        const int tap = kb / a.c_blocks;
                        const int cb = kb - tap * a.c_blocks;
                        const int ky = tap / a.window.kernel_w;
@@ -1054,20 +1096,23 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
             const std::uint64_t b_desc0 = swizzled_descriptor(smem_address(b_smem), k_block);
             const int a_block16 = a_block_bytes >> 4;
             const int b_block16 = b_block_bytes >> 4;
+            const std::uint32_t tile_columns = static_cast<std::uint32_t>(m_tiles * n_tile);
             std::uint32_t g = 0;
             int local = 0;
             bool ok = true;
             int sa = 0, sb_ring = 0;                   // ring stages of the next A and B blocks
             std::uint32_t a_phase = 0, b_ring_phase = 0;
-            for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++local) {
-                const int buffer = local % tmem_buffers;
-                const std::uint32_t use = static_cast<std::uint32_t>(local / tmem_buffers);
-                if (*abort || !barrier_sleep_wait(smem_address(&tail->tmem_empty[buffer]), (use & 1u) ^ 1u, a.status)) {
+            RingPosition accumulator{0, 0u};
+            for (int t = blockIdx.x; t < total_tiles && ok;
+                 t += gridDim.x, ++local, accumulator.advance(1, tmem_buffers)) {
+                const int buffer = accumulator.slot;
+                if (*abort ||
+                    !barrier_sleep_wait(smem_address(&tail->tmem_empty[buffer]), accumulator.phase ^ 1u, a.status)) {
                     *abort = 1;
                     break;
                 }
                 tmem_fence_after();
-                const std::uint32_t acc = tmem + static_cast<std::uint32_t>(buffer * n_tile);
+                const std::uint32_t acc = tmem + static_cast<std::uint32_t>(buffer) * tile_columns;
                 for (int kb0 = 0; kb0 < k_blocks; kb0 += group, ++g) {
                     // (TMA writes are ordered before the MMA's reads by the full
                     // barriers; only TMEM reuse needs a tcgen05 fence, above.)
@@ -1089,12 +1134,16 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
                     const std::uint64_t b_desc = b_desc0 +
                         static_cast<std::uint64_t>(((a.b_resident ? kb0 * b_block_bytes : sb_ring * b_stage_bytes)) >> 4);
                     const std::uint32_t first = kb0 == 0 ? 0u : 1u;
+                    const std::uint32_t sub_columns = static_cast<std::uint32_t>(n_tile);
                     if (steps == 4) {
-                        issue_stage_group<4>(group, acc, a_desc, b_desc, idesc, first, a_block16, b_block16);
+                        issue_stage_group<4, MTiles>(group, acc, sub_columns, a_desc, b_desc, idesc, first, a_block16,
+                                                     b_block16);
                     } else if (steps == 2) {
-                        issue_stage_group<2>(group, acc, a_desc, b_desc, idesc, first, a_block16, b_block16);
+                        issue_stage_group<2, MTiles>(group, acc, sub_columns, a_desc, b_desc, idesc, first, a_block16,
+                                                     b_block16);
                     } else {
-                        issue_stage_group<1>(group, acc, a_desc, b_desc, idesc, first, a_block16, b_block16);
+                        issue_stage_group<1, MTiles>(group, acc, sub_columns, a_desc, b_desc, idesc, first, a_block16,
+                                                     b_block16);
                     }
                     mma_commit(smem_address(&tail->empty_a[sa]));
                     if (!a.b_resident) mma_commit(smem_address(&tail->empty_b[sb_ring]));
@@ -1134,31 +1183,35 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
                 at[j] = make_short2(static_cast<short>(hy), static_cast<short>(hx));
             }
         }
-        for (int l = 0; l < my_tiles; ++l) {
-            const int slot = l % window_slots;
-            const std::uint32_t phase = static_cast<std::uint32_t>(l / window_slots) & 1u;
+        RingPosition ring{0, 0u};
+        for (int l = 0; l < my_tiles; ++l, ring.advance(1, window_slots)) {
+            const int slot = ring.slot;
             const bool waited =
-                *abort == 0 && barrier_sleep_wait(smem_address(&tail->window_empty[slot]), phase ^ 1u, a.status);
+                *abort == 0 && barrier_sleep_wait(smem_address(&tail->window_empty[slot]), ring.phase ^ 1u, a.status);
             if (!__all_sync(0xffffffffu, waited)) {
                 *abort = 1;
                 break;
             }
-            int n_unused, tx;
-            const int p_tile =
+            int n_unused;
+            const int pg =
                 by_n_tiles.divide(static_cast<int>(blockIdx.x) + l * static_cast<int>(gridDim.x), n_unused);
-            const int ty = by_tiles_x.divide(p_tile, tx);
-            const int iy0 = ty * a.patch_h - a.window.pad_top;
-            const int ix0 = tx * a.patch_w - a.window.pad_left;
-            float* halo = halo_maxima + slot * halo_slot_floats;
+            for (int m = 0; m < m_tiles; ++m) {
+                int tx;
+                const int ty = by_tiles_x.divide(pg * m_tiles + m, tx);  // past the last patch: all outside
+                const int iy0 = ty * a.patch_h - a.window.pad_top;
+                const int ix0 = tx * a.patch_w - a.window.pad_left;
+                float* halo = halo_maxima + slot * halo_slot + m * halo_slot_floats;
 #pragma unroll
-            for (int j = 0; j < halo_lane_items; ++j) {
-                const int i = lane + 32 * j;
-                if (i < halo_count) {
-                    const int iy = iy0 + at[j].x;
-                    const int ix = ix0 + at[j].y;
-                    const bool inside = iy >= 0 && iy < a.in_h && ix >= 0 && ix < a.in_w;
-                    cp_async4(smem_address(halo + i),
-                              a.pixel_max + (inside ? static_cast<std::size_t>(iy) * a.in_w + ix : 0), inside ? 4 : 0);
+                for (int j = 0; j < halo_lane_items; ++j) {
+                    const int i = lane + 32 * j;
+                    if (i < halo_count) {
+                        const int iy = iy0 + at[j].x;
+                        const int ix = ix0 + at[j].y;
+                        const bool inside = iy >= 0 && iy < a.in_h && ix >= 0 && ix < a.in_w;
+                        cp_async4(smem_address(halo + i),
+                                  a.pixel_max + (inside ? static_cast<std::size_t>(iy) * a.in_w + ix : 0),
+                                  inside ? 4 : 0);
+                    }
                 }
             }
             cp_async_arrive(smem_address(&tail->window_full[slot]));
@@ -1174,8 +1227,9 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
         const int parts = 3 / groups;
         const int row = quarter * 32 + lane;
         const std::uint32_t lane_base = static_cast<std::uint32_t>(quarter * 32) << 16;
-        const int pair_offset = a.chunk_add ? n_tile / 2 : 0;
-        const int columns = a.chunk_add ? n_tile / 2 : n_tile;
+        const bool chunk_add = fusions && a.chunk_add;
+        const int pair_offset = chunk_add ? n_tile / 2 : 0;
+        const int columns = chunk_add ? n_tile / 2 : n_tile;
         const int chunks = columns / 16;
         const int per_part = (chunks + parts - 1) / parts;
         const int first_column = min(part * per_part, chunks) * 16;
@@ -1190,61 +1244,66 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
         const int kernel_h = a.window.kernel_h;
         const int kernel_w = a.window.kernel_w;
         const int halo_w = a.patch_w + kernel_w - 1;
-        int local = first_local;
+        RingPosition halo_ring{0, 0u};
+        RingPosition accumulator{0, 0u};
+        halo_ring.advance(first_local, window_slots);
+        accumulator.advance(first_local, tmem_buffers);
         for (int t = static_cast<int>(blockIdx.x) + first_local * static_cast<int>(gridDim.x); t < total_tiles;
-             t += tile_step, local += groups) {
-            int n_index, tx;
-            const int p_tile = by_n_tiles.divide(t, n_index);
-            const int ty = by_tiles_x.divide(p_tile, tx);
-            const int y = ty * a.patch_h + patch_y;
-            const int x = tx * a.patch_w + patch_x;
-            const bool real = y < a.out_h && x < a.out_w;
-            const int p = real ? y * a.out_w + x : 0;
-            // This position's window from the tile's halo of pixel maxima: the
-            // largest maximum sets the exponent, a non-finite pixel makes the row
-            // NaN, and a non-zero pixel whose exponent differs from the largest
-            // marks the window as mixed (its result comes from the fallback).
-            const int slot = local % window_slots;
-            const bool ready = barrier_sleep_wait(smem_address(&tail->window_full[slot]),
-                                                  static_cast<std::uint32_t>(local / window_slots) & 1u, a.status);
+             t += tile_step, halo_ring.advance(groups, window_slots), accumulator.advance(groups, tmem_buffers)) {
+            int n_index;
+            const int pg = by_n_tiles.divide(t, n_index);
+            // This position's window in each sub-tile, from the tile's halos of
+            // pixel maxima: the largest maximum sets the exponent, a non-finite
+            // pixel makes the row NaN (window_nan), and a non-zero pixel whose
+            // exponent differs from the largest marks the window as mixed
+            // (window_mixed: its result comes from the fallback).
+            const int slot = halo_ring.slot;
+            const bool ready = barrier_sleep_wait(smem_address(&tail->window_full[slot]), halo_ring.phase, a.status);
             if (!__all_sync(0xffffffffu, ready)) {
                 *abort = 1;
                 break;
             }
-            float largest = 0.0f;
-            float smallest = __uint_as_float(0x7f800000u);  // smallest non-zero
-            {
-                const float* halo = halo_maxima + slot * halo_slot_floats + patch_y * halo_w + patch_x;
+            int codes[MTiles];
+#pragma unroll
+            for (int m = 0; m < MTiles; ++m) codes[m] = window_nan;
+            bool any_mixed = false;
+#pragma unroll
+#pragma unroll
+            for (int m = 0; m < MTiles; ++m) {
+                float largest = 0.0f;
+                float smallest = __uint_as_float(0x7f800000u);  // smallest non-zero
+                const float* halo = halo_maxima + slot * halo_slot + m * halo_slot_floats + patch_y * halo_w + patch_x;
 #pragma unroll
                 for (int ky = 0; ky < 3; ++ky) {
 #pragma unroll
                     for (int kx = 0; kx < 3; ++kx) {
                         if (ky < kernel_h && kx < kernel_w) {
-                            const float m = halo[ky * halo_w + kx];
-                            largest = fmaxf(largest, m);
-                            if (m > 0.0f) smallest = fminf(smallest, m);
+                            const float v = halo[ky * halo_w + kx];
+                            largest = fmaxf(largest, v);
+                            if (v > 0.0f) smallest = fminf(smallest, v);
                         }
+                    }
+                }
+                int tx;
+                const int ty = by_tiles_x.divide(pg * m_tiles + m, tx);
+                const bool real_m = pg * m_tiles + m < a.p_tiles && ty * a.patch_h + patch_y < a.out_h &&
+                    tx * a.patch_w + patch_x < a.out_w;
+                if (real_m && largest != __uint_as_float(0x7f800000u)) {
+                    codes[m] = activation_exponent(largest, 8);
+                    if (largest > 0.0f && frexp_exponent(smallest) != frexp_exponent(largest)) {
+                        codes[m] = window_mixed;
+                        any_mixed = true;
                     }
                 }
             }
             barrier_arrive(smem_address(&tail->window_empty[slot]));
-            int exponent = window_nan;
-            bool mixed = false;
-            if (real && largest != __uint_as_float(0x7f800000u)) {
-                exponent = activation_exponent(largest, 8);
-                mixed = largest > 0.0f && frexp_exponent(smallest) != frexp_exponent(largest);
-            }
-            if (a.fallback != nullptr && part == 0 && __any_sync(0xffffffffu, mixed) && lane == 0) {
+            if (a.fallback != nullptr && part == 0 && __any_sync(0xffffffffu, any_mixed) && lane == 0) {
                 atomicOr(a.fallback, 1u);
                 if (a.condition != 0) cudaGraphSetConditional(a.condition, 1u);
             }
-            // A mixed window's accumulators are not this position's result:
-            // nothing is stored for it (nor added to a staged maximum, which
-            // can only grow), and the fallback conv writes it instead.
-            const bool store = real && !mixed;
-            const int buffer = local % tmem_buffers;
-            const std::uint32_t use = static_cast<std::uint32_t>(local / tmem_buffers);
-            bool waited = *abort == 0 && barrier_sleep_wait(smem_address(&tail->tmem_full[buffer]), use & 1u, a.status);
+            const int buffer = accumulator.slot;
+            bool waited =
+                *abort == 0 && barrier_sleep_wait(smem_address(&tail->tmem_full[buffer]), accumulator.phase, a.status);
             waited = __all_sync(0xffffffffu, waited);  // tcgen05.ld is warp-aligned
             if (!waited) {
                 *abort = 1;
@@ -1252,8 +1311,22 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
             }
             tmem_fence_after();
             const int physical0 = n_index * n_tile;
-            const int logical0 = a.chunk_add ? n_index * (n_tile / 2) : physical0;
-            const std::uint32_t acc = tmem + static_cast<std::uint32_t>(buffer * n_tile) + lane_base;
+            const int logical0 = chunk_add ? n_index * (n_tile / 2) : physical0;
+            for (int m = 0; m < m_tiles; ++m) {
+            int tx;
+            const int ty = by_tiles_x.divide(pg * m_tiles + m, tx);
+            const int y = ty * a.patch_h + patch_y;
+            const int x = tx * a.patch_w + patch_x;
+            const bool real = pg * m_tiles + m < a.p_tiles && y < a.out_h && x < a.out_w;
+            const int p = real ? y * a.out_w + x : 0;
+            const int code = (MTiles == 1 || m == 0) ? codes[0] : codes[MTiles - 1];
+            // A mixed window's accumulators are not this position's result:
+            // nothing is stored for it (nor added to a staged maximum, which
+            // can only grow), and the fallback conv writes it instead.
+            const bool store = real && code != window_mixed;
+            const int exponent = code == window_mixed ? window_nan : code;
+            const std::uint32_t acc = tmem + static_cast<std::uint32_t>(buffer * m_tiles * n_tile + m * n_tile) +
+                lane_base;
             const bool normal = exponent >= -126 && exponent <= 127;
             const bool plain = normal || exponent == INT_MIN;
             const float power = normal ? power_of_two(exponent) : 1.0f;
@@ -1295,7 +1368,7 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
 #pragma unroll
                     for (int j = 0; j < 16; ++j) v[j] = xv.v[j];
                 }
-                if (a.wsilu) {
+                if (fusions && a.wsilu) {
                     Sixteen16 xv;
 #pragma unroll
                     for (int j = 0; j < 16; ++j) xv.v[j] = v[j];
@@ -1309,7 +1382,7 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
             for (int j0 = first_column; j0 < last_column; j0 += 16) {
                 float v[16];
                 values16(j0, v);
-                if (a.chunk_add) {
+                if (chunk_add) {
                     float w[16];
                     values16(j0 + pair_offset, w);
 #pragma unroll
@@ -1322,7 +1395,7 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
 #pragma unroll
                         for (int j = 0; j < 16; ++j) v[j] = canonical_nan();
                     }
-                    if (a.residual != nullptr) {
+                    if (fusions && a.residual != nullptr) {
                         float add[16];
                         if (a.residual_c_pad > 0) {
                             if (count > 0) {
@@ -1349,7 +1422,7 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
 #pragma unroll
                         for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], add[j]);
                     }
-                    if (a.out_max != nullptr) {
+                    if (fusions && a.out_max != nullptr) {
                         if (c0 < a.out_c_pad) {
                             float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.out) +
                                                                   static_cast<std::size_t>(p) * a.out_c_pad + c0);
@@ -1414,10 +1487,11 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
                 }
                 __syncwarp();  // tcgen05.ld is warp-aligned: reconverge before the next columns
             }
-            if (a.out_max != nullptr && store && first_column < last_column) {
+            if (fusions && a.out_max != nullptr && store && first_column < last_column) {
                 atomicMax(reinterpret_cast<unsigned int*>(a.out_max) + p,
                           __float_as_uint(max_from_magnitude_bits(staged_max)));
             }
+            }  // sub-tiles
             tmem_fence_before();
             barrier_arrive(smem_address(&tail->tmem_empty[buffer]));
         }
@@ -1472,7 +1546,10 @@ bool valid_direct(const DirectConvArgs& a) {
         a.positions == a.out_h * a.out_w &&
         a.group >= 1 && a.group <= 4 &&
         a.k_blocks % a.group == 0 &&
-        a.a_stages * a.group <= 32 && (a.b_resident || a.b_stages * a.group <= 32) &&
+        (a.m_tiles == 1 || (a.m_tiles == 2 && (a.group == 1 || a.group == 3) && 2 * a.n_tile <= 512 && !a.wsilu &&
+                            !a.chunk_add &&
+                            a.residual == nullptr && a.out_max == nullptr)) &&
+        a.a_stages * a.group * a.m_tiles <= 32 && (a.b_resident || a.b_stages * a.group <= 32) &&
         a.a_stages >= 2 && a.a_stages <= max_direct_stages && a.b_stages >= 1 &&
         a.b_stages <= max_direct_stages && (!a.b_resident || (a.n_tiles == 1 && a.b_stages == a.k_blocks)) &&
         (a.b_resident || a.b_stages >= 2) && a.d2s_block >= 0 &&
@@ -1489,10 +1566,10 @@ bool valid_direct(const DirectConvArgs& a) {
 }  // namespace
 
 int direct_conv_shared_bytes(int k_block, int n_tile, int n_tiles, int a_stages, int b_stages, int group,
-                             bool b_resident) {
-    return 1024 + a_stages * group * tile_positions_m * k_block + b_stages * (b_resident ? 1 : group) * n_tile * k_block +
-        tail_bytes() +
-        halo_ring_bytes() + column_bytes(n_tile * n_tiles);
+                             bool b_resident, int m_tiles) {
+    return 1024 + a_stages * group * m_tiles * tile_positions_m * k_block +
+        b_stages * (b_resident ? 1 : group) * n_tile * k_block + tail_bytes() + halo_ring_bytes(m_tiles) +
+        column_bytes(n_tile * n_tiles);
 }
 
 cudaError_t encode_activation_map(CUtensorMap* map, const void* base, std::uint64_t c8, std::uint64_t height,
@@ -1662,22 +1739,31 @@ cudaError_t direct_conv(const CUtensorMap& a_map, const CUtensorMap& b_map, cons
     if (!valid_direct(args)) return cudaErrorInvalidValue;
     // As many accumulator buffers as fit in TMEM's 512 columns (n_tile <= 256: two
     // at least), up to eight; the allocation is the next power of two.
-    const int buffers = std::min(max_tmem_buffers, 512 / args.n_tile);
+    const int tile_columns = args.m_tiles * args.n_tile;
+    const int buffers = std::min(max_tmem_buffers, 512 / tile_columns);
     std::uint32_t columns = 32;
-    while (static_cast<int>(columns) < buffers * args.n_tile) columns <<= 1;
+    while (static_cast<int>(columns) < buffers * tile_columns) columns <<= 1;
     const int smem = direct_conv_shared_bytes(args.k_block, args.n_tile, args.n_tiles, args.a_stages, args.b_stages,
-                                              args.group, args.b_resident != 0);
+                                              args.group, args.b_resident != 0, args.m_tiles);
     if (smem > direct_conv_max_shared) return cudaErrorInvalidValue;
     static bool configured = false;
     if (!configured) {
-        const cudaError_t set = cudaFuncSetAttribute(direct_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                     direct_conv_max_shared);
+        cudaError_t set = cudaFuncSetAttribute(direct_conv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               direct_conv_max_shared);
+        if (set == cudaSuccess) {
+            set = cudaFuncSetAttribute(direct_conv_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       direct_conv_max_shared);
+        }
         if (set != cudaSuccess) return set;
         configured = true;
     }
-    const int tiles = args.p_tiles * args.n_tiles;
+    const int tiles = (args.p_tiles + args.m_tiles - 1) / args.m_tiles * args.n_tiles;
     const int grid = tiles < sm_count ? tiles : sm_count;
-    return launch_overlapped(direct_conv_kernel, dim3(grid), dim3(direct_threads), smem, stream, a_map, b_map, args,
+    if (args.m_tiles == 2) {
+        return launch_overlapped(direct_conv_kernel<2>, dim3(grid), dim3(direct_threads), smem, stream, a_map, b_map,
+                                 args, buffers, columns);
+    }
+    return launch_overlapped(direct_conv_kernel<1>, dim3(grid), dim3(direct_threads), smem, stream, a_map, b_map, args,
                              buffers, columns);
 }
 

@@ -158,6 +158,8 @@ struct DirectConvArgs {
     int k_blocks;                  // taps * c_blocks
     int group;                     // K blocks per pipeline stage (1-4, dividing k_blocks; resident weights stay
                                    // one block per stage)
+    int m_tiles;                   // patches of 128 positions per tile sharing each B block (1 or 2): two
+                                   // accumulators of n_tile columns; plain or depth_to_space stores only
     int positions, p_tiles;        // out_h * out_w; tiles_y * tiles_x
     int patch_h, patch_w, tiles_y, tiles_x;
     int a_stages, b_stages;
@@ -205,7 +207,7 @@ cudaError_t encode_weight_map(CUtensorMap* map, const void* base, std::uint64_t 
 cudaError_t direct_conv(const CUtensorMap& a_map, const CUtensorMap& b_map, const DirectConvArgs& args,
                         cudaStream_t stream);
 int direct_conv_shared_bytes(int k_block, int n_tile, int n_tiles, int a_stages, int b_stages, int group,
-                             bool b_resident);
+                             bool b_resident, int m_tiles);
 constexpr int direct_conv_max_shared = 232448;
 
 // Diagnostics: one thread waits on an mbarrier that nothing arrives on, with the

@@ -599,3 +599,28 @@ def test_three_channel_fields(cuda, oracle, half, width, stride):
         assert_half_parity(program, [x], oracle, label)
     else:
         assert_parity(program, [x], oracle, label)
+
+
+@pytest.mark.parametrize("half", [False, True], ids=["f32", "f16"])
+@pytest.mark.parametrize("shape", [(128, 256, 33, 47, None), (256, 256, 12, 90, None), (128, 512, 9, 200, None),
+                                   (128, 512, 20, 45, 2)],
+                         ids=["128to256", "256to256", "two_n_tiles", "d2s"])
+def test_paired_tiles(cuda, oracle, half, shape):
+    """Deep-K w8a8 3x3 convs with 128-byte K blocks and few tiles: the planner
+    pairs two patches per tile, sharing each weight block between two
+    accumulators. Ragged patch counts leave the last pair half empty; the
+    inputs mix magnitudes (mixed windows: the fallback writes those
+    positions), zeros and non-finite values."""
+    cin, cout, h, w, block = shape
+    stream = SeededStream(300 + cin + cout + h)
+    program = d2s_program(stream, cin, cout, block, (8, 8)) if block else \
+        conv_program(stream, cin, cout, (3, 3), (1, 1), (1, 1, 1, 1), (8, 8))
+    x = stream.tensor(cin, h, w, 2.0)
+    x[:, h // 3, :] *= np.float32(0.01)   # rows of much smaller pixels: mixed windows around them
+    x[:, :, 5] = 0.0                      # an all-zero column
+    x[3, 2, 7] = np.inf                   # one non-finite pixel: NaN rows around it
+    label = f"paired {cin}->{cout} {h}x{w}"
+    if half:
+        assert_half_parity(program, [x], oracle, label)
+    else:
+        assert_parity(program, [x], oracle, label)
