@@ -953,10 +953,11 @@ __device__ __forceinline__ void ring_issue(int lane, int ring, int per_item, int
     __syncwarp();
 }
 
-// MTiles = 2: two patches per tile sharing each B block; that instance carries
-// no WSiLU, chunk-add, residual or staged output (the planner pairs only plain
-// and depth_to_space stores), which keeps it within the register budget.
-template <int MTiles>
+// MTiles = 2: two patches per tile sharing each B block. Fusions = false: no
+// WSiLU, chunk-add, residual or staged output (plain or depth_to_space stores);
+// those instances keep registers for a TMEM load one chunk ahead in the
+// epilogue. Pairs exist only without fusions.
+template <int MTiles, bool Fusions>
 __global__ void __launch_bounds__(direct_threads, 1)
 direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map,
                    DirectConvArgs a, int tmem_buffers, std::uint32_t tmem_columns) {
@@ -969,7 +970,8 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
     // their B boxes unless the weights are resident, one K block per stage).
     const int group = a.group;
     constexpr int m_tiles = MTiles;  // sub-tiles of 128 positions sharing each B stage
-    constexpr bool fusions = MTiles == 1;
+    static_assert(MTiles == 1 || !Fusions, "paired tiles carry no fusions");
+    constexpr bool fusions = Fusions;
     const int a_block_bytes = tile_positions_m * k_block;
     const int b_block_bytes = n_tile * k_block;
     const int a_stage_bytes = group * m_tiles * a_block_bytes;
@@ -1379,15 +1381,8 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
             };
 
             std::uint32_t staged_max = 0;
-            for (int j0 = first_column; j0 < last_column; j0 += 16) {
-                float v[16];
-                values16(j0, v);
-                if (chunk_add) {
-                    float w[16];
-                    values16(j0 + pair_offset, w);
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], w[j]);
-                }
+            // Stores (and residual adds, staged maxima) of the 16 values at columns j0..
+            auto emit = [&](int j0, float (&v)[16]) {
                 const int c0 = logical0 + j0;
                 const int count = a.out_channels - c0 < 16 ? a.out_channels - c0 : 16;
                 if (store) {
@@ -1485,7 +1480,76 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
                         }
                     }
                 }
-                __syncwarp();  // tcgen05.ld is warp-aligned: reconverge before the next columns
+            };
+            if constexpr (Fusions) {
+                for (int j0 = first_column; j0 < last_column; j0 += 16) {
+                    float v[16];
+                    values16(j0, v);
+                    if (chunk_add) {
+                        float w[16];
+                        values16(j0 + pair_offset, w);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], w[j]);
+                    }
+                    emit(j0, v);
+                    __syncwarp();  // tcgen05.ld is warp-aligned: reconverge before the next columns
+                }
+            } else {
+                // The next chunk's TMEM load is issued before this chunk's
+                // arithmetic and stores, which hide its latency.
+                int hh[16];
+                if (first_column < last_column) {
+                    tmem_load16(acc + static_cast<std::uint32_t>(first_column), hh);
+                    tmem_load_wait();
+                }
+                for (int j0 = first_column; j0 < last_column; j0 += 16) {
+                    const bool more = j0 + 16 < last_column;
+                    int next[16];
+                    if (more) tmem_load16(acc + static_cast<std::uint32_t>(j0 + 16), next);
+                    const float4* scale4 = reinterpret_cast<const float4*>(column_scale + physical0 + j0);
+                    const float4* bias4 = reinterpret_cast<const float4*>(column_bias + physical0 + j0);
+                    float v[16];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const float4 f = scale4[q];
+                        v[4 * q] = __fmul_rn(__int2float_rn(hh[4 * q]), f.x);
+                        v[4 * q + 1] = __fmul_rn(__int2float_rn(hh[4 * q + 1]), f.y);
+                        v[4 * q + 2] = __fmul_rn(__int2float_rn(hh[4 * q + 2]), f.z);
+                        v[4 * q + 3] = __fmul_rn(__int2float_rn(hh[4 * q + 3]), f.w);
+                    }
+                    if (plain) {
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const float4 h = bias4[q];
+                            v[4 * q] = __fadd_rn(__fmul_rn(v[4 * q], power), h.x);
+                            v[4 * q + 1] = __fadd_rn(__fmul_rn(v[4 * q + 1], power), h.y);
+                            v[4 * q + 2] = __fadd_rn(__fmul_rn(v[4 * q + 2], power), h.z);
+                            v[4 * q + 3] = __fadd_rn(__fmul_rn(v[4 * q + 3], power), h.w);
+                        }
+                    } else {
+                        Sixteen16 xv, bv;
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const float4 h = bias4[q];
+                            bv.v[4 * q] = h.x;
+                            bv.v[4 * q + 1] = h.y;
+                            bv.v[4 * q + 2] = h.z;
+                            bv.v[4 * q + 3] = h.w;
+                        }
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) xv.v[j] = v[j];
+                        xv = direct_ldexp_add16(xv, bv, exponent);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) v[j] = xv.v[j];
+                    }
+                    emit(j0, v);
+                    if (more) {
+                        tmem_load_wait();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) hh[j] = next[j];
+                    }
+                    __syncwarp();  // tcgen05.ld is warp-aligned: reconverge before the next columns
+                }
             }
             if (fusions && a.out_max != nullptr && store && first_column < last_column) {
                 atomicMax(reinterpret_cast<unsigned int*>(a.out_max) + p,
@@ -1748,10 +1812,14 @@ cudaError_t direct_conv(const CUtensorMap& a_map, const CUtensorMap& b_map, cons
     if (smem > direct_conv_max_shared) return cudaErrorInvalidValue;
     static bool configured = false;
     if (!configured) {
-        cudaError_t set = cudaFuncSetAttribute(direct_conv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               direct_conv_max_shared);
+        cudaError_t set = cudaFuncSetAttribute(direct_conv_kernel<1, true>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, direct_conv_max_shared);
         if (set == cudaSuccess) {
-            set = cudaFuncSetAttribute(direct_conv_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            set = cudaFuncSetAttribute(direct_conv_kernel<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       direct_conv_max_shared);
+        }
+        if (set == cudaSuccess) {
+            set = cudaFuncSetAttribute(direct_conv_kernel<2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        direct_conv_max_shared);
         }
         if (set != cudaSuccess) return set;
@@ -1760,11 +1828,16 @@ cudaError_t direct_conv(const CUtensorMap& a_map, const CUtensorMap& b_map, cons
     const int tiles = (args.p_tiles + args.m_tiles - 1) / args.m_tiles * args.n_tiles;
     const int grid = tiles < sm_count ? tiles : sm_count;
     if (args.m_tiles == 2) {
-        return launch_overlapped(direct_conv_kernel<2>, dim3(grid), dim3(direct_threads), smem, stream, a_map, b_map,
-                                 args, buffers, columns);
+        return launch_overlapped(direct_conv_kernel<2, false>, dim3(grid), dim3(direct_threads), smem, stream, a_map,
+                                 b_map, args, buffers, columns);
     }
-    return launch_overlapped(direct_conv_kernel<1>, dim3(grid), dim3(direct_threads), smem, stream, a_map, b_map, args,
-                             buffers, columns);
+    const bool fusions = args.wsilu || args.chunk_add || args.residual != nullptr || args.out_max != nullptr;
+    if (fusions) {
+        return launch_overlapped(direct_conv_kernel<1, true>, dim3(grid), dim3(direct_threads), smem, stream, a_map,
+                                 b_map, args, buffers, columns);
+    }
+    return launch_overlapped(direct_conv_kernel<1, false>, dim3(grid), dim3(direct_threads), smem, stream, a_map, b_map,
+                             args, buffers, columns);
 }
 
 }  // namespace nvcr_sm100::kernels
