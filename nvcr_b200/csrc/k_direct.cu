@@ -410,16 +410,16 @@ __device__ __forceinline__ std::uint32_t word_of(const uint4& v, int w) {
     return w == 0 ? v.x : (w == 1 ? v.y : (w == 2 ? v.z : v.w));
 }
 
-__global__ void __launch_bounds__(256) quantise_half_planes_kernel(const __half* __restrict__ in, int channels,
-                                                                   int c8, int pixels, int sub_tiles,
-                                                                   std::int8_t* __restrict__ out,
-                                                                   float* __restrict__ pixel_max,
-                                                                   unsigned int* __restrict__ clear_word) {
+template <int CPT>  // channels per thread: 16 (8 also compiles: half the registers)
+__global__ void __launch_bounds__(CPT == 8 ? 512 : 256, CPT == 8 ? 2 : 1)
+    quantise_half_planes_kernel(const __half* __restrict__ in, int channels, int c8, int pixels, int sub_tiles,
+                                std::int8_t* __restrict__ out, float* __restrict__ pixel_max,
+                                unsigned int* __restrict__ clear_word) {
     grid_dependency_wait();
     launch_dependents();
     if (clear_word != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *clear_word = 0u;
     extern __shared__ uint4 group_maxima[];  // [sub_tiles][groups][16]
-    const int groups = c8 / 16;
+    const int groups = c8 / CPT;
     const int per_tile = 16 * groups;
     const int s = static_cast<int>(threadIdx.x) / per_tile;
     const int r = static_cast<int>(threadIdx.x) - s * per_tile;
@@ -427,16 +427,16 @@ __global__ void __launch_bounds__(256) quantise_half_planes_kernel(const __half*
     const int v = r & 15;
     const long long p0 = (static_cast<long long>(blockIdx.x) * sub_tiles + s) * 128 + v * 8;
     const bool live = p0 < pixels;
-    uint4 x[16];
+    uint4 x[CPT];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-        const int c = cg * 16 + j;
+    for (int j = 0; j < CPT; ++j) {
+        const int c = cg * CPT + j;
         x[j] = make_uint4(0u, 0u, 0u, 0u);
         if (live && c < channels) x[j] = __ldg(reinterpret_cast<const uint4*>(in + static_cast<std::size_t>(c) * pixels + p0));
     }
     std::uint32_t m[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
+    for (int j = 0; j < CPT; ++j) {
 #pragma unroll
         for (int w = 0; w < 4; ++w) m[w] = __vmaxu2(m[w], word_of(x[j], w) & 0x7fff7fffu);
     }
@@ -471,12 +471,12 @@ __global__ void __launch_bounds__(256) quantise_half_planes_kernel(const __half*
         target[1] = make_float4(maxima[4], maxima[5], maxima[6], maxima[7]);
     }
     constexpr std::uint32_t magic = 0x66006600u;  // 1536 in both halves
-    std::int8_t* row = out + p0 * c8 + cg * 16;
+    std::int8_t* row = out + p0 * c8 + cg * CPT;
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
-        std::uint32_t even[4], odd[4];  // records of pixels 2w and 2w + 1, channels 4k .. 4k + 3 in word k
+        std::uint32_t even[CPT / 4], odd[CPT / 4];  // records of pixels 2w and 2w + 1, channels 4k .. 4k + 3 in word k
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
+        for (int k = 0; k < CPT / 4; ++k) {
             const std::uint32_t r0 = hfma2_bits(word_of(x[4 * k], w), scale_bits[w], magic);
             const std::uint32_t r1 = hfma2_bits(word_of(x[4 * k + 1], w), scale_bits[w], magic);
             const std::uint32_t r2 = hfma2_bits(word_of(x[4 * k + 2], w), scale_bits[w], magic);
@@ -493,7 +493,7 @@ __global__ void __launch_bounds__(256) quantise_half_planes_kernel(const __half*
             if ((slow >> p) & 1u) {
                 const PixelScale sc = pixel_scale(maxima[p]);
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
+                for (int k = 0; k < CPT / 4; ++k) {
                     std::uint32_t word = 0;
 #pragma unroll
                     for (int b = 0; b < 4; ++b) {
@@ -505,8 +505,12 @@ __global__ void __launch_bounds__(256) quantise_half_planes_kernel(const __half*
                     words[k] = word;
                 }
             }
-            *reinterpret_cast<uint4*>(row + static_cast<std::size_t>(p) * c8) =
-                make_uint4(words[0], words[1], words[2], words[3]);
+            if constexpr (CPT == 16) {
+                *reinterpret_cast<uint4*>(row + static_cast<std::size_t>(p) * c8) =
+                    make_uint4(words[0], words[1], words[2], words[3]);
+            } else {
+                *reinterpret_cast<uint2*>(row + static_cast<std::size_t>(p) * c8) = make_uint2(words[0], words[1]);
+            }
         }
     }
 }
@@ -615,7 +619,7 @@ __global__ void __launch_bounds__(field_run) quantise_fields_fixed_kernel(const 
                                                                           float* __restrict__ field_max) {
     grid_dependency_wait();
     launch_dependents();
-    extern __shared__ float rows[];  // [C * KH][span]
+    extern __shared__ float rows[];  // [C * KH][pitch], column 0 at input column ix0 - shift
     constexpr int values = C * KH * KW;
     static_assert(values <= C8 && C8 % 32 == 0 && C8 <= 64, "field width");
     const int oy = blockIdx.y;
@@ -623,11 +627,15 @@ __global__ void __launch_bounds__(field_run) quantise_fields_fixed_kernel(const 
     const int iy0 = oy * w.stride_y - w.pad_top;
     const int ix0 = ox0 * w.stride_x - w.pad_left;
     const unsigned plane = static_cast<unsigned>(in_h) * static_cast<unsigned>(in_w);
-    if (Half && vector_rows) {
-        // 16-byte loads from the aligned column at or before ix0 (in_w is a
-        // multiple of 8, so every row starts 16-byte aligned).
-        const int a0 = ix0 >= 0 ? (ix0 & ~7) : -((-ix0 + 7) & ~7);
-        const int vectors = (ix0 + span - a0 + 7) / 8;
+    // Staged rows start at the aligned column at or before ix0 when 16-byte row
+    // loads apply (in_w a multiple of 8: every row starts 16-byte aligned), so
+    // each load becomes two 16-byte shared stores; `shift` = ix0 - that column.
+    const bool vectors_apply = Half && vector_rows;
+    const int a0 = vectors_apply ? (ix0 >= 0 ? (ix0 & ~7) : -((-ix0 + 7) & ~7)) : ix0;
+    const int shift = ix0 - a0;
+    const int pitch = (span + 7 + 7) & ~7;  // the shift (< 8) plus span, in whole 8-float vectors
+    if (vectors_apply) {
+        const int vectors = (shift + span + 7) / 8;
         for (int i = threadIdx.x; i < C * KH * vectors; i += field_run) {
             const int rc = i / vectors;
             const int vcol = i - rc * vectors;
@@ -653,13 +661,15 @@ __global__ void __launch_bounds__(field_run) quantise_fields_fixed_kernel(const 
                                  h[4] | (static_cast<unsigned>(h[5]) << 16), h[6] | (static_cast<unsigned>(h[7]) << 16));
             }
             const std::uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+            float f[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                const int col = x0 + j - ix0;
-                if (col >= 0 && col < span) {
-                    rows[rc * span + col] =
-                        __half2float(__ushort_as_half(static_cast<unsigned short>(words[j >> 1] >> (16 * (j & 1)))));
-                }
+                f[j] = __half2float(__ushort_as_half(static_cast<unsigned short>(words[j >> 1] >> (16 * (j & 1)))));
+            }
+            if (8 * vcol + 8 <= pitch) {
+                float4* target = reinterpret_cast<float4*>(rows + rc * pitch + 8 * vcol);
+                target[0] = make_float4(f[0], f[1], f[2], f[3]);
+                target[1] = make_float4(f[4], f[5], f[6], f[7]);
             }
         }
     } else {
@@ -674,13 +684,13 @@ __global__ void __launch_bounds__(field_run) quantise_fields_fixed_kernel(const 
                 const unsigned at = static_cast<unsigned>(c) * plane + static_cast<unsigned>(iy) * in_w + ix;
                 v = Half ? __half2float(static_cast<const __half*>(in)[at]) : static_cast<const float*>(in)[at];
             }
-            rows[i] = v;
+            rows[rc * pitch + col] = v;
         }
     }
     __syncthreads();
     const int ox = ox0 + static_cast<int>(threadIdx.x);
     if (ox >= out_w) return;
-    const float* base = rows + static_cast<int>(threadIdx.x) * w.stride_x;
+    const float* base = rows + shift + static_cast<int>(threadIdx.x) * w.stride_x;
     float v[C8];
     std::uint32_t m = 0;
 #pragma unroll
@@ -688,7 +698,7 @@ __global__ void __launch_bounds__(field_run) quantise_fields_fixed_kernel(const 
         if (k < values) {
             const int c = k / (KH * KW);
             const int tap = k % (KH * KW);
-            v[k] = base[(c * KH + tap / KW) * span + tap % KW];
+            v[k] = base[(c * KH + tap / KW) * pitch + tap % KW];
             m = max(m, magnitude_bits_of(v[k]));
         } else {
             v[k] = 0.0f;
@@ -1690,14 +1700,18 @@ cudaError_t quantise_pixels(const void* in, PixelSource form, int channels, int 
     const bool half = form == PixelSource::planes_f16;
     if (half && c8 <= half_planes_max_c8 && pixels % 8 == 0 && (reinterpret_cast<std::uintptr_t>(in) & 15u) == 0 &&
         (reinterpret_cast<std::uintptr_t>(pixel_max) & 15u) == 0) {
-        const int per_tile = c8;  // 16 threads per channel group of 16
+        // Sixteen channels per thread (16 threads per group of 16). (Eight per
+        // thread, for twice the resident blocks, measured slower: the per-pixel
+        // work doubles and the kernel spills.)
+        const int per_tile = c8;
         const int sub_tiles = per_tile >= 256 ? 1 : 256 / per_tile;
         const long long block_pixels = 128LL * sub_tiles;
         const unsigned blocks = static_cast<unsigned>((pixels + block_pixels - 1) / block_pixels);
         const std::size_t bytes = static_cast<std::size_t>(sub_tiles) * per_tile * sizeof(uint4);
-        return launch_overlapped(quantise_half_planes_kernel, dim3(blocks), dim3(static_cast<unsigned>(per_tile * sub_tiles)),
-                                 bytes, stream, static_cast<const __half*>(in), channels, c8, pixels, sub_tiles, out,
-                                 pixel_max, clear_word);
+        return launch_overlapped(quantise_half_planes_kernel<16>, dim3(blocks),
+                                 dim3(static_cast<unsigned>(per_tile * sub_tiles)), bytes, stream,
+                                 static_cast<const __half*>(in), channels, c8, pixels, sub_tiles, out, pixel_max,
+                                 clear_word);
     }
     // Planes whose length is a whole number of 16-byte vectors and whose base is
     // 16-byte aligned take the vector-load kernel.
@@ -1753,7 +1767,8 @@ cudaError_t quantise_fields(const void* in, int source_half, int channels, int i
     if (channels == 3 && window.kernel_h == 3 && window.kernel_w == 3 && c8 == 32 && span <= 4 * field_run &&
         out_h <= 65535 && static_cast<long long>(channels) * in_h * in_w < (1LL << 31)) {
         const dim3 grid(static_cast<unsigned>((out_w + field_run - 1) / field_run), static_cast<unsigned>(out_h));
-        const std::size_t bytes = static_cast<std::size_t>(channels) * window.kernel_h * span * 4;
+        const int pitch = (span + 7 + 7) & ~7;
+        const std::size_t bytes = static_cast<std::size_t>(channels) * window.kernel_h * pitch * 4;
         const int vector_rows = source_half && in_w % 8 == 0 && (reinterpret_cast<std::uintptr_t>(in) & 15u) == 0;
         return source_half ? launch_overlapped(quantise_fields_fixed_kernel<true, 3, 3, 3, 32>, grid, dim3(field_run),
                                                bytes, stream, in, in_h, in_w, window, out_h, out_w, span, vector_rows,
