@@ -411,7 +411,7 @@ __device__ __forceinline__ std::uint32_t word_of(const uint4& v, int w) {
 }
 
 template <int CPT>  // channels per thread: 16 (8 also compiles: half the registers)
-__global__ void __launch_bounds__(CPT == 8 ? 512 : 256, CPT == 8 ? 2 : 1)
+__global__ void __launch_bounds__(CPT == 8 ? 512 : 256, 2)
     quantise_half_planes_kernel(const __half* __restrict__ in, int channels, int c8, int pixels, int sub_tiles,
                                 std::int8_t* __restrict__ out, float* __restrict__ pixel_max,
                                 unsigned int* __restrict__ clear_word) {
