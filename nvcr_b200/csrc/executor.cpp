@@ -3,6 +3,7 @@
 #include <algorithm>
 #include <functional>
 #include <climits>
+#include <cmath>
 #include <cstdlib>
 #include <cstring>
 #include <limits>
@@ -57,6 +58,15 @@ struct Executor::IntegerConv {
     int k_block{0}, c_blocks{0}, direct_k_blocks{0};
     int direct_a_stages{0}, direct_b_stages{0}, direct_group{1};
     bool direct_b_resident{false};
+    // Every scale and bias finite (the direct conv's vector stores need no NaN
+    // handling), and every accumulator below 2^22 in magnitude (127 times the
+    // largest row sum of |q|: exact float conversion by integer addition).
+    bool finite_columns{true};
+    bool small_accumulators{false};
+    // Window exponents e for which y * 2^e is exact for every y = RN(x * scale)
+    // of the conv (|x| < 2^31, no overflow, nothing subnormal), so that
+    // RN(RN(y * 2^e) + bias) is one fused multiply-add; empty when lo > hi.
+    int fma_lo{1}, fma_hi{0};
     // Ring depths for tiles of two patches sharing each weight block (deep-K
     // convs with k_block 128 and at most 256 columns); 0 when not prepared.
     int pair_a_stages{0}, pair_b_stages{0}, pair_group{1};
@@ -630,6 +640,7 @@ Status Executor::prepare_integer_conv(std::size_t step_index) {
         if (row < 0) continue;
         scales[physical] = quantized.scales[static_cast<std::size_t>(row)];
         bias[physical] = program_.weights[node.bias_offset + static_cast<std::size_t>(row)];
+        if (!std::isfinite(scales[physical]) || !std::isfinite(bias[physical])) conv.finite_columns = false;
         long long high_sum = 0;
         long long low_sum = 0;
         for (int c = 0; c < conv.c_pad; ++c) {
@@ -641,6 +652,26 @@ Status Executor::prepare_integer_conv(std::size_t step_index) {
         }
         // cx (aw sum Wh + sum Wl') + K cw cx, over all K = k_taps * c_pad entries.
         row_terms[physical] = cx * (aw * high_sum + low_sum) + static_cast<long long>(conv.k_real) * cw * cx;
+    }
+    {
+        float smallest = std::numeric_limits<float>::infinity();
+        float largest = 0.0f;
+        for (int physical = 0; physical < n_padded; ++physical) {
+            const float magnitude = std::fabs(scales[physical]);
+            if (source_row(physical) < 0 || magnitude == 0.0f) continue;
+            smallest = std::min(smallest, magnitude);
+            largest = std::max(largest, magnitude);
+        }
+        if (!conv.finite_columns) {
+            conv.fma_lo = 1;
+            conv.fma_hi = 0;
+        } else if (largest == 0.0f) {
+            conv.fma_lo = -126;
+            conv.fma_hi = 127;
+        } else if (smallest >= std::numeric_limits<float>::min()) {
+            conv.fma_lo = std::max(-126, -126 - std::ilogb(smallest));
+            conv.fma_hi = std::min(127, 94 - std::ilogb(largest));
+        }
     }
     // column term factors: cw (ax sum Xh + sum Xl')
     const long long ax = conv.activation_limbs == 2 ? 256 : 1;
@@ -833,6 +864,7 @@ Status Executor::prepare_direct(IntegerConv& conv, const Step& step, const Node&
     const std::size_t row_bytes = static_cast<std::size_t>(taps) * conv.c8;
     std::vector<std::int8_t> matrix(static_cast<std::size_t>(n_padded) * row_bytes, 0);
     const int rows = node.out_channels;
+    long long largest_row_sum = 0;
     for (int physical = 0; physical < n_padded; ++physical) {
         int row = physical < rows ? physical : -1;
         if (conv.chunk_add) {
@@ -844,6 +876,7 @@ Status Executor::prepare_direct(IntegerConv& conv, const Step& step, const Node&
         }
         if (row < 0) continue;
         const std::size_t at = static_cast<std::size_t>(row) * node.in_channels;
+        long long row_sum = 0;
         for (int tap = 0; tap < taps; ++tap) {
             for (int c = 0; c < conv.c8; ++c) {
                 int q = 0;
@@ -854,9 +887,12 @@ Status Executor::prepare_direct(IntegerConv& conv, const Step& step, const Node&
                 }
                 matrix[static_cast<std::size_t>(physical) * row_bytes + static_cast<std::size_t>(tap) * conv.c8 + c] =
                     static_cast<std::int8_t>(q);
+                row_sum += q < 0 ? -q : q;
             }
         }
+        largest_row_sum = std::max(largest_row_sum, row_sum);
     }
+    conv.small_accumulators = largest_row_sum * 127 < (1LL << 22);
     cudaError_t status = cudaMalloc(&conv.direct_allocation, matrix.size());
     if (status != cudaSuccess) return cuda_error("cudaMalloc direct weights", status);
     status = cudaMemcpy(conv.direct_allocation, matrix.data(), matrix.size(), cudaMemcpyHostToDevice);
@@ -1289,6 +1325,14 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
         d.out_c_pad = out_c_pad;
         d.out_channels = conv.out_channels;
         d.d2s_block = step.d2s_block;
+        d.vector_store = out_half && step.d2s_block == 0 && !step.wsilu && !step.chunk_add && residual == nullptr &&
+                out_max == nullptr && conv.finite_columns && pc.d_patch_w % 8 == 0 && conv_out.width % 8 == 0 &&
+                conv.out_channels % 8 == 0 && (reinterpret_cast<std::uintptr_t>(out) & 15u) == 0
+            ? 1
+            : 0;
+        d.small_accumulators = conv.small_accumulators ? 1 : 0;
+        d.fma_lo = conv.fma_lo;
+        d.fma_hi = conv.fma_hi;
         d.fallback = fallback;
         d.status = status_;
         // In a captured run the fallback becomes a conditional node: the conv

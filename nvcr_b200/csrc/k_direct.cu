@@ -41,6 +41,7 @@
 #include "tcgen05.cuh"
 
 #include <climits>
+#include <type_traits>
 
 #include <cuda_fp16.h>
 
@@ -93,6 +94,12 @@ __device__ __forceinline__ std::uint64_t swizzled_descriptor(std::uint32_t addre
 
 // Bytes of the per-column scales and biases after the tail.
 __host__ __device__ constexpr int column_bytes(int columns) { return columns * 8; }
+
+// After the column parameters, per epilogue warp: one block of 16 channels x
+// 32 positions of FP16 results on its way from the accumulator layout (a thread
+// per position) to 16-byte runs of one channel's consecutive positions.
+constexpr int staging_warp_bytes = 16 * 32 * 2;
+constexpr int staging_bytes = epilogue_warps * staging_warp_bytes;
 
 __host__ __device__ constexpr int tail_bytes() { return static_cast<int>((sizeof(DirectTail) + 15) / 16 * 16); }
 
@@ -511,6 +518,166 @@ __global__ void __launch_bounds__(CPT == 8 ? 512 : 256, 2)
             } else {
                 *reinterpret_cast<uint2*>(row + static_cast<std::size_t>(p) * c8) = make_uint2(words[0], words[1]);
             }
+        }
+    }
+}
+
+// The same quantisation as a persistent, streamed kernel: one block of 256
+// threads per SM walks its tiles (sub_tiles x 128 pixels x c8 channels), whose
+// planes arrive by TMA (one [c8][128] FP16 box per sub-tile, channels past the
+// last zero-filled) into a ring of streamed_stages shared-memory stages issued
+// streamed_stages - 1 tiles ahead, so HBM reads of later tiles overlap the
+// arithmetic and stores of the current one. Per tile the arithmetic is the
+// plane kernel's above, reading the tile from shared memory.
+constexpr int streamed_stages = 3;
+constexpr int streamed_threads = 256;
+constexpr int streamed_stage_bytes = streamed_threads * 16 * 16;  // 16 channels x 8 pixels of FP16 a thread
+
+__global__ void __launch_bounds__(streamed_threads, 1)
+    quantise_half_planes_streamed_kernel(const __grid_constant__ CUtensorMap planes, int channels, int c8, int pixels,
+                                         int sub_tiles, int tiles, std::int8_t* __restrict__ out,
+                                         float* __restrict__ pixel_max, unsigned int* __restrict__ clear_word) {
+    extern __shared__ std::uint8_t streamed_raw[];
+    // TMA destinations start 1 KiB aligned (the allocation has 1 KiB spare).
+    std::uint8_t* streamed_smem =
+        streamed_raw + (((smem_address(streamed_raw) + 1023u) & ~1023u) - smem_address(streamed_raw));
+    constexpr int CPT = 16;
+    const int groups = c8 / CPT;
+    const int per_tile = 16 * groups;
+    uint4* group_maxima = reinterpret_cast<uint4*>(streamed_smem + streamed_stages * streamed_stage_bytes);
+    auto* full = reinterpret_cast<unsigned long long*>(group_maxima + sub_tiles * groups * 16);
+    __shared__ unsigned int failed;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < streamed_stages; ++s) barrier_init(smem_address(&full[s]), 1);
+        failed = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        fence_proxy_async_shared();
+    }
+    __syncthreads();
+    grid_dependency_wait();
+    launch_dependents();
+    if (clear_word != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *clear_word = 0u;
+    const int step = static_cast<int>(gridDim.x);
+    const int first = static_cast<int>(blockIdx.x);
+    const int my_tiles = first < tiles ? (tiles - first + step - 1) / step : 0;
+    const std::uint32_t stage_base = smem_address(streamed_smem);
+    const std::uint32_t sub_bytes = static_cast<std::uint32_t>(c8) * 256u;
+    auto issue = [&](int local, int stage) {
+        const std::uint32_t bar = smem_address(&full[stage]);
+        barrier_expect_bytes(bar, sub_bytes * static_cast<std::uint32_t>(sub_tiles));
+        const int tile = first + local * step;
+        for (int sub = 0; sub < sub_tiles; ++sub) {
+            tma_load_2d(stage_base + static_cast<std::uint32_t>(stage) * streamed_stage_bytes + sub * sub_bytes, &planes,
+                        bar, (tile * sub_tiles + sub) * 128, 0);
+        }
+    };
+    if (threadIdx.x == 0) {
+        for (int k = 0; k < streamed_stages - 1 && k < my_tiles; ++k) issue(k, k);
+    }
+    const int s = static_cast<int>(threadIdx.x) / per_tile;
+    const int r = static_cast<int>(threadIdx.x) - s * per_tile;
+    const int cg = r >> 4;
+    const int v = r & 15;
+    const bool active = s < sub_tiles;
+    int stage = 0;
+    std::uint32_t phase = 0;
+    for (int i = 0; i < my_tiles; ++i) {
+        if (threadIdx.x == 0 && i + streamed_stages - 1 < my_tiles) {
+            const int ahead = stage == 0 ? streamed_stages - 1 : stage - 1;  // (i + stages - 1) % stages
+            issue(i + streamed_stages - 1, ahead);
+        }
+        const bool landed = barrier_wait(smem_address(&full[stage]), phase, &failed);
+        if (!__syncthreads_and(landed ? 1 : 0)) return;  // a copy that never landed: nothing more is written
+        const int tile = first + i * step;
+        const long long p0 = (static_cast<long long>(tile) * sub_tiles + s) * 128 + v * 8;
+        const bool live = active && p0 < pixels;
+        const std::uint8_t* tile_smem = streamed_smem + stage * streamed_stage_bytes + s * c8 * 256;
+        uint4 x[CPT];
+#pragma unroll
+        for (int j = 0; j < CPT; ++j) {
+            x[j] = active ? *reinterpret_cast<const uint4*>(tile_smem + (cg * CPT + j) * 256 + v * 16)
+                          : make_uint4(0u, 0u, 0u, 0u);
+        }
+        std::uint32_t m[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+        for (int j = 0; j < CPT; ++j) {
+#pragma unroll
+            for (int w = 0; w < 4; ++w) m[w] = __vmaxu2(m[w], word_of(x[j], w) & 0x7fff7fffu);
+        }
+        if (active) group_maxima[(s * groups + cg) * 16 + v] = make_uint4(m[0], m[1], m[2], m[3]);
+        __syncthreads();
+        if (live) {
+            for (int g = 0; g < groups; ++g) {
+                const uint4 q = group_maxima[(s * groups + g) * 16 + v];
+                m[0] = __vmaxu2(m[0], q.x);
+                m[1] = __vmaxu2(m[1], q.y);
+                m[2] = __vmaxu2(m[2], q.z);
+                m[3] = __vmaxu2(m[3], q.w);
+            }
+            float maxima[8];
+            std::uint32_t scale_bits[4] = {0u, 0u, 0u, 0u};
+            std::uint32_t slow = 0;
+#pragma unroll
+            for (int p = 0; p < 8; ++p) {
+                const std::uint32_t magnitude = (m[p >> 1] >> (16 * (p & 1))) & 0xffffu;
+                const bool finite = magnitude < 0x7c00u;
+                const float maximum = finite ? __half2float(__ushort_as_half(static_cast<unsigned short>(magnitude)))
+                                             : __uint_as_float(0x7f800000u);
+                maxima[p] = maximum;
+                const int e = activation_exponent(maximum, 8);
+                const bool fast = finite && e >= -15 && e <= 14 && __fmul_rn(maximum, power_of_two(-e)) < 127.5f;
+                slow |= fast ? 0u : 1u << p;
+                scale_bits[p >> 1] |= (fast ? static_cast<std::uint32_t>(15 - e) << 10 : 0u) << (16 * (p & 1));
+            }
+            if (cg == 0) {
+                float4* target = reinterpret_cast<float4*>(pixel_max + p0);
+                target[0] = make_float4(maxima[0], maxima[1], maxima[2], maxima[3]);
+                target[1] = make_float4(maxima[4], maxima[5], maxima[6], maxima[7]);
+            }
+            constexpr std::uint32_t magic = 0x66006600u;  // 1536 in both halves
+            std::int8_t* row = out + p0 * c8 + cg * CPT;
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+                std::uint32_t even[CPT / 4], odd[CPT / 4];
+#pragma unroll
+                for (int k = 0; k < CPT / 4; ++k) {
+                    const std::uint32_t r0 = hfma2_bits(word_of(x[4 * k], w), scale_bits[w], magic);
+                    const std::uint32_t r1 = hfma2_bits(word_of(x[4 * k + 1], w), scale_bits[w], magic);
+                    const std::uint32_t r2 = hfma2_bits(word_of(x[4 * k + 2], w), scale_bits[w], magic);
+                    const std::uint32_t r3 = hfma2_bits(word_of(x[4 * k + 3], w), scale_bits[w], magic);
+                    const std::uint32_t lo = byte_perm(r0, r1, 0x6240u);
+                    const std::uint32_t hi = byte_perm(r2, r3, 0x6240u);
+                    even[k] = byte_perm(lo, hi, 0x5410u);
+                    odd[k] = byte_perm(lo, hi, 0x7632u);
+                }
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int p = 2 * w + e;
+                    std::uint32_t* words = e == 0 ? even : odd;
+                    if ((slow >> p) & 1u) {
+                        const PixelScale sc = pixel_scale(maxima[p]);
+#pragma unroll
+                        for (int k = 0; k < CPT / 4; ++k) {
+                            std::uint32_t word = 0;
+#pragma unroll
+                            for (int b = 0; b < 4; ++b) {
+                                const std::uint32_t bits = (word_of(x[4 * k + b], w) >> (16 * e)) & 0xffffu;
+                                const float value = __half2float(__ushort_as_half(static_cast<unsigned short>(bits)));
+                                const int q = sc.finite ? quantise_one(value, sc.normal, sc.scale, sc.exponent) : 0;
+                                word |= (static_cast<std::uint32_t>(q) & 0xffu) << (8 * b);
+                            }
+                            words[k] = word;
+                        }
+                    }
+                    *reinterpret_cast<uint4*>(row + static_cast<std::size_t>(p) * c8) =
+                        make_uint4(words[0], words[1], words[2], words[3]);
+                }
+            }
+        }
+        __syncthreads();  // the stage and the group maxima are free for the next tile
+        if (++stage == streamed_stages) {
+            stage = 0;
+            phase ^= 1u;
         }
     }
 }
@@ -997,6 +1164,7 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
         reinterpret_cast<float*>(reinterpret_cast<std::uint8_t*>(halo_maxima) + halo_ring_bytes(m_tiles));
     const int halo_slot = m_tiles * halo_slot_floats;  // floats of one tile's halos
     float* column_bias = column_scale + all_columns;
+    const std::uint32_t staging = smem_address(column_scale) + static_cast<std::uint32_t>(column_bytes(all_columns));
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     // A tile: m_tiles consecutive patches (p_tile = pg * m_tiles + m) of one N tile.
@@ -1504,6 +1672,107 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
                     emit(j0, v);
                     __syncwarp();  // tcgen05.ld is warp-aligned: reconverge before the next columns
                 }
+            } else if (a.vector_store != 0 &&
+                       __all_sync(0xffffffffu, !real || (code != window_mixed && exponent >= a.fma_lo &&
+                                                         exponent <= a.fma_hi && normal))) {
+                // Vector stores (every real position of the warp stored, with an
+                // exponent e for which y * 2^e is exact for every y = RN(x *
+                // scale) of the conv, so RN(RN(y * 2^e) + bias) = fma(y, 2^e,
+                // bias)). The accumulators come out in the fragment layout
+                // (16x256b: a thread holds two columns of lanes g and g + 8),
+                // are converted to FP16 pairs and stored transposed into the
+                // warp's staging block ([16 channels][32 positions], 16-byte
+                // pieces swizzled by (channel / 2) % 4: conflict-free both
+                // ways), from which each lane writes 8 positions of two channels.
+                const int g = lane >> 2;
+                const int t4 = lane & 3;
+                float powers[4];  // positions 8i + g of the warp (matrix i)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) powers[i] = __shfl_sync(0xffffffffu, power, 8 * i + g);
+                const bool piece_real = __shfl_sync(0xffffffffu, real ? 1 : 0, 8 * t4) != 0;
+                const int piece_p = __shfl_sync(0xffffffffu, p, 8 * t4);
+                const int store_channel = lane >> 2;
+                const std::size_t plane = static_cast<std::size_t>(a.positions);
+                uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(a.out) +
+                                                      static_cast<std::size_t>(logical0 + first_column + store_channel) *
+                                                          plane +
+                                                      piece_p);
+                const std::size_t dst_chunk = 2 * plane;  // 16 planes, in uint4
+                const std::size_t dst_half = plane;       // 8 planes, in uint4
+                // Stored channels left from the first column (multiples of 8).
+                const int stored = piece_real ? a.out_channels - logical0 - first_column : 0;
+                const std::uint32_t block = staging + static_cast<std::uint32_t>(warp * staging_warp_bytes);
+                const int row_channel = lane & 7;
+                const std::uint32_t st_address = block + static_cast<std::uint32_t>(
+                    row_channel * 64 + (((lane >> 3) ^ ((row_channel >> 1) & 3)) << 4));
+                const std::uint32_t ld_address = block + static_cast<std::uint32_t>(
+                    store_channel * 64 + ((t4 ^ ((store_channel >> 1) & 3)) << 4));
+                const std::uint32_t upper = acc + (16u << 16);  // TMEM lanes 16..31 of the warp
+                const float* scale_at = column_scale + physical0 + first_column + 2 * t4;
+                const float* bias_at = column_bias + physical0 + first_column + 2 * t4;
+                const int chunks16 = (last_column - first_column) >> 4;
+                auto load16 = [&](std::uint32_t (&r)[16], int c) {
+                    tmem_load_16x256b_x2(acc + static_cast<std::uint32_t>(first_column + 16 * c), r);
+                    tmem_load_16x256b_x2(upper + static_cast<std::uint32_t>(first_column + 16 * c), r + 8);
+                };
+                // Chunk c: channels 16c .. 16c + 15 from the first column. r[0..7]
+                // hold lanes g, g + 8 and r[8..15] lanes 16 + g, 24 + g; within
+                // each eight, columns 2t4, 2t4 + 1 of the first eight channels,
+                // then of the second eight.
+                auto columns = [&](auto small_tag) {
+                    constexpr bool small = decltype(small_tag)::value;
+                    std::uint32_t r[16];
+                    if (chunks16 > 0) {
+                        load16(r, 0);
+                        tmem_load_wait_regs(r);
+                    }
+                    for (int c = 0; c < chunks16; ++c) {
+                        const float2 s0 = *reinterpret_cast<const float2*>(scale_at + 16 * c);
+                        const float2 s1 = *reinterpret_cast<const float2*>(scale_at + 16 * c + 8);
+                        const float2 h0 = *reinterpret_cast<const float2*>(bias_at + 16 * c);
+                        const float2 h1 = *reinterpret_cast<const float2*>(bias_at + 16 * c + 8);
+                        std::uint32_t packed[2][4];
+#pragma unroll
+                        for (int half = 0; half < 2; ++half) {
+                            const float2 s = half == 0 ? s0 : s1;
+                            const float2 h = half == 0 ? h0 : h1;
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                const int at = (i >> 1) * 8 + half * 4 + (i & 1) * 2;
+                                float x0, x1;
+                                if (small) {  // exact: |r| < 2^22
+                                    x0 = __fadd_rn(__uint_as_float(r[at] + 0x4B400000u), -round_magic);
+                                    x1 = __fadd_rn(__uint_as_float(r[at + 1] + 0x4B400000u), -round_magic);
+                                } else {
+                                    x0 = __int2float_rn(static_cast<int>(r[at]));
+                                    x1 = __int2float_rn(static_cast<int>(r[at + 1]));
+                                }
+                                const float v0 = __fmaf_rn(__fmul_rn(x0, s.x), powers[i], h.x);
+                                const float v1 = __fmaf_rn(__fmul_rn(x1, s.y), powers[i], h.y);
+                                const __half2 pair = __floats2half2_rn(v0, v1);
+                                packed[half][i] = *reinterpret_cast<const std::uint32_t*>(&pair);
+                            }
+                        }
+                        // The next chunk's TMEM loads fly during this chunk's stores.
+                        const bool more = c + 1 < chunks16;
+                        if (more) load16(r, c + 1);
+                        stmatrix_x4_trans(st_address, packed[0]);
+                        stmatrix_x4_trans(st_address + 512u, packed[1]);
+                        __syncwarp();
+                        const uint4 first = load_shared_v4(ld_address);
+                        const uint4 second = load_shared_v4(ld_address + 512u);
+                        uint4* d = dst + static_cast<std::size_t>(c) * dst_chunk;
+                        if (16 * c < stored) d[0] = first;
+                        if (16 * c + 8 < stored) d[dst_half] = second;
+                        __syncwarp();  // the block is rewritten by the next chunk
+                        if (more) tmem_load_wait_regs(r);
+                    }
+                };
+                if (a.small_accumulators != 0) {
+                    columns(std::true_type{});
+                } else {
+                    columns(std::false_type{});
+                }
             } else {
                 // The next chunk's TMEM load is issued before this chunk's
                 // arithmetic and stores, which hide its latency.
@@ -1643,7 +1912,7 @@ int direct_conv_shared_bytes(int k_block, int n_tile, int n_tiles, int a_stages,
                              bool b_resident, int m_tiles) {
     return 1024 + a_stages * group * m_tiles * tile_positions_m * k_block +
         b_stages * (b_resident ? 1 : group) * n_tile * k_block + tail_bytes() + halo_ring_bytes(m_tiles) +
-        column_bytes(n_tile * n_tiles);
+        column_bytes(n_tile * n_tiles) + staging_bytes;
 }
 
 cudaError_t encode_activation_map(CUtensorMap* map, const void* base, std::uint64_t c8, std::uint64_t height,
@@ -1706,6 +1975,41 @@ cudaError_t quantise_pixels(const void* in, PixelSource form, int channels, int 
         const int per_tile = c8;
         const int sub_tiles = per_tile >= 256 ? 1 : 256 / per_tile;
         const long long block_pixels = 128LL * sub_tiles;
+        const long long tile_count = (pixels + block_pixels - 1) / block_pixels;
+        static const int sm_count = [] {
+            int device = 0;
+            int count = 148;
+            if (cudaGetDevice(&device) == cudaSuccess) cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, device);
+            return count;
+        }();
+        // Streamed (persistent blocks, planes by TMA: a box of 128 pixels x c8
+        // channel rows per sub-tile, rows past the last channel zero-filled)
+        // with several tiles per SM; with fewer, one tile per block and two
+        // blocks per SM measured faster.
+        const EncodeTiled encode = tiled_encoder();
+        CUtensorMap planes;
+        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(pixels), static_cast<cuuint64_t>(channels)};
+        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(pixels) * 2u};
+        const cuuint32_t box[2] = {128u, static_cast<cuuint32_t>(c8)};
+        const cuuint32_t element_strides[2] = {1u, 1u};
+        if (encode != nullptr && tile_count >= 4LL * sm_count && tile_count < (1LL << 31) &&
+            encode(&planes, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(in), dims, strides, box,
+                   element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
+            const std::size_t bytes = 1024 + static_cast<std::size_t>(streamed_stages) * streamed_stage_bytes +
+                static_cast<std::size_t>(sub_tiles) * c8 * 16 + streamed_stages * sizeof(unsigned long long);
+            static bool streamed_configured = false;
+            if (!streamed_configured) {
+                cudaFuncSetAttribute(quantise_half_planes_streamed_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(streamed_stages * streamed_stage_bytes + 9216));
+                streamed_configured = true;
+            }
+            const int tiles = static_cast<int>(tile_count);
+            const int grid = tiles < sm_count ? tiles : sm_count;
+            return launch_overlapped(quantise_half_planes_streamed_kernel, dim3(static_cast<unsigned>(grid)),
+                                     dim3(streamed_threads), bytes, stream, planes, channels, c8, pixels, sub_tiles,
+                                     tiles, out, pixel_max, clear_word);
+        }
         const unsigned blocks = static_cast<unsigned>((pixels + block_pixels - 1) / block_pixels);
         const std::size_t bytes = static_cast<std::size_t>(sub_tiles) * per_tile * sizeof(uint4);
         return launch_overlapped(quantise_half_planes_kernel<16>, dim3(blocks),

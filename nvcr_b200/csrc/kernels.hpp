@@ -178,6 +178,17 @@ struct DirectConvArgs {
     int out_c_pad;
     int out_channels;
     int d2s_block;
+    // 1 when the plain FP16 output may be written as 16-byte runs of 8 positions
+    // of one channel: no fusions, no depth_to_space, patch_w, out_w and
+    // out_channels multiples of 8, `out` 16-byte aligned, finite scales and biases.
+    int vector_store;
+    // 1 when every accumulator is below 2^22 in magnitude (127 * the largest
+    // row sum of |weights|), so it converts to float exactly by integer addition.
+    int small_accumulators;
+    // Window exponents for which the vector stores fuse the power-of-two scale
+    // and the bias add into one multiply-add (exact there); others take the
+    // per-channel stores.
+    int fma_lo, fma_hi;
     unsigned int* fallback;        // multi-tap windows: set to 1 when a window mixes exponents; else null
     unsigned int* status;
     // When not zero, a conditional-node handle of the graph this launch belongs

@@ -172,6 +172,43 @@ static __device__ __forceinline__ void tmem_load16(std::uint32_t address, int (&
 
 static __device__ __forceinline__ void tmem_load_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// 16 TMEM lanes x 16 32-bit columns in the mma accumulator fragment layout:
+// thread t holds (lane t/4, columns 2(t%4), 2(t%4)+1) in r0, r1 and lane
+// t/4 + 8 of the same columns in r2, r3; r4..r7 the same for columns 8..15.
+static __device__ __forceinline__ void tmem_load_16x256b_x2(std::uint32_t address, std::uint32_t* r) {
+    asm volatile("tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(address));
+}
+
+// tcgen05.wait::ld that also carries the loaded registers, so no use of them
+// can be scheduled before the wait.
+static __device__ __forceinline__ void tmem_load_wait_regs(std::uint32_t (&r)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15])
+                 :
+                 : "memory");
+}
+
+// Four 8x8 matrices of 16-bit elements, each stored transposed: lane l gives
+// the shared address of row l % 8 of matrix l / 8, which receives column l % 8
+// of that matrix from the fragment (thread t holding elements 2(t%4), 2(t%4)+1
+// of row t/4 in register i for matrix i).
+static __device__ __forceinline__ void stmatrix_x4_trans(std::uint32_t address, const std::uint32_t (&r)[4]) {
+    asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(address), "r"(r[0]),
+                 "r"(r[1]), "r"(r[2]), "r"(r[3])
+                 : "memory");
+}
+
+static __device__ __forceinline__ uint4 load_shared_v4(std::uint32_t address) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(address)
+                 : "memory");
+    return v;
+}
+
 // Arrive (count one) on an mbarrier from a generic-proxy thread.
 static __device__ __forceinline__ void barrier_arrive(std::uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");

@@ -624,3 +624,43 @@ def test_paired_tiles(cuda, oracle, half, shape):
         assert_half_parity(program, [x], oracle, label)
     else:
         assert_parity(program, [x], oracle, label)
+
+
+def uniform_window_input(stream: SeededStream, cin: int, h: int, w: int) -> np.ndarray:
+    """Values in +-100 with channel 0 at 120 at every pixel, so each pixel's
+    max is 120 and its exponent that of its block's scale: blocks of 8 rows x
+    32 columns scaled by 2^k for k from -24 to 9 (FP16-representable), so
+    every window inside a block has one exponent (the direct conv's result)
+    and windows across a block edge mix exponents (the fallback's)."""
+    x = stream.tensor(cin, h, w, 100.0)
+    x[0] = 120.0
+    rows, cols = np.meshgrid(np.arange(h), np.arange(w), indexing="ij")
+    exponents = ((rows // 8) * 17 + (cols // 32) * 5) % 34 - 24
+    return (x * np.ldexp(np.float32(1.0), exponents).astype(np.float32)[None, :, :]).astype(np.float32)
+
+
+@pytest.mark.parametrize("weight_scale", [1.0, 2.0 ** -100], ids=["ordinary", "tiny_weights"])
+@pytest.mark.parametrize("shape", [(16, 72, (3, 3), 21, 64), (64, 64, (3, 3), 19, 48), (128, 256, (1, 1), 13, 56),
+                                   (256, 256, (3, 3), 12, 96)],
+                         ids=["small_acc", "wide_acc", "pointwise", "paired"])
+def test_vector_stores(cuda, oracle, shape, weight_scale):
+    """FP16 outputs of the direct conv written as 16-byte runs of one channel
+    (widths multiples of 8) over inputs whose windows mostly share one
+    exponent: accumulators below 2^22 (converted by integer addition) and
+    above it, window exponents from -24 to 9, a channel count that is not a
+    multiple of 16, patches past the bottom and right edges, paired patches,
+    and, with tiny weights (scales near 2^-108), window exponents outside the
+    range where the power-of-two scale and the bias add fuse exactly, which
+    the per-channel stores take."""
+    cin, cout, kernel, h, w = shape
+    stream = SeededStream(700 + cin + cout + h)
+    p = Program(name="vector")
+    x_in = p.add_input("x", cin)
+    weights = stream.uniform(-0.5, 0.5, cout * cin * kernel[0] * kernel[1]) * np.float32(weight_scale)
+    bias = stream.uniform(-0.2, 0.2, cout)
+    pads = (1, 1, 1, 1) if kernel == (3, 3) else (0, 0, 0, 0)
+    y = p.dense_conv(x_in, cout, weights.astype(np.float32), bias, "c", kernel=kernel, stride=(1, 1), pads=pads,
+                     bits=(8, 8))
+    program = p.finish([y])
+    x = uniform_window_input(stream, cin, h, w)
+    assert_half_parity(program, [x], oracle, f"vector stores {shape} x{weight_scale}")
