@@ -71,6 +71,14 @@ struct Executor::IntegerConv {
     // convs with k_block 128 and at most 256 columns); 0 when not prepared.
     int pair_a_stages{0}, pair_b_stages{0}, pair_group{1};
     bool pair_b_resident{false};
+    // Row halos (multi-column windows with 128-byte K blocks): patches of one
+    // output row of 128 positions whose A stages are single halo rows; ring
+    // depths for one patch and for pairs per tile (0 when not prepared).
+    int row_bytes{0};
+    int row_a_stages{0}, row_b_stages{0};
+    bool row_b_resident{false};
+    int row_pair_a_stages{0}, row_pair_b_stages{0};
+    bool row_pair_b_resident{false};
     void* direct_allocation{nullptr};
     CUtensorMap direct_b_map{};
 };
@@ -111,6 +119,7 @@ struct PlannedConv {
     std::size_t fallback{0};
     int d_patch_h{0}, d_patch_w{0}, d_tiles_y{0}, d_tiles_x{0};
     int m_tiles{1};  // patches per tile sharing each weight block
+    bool row_halo{false};  // one-row patches of 128 positions with row-halo A stages
     CUtensorMap a_map{};
     const void* a_base{nullptr};
 };
@@ -861,6 +870,33 @@ Status Executor::prepare_direct(IntegerConv& conv, const Step& step, const Node&
             }
         }
     }
+    // Row halos: an A stage per (window row, channel block) moves patch_w +
+    // kernel_w - 1 rows instead of kernel_w * patch_w, leaving the weights most
+    // of the copies; they stream one K block per stage. 128-byte K blocks only:
+    // with 64-byte ones (N 64 there) the MMAs on the shifted rows issued at
+    // less than half the rate of per-tap boxes' and the conv ran slower.
+    if (!conv.fields && w.kernel_w >= 2 && conv.k_block == 128) {
+        conv.row_bytes = kernels::direct_row_bytes(128, w.kernel_w, conv.k_block);
+        const bool resident = conv.n_tiles == 1 && conv.direct_k_blocks <= 16;
+        for (const int m_tiles : {1, 2}) {
+            if (m_tiles == 2 && 2 * conv.n_tile > 512) continue;
+            constexpr int depths[][2] = {{8, 8}, {6, 8}, {6, 6}, {4, 8}, {4, 6}, {4, 4}, {3, 8}, {3, 6},
+                                         {3, 4}, {2, 8}, {2, 6}, {2, 5}, {2, 4}, {2, 3}};
+            for (const auto& depth : depths) {
+                const int b_stages = resident ? conv.direct_k_blocks : depth[1];
+                if (depth[0] * m_tiles > 32 || b_stages > 16) continue;
+                if (kernels::direct_conv_row_shared_bytes(conv.k_block, conv.n_tile, conv.n_tiles, depth[0], b_stages,
+                                                          resident, m_tiles, conv.row_bytes) >
+                    kernels::direct_conv_max_shared) {
+                    continue;
+                }
+                (m_tiles == 1 ? conv.row_a_stages : conv.row_pair_a_stages) = depth[0];
+                (m_tiles == 1 ? conv.row_b_stages : conv.row_pair_b_stages) = b_stages;
+                (m_tiles == 1 ? conv.row_b_resident : conv.row_pair_b_resident) = resident;
+                break;
+            }
+        }
+    }
     const std::size_t row_bytes = static_cast<std::size_t>(taps) * conv.c8;
     std::vector<std::int8_t> matrix(static_cast<std::size_t>(n_padded) * row_bytes, 0);
     const int rows = node.out_channels;
@@ -1051,12 +1087,26 @@ Result<Executor::Plan*> Executor::plan_for(const std::vector<Extent>& input_exte
                         pc.d_tiles_x = tiles_x;
                     }
                 }
+                // Row halos when one-row patches of 128 waste at most 1/8 of the
+                // positions.
+                pc.row_halo = false;
+                if (conv.row_a_stages > 0) {
+                    const int row_tiles_x = (out.width + 127) / 128;
+                    if (static_cast<long long>(row_tiles_x) * 128 * 8 <= static_cast<long long>(out.width) * 9) {
+                        pc.row_halo = true;
+                        pc.d_patch_h = 1;
+                        pc.d_patch_w = 128;
+                        pc.d_tiles_y = out.height;
+                        pc.d_tiles_x = row_tiles_x;
+                    }
+                }
                 // Tiles of two patches (plain or depth_to_space outputs only) when
                 // two accumulators still leave TMEM two buffers, or when the conv
                 // has about two tiles per SM or fewer (then one tile per SM needs
                 // no second buffer).
                 const long long tiles = static_cast<long long>(pc.d_tiles_y) * pc.d_tiles_x * conv.n_tiles;
-                if (conv.pair_a_stages > 0 && !step.wsilu && !step.chunk_add && !step.residual &&
+                const bool pair_ready = pc.row_halo ? conv.row_pair_a_stages > 0 : conv.pair_a_stages > 0;
+                if (pair_ready && !step.wsilu && !step.chunk_add && !step.residual &&
                     !staged_tensor_[step.output] && (4 * conv.n_tile <= 512 || tiles <= 2LL * sm_count_)) {
                     pc.m_tiles = 2;
                 }
@@ -1282,8 +1332,10 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
             if (!marked) return marked;
         }
         if (pc.a_base != quantised) {
-            status = kernels::encode_activation_map(&pc.a_map, quantised, conv.c8, grid_h, grid_w, conv.k_block,
-                                                    pc.d_patch_w, pc.d_patch_h);
+            status = kernels::encode_activation_map(
+                &pc.a_map, quantised, conv.c8, grid_h, grid_w, conv.k_block,
+                pc.row_halo ? static_cast<std::uint32_t>(pc.d_patch_w + conv.window.kernel_w - 1) : pc.d_patch_w,
+                pc.row_halo ? 1u : static_cast<std::uint32_t>(pc.d_patch_h));
             if (status != cudaSuccess) return cuda_error("cuTensorMapEncodeTiled activations", status);
             pc.a_base = quantised;
         }
@@ -1306,10 +1358,19 @@ Status Executor::launch_step(const Step& step, Plan& plan, std::size_t index) {
         d.tiles_x = pc.d_tiles_x;
         d.p_tiles = pc.d_tiles_y * pc.d_tiles_x;
         d.m_tiles = pc.m_tiles;
-        d.group = pc.m_tiles == 2 ? conv.pair_group : conv.direct_group;
-        d.a_stages = pc.m_tiles == 2 ? conv.pair_a_stages : conv.direct_a_stages;
-        d.b_stages = pc.m_tiles == 2 ? conv.pair_b_stages : conv.direct_b_stages;
-        d.b_resident = (pc.m_tiles == 2 ? conv.pair_b_resident : conv.direct_b_resident) ? 1 : 0;
+        if (pc.row_halo) {
+            d.row_halo = 1;
+            d.a_row_bytes = conv.row_bytes;
+            d.group = conv.window.kernel_w;
+            d.a_stages = pc.m_tiles == 2 ? conv.row_pair_a_stages : conv.row_a_stages;
+            d.b_stages = pc.m_tiles == 2 ? conv.row_pair_b_stages : conv.row_b_stages;
+            d.b_resident = (pc.m_tiles == 2 ? conv.row_pair_b_resident : conv.row_b_resident) ? 1 : 0;
+        } else {
+            d.group = pc.m_tiles == 2 ? conv.pair_group : conv.direct_group;
+            d.a_stages = pc.m_tiles == 2 ? conv.pair_a_stages : conv.direct_a_stages;
+            d.b_stages = pc.m_tiles == 2 ? conv.pair_b_stages : conv.direct_b_stages;
+            d.b_resident = (pc.m_tiles == 2 ? conv.pair_b_resident : conv.direct_b_resident) ? 1 : 0;
+        }
         d.n_tile = conv.n_tile;
         d.n_tiles = conv.n_tiles;
         d.scales = conv.scales;

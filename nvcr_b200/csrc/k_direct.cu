@@ -92,6 +92,17 @@ __device__ __forceinline__ std::uint64_t swizzled_descriptor(std::uint32_t addre
         (atom << 32) | (static_cast<std::uint64_t>(1) << 46) | (layout << 61);
 }
 
+// Descriptor of an A block starting `dx` rows into a swizzled row-halo box
+// (the box 1 KiB aligned): the start address moved by dx rows and the matrix
+// base offset left 0. The tensor cores apply the swizzle by the operand's
+// shared-memory address bits, as the TMA did when it wrote the box, so a start
+// anywhere on a row boundary reads the rows that follow it (measured on B200:
+// full-size outputs identical to the per-tap boxes' with base offset 0, wrong
+// with the base offset set to the start's swizzle phase).
+__device__ __forceinline__ std::uint64_t row_descriptor(std::uint32_t address, int k_block) {
+    return swizzled_descriptor(address, k_block);
+}
+
 // Bytes of the per-column scales and biases after the tail.
 __host__ __device__ constexpr int column_bytes(int columns) { return columns * 8; }
 
@@ -1052,6 +1063,23 @@ __device__ __forceinline__ void issue_stage(std::uint32_t acc, std::uint32_t sub
     }
 }
 
+// The MMAs of one K block of a row-halo stage: MTiles patches x Steps K steps
+// of 32 bytes, every descriptor a constant offset from the first.
+template <int Steps, int MTiles>
+__device__ __forceinline__ void issue_row_block(std::uint32_t acc, std::uint32_t n_tile, std::uint64_t a_desc,
+                                                int a_block16, std::uint64_t b_desc, std::uint32_t idesc,
+                                                std::uint32_t first) {
+#pragma unroll
+    for (int m = 0; m < MTiles; ++m) {
+#pragma unroll
+        for (int kk = 0; kk < Steps; ++kk) {
+            mma_i8(acc + static_cast<std::uint32_t>(m) * n_tile,
+                   a_desc + static_cast<std::uint64_t>(m * a_block16 + 2 * kk), b_desc + static_cast<std::uint64_t>(2 * kk),
+                   idesc, kk == 0 ? first : 1u);
+        }
+    }
+}
+
 template <int Steps, int MTiles>
 __device__ __forceinline__ void issue_stage_group(int group, std::uint32_t acc, std::uint32_t sub_columns,
                                                   std::uint64_t a_desc, std::uint64_t b_desc, std::uint32_t idesc,
@@ -1145,14 +1173,21 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
     const int k_block = a.k_block;
     // A stage holds `group` consecutive K blocks of one tile (their A boxes, and
     // their B boxes unless the weights are resident, one K block per stage).
+    // Row halos (patches of one output row): an A stage is one input row of the
+    // patch's halo (patch_w + kernel_w - 1 pixels of one channel block, row dy
+    // of the window) serving the window's kernel_w K blocks (dx = 0 ..), each
+    // reading the same rows shifted by dx; B stages hold one K block each.
     const int group = a.group;
+    const bool row_halo = a.row_halo != 0;
     constexpr int m_tiles = MTiles;  // sub-tiles of 128 positions sharing each B stage
     static_assert(MTiles == 1 || !Fusions, "paired tiles carry no fusions");
     constexpr bool fusions = Fusions;
-    const int a_block_bytes = tile_positions_m * k_block;
+    const int a_block_bytes = row_halo ? a.a_row_bytes : tile_positions_m * k_block;
     const int b_block_bytes = n_tile * k_block;
-    const int a_stage_bytes = group * m_tiles * a_block_bytes;
-    const int b_stage_bytes = (a.b_resident ? 1 : group) * b_block_bytes;
+    const int a_stage_bytes = (row_halo ? 1 : group) * m_tiles * a_block_bytes;
+    const int b_stage_bytes = (a.b_resident || row_halo ? 1 : group) * b_block_bytes;
+    // Bytes the TMA writes into an A stage (a row halo box is not a whole 1 KiB).
+    const int a_stage_fill = row_halo ? m_tiles * (a.patch_w + a.window.kernel_w - 1) * k_block : a_stage_bytes;
     // Shared memory: [A stages][B stages][tail][halo ring][column parameters];
     // stage sizes are multiples of 1024 bytes, so every stage keeps the 1 KiB
     // swizzle alignment.
@@ -1220,18 +1255,30 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
     const int my_tiles = total_tiles > static_cast<int>(blockIdx.x)
         ? (total_tiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x)
         : 0;
-    const int stages_per_tile = k_blocks / group;
+    const int stages_per_tile = k_blocks / group;                   // A stages
+    const int b_per_tile = row_halo ? k_blocks : stages_per_tile;  // B stages
+    const int c_blocks = a.c_blocks;
+    const int kernel_w = a.window.kernel_w;
     if (warp == weight_warp) {
         // ---------------- weights by TMA (resident weights: the first tile's K blocks, once)
-        const int items = a.b_resident ? (my_tiles > 0 ? k_blocks : 0) : my_tiles * stages_per_tile;
-        const int boxes = a.b_resident ? 1 : group;
+        const int items = a.b_resident ? (my_tiles > 0 ? k_blocks : 0) : my_tiles * b_per_tile;
+        const int boxes = a.b_resident || row_halo ? 1 : group;
         ring_issue(lane, a.b_stages, boxes, items, smem_address(&tail->empty_b[0]), smem_address(&tail->full_b[0]),
                    abort, a.status, [&](int item, int stage, int part) {
                        int n_index = 0;
                        int kb0 = item;
                        if (!a.b_resident) {
-                           const int local_tile = item / stages_per_tile;
-                           kb0 = (item - local_tile * stages_per_tile) * group;
+                           const int local_tile = item / b_per_tile;
+                           const int j = item - local_tile * b_per_tile;
+                           if (row_halo) {
+                               // the MMA's order: row dy, channel block cb, then dx
+                               const int s_row = j / kernel_w;
+                               const int dx = j - s_row * kernel_w;
+                               const int dy = s_row / c_blocks;
+                               kb0 = (dy * kernel_w + dx) * c_blocks + (s_row - dy * c_blocks);
+                           } else {
+                               kb0 = j * group;
+                           }
                            by_n_tiles.divide(static_cast<int>(blockIdx.x) + local_tile * static_cast<int>(gridDim.x),
                                              n_index);
                        }
@@ -1244,23 +1291,32 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
     } else if (warp == activation_warp) {
         // ---------------- activations by TMA: one box per (tap, channel block)
         grid_dependency_wait();
-        ring_issue(lane, a.a_stages, group * m_tiles, my_tiles * stages_per_tile, smem_address(&tail->empty_a[0]),
-                   smem_address(&tail->full_a[0]), abort, a.status, [&](int item, int stage, int part) {
+        ring_issue(lane, a.a_stages, (row_halo ? 1 : group) * m_tiles, my_tiles * stages_per_tile,
+                   smem_address(&tail->empty_a[0]), smem_address(&tail->full_a[0]), abort, a.status,
+                   [&](int item, int stage, int part) {
                        const int local_tile = item / stages_per_tile;
                        const int block = part / m_tiles;  // K block of the stage
                        const int m = part - block * m_tiles;
-                       const int kb = (item - local_tile * stages_per_tile) * group + block;
+                       const int s_tile = item - local_tile * stages_per_tile;
                        int n_unused, tx;
                        const int pg = by_n_tiles.divide(
                            static_cast<int>(blockIdx.x) + local_tile * static_cast<int>(gridDim.x), n_unused);
                        // A sub-tile past the last patch loads rows below the image: zero fill.
                        const int ty = by_tiles_x.divide(pg * m_tiles + m, tx);
-                       const int tap = kb / a.c_blocks;
-                       const int cb = kb - tap * a.c_blocks;
-                       const int ky = tap / a.window.kernel_w;
-                       const int kx = tap - ky * a.window.kernel_w;
+                       int cb, ky, kx;
+                       if (row_halo) {  // stage s_tile = row ky of the window, channel block cb; all dx
+                           ky = s_tile / c_blocks;
+                           cb = s_tile - ky * c_blocks;
+                           kx = 0;
+                       } else {
+                           const int kb = s_tile * group + block;
+                           const int tap = kb / c_blocks;
+                           cb = kb - tap * c_blocks;
+                           ky = tap / kernel_w;
+                           kx = tap - ky * kernel_w;
+                       }
                        const std::uint32_t full = smem_address(&tail->full_a[stage]);
-                       if (part == 0) barrier_expect_bytes(full, static_cast<std::uint32_t>(a_stage_bytes));
+                       if (part == 0) barrier_expect_bytes(full, static_cast<std::uint32_t>(a_stage_fill));
                        __syncwarp(__activemask());  // the stage's bytes are armed before any copy
                        // Innermost coordinate: the channel block's first byte, a multiple of k_block.
                        tma_load_3d(smem_address(smem + stage * a_stage_bytes + part * a_block_bytes), &a_map, full,
@@ -1276,6 +1332,10 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
             const std::uint64_t b_desc0 = swizzled_descriptor(smem_address(b_smem), k_block);
             const int a_block16 = a_block_bytes >> 4;
             const int b_block16 = b_block_bytes >> 4;
+            // Row halos: the descriptor of the first A stage's first row; stages,
+            // patches and dx rows are address offsets in its low field.
+            const std::uint64_t row_desc0 = row_descriptor(smem_address(smem), k_block);
+            const std::uint64_t k_block16 = static_cast<std::uint64_t>(k_block >> 4);
             const std::uint32_t tile_columns = static_cast<std::uint32_t>(m_tiles * n_tile);
             std::uint32_t g = 0;
             int local = 0;
@@ -1293,6 +1353,59 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
                 }
                 tmem_fence_after();
                 const std::uint32_t acc = tmem + static_cast<std::uint32_t>(buffer) * tile_columns;
+                if (row_halo) {
+                    // Stages in (dy, cb) order; within one, K blocks dx = 0 ..
+                    // kernel_w - 1 read the stage's rows from row dx on: the
+                    // descriptor starts dx rows in, with the matching base offset.
+                    int dy = 0, cb = 0;
+                    for (int st = 0; st < stages_per_tile && ok; ++st, ++g) {
+                        bool ready = barrier_sleep_wait(smem_address(&tail->full_a[sa]), a_phase, a.status);
+                        std::uint64_t a_desc = row_desc0 + static_cast<std::uint64_t>((sa * a_stage_bytes) >> 4);
+                        for (int dx = 0; dx < kernel_w && ready; ++dx, a_desc += k_block16) {
+                            const int kb = (dy * kernel_w + dx) * c_blocks + cb;
+                            if (!a.b_resident) {
+                                ready = barrier_sleep_wait(smem_address(&tail->full_b[sb_ring]), b_ring_phase, a.status);
+                            } else if (local == 0) {
+                                ready = barrier_sleep_wait(smem_address(&tail->full_b[kb]), 0u, a.status);
+                            }
+                            if (!ready) break;
+                            const std::uint64_t b_desc = b_desc0 +
+                                static_cast<std::uint64_t>((a.b_resident ? kb * b_block_bytes : sb_ring * b_stage_bytes) >> 4);
+                            const std::uint32_t first = (st == 0 && dx == 0) ? 0u : 1u;
+                            if (steps == 4) {
+                                issue_row_block<4, MTiles>(acc, static_cast<std::uint32_t>(n_tile), a_desc, a_block16,
+                                                           b_desc, idesc, first);
+                            } else {
+                                issue_row_block<2, MTiles>(acc, static_cast<std::uint32_t>(n_tile), a_desc, a_block16,
+                                                           b_desc, idesc, first);
+                            }
+                            if (!a.b_resident) {
+                                mma_commit(smem_address(&tail->empty_b[sb_ring]));
+                                if (++sb_ring == a.b_stages) {
+                                    sb_ring = 0;
+                                    b_ring_phase ^= 1u;
+                                }
+                            }
+                        }
+                        if (!ready) {
+                            *abort = 1;
+                            ok = false;
+                            break;
+                        }
+                        mma_commit(smem_address(&tail->empty_a[sa]));
+                        if (++sa == a.a_stages) {
+                            sa = 0;
+                            a_phase ^= 1u;
+                        }
+                        if (++cb == c_blocks) {
+                            cb = 0;
+                            ++dy;
+                        }
+                    }
+                    if (!ok) break;
+                    mma_commit(smem_address(&tail->tmem_full[buffer]));
+                    continue;
+                }
                 for (int kb0 = 0; kb0 < k_blocks; kb0 += group, ++g) {
                     // (TMA writes are ordered before the MMA's reads by the full
                     // barriers; only TMEM reuse needs a tcgen05 fence, above.)
@@ -1889,10 +2002,13 @@ bool valid_direct(const DirectConvArgs& a) {
         a.positions == a.out_h * a.out_w &&
         a.group >= 1 && a.group <= 4 &&
         a.k_blocks % a.group == 0 &&
-        (a.m_tiles == 1 || (a.m_tiles == 2 && (a.group == 1 || a.group == 3) && 2 * a.n_tile <= 512 && !a.wsilu &&
-                            !a.chunk_add &&
-                            a.residual == nullptr && a.out_max == nullptr)) &&
-        a.a_stages * a.group * a.m_tiles <= 32 && (a.b_resident || a.b_stages * a.group <= 32) &&
+        (a.m_tiles == 1 || (a.m_tiles == 2 && (a.row_halo || a.group == 1 || a.group == 3) && 2 * a.n_tile <= 512 &&
+                            !a.wsilu && !a.chunk_add && a.residual == nullptr && a.out_max == nullptr)) &&
+        (!a.row_halo ||
+         (a.patch_h == 1 && a.group == a.window.kernel_w && a.patch_w + a.window.kernel_w - 1 <= 256 &&
+          a.a_row_bytes == direct_row_bytes(a.patch_w, a.window.kernel_w, a.k_block))) &&
+        a.a_stages * (a.row_halo ? 1 : a.group) * a.m_tiles <= 32 &&
+        (a.b_resident || a.b_stages * (a.row_halo ? 1 : a.group) <= 32) &&
         a.a_stages >= 2 && a.a_stages <= max_direct_stages && a.b_stages >= 1 &&
         a.b_stages <= max_direct_stages && (!a.b_resident || (a.n_tiles == 1 && a.b_stages == a.k_blocks)) &&
         (a.b_resident || a.b_stages >= 2) && a.d2s_block >= 0 &&
@@ -1913,6 +2029,16 @@ int direct_conv_shared_bytes(int k_block, int n_tile, int n_tiles, int a_stages,
     return 1024 + a_stages * group * m_tiles * tile_positions_m * k_block +
         b_stages * (b_resident ? 1 : group) * n_tile * k_block + tail_bytes() + halo_ring_bytes(m_tiles) +
         column_bytes(n_tile * n_tiles) + staging_bytes;
+}
+
+int direct_row_bytes(int patch_w, int kernel_w, int k_block) {
+    return ((patch_w + kernel_w - 1) * k_block + 1023) / 1024 * 1024;
+}
+
+int direct_conv_row_shared_bytes(int k_block, int n_tile, int n_tiles, int a_stages, int b_stages, bool b_resident,
+                                 int m_tiles, int row_bytes) {
+    return 1024 + a_stages * m_tiles * row_bytes + b_stages * n_tile * k_block + tail_bytes() +
+        halo_ring_bytes(m_tiles) + column_bytes(n_tile * n_tiles) + staging_bytes;
 }
 
 cudaError_t encode_activation_map(CUtensorMap* map, const void* base, std::uint64_t c8, std::uint64_t height,
@@ -2126,8 +2252,11 @@ cudaError_t direct_conv(const CUtensorMap& a_map, const CUtensorMap& b_map, cons
     const int buffers = std::min(max_tmem_buffers, 512 / tile_columns);
     std::uint32_t columns = 32;
     while (static_cast<int>(columns) < buffers * tile_columns) columns <<= 1;
-    const int smem = direct_conv_shared_bytes(args.k_block, args.n_tile, args.n_tiles, args.a_stages, args.b_stages,
-                                              args.group, args.b_resident != 0, args.m_tiles);
+    const int smem = args.row_halo
+        ? direct_conv_row_shared_bytes(args.k_block, args.n_tile, args.n_tiles, args.a_stages, args.b_stages,
+                                       args.b_resident != 0, args.m_tiles, args.a_row_bytes)
+        : direct_conv_shared_bytes(args.k_block, args.n_tile, args.n_tiles, args.a_stages, args.b_stages, args.group,
+                                   args.b_resident != 0, args.m_tiles);
     if (smem > direct_conv_max_shared) return cudaErrorInvalidValue;
     static bool configured = false;
     if (!configured) {

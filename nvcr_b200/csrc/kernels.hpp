@@ -189,6 +189,12 @@ struct DirectConvArgs {
     // and the bias add into one multiply-add (exact there); others take the
     // per-channel stores.
     int fma_lo, fma_hi;
+    // 1: patches of one output row (patch_h 1), each A stage one halo row of
+    // patch_w + kernel_w - 1 pixels of one channel block (a_row_bytes apart per
+    // patch, direct_row_bytes) serving the window row's kernel_w K blocks; group
+    // = kernel_w and B stages hold one K block each.
+    int row_halo;
+    int a_row_bytes;
     unsigned int* fallback;        // multi-tap windows: set to 1 when a window mixes exponents; else null
     unsigned int* status;
     // When not zero, a conditional-node handle of the graph this launch belongs
@@ -219,6 +225,11 @@ cudaError_t direct_conv(const CUtensorMap& a_map, const CUtensorMap& b_map, cons
                         cudaStream_t stream);
 int direct_conv_shared_bytes(int k_block, int n_tile, int n_tiles, int a_stages, int b_stages, int group,
                              bool b_resident, int m_tiles);
+// Row halos: the bytes of one patch's A box ((patch_w + kernel_w - 1) pixels x
+// k_block bytes, rounded up to 1 KiB) and the shared memory of that layout.
+int direct_row_bytes(int patch_w, int kernel_w, int k_block);
+int direct_conv_row_shared_bytes(int k_block, int n_tile, int n_tiles, int a_stages, int b_stages, bool b_resident,
+                                 int m_tiles, int row_bytes);
 constexpr int direct_conv_max_shared = 232448;
 
 // Diagnostics: one thread waits on an mbarrier that nothing arrives on, with the

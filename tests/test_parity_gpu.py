@@ -664,3 +664,33 @@ def test_vector_stores(cuda, oracle, shape, weight_scale):
     program = p.finish([y])
     x = uniform_window_input(stream, cin, h, w)
     assert_half_parity(program, [x], oracle, f"vector stores {shape} x{weight_scale}")
+
+
+@pytest.mark.parametrize("half", [False, True], ids=["f32", "f16"])
+@pytest.mark.parametrize("shape", [(128, 256, 9, 120, None), (256, 256, 7, 240, None), (128, 128, 5, 256, None),
+                                   (128, 64, 11, 250, None), (256, 512, 6, 120, 2), (128, 256, 3, 360, None),
+                                   (64, 64, 10, 240, None), (64, 96, 9, 120, None), (192, 64, 5, 128, None)],
+                         ids=["120", "240", "256", "250_narrow_n", "d2s", "360_three_patches", "k64_240",
+                              "k64_ragged_n", "k64_three_blocks"])
+def test_row_halos(cuda, oracle, half, shape):
+    """Row-halo direct convs: 3x3 windows over 128-byte channel blocks on
+    widths within 1/8 of a multiple of 128, whose patches are single output
+    rows of 128 positions and whose A stages are one input row of 130 pixels
+    read by three K blocks starting 0, 1 and 2 rows in (64-byte channel blocks,
+    the k64 cases, take per-tap boxes on the same widths). The inputs' windows
+    mostly share one exponent (the direct conv's results) with block edges
+    that mix exponents (the fallback's), an all-zero column and one non-finite
+    pixel; patches past the right edge, one to three patches per row, one and
+    two N tiles, one to three channel blocks and a depth_to_space output."""
+    cin, cout, h, w, block = shape
+    stream = SeededStream(900 + cin + cout + w)
+    program = d2s_program(stream, cin, cout, block, (8, 8)) if block else \
+        conv_program(stream, cin, cout, (3, 3), (1, 1), (1, 1, 1, 1), (8, 8))
+    x = uniform_window_input(stream, cin, h, w)
+    x[:, :, 7] = 0.0
+    x[5, 1, 11] = np.inf
+    label = f"row halos {cin}->{cout} {h}x{w}"
+    if half:
+        assert_half_parity(program, [x], oracle, label)
+    else:
+        assert_parity(program, [x], oracle, label)
