@@ -429,12 +429,13 @@ def main():
     else:
         achieved = all_ops / (all_ms / 1000.0) / 1e12 if all_ms else 0.0
     traffic = None
-    traffic_file = ROOT / "profiles" / "fused_conv_traffic.json"
+    traffic_file = ROOT / "profiles" / "direct_conv_traffic.json"
     if traffic_file.exists():
         traffic = json.loads(traffic_file.read_text()).get("bytes_per_launch")
     roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(int8_peak, 1), "unit": "TOPS",
                 "frac": round(achieved / int8_peak, 4), "traffic": traffic,
-                "kernel": "integer_conv on the tensor-bound layers (L4, L5): tcgen05 kind::i8 implicit GEMM",
+                "kernel": "direct_conv_kernel on the tensor-bound layers (L4, L5): tcgen05 kind::i8 over the int8 "
+                          "per-pixel copy, row-halo A stages; traffic: one L4 launch (profiles/direct_conv_traffic.json)",
                 "peak_source": int8_source,
                 "time_share": shares,
                 "layers": layer_rows}
