@@ -124,6 +124,9 @@ __host__ __device__ constexpr int halo_ring_bytes(int m_tiles) { return window_s
 __device__ __forceinline__ void cp_async4(std::uint32_t dst, const void* src, int src_bytes) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
+__device__ __forceinline__ void cp_async16(std::uint32_t dst, const void* src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
 // An arrival on the mbarrier once all of this thread's earlier cp.async copies
 // have landed (the barrier's count includes it).
 __device__ __forceinline__ void cp_async_arrive(std::uint32_t bar) {
@@ -1476,6 +1479,16 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
                 at[j] = make_short2(static_cast<short>(hy), static_cast<short>(hx));
             }
         }
+        // Pointwise windows without padding over rows of whole 16-byte vectors:
+        // the halo is the patch, 32 vectors of 4 maxima, one copy per lane
+        // (a copy per maximum made this warp the pace of pointwise convs with
+        // two patches per tile: about 3 K cycles per tile).
+        const int row_vectors = a.patch_w / 4;
+        const bool vector_halo = a.window.kernel_h == 1 && a.window.kernel_w == 1 && a.window.pad_top == 0 &&
+            a.window.pad_left == 0 && a.in_w % 4 == 0 && a.patch_w % 4 == 0 && a.patch_h * row_vectors == 32 &&
+            (reinterpret_cast<std::uintptr_t>(a.pixel_max) & 15u) == 0;
+        const int vector_row = vector_halo ? lane / row_vectors : 0;
+        const int vector_col = vector_halo ? 4 * (lane - vector_row * row_vectors) : 0;
         RingPosition ring{0, 0u};
         for (int l = 0; l < my_tiles; ++l, ring.advance(1, window_slots)) {
             const int slot = ring.slot;
@@ -1494,6 +1507,15 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
                 const int iy0 = ty * a.patch_h - a.window.pad_top;
                 const int ix0 = tx * a.patch_w - a.window.pad_left;
                 float* halo = halo_maxima + slot * halo_slot + m * halo_slot_floats;
+                if (vector_halo) {
+                    const int iy = iy0 + vector_row;
+                    const int ix = ix0 + vector_col;  // all four inside or all outside: in_w % 4 == 0
+                    const bool inside = iy < a.in_h && ix < a.in_w;
+                    cp_async16(smem_address(halo + vector_row * halo_w + vector_col),
+                               a.pixel_max + (inside ? static_cast<std::size_t>(iy) * a.in_w + ix : 0),
+                               inside ? 16 : 0);
+                    continue;
+                }
 #pragma unroll
                 for (int j = 0; j < halo_lane_items; ++j) {
                     const int i = lane + 32 * j;
