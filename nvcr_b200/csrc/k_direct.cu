@@ -115,15 +115,41 @@ constexpr int staging_bytes = epilogue_warps * staging_warp_bytes;
 __host__ __device__ constexpr int tail_bytes() { return static_cast<int>((sizeof(DirectTail) + 15) / 16 * 16); }
 
 // The window warp stages each tile's halo of pixel maxima ((patch_h + 2) x
-// (patch_w + 2) at most: 390 floats for a 1 x 128 patch) in one of
-// window_slots slots, that many tiles ahead.
-constexpr int halo_slot_floats = 400;
+// (patch_w + 2) at most: 390 floats for a 1 x 128 patch, 408 with rows of
+// whole 16-byte vectors) in one of window_slots slots, that many tiles ahead.
+constexpr int halo_slot_floats = 416;
 constexpr int halo_lane_items = (halo_slot_floats + 31) / 32;
 __host__ __device__ constexpr int halo_ring_bytes(int m_tiles) { return window_slots * m_tiles * halo_slot_floats * 4; }
 
 __device__ __forceinline__ void cp_async4(std::uint32_t dst, const void* src, int src_bytes) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
+// Layout of a tile's halo of pixel maxima in its slot: rows `pitch` floats
+// apart, the halo's first column at `shift`. With vector copies (image rows of
+// whole 16-byte vectors, the maxima 16-byte aligned, patch_w a multiple of 4)
+// every halo row starts at the 16-byte vector holding its first column
+// (`shift` = that column mod 4, the same for every patch) and spans whole
+// vectors; otherwise rows are halo_w floats from column 0.
+struct HaloLayout {
+    bool vectors;
+    int shift, pitch, row_vectors;
+};
+__device__ __forceinline__ HaloLayout halo_layout(const DirectConvArgs& a) {
+    const int halo_h = a.patch_h + a.window.kernel_h - 1;
+    const int halo_w = a.patch_w + a.window.kernel_w - 1;
+    HaloLayout h;
+    h.shift = ((-a.window.pad_left) % 4 + 4) % 4;
+    h.row_vectors = (halo_w + h.shift + 3) / 4;
+    h.vectors = a.in_w % 4 == 0 && a.patch_w % 4 == 0 && (reinterpret_cast<std::uintptr_t>(a.pixel_max) & 15u) == 0 &&
+        halo_h * 4 * h.row_vectors <= halo_slot_floats;
+    if (!h.vectors) {
+        h.shift = 0;
+        h.row_vectors = 0;
+    }
+    h.pitch = h.vectors ? 4 * h.row_vectors : halo_w;
+    return h;
+}
+
 __device__ __forceinline__ void cp_async16(std::uint32_t dst, const void* src, int src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
@@ -1479,16 +1505,22 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
                 at[j] = make_short2(static_cast<short>(hy), static_cast<short>(hx));
             }
         }
-        // Pointwise windows without padding over rows of whole 16-byte vectors:
-        // the halo is the patch, 32 vectors of 4 maxima, one copy per lane
-        // (a copy per maximum made this warp the pace of pointwise convs with
-        // two patches per tile: about 3 K cycles per tile).
-        const int row_vectors = a.patch_w / 4;
-        const bool vector_halo = a.window.kernel_h == 1 && a.window.kernel_w == 1 && a.window.pad_top == 0 &&
-            a.window.pad_left == 0 && a.in_w % 4 == 0 && a.patch_w % 4 == 0 && a.patch_h * row_vectors == 32 &&
-            (reinterpret_cast<std::uintptr_t>(a.pixel_max) & 15u) == 0;
-        const int vector_row = vector_halo ? lane / row_vectors : 0;
-        const int vector_col = vector_halo ? 4 * (lane - vector_row * row_vectors) : 0;
+        // Halos of whole 16-byte vectors where the layout allows (a copy per
+        // maximum made this warp the pace of pointwise convs with two patches
+        // per tile: about 3 K cycles per tile): at most 104 vectors, four per
+        // lane, their (row, vector) precomputed.
+        const HaloLayout layout = halo_layout(a);
+        const int halo_vectors = halo_h * layout.row_vectors;
+        short2 vat[4];
+        {
+            const TileDivider by_row_vectors(layout.vectors ? layout.row_vectors : 1);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                int vx;
+                const int vy = by_row_vectors.divide(lane + 32 * j, vx);
+                vat[j] = make_short2(static_cast<short>(vy), static_cast<short>(vx));
+            }
+        }
         RingPosition ring{0, 0u};
         for (int l = 0; l < my_tiles; ++l, ring.advance(1, window_slots)) {
             const int slot = ring.slot;
@@ -1507,13 +1539,19 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
                 const int iy0 = ty * a.patch_h - a.window.pad_top;
                 const int ix0 = tx * a.patch_w - a.window.pad_left;
                 float* halo = halo_maxima + slot * halo_slot + m * halo_slot_floats;
-                if (vector_halo) {
-                    const int iy = iy0 + vector_row;
-                    const int ix = ix0 + vector_col;  // all four inside or all outside: in_w % 4 == 0
-                    const bool inside = iy < a.in_h && ix < a.in_w;
-                    cp_async16(smem_address(halo + vector_row * halo_w + vector_col),
-                               a.pixel_max + (inside ? static_cast<std::size_t>(iy) * a.in_w + ix : 0),
-                               inside ? 16 : 0);
+                if (layout.vectors) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        if (lane + 32 * j < halo_vectors) {
+                            const int iy = iy0 + vat[j].x;
+                            // a multiple of 4: the vector is wholly inside or outside (in_w % 4 == 0)
+                            const int ix = ix0 - layout.shift + 4 * vat[j].y;
+                            const bool inside = iy >= 0 && iy < a.in_h && ix >= 0 && ix < a.in_w;
+                            cp_async16(smem_address(halo + vat[j].x * layout.pitch + 4 * vat[j].y),
+                                       a.pixel_max + (inside ? static_cast<std::size_t>(iy) * a.in_w + ix : 0),
+                                       inside ? 16 : 0);
+                        }
+                    }
                     continue;
                 }
 #pragma unroll
@@ -1558,7 +1596,7 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
         const int tile_step = groups * static_cast<int>(gridDim.x);
         const int kernel_h = a.window.kernel_h;
         const int kernel_w = a.window.kernel_w;
-        const int halo_w = a.patch_w + kernel_w - 1;
+        const HaloLayout halo_geometry = halo_layout(a);
         RingPosition halo_ring{0, 0u};
         RingPosition accumulator{0, 0u};
         halo_ring.advance(first_local, window_slots);
@@ -1587,13 +1625,14 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
             for (int m = 0; m < MTiles; ++m) {
                 float largest = 0.0f;
                 float smallest = __uint_as_float(0x7f800000u);  // smallest non-zero
-                const float* halo = halo_maxima + slot * halo_slot + m * halo_slot_floats + patch_y * halo_w + patch_x;
+                const float* halo = halo_maxima + slot * halo_slot + m * halo_slot_floats + halo_geometry.shift +
+                    patch_y * halo_geometry.pitch + patch_x;
 #pragma unroll
                 for (int ky = 0; ky < 3; ++ky) {
 #pragma unroll
                     for (int kx = 0; kx < 3; ++kx) {
                         if (ky < kernel_h && kx < kernel_w) {
-                            const float v = halo[ky * halo_w + kx];
+                            const float v = halo[ky * halo_geometry.pitch + kx];
                             largest = fmaxf(largest, v);
                             if (v > 0.0f) smallest = fminf(smallest, v);
                         }
