@@ -443,6 +443,21 @@ __global__ void __launch_bounds__(256) quantise_planes_wide_kernel(const void* _
 // into per-pixel records, stored as one 16-byte piece per pixel and group.
 constexpr int half_planes_max_c8 = 256;
 
+// The FP16 fast path of a pixel from its max |x| as FP16 bits (finite when
+// below 0x7c00): 2^-e as FP16 bits when the pixel takes it, else 0. The pixel's
+// exponent is e = frexp(max) - 7, and the path needs -15 <= e <= 14 and
+// max * 2^-e < 127.5 (the FP16 fused multiply-add with 1536 then leaves q in
+// the low byte). On the bits: a normal max = 1.m * 2^(E - 15) has e = E - 21, so
+// the path holds for E >= 6 with m < 1016/1024 (1.m * 64 < 127.5), and 2^-e is
+// the FP16 of exponent field 36 - E; an all-zero pixel (e = 0) takes it with
+// 2^0; subnormal, infinite and NaN maxima do not. (Equal to the float rule for
+// every FP16 pattern, checked exhaustively.)
+__device__ __forceinline__ std::uint32_t half_fast_scale(std::uint32_t magnitude) {
+    const std::uint32_t exponent = magnitude >> 10;
+    const bool fast = exponent >= 6u && exponent < 31u && (magnitude & 0x3ffu) < 1016u;
+    return magnitude == 0u ? 15u << 10 : (fast ? (36u - exponent) << 10 : 0u);
+}
+
 __device__ __forceinline__ std::uint32_t hfma2_bits(std::uint32_t x, std::uint32_t s, std::uint32_t c) {
     std::uint32_t r;
     asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(x), "r"(s), "r"(c));
@@ -507,10 +522,9 @@ __global__ void __launch_bounds__(CPT == 8 ? 512 : 256, 2)
         const float maximum = finite ? __half2float(__ushort_as_half(static_cast<unsigned short>(magnitude)))
                                      : __uint_as_float(0x7f800000u);
         maxima[p] = maximum;
-        const int e = activation_exponent(maximum, 8);
-        const bool fast = finite && e >= -15 && e <= 14 && __fmul_rn(maximum, power_of_two(-e)) < 127.5f;
-        slow |= fast ? 0u : 1u << p;
-        scale_bits[p >> 1] |= (fast ? static_cast<std::uint32_t>(15 - e) << 10 : 0u) << (16 * (p & 1));
+        const std::uint32_t fast_scale = half_fast_scale(magnitude);
+        slow |= fast_scale != 0u ? 0u : 1u << p;
+        scale_bits[p >> 1] |= fast_scale << (16 * (p & 1));
     }
     if (cg == 0) {
         float4* target = reinterpret_cast<float4*>(pixel_max + p0);
@@ -664,10 +678,9 @@ __global__ void __launch_bounds__(streamed_threads, 1)
                 const float maximum = finite ? __half2float(__ushort_as_half(static_cast<unsigned short>(magnitude)))
                                              : __uint_as_float(0x7f800000u);
                 maxima[p] = maximum;
-                const int e = activation_exponent(maximum, 8);
-                const bool fast = finite && e >= -15 && e <= 14 && __fmul_rn(maximum, power_of_two(-e)) < 127.5f;
-                slow |= fast ? 0u : 1u << p;
-                scale_bits[p >> 1] |= (fast ? static_cast<std::uint32_t>(15 - e) << 10 : 0u) << (16 * (p & 1));
+                const std::uint32_t fast_scale = half_fast_scale(magnitude);
+                slow |= fast_scale != 0u ? 0u : 1u << p;
+                scale_bits[p >> 1] |= fast_scale << (16 * (p & 1));
             }
             if (cg == 0) {
                 float4* target = reinterpret_cast<float4*>(pixel_max + p0);
@@ -1927,9 +1940,10 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
                                 packed[half][i] = *reinterpret_cast<const std::uint32_t*>(&pair);
                             }
                         }
-                        // The next chunk's TMEM loads fly during this chunk's stores.
-                        const bool more = c + 1 < chunks16;
-                        if (more) load16(r, c + 1);
+                        // The next chunk's TMEM loads fly during this chunk's stores
+                        // (the last chunk reloads its own columns: no branch around
+                        // the warp-wide loads).
+                        load16(r, c + 1 < chunks16 ? c + 1 : c);
                         stmatrix_x4_trans(st_address, packed[0]);
                         stmatrix_x4_trans(st_address + 512u, packed[1]);
                         __syncwarp();
@@ -1939,7 +1953,7 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
                         if (16 * c < stored) d[0] = first;
                         if (16 * c + 8 < stored) d[dst_half] = second;
                         __syncwarp();  // the block is rewritten by the next chunk
-                        if (more) tmem_load_wait_regs(r);
+                        tmem_load_wait_regs(r);
                     }
                 };
                 if (a.small_accumulators != 0) {
