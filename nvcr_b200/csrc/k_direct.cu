@@ -475,19 +475,23 @@ __device__ __forceinline__ std::uint32_t word_of(const uint4& v, int w) {
 template <int CPT>  // channels per thread: 16 (8 also compiles: half the registers)
 __global__ void __launch_bounds__(CPT == 8 ? 512 : 256, 2)
     quantise_half_planes_kernel(const __half* __restrict__ in, int channels, int c8, int pixels, int sub_tiles,
-                                std::int8_t* __restrict__ out, float* __restrict__ pixel_max,
+                                int octet_shift, std::int8_t* __restrict__ out, float* __restrict__ pixel_max,
                                 unsigned int* __restrict__ clear_word) {
     grid_dependency_wait();
     launch_dependents();
     if (clear_word != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *clear_word = 0u;
-    extern __shared__ uint4 group_maxima[];  // [sub_tiles][groups][16]
+    // A sub-tile is `octets` x 8 pixels (octets = 16, 8 or 4: fewer for small
+    // inputs, so the blocks cover every SM) x c8 channels; thread (cg, v) takes
+    // channels cg * CPT .. and pixels 8v ...
+    extern __shared__ uint4 group_maxima[];  // [sub_tiles][groups][octets]
+    const int octets = 1 << octet_shift;
     const int groups = c8 / CPT;
-    const int per_tile = 16 * groups;
+    const int per_tile = octets * groups;
     const int s = static_cast<int>(threadIdx.x) / per_tile;
     const int r = static_cast<int>(threadIdx.x) - s * per_tile;
-    const int cg = r >> 4;
-    const int v = r & 15;
-    const long long p0 = (static_cast<long long>(blockIdx.x) * sub_tiles + s) * 128 + v * 8;
+    const int cg = r >> octet_shift;
+    const int v = r & (octets - 1);
+    const long long p0 = (static_cast<long long>(blockIdx.x) * sub_tiles + s) * (8 * octets) + v * 8;
     const bool live = p0 < pixels;
     uint4 x[CPT];
 #pragma unroll
@@ -502,11 +506,11 @@ __global__ void __launch_bounds__(CPT == 8 ? 512 : 256, 2)
 #pragma unroll
         for (int w = 0; w < 4; ++w) m[w] = __vmaxu2(m[w], word_of(x[j], w) & 0x7fff7fffu);
     }
-    group_maxima[(s * groups + cg) * 16 + v] = make_uint4(m[0], m[1], m[2], m[3]);
+    group_maxima[(s * groups + cg) * octets + v] = make_uint4(m[0], m[1], m[2], m[3]);
     __syncthreads();
     if (!live) return;
     for (int g = 0; g < groups; ++g) {
-        const uint4 q = group_maxima[(s * groups + g) * 16 + v];
+        const uint4 q = group_maxima[(s * groups + g) * octets + v];
         m[0] = __vmaxu2(m[0], q.x);
         m[1] = __vmaxu2(m[1], q.y);
         m[2] = __vmaxu2(m[2], q.z);
@@ -2211,12 +2215,33 @@ cudaError_t quantise_pixels(const void* in, PixelSource form, int channels, int 
                                      dim3(streamed_threads), bytes, stream, planes, channels, c8, pixels, sub_tiles,
                                      tiles, out, pixel_max, clear_word);
         }
-        const unsigned blocks = static_cast<unsigned>((pixels + block_pixels - 1) / block_pixels);
-        const std::size_t bytes = static_cast<std::size_t>(sub_tiles) * per_tile * sizeof(uint4);
+        // Sub-tiles of 128, 64 or 32 pixels and as many per block (up to 256
+        // threads) as leave at least two blocks per SM: a small input (config
+        // 2 L5: 8160 pixels of 256 channels) otherwise runs on part of the SMs.
+        int octet_shift = 4;
+        int sub = sub_tiles;
+        for (const int shift : {4, 3, 2}) {
+            const int tile_threads = (1 << shift) * (c8 / 16);
+            bool found = false;
+            for (int candidate = tile_threads >= 256 ? 1 : 256 / tile_threads; candidate >= 1; candidate /= 2) {
+                octet_shift = shift;
+                sub = candidate;
+                const long long pixels_per_block = 8LL * (1 << shift) * candidate;
+                if ((pixels + pixels_per_block - 1) / pixels_per_block >= 2LL * sm_count) {
+                    found = true;
+                    break;
+                }
+            }
+            if (found) break;
+        }
+        const long long pixels_per_block = 8LL * (1 << octet_shift) * sub;
+        const int tile_threads = (1 << octet_shift) * (c8 / 16);
+        const unsigned blocks = static_cast<unsigned>((pixels + pixels_per_block - 1) / pixels_per_block);
+        const std::size_t bytes = static_cast<std::size_t>(sub) * tile_threads * sizeof(uint4);
         return launch_overlapped(quantise_half_planes_kernel<16>, dim3(blocks),
-                                 dim3(static_cast<unsigned>(per_tile * sub_tiles)), bytes, stream,
-                                 static_cast<const __half*>(in), channels, c8, pixels, sub_tiles, out, pixel_max,
-                                 clear_word);
+                                 dim3(static_cast<unsigned>(tile_threads * sub)), bytes, stream,
+                                 static_cast<const __half*>(in), channels, c8, pixels, sub, octet_shift, out,
+                                 pixel_max, clear_word);
     }
     // Planes whose length is a whole number of 16-byte vectors and whose base is
     // 16-byte aligned take the vector-load kernel.
