@@ -858,6 +858,10 @@ __global__ void __launch_bounds__(field_run) quantise_fields_fixed_kernel(const 
     const int a0 = vectors_apply ? (ix0 >= 0 ? (ix0 & ~7) : -((-ix0 + 7) & ~7)) : ix0;
     const int shift = ix0 - a0;
     const int pitch = (span + 7 + 7) & ~7;  // the shift (< 8) plus span, in whole 8-float vectors
+    // Stride 2 with vector rows: each staged row is split by column parity, so
+    // the gather's lanes (positions 2 columns apart) read consecutive floats
+    // instead of every other one (two lanes per bank).
+    const bool split = vectors_apply && w.stride_x == 2;
     if (vectors_apply) {
         const int vectors = (shift + span + 7) / 8;
         for (int i = threadIdx.x; i < C * KH * vectors; i += field_run) {
@@ -891,9 +895,15 @@ __global__ void __launch_bounds__(field_run) quantise_fields_fixed_kernel(const 
                 f[j] = __half2float(__ushort_as_half(static_cast<unsigned short>(words[j >> 1] >> (16 * (j & 1)))));
             }
             if (8 * vcol + 8 <= pitch) {
-                float4* target = reinterpret_cast<float4*>(rows + rc * pitch + 8 * vcol);
-                target[0] = make_float4(f[0], f[1], f[2], f[3]);
-                target[1] = make_float4(f[4], f[5], f[6], f[7]);
+                if (split) {  // even columns in the row's first half, odd ones in its second
+                    *reinterpret_cast<float4*>(rows + rc * pitch + 4 * vcol) = make_float4(f[0], f[2], f[4], f[6]);
+                    *reinterpret_cast<float4*>(rows + rc * pitch + pitch / 2 + 4 * vcol) =
+                        make_float4(f[1], f[3], f[5], f[7]);
+                } else {
+                    float4* target = reinterpret_cast<float4*>(rows + rc * pitch + 8 * vcol);
+                    target[0] = make_float4(f[0], f[1], f[2], f[3]);
+                    target[1] = make_float4(f[4], f[5], f[6], f[7]);
+                }
             }
         }
     } else {
@@ -914,7 +924,15 @@ __global__ void __launch_bounds__(field_run) quantise_fields_fixed_kernel(const 
     __syncthreads();
     const int ox = ox0 + static_cast<int>(threadIdx.x);
     if (ox >= out_w) return;
-    const float* base = rows + shift + static_cast<int>(threadIdx.x) * w.stride_x;
+    // Column of tap kx within a staged row: shift + stride * t + kx, or in a
+    // parity-split row (column & 1) * pitch / 2 + column / 2 = offset[kx] + t.
+    int column_of[KW];
+#pragma unroll
+    for (int kx = 0; kx < KW; ++kx) {
+        const int column = shift + kx;
+        column_of[kx] = split ? (column & 1) * (pitch / 2) + (column >> 1) + static_cast<int>(threadIdx.x)
+                              : column + static_cast<int>(threadIdx.x) * w.stride_x;
+    }
     float v[C8];
     std::uint32_t m = 0;
 #pragma unroll
@@ -922,7 +940,7 @@ __global__ void __launch_bounds__(field_run) quantise_fields_fixed_kernel(const 
         if (k < values) {
             const int c = k / (KH * KW);
             const int tap = k % (KH * KW);
-            v[k] = base[(c * KH + tap / KW) * pitch + tap % KW];
+            v[k] = rows[(c * KH + tap / KW) * pitch + column_of[tap % KW]];
             m = max(m, magnitude_bits_of(v[k]));
         } else {
             v[k] = 0.0f;
