@@ -669,9 +669,10 @@ def test_vector_stores(cuda, oracle, shape, weight_scale):
 @pytest.mark.parametrize("half", [False, True], ids=["f32", "f16"])
 @pytest.mark.parametrize("shape", [(128, 256, 9, 120, None), (256, 256, 7, 240, None), (128, 128, 5, 256, None),
                                    (128, 64, 11, 250, None), (256, 512, 6, 120, 2), (128, 256, 3, 360, None),
-                                   (64, 64, 10, 240, None), (64, 96, 9, 120, None), (192, 64, 5, 128, None)],
+                                   (64, 64, 10, 240, None), (64, 96, 9, 120, None), (192, 64, 5, 128, None),
+                                   (40, 48, 6, 128, None)],
                          ids=["120", "240", "256", "250_narrow_n", "d2s", "360_three_patches", "k64_240",
-                              "k64_ragged_n", "k64_three_blocks"])
+                              "k64_ragged_n", "k64_three_blocks", "k64_40_channels"])
 def test_row_halos(cuda, oracle, half, shape):
     """Row-halo direct convs: 3x3 windows over 128-byte channel blocks on
     widths within 1/8 of a multiple of 128, whose patches are single output
