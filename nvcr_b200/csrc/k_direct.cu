@@ -1662,6 +1662,16 @@ direct_conv_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_const
                 float smallest = __uint_as_float(0x7f800000u);  // smallest non-zero
                 const float* halo = halo_maxima + slot * halo_slot + m * halo_slot_floats + halo_geometry.shift +
                     patch_y * halo_geometry.pitch + patch_x;
+                if (kernel_h == 1 && kernel_w == 1) {
+                    // One pixel per window: its exponent, never mixed.
+                    int tx;
+                    const int ty = by_tiles_x.divide(pg * m_tiles + m, tx);
+                    const bool real_m = pg * m_tiles + m < a.p_tiles && ty * a.patch_h + patch_y < a.out_h &&
+                        tx * a.patch_w + patch_x < a.out_w;
+                    const float v = halo[0];
+                    if (real_m && v != __uint_as_float(0x7f800000u)) codes[m] = activation_exponent(v, 8);
+                    continue;
+                }
 #pragma unroll
                 for (int ky = 0; ky < 3; ++ky) {
 #pragma unroll
